@@ -1,0 +1,399 @@
+// Torch op registry for the k8v4 sm_100a kernel library: torch.ops.k8v4.*.
+//
+// Each op validates dtypes, devices, shapes and strides on the host, then
+// calls the raw-pointer launcher of its .cu file on the current stream. The
+// op set mirrors the reference's xe2_kv registry (k8v4_v030/native/
+// xe2_kv_ops.cpp:1779-1837) where the semantics carry over (paged store,
+// batched decode over every request in one launch) and adds the GEMM, norm,
+// activation, embedding and prefill-attention ops the reference took from
+// libraries.
+#include <torch/library.h>
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_runtime.h>
+
+extern "C" {
+int k8v4_kv_store(int fmt, const void* k, int64_t k_stride_t, const void* v, int64_t v_stride_t, const int64_t* slots,
+                  void* cache, int64_t num_pages, int page_bytes, int T, int hkv, cudaStream_t st);
+int k8v4_rope_store(const void* qkv, const float* cos_sin, const int64_t* positions, void* q_out,
+                    const int64_t* slots, void* cache, int64_t num_pages, int page_bytes, int T, int hq, int hkv,
+                    cudaStream_t st);
+int k8v4_decode_attn(const void* q, const int32_t* cu_q, const int32_t* seq_lens, const int32_t* q_ends,
+                     const int32_t* block_table, int bt_stride, const void* cache, int64_t num_pages, int hkv,
+                     int head_offset, int heads, int gqa, int hq_total, int nseq, int max_q_len, int nsplit,
+                     float sm_scale, void* out, float* ws_o, float* ws_ml, cudaStream_t st);
+int64_t k8v4_decode_ws_floats(int nseq, int heads, int nsplit, int max_q_len, int gqa);
+int k8v4_prefill_attn(const void* q, const int32_t* cu_q, const int32_t* seq_lens, const int32_t* block_table,
+                      int bt_stride, const void* cache, int64_t num_pages, int hkv, int head_offset, int heads,
+                      int gqa, int hq_total, int nseq, int max_q_len, float sm_scale, void* out, cudaStream_t st);
+int k8v4_wq_gemm(int mode, const void* w, const void* wscale, const void* x, const float* xscale,
+                 const void* residual, void* out, float* ws, int M, int N, int K, int ldo, int split,
+                 cudaStream_t st);
+int k8v4_rmsnorm(const void* x, void* residual, const void* w, void* y, void* yq, float* yscale, int rows, int n,
+                 float eps, cudaStream_t st);
+int k8v4_silu_mul(const void* gu, void* y, void* yq, float* yscale, int rows, int inter, cudaStream_t st);
+int k8v4_quant_rows(const void* x, void* q, float* scale, int rows, int n, cudaStream_t st);
+int k8v4_embed_int8(const int64_t* ids, const void* codes, const void* scales, void* out, int T, int n,
+                    int64_t start, int64_t rows, cudaStream_t st);
+int k8v4_splitk_finish(float* ws, const void* residual, void* out, int64_t total, int zero_ws, cudaStream_t st);
+int k8v4_argmax(const void* logits, int rows, int vocab, int64_t offset, float* best_val, int64_t* best_idx,
+                cudaStream_t st);
+int k8v4_status_gemm(int clear);
+int k8v4_status_store(int clear);
+int k8v4_status_misc(int clear);
+int k8v4_status_decode(int clear);
+int k8v4_status_prefill(int clear);
+int k8v4_status_sampler(int clear);
+}
+
+namespace {
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void check_cuda(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+}
+void check_contig(const at::Tensor& t, const char* name) {
+  check_cuda(t, name);
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+}
+void check_rc(int rc, const char* what) { TORCH_CHECK(rc == 0, "k8v4 ", what, " launch failed (code ", rc, ")"); }
+
+// ------------------------------------------------------------------ KV store
+void kv_store(int64_t fmt, const at::Tensor& k, const at::Tensor& v, const at::Tensor& slots, at::Tensor& cache,
+              int64_t hkv) {
+  check_cuda(k, "k");
+  check_cuda(v, "v");
+  check_contig(slots, "slot_mapping");
+  check_contig(cache, "cache");
+  TORCH_CHECK(k.scalar_type() == at::kBFloat16 && v.scalar_type() == at::kBFloat16, "k/v must be bf16");
+  TORCH_CHECK(slots.scalar_type() == at::kLong, "slot_mapping must be int64");
+  TORCH_CHECK(cache.scalar_type() == at::kByte && cache.dim() == 2, "cache must be uint8 [pages, page_bytes]");
+  TORCH_CHECK(k.dim() == 3 && v.dim() == 3 && k.size(1) == hkv && v.size(1) == hkv, "k/v must be [T, hkv, D]");
+  TORCH_CHECK(k.stride(2) == 1 && v.stride(2) == 1 && k.stride(1) == k.size(2) && v.stride(1) == v.size(2),
+              "k/v heads must be dense");
+  const int D = fmt == 0 ? 256 : 128;
+  TORCH_CHECK(k.size(2) == D && v.size(2) == D, "head_dim must be ", D);
+  TORCH_CHECK(slots.numel() == k.size(0) && v.size(0) == k.size(0), "token count mismatch");
+  const int page = fmt == 0 ? 64 : 16;
+  const int64_t per_head = fmt == 0 ? 396 : 202;
+  TORCH_CHECK(cache.size(1) == page * hkv * per_head, "cache page_bytes mismatch");
+  c10::cuda::CUDAGuard g(cache.device());
+  check_rc(k8v4_kv_store((int)fmt, k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0), slots.data_ptr<int64_t>(),
+                         cache.data_ptr(), cache.size(0), (int)cache.size(1), (int)k.size(0), (int)hkv, cur_stream()),
+           "kv_store");
+}
+
+void rope_store(const at::Tensor& qkv, const at::Tensor& cos_sin, const at::Tensor& positions, at::Tensor& q_out,
+                const at::Tensor& slots, at::Tensor& cache, int64_t hq, int64_t hkv) {
+  check_contig(qkv, "qkv");
+  check_contig(cos_sin, "cos_sin");
+  check_contig(positions, "positions");
+  check_contig(q_out, "q_out");
+  check_contig(slots, "slot_mapping");
+  check_contig(cache, "cache");
+  TORCH_CHECK(qkv.scalar_type() == at::kBFloat16 && q_out.scalar_type() == at::kBFloat16, "qkv/q_out bf16");
+  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.size(-1) == 128, "cos_sin fp32 [pos, 128]");
+  TORCH_CHECK(positions.scalar_type() == at::kLong && slots.scalar_type() == at::kLong, "positions/slots int64");
+  const int64_t T = qkv.size(0);
+  TORCH_CHECK(qkv.numel() == T * (hq + 2 * hkv) * 128, "qkv must be [T, (hq + 2 hkv) * 128]");
+  TORCH_CHECK(q_out.numel() == T * hq * 128, "q_out must be [T, hq, 128]");
+  TORCH_CHECK(positions.numel() == T && slots.numel() == T, "positions/slots length");
+  TORCH_CHECK(cache.scalar_type() == at::kByte && cache.size(1) == 16 * hkv * 202, "b200 cache layout");
+  c10::cuda::CUDAGuard g(cache.device());
+  check_rc(k8v4_rope_store(qkv.data_ptr(), cos_sin.data_ptr<float>(), positions.data_ptr<int64_t>(), q_out.data_ptr(),
+                           slots.data_ptr<int64_t>(), cache.data_ptr(), cache.size(0), (int)cache.size(1), (int)T,
+                           (int)hq, (int)hkv, cur_stream()),
+           "rope_store");
+}
+
+// ----------------------------------------------------------------- attention
+void check_attn_common(const at::Tensor& q, const at::Tensor& cu_q, const at::Tensor& seq_lens,
+                       const at::Tensor& block_table, const at::Tensor& cache, const at::Tensor& out, int64_t hkv) {
+  check_contig(q, "q");
+  check_contig(cu_q, "cu_q");
+  check_contig(seq_lens, "seq_lens");
+  check_contig(block_table, "block_table");
+  check_contig(cache, "cache");
+  check_contig(out, "out");
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && out.scalar_type() == at::kBFloat16, "q/out bf16");
+  TORCH_CHECK(q.dim() == 3 && q.size(2) == 128 && out.sizes() == q.sizes(), "q/out must be [T, hq, 128]");
+  TORCH_CHECK(cu_q.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kInt &&
+                  block_table.scalar_type() == at::kInt,
+              "cu_q / seq_lens / block_table must be int32");
+  TORCH_CHECK(block_table.dim() == 2 && block_table.size(0) == seq_lens.numel() &&
+                  cu_q.numel() == seq_lens.numel() + 1,
+              "batch metadata shapes");
+  TORCH_CHECK(cache.scalar_type() == at::kByte && cache.dim() == 2 && cache.size(1) == 16 * hkv * 202,
+              "cache must be b200 [pages, 16*hkv*202]");
+}
+
+void decode_attn(const at::Tensor& q, const at::Tensor& cu_q, const at::Tensor& seq_lens,
+                 const c10::optional<at::Tensor>& q_ends, const at::Tensor& block_table, const at::Tensor& cache,
+                 int64_t hkv, int64_t head_offset, int64_t heads, int64_t gqa, int64_t max_q_len, int64_t nsplit,
+                 double sm_scale, at::Tensor& out, const c10::optional<at::Tensor>& ws) {
+  check_attn_common(q, cu_q, seq_lens, block_table, cache, out, hkv);
+  TORCH_CHECK(max_q_len * gqa <= 64, "decode tile holds at most 64 query rows per KV head");
+  TORCH_CHECK(head_offset >= 0 && heads >= 1 && head_offset + heads <= hkv, "head range");
+  TORCH_CHECK(q.size(1) == hkv * gqa || q.size(1) == heads * gqa, "q heads vs layout");
+  const int32_t* qe = nullptr;
+  if (q_ends.has_value()) {
+    check_contig(*q_ends, "q_ends");
+    TORCH_CHECK(q_ends->scalar_type() == at::kInt && q_ends->numel() == q.size(0), "q_ends int32 [T]");
+    qe = q_ends->data_ptr<int32_t>();
+  }
+  const int nseq = (int)seq_lens.numel();
+  float* ws_o = nullptr;
+  float* ws_ml = nullptr;
+  if (nsplit > 1) {
+    TORCH_CHECK(ws.has_value(), "nsplit > 1 needs a workspace");
+    check_contig(*ws, "ws");
+    TORCH_CHECK(ws->scalar_type() == at::kFloat, "ws fp32");
+    const int64_t need = k8v4_decode_ws_floats(nseq, (int)heads, (int)nsplit, (int)max_q_len, (int)gqa);
+    TORCH_CHECK(ws->numel() >= need, "decode workspace too small: need ", need, " floats");
+    const int64_t ml = need / (128 + 2) * 2;
+    ws_ml = ws->data_ptr<float>();
+    ws_o = ws_ml + ml;
+  }
+  c10::cuda::CUDAGuard g(cache.device());
+  check_rc(k8v4_decode_attn(q.data_ptr(), cu_q.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(), qe,
+                            block_table.data_ptr<int32_t>(), (int)block_table.stride(0), cache.data_ptr(),
+                            cache.size(0), (int)hkv, (int)head_offset, (int)heads, (int)gqa, (int)q.size(1), nseq,
+                            (int)max_q_len, (int)nsplit, (float)sm_scale, out.data_ptr(), ws_o, ws_ml, cur_stream()),
+           "decode_attn");
+}
+
+int64_t decode_ws_floats(int64_t nseq, int64_t heads, int64_t nsplit, int64_t max_q_len, int64_t gqa) {
+  return k8v4_decode_ws_floats((int)nseq, (int)heads, (int)nsplit, (int)max_q_len, (int)gqa);
+}
+
+void prefill_attn(const at::Tensor& q, const at::Tensor& cu_q, const at::Tensor& seq_lens,
+                  const at::Tensor& block_table, const at::Tensor& cache, int64_t hkv, int64_t head_offset,
+                  int64_t heads, int64_t gqa, int64_t max_q_len, double sm_scale, at::Tensor& out) {
+  check_attn_common(q, cu_q, seq_lens, block_table, cache, out, hkv);
+  TORCH_CHECK(head_offset >= 0 && heads >= 1 && head_offset + heads <= hkv, "head range");
+  c10::cuda::CUDAGuard g(cache.device());
+  check_rc(k8v4_prefill_attn(q.data_ptr(), cu_q.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(),
+                             block_table.data_ptr<int32_t>(), (int)block_table.stride(0), cache.data_ptr(),
+                             cache.size(0), (int)hkv, (int)head_offset, (int)heads, (int)gqa, (int)q.size(1),
+                             (int)seq_lens.numel(), (int)max_q_len, (float)sm_scale, out.data_ptr(), cur_stream()),
+           "prefill_attn");
+}
+
+// --------------------------------------------------------------------- GEMM
+// mode 0: W4A16 (x bf16), 1: W4A8 (x int8 + xscale), 2: W8A8 (w int8 [N,K] + per-row scale).
+void wq_gemm(int64_t mode, const at::Tensor& w, const at::Tensor& wscale, const at::Tensor& x,
+             const c10::optional<at::Tensor>& xscale, const c10::optional<at::Tensor>& residual, at::Tensor& out,
+             const c10::optional<at::Tensor>& ws, int64_t split) {
+  check_contig(w, "weight");
+  check_contig(wscale, "weight scale");
+  check_contig(x, "x");
+  check_contig(out, "out");
+  TORCH_CHECK(x.dim() == 2, "x must be 2D");
+  const int64_t M = x.size(0), K = x.size(1);
+  int64_t N;
+  if (mode == 2) {
+    TORCH_CHECK(w.scalar_type() == at::kChar && w.dim() == 2 && w.size(1) == K, "W8 weight int8 [N, K]");
+    N = w.size(0);
+    TORCH_CHECK(wscale.numel() == N && wscale.scalar_type() == at::kHalf, "W8 scale fp16 [N]");
+  } else {
+    TORCH_CHECK(w.scalar_type() == at::kInt && w.dim() == 2 && w.size(0) * 8 == K, "W4 qweight int32 [K/8, N]");
+    N = w.size(1);
+    TORCH_CHECK(wscale.scalar_type() == at::kHalf && wscale.dim() == 2 && wscale.size(0) * 128 == K &&
+                    wscale.size(1) == N,
+                "W4 scales fp16 [K/128, N]");
+  }
+  TORCH_CHECK(N % 128 == 0 && K % 128 == 0, "N and K must be multiples of 128");
+  if (mode == 0) {
+    TORCH_CHECK(x.scalar_type() == at::kBFloat16, "W4A16 takes bf16 activations");
+  } else {
+    TORCH_CHECK(x.scalar_type() == at::kChar, "A8 modes take int8 activations");
+    TORCH_CHECK(xscale.has_value() && xscale->is_cuda() && xscale->scalar_type() == at::kFloat &&
+                    xscale->numel() == M,
+                "A8 modes need fp32 per-token scales");
+  }
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.dim() == 2 && out.size(0) == M && out.size(1) == N,
+              "out must be bf16 [M, N]");
+  const void* res = nullptr;
+  if (residual.has_value()) {
+    check_contig(*residual, "residual");
+    TORCH_CHECK(residual->sizes() == out.sizes() && residual->scalar_type() == at::kBFloat16, "residual shape");
+    res = residual->data_ptr();
+  }
+  float* wsp = nullptr;
+  if (split > 1) {
+    TORCH_CHECK(ws.has_value(), "split-K needs an fp32 workspace");
+    check_contig(*ws, "ws");
+    TORCH_CHECK(ws->scalar_type() == at::kFloat && ws->numel() >= M * N, "workspace [M, N] fp32");
+    wsp = ws->data_ptr<float>();
+  }
+  c10::cuda::CUDAGuard g(x.device());
+  const float* xs = (mode == 0) ? nullptr : xscale->data_ptr<float>();
+  check_rc(k8v4_wq_gemm((int)mode, w.data_ptr(), wscale.data_ptr(), x.data_ptr(), xs, res, out.data_ptr(), wsp,
+                        (int)M, (int)N, (int)K, (int)N, (int)split, cur_stream()),
+           "wq_gemm");
+  if (split > 1) {
+    check_rc(k8v4_splitk_finish(wsp, res, out.data_ptr(), M * N, 1, cur_stream()), "splitk_finish");
+  }
+}
+
+// -------------------------------------------------------------- fused misc
+void rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual, const at::Tensor& w,
+             const c10::optional<at::Tensor>& y, const c10::optional<at::Tensor>& yq,
+             const c10::optional<at::Tensor>& yscale, double eps) {
+  check_contig(x, "x");
+  check_contig(w, "weight");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "bf16 inputs");
+  const int64_t n = x.size(-1), rows = x.numel() / n;
+  TORCH_CHECK(w.numel() == n, "weight size");
+  void* r = nullptr;
+  if (residual.has_value()) {
+    check_contig(*residual, "residual");
+    TORCH_CHECK(residual->numel() == x.numel(), "residual size");
+    r = residual->data_ptr();
+  }
+  void* yp = nullptr;
+  if (y.has_value()) {
+    check_contig(*y, "y");
+    TORCH_CHECK(y->numel() == x.numel() && y->scalar_type() == at::kBFloat16, "y");
+    yp = y->data_ptr();
+  }
+  void* qp = nullptr;
+  float* sp = nullptr;
+  if (yq.has_value()) {
+    check_contig(*yq, "yq");
+    TORCH_CHECK(yq->numel() == x.numel() && yq->scalar_type() == at::kChar, "yq int8");
+    TORCH_CHECK(yscale.has_value() && yscale->numel() == rows && yscale->scalar_type() == at::kFloat, "yscale");
+    qp = yq->data_ptr();
+    sp = yscale->data_ptr<float>();
+  }
+  c10::cuda::CUDAGuard g(x.device());
+  check_rc(k8v4_rmsnorm(x.data_ptr(), r, w.data_ptr(), yp, qp, sp, (int)rows, (int)n, (float)eps, cur_stream()),
+           "rmsnorm");
+}
+
+void silu_mul(const at::Tensor& gu, const c10::optional<at::Tensor>& y, const c10::optional<at::Tensor>& yq,
+              const c10::optional<at::Tensor>& yscale) {
+  check_contig(gu, "gate_up");
+  TORCH_CHECK(gu.scalar_type() == at::kBFloat16 && gu.dim() == 2 && gu.size(1) % 2 == 0, "gate_up bf16 [T, 2I]");
+  const int64_t rows = gu.size(0), inter = gu.size(1) / 2;
+  void* yp = nullptr;
+  if (y.has_value()) {
+    check_contig(*y, "y");
+    TORCH_CHECK(y->numel() == rows * inter && y->scalar_type() == at::kBFloat16, "y");
+    yp = y->data_ptr();
+  }
+  void* qp = nullptr;
+  float* sp = nullptr;
+  if (yq.has_value()) {
+    check_contig(*yq, "yq");
+    TORCH_CHECK(yq->numel() == rows * inter && yq->scalar_type() == at::kChar, "yq");
+    TORCH_CHECK(yscale.has_value() && yscale->numel() == rows && yscale->scalar_type() == at::kFloat, "yscale");
+    qp = yq->data_ptr();
+    sp = yscale->data_ptr<float>();
+  }
+  c10::cuda::CUDAGuard g(gu.device());
+  check_rc(k8v4_silu_mul(gu.data_ptr(), yp, qp, sp, (int)rows, (int)inter, cur_stream()), "silu_mul");
+}
+
+void quant_rows(const at::Tensor& x, at::Tensor& q, at::Tensor& scale) {
+  check_contig(x, "x");
+  check_contig(q, "q");
+  check_contig(scale, "scale");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && q.scalar_type() == at::kChar && scale.scalar_type() == at::kFloat,
+              "dtypes");
+  const int64_t n = x.size(-1), rows = x.numel() / n;
+  TORCH_CHECK(q.numel() == x.numel() && scale.numel() == rows, "shapes");
+  c10::cuda::CUDAGuard g(x.device());
+  check_rc(k8v4_quant_rows(x.data_ptr(), q.data_ptr(), scale.data_ptr<float>(), (int)rows, (int)n, cur_stream()),
+           "quant_rows");
+}
+
+void embed_int8(const at::Tensor& ids, const at::Tensor& codes, const at::Tensor& scales, at::Tensor& out,
+                int64_t start) {
+  check_contig(ids, "ids");
+  check_contig(codes, "codes");
+  check_contig(scales, "scales");
+  check_contig(out, "out");
+  TORCH_CHECK(ids.scalar_type() == at::kLong && codes.scalar_type() == at::kChar && scales.scalar_type() == at::kHalf &&
+                  out.scalar_type() == at::kBFloat16,
+              "dtypes");
+  TORCH_CHECK(codes.dim() == 2 && scales.numel() == codes.size(0) && out.numel() == ids.numel() * codes.size(1),
+              "shapes");
+  c10::cuda::CUDAGuard g(out.device());
+  check_rc(k8v4_embed_int8(ids.data_ptr<int64_t>(), codes.data_ptr(), scales.data_ptr(), out.data_ptr(),
+                           (int)ids.numel(), (int)codes.size(1), start, codes.size(0), cur_stream()),
+           "embed_int8");
+}
+
+void argmax(const at::Tensor& logits, int64_t offset, at::Tensor& best_val, at::Tensor& best_idx) {
+  check_contig(logits, "logits");
+  check_contig(best_val, "best_val");
+  check_contig(best_idx, "best_idx");
+  TORCH_CHECK(logits.scalar_type() == at::kBFloat16 && logits.dim() == 2, "logits bf16 [rows, vocab]");
+  TORCH_CHECK(best_val.scalar_type() == at::kFloat && best_idx.scalar_type() == at::kLong &&
+                  best_val.numel() == logits.size(0) && best_idx.numel() == logits.size(0),
+              "outputs");
+  c10::cuda::CUDAGuard g(logits.device());
+  check_rc(k8v4_argmax(logits.data_ptr(), (int)logits.size(0), (int)logits.size(1), offset,
+                       best_val.data_ptr<float>(), best_idx.data_ptr<int64_t>(), cur_stream()),
+           "argmax");
+}
+
+// Read (and optionally clear) the device status words of every kernel unit.
+int64_t status(bool clear) {
+  int v = 0;
+  const int c = clear ? 1 : 0;
+  int s[6] = {k8v4_status_gemm(c), k8v4_status_store(c), k8v4_status_misc(c), k8v4_status_decode(c),
+              k8v4_status_prefill(c), k8v4_status_sampler(c)};
+  for (int i = 0; i < 6; ++i)
+    if (s[i]) v = s[i];
+  return v;
+}
+
+}  // namespace
+
+TORCH_LIBRARY(k8v4, m) {
+  m.def("kv_store(int fmt, Tensor k, Tensor v, Tensor slot_mapping, Tensor(a!) cache, int hkv) -> ()");
+  m.def(
+      "rope_store(Tensor qkv, Tensor cos_sin, Tensor positions, Tensor(a!) q_out, Tensor slot_mapping, "
+      "Tensor(b!) cache, int hq, int hkv) -> ()");
+  m.def(
+      "decode_attn(Tensor q, Tensor cu_q, Tensor seq_lens, Tensor? q_ends, Tensor block_table, Tensor cache, "
+      "int hkv, int head_offset, int heads, int gqa, int max_q_len, int nsplit, float sm_scale, Tensor(a!) out, "
+      "Tensor(b!)? ws) -> ()");
+  m.def("decode_ws_floats(int nseq, int heads, int nsplit, int max_q_len, int gqa) -> int");
+  m.def(
+      "prefill_attn(Tensor q, Tensor cu_q, Tensor seq_lens, Tensor block_table, Tensor cache, int hkv, "
+      "int head_offset, int heads, int gqa, int max_q_len, float sm_scale, Tensor(a!) out) -> ()");
+  m.def(
+      "wq_gemm(int mode, Tensor w, Tensor wscale, Tensor x, Tensor? xscale, Tensor? residual, Tensor(a!) out, "
+      "Tensor(b!)? ws, int split) -> ()");
+  m.def(
+      "rmsnorm(Tensor x, Tensor(a!)? residual, Tensor w, Tensor(b!)? y, Tensor(c!)? yq, Tensor(d!)? yscale, "
+      "float eps) -> ()");
+  m.def("silu_mul(Tensor gate_up, Tensor(a!)? y, Tensor(b!)? yq, Tensor(c!)? yscale) -> ()");
+  m.def("quant_rows(Tensor x, Tensor(a!) q, Tensor(b!) scale) -> ()");
+  m.def("embed_int8(Tensor ids, Tensor codes, Tensor scales, Tensor(a!) out, int start) -> ()");
+  m.def("argmax(Tensor logits, int offset, Tensor(a!) best_val, Tensor(b!) best_idx) -> ()");
+  m.def("status(bool clear) -> int");
+}
+
+TORCH_LIBRARY_IMPL(k8v4, CUDA, m) {
+  m.impl("kv_store", &kv_store);
+  m.impl("rope_store", &rope_store);
+  m.impl("decode_attn", &decode_attn);
+  m.impl("prefill_attn", &prefill_attn);
+  m.impl("wq_gemm", &wq_gemm);
+  m.impl("rmsnorm", &rmsnorm);
+  m.impl("silu_mul", &silu_mul);
+  m.impl("quant_rows", &quant_rows);
+  m.impl("embed_int8", &embed_int8);
+  m.impl("argmax", &argmax);
+}
+
+TORCH_LIBRARY_IMPL(k8v4, CompositeExplicitAutograd, m) {
+  m.impl("decode_ws_floats", &decode_ws_floats);
+  m.impl("status", &status);
+}

@@ -1,0 +1,70 @@
+// Shared device helpers for the k8v4 sm_100a kernel library.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#ifndef K8V4_HOST_DEVICE
+#define K8V4_HOST_DEVICE __host__ __device__
+#endif
+
+namespace k8v4 {
+
+// Error codes written into the library's device status word when a kernel
+// gives up instead of waiting forever (bounded waits) or rejects its inputs.
+enum : int {
+  kOk = 0,
+  kErrMbarTimeout = 1,     // an mbarrier wait ran past its time limit
+  kErrPeerTimeout = 2,     // a wait on a peer GPU's flag ran past its limit
+  kErrBadShape = 3,        // device-side shape guard tripped
+  kErrBadIndex = 4,        // device-side bounds guard tripped (debug builds)
+};
+
+// Nanoseconds a device-side wait may spin before it records a timeout.
+#ifndef K8V4_WAIT_LIMIT_NS
+#define K8V4_WAIT_LIMIT_NS 2000000000ull
+#endif
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Device status word of this translation unit (one per device that loaded
+// the library). Each .cu file exports a reader through K8V4_STATUS_API.
+static __device__ int g_k8v4_status;
+
+#define K8V4_STATUS_API(unit)                                              \
+  extern "C" int k8v4_status_##unit(int clear) {                           \
+    int v = 0;                                                             \
+    cudaMemcpyFromSymbol(&v, k8v4::g_k8v4_status, sizeof(int));            \
+    if (clear && v) {                                                      \
+      int z = 0;                                                           \
+      cudaMemcpyToSymbol(k8v4::g_k8v4_status, &z, sizeof(int));            \
+    }                                                                      \
+    return v;                                                              \
+  }
+
+__device__ __forceinline__ void record_error(int code) {
+  atomicCAS(&g_k8v4_status, 0, code);
+}
+
+__device__ __forceinline__ float bf2f(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ __nv_bfloat16 f2bf(float v) { return __float2bfloat16_rn(v); }
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+K8V4_HOST_DEVICE inline int cdiv(int a, int b) { return (a + b - 1) / b; }
+
+}  // namespace k8v4

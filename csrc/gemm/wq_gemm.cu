@@ -1,0 +1,441 @@
+// Quantized-weight GEMM on tcgen05: Y[t, n] = sum_k X[t, k] * W[n, k].
+//
+// Weights are the MMA "A" operand (128 output features per CTA = the TMEM
+// lanes) and tokens are the MMA "N" dimension (BT = 16..128 per CTA), so one
+// kernel serves decode (a handful of tokens) and prefill (thousands).
+//
+//   mode W4A16 : GPTQ int4 (group 128, symmetric, codes q+8) x bf16 tokens.
+//                Converter warps turn each int4 code into the exact bf16
+//                integer (q-8); tcgen05.mma.kind::f16 accumulates one K group
+//                into a TMEM partial; accumulator warps fold the fp32 group
+//                scale in: acc += partial * scale[g][n].
+//   mode W4A8  : same weights x int8 tokens (per-token scale). Converters
+//                emit int8 (q-8); tcgen05.mma.kind::i8 gives an int32 group
+//                partial; accumulator warps rescale in fp32 and apply the
+//                token scale at the end. (reference: int4_gemm_w4a8 called at
+//                k8v4_v030/w4a8_prefill.py:146-157)
+//   mode W8A8  : int8 per-row weights (lm_head) x int8 tokens; the weight
+//                tile goes straight from TMA into the MMA, one group = all K.
+//
+// Roles: warp 0 issues TMA, warp 1 owns TMEM and issues MMAs (one elected
+// thread), the next NCONV warps convert raw weights, the last NACC warps
+// accumulate TMEM partials and write the output. TMEM partials are double
+// buffered so group g+1's MMAs overlap group g's rescale.
+//
+// Split-K: gridDim.z slices K; with more than one slice the CTA adds fp32
+// partial sums into `ws` with red.global.add and a finishing kernel converts.
+#include "../tc.cuh"
+
+namespace k8v4 {
+namespace gemm {
+
+using namespace tc;
+
+enum Mode : int { W4A16 = 0, W4A8 = 1, W8A8 = 2 };
+
+struct Params {
+  const int32_t* qweight;      // W4: [K/8, N] int32 (GPTQ, low nibble first)
+  const __half* wscale;        // W4: [K/128, N]; W8: [N]
+  const float* xscale;         // A8: [M] per-token scale
+  const __nv_bfloat16* residual;  // optional [M, ldo]
+  __nv_bfloat16* out;          // [M, ldo] (split == 1)
+  float* ws;                   // [M, ldo] fp32 accumulation (split > 1)
+  int M, N, K, ldo;
+  int k_per_split;             // multiple of 128
+};
+
+template <int MODE, int BT, int NCONV, int NACC, int STAGES, int RSTAGES>
+struct Cfg {
+  static constexpr int BK = (MODE == W4A16) ? 64 : 128;    // k per stage (128-byte rows)
+  static constexpr int KB_PER_GROUP = (MODE == W4A16) ? 2 : 1;  // stages per K group (W8: all)
+  static constexpr int A_BYTES = 128 * 128;                // 128 rows x 128 B
+  static constexpr int B_BYTES = BT * 128;
+  static constexpr int RAW_BYTES = (MODE == W8A8) ? 0 : (BK / 8) * 128 * 4;
+  static constexpr int NWARPS = 2 + NCONV + NACC;
+  static constexpr int NTHREADS = NWARPS * 32;
+  static constexpr int TMEM_COLS = (2 * BT < 32) ? 32 : 2 * BT;
+  static constexpr int ACC_SPLIT = NACC / 4;               // column slices per lane quadrant
+  static constexpr int COLS = BT / ACC_SPLIT;              // columns per accumulator thread
+  static constexpr int UMMA_K = (MODE == W4A16) ? 16 : 32;
+  static constexpr int SMEM_BYTES =
+      1024 + STAGES * (A_BYTES + B_BYTES) + RSTAGES * RAW_BYTES + 1024;
+  static_assert(NACC == 4 || NACC == 8, "accumulator warps cover the 4 lane quadrants");
+  static_assert(COLS % 8 == 0, "columns per accumulator thread");
+  static_assert(BT % 16 == 0 && BT >= 16 && BT <= 256, "MMA N");
+};
+
+// int4 x 8 (GPTQ low nibble first) -> 8 exact bf16 values (q-8) as 4 words.
+__device__ __forceinline__ void int4x8_to_bf16(uint32_t w, uint32_t (&o)[4]) {
+  // Byte j of w holds codes (2j, 2j+1); byte j of w>>4 holds code 2j+1 in its
+  // low nibble. One byte_perm puts code 2j in bits 0-3 and code 2j+1 in bits
+  // 16-19; OR-ing exponent 2^7 (bf16 ulp 1) makes the pair (128+c0, 128+c1)
+  // and one bf16x2 subtraction of 136 leaves (c0-8, c1-8) exactly.
+  const uint32_t w4 = w >> 4;
+  const __nv_bfloat162 bias = __halves2bfloat162(__float2bfloat16(136.0f), __float2bfloat16(136.0f));
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t dup = __byte_perm(w, w4, 0x0400 + j * 0x0101);
+    const uint32_t m = (dup & 0x000F000Fu) | 0x43004300u;
+    __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(&m);
+    v = __hsub2(v, bias);
+    o[j] = *reinterpret_cast<uint32_t*>(&v);
+  }
+}
+
+// int4 x 8 -> 8 int8 values (q-8) as 2 words (bytes in k order).
+__device__ __forceinline__ void int4x8_to_s8(uint32_t w, uint32_t& o0, uint32_t& o1) {
+  const uint32_t lo = (w & 0x0F0F0F0Fu) | 0x80808080u;         // codes 0,2,4,6
+  const uint32_t hi = ((w >> 4) & 0x0F0F0F0Fu) | 0x80808080u;  // codes 1,3,5,7
+  uint32_t a = __byte_perm(lo, hi, 0x5140);                     // 0,1,2,3
+  uint32_t b = __byte_perm(lo, hi, 0x7362);                     // 4,5,6,7
+  // per-byte (c | 0x80) - 8 never borrows across bytes; xor restores sign.
+  o0 = (a - 0x08080808u) ^ 0x80808080u;
+  o1 = (b - 0x08080808u) ^ 0x80808080u;
+}
+
+// Exact int32 -> fp32 for |v| < 2^22 with full-rate integer/float ops.
+__device__ __forceinline__ float i2f_small(uint32_t v) {
+  return __int_as_float(static_cast<int>(v) + 0x4B400000) - 12582912.0f;
+}
+
+template <int MODE, int BT, int NCONV, int NACC, int STAGES, int RSTAGES>
+__global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES>::NTHREADS, 1)
+    wq_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
+                   const Params p) {
+  using C = Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + STAGES * C::A_BYTES;
+  uint8_t* sR = sB + STAGES * C::B_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sR + RSTAGES * C::RAW_BYTES);
+  uint64_t* a_full = bars;                 // converters (or TMA for W8) -> MMA
+  uint64_t* b_full = a_full + STAGES;      // TMA -> MMA
+  uint64_t* ab_empty = b_full + STAGES;    // MMA -> TMA / converters
+  uint64_t* r_full = ab_empty + STAGES;    // TMA -> converters
+  uint64_t* r_empty = r_full + RSTAGES;    // converters -> TMA
+  uint64_t* acc_full = r_empty + RSTAGES;  // MMA -> accumulators (2)
+  uint64_t* acc_empty = acc_full + 2;      // accumulators -> MMA (2)
+  uint64_t* done_bar = acc_empty + 2;     // MMA drain on exit
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * 128;
+  const int t0 = blockIdx.y * BT;
+  const int kbeg = blockIdx.z * p.k_per_split;
+  const int kend = min(p.K, kbeg + p.k_per_split);
+  const int nkb = (kend - kbeg) / C::BK;
+  const int kb_per_group = (MODE == W8A8) ? nkb : C::KB_PER_GROUP;
+  const int ngroups = (MODE == W8A8) ? 1 : nkb / kb_per_group;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&a_full[s], (MODE == W8A8) ? 1 : NCONV);
+      mbar_init(&b_full[s], 1);
+      mbar_init(&ab_empty[s], 1);
+    }
+    for (int s = 0; s < RSTAGES; ++s) {
+      mbar_init(&r_full[s], 1);
+      mbar_init(&r_empty[s], NCONV);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&acc_full[s], 1);
+      mbar_init(&acc_empty[s], NACC);
+    }
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0 && nkb > 0) {
+      prefetch_tmap(&tm_w);
+      prefetch_tmap(&tm_x);
+      int rs = 0, rphase = 0, issued = 0, raw_issued = 0;
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (kb / STAGES) & 1;
+        const int k0 = kbeg + kb * C::BK;
+        if (MODE != W8A8) {
+          if (kb >= RSTAGES && !mbar_wait(&r_empty[rs], rphase ^ 1, abort_flag)) break;
+          mbar_arrive_expect_tx(&r_full[rs], C::RAW_BYTES);
+          tma_load_2d(sR + rs * C::RAW_BYTES, &tm_w, &r_full[rs], n0, k0 / 8);
+          ++raw_issued;
+          if (++rs == RSTAGES) { rs = 0; rphase ^= 1; }
+        }
+        if (kb >= STAGES && !mbar_wait(&ab_empty[s], ph ^ 1, abort_flag)) break;
+        if (MODE == W8A8) {
+          mbar_arrive_expect_tx(&a_full[s], C::A_BYTES);
+          tma_load_2d(sA + s * C::A_BYTES, &tm_w, &a_full[s], k0, n0);
+        }
+        mbar_arrive_expect_tx(&b_full[s], C::B_BYTES);
+        tma_load_2d(sB + s * C::B_BYTES, &tm_x, &b_full[s], k0, t0);
+        ++issued;
+      }
+      if (*abort_flag) {
+        // Wait (bounded) for this CTA's own copies still in flight.
+        for (int kb = issued - 1; kb >= 0 && kb >= issued - STAGES; --kb) {
+          mbar_wait_drain(&b_full[kb % STAGES], (kb / STAGES) & 1);
+          if (MODE == W8A8) mbar_wait_drain(&a_full[kb % STAGES], (kb / STAGES) & 1);
+        }
+        if (MODE != W8A8)
+          for (int kb = raw_issued - 1; kb >= 0 && kb >= raw_issued - RSTAGES; --kb)
+            mbar_wait_drain(&r_full[kb % RSTAGES], (kb / RSTAGES) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------------- MMA
+    if (lane == 0 && nkb > 0) {
+      const uint32_t idesc = (MODE == W4A16) ? idesc_bf16(128, BT) : idesc_s8(128, BT);
+      bool ok = true;
+      for (int g = 0; g < ngroups && ok; ++g) {
+        const int buf = g & 1;
+        if (g >= 2 && !mbar_wait(&acc_empty[buf], ((g >> 1) - 1) & 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t dtm = tmem + buf * BT;
+        for (int j = 0; j < kb_per_group; ++j) {
+          const int kb = g * kb_per_group + j;
+          const int s = kb % STAGES;
+          const uint32_t ph = (kb / STAGES) & 1;
+          if (!mbar_wait(&a_full[s], ph, abort_flag) || !mbar_wait(&b_full[s], ph, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + s * C::A_BYTES);
+          const uint32_t b_base = smem_u32(sB + s * C::B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < C::BK / C::UMMA_K; ++kk) {
+            const uint64_t ad = sdesc_sw128(a_base + kk * 32, 16, 1024);
+            const uint64_t bd = sdesc_sw128(b_base + kk * 32, 16, 1024);
+            if (MODE == W4A16)
+              mma_f16(dtm, ad, bd, idesc, (j > 0 || kk > 0) ? 1u : 0u);
+            else
+              mma_i8(dtm, ad, bd, idesc, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(&ab_empty[s]);
+        }
+        if (ok) mma_commit(&acc_full[buf]);
+      }
+      // Every MMA this thread issued must finish before TMEM is released.
+      mma_commit(done_bar);
+      mbar_wait_drain(done_bar, 0);
+    }
+  } else if (warp < 2 + NCONV) {
+    // ---------------------------------------------------------- converters
+    if (MODE != W8A8) {
+      const int ct = threadIdx.x - 64;  // 0 .. NCONV*32-1
+      int rs = 0, rphase = 0;
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (kb / STAGES) & 1;
+        if (!mbar_wait(&r_full[rs], rphase, abort_flag)) break;
+        if (kb >= STAGES && !mbar_wait(&ab_empty[s], ph ^ 1, abort_flag)) break;
+        const uint32_t* raw = reinterpret_cast<const uint32_t*>(sR + rs * C::RAW_BYTES);
+        uint8_t* dst = sA + s * C::A_BYTES;
+#pragma unroll 4
+        for (int item = ct; item < 1024; item += NCONV * 32) {
+          const int f = item & 127;
+          const int c = item >> 7;
+          uint4 v;
+          if (MODE == W4A16) {
+            uint32_t o[4];
+            int4x8_to_bf16(raw[c * 128 + f], o);
+            v = make_uint4(o[0], o[1], o[2], o[3]);
+          } else {
+            uint32_t o0, o1, o2, o3;
+            int4x8_to_s8(raw[(2 * c) * 128 + f], o0, o1);
+            int4x8_to_s8(raw[(2 * c + 1) * 128 + f], o2, o3);
+            v = make_uint4(o0, o1, o2, o3);
+          }
+          *reinterpret_cast<uint4*>(dst + sw128_offset(f, c)) = v;
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&r_empty[rs]);
+          mbar_arrive(&a_full[s]);
+        }
+        if (++rs == RSTAGES) { rs = 0; rphase ^= 1; }
+      }
+    }
+  } else {
+    // --------------------------------------------------------- accumulators
+    const int aw = warp - 2 - NCONV;  // 0 .. NACC-1
+    const int quad = warp & 3;        // TMEM lane quadrant this warp may access
+    const int slice = aw / 4;         // column slice
+    const int row = quad * 32 + lane; // feature within the tile
+    const int n = n0 + row;
+    const int c0 = slice * C::COLS;
+    float acc[C::COLS];
+#pragma unroll
+    for (int i = 0; i < C::COLS; ++i) acc[i] = 0.f;
+    bool ok = nkb > 0;
+    for (int g = 0; g < ngroups && ok; ++g) {
+      const int buf = g & 1;
+      if (!mbar_wait(&acc_full[buf], (g >> 1) & 1, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      float gs = 1.f;
+      if (MODE != W8A8 && n < p.N) gs = __half2float(p.wscale[(size_t)((kbeg / 128) + g) * p.N + n]);
+      const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + buf * BT + c0;
+#pragma unroll
+      for (int cc = 0; cc < C::COLS; cc += 8) {
+        uint32_t r[8];
+        tmem_ld8(taddr + cc, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float v = (MODE == W4A16) ? __uint_as_float(r[i]) : ((MODE == W4A8) ? i2f_small(r[i]) : (float)(int)r[i]);
+          acc[cc + i] = fmaf(v, gs, acc[cc + i]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+    if (ok && n < p.N) {
+      const float rs = (MODE == W8A8) ? __half2float(p.wscale[n]) : 1.f;
+#pragma unroll
+      for (int i = 0; i < C::COLS; ++i) {
+        const int t = t0 + c0 + i;
+        if (t < p.M) {
+          float v = acc[i] * rs;
+          if (MODE != W4A16) v *= p.xscale[t];
+          const size_t o = (size_t)t * p.ldo + n;
+          if (gridDim.z > 1) {
+            atomicAdd(p.ws + o, v);
+          } else {
+            if (p.residual) v += __bfloat162float(p.residual[o]);
+            p.out[o] = __float2bfloat16_rn(v);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// -------------------------------------------------------------------- host
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// 2D row-major tensor map: inner dim `cols` (elements), `rows` rows, row stride in bytes.
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t cols,
+                 uint64_t rows, uint64_t row_stride_bytes, uint32_t box_cols, uint32_t box_rows, bool swizzle128) {
+  EncodeTiledFn enc = get_encode();
+  if (!enc) return -1;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  (void)elem_bytes;
+  CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -2;
+}
+
+template <int MODE, int BT, int NCONV, int NACC, int STAGES, int RSTAGES>
+static int launch_cfg(const void* w, const void* x, const Params& p, int split, cudaStream_t st) {
+  using C = Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES>;
+  CUtensorMap tw, tx;
+  int rc;
+  if (MODE == W8A8)
+    rc = make_tmap_2d(&tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.K, p.N, p.K, 128, 128, true);
+  else
+    rc = make_tmap_2d(&tw, w, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, p.N, p.K / 8, (uint64_t)p.N * 4, 128, C::BK / 8,
+                      false);
+  if (rc) return 100 + rc;
+  if (MODE == W4A16)
+    rc = make_tmap_2d(&tx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.K, p.M, (uint64_t)p.K * 2, 64, BT, true);
+  else
+    rc = make_tmap_2d(&tx, x, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.K, p.M, p.K, 128, BT, true);
+  if (rc) return 200 + rc;
+  auto kern = wq_gemm_kernel<MODE, BT, NCONV, NACC, STAGES, RSTAGES>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    attr_set = true;
+  }
+  dim3 grid(cdiv(p.N, 128), cdiv(p.M, BT), split);
+  kern<<<grid, C::NTHREADS, C::SMEM_BYTES, st>>>(tw, tx, p);
+  return cudaGetLastError() == cudaSuccess ? 0 : 300;
+}
+
+}  // namespace gemm
+}  // namespace k8v4
+
+using namespace k8v4;
+using namespace k8v4::gemm;
+
+K8V4_STATUS_API(gemm)
+
+// Tokens per CTA for a given M: small M streams weights (decode), large M
+// reuses each converted weight tile over 128 tokens (prefill).
+extern "C" int k8v4_wq_gemm(int mode, const void* w, const void* wscale, const void* x, const float* xscale,
+                            const void* residual, void* out, float* ws, int M, int N, int K, int ldo, int split,
+                            cudaStream_t st) {
+  if (N % 128 || K % 128 || M <= 0) return 1;
+  if (split < 1) split = 1;
+  const int kgroups = K / 128;
+  if (split > kgroups) split = kgroups;
+  Params p;
+  p.qweight = reinterpret_cast<const int32_t*>(w);
+  p.wscale = reinterpret_cast<const __half*>(wscale);
+  p.xscale = xscale;
+  p.residual = reinterpret_cast<const __nv_bfloat16*>(residual);
+  p.out = reinterpret_cast<__nv_bfloat16*>(out);
+  p.ws = ws;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.ldo = ldo;
+  p.k_per_split = cdiv(kgroups, split) * 128;
+  split = cdiv(K, p.k_per_split);
+  if (split > 1 && !ws) return 2;
+  if (mode == W4A16) {
+    if (M <= 16) return launch_cfg<W4A16, 16, 8, 4, 4, 16>(w, x, p, split, st);
+    if (M <= 32) return launch_cfg<W4A16, 32, 8, 4, 4, 16>(w, x, p, split, st);
+    if (M <= 64) return launch_cfg<W4A16, 64, 8, 4, 4, 12>(w, x, p, split, st);
+    return launch_cfg<W4A16, 128, 4, 8, 4, 8>(w, x, p, split, st);
+  }
+  if (mode == W4A8) {
+    if (M <= 32) return launch_cfg<W4A8, 32, 8, 4, 4, 8>(w, x, p, split, st);
+    return launch_cfg<W4A8, 128, 4, 8, 4, 4>(w, x, p, split, st);
+  }
+  if (mode == W8A8) {
+    if (M <= 32) return launch_cfg<W8A8, 32, 4, 4, 6, 1>(w, x, p, split, st);
+    return launch_cfg<W8A8, 128, 4, 8, 4, 1>(w, x, p, split, st);
+  }
+  return 3;
+}

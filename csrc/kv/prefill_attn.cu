@@ -1,0 +1,424 @@
+// Paged causal prefill attention directly on int8-K / int4-V pages.
+//
+// Replaces the reference's per-KV-head gather + oneDNN SDPA pipeline
+// (k8v4_v030/onednn_prefill.py:188-241, native/k8v4_sdpa.cpp:83-228 and the
+// Triton gather prefill_gather_triton.py:15-66): no fp16 copy of the prefix is
+// materialized, nothing is compiled per shape and there are no host waits.
+//
+// One CTA per (query tile, KV head, sequence). A query tile is TQ = 128/gqa
+// consecutive tokens x the gqa query heads of this KV head = up to 128 rows,
+// so every K/V tile read serves all grouped heads. Causality is bottom-right:
+// the chunk's tokens are the last q_len tokens of the sequence.
+//
+//   S[row, key]  = Q8(int8, per-row scale) x K_tile^T      tcgen05 kind::i8
+//   softmax      : one thread per row, lazy rescale (tau 8, log2 units)
+//   O[row, dim] += P(fp16) x V_tile(fp16, MN-major)         tcgen05 kind::f16
+//
+// Warp roles: 0 = TMA producer, 1 = TMEM owner + MMA issuer, 2-5 = V
+// converters, 6-9 = softmax / epilogue (thread = TMEM lane = row).
+#include "attn_common.cuh"
+
+namespace k8v4 {
+namespace attn {
+
+using namespace tc;
+
+struct PrefillParams {
+  const __nv_bfloat16* q;      // [T, hq_total, D]
+  const int32_t* cu_q;         // [nseq + 1]
+  const int32_t* seq_lens;     // [nseq]
+  const int32_t* block_table;  // [nseq, bt_stride]
+  const uint8_t* cache;
+  __nv_bfloat16* out;          // [T, hq_total, D]
+  int bt_stride;
+  int hkv, gqa, hq_total, head_offset;
+  int n_qtiles;
+  float sm_scale_log2;
+};
+
+struct PCfg {
+  static constexpr int STAGES = 3;
+  static constexpr int NTHREADS = 320;
+  static constexpr int P_BYTES = 128 * 256;  // P fp16: 2 K-atoms of 128 rows
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_VT = OFF_K + STAGES * K_TILE_BYTES;
+  static constexpr int OFF_P = OFF_VT + 2 * VT_BYTES;
+  static constexpr int OFF_Q = OFF_P + P_BYTES;
+  static constexpr int OFF_VS = OFF_Q + 128 * 128;
+  static constexpr int OFF_MISC = OFF_VS + STAGES * VS_TILE_BYTES;
+  static constexpr int SMEM_BYTES = 1024 + OFF_MISC + 2048;
+};
+
+__global__ void __launch_bounds__(320, 1)
+    prefill_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const PrefillParams p) {
+  using C = PCfg;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = sm + C::OFF_K;
+  uint8_t* sVT = sm + C::OFF_VT;
+  uint8_t* sP = sm + C::OFF_P;
+  uint8_t* sQ = sm + C::OFF_Q;
+  uint8_t* sVS = sm + C::OFF_VS;
+  uint8_t* misc = sm + C::OFF_MISC;
+  uint64_t* kv_full = reinterpret_cast<uint64_t*>(misc);
+  uint64_t* kv_empty = kv_full + C::STAGES;
+  uint64_t* s_full = kv_empty + C::STAGES;  // [2]
+  uint64_t* p_full = s_full + 2;            // [1] P tile written
+  uint64_t* v_full = p_full + 1;            // [2]
+  uint64_t* pv_empty = v_full + 2;          // [2] PV of tile j (buffer j&1) finished
+  uint64_t* done_bar = pv_empty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  float* q_scale = reinterpret_cast<float*>(misc + 256);  // [128]
+  int* row_end = reinterpret_cast<int*>(q_scale + 128);   // [128]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = p.n_qtiles - 1 - blockIdx.x;  // longest tiles first
+  const int hl = blockIdx.y, h = hl + p.head_offset, seq = blockIdx.z;
+  const int qb = p.cu_q[seq], q_len = p.cu_q[seq + 1] - qb;
+  const int TQ = 128 / p.gqa;
+  const int t0 = qt * TQ;
+  if (t0 >= q_len) return;  // uniform for the CTA: nothing allocated yet
+  const int tq = min(TQ, q_len - t0);
+  const int R = tq * p.gqa;
+  const int seq_len = p.seq_lens[seq];
+  const int ctx = seq_len - q_len;
+  const int n_keys = ctx + t0 + tq;  // keys the last token of the tile sees
+  const int nt = (n_keys + TILE - 1) / TILE;
+  const int full_keys = ctx + t0 + 1;  // keys every row of the tile sees
+  const int32_t* bt = p.block_table + (int64_t)seq * p.bt_stride;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1 + 4 + 4);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&v_full[b], 4);
+      mbar_init(&pv_empty[b], 1);
+    }
+    mbar_init(p_full, 4);
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  // ---- prologue: quantized query rows (A operand, K-major SW128)
+  for (int r = warp; r < 128; r += 10) {
+    float x[4] = {0.f, 0.f, 0.f, 0.f};
+    int end = 0;
+    if (r < R) {
+      const int t = t0 + r / p.gqa, g = r % p.gqa;
+      const __nv_bfloat16* src = p.q + ((int64_t)(qb + t) * p.hq_total + (int64_t)h * p.gqa + g) * D + lane * 4;
+      const uint2 raw = *reinterpret_cast<const uint2*>(src);
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+      const float2 a = __bfloat1622float2(h2[0]), b = __bfloat1622float2(h2[1]);
+      x[0] = a.x; x[1] = a.y; x[2] = b.x; x[3] = b.y;
+      end = ctx + t + 1;
+    }
+    float amax = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
+    amax = warp_max(amax);
+    const float s = amax / 127.f;
+    const float inv = s > 0.f ? 1.f / s : 0.f;
+    uint32_t w = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int qi = (int)fminf(fmaxf(rintf(x[j] * inv), -127.f), 127.f);
+      w |= ((uint32_t)(uint8_t)(int8_t)qi) << (8 * j);
+    }
+    *reinterpret_cast<uint32_t*>(sQ + sw128_offset(r, lane >> 2) + (lane & 3) * 4) = w;
+    if (lane == 0) {
+      q_scale[r] = s * p.sm_scale_log2;
+      row_end[r] = end;
+    }
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const uint32_t tm_s = tmem;         // S buffers: cols [0, 256)
+  const uint32_t tm_o = tmem + 256;   // O: cols [256, 384)
+  const int n_pages = (n_keys + PAGE - 1) / PAGE;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tmap(&tm_k);
+      int issued = 0;
+      for (int j = 0; j < nt; ++j) {
+        const int s = j % C::STAGES;
+        if (j >= C::STAGES && !mbar_wait(&kv_empty[s], ((j / C::STAGES) - 1) & 1, abort_flag)) break;
+        const int pg0 = j * TILE_PAGES;
+        const int npg = min(TILE_PAGES, n_pages - pg0);
+        mbar_arrive_expect_tx(&kv_full[s], npg * (K_BYTES + VS_BYTES));
+        for (int i = 0; i < npg; ++i) {
+          const int64_t run = (int64_t)bt[pg0 + i] * p.hkv + h;
+          tma_load_3d(sK + s * K_TILE_BYTES + i * K_BYTES, &tm_k, &kv_full[s], 0, 0, (int)run);
+          bulk_load(sVS + s * VS_TILE_BYTES + i * VS_BYTES, p.cache + run * HEAD_BYTES + VS_OFF, VS_BYTES,
+                    &kv_full[s]);
+        }
+        ++issued;
+      }
+      if (*abort_flag)
+        for (int j = issued - 1; j >= 0 && j >= issued - C::STAGES; --j)
+          mbar_wait_drain(&kv_full[j % C::STAGES], (j / C::STAGES) & 1);
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------------- MMA
+    if (lane == 0) {
+      const uint32_t id_qk = idesc_s8(128, 128);
+      const uint32_t id_pv = idesc_f16(128, 128, false, true);
+      const uint32_t q_base = smem_u32(sQ);
+      const uint32_t p_base = smem_u32(sP);
+      bool ok = true;
+      for (int j = 0; j <= nt && ok; ++j) {
+        if (j < nt) {
+          const int s = j % C::STAGES, b = j & 1;
+          if (!mbar_wait(&kv_full[s], (j / C::STAGES) & 1, abort_flag)) break;
+          tc_fence_after();
+          const uint32_t k_base = smem_u32(sK + s * K_TILE_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_i8(tm_s + b * 128, sdesc_sw128(q_base + kk * 32, 16, 1024), sdesc_sw128(k_base + kk * 32, 16, 1024),
+                   id_qk, kk > 0 ? 1u : 0u);
+          mma_commit(&s_full[b]);
+          mma_commit(&kv_empty[s]);
+        }
+        if (j >= 1) {
+          const int jj = j - 1, b = jj & 1;
+          if (!mbar_wait(p_full, jj & 1, abort_flag) || !mbar_wait(&v_full[b], (jj >> 1) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t vt_base = smem_u32(sVT + b * VT_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t ad = sdesc_sw128(p_base + (kk >> 2) * (128 * 128) + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = sdesc_sw128(vt_base + kk * 2048, VT_LBO, 1024);
+            mma_f16(tm_o, ad, bd, id_pv, (jj > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(&pv_empty[b]);
+        }
+      }
+      mma_commit(done_bar);
+      mbar_wait_drain(done_bar, 0);
+    }
+  } else if (warp < 6) {
+    // ---------------------------------------------------------- converters
+    const int ct = threadIdx.x - 64;
+    for (int j = 0; j < nt; ++j) {
+      const int s = j % C::STAGES, b = j & 1;
+      if (!mbar_wait(&kv_full[s], (j / C::STAGES) & 1, abort_flag)) break;
+      // V^T buffer b was last read by PV of tile j-2
+      if (j >= 2 && !mbar_wait(&pv_empty[b], ((j >> 1) - 1) & 1, abort_flag)) break;
+      const int nvalid = min(TILE, n_keys - j * TILE);
+      const uint8_t* vs = sVS + s * VS_TILE_BYTES;
+      uint8_t* vt = sVT + b * VT_BYTES;
+#pragma unroll 4
+      for (int item = ct; item < TILE * 16; item += 128) {
+        const int key = item >> 4, chunk = item & 15;
+        if (key < nvalid) {
+          const uint8_t* run = vs + (key >> 4) * VS_BYTES;
+          const int kk = key & 15;
+          const uint32_t w = *reinterpret_cast<const uint32_t*>(run + kk * 64 + chunk * 4);
+          const __half sc = *reinterpret_cast<const __half*>(run + VSC_OFF + (kk * 4 + (chunk >> 2)) * 2);
+          v_chunk_to_f16(w, sc, vt, key, chunk);
+        } else {
+          v_chunk_zero(vt, key, chunk);
+        }
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&v_full[b]);
+        mbar_arrive(&kv_empty[s]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------- softmax
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const bool live = row < R;
+    const float qs = q_scale[row];
+    const int end = row_end[row];
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nt; ++j) {
+      const int s = j % C::STAGES, b = j & 1;
+      if (!mbar_wait(&s_full[b], (j >> 1) & 1, abort_flag) ||
+          !mbar_wait(&kv_full[s], (j / C::STAGES) & 1, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint8_t* vs = sVS + s * VS_TILE_BYTES;
+      const int key0 = j * TILE;
+      const bool masked_tile = key0 + TILE > full_keys;
+      const uint32_t s_addr = tm_s + b * 128 + lane_off;
+      // pass 1: row max of the scaled, masked scores (TMEM is read twice
+      // instead of holding 128 scores in registers)
+      float tmax = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < TILE; c += 32) {
+        uint32_t r32[32];
+        tmem_ld32(s_addr + c, r32);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int kl = c + i;
+          const float ks = __half2float(*reinterpret_cast<const __half*>(vs + (kl >> 4) * VS_BYTES + KS_OFF + (kl & 15) * 2));
+          float v = i2f_small(r32[i]) * (qs * ks);
+          if (masked_tile && key0 + kl >= end) v = -INFINITY;
+          tmax = fmaxf(tmax, v);
+        }
+      }
+      float mn = m_run, a = 1.f;
+      if (tmax > m_run + RESCALE_TAU || (m_run == -INFINITY && tmax > -INFINITY)) {
+        mn = tmax;
+        a = (m_run == -INFINITY) ? 0.f : exp2f(m_run - mn);
+      }
+      float lsum = 0.f;
+      // P (fp16) must not overwrite the buffer PV j-1 is still reading
+      if (j >= 1 && !mbar_wait(&pv_empty[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag)) { ok = false; break; }
+      if (a != 1.f && j > 0 && live) {
+        tc_fence_after();
+        // rescale this row of O
+#pragma unroll
+        for (int c = 0; c < D; c += 8) {
+          uint32_t r8[8];
+          tmem_ld8(tm_o + lane_off + c, r8);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) r8[i] = __float_as_uint(__uint_as_float(r8[i]) * a);
+          tmem_st8(tm_o + lane_off + c, r8);
+        }
+        tmem_st_wait();
+      }
+      // pass 2: probabilities -> P (fp16, K-major SW128, this thread's row)
+      uint8_t* prow = sP + row * 128;
+#pragma unroll
+      for (int c = 0; c < TILE; c += 32) {
+        uint32_t r32[32];
+        tmem_ld32(s_addr + c, r32);
+        tmem_ld_wait();
+#pragma unroll
+        for (int c8 = 0; c8 < 32; c8 += 8) {
+          uint32_t w[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            float pv[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int kl = c + c8 + 2 * i + e;
+              const float ks = __half2float(*reinterpret_cast<const __half*>(vs + (kl >> 4) * VS_BYTES + KS_OFF + (kl & 15) * 2));
+              const float v = i2f_small(r32[c8 + 2 * i + e]) * (qs * ks);
+              const bool vis = !(masked_tile && key0 + kl >= end) && mn != -INFINITY && live;
+              pv[e] = vis ? exp2f(v - mn) : 0.f;
+            }
+            lsum += pv[0] + pv[1];
+            __half2 h2 = __floats2half2_rn(pv[0], pv[1]);
+            w[i] = *reinterpret_cast<uint32_t*>(&h2);
+          }
+          const int cc = c + c8;
+          const int atom = cc >> 6, ch = (cc & 63) >> 3;
+          *reinterpret_cast<uint4*>(prow + atom * (128 * 128) + ((ch ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+      tc_fence_before();
+      // S buffer b and the k_scale reads are done
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&kv_empty[s]);
+      l_run = l_run * a + lsum;
+      m_run = mn;
+      fence_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    // ------------------------------------------------------------ epilogue
+    if (ok && nt > 0 && !mbar_wait(&pv_empty[(nt - 1) & 1], ((nt - 1) >> 1) & 1, abort_flag)) ok = false;
+    if (ok && live) {
+      tc_fence_after();
+      const int t = t0 + row / p.gqa, g = row % p.gqa;
+      __nv_bfloat16* dst = p.out + ((int64_t)(qb + t) * p.hq_total + (int64_t)h * p.gqa + g) * D;
+      const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
+#pragma unroll
+      for (int c = 0; c < D; c += 32) {
+        uint32_t r32[32];
+        tmem_ld32(tm_o + lane_off + c, r32);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          uint4 o;
+          __nv_bfloat162 b0 = __floats2bfloat162_rn(__uint_as_float(r32[i]) * inv_l, __uint_as_float(r32[i + 1]) * inv_l);
+          __nv_bfloat162 b1 = __floats2bfloat162_rn(__uint_as_float(r32[i + 2]) * inv_l, __uint_as_float(r32[i + 3]) * inv_l);
+          __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(r32[i + 4]) * inv_l, __uint_as_float(r32[i + 5]) * inv_l);
+          __nv_bfloat162 b3 = __floats2bfloat162_rn(__uint_as_float(r32[i + 6]) * inv_l, __uint_as_float(r32[i + 7]) * inv_l);
+          o.x = *reinterpret_cast<uint32_t*>(&b0);
+          o.y = *reinterpret_cast<uint32_t*>(&b1);
+          o.z = *reinterpret_cast<uint32_t*>(&b2);
+          o.w = *reinterpret_cast<uint32_t*>(&b3);
+          *reinterpret_cast<uint4*>(dst + c + i) = o;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+}  // namespace attn
+}  // namespace k8v4
+
+using namespace k8v4;
+using namespace k8v4::attn;
+
+extern "C" int k8v4_make_kv_tmap(void* map_out, const void* cache, int64_t num_pages, int hkv);
+
+K8V4_STATUS_API(prefill)
+
+// Paged causal prefill over `heads` KV heads starting at head_offset.
+extern "C" int k8v4_prefill_attn(const void* q, const int32_t* cu_q, const int32_t* seq_lens,
+                                 const int32_t* block_table, int bt_stride, const void* cache, int64_t num_pages,
+                                 int hkv, int head_offset, int heads, int gqa, int hq_total, int nseq, int max_q_len,
+                                 float sm_scale, void* out, cudaStream_t st) {
+  if (nseq <= 0 || max_q_len <= 0) return 0;
+  if (gqa < 1 || 128 / gqa < 1) return 1;
+  CUtensorMap tm;
+  if (k8v4_make_kv_tmap(&tm, cache, num_pages, hkv)) return 3;
+  PrefillParams p;
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q);
+  p.cu_q = cu_q;
+  p.seq_lens = seq_lens;
+  p.block_table = block_table;
+  p.cache = reinterpret_cast<const uint8_t*>(cache);
+  p.out = reinterpret_cast<__nv_bfloat16*>(out);
+  p.bt_stride = bt_stride;
+  p.hkv = hkv;
+  p.gqa = gqa;
+  p.hq_total = hq_total;
+  p.head_offset = head_offset;
+  p.n_qtiles = cdiv(max_q_len, 128 / gqa);
+  p.sm_scale_log2 = sm_scale * LOG2E;
+  static bool set = false;
+  if (!set) {
+    cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PCfg::SMEM_BYTES);
+    set = true;
+  }
+  dim3 grid(p.n_qtiles, heads, nseq);
+  prefill_attn_kernel<<<grid, PCfg::NTHREADS, PCfg::SMEM_BYTES, st>>>(tm, p);
+  return cudaGetLastError() == cudaSuccess ? 0 : 10;
+}

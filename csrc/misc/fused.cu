@@ -1,0 +1,283 @@
+// Memory-bound fused elementwise kernels around the GEMMs:
+//   * RMSNorm with optional residual add and optional per-token int8 output
+//     (the activation quantization of the W4A8 path, reference
+//     k8v4_v030/w4a8_prefill.py:192-203, fused into the norm that produces it)
+//   * SiLU(gate) * up with optional per-token int8 output
+//   * INT8 embedding lookup (codes x per-row fp16 scale, vocab-sharded;
+//     reference k8v4_v030/embed_int8_runtime.py:53-56)
+//   * split-K finish: fp32 partial sums -> bf16 (+ residual)
+//   * per-token int8 quantization of bf16 rows
+// One CTA per token row; 16-byte vector loads; fp32 math.
+#include "../common.cuh"
+
+namespace k8v4 {
+namespace misc {
+
+constexpr int kThreads = 256;
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = (l < (int)(blockDim.x >> 5)) ? red[l] : 0.f;
+  return warp_sum(t);
+}
+__device__ __forceinline__ float block_max(float v, float* red) {
+  v = warp_max(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = (l < (int)(blockDim.x >> 5)) ? red[l] : 0.f;
+  return warp_max(t);
+}
+
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&f)[8]) {
+  const uint4 raw = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 v = __bfloat1622float2(h[j]);
+    f[2 * j] = v.x;
+    f[2 * j + 1] = v.y;
+  }
+}
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&f)[8]) {
+  uint4 raw;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(f[2 * j], f[2 * j + 1]);
+  *reinterpret_cast<uint4*>(p) = raw;
+}
+
+// Quantize the row held in registers (VPT vectors of 8 per thread) to int8
+// with scale amax/127 (clamped to >= 1e-5 like the reference), write codes
+// and the fp32 scale.
+template <int VPT>
+__device__ __forceinline__ void quant_row(const float (&v)[VPT][8], int n, int8_t* q, float* scale, float* red) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = (threadIdx.x + i * kThreads) * 8;
+    if (c < n)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[i][j]));
+  }
+  amax = block_max(amax, red);
+  const float s = fmaxf(amax / 127.f, 1e-5f);
+  const float inv = 1.f / s;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = (threadIdx.x + i * kThreads) * 8;
+    if (c < n) {
+      uint32_t w[2] = {0, 0};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int qi = (int)fminf(fmaxf(rintf(v[i][j] * inv), -127.f), 127.f);
+        w[j >> 2] |= ((uint32_t)(uint8_t)(int8_t)qi) << (8 * (j & 3));
+      }
+      *reinterpret_cast<uint2*>(q + c) = make_uint2(w[0], w[1]);
+    }
+  }
+  if (threadIdx.x == 0) *scale = s;
+}
+
+// x: [T, n] bf16. If residual != nullptr: h = x + residual, residual <- h.
+// y = h * rsqrt(mean(h^2) + eps) * w. Outputs bf16 y and/or int8 y + scale.
+template <int VPT>
+__global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const __nv_bfloat16* __restrict__ x,
+                                                           __nv_bfloat16* residual, const __nv_bfloat16* __restrict__ w,
+                                                           __nv_bfloat16* y, int8_t* yq, float* yscale, int n,
+                                                           float eps) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  float v[VPT][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = (threadIdx.x + i * kThreads) * 8;
+    if (c < n) {
+      load8(x + row * n + c, v[i]);
+      if (residual) {
+        float r[8];
+        load8(residual + row * n + c, r);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] += r[j];
+        // the residual stream is kept in bf16
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = __bfloat162float(__float2bfloat16_rn(v[i][j]));
+        store8(residual + row * n + c, v[i]);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+    }
+  }
+  ss = block_sum(ss, red);
+  const float inv = rsqrtf(ss / (float)n + eps);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = (threadIdx.x + i * kThreads) * 8;
+    if (c < n) {
+      float g[8];
+      load8(w + c, g);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[i][j] = __bfloat162float(__float2bfloat16_rn(v[i][j] * inv)) * g[j];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[i][j] = __bfloat162float(__float2bfloat16_rn(v[i][j]));
+      if (y) store8(y + row * n + c, v[i]);
+    }
+  }
+  if (yq) quant_row<VPT>(v, n, yq + row * n, yscale + row, red);
+}
+
+// gu: [T, 2I] = [gate | up]. out = silu(gate) * up (bf16 and/or int8 + scale).
+template <int VPT>
+__global__ void __launch_bounds__(kThreads) silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* y,
+                                                            int8_t* yq, float* yscale, int inter) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  float v[VPT][8];
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = (threadIdx.x + i * kThreads) * 8;
+    if (c < inter) {
+      float g[8], u[8];
+      load8(gu + row * 2 * inter + c, g);
+      load8(gu + row * 2 * inter + inter + c, u);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float s = g[j] / (1.f + __expf(-g[j]));
+        v[i][j] = __bfloat162float(__float2bfloat16_rn(s * u[j]));
+      }
+      if (y) store8(y + row * inter + c, v[i]);
+    }
+  }
+  if (yq) quant_row<VPT>(v, inter, yq + row * inter, yscale + row, red);
+}
+
+// Row-wise int8 quantization of bf16 rows.
+template <int VPT>
+__global__ void __launch_bounds__(kThreads) quant_rows_kernel(const __nv_bfloat16* __restrict__ x, int8_t* q, float* scale,
+                                                              int n) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  float v[VPT][8];
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = (threadIdx.x + i * kThreads) * 8;
+    if (c < n) load8(x + row * n + c, v[i]);
+  }
+  quant_row<VPT>(v, n, q + row * n, scale + row, red);
+}
+
+// out[t] = codes[id - start] * scale[id - start] for ids inside [start, start + rows), else 0.
+__global__ void embed_int8_kernel(const int64_t* __restrict__ ids, const int8_t* __restrict__ codes,
+                                  const __half* __restrict__ scales, __nv_bfloat16* out, int n, int64_t start,
+                                  int64_t rows) {
+  const int64_t t = blockIdx.x;
+  const int64_t id = ids[t] - start;
+  const bool in = id >= 0 && id < rows;
+  const float s = in ? __half2float(scales[id]) : 0.f;
+  for (int c = threadIdx.x * 8; c < n; c += blockDim.x * 8) {
+    float f[8];
+    if (in) {
+      const uint2 raw = *reinterpret_cast<const uint2*>(codes + id * n + c);
+      const int8_t* b = reinterpret_cast<const int8_t*>(&raw);
+      // bf16 product of the two bf16-rounded factors, like F.embedding(..).to(bf16) * scale.to(bf16)
+      const float sb = __bfloat162float(__float2bfloat16_rn(s));
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f[j] = (float)b[j] * sb;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f[j] = 0.f;
+    }
+    store8(out + t * n + c, f);
+  }
+}
+
+// out = bf16(ws (+ residual)); optionally zero ws for the next accumulation.
+__global__ void splitk_finish_kernel(float* ws, const __nv_bfloat16* residual, __nv_bfloat16* out, int64_t total,
+                                     int zero_ws) {
+  const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (i >= total) return;
+  float4 a = *reinterpret_cast<float4*>(ws + i);
+  if (residual) {
+    const uint2 raw = *reinterpret_cast<const uint2*>(residual + i);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+    const float2 r0 = __bfloat1622float2(h[0]), r1 = __bfloat1622float2(h[1]);
+    a.x += r0.x; a.y += r0.y; a.z += r1.x; a.w += r1.y;
+  }
+  __nv_bfloat162 o0 = __floats2bfloat162_rn(a.x, a.y), o1 = __floats2bfloat162_rn(a.z, a.w);
+  uint2 w;
+  w.x = *reinterpret_cast<uint32_t*>(&o0);
+  w.y = *reinterpret_cast<uint32_t*>(&o1);
+  *reinterpret_cast<uint2*>(out + i) = w;
+  if (zero_ws) *reinterpret_cast<float4*>(ws + i) = make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+}  // namespace misc
+}  // namespace k8v4
+
+using namespace k8v4;
+using namespace k8v4::misc;
+
+K8V4_STATUS_API(misc)
+
+#define K8V4_VPT_DISPATCH(n, KERNEL, ...)                                         \
+  do {                                                                            \
+    const int vpt_ = cdiv(cdiv((n), 8), kThreads);                                \
+    if (vpt_ <= 1) KERNEL<1><<<rows, kThreads, 0, st>>>(__VA_ARGS__);             \
+    else if (vpt_ <= 2) KERNEL<2><<<rows, kThreads, 0, st>>>(__VA_ARGS__);        \
+    else if (vpt_ <= 4) KERNEL<4><<<rows, kThreads, 0, st>>>(__VA_ARGS__);        \
+    else if (vpt_ <= 9) KERNEL<9><<<rows, kThreads, 0, st>>>(__VA_ARGS__);        \
+    else return 2;                                                                \
+  } while (0)
+
+extern "C" int k8v4_rmsnorm(const void* x, void* residual, const void* w, void* y, void* yq, float* yscale, int rows,
+                            int n, float eps, cudaStream_t st) {
+  if (rows <= 0) return 0;
+  if (n % 8) return 1;
+  K8V4_VPT_DISPATCH(n, rmsnorm_kernel, reinterpret_cast<const __nv_bfloat16*>(x),
+                    reinterpret_cast<__nv_bfloat16*>(residual), reinterpret_cast<const __nv_bfloat16*>(w),
+                    reinterpret_cast<__nv_bfloat16*>(y), reinterpret_cast<int8_t*>(yq), yscale, n, eps);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+extern "C" int k8v4_silu_mul(const void* gu, void* y, void* yq, float* yscale, int rows, int inter,
+                             cudaStream_t st) {
+  if (rows <= 0) return 0;
+  if (inter % 8) return 1;
+  K8V4_VPT_DISPATCH(inter, silu_mul_kernel, reinterpret_cast<const __nv_bfloat16*>(gu),
+                    reinterpret_cast<__nv_bfloat16*>(y), reinterpret_cast<int8_t*>(yq), yscale, inter);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+extern "C" int k8v4_quant_rows(const void* x, void* q, float* scale, int rows, int n, cudaStream_t st) {
+  if (rows <= 0) return 0;
+  if (n % 8) return 1;
+  K8V4_VPT_DISPATCH(n, quant_rows_kernel, reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<int8_t*>(q),
+                    scale, n);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+extern "C" int k8v4_embed_int8(const int64_t* ids, const void* codes, const void* scales, void* out, int T, int n,
+                               int64_t start, int64_t rows, cudaStream_t st) {
+  if (T <= 0) return 0;
+  if (n % 8) return 1;
+  embed_int8_kernel<<<T, 128, 0, st>>>(ids, reinterpret_cast<const int8_t*>(codes),
+                                       reinterpret_cast<const __half*>(scales), reinterpret_cast<__nv_bfloat16*>(out),
+                                       n, start, rows);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+extern "C" int k8v4_splitk_finish(float* ws, const void* residual, void* out, int64_t total, int zero_ws,
+                                  cudaStream_t st) {
+  if (total <= 0) return 0;
+  if (total % 4) return 1;
+  const int64_t threads = total / 4;
+  splitk_finish_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
+      ws, reinterpret_cast<const __nv_bfloat16*>(residual), reinterpret_cast<__nv_bfloat16*>(out), total, zero_ws);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}

@@ -1,0 +1,179 @@
+"""Python entry points of the sm_100a kernel library (``torch.ops.k8v4``).
+
+The extension ``k8v4_xpu_b200._C`` is built in-tree by ``setup.py
+build_ext --inplace``. On a machine with a CUDA device a missing or broken
+extension raises instead of falling back to slower code: every op here runs
+the CUDA kernel or fails loudly.
+"""
+from __future__ import annotations
+
+import importlib
+import math
+import os
+
+import torch
+
+_LOADED = False
+_ERROR: str | None = None
+
+
+def load() -> bool:
+    """Import the extension once. Returns False (and records why) on failure."""
+    global _LOADED, _ERROR
+    if _LOADED:
+        return True
+    try:
+        importlib.import_module("k8v4_xpu_b200._C")
+        _ = torch.ops.k8v4.status
+        _LOADED = True
+        _ERROR = None
+    except Exception as exc:  # pragma: no cover - depends on the build
+        _ERROR = "%s: %s" % (type(exc).__name__, exc)
+    return _LOADED
+
+
+def require() -> None:
+    """Raise if the kernel library is not usable."""
+    if not load():
+        raise RuntimeError(
+            "k8v4 CUDA extension is not available (%s); build it with "
+            "`python setup.py build_ext --inplace`" % _ERROR)
+
+
+def available() -> bool:
+    return load()
+
+
+def extension_path() -> str | None:
+    if not load():
+        return None
+    mod = importlib.import_module("k8v4_xpu_b200._C")
+    return os.path.abspath(mod.__file__)
+
+
+def status(clear: bool = True) -> int:
+    """Device status word (0 = ok, 1 = a bounded wait timed out, ...)."""
+    require()
+    return int(torch.ops.k8v4.status(clear))
+
+
+# ------------------------------------------------------------------ KV cache
+FMT_REF, FMT_B200 = 0, 1
+
+
+def kv_store(k: torch.Tensor, v: torch.Tensor, slots: torch.Tensor, cache: torch.Tensor, hkv: int,
+             fmt: int = FMT_B200) -> None:
+    require()
+    torch.ops.k8v4.kv_store(fmt, k, v, slots, cache, hkv)
+
+
+def rope_store(qkv: torch.Tensor, cos_sin: torch.Tensor, positions: torch.Tensor, q_out: torch.Tensor,
+               slots: torch.Tensor, cache: torch.Tensor, hq: int, hkv: int) -> None:
+    require()
+    torch.ops.k8v4.rope_store(qkv, cos_sin, positions, q_out, slots, cache, hq, hkv)
+
+
+def decode_ws_floats(nseq: int, heads: int, nsplit: int, max_q_len: int, gqa: int) -> int:
+    require()
+    return int(torch.ops.k8v4.decode_ws_floats(nseq, heads, nsplit, max_q_len, gqa))
+
+
+def decode_attn(q, cu_q, seq_lens, block_table, cache, hkv, gqa, max_q_len, nsplit=1, out=None, ws=None,
+                q_ends=None, head_offset=0, heads=None, sm_scale=None):
+    """Split-K decode attention for every sequence of the batch in one launch."""
+    require()
+    heads = hkv if heads is None else heads
+    if out is None:
+        out = torch.empty_like(q)
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(q.shape[-1])
+    if nsplit > 1 and ws is None:
+        ws = torch.empty(decode_ws_floats(seq_lens.numel(), heads, nsplit, max_q_len, gqa),
+                         dtype=torch.float32, device=q.device)
+    torch.ops.k8v4.decode_attn(q, cu_q, seq_lens, q_ends, block_table, cache, hkv, head_offset, heads, gqa,
+                               max_q_len, nsplit, float(sm_scale), out, ws if nsplit > 1 else None)
+    return out
+
+
+def prefill_attn(q, cu_q, seq_lens, block_table, cache, hkv, gqa, max_q_len, out=None, head_offset=0,
+                 heads=None, sm_scale=None):
+    """Paged causal (bottom-right) attention of new tokens over their whole context."""
+    require()
+    heads = hkv if heads is None else heads
+    if out is None:
+        out = torch.empty_like(q)
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(q.shape[-1])
+    torch.ops.k8v4.prefill_attn(q, cu_q, seq_lens, block_table, cache, hkv, head_offset, heads, gqa, max_q_len,
+                                float(sm_scale), out)
+    return out
+
+
+# ---------------------------------------------------------------------- GEMM
+W4A16, W4A8, W8A8 = 0, 1, 2
+
+
+def wq_gemm(mode: int, w: torch.Tensor, wscale: torch.Tensor, x: torch.Tensor, xscale=None, residual=None,
+            out=None, ws=None, split: int = 1) -> torch.Tensor:
+    require()
+    n = w.shape[0] if mode == W8A8 else w.shape[1]
+    if out is None:
+        out = torch.empty((x.shape[0], n), dtype=torch.bfloat16, device=x.device)
+    if split > 1 and ws is None:
+        ws = torch.zeros((x.shape[0], n), dtype=torch.float32, device=x.device)
+    torch.ops.k8v4.wq_gemm(mode, w, wscale, x, xscale, residual, out, ws, split)
+    return out
+
+
+# ------------------------------------------------------------------- fused
+def rmsnorm(x, w, eps=1e-6, residual=None, out=None, quant=False):
+    """RMSNorm (optionally residual-add first); returns y, or (q, scale) with quant."""
+    require()
+    rows = x.numel() // x.shape[-1]
+    if quant:
+        q = torch.empty(x.shape, dtype=torch.int8, device=x.device)
+        s = torch.empty(rows, dtype=torch.float32, device=x.device)
+        torch.ops.k8v4.rmsnorm(x, residual, w, out, q, s, eps)
+        return (out, q, s) if out is not None else (q, s)
+    if out is None:
+        out = torch.empty_like(x)
+    torch.ops.k8v4.rmsnorm(x, residual, w, out, None, None, eps)
+    return out
+
+
+def silu_mul(gu, out=None, quant=False):
+    require()
+    rows, inter = gu.shape[0], gu.shape[1] // 2
+    if quant:
+        q = torch.empty((rows, inter), dtype=torch.int8, device=gu.device)
+        s = torch.empty(rows, dtype=torch.float32, device=gu.device)
+        torch.ops.k8v4.silu_mul(gu, out, q, s)
+        return q, s
+    if out is None:
+        out = torch.empty((rows, inter), dtype=torch.bfloat16, device=gu.device)
+    torch.ops.k8v4.silu_mul(gu, out, None, None)
+    return out
+
+
+def quant_rows(x):
+    require()
+    q = torch.empty(x.shape, dtype=torch.int8, device=x.device)
+    s = torch.empty(x.numel() // x.shape[-1], dtype=torch.float32, device=x.device)
+    torch.ops.k8v4.quant_rows(x, q, s)
+    return q, s
+
+
+def embed_int8(ids, codes, scales, start=0, out=None):
+    require()
+    if out is None:
+        out = torch.empty((ids.numel(), codes.shape[1]), dtype=torch.bfloat16, device=codes.device)
+    torch.ops.k8v4.embed_int8(ids, codes, scales, out, int(start))
+    return out
+
+
+def argmax(logits, offset=0):
+    require()
+    v = torch.empty(logits.shape[0], dtype=torch.float32, device=logits.device)
+    i = torch.empty(logits.shape[0], dtype=torch.int64, device=logits.device)
+    torch.ops.k8v4.argmax(logits, int(offset), v, i)
+    return v, i

@@ -1,0 +1,35 @@
+"""Build the k8v4 sm_100a kernel library in-tree: k8v4_xpu_b200/_C*.so.
+
+    python setup.py build_ext --inplace
+
+Every CUDA source is compiled for sm_100a only (tcgen05 / TMA / TMEM code).
+"""
+import glob
+import os
+
+from setuptools import setup
+from torch.utils.cpp_extension import BuildExtension, CUDAExtension
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+SOURCES = ["csrc/bindings.cpp"] + sorted(glob.glob("csrc/**/*.cu", recursive=True))
+NVCC = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-lineinfo", "-std=c++17",
+    "--expt-relaxed-constexpr",
+    "-diag-suppress", "20044",
+]
+
+setup(
+    name="k8v4_xpu_b200",
+    version="0.1.0",
+    packages=[],
+    ext_modules=[
+        CUDAExtension(
+            name="k8v4_xpu_b200._C",
+            sources=SOURCES,
+            include_dirs=[os.path.join(ROOT, "csrc")],
+            extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC},
+        )
+    ],
+    cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+)

@@ -1,0 +1,269 @@
+"""Numerics of the sm_100a kernels against plain PyTorch fp32 references."""
+import math
+
+import pytest
+import torch
+
+from k8v4_xpu_b200 import ops
+from k8v4_xpu_b200.kv.layout import b200_layout, ref_layout
+from k8v4_xpu_b200.kv.oracle import attention_ref
+from k8v4_xpu_b200.kv.pack import gather_sequence, store_tokens
+from k8v4_xpu_b200.models import gptq
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _gen(seed):
+    return torch.Generator(device="cpu").manual_seed(seed)
+
+
+# ------------------------------------------------------------------ KV store
+@pytest.mark.parametrize("fmt", ["b200", "ref"])
+def test_kv_store_bytes_match_oracle(fmt):
+    hkv = 4 if fmt == "ref" else 2
+    layout = b200_layout(hkv) if fmt == "b200" else ref_layout(hkv)
+    D = layout.head_dim
+    g = _gen(1)
+    T, pages = 70, 12
+    k = (torch.randn(T, hkv, D, generator=g) * 3).bfloat16()
+    v = (torch.randn(T, hkv, D, generator=g) * 2).bfloat16()
+    k[5] = 0  # all-zero row: scale 0
+    v[6, 0] = 1.5  # constant row (affine edge case)
+    slots = torch.randperm(pages * layout.page, generator=g)[:T].to(torch.int64)
+    slots[3] = -1  # skipped
+    slots[4] = pages * layout.page + 5  # past the cache: skipped
+    ref = torch.zeros(pages, layout.page_bytes, dtype=torch.uint8)
+    store_tokens(ref, slots, k, v, layout)
+    cache = torch.zeros(pages, layout.page_bytes, dtype=torch.uint8, device=DEV)
+    ops.kv_store(k.to(DEV), v.to(DEV), slots.to(DEV), cache, hkv, fmt=ops.FMT_B200 if fmt == "b200" else ops.FMT_REF)
+    torch.cuda.synchronize()
+    got = cache.cpu()
+    diff = (got != ref).nonzero()
+    assert diff.numel() == 0, "first differing bytes: %s" % diff[:8].tolist()
+
+
+def _rope_table(max_pos, D=128, theta=1e6):
+    inv = 1.0 / (theta ** (torch.arange(0, D, 2, dtype=torch.float64) / D))
+    ang = torch.arange(max_pos, dtype=torch.float64).view(-1, 1) * inv.view(1, -1)
+    return torch.cat([ang.cos(), ang.sin()], dim=1).float()
+
+
+def rope_ref(x, pos, table):
+    D = x.shape[-1]
+    c = table[pos, : D // 2].unsqueeze(1)
+    s = table[pos, D // 2:].unsqueeze(1)
+    x1, x2 = x[..., : D // 2].float(), x[..., D // 2:].float()
+    return torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], dim=-1)
+
+
+def test_rope_store_matches_oracle():
+    hq, hkv, D = 12, 2, 128
+    layout = b200_layout(hkv)
+    g = _gen(2)
+    T, pages = 37, 8
+    qkv = torch.randn(T, (hq + 2 * hkv) * D, generator=g).bfloat16()
+    pos = torch.randint(0, 4000, (T,), generator=g)
+    slots = torch.randperm(pages * 16, generator=g)[:T].to(torch.int64)
+    table = _rope_table(4096)
+    q_out = torch.empty(T, hq, D, dtype=torch.bfloat16, device=DEV)
+    cache = torch.zeros(pages, layout.page_bytes, dtype=torch.uint8, device=DEV)
+    ops.rope_store(qkv.to(DEV), table.to(DEV), pos.to(DEV), q_out, slots.to(DEV), cache, hq, hkv)
+    torch.cuda.synchronize()
+    x = qkv.view(T, hq + 2 * hkv, D)
+    q_ref = rope_ref(x[:, :hq], pos, table).bfloat16()
+    k_ref = rope_ref(x[:, hq:hq + hkv], pos, table).bfloat16()
+    v_ref = x[:, hq + hkv:]
+    assert torch.equal(q_out.cpu(), q_ref)
+    ref = torch.zeros(pages, layout.page_bytes, dtype=torch.uint8)
+    store_tokens(ref, slots, k_ref, v_ref, layout)
+    assert torch.equal(cache.cpu(), ref)
+
+
+# --------------------------------------------------------------------- GEMM
+def _int4_weights(N, K, seed):
+    g = _gen(seed)
+    w = torch.randn(N, K, generator=g) * 0.02
+    codes, scales = gptq.quantize_int4_rtn(w.t().contiguous())
+    t = gptq.pack_int4(codes, scales)
+    return t["qweight"], t["scales"]
+
+
+@pytest.mark.parametrize("M", [1, 7, 28, 64, 200])
+@pytest.mark.parametrize("split", [1, 3])
+def test_w4a16_gemm(M, split):
+    N, K = 384, 1024
+    qw, sc = _int4_weights(N, K, 3)
+    x = torch.randn(M, K, generator=_gen(4)).bfloat16()
+    ref = gptq.w4a16_ref(x, qw, sc)
+    out = ops.wq_gemm(ops.W4A16, qw.to(DEV), sc.to(DEV), x.to(DEV), split=split)
+    torch.cuda.synchronize()
+    assert ops.status() == 0
+    err = (out.float().cpu() - ref).abs().max().item()
+    assert err <= 2e-2 * ref.abs().max().item() + 1e-3, err
+
+
+@pytest.mark.parametrize("M", [1, 28, 130, 300])
+def test_w4a8_gemm(M):
+    N, K = 256, 1280
+    qw, sc = _int4_weights(N, K, 5)
+    x = torch.randn(M, K, generator=_gen(6)).bfloat16()
+    xq, xs = gptq.quant_act_rows(x)
+    ref = gptq.w4a8_ref(xq, xs, qw, sc)
+    out = ops.wq_gemm(ops.W4A8, qw.to(DEV), sc.to(DEV), xq.to(DEV), xscale=xs.to(DEV))
+    torch.cuda.synchronize()
+    assert ops.status() == 0
+    err = (out.float().cpu() - ref).abs().max().item()
+    assert err <= 1e-2 * ref.abs().max().item() + 1e-3, err
+
+
+@pytest.mark.parametrize("M", [1, 40])
+def test_w8a8_gemm(M):
+    N, K = 512, 512
+    w = torch.randn(N, K, generator=_gen(7)) * 0.05
+    wq, ws = gptq.quantize_int8_rows(w)
+    x = torch.randn(M, K, generator=_gen(8)).bfloat16()
+    xq, xs = gptq.quant_act_rows(x)
+    ref = gptq.w8a8_ref(xq, xs, wq, ws.view(-1))
+    out = ops.wq_gemm(ops.W8A8, wq.to(DEV), ws.view(-1).to(DEV), xq.to(DEV), xscale=xs.to(DEV))
+    torch.cuda.synchronize()
+    assert ops.status() == 0
+    err = (out.float().cpu() - ref).abs().max().item()
+    assert err <= 1e-2 * ref.abs().max().item() + 1e-3, err
+
+
+def test_gemm_residual():
+    N, K, M = 256, 512, 5
+    qw, sc = _int4_weights(N, K, 9)
+    x = torch.randn(M, K, generator=_gen(10)).bfloat16()
+    r = torch.randn(M, N, generator=_gen(11)).bfloat16()
+    ref = gptq.w4a16_ref(x, qw, sc) + r.float()
+    out = ops.wq_gemm(ops.W4A16, qw.to(DEV), sc.to(DEV), x.to(DEV), residual=r.to(DEV))
+    torch.cuda.synchronize()
+    assert (out.float().cpu() - ref).abs().max().item() < 0.05
+
+
+# ---------------------------------------------------------------- attention
+def _paged_setup(lens, hkv, gqa, seed, q_lens=None, pages_extra=3):
+    layout = b200_layout(hkv, gqa)
+    g = _gen(seed)
+    D = 128
+    q_lens = q_lens or [1] * len(lens)
+    total_pages = sum((n + 15) // 16 for n in lens) + pages_extra
+    perm = torch.randperm(total_pages, generator=g)
+    width = max((n + 15) // 16 for n in lens)
+    bt = torch.zeros(len(lens), width, dtype=torch.int32)
+    cache = torch.zeros(total_pages, layout.page_bytes, dtype=torch.uint8)
+    seqs = []
+    off = 0
+    for i, n in enumerate(lens):
+        np_ = (n + 15) // 16
+        pages = perm[off:off + np_]
+        off += np_
+        bt[i, :np_] = pages.to(torch.int32)
+        k = torch.randn(n, hkv, D, generator=g).bfloat16()
+        v = torch.randn(n, hkv, D, generator=g).bfloat16()
+        slots = (pages.repeat_interleave(16) * 16 + torch.arange(16).repeat(np_))[:n].to(torch.int64)
+        store_tokens(cache, slots, k, v, layout)
+        q = torch.randn(q_lens[i], hkv * gqa, D, generator=g).bfloat16()
+        seqs.append((q, pages.tolist()))
+    return layout, cache, bt, seqs
+
+
+def _reference(layout, cache, seqs, lens, q_lens):
+    outs = []
+    for (q, pages), n, ql in zip(seqs, lens, q_lens):
+        kd, vd = gather_sequence(cache, pages, n, layout)
+        ends = [n - ql + t + 1 for t in range(ql)]
+        outs.append(attention_ref(q.float(), kd, vd, ends, layout.gqa))
+    return torch.cat(outs, 0)
+
+
+@pytest.mark.parametrize("q_len", [1, 7])
+@pytest.mark.parametrize("nsplit", [1, 4])
+@pytest.mark.parametrize("gqa,hkv", [(6, 4), (3, 1)])
+def test_decode_attn(q_len, nsplit, gqa, hkv):
+    lens = [37, 300, 1024, 16]
+    q_lens = [q_len] * len(lens)
+    layout, cache, bt, seqs = _paged_setup(lens, hkv, gqa, 12, q_lens)
+    ref = _reference(layout, cache, seqs, lens, q_lens)
+    q = torch.cat([s[0] for s in seqs], 0).to(DEV)
+    cu = torch.tensor([0] + list(torch.cumsum(torch.tensor(q_lens), 0)), dtype=torch.int32, device=DEV)
+    out = ops.decode_attn(q, cu, torch.tensor(lens, dtype=torch.int32, device=DEV), bt.to(DEV), cache.to(DEV),
+                          hkv, gqa, q_len, nsplit=nsplit)
+    torch.cuda.synchronize()
+    assert ops.status() == 0
+    err = (out.float().cpu() - ref).abs().max().item()
+    assert err < 2e-2, err
+
+
+@pytest.mark.parametrize("ctx,q_len", [(0, 50), (200, 300), (1000, 21)])
+@pytest.mark.parametrize("gqa,hkv", [(6, 4), (3, 2)])
+def test_prefill_attn(ctx, q_len, gqa, hkv):
+    lens = [ctx + q_len, ctx // 2 + q_len]
+    q_lens = [q_len, q_len]
+    layout, cache, bt, seqs = _paged_setup(lens, hkv, gqa, 13, q_lens)
+    ref = _reference(layout, cache, seqs, lens, q_lens)
+    q = torch.cat([s[0] for s in seqs], 0).to(DEV)
+    cu = torch.tensor([0, q_len, 2 * q_len], dtype=torch.int32, device=DEV)
+    out = ops.prefill_attn(q, cu, torch.tensor(lens, dtype=torch.int32, device=DEV), bt.to(DEV), cache.to(DEV),
+                           hkv, gqa, q_len)
+    torch.cuda.synchronize()
+    assert ops.status() == 0
+    err = (out.float().cpu() - ref).abs().max().item()
+    assert err < 2e-2, err
+
+
+# ------------------------------------------------------------------- fused
+def test_rmsnorm_and_quant():
+    T, n = 9, 5120
+    x = torch.randn(T, n, generator=_gen(20)).bfloat16()
+    r = torch.randn(T, n, generator=_gen(21)).bfloat16()
+    w = (1 + 0.1 * torch.randn(n, generator=_gen(22))).bfloat16()
+    h = (x.float() + r.float()).bfloat16()
+    hf = h.float()
+    y_ref = (w.float() * (hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + 1e-6)).bfloat16().float()).bfloat16()
+    rd = r.to(DEV)
+    y, q, s = ops.rmsnorm(x.to(DEV), w.to(DEV), 1e-6, residual=rd, out=torch.empty_like(rd), quant=True)
+    torch.cuda.synchronize()
+    assert torch.equal(rd.cpu(), h)
+    assert (y.float().cpu() - y_ref.float()).abs().max().item() <= 0.02
+    q_ref, s_ref = gptq.quant_act_rows(y.cpu())
+    assert torch.allclose(s.cpu(), s_ref)
+    assert (q.cpu().int() - q_ref.int()).abs().max().item() <= 1
+
+
+def test_silu_mul_and_quant():
+    T, inter = 5, 2048
+    gu = torch.randn(T, 2 * inter, generator=_gen(23)).bfloat16()
+    y = ops.silu_mul(gu.to(DEV))
+    ref = (torch.nn.functional.silu(gu[:, :inter].float()) * gu[:, inter:].float())
+    assert (y.float().cpu() - ref).abs().max().item() < 0.02
+    q, s = ops.silu_mul(gu.to(DEV), quant=True)
+    q_ref, s_ref = gptq.quant_act_rows(y.cpu())
+    assert torch.allclose(s.cpu(), s_ref, rtol=1e-3)
+
+
+def test_embed_int8_shard_and_padding():
+    V, H = 62, 64
+    codes = (torch.arange(V * H).reshape(V, H) % 127 - 63).to(torch.int8)
+    scale = (torch.arange(1, V + 1).reshape(V, 1).half() / 1000)
+    for rank in (0, 1):
+        start, end = rank * 32, min((rank + 1) * 32, V)
+        ids = torch.tensor([0, 1, 15, 29, 31, 45, 61])
+        out = ops.embed_int8(ids.to(DEV), codes[start:end].contiguous().to(DEV),
+                             scale[start:end].contiguous().view(-1).to(DEV), start=start)
+        torch.cuda.synchronize()
+        inside = (ids >= start) & (ids < end)
+        exp = torch.zeros(len(ids), H, dtype=torch.bfloat16)
+        gi = ids[inside]
+        exp[inside] = codes[gi].bfloat16() * scale[gi].bfloat16()
+        assert torch.equal(out.cpu(), exp)
+
+
+def test_argmax():
+    logits = torch.randn(3, 151936, generator=_gen(30)).bfloat16()
+    logits[1, 77] = 100.0
+    v, i = ops.argmax(logits.to(DEV), offset=5)
+    assert torch.equal(i.cpu(), logits.float().argmax(-1) + 5)
