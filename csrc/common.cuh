@@ -35,20 +35,25 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // Device status word of this translation unit (one per device that loaded
 // the library). Each .cu file exports a reader through K8V4_STATUS_API.
 static __device__ int g_k8v4_status;
+// Where the first recorded error happened (site id of the wait, see tc.cuh).
+static __device__ int g_k8v4_site;
 
+// Returns the status code in the low byte and the site id above it.
 #define K8V4_STATUS_API(unit)                                              \
   extern "C" int k8v4_status_##unit(int clear) {                           \
-    int v = 0;                                                             \
+    int v = 0, site = 0;                                                   \
     cudaMemcpyFromSymbol(&v, k8v4::g_k8v4_status, sizeof(int));            \
+    cudaMemcpyFromSymbol(&site, k8v4::g_k8v4_site, sizeof(int));           \
     if (clear && v) {                                                      \
       int z = 0;                                                           \
       cudaMemcpyToSymbol(k8v4::g_k8v4_status, &z, sizeof(int));            \
+      cudaMemcpyToSymbol(k8v4::g_k8v4_site, &z, sizeof(int));              \
     }                                                                      \
-    return v;                                                              \
+    return v ? (v | (site << 8)) : 0;                                      \
   }
 
-__device__ __forceinline__ void record_error(int code) {
-  atomicCAS(&g_k8v4_status, 0, code);
+__device__ __forceinline__ void record_error(int code, int site = 0) {
+  if (atomicCAS(&g_k8v4_status, 0, code) == 0) g_k8v4_site = site;
 }
 
 __device__ __forceinline__ float bf2f(__nv_bfloat16 v) { return __bfloat162float(v); }

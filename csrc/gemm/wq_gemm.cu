@@ -168,13 +168,13 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES>::N
         const uint32_t ph = (kb / STAGES) & 1;
         const int k0 = kbeg + kb * C::BK;
         if (MODE != W8A8) {
-          if (kb >= RSTAGES && !mbar_wait(&r_empty[rs], rphase ^ 1, abort_flag)) break;
+          if (kb >= RSTAGES && !mbar_wait(&r_empty[rs], rphase ^ 1, abort_flag, 101)) break;
           mbar_arrive_expect_tx(&r_full[rs], C::RAW_BYTES);
           tma_load_2d(sR + rs * C::RAW_BYTES, &tm_w, &r_full[rs], n0, k0 / 8);
           ++raw_issued;
           if (++rs == RSTAGES) { rs = 0; rphase ^= 1; }
         }
-        if (kb >= STAGES && !mbar_wait(&ab_empty[s], ph ^ 1, abort_flag)) break;
+        if (kb >= STAGES && !mbar_wait(&ab_empty[s], ph ^ 1, abort_flag, 102)) break;
         if (MODE == W8A8) {
           mbar_arrive_expect_tx(&a_full[s], C::A_BYTES);
           tma_load_2d(sA + s * C::A_BYTES, &tm_w, &a_full[s], k0, n0);
@@ -201,14 +201,14 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES>::N
       bool ok = true;
       for (int g = 0; g < ngroups && ok; ++g) {
         const int buf = g & 1;
-        if (g >= 2 && !mbar_wait(&acc_empty[buf], ((g >> 1) - 1) & 1, abort_flag)) break;
+        if (g >= 2 && !mbar_wait(&acc_empty[buf], ((g >> 1) - 1) & 1, abort_flag, 103)) break;
         tc_fence_after();
         const uint32_t dtm = tmem + buf * BT;
         for (int j = 0; j < kb_per_group; ++j) {
           const int kb = g * kb_per_group + j;
           const int s = kb % STAGES;
           const uint32_t ph = (kb / STAGES) & 1;
-          if (!mbar_wait(&a_full[s], ph, abort_flag) || !mbar_wait(&b_full[s], ph, abort_flag)) {
+          if (!mbar_wait(&a_full[s], ph, abort_flag, 104) || !mbar_wait(&b_full[s], ph, abort_flag, 105)) {
             ok = false;
             break;
           }
@@ -240,8 +240,8 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES>::N
       for (int kb = 0; kb < nkb; ++kb) {
         const int s = kb % STAGES;
         const uint32_t ph = (kb / STAGES) & 1;
-        if (!mbar_wait(&r_full[rs], rphase, abort_flag)) break;
-        if (kb >= STAGES && !mbar_wait(&ab_empty[s], ph ^ 1, abort_flag)) break;
+        if (!mbar_wait_all(&r_full[rs], rphase, abort_flag, 106)) break;
+        if (kb >= STAGES && !mbar_wait_all(&ab_empty[s], ph ^ 1, abort_flag, 107)) break;
         const uint32_t* raw = reinterpret_cast<const uint32_t*>(sR + rs * C::RAW_BYTES);
         uint8_t* dst = sA + s * C::A_BYTES;
 #pragma unroll 4
@@ -284,7 +284,7 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES>::N
     bool ok = nkb > 0;
     for (int g = 0; g < ngroups && ok; ++g) {
       const int buf = g & 1;
-      if (!mbar_wait(&acc_full[buf], (g >> 1) & 1, abort_flag)) { ok = false; break; }
+      if (!mbar_wait_all(&acc_full[buf], (g >> 1) & 1, abort_flag, 108)) { ok = false; break; }
       tc_fence_after();
       float gs = 1.f;
       if (MODE != W8A8 && n < p.N) gs = __half2float(p.wscale[(size_t)((kbeg / 128) + g) * p.N + n]);

@@ -166,7 +166,7 @@ __global__ void __launch_bounds__(320, 1)
       int issued = 0;
       for (int j = 0; j < nt; ++j) {
         const int s = j % C::STAGES;
-        if (j >= C::STAGES && !mbar_wait(&kv_empty[s], ((j / C::STAGES) - 1) & 1, abort_flag)) break;
+        if (j >= C::STAGES && !mbar_wait(&kv_empty[s], ((j / C::STAGES) - 1) & 1, abort_flag, 201)) break;
         const int pg0 = (tile_beg + j) * TILE_PAGES;
         const int npg = min(TILE_PAGES, n_pages - pg0);
         mbar_arrive_expect_tx(&kv_full[s], npg * (K_BYTES + VS_BYTES));
@@ -193,7 +193,7 @@ __global__ void __launch_bounds__(320, 1)
       for (int j = 0; j <= nt && ok; ++j) {
         if (j < nt) {
           const int s = j % C::STAGES, b = j & 1;
-          if (!mbar_wait(&kv_full[s], (j / C::STAGES) & 1, abort_flag)) break;
+          if (!mbar_wait(&kv_full[s], (j / C::STAGES) & 1, abort_flag, 202)) break;
           tc_fence_after();
           const uint32_t k_base = smem_u32(sK + s * K_TILE_BYTES);
 #pragma unroll
@@ -205,7 +205,7 @@ __global__ void __launch_bounds__(320, 1)
         }
         if (j >= 1) {
           const int jj = j - 1, b = jj & 1;
-          if (!mbar_wait(&p_full[b], (jj >> 1) & 1, abort_flag) || !mbar_wait(&v_full[b], (jj >> 1) & 1, abort_flag)) {
+          if (!mbar_wait(&p_full[b], (jj >> 1) & 1, abort_flag, 203) || !mbar_wait(&v_full[b], (jj >> 1) & 1, abort_flag, 204)) {
             ok = false;
             break;
           }
@@ -229,8 +229,8 @@ __global__ void __launch_bounds__(320, 1)
     const int ct = threadIdx.x - 64;  // 0..127
     for (int j = 0; j < nt; ++j) {
       const int s = j % C::STAGES, b = j & 1;
-      if (!mbar_wait(&kv_full[s], (j / C::STAGES) & 1, abort_flag)) break;
-      if (j >= 2 && !mbar_wait(&pv_empty[b], ((j >> 1) - 1) & 1, abort_flag)) break;
+      if (!mbar_wait_all(&kv_full[s], (j / C::STAGES) & 1, abort_flag, 205)) break;
+      if (j >= 2 && !mbar_wait_all(&pv_empty[b], ((j >> 1) - 1) & 1, abort_flag, 206)) break;
       const int key0 = (tile_beg + j) * TILE;
       const int nvalid = min(TILE, seq_len - key0);
       const uint8_t* vs = sVS + s * VS_TILE_BYTES;
@@ -263,22 +263,26 @@ __global__ void __launch_bounds__(320, 1)
     float l_acc[NPAD];
 #pragma unroll
     for (int r = 0; r < NPAD; ++r) l_acc[r] = 0.f;
+    // Every softmax warp runs every iteration and every named barrier, even
+    // after a failed (timed-out) wait: a failure only turns the work off, so
+    // the four warps always meet at the same bar.sync.
     bool ok = true;
     for (int j = 0; j < nt; ++j) {
       const int s = j % C::STAGES, b = j & 1;
-      if (!mbar_wait(&s_full[b], (j >> 1) & 1, abort_flag) || !mbar_wait(&kv_full[s], (j / C::STAGES) & 1, abort_flag)) {
+      if (ok && (!mbar_wait_all(&s_full[b], (j >> 1) & 1, abort_flag, 207) ||
+                 !mbar_wait_all(&kv_full[s], (j / C::STAGES) & 1, abort_flag, 208)))
         ok = false;
-        break;
-      }
-      tc_fence_after();
       const int key = (tile_beg + j) * TILE + key_local;
-      const uint8_t* vs = sVS + s * VS_TILE_BYTES;
-      const float ks = (key < seq_len)
-                           ? __half2float(*reinterpret_cast<const __half*>(vs + (key_local >> 4) * VS_BYTES + KS_OFF +
-                                                                           (key_local & 15) * 2))
-                           : 0.f;
       float sc[NPAD];
-      {
+#pragma unroll
+      for (int r = 0; r < NPAD; ++r) sc[r] = -INFINITY;
+      if (ok) {
+        tc_fence_after();
+        const uint8_t* vs = sVS + s * VS_TILE_BYTES;
+        const float ks = (key < seq_len)
+                             ? __half2float(*reinterpret_cast<const __half*>(vs + (key_local >> 4) * VS_BYTES + KS_OFF +
+                                                                             (key_local & 15) * 2))
+                             : 0.f;
         const uint32_t ta = tm_s + b * NPAD + ((uint32_t)(quad * 32) << 16);
 #pragma unroll
         for (int c = 0; c < NPAD; c += 16) {
@@ -288,15 +292,15 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
           for (int i = 0; i < 16; ++i) sc[c + i] = i2f_small(r16[i]);
         }
-      }
-      // scores (log2 domain), masked, and this warp's per-row max
+        // scores (log2 domain), masked, and this warp's per-row max
 #pragma unroll
-      for (int r = 0; r < NPAD; ++r) {
-        if (r < R) {
-          const float v = sc[r] * (q_scale[r] * ks);
-          sc[r] = (key < row_end[r]) ? v : -INFINITY;
-          const float wm = warp_max(sc[r]);
-          if (lane == 0) red[sw * NPAD + r] = wm;
+        for (int r = 0; r < NPAD; ++r) {
+          if (r < R) {
+            const float v = sc[r] * (q_scale[r] * ks);
+            sc[r] = (key < row_end[r]) ? v : -INFINITY;
+            const float wm = warp_max(sc[r]);
+            if (lane == 0) red[sw * NPAD + r] = wm;
+          }
         }
       }
       asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -306,67 +310,75 @@ __global__ void __launch_bounds__(320, 1)
       int any_rescale = 0;
       float* mw = m_ref + sw * NPAD;
       float* aw = alpha + sw * NPAD;
+      if (ok) {
 #pragma unroll
-      for (int r = 0; r < NPAD; ++r) {
-        if (r < R) {
-          const float tmax = fmaxf(fmaxf(red[r], red[NPAD + r]), fmaxf(red[2 * NPAD + r], red[3 * NPAD + r]));
-          const float mo = mw[r];
-          float a = 1.f, mn = mo;
-          if (tmax > mo + RESCALE_TAU || (mo == -INFINITY && tmax > -INFINITY)) {
-            mn = tmax;
-            a = (mo == -INFINITY) ? 0.f : exp2f(mo - mn);
-            any_rescale = 1;
-          }
-          l_acc[r] *= a;
-          sc[r] = (sc[r] == -INFINITY || mn == -INFINITY) ? 0.f : exp2f(sc[r] - mn);
-          l_acc[r] += sc[r];
-          __syncwarp();
-          if (lane == 0) {
-            mw[r] = mn;
-            aw[r] = a;
+        for (int r = 0; r < NPAD; ++r) {
+          if (r < R) {
+            const float tmax = fmaxf(fmaxf(red[r], red[NPAD + r]), fmaxf(red[2 * NPAD + r], red[3 * NPAD + r]));
+            const float mo = mw[r];
+            float a = 1.f, mn = mo;
+            if (tmax > mo + RESCALE_TAU || (mo == -INFINITY && tmax > -INFINITY)) {
+              mn = tmax;
+              a = (mo == -INFINITY) ? 0.f : exp2f(mo - mn);
+              any_rescale = 1;
+            }
+            l_acc[r] *= a;
+            sc[r] = (sc[r] == -INFINITY || mn == -INFINITY) ? 0.f : exp2f(sc[r] - mn);
+            l_acc[r] += sc[r];
+            __syncwarp();
+            if (lane == 0) {
+              mw[r] = mn;
+              aw[r] = a;
+            }
           }
         }
-      }
-      __syncwarp();
-      // rescale O^T columns when a row's reference max moved (needs PV j-1 done)
-      if (any_rescale && j > 0) {
-        const int pb = (j - 1) & 1;
-        if (!mbar_wait(&pv_empty[pb], ((j - 1) >> 1) & 1, abort_flag)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t ta = tm_o + ((uint32_t)(quad * 32) << 16);
+        __syncwarp();
+        // rescale O^T columns when a row's reference max moved (needs PV j-1 done)
+        if (any_rescale && j > 0) {
+          const int pb = (j - 1) & 1;
+          if (!mbar_wait_all(&pv_empty[pb], ((j - 1) >> 1) & 1, abort_flag, 209)) {
+            ok = false;
+          } else {
+            tc_fence_after();
+            const uint32_t ta = tm_o + ((uint32_t)(quad * 32) << 16);
 #pragma unroll
-        for (int c = 0; c < NPAD; c += 8) {
-          uint32_t r8[8];
-          tmem_ld8(ta + c, r8);
-          tmem_ld_wait();
+            for (int c = 0; c < NPAD; c += 8) {
+              uint32_t r8[8];
+              tmem_ld8(ta + c, r8);
+              tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 8; ++i) r8[i] = __float_as_uint(__uint_as_float(r8[i]) * (c + i < R ? aw[c + i] : 1.f));
-          tmem_st8(ta + c, r8);
+              for (int i = 0; i < 8; ++i)
+                r8[i] = __float_as_uint(__uint_as_float(r8[i]) * (c + i < R ? aw[c + i] : 1.f));
+              tmem_st8(ta + c, r8);
+            }
+            tmem_st_wait();
+          }
         }
-        tmem_st_wait();
       }
       // P^T (fp16, K-major SW128): row r, key key_local
-      if (j >= 2 && !mbar_wait(&pv_empty[b], ((j >> 1) - 1) & 1, abort_flag)) { ok = false; break; }
-      uint8_t* pt = sPT + b * C::PT_BYTES + (key_local >> 6) * (NPAD * 128) + (key_local & 7) * 2;
-      const int kc = (key_local & 63) >> 3;
+      if (ok && j >= 2 && !mbar_wait_all(&pv_empty[b], ((j >> 1) - 1) & 1, abort_flag, 210)) ok = false;
+      if (ok) {
+        uint8_t* pt = sPT + b * C::PT_BYTES + (key_local >> 6) * (NPAD * 128) + (key_local & 7) * 2;
+        const int kc = (key_local & 63) >> 3;
 #pragma unroll
-      for (int r = 0; r < NPAD; ++r) {
-        const __half hv = __float2half_rn(r < R ? sc[r] : 0.f);
-        *reinterpret_cast<__half*>(pt + r * 128 + ((kc ^ (r & 7)) << 4)) = hv;
+        for (int r = 0; r < NPAD; ++r) {
+          const __half hv = __float2half_rn(r < R ? sc[r] : 0.f);
+          *reinterpret_cast<__half*>(pt + r * 128 + ((kc ^ (r & 7)) << 4)) = hv;
+        }
+        fence_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&p_full[b]);
+          mbar_arrive(&kv_empty[s]);
+        }
       }
-      fence_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&p_full[b]);
-        mbar_arrive(&kv_empty[s]);
-      }
-      asm volatile("bar.sync 1, 128;" ::: "memory");  // m_ref / alpha stable before the next tile
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // red / m / alpha reads done before the next tile
     }
     // ------------------------------------------------------------ epilogue
     if (ok && nt > 0) {
       const int lb = (nt - 1) & 1;
-      if (!mbar_wait(&pv_empty[lb], ((nt - 1) >> 1) & 1, abort_flag)) ok = false;
+      if (!mbar_wait_all(&pv_empty[lb], ((nt - 1) >> 1) & 1, abort_flag, 211)) ok = false;
     }
     // row sums across the 128 key-threads
 #pragma unroll

@@ -153,7 +153,7 @@ __global__ void __launch_bounds__(320, 1)
       int issued = 0;
       for (int j = 0; j < nt; ++j) {
         const int s = j % C::STAGES;
-        if (j >= C::STAGES && !mbar_wait(&kv_empty[s], ((j / C::STAGES) - 1) & 1, abort_flag)) break;
+        if (j >= C::STAGES && !mbar_wait(&kv_empty[s], ((j / C::STAGES) - 1) & 1, abort_flag, 301)) break;
         const int pg0 = j * TILE_PAGES;
         const int npg = min(TILE_PAGES, n_pages - pg0);
         mbar_arrive_expect_tx(&kv_full[s], npg * (K_BYTES + VS_BYTES));
@@ -180,7 +180,7 @@ __global__ void __launch_bounds__(320, 1)
       for (int j = 0; j <= nt && ok; ++j) {
         if (j < nt) {
           const int s = j % C::STAGES, b = j & 1;
-          if (!mbar_wait(&kv_full[s], (j / C::STAGES) & 1, abort_flag)) break;
+          if (!mbar_wait(&kv_full[s], (j / C::STAGES) & 1, abort_flag, 302)) break;
           tc_fence_after();
           const uint32_t k_base = smem_u32(sK + s * K_TILE_BYTES);
 #pragma unroll
@@ -192,7 +192,7 @@ __global__ void __launch_bounds__(320, 1)
         }
         if (j >= 1) {
           const int jj = j - 1, b = jj & 1;
-          if (!mbar_wait(p_full, jj & 1, abort_flag) || !mbar_wait(&v_full[b], (jj >> 1) & 1, abort_flag)) {
+          if (!mbar_wait(p_full, jj & 1, abort_flag, 303) || !mbar_wait(&v_full[b], (jj >> 1) & 1, abort_flag, 304)) {
             ok = false;
             break;
           }
@@ -215,9 +215,9 @@ __global__ void __launch_bounds__(320, 1)
     const int ct = threadIdx.x - 64;
     for (int j = 0; j < nt; ++j) {
       const int s = j % C::STAGES, b = j & 1;
-      if (!mbar_wait(&kv_full[s], (j / C::STAGES) & 1, abort_flag)) break;
+      if (!mbar_wait_all(&kv_full[s], (j / C::STAGES) & 1, abort_flag, 305)) break;
       // V^T buffer b was last read by PV of tile j-2
-      if (j >= 2 && !mbar_wait(&pv_empty[b], ((j >> 1) - 1) & 1, abort_flag)) break;
+      if (j >= 2 && !mbar_wait_all(&pv_empty[b], ((j >> 1) - 1) & 1, abort_flag, 306)) break;
       const int nvalid = min(TILE, n_keys - j * TILE);
       const uint8_t* vs = sVS + s * VS_TILE_BYTES;
       uint8_t* vt = sVT + b * VT_BYTES;
@@ -253,8 +253,8 @@ __global__ void __launch_bounds__(320, 1)
     bool ok = true;
     for (int j = 0; j < nt; ++j) {
       const int s = j % C::STAGES, b = j & 1;
-      if (!mbar_wait(&s_full[b], (j >> 1) & 1, abort_flag) ||
-          !mbar_wait(&kv_full[s], (j / C::STAGES) & 1, abort_flag)) {
+      if (!mbar_wait_all(&s_full[b], (j >> 1) & 1, abort_flag, 307) ||
+          !mbar_wait_all(&kv_full[s], (j / C::STAGES) & 1, abort_flag, 308)) {
         ok = false;
         break;
       }
@@ -287,8 +287,10 @@ __global__ void __launch_bounds__(320, 1)
       }
       float lsum = 0.f;
       // P (fp16) must not overwrite the buffer PV j-1 is still reading
-      if (j >= 1 && !mbar_wait(&pv_empty[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag)) { ok = false; break; }
-      if (a != 1.f && j > 0 && live) {
+      if (j >= 1 && !mbar_wait_all(&pv_empty[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, 309)) { ok = false; break; }
+      // tcgen05.ld/st are warp-collective: the warp rescales together when any
+      // of its rows needs it (rows that do not use a == 1).
+      if (__any_sync(0xffffffffu, a != 1.f && j > 0 && live)) {
         tc_fence_after();
         // rescale this row of O
 #pragma unroll
@@ -344,10 +346,10 @@ __global__ void __launch_bounds__(320, 1)
       if (lane == 0) mbar_arrive(p_full);
     }
     // ------------------------------------------------------------ epilogue
-    if (ok && nt > 0 && !mbar_wait(&pv_empty[(nt - 1) & 1], ((nt - 1) >> 1) & 1, abort_flag)) ok = false;
-    if (ok && live) {
+    if (ok && nt > 0 && !mbar_wait_all(&pv_empty[(nt - 1) & 1], ((nt - 1) >> 1) & 1, abort_flag, 310)) ok = false;
+    if (ok) {  // warp-uniform (voted waits): every lane joins the TMEM loads
       tc_fence_after();
-      const int t = t0 + row / p.gqa, g = row % p.gqa;
+      const int t = t0 + (live ? row : 0) / p.gqa, g = (live ? row : 0) % p.gqa;
       __nv_bfloat16* dst = p.out + ((int64_t)(qb + t) * p.hq_total + (int64_t)h * p.gqa + g) * D;
       const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
 #pragma unroll
@@ -366,7 +368,7 @@ __global__ void __launch_bounds__(320, 1)
           o.y = *reinterpret_cast<uint32_t*>(&b1);
           o.z = *reinterpret_cast<uint32_t*>(&b2);
           o.w = *reinterpret_cast<uint32_t*>(&b3);
-          *reinterpret_cast<uint4*>(dst + c + i) = o;
+          if (live) *reinterpret_cast<uint4*>(dst + c + i) = o;
         }
       }
     }

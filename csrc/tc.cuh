@@ -44,7 +44,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait. Returns false (and leaves the abort flag set) on timeout or
 // when another role of the CTA already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          int site = 0) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
@@ -52,10 +53,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     if (*abort_flag) return false;
     if (globaltimer_ns() - t0 > K8V4_WAIT_LIMIT_NS) {
       *abort_flag = 1;
-      record_error(kErrMbarTimeout);
+      record_error(kErrMbarTimeout, site);
       return false;
     }
   }
+}
+
+// Warp-uniform bounded wait: every lane polls, then the warp votes, so a
+// timeout seen by one lane turns the whole warp off together (the callers use
+// .sync.aligned tcgen05 ops and __syncwarp afterwards).
+__device__ __forceinline__ bool mbar_wait_all(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                              int site = 0) {
+  const bool ok = mbar_wait(bar, parity, abort_flag, site);
+  return __all_sync(0xffffffffu, ok) != 0;
 }
 
 // Bounded wait used while draining after an abort: ignores the abort flag

@@ -1,0 +1,88 @@
+"""Quantized linear layers and the W4A8 / W4A16 path policy.
+
+Every linear of the decoder stores GPTQ INT4 (group 128) weights. The path
+choice follows the reference's MLP-only rule (``k8v4_v030/w4a8_prefill.py:
+19,160-176,237-252``): a linear whose name contains ``.mlp.`` runs W4A8
+(int8 activations with a per-token scale) when the call has more than
+``SMALL_M_MAX`` rows; everything else (attention projections at any M and
+every linear at decode sizes) runs W4A16. Both are the same tcgen05 kernel
+family (``csrc/gemm/wq_gemm.cu``); the choice is made per call from the
+runtime row count, so one captured decode graph and an eager prefill chunk
+can each take the right path.
+"""
+from __future__ import annotations
+
+import os
+
+import torch
+
+from .. import ops
+
+SMALL_M_MAX = 128
+NUM_SMS = 148
+
+
+def w4a8_enabled() -> bool:
+    """``K8V4_PREFILL_GEMM`` = ``w4a8`` (default) or ``w4a16`` (MLP keeps W4A16)."""
+    mode = os.environ.get("K8V4_PREFILL_GEMM", "w4a8").strip().lower()
+    if mode not in ("w4a8", "w4a16"):
+        raise ValueError("K8V4_PREFILL_GEMM must be w4a8 or w4a16, got %r" % mode)
+    return mode == "w4a8"
+
+
+def uses_w4a8(name: str, rows: int, enabled: bool = True) -> bool:
+    """The reference's runtime gate: MLP linears, rows > SMALL_M_MAX."""
+    return enabled and ".mlp." in name and rows > SMALL_M_MAX
+
+
+def split_for(rows: int, n: int, k: int, sms: int = NUM_SMS) -> int:
+    """Split-K factor that fills the GPU for skinny (decode) GEMMs."""
+    if rows > 64:
+        return 1
+    tiles = (n + 127) // 128
+    if tiles >= sms:
+        return 1
+    groups = k // 128
+    split = max(1, min(sms // tiles, groups // 4 if groups >= 8 else 1))
+    return split
+
+
+class Int4Linear:
+    """GPTQ INT4 weights ``qweight`` [K/8, N] int32 + ``scales`` [K/128, N] fp16."""
+
+    def __init__(self, name: str, qweight: torch.Tensor, scales: torch.Tensor):
+        if qweight.dim() != 2 or scales.dim() != 2:
+            raise ValueError("qweight / scales must be 2D")
+        self.name = name
+        self.qweight = qweight
+        self.scales = scales
+        self.in_features = qweight.shape[0] * 8
+        self.out_features = qweight.shape[1]
+
+    def __call__(self, x: torch.Tensor | None = None, xq: torch.Tensor | None = None,
+                 xs: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                 ws: torch.Tensor | None = None, split: int | None = None) -> torch.Tensor:
+        if xq is not None:
+            rows = xq.shape[0]
+            return ops.wq_gemm(ops.W4A8, self.qweight, self.scales, xq, xscale=xs, out=out)
+        rows = x.shape[0]
+        if split is None:
+            split = split_for(rows, self.out_features, self.in_features) if ws is not None else 1
+        return ops.wq_gemm(ops.W4A16, self.qweight, self.scales, x, out=out, ws=ws, split=split)
+
+    def reference(self, x: torch.Tensor) -> torch.Tensor:
+        from ..models.gptq import dequant_int4
+        return x.float() @ dequant_int4(self.qweight, self.scales)
+
+
+class Int8RowLinear:
+    """Per-row INT8 weights ``[N, K]`` + fp16 scales ``[N]`` (the lm_head)."""
+
+    def __init__(self, name: str, weight: torch.Tensor, scale: torch.Tensor):
+        self.name = name
+        self.weight = weight
+        self.scale = scale.reshape(-1)
+        self.out_features, self.in_features = weight.shape
+
+    def __call__(self, xq: torch.Tensor, xs: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        return ops.wq_gemm(ops.W8A8, self.weight, self.scale, xq, xscale=xs, out=out)

@@ -1,0 +1,294 @@
+"""The dense K8/V4 decoder: weights, random init, and the forward pass.
+
+Per layer (one rank of a TP group):
+
+    residual, h = rmsnorm(x + residual)            fused add + norm
+    qkv         = h @ Wqkv                         W4A16 (tcgen05)
+    q, K/V      = rope_store(qkv)                  RoPE + K8/V4 quantized page write
+    a           = paged attention(q, pages)        decode: split-K; prefill: causal tiles
+    x           = a @ Wo                           W4A16, then TP all-reduce
+    residual, h = rmsnorm(x + residual)            (+ int8 quant when W4A8 runs)
+    gu          = h @ Wgate_up                     W4A8 above 128 rows, else W4A16
+    act         = silu(gate) * up                  (+ int8 quant)
+    x           = act @ Wdown                      then TP all-reduce
+
+The embedding is the INT8 side-file lookup (vocab sharded under TP), the
+lm_head is INT8 per-row with int8 activations, sampling is a per-rank argmax
+reduced across ranks. Attention metadata (slots, block tables, lengths) comes
+in a :class:`StepInputs`.
+"""
+from __future__ import annotations
+
+import dataclasses
+import math
+
+import torch
+
+from .. import ops
+from ..kv.layout import PageLayout, b200_layout
+from ..layers.linear import Int4Linear, Int8RowLinear, uses_w4a8, w4a8_enabled
+from . import gptq
+from .config import ModelConfig, TPShape
+
+
+@dataclasses.dataclass
+class StepInputs:
+    """Device tensors describing one forward over a packed token batch."""
+
+    input_ids: torch.Tensor      # [T] int64
+    positions: torch.Tensor      # [T] int64
+    slots: torch.Tensor          # [T] int64 KV slot of each token
+    cu_q: torch.Tensor           # [B+1] int32
+    seq_lens: torch.Tensor       # [B] int32 (context incl. these tokens)
+    block_table: torch.Tensor    # [B, W] int32
+    logit_rows: torch.Tensor     # [B'] int64 rows of the batch whose logits are needed
+    max_q_len: int
+    is_decode: bool              # every sequence has q_len <= the decode tile
+    q_ends: torch.Tensor | None = None  # [T] int32 per-token visible end (MTP trees)
+    nsplit: int = 1              # decode split-K factor
+
+
+@dataclasses.dataclass
+class LayerWeights:
+    input_norm: torch.Tensor
+    post_norm: torch.Tensor
+    qkv: Int4Linear
+    o: Int4Linear
+    gate_up: Int4Linear
+    down: Int4Linear
+
+
+def rope_table(max_pos: int, head_dim: int, theta: float, device) -> torch.Tensor:
+    """fp32 ``[max_pos, head_dim]``: cos of the half-dim frequencies then sin."""
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim))
+    pos = torch.arange(max_pos, dtype=torch.float64)
+    ang = pos.view(-1, 1) * inv.view(1, -1)
+    return torch.cat([ang.cos(), ang.sin()], dim=1).float().to(device)
+
+
+def _rand_int4(k: int, n: int, gen: torch.Generator, device, std: float = 0.02):
+    w = torch.randn(k, n, generator=gen, device=device) * std
+    codes, scales = gptq.quantize_int4_rtn(w)
+    t = gptq.pack_int4(codes, scales)
+    return t["qweight"], t["scales"]
+
+
+class DenseModel:
+    """One TP rank of the dense decoder (weights resident on ``device``)."""
+
+    def __init__(self, cfg: ModelConfig, tp: int = 1, rank: int = 0, device="cuda", comm=None):
+        self.cfg = cfg
+        self.tp = tp
+        self.rank = rank
+        self.device = torch.device(device)
+        self.shape: TPShape = cfg.tp_shard(tp)
+        self.comm = comm
+        self.layout: PageLayout = b200_layout(self.shape.hkv_local, self.shape.gqa_local)
+        self.layers: list[LayerWeights] = []
+        self.embed_codes = self.embed_scales = None
+        self.final_norm = None
+        self.lm_head: Int8RowLinear | None = None
+        self.vocab_start = rank * self.shape.vocab_local
+        self.rope = None
+        self.w4a8 = w4a8_enabled()
+        self.mtp = None
+
+    # ------------------------------------------------------------- weights
+    def random_init(self, seed: int = 0, layers: int | None = None) -> "DenseModel":
+        """Random-init weights of the architecture, quantized on the device.
+
+        Every rank draws the *full* matrices from the same seed and keeps its
+        shard, so TP ranks hold a consistent model.
+        """
+        cfg, sh = self.cfg, self.shape
+        dev = self.device
+        gen = torch.Generator(device=dev).manual_seed(seed)
+        H, D = cfg.hidden, cfg.head_dim
+        n_layers = cfg.num_layers if layers is None else layers
+        self.layers = []
+        for li in range(n_layers):
+            qkv_q, qkv_s = self._shard_qkv(*_rand_int4(H, cfg.q_size + 2 * cfg.kv_size, gen, dev))
+            o_q, o_s = _rand_int4(cfg.q_size, H, gen, dev)
+            o_q, o_s = self._shard_rows(o_q, o_s, sh.hq_local * D)
+            gu_q, gu_s = _rand_int4(H, 2 * cfg.intermediate, gen, dev)
+            gu_q, gu_s = self._shard_gate_up(gu_q, gu_s)
+            dn_q, dn_s = _rand_int4(cfg.intermediate, H, gen, dev)
+            dn_q, dn_s = self._shard_rows(dn_q, dn_s, sh.inter_local)
+            pre = "model.layers.%d." % li
+            self.layers.append(LayerWeights(
+                input_norm=(1.0 + 0.02 * torch.randn(H, generator=gen, device=dev)).bfloat16(),
+                post_norm=(1.0 + 0.02 * torch.randn(H, generator=gen, device=dev)).bfloat16(),
+                qkv=Int4Linear(pre + "self_attn.qkv_proj", qkv_q, qkv_s),
+                o=Int4Linear(pre + "self_attn.o_proj", o_q, o_s),
+                gate_up=Int4Linear(pre + "mlp.gate_up_proj", gu_q, gu_s),
+                down=Int4Linear(pre + "mlp.down_proj", dn_q, dn_s),
+            ))
+        V = cfg.vocab
+        v0, v1 = self.vocab_start, self.vocab_start + sh.vocab_local
+        emb = torch.randn(V, H, generator=gen, device=dev) * 0.02
+        codes, scales = gptq.quantize_int8_rows(emb[v0:v1])
+        self.embed_codes, self.embed_scales = codes.contiguous(), scales.view(-1).contiguous()
+        del emb
+        head = torch.randn(V, H, generator=gen, device=dev) * 0.02
+        hq, hs = gptq.quantize_int8_rows(head[v0:v1])
+        self.lm_head = Int8RowLinear("lm_head", hq.contiguous(), hs.view(-1).contiguous())
+        del head
+        self.final_norm = (1.0 + 0.02 * torch.randn(H, generator=gen, device=dev)).bfloat16()
+        self.rope = rope_table(cfg.max_position, D, cfg.rope_theta, dev)
+        return self
+
+    def _shard_qkv(self, qw, sc):
+        """Column shard of the fused [q | k | v] projection for this rank."""
+        cfg, sh = self.cfg, self.shape
+        D = cfg.head_dim
+        q0 = self.rank * sh.hq_local * D
+        cols = [torch.arange(q0, q0 + sh.hq_local * D, device=qw.device)]
+        kv_heads = sh.kv_heads_of(self.rank, cfg.num_kv_heads)
+        for base in (cfg.q_size, cfg.q_size + cfg.kv_size):
+            for h in kv_heads:
+                cols.append(torch.arange(base + h * D, base + (h + 1) * D, device=qw.device))
+        idx = torch.cat(cols)
+        return qw[:, idx].contiguous(), sc[:, idx].contiguous()
+
+    def _shard_rows(self, qw, sc, k_local):
+        """Row (K) shard for a row-parallel projection."""
+        if self.tp == 1:
+            return qw, sc
+        k0 = self.rank * k_local
+        return (qw[k0 // 8:(k0 + k_local) // 8].contiguous(),
+                sc[k0 // 128:(k0 + k_local) // 128].contiguous())
+
+    def _shard_gate_up(self, qw, sc):
+        if self.tp == 1:
+            return qw, sc
+        I, il = self.cfg.intermediate, self.shape.inter_local
+        r = self.rank
+        idx = torch.cat([torch.arange(r * il, (r + 1) * il), torch.arange(I + r * il, I + (r + 1) * il)]).to(qw.device)
+        return qw[:, idx].contiguous(), sc[:, idx].contiguous()
+
+    # ------------------------------------------------------------- forward
+    def _all_reduce(self, t: torch.Tensor) -> torch.Tensor:
+        if self.tp > 1:
+            self.comm.all_reduce(t)
+        return t
+
+    def embed(self, ids: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        x = ops.embed_int8(ids, self.embed_codes, self.embed_scales, start=self.vocab_start, out=out)
+        return self._all_reduce(x)
+
+    def forward(self, inp: StepInputs, kv_caches: list[torch.Tensor], ws=None) -> torch.Tensor:
+        """Run every layer; returns the final-normed hidden rows ``inp.logit_rows``."""
+        cfg, sh = self.cfg, self.shape
+        T = inp.input_ids.shape[0]
+        H, D = cfg.hidden, cfg.head_dim
+        x = self.embed(inp.input_ids)
+        residual = None
+        hq, hkv = sh.hq_local, sh.hkv_local
+        splitk_ws = ws.splitk if ws is not None else None
+        for li, L in enumerate(self.layers):
+            # ---- attention block
+            if residual is None:
+                residual = x.clone()
+                h = ops.rmsnorm(x, L.input_norm, cfg.rms_eps)
+            else:
+                h = ops.rmsnorm(x, L.input_norm, cfg.rms_eps, residual=residual)
+            qkv = L.qkv(h, ws=splitk_ws)
+            q = torch.empty((T, hq, D), dtype=torch.bfloat16, device=self.device)
+            cache = kv_caches[li]
+            ops.rope_store(qkv, self.rope, inp.positions, q, inp.slots, cache, hq, hkv)
+            if inp.is_decode:
+                a = ops.decode_attn(q, inp.cu_q, inp.seq_lens, inp.block_table, cache, hkv, sh.gqa_local,
+                                    inp.max_q_len, nsplit=inp.nsplit, q_ends=inp.q_ends,
+                                    ws=(ws.attn if ws is not None else None))
+            else:
+                a = ops.prefill_attn(q, inp.cu_q, inp.seq_lens, inp.block_table, cache, hkv, sh.gqa_local,
+                                     inp.max_q_len)
+            x = L.o(a.view(T, hq * D), ws=splitk_ws)
+            self._all_reduce(x)
+            # ---- MLP block
+            if uses_w4a8(L.gate_up.name, T, self.w4a8):
+                hq8, hs = ops.rmsnorm(x, L.post_norm, cfg.rms_eps, residual=residual, quant=True)
+                gu = L.gate_up(xq=hq8, xs=hs)
+                aq, as_ = ops.silu_mul(gu, quant=True)
+                x = L.down(xq=aq, xs=as_)
+            else:
+                h = ops.rmsnorm(x, L.post_norm, cfg.rms_eps, residual=residual)
+                gu = L.gate_up(h, ws=splitk_ws)
+                act = ops.silu_mul(gu)
+                x = L.down(act, ws=splitk_ws)
+            self._all_reduce(x)
+        rows = inp.logit_rows
+        xs = x.index_select(0, rows)
+        rs = residual.index_select(0, rows)
+        return ops.rmsnorm(xs, self.final_norm, cfg.rms_eps, residual=rs)
+
+    def logits(self, hidden: torch.Tensor) -> torch.Tensor:
+        """Local vocab shard logits ``[rows, V/tp]`` (bf16)."""
+        q, s = ops.quant_rows(hidden)
+        return self.lm_head(q, s)
+
+    def greedy(self, hidden: torch.Tensor) -> torch.Tensor:
+        """Greedy token ids ``[rows]`` (int64), reduced over vocab shards."""
+        lg = self.logits(hidden)
+        val, idx = ops.argmax(lg, offset=self.vocab_start)
+        if self.tp > 1:
+            val, idx = self.comm.argmax_reduce(val, idx)
+        return idx
+
+    # ------------------------------------------------------------ reference
+    def reference_forward(self, inp: StepInputs, kv_caches_cpu: list[torch.Tensor]):
+        """fp32 torch reference of :meth:`forward` (TP1) for tests."""
+        from ..kv.oracle import attention_ref
+        from ..kv.pack import gather_sequence, store_tokens
+        cfg = self.cfg
+        H, D = cfg.hidden, cfg.head_dim
+        ids = inp.input_ids.cpu()
+        x = (self.embed_codes.cpu()[ids].bfloat16() * self.embed_scales.cpu()[ids].view(-1, 1).bfloat16())
+        residual = None
+        sh = self.shape
+        cu = inp.cu_q.cpu().tolist()
+        lens = inp.seq_lens.cpu().tolist()
+        bt = inp.block_table.cpu()
+        pos = inp.positions.cpu()
+        rope = self.rope.cpu()
+
+        def norm(v, w, res):
+            if res is not None:
+                v = (v.float() + res.float()).bfloat16()
+            vf = v.float()
+            y = (vf * torch.rsqrt(vf.pow(2).mean(-1, keepdim=True) + cfg.rms_eps)).bfloat16()
+            return (w.cpu().float() * y.float()).bfloat16(), v
+
+        def rot(t):
+            c = rope[pos, : D // 2].unsqueeze(1)
+            s = rope[pos, D // 2:].unsqueeze(1)
+            a, b = t[..., : D // 2].float(), t[..., D // 2:].float()
+            return torch.cat([a * c - b * s, b * c + a * s], -1).bfloat16()
+
+        for li, L in enumerate(self.layers):
+            h, residual = norm(x, L.input_norm, residual) if residual is not None else (norm(x, L.input_norm, None)[0], x)
+            qkv = (h.float() @ gptq.dequant_int4(L.qkv.qweight.cpu(), L.qkv.scales.cpu())).bfloat16()
+            T = qkv.shape[0]
+            qkv = qkv.view(T, sh.hq_local + 2 * sh.hkv_local, D)
+            q = rot(qkv[:, : sh.hq_local])
+            k = rot(qkv[:, sh.hq_local: sh.hq_local + sh.hkv_local])
+            v = qkv[:, sh.hq_local + sh.hkv_local:]
+            store_tokens(kv_caches_cpu[li], inp.slots.cpu(), k, v, self.layout)
+            outs = []
+            for b in range(len(lens)):
+                qs = q[cu[b]:cu[b + 1]]
+                ql = qs.shape[0]
+                npg = (lens[b] + 15) // 16
+                kd, vd = gather_sequence(kv_caches_cpu[li], bt[b, :npg].tolist(), lens[b], self.layout)
+                ends = [lens[b] - ql + t + 1 for t in range(ql)]
+                outs.append(attention_ref(qs.float(), kd, vd, ends, sh.gqa_local))
+            a = torch.cat(outs, 0).bfloat16().view(T, -1)
+            x = (a.float() @ gptq.dequant_int4(L.o.qweight.cpu(), L.o.scales.cpu())).bfloat16()
+            h, residual = norm(x, L.post_norm, residual)
+            gu = (h.float() @ gptq.dequant_int4(L.gate_up.qweight.cpu(), L.gate_up.scales.cpu())).bfloat16()
+            I = gu.shape[1] // 2
+            act = (torch.nn.functional.silu(gu[:, :I].float()) * gu[:, I:].float()).bfloat16()
+            x = (act.float() @ gptq.dequant_int4(L.down.qweight.cpu(), L.down.scales.cpu())).bfloat16()
+        rows = inp.logit_rows.cpu()
+        y, _ = norm(x[rows], self.final_norm, residual[rows])
+        return y

@@ -7,7 +7,7 @@ the CUDA kernel or fails loudly.
 """
 from __future__ import annotations
 
-import importlib
+import glob
 import math
 import os
 
@@ -23,7 +23,10 @@ def load() -> bool:
     if _LOADED:
         return True
     try:
-        importlib.import_module("k8v4_xpu_b200._C")
+        path = _library_file()
+        if path is None:
+            raise ImportError("no built k8v4_xpu_b200/_C*.so")
+        torch.ops.load_library(path)
         _ = torch.ops.k8v4.status
         _LOADED = True
         _ERROR = None
@@ -44,11 +47,17 @@ def available() -> bool:
     return load()
 
 
+def _library_file() -> str | None:
+    pkg = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    found = sorted(glob.glob(os.path.join(pkg, "_C*.so")))
+    return found[0] if found else None
+
+
 def extension_path() -> str | None:
+    """Path of the loaded in-tree kernel library."""
     if not load():
         return None
-    mod = importlib.import_module("k8v4_xpu_b200._C")
-    return os.path.abspath(mod.__file__)
+    return _library_file()
 
 
 def status(clear: bool = True) -> int:

@@ -1,0 +1,306 @@
+"""The serving engine: requests in, tokens out.
+
+``LLMEngine`` owns one TP rank's model, its K8/V4 cache (one uint8 page
+pool per layer), the block manager, the scheduler, the decode CUDA-graph
+runner and the optional MTP speculator. ``step()`` runs one scheduler step:
+
+1. the scheduler picks decode tokens and prefill chunks (token budget 4,224);
+2. the host builds the step's metadata (ids, positions, slots, block tables,
+   lengths) in pinned memory and copies it to the device in one go;
+3. decode-only steps replay a captured CUDA graph, other steps run eagerly;
+4. the sampled ids come back to pinned host memory; sequences advance.
+
+Every TP rank runs the same engine on the same request stream (rank 0 drives
+the API; the others follow with identical scheduling decisions), so ranks
+issue the same collectives in the same order.
+"""
+from __future__ import annotations
+
+import dataclasses
+import math
+import os
+import time
+
+import numpy as np
+import torch
+
+from .. import ops
+from ..kv.layout import ATTN_TILE_ROWS
+from ..models.config import ModelConfig
+from ..models.dense import DenseModel, StepInputs
+from .block_manager import BlockManager, CapacityError
+from .scheduler import SamplingParams, Scheduler, Sequence
+from .workspace import Workspace
+
+NUM_SMS = 148
+
+
+@dataclasses.dataclass
+class EngineConfig:
+    """Typed engine configuration (CLI > env > defaults; see ``config.resolve``)."""
+
+    model: str = "dense-27b"
+    tensor_parallel_size: int = 1
+    context_parallel_size: int = 1
+    kv_cache_dtype: str = "int8_k_int4_v"
+    max_model_len: int = 262144
+    max_num_seqs: int = 4
+    max_num_batched_tokens: int = 4224
+    enable_prefix_caching: bool = True
+    block_size: int = 16
+    gpu_memory_utilization: float = 0.90
+    num_kv_blocks: int | None = None
+    speculative_tokens: int = 0      # MTP draft tokens per step (6 in the reference profile)
+    cuda_graphs: bool = True          # FULL_DECODE_ONLY capture
+    capture_sizes: tuple[int, ...] = ()
+    seed: int = 0
+    layers: int | None = None         # override (tests / smoke)
+    forced_accept_mean: float | None = None  # MTP forced-acceptance benchmark mode
+    device: str = "cuda"
+
+    def __post_init__(self):
+        if self.kv_cache_dtype != "int8_k_int4_v":
+            raise ValueError("kv_cache_dtype must be int8_k_int4_v")
+        if self.max_num_batched_tokens < 1:
+            raise ValueError("max_num_batched_tokens must be positive")
+
+
+def decode_splits(max_pages: int, nseq: int, heads: int) -> int:
+    """Split-K factor for decode attention: about two waves of CTAs."""
+    tiles = max(1, (max_pages + 7) // 8)
+    want = max(1, (2 * NUM_SMS) // max(1, nseq * heads))
+    return int(max(1, min(want, tiles, 64)))
+
+
+class LLMEngine:
+    def __init__(self, cfg: EngineConfig, model_cfg: ModelConfig, comm=None, rank: int = 0):
+        self.cfg = cfg
+        self.mcfg = model_cfg
+        self.rank = rank
+        self.tp = cfg.tensor_parallel_size
+        self.device = torch.device(cfg.device)
+        ops.require()
+        self.model = DenseModel(model_cfg, tp=self.tp, rank=rank, device=self.device, comm=comm)
+        self.model.random_init(seed=cfg.seed, layers=cfg.layers)
+        self.layout = self.model.layout
+        self._alloc_cache()
+        self.blocks = BlockManager(self.num_blocks, cfg.block_size, self.layout.page, cfg.enable_prefix_caching)
+        width = 1 + cfg.speculative_tokens
+        self.scheduler = Scheduler(self.blocks, cfg.max_num_seqs, cfg.max_num_batched_tokens, width,
+                                   cfg.max_model_len)
+        self.max_pages = (cfg.max_model_len + self.layout.page - 1) // self.layout.page + 1
+        self.max_q = max(1, width)
+        self.max_tokens = max(cfg.max_num_batched_tokens, cfg.max_num_seqs * width)
+        self.ws = Workspace(self.device, self.max_tokens, cfg.max_num_seqs, self.max_pages,
+                            max(2 * model_cfg.intermediate // self.tp, model_cfg.hidden, 4096),
+                            self.layout.hkv, self.layout.gqa, self.max_q, 64)
+        self.graphs = None
+        self.mtp = None
+        if cfg.speculative_tokens:
+            from ..spec.mtp import MTPSpeculator
+            self.mtp = MTPSpeculator(self, cfg.speculative_tokens, cfg.forced_accept_mean, cfg.seed)
+        if cfg.cuda_graphs:
+            from .graphs import DecodeGraphs
+            self.graphs = DecodeGraphs(self)
+        # pinned host staging for the per-step copies
+        self._pin_i64 = torch.zeros(4 * self.max_tokens, dtype=torch.int64, pin_memory=True)
+        self._pin_i32 = torch.zeros(2 * (cfg.max_num_seqs + 1) + cfg.max_num_seqs * self.max_pages
+                                    + self.max_tokens, dtype=torch.int32, pin_memory=True)
+        self._pin_out = torch.zeros(self.max_tokens, dtype=torch.int64, pin_memory=True)
+        self.h2d_bytes = 0
+        self.d2h_bytes = 0
+        self.stats = {"steps": 0, "prompt_tokens": 0, "generated_tokens": 0, "prefill_time": 0.0,
+                      "decode_time": 0.0, "iteration_tokens": []}
+
+    # ---------------------------------------------------------------- cache
+    def _alloc_cache(self) -> None:
+        cfg = self.cfg
+        page_bytes = self.layout.page_bytes
+        n_layers = len(self.model.layers)
+        if cfg.num_kv_blocks is not None:
+            blocks = int(cfg.num_kv_blocks)
+        else:
+            free, total = torch.cuda.mem_get_info(self.device)
+            budget = free - (1 - cfg.gpu_memory_utilization) * total - (4 << 30)
+            blocks = int(budget // (page_bytes * n_layers * (cfg.block_size // self.layout.page)))
+            need = ((cfg.max_model_len + cfg.block_size - 1) // cfg.block_size + 1) * cfg.max_num_seqs
+            blocks = max(1, min(blocks, need))
+        if blocks < 1:
+            raise CapacityError("no memory left for the KV cache")
+        self.num_blocks = blocks
+        pages = blocks * (cfg.block_size // self.layout.page)
+        self.kv_pool = torch.empty((n_layers, pages, page_bytes), dtype=torch.uint8, device=self.device)
+        self.kv_caches = [self.kv_pool[i] for i in range(n_layers)]
+        self.kv_capacity_tokens = blocks * cfg.block_size
+
+    # ------------------------------------------------------------- requests
+    def add_request(self, prompt: list[int], params: SamplingParams | None = None) -> Sequence:
+        return self.scheduler.add(prompt, params)
+
+    def has_unfinished(self) -> bool:
+        return self.scheduler.has_work()
+
+    # ----------------------------------------------------------------- step
+    def _build_inputs(self, sched) -> tuple[StepInputs, list]:
+        """Pack the step's metadata on the host, copy it to the device once."""
+        chunks = sched.chunks
+        T = sched.num_tokens
+        B = len(chunks)
+        ids = np.zeros(T, np.int64)
+        pos = np.zeros(T, np.int64)
+        slots = np.zeros(T, np.int64)
+        cu = np.zeros(B + 1, np.int32)
+        lens = np.zeros(B, np.int32)
+        logit_rows = []
+        tables = []
+        t = 0
+        max_q = 1
+        for i, c in enumerate(chunks):
+            seq = c.seq
+            toks = seq.tokens
+            n = c.num_tokens
+            feed = toks[c.start:c.start + n] if c.is_prefill else ([toks[-1]] + seq.draft)[:n]
+            ids[t:t + n] = feed
+            pos[t:t + n] = np.arange(c.start, c.start + n)
+            for j in range(n):
+                slots[t + j] = self.blocks.slot(seq.seq_id, c.start + j)
+            cu[i + 1] = t + n
+            lens[i] = c.start + n
+            if c.needs_logits:
+                if c.is_prefill:
+                    logit_rows.append(t + n - 1)
+                else:
+                    logit_rows.extend(range(t, t + n))
+            tables.append(self.blocks.page_table(seq.seq_id))
+            max_q = max(max_q, n)
+            t += n
+        W = max(len(tb) for tb in tables)
+        bt = np.zeros((B, W), np.int32)
+        for i, tb in enumerate(tables):
+            bt[i, :len(tb)] = tb
+        dev = self.device
+        # one pinned staging buffer per dtype, one async copy each
+        L = len(logit_rows)
+        i64 = self._pin_i64[: 3 * T + L].numpy()
+        i64[:T], i64[T:2 * T], i64[2 * T:3 * T], i64[3 * T:] = ids, pos, slots, logit_rows
+        i32 = self._pin_i32[: B + 1 + B + B * W].numpy()
+        i32[: B + 1] = cu
+        i32[B + 1: 2 * B + 1] = lens
+        i32[2 * B + 1:] = bt.reshape(-1)
+        g64 = self._pin_i64[: 3 * T + L].to(dev, non_blocking=True)
+        g32 = self._pin_i32[: 2 * B + 1 + B * W].to(dev, non_blocking=True)
+        self.h2d_bytes += g64.numel() * 8 + g32.numel() * 4
+        inp = StepInputs(
+            input_ids=g64[:T], positions=g64[T:2 * T], slots=g64[2 * T:3 * T], logit_rows=g64[3 * T:],
+            cu_q=g32[: B + 1], seq_lens=g32[B + 1: 2 * B + 1], block_table=g32[2 * B + 1:].view(B, W),
+            max_q_len=max_q, is_decode=sched.is_decode_only and max_q * self.layout.gqa <= 64,
+        )
+        if inp.is_decode:
+            inp.nsplit = decode_splits(W, B, self.layout.hkv)
+        return inp, logit_rows
+
+    def step(self) -> list[Sequence]:
+        """One scheduler step. Returns sequences that finished during it."""
+        sched = self.scheduler.schedule()
+        if not sched.chunks:
+            return []
+        t0 = time.perf_counter()
+        if self.mtp is not None and sched.is_decode_only:
+            finished = self.mtp.step(sched)
+        else:
+            finished = self._plain_step(sched)
+        dt = time.perf_counter() - t0
+        self.stats["steps"] += 1
+        self.stats["iteration_tokens"].append(sched.num_tokens)
+        if sched.is_decode_only:
+            self.stats["decode_time"] += dt
+        else:
+            self.stats["prefill_time"] += dt
+        return finished
+
+    def _plain_step(self, sched) -> list[Sequence]:
+        if self.graphs is not None and sched.is_decode_only and self.graphs.can_run(sched):
+            tokens = self.graphs.run(sched)
+        else:
+            inp, _ = self._build_inputs(sched)
+            hidden = self.model.forward(inp, self.kv_caches, self.ws)
+            tokens = self._sample(hidden)
+        return self._commit(sched, tokens)
+
+    def _sample(self, hidden: torch.Tensor) -> np.ndarray:
+        ids = self.model.greedy(hidden)
+        n = ids.numel()
+        out = self._pin_out[:n]
+        out.copy_(ids, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        self.d2h_bytes += n * 8
+        return out.numpy().copy()
+
+    def _commit(self, sched, tokens: np.ndarray) -> list[Sequence]:
+        finished = []
+        k = 0
+        now = time.monotonic()
+        for c in sched.chunks:
+            seq = c.seq
+            seq.computed = c.start + c.num_tokens
+            if c.is_prefill:
+                self.stats["prompt_tokens"] += c.num_tokens
+            self.blocks.publish(seq.seq_id, seq.tokens, seq.computed)
+            if not c.needs_logits:
+                continue
+            tok = int(tokens[k])
+            k += 1
+            if seq.first_token_time is None:
+                seq.first_token_time = now
+            seq.output.append(tok)
+            self.stats["generated_tokens"] += 1
+            if self._should_stop(seq, tok):
+                self.scheduler.finish(seq, "length" if len(seq.output) >= seq.params.max_tokens else "stop")
+                finished.append(seq)
+        return finished
+
+    def _should_stop(self, seq: Sequence, tok: int) -> bool:
+        if len(seq.output) >= seq.params.max_tokens:
+            return True
+        return (not seq.params.ignore_eos) and tok in seq.params.stop_token_ids
+
+    # ------------------------------------------------------------ helpers
+    def generate(self, prompts: list[list[int]], params: SamplingParams | None = None) -> list[list[int]]:
+        seqs = [self.add_request(p, params) for p in prompts]
+        while self.has_unfinished():
+            self.step()
+        return [s.output for s in seqs]
+
+    def fork_sequence(self, seq: Sequence) -> Sequence:
+        """A new running sequence with the same tokens and its own copy of the KV tail."""
+        child = Sequence(next(self.scheduler._ids), list(seq.prompt), seq.params, list(seq.output))
+        copies = self.blocks.fork(seq.seq_id, child.seq_id, seq.computed)
+        r = self.blocks.ratio
+        for src, dst in copies:
+            for layer in self.kv_caches:
+                layer[dst * r:(dst + 1) * r].copy_(layer[src * r:(src + 1) * r])
+        child.computed = seq.computed
+        child.status = seq.status
+        child.first_token_time = seq.first_token_time
+        self.scheduler.running.append(child)
+        return child
+
+    def clone_sequence_private(self, seq: Sequence) -> Sequence:
+        """A new running sequence holding a private copy of every KV page.
+
+        Used to build several long contexts from one prefill without sharing
+        pages (so concurrent decodes read distinct memory).
+        """
+        child = Sequence(next(self.scheduler._ids), list(seq.prompt), seq.params, list(seq.output))
+        self.blocks.tables[child.seq_id] = []
+        self.blocks.keys[child.seq_id] = []
+        self.blocks.ensure(child.seq_id, seq.computed)
+        src = torch.tensor(self.blocks.page_table(seq.seq_id), device=self.device)
+        dst = torch.tensor(self.blocks.page_table(child.seq_id), device=self.device)
+        for layer in self.kv_caches:
+            layer.index_copy_(0, dst, layer.index_select(0, src))
+        child.computed = seq.computed
+        child.status = seq.status
+        child.first_token_time = seq.first_token_time
+        self.scheduler.running.append(child)
+        return child

@@ -1,0 +1,131 @@
+"""Full-decode-only CUDA graphs.
+
+One graph per (batch size, query width) in the capture list: the whole
+decode forward (embedding, every layer's GEMMs, RoPE + KV write, split-K
+attention, collectives) plus the lm_head and greedy sampling. Graph inputs
+live in the workspace's persistent buffers; a step copies that step's
+metadata into them from pinned host memory and replays. Capture sizes follow
+the reference's FULL_DECODE_ONLY profile (multiples of the decode width,
+``k8v4_v030/launch.sh:65-70``); prefill never runs inside a graph (the
+reference raised if it tried, ``k8v4_v030/backend.py:290-291``).
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from ..models.dense import StepInputs
+
+
+class DecodeGraphs:
+    def __init__(self, engine, widths: tuple[int, ...] | None = None):
+        self.engine = engine
+        cfg = engine.cfg
+        self.width = 1 + cfg.speculative_tokens
+        sizes = cfg.capture_sizes or tuple(range(1, cfg.max_num_seqs + 1))
+        self.sizes = sorted(set(int(s) for s in sizes if 1 <= s <= cfg.max_num_seqs))
+        self.graphs: dict[tuple[int, int], tuple[torch.cuda.CUDAGraph, torch.Tensor, int]] = {}
+        self.pool = None
+        self.captured = False
+
+    def can_run(self, sched) -> bool:
+        B = len(sched.chunks)
+        widths = {c.num_tokens for c in sched.chunks}
+        return len(widths) == 1 and next(iter(widths)) in (1, self.width) and B <= max(self.sizes)
+
+    def _inputs(self, B: int, w: int, nsplit: int) -> StepInputs:
+        ws = self.engine.ws
+        T = B * w
+        return StepInputs(
+            input_ids=ws.input_ids[:T], positions=ws.positions[:T], slots=ws.slots[:T],
+            cu_q=ws.cu_q[: B + 1], seq_lens=ws.seq_lens[:B], block_table=ws.block_table[:B],
+            logit_rows=ws.logit_rows[:T], max_q_len=w, is_decode=True, nsplit=nsplit,
+        )
+
+    def capture(self, widths: tuple[int, ...] | None = None) -> None:
+        eng = self.engine
+        from .engine import decode_splits
+        widths = widths or tuple(sorted({1, self.width}))
+        ws = eng.ws
+        stream = torch.cuda.Stream(device=eng.device)
+        for w in widths:
+            for B in self.sizes:
+                nsplit = decode_splits(eng.max_pages, B, eng.layout.hkv)
+                T = B * w
+                # benign metadata: every sequence one page long
+                ws.cu_q[: B + 1].copy_(torch.arange(0, T + 1, w, dtype=torch.int32, device=eng.device))
+                ws.seq_lens[:B].fill_(w)
+                ws.block_table[:B].zero_()
+                ws.slots[:T].copy_(torch.arange(T, device=eng.device) % eng.layout.page)
+                ws.positions[:T].zero_()
+                ws.input_ids[:T].zero_()
+                ws.logit_rows[:T].copy_(torch.arange(T, device=eng.device))
+                inp = self._inputs(B, w, nsplit)
+                stream.wait_stream(torch.cuda.current_stream(eng.device))
+                with torch.cuda.stream(stream):
+                    for _ in range(2):  # warm-up (kernel attributes, allocator)
+                        hid = eng.model.forward(inp, eng.kv_caches, ws)
+                        out = eng.model.greedy(hid)
+                torch.cuda.current_stream(eng.device).wait_stream(stream)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, pool=self.pool, stream=stream):
+                    hid = eng.model.forward(inp, eng.kv_caches, ws)
+                    out = eng.model.greedy(hid)
+                if self.pool is None:
+                    self.pool = g.pool()
+                self.graphs[(B, w)] = (g, out, nsplit)
+        torch.cuda.synchronize(eng.device)
+        self.captured = True
+
+    def run(self, sched) -> np.ndarray:
+        eng = self.engine
+        if not self.captured:
+            self.capture()
+        B_real = len(sched.chunks)
+        w = sched.chunks[0].num_tokens
+        B = next(s for s in self.sizes if s >= B_real)
+        g, out, _nsplit = self.graphs[(B, w)]
+        T = B * w
+        ws = eng.ws
+        # host metadata (padding rows repeat sequence 0 with a dropped write)
+        ids = np.zeros(T, np.int64)
+        pos = np.zeros(T, np.int64)
+        slots = np.full(T, -1, np.int64)
+        lens = np.zeros(B, np.int32)
+        tables = []
+        for i, c in enumerate(sched.chunks):
+            seq = c.seq
+            toks = [seq.tokens[-1]] + seq.draft
+            ids[i * w:(i + 1) * w] = toks[:w]
+            pos[i * w:(i + 1) * w] = np.arange(c.start, c.start + w)
+            for j in range(w):
+                slots[i * w + j] = eng.blocks.slot(seq.seq_id, c.start + j)
+            lens[i] = c.start + w
+            tables.append(eng.blocks.page_table(seq.seq_id))
+        for i in range(B_real, B):
+            lens[i] = w  # padding sequence: reads page 0, writes nothing
+            tables.append([0])
+        Wd = ws.block_table.shape[1]
+        pin64 = eng._pin_i64[: 3 * T].numpy()
+        pin64[:T], pin64[T:2 * T], pin64[2 * T:] = ids, pos, slots
+        pin32 = eng._pin_i32[: B + B * Wd].numpy()
+        pin32[:B] = lens
+        bt = pin32[B:].reshape(B, Wd)
+        bt[:] = 0
+        for i, tb in enumerate(tables):
+            bt[i, :len(tb)] = tb
+        g64 = eng._pin_i64[: 3 * T].to(eng.device, non_blocking=True)
+        g32 = eng._pin_i32[: B + B * Wd].to(eng.device, non_blocking=True)
+        ws.input_ids[:T].copy_(g64[:T], non_blocking=True)
+        ws.positions[:T].copy_(g64[T:2 * T], non_blocking=True)
+        ws.slots[:T].copy_(g64[2 * T:], non_blocking=True)
+        ws.seq_lens[:B].copy_(g32[:B], non_blocking=True)
+        ws.block_table[:B].copy_(g32[B:].view(B, Wd), non_blocking=True)
+        eng.h2d_bytes += 3 * T * 8 + (B + B * Wd) * 4
+        g.replay()
+        n = B_real * w
+        host = eng._pin_out[:n]
+        host.copy_(out[:n], non_blocking=True)
+        torch.cuda.current_stream(eng.device).synchronize()
+        eng.d2h_bytes += n * 8
+        return host.numpy().copy()

@@ -1,0 +1,188 @@
+"""Continuous-batching scheduler with chunked prefill.
+
+Each step spends a token budget (``max_num_batched_tokens``, default 4,224 as
+in the reference deployment, ``k8v4_v030/launch.sh:185``) decode-first:
+every running sequence that is generating gets its decode tokens (1, or
+1 + draft tokens under MTP), then the remaining budget goes to prefill chunks
+of sequences that still have prompt tokens, in arrival order, admitting
+waiting requests while ``max_num_seqs`` and the KV pool allow. A prompt
+longer than the remaining budget is split into chunks across steps.
+"""
+from __future__ import annotations
+
+import collections
+import dataclasses
+import enum
+import itertools
+import time
+
+from .block_manager import BlockManager, CapacityError
+
+
+class SeqStatus(enum.Enum):
+    WAITING = "waiting"
+    RUNNING = "running"
+    FINISHED = "finished"
+
+
+@dataclasses.dataclass
+class SamplingParams:
+    max_tokens: int = 16
+    ignore_eos: bool = False
+    stop_token_ids: tuple[int, ...] = ()
+    temperature: float = 0.0  # greedy decoding (the benchmark path)
+
+
+@dataclasses.dataclass
+class Sequence:
+    seq_id: int
+    prompt: list[int]
+    params: SamplingParams
+    output: list[int] = dataclasses.field(default_factory=list)
+    status: SeqStatus = SeqStatus.WAITING
+    computed: int = 0          # tokens whose KV is written
+    cached_tokens: int = 0     # prompt tokens served by the prefix cache
+    arrival: float = dataclasses.field(default_factory=time.monotonic)
+    first_token_time: float | None = None
+    finish_time: float | None = None
+    finish_reason: str | None = None
+    draft: list[int] = dataclasses.field(default_factory=list)  # MTP proposals for the next step
+    prefill_start: float | None = None
+
+    @property
+    def tokens(self) -> list[int]:
+        return self.prompt + self.output
+
+    @property
+    def num_tokens(self) -> int:
+        return len(self.prompt) + len(self.output)
+
+    @property
+    def in_prefill(self) -> bool:
+        return self.computed < len(self.prompt)
+
+    @property
+    def done(self) -> bool:
+        return self.status == SeqStatus.FINISHED
+
+
+@dataclasses.dataclass
+class ScheduledChunk:
+    seq: Sequence
+    start: int        # first token position of this chunk
+    num_tokens: int   # tokens fed this step
+    is_prefill: bool
+    needs_logits: bool
+
+
+@dataclasses.dataclass
+class SchedulerOutput:
+    chunks: list[ScheduledChunk]
+    num_tokens: int
+    is_decode_only: bool
+    preempted: list[Sequence] = dataclasses.field(default_factory=list)
+
+
+class Scheduler:
+    def __init__(self, blocks: BlockManager, max_num_seqs: int = 4, max_num_batched_tokens: int = 4224,
+                 decode_width: int = 1, max_model_len: int = 262144):
+        if max_num_batched_tokens < 1 or max_num_seqs < 1:
+            raise ValueError("scheduler limits must be positive")
+        self.blocks = blocks
+        self.max_num_seqs = max_num_seqs
+        self.max_num_batched_tokens = max_num_batched_tokens
+        self.decode_width = decode_width  # tokens per decoding sequence per step (1 + MTP drafts)
+        self.max_model_len = max_model_len
+        self.waiting: collections.deque[Sequence] = collections.deque()
+        self.running: list[Sequence] = []
+        self._ids = itertools.count()
+        self.num_preemptions = 0
+
+    def add(self, prompt: list[int], params: SamplingParams | None = None) -> Sequence:
+        if not prompt:
+            raise ValueError("empty prompt")
+        params = params or SamplingParams()
+        if len(prompt) + params.max_tokens > self.max_model_len:
+            raise ValueError("prompt + max_tokens exceeds max_model_len %d" % self.max_model_len)
+        seq = Sequence(next(self._ids), list(prompt), params)
+        self.waiting.append(seq)
+        return seq
+
+    def has_work(self) -> bool:
+        return bool(self.waiting or self.running)
+
+    def _admit(self, seq: Sequence) -> bool:
+        try:
+            cached = self.blocks.allocate(seq.seq_id, seq.prompt)
+        except CapacityError:
+            return False
+        seq.cached_tokens = cached
+        seq.computed = cached
+        seq.status = SeqStatus.RUNNING
+        self.running.append(seq)
+        return True
+
+    def schedule(self) -> SchedulerOutput:
+        budget = self.max_num_batched_tokens
+        chunks: list[ScheduledChunk] = []
+        preempted: list[Sequence] = []
+        # 1) decode tokens of generating sequences
+        for seq in list(self.running):
+            if seq.in_prefill:
+                continue
+            width = 1 + len(seq.draft)
+            if width > budget:
+                continue
+            try:
+                self.blocks.ensure(seq.seq_id, seq.computed + width)
+            except CapacityError:
+                self._preempt(seq)
+                preempted.append(seq)
+                continue
+            chunks.append(ScheduledChunk(seq, seq.computed, width, False, True))
+            budget -= width
+        # 2) prefill chunks of admitted sequences, then admit new ones
+        for seq in self.running:
+            if budget <= 0:
+                break
+            if not seq.in_prefill or any(c.seq is seq for c in chunks):
+                continue
+            n = min(budget, len(seq.prompt) - seq.computed)
+            self.blocks.ensure(seq.seq_id, seq.computed + n)
+            last = seq.computed + n == len(seq.prompt)
+            chunks.append(ScheduledChunk(seq, seq.computed, n, True, last))
+            budget -= n
+        while budget > 0 and self.waiting and len(self.running) < self.max_num_seqs:
+            seq = self.waiting[0]
+            if not self._admit(seq):
+                break
+            self.waiting.popleft()
+            seq.prefill_start = time.monotonic()
+            n = min(budget, len(seq.prompt) - seq.computed)
+            self.blocks.ensure(seq.seq_id, seq.computed + n)
+            last = seq.computed + n == len(seq.prompt)
+            chunks.append(ScheduledChunk(seq, seq.computed, n, True, last))
+            budget -= n
+        total = sum(c.num_tokens for c in chunks)
+        decode_only = bool(chunks) and all(not c.is_prefill for c in chunks)
+        return SchedulerOutput(chunks, total, decode_only, preempted)
+
+    def _preempt(self, seq: Sequence) -> None:
+        """Recompute-style preemption: free the blocks and requeue at the front."""
+        self.blocks.free_seq(seq.seq_id)
+        self.running.remove(seq)
+        seq.status = SeqStatus.WAITING
+        seq.prompt = seq.prompt + seq.output
+        seq.output = []
+        seq.computed = 0
+        seq.draft = []
+        self.waiting.appendleft(seq)
+        self.num_preemptions += 1
+
+    def finish(self, seq: Sequence, reason: str) -> None:
+        seq.status = SeqStatus.FINISHED
+        seq.finish_reason = reason
+        seq.finish_time = time.monotonic()
+        if seq in self.running:
+            self.running.remove(seq)
+        self.blocks.free_seq(seq.seq_id)

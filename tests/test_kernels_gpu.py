@@ -99,7 +99,8 @@ def test_w4a16_gemm(M, split):
     ref = gptq.w4a16_ref(x, qw, sc)
     out = ops.wq_gemm(ops.W4A16, qw.to(DEV), sc.to(DEV), x.to(DEV), split=split)
     torch.cuda.synchronize()
-    assert ops.status() == 0
+    st = ops.status()
+    assert st == 0, "device status 0x%x (code | site<<8)" % st
     err = (out.float().cpu() - ref).abs().max().item()
     assert err <= 2e-2 * ref.abs().max().item() + 1e-3, err
 
@@ -113,7 +114,8 @@ def test_w4a8_gemm(M):
     ref = gptq.w4a8_ref(xq, xs, qw, sc)
     out = ops.wq_gemm(ops.W4A8, qw.to(DEV), sc.to(DEV), xq.to(DEV), xscale=xs.to(DEV))
     torch.cuda.synchronize()
-    assert ops.status() == 0
+    st = ops.status()
+    assert st == 0, "device status 0x%x (code | site<<8)" % st
     err = (out.float().cpu() - ref).abs().max().item()
     assert err <= 1e-2 * ref.abs().max().item() + 1e-3, err
 
@@ -128,7 +130,8 @@ def test_w8a8_gemm(M):
     ref = gptq.w8a8_ref(xq, xs, wq, ws.view(-1))
     out = ops.wq_gemm(ops.W8A8, wq.to(DEV), ws.view(-1).to(DEV), xq.to(DEV), xscale=xs.to(DEV))
     torch.cuda.synchronize()
-    assert ops.status() == 0
+    st = ops.status()
+    assert st == 0, "device status 0x%x (code | site<<8)" % st
     err = (out.float().cpu() - ref).abs().max().item()
     assert err <= 1e-2 * ref.abs().max().item() + 1e-3, err
 
@@ -193,7 +196,8 @@ def test_decode_attn(q_len, nsplit, gqa, hkv):
     out = ops.decode_attn(q, cu, torch.tensor(lens, dtype=torch.int32, device=DEV), bt.to(DEV), cache.to(DEV),
                           hkv, gqa, q_len, nsplit=nsplit)
     torch.cuda.synchronize()
-    assert ops.status() == 0
+    st = ops.status()
+    assert st == 0, "device status 0x%x (code | site<<8)" % st
     err = (out.float().cpu() - ref).abs().max().item()
     assert err < 2e-2, err
 
@@ -210,7 +214,8 @@ def test_prefill_attn(ctx, q_len, gqa, hkv):
     out = ops.prefill_attn(q, cu, torch.tensor(lens, dtype=torch.int32, device=DEV), bt.to(DEV), cache.to(DEV),
                            hkv, gqa, q_len)
     torch.cuda.synchronize()
-    assert ops.status() == 0
+    st = ops.status()
+    assert st == 0, "device status 0x%x (code | site<<8)" % st
     err = (out.float().cpu() - ref).abs().max().item()
     assert err < 2e-2, err
 
