@@ -15,6 +15,13 @@ import torch
 
 _LOADED = False
 _ERROR: str | None = None
+# Kernel launches issued through this module (graph captures record deltas).
+LAUNCHES = 0
+
+
+def _count(n: int = 1) -> None:
+    global LAUNCHES
+    LAUNCHES += n
 
 
 def load() -> bool:
@@ -74,12 +81,14 @@ def kv_store(k: torch.Tensor, v: torch.Tensor, slots: torch.Tensor, cache: torch
              fmt: int = FMT_B200) -> None:
     require()
     torch.ops.k8v4.kv_store(fmt, k, v, slots, cache, hkv)
+    _count()
 
 
 def rope_store(qkv: torch.Tensor, cos_sin: torch.Tensor, positions: torch.Tensor, q_out: torch.Tensor,
                slots: torch.Tensor, cache: torch.Tensor, hq: int, hkv: int) -> None:
     require()
     torch.ops.k8v4.rope_store(qkv, cos_sin, positions, q_out, slots, cache, hq, hkv)
+    _count()
 
 
 def decode_ws_floats(nseq: int, heads: int, nsplit: int, max_q_len: int, gqa: int) -> int:
@@ -101,6 +110,7 @@ def decode_attn(q, cu_q, seq_lens, block_table, cache, hkv, gqa, max_q_len, nspl
                          dtype=torch.float32, device=q.device)
     torch.ops.k8v4.decode_attn(q, cu_q, seq_lens, q_ends, block_table, cache, hkv, head_offset, heads, gqa,
                                max_q_len, nsplit, float(sm_scale), out, ws if nsplit > 1 else None)
+    _count(2 if nsplit > 1 else 1)
     return out
 
 
@@ -115,6 +125,7 @@ def prefill_attn(q, cu_q, seq_lens, block_table, cache, hkv, gqa, max_q_len, out
         sm_scale = 1.0 / math.sqrt(q.shape[-1])
     torch.ops.k8v4.prefill_attn(q, cu_q, seq_lens, block_table, cache, hkv, head_offset, heads, gqa, max_q_len,
                                 float(sm_scale), out)
+    _count()
     return out
 
 
@@ -130,7 +141,10 @@ def wq_gemm(mode: int, w: torch.Tensor, wscale: torch.Tensor, x: torch.Tensor, x
         out = torch.empty((x.shape[0], n), dtype=torch.bfloat16, device=x.device)
     if split > 1 and ws is None:
         ws = torch.zeros((x.shape[0], n), dtype=torch.float32, device=x.device)
+    if x.shape[0] == 0:
+        return out
     torch.ops.k8v4.wq_gemm(mode, w, wscale, x, xscale, residual, out, ws, split)
+    _count(2 if split > 1 else 1)
     return out
 
 
@@ -143,10 +157,12 @@ def rmsnorm(x, w, eps=1e-6, residual=None, out=None, quant=False):
         q = torch.empty(x.shape, dtype=torch.int8, device=x.device)
         s = torch.empty(rows, dtype=torch.float32, device=x.device)
         torch.ops.k8v4.rmsnorm(x, residual, w, out, q, s, eps)
+        _count()
         return (out, q, s) if out is not None else (q, s)
     if out is None:
         out = torch.empty_like(x)
     torch.ops.k8v4.rmsnorm(x, residual, w, out, None, None, eps)
+    _count()
     return out
 
 
@@ -157,10 +173,12 @@ def silu_mul(gu, out=None, quant=False):
         q = torch.empty((rows, inter), dtype=torch.int8, device=gu.device)
         s = torch.empty(rows, dtype=torch.float32, device=gu.device)
         torch.ops.k8v4.silu_mul(gu, out, q, s)
+        _count()
         return q, s
     if out is None:
         out = torch.empty((rows, inter), dtype=torch.bfloat16, device=gu.device)
     torch.ops.k8v4.silu_mul(gu, out, None, None)
+    _count()
     return out
 
 
@@ -169,6 +187,7 @@ def quant_rows(x):
     q = torch.empty(x.shape, dtype=torch.int8, device=x.device)
     s = torch.empty(x.numel() // x.shape[-1], dtype=torch.float32, device=x.device)
     torch.ops.k8v4.quant_rows(x, q, s)
+    _count()
     return q, s
 
 
@@ -177,6 +196,7 @@ def embed_int8(ids, codes, scales, start=0, out=None):
     if out is None:
         out = torch.empty((ids.numel(), codes.shape[1]), dtype=torch.bfloat16, device=codes.device)
     torch.ops.k8v4.embed_int8(ids, codes, scales, out, int(start))
+    _count()
     return out
 
 
@@ -185,4 +205,5 @@ def argmax(logits, offset=0):
     v = torch.empty(logits.shape[0], dtype=torch.float32, device=logits.device)
     i = torch.empty(logits.shape[0], dtype=torch.int64, device=logits.device)
     torch.ops.k8v4.argmax(logits, int(offset), v, i)
+    _count()
     return v, i

@@ -109,6 +109,7 @@ class LLMEngine:
         self._pin_out = torch.zeros(self.max_tokens, dtype=torch.int64, pin_memory=True)
         self.h2d_bytes = 0
         self.d2h_bytes = 0
+        self._h2d_done = None
         self.stats = {"steps": 0, "prompt_tokens": 0, "generated_tokens": 0, "prefill_time": 0.0,
                       "decode_time": 0.0, "iteration_tokens": []}
 
@@ -179,6 +180,9 @@ class LLMEngine:
         for i, tb in enumerate(tables):
             bt[i, :len(tb)] = tb
         dev = self.device
+        # the previous step's async copies must have drained the pinned buffers
+        if self._h2d_done is not None:
+            self._h2d_done.synchronize()
         # one pinned staging buffer per dtype, one async copy each
         L = len(logit_rows)
         i64 = self._pin_i64[: 3 * T + L].numpy()
@@ -190,6 +194,8 @@ class LLMEngine:
         g64 = self._pin_i64[: 3 * T + L].to(dev, non_blocking=True)
         g32 = self._pin_i32[: 2 * B + 1 + B * W].to(dev, non_blocking=True)
         self.h2d_bytes += g64.numel() * 8 + g32.numel() * 4
+        self._h2d_done = torch.cuda.Event()
+        self._h2d_done.record(torch.cuda.current_stream(dev))
         inp = StepInputs(
             input_ids=g64[:T], positions=g64[T:2 * T], slots=g64[2 * T:3 * T], logit_rows=g64[3 * T:],
             cu_q=g32[: B + 1], seq_lens=g32[B + 1: 2 * B + 1], block_table=g32[2 * B + 1:].view(B, W),
@@ -222,9 +228,10 @@ class LLMEngine:
         if self.graphs is not None and sched.is_decode_only and self.graphs.can_run(sched):
             tokens = self.graphs.run(sched)
         else:
-            inp, _ = self._build_inputs(sched)
+            inp, rows = self._build_inputs(sched)
             hidden = self.model.forward(inp, self.kv_caches, self.ws)
-            tokens = self._sample(hidden)
+            # a step made only of non-final prefill chunks samples nothing
+            tokens = self._sample(hidden) if rows else np.zeros(0, np.int64)
         return self._commit(sched, tokens)
 
     def _sample(self, hidden: torch.Tensor) -> np.ndarray:

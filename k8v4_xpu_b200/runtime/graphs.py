@@ -14,6 +14,7 @@ from __future__ import annotations
 import numpy as np
 import torch
 
+from .. import ops
 from ..models.dense import StepInputs
 
 
@@ -27,6 +28,7 @@ class DecodeGraphs:
         self.graphs: dict[tuple[int, int], tuple[torch.cuda.CUDAGraph, torch.Tensor, int]] = {}
         self.pool = None
         self.captured = False
+        self.kernels: dict[tuple[int, int], int] = {}  # our kernel launches per replay
 
     def can_run(self, sched) -> bool:
         B = len(sched.chunks)
@@ -68,14 +70,22 @@ class DecodeGraphs:
                         out = eng.model.greedy(hid)
                 torch.cuda.current_stream(eng.device).wait_stream(stream)
                 g = torch.cuda.CUDAGraph()
+                before = ops.LAUNCHES
                 with torch.cuda.graph(g, pool=self.pool, stream=stream):
                     hid = eng.model.forward(inp, eng.kv_caches, ws)
                     out = eng.model.greedy(hid)
+                self.kernels[(B, w)] = ops.LAUNCHES - before
                 if self.pool is None:
                     self.pool = g.pool()
                 self.graphs[(B, w)] = (g, out, nsplit)
         torch.cuda.synchronize(eng.device)
         self.captured = True
+
+    def release(self) -> None:
+        """Drop every graph (graphs holding NCCL calls must go before the process group)."""
+        self.graphs.clear()
+        self.pool = None
+        self.captured = False
 
     def run(self, sched) -> np.ndarray:
         eng = self.engine
