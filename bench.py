@@ -82,7 +82,7 @@ class ClockSampler:
             self.proc.kill()
         if self.thread:
             self.thread.join(timeout=2)
-        sm, mx, reasons = [], None, set()
+        sm, mx, reasons, loaded = [], None, set(), []
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
         for ln in self.lines:
             parts = [p.strip() for p in ln.split(",")]
@@ -91,20 +91,23 @@ class ClockSampler:
             try:
                 sm.append(float(parts[1]))
                 mx = float(parts[2])
+                if float(parts[3]) > 300.0:  # power.draw: the GPU is busy
+                    loaded.append(float(parts[1]))
             except ValueError:
                 continue
             for name, val in zip(names, parts[5:9]):
                 if val.lower().startswith("active"):
                     reasons.add(name)
-        sm.sort()
-        med = sm[len(sm) // 2] if sm else None
-        return {"sm_mhz": med, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        use = sorted(loaded or sm)
+        med = use[len(use) // 2] if use else None
+        return {"sm_mhz": med, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm),
+                "samples_under_load": len(loaded)}
 
 
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=32)
+    ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--ctx", type=int, default=128197)
@@ -147,7 +150,7 @@ def main() -> int:
 
     rng = np.random.default_rng(0)
     prompt = rng.integers(0, mcfg.vocab, size=ctx).tolist()
-    params = SamplingParams(max_tokens=10**9, ignore_eos=True)
+    params = SamplingParams(max_tokens=decode_budget, ignore_eos=True)
 
     def sync_all():
         torch.cuda.synchronize(dev)

@@ -202,7 +202,8 @@ class LLMEngine:
             max_q_len=max_q, is_decode=sched.is_decode_only and max_q * self.layout.gqa <= 64,
         )
         if inp.is_decode:
-            inp.nsplit = decode_splits(W, B, self.layout.hkv)
+            # same split count as the captured graphs: eager and graph decode are bitwise equal
+            inp.nsplit = decode_splits(self.max_pages, B, self.layout.hkv)
         return inp, logit_rows
 
     def step(self) -> list[Sequence]:

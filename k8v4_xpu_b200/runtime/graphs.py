@@ -58,7 +58,7 @@ class DecodeGraphs:
                 ws.cu_q[: B + 1].copy_(torch.arange(0, T + 1, w, dtype=torch.int32, device=eng.device))
                 ws.seq_lens[:B].fill_(w)
                 ws.block_table[:B].zero_()
-                ws.slots[:T].copy_(torch.arange(T, device=eng.device) % eng.layout.page)
+                ws.slots[:T].fill_(-1)  # capture must not write into live KV pages
                 ws.positions[:T].zero_()
                 ws.input_ids[:T].zero_()
                 ws.logit_rows[:T].copy_(torch.arange(T, device=eng.device))
