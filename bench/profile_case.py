@@ -1,0 +1,78 @@
+#!/usr/bin/env python3
+"""Small, self-terminating cases of single kernels for ncu captures.
+
+Each case holds at most a few hundred MB on the device (inputs just above the
+126 MB L2 so DRAM counters mean something) and launches the kernel a handful
+of times, so an ``ncu --set full -k <kernel> -c 1..3`` capture ends by itself.
+
+    python bench/profile_case.py --case decode|decode7|gemm_m1|gemm_prefill|w4a8_prefill|prefill
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+from k8v4_xpu_b200 import ops  # noqa: E402
+from k8v4_xpu_b200.layers.linear import split_for  # noqa: E402
+
+sys.path.insert(0, os.path.join(ROOT, "bench"))
+from microbench import fill_cache, rand_int4  # noqa: E402
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--case", required=True)
+    ap.add_argument("--reps", type=int, default=3)
+    a = ap.parse_args()
+    ops.require()
+    c = a.case
+    if c in ("decode", "decode7"):
+        ctx, hkv, gqa = 160000, 4, 6
+        q_len = 7 if c == "decode7" else 1
+        layout, cache, bt = fill_cache(ctx, 1, hkv, gqa)
+        q = torch.randn(q_len, hkv * gqa, 128, device="cuda").bfloat16()
+        cu = torch.tensor([0, q_len], dtype=torch.int32, device="cuda")
+        lens = torch.tensor([ctx], dtype=torch.int32, device="cuda")
+        fn = lambda: ops.decode_attn(q, cu, lens, bt, cache, hkv, gqa, q_len, nsplit=37)  # noqa: E731
+    elif c == "prefill":
+        ctx, hkv, gqa, ql = 40000, 4, 6, 4224
+        layout, cache, bt = fill_cache(ctx, 1, hkv, gqa)
+        q = torch.randn(ql, hkv * gqa, 128, device="cuda").bfloat16()
+        cu = torch.tensor([0, ql], dtype=torch.int32, device="cuda")
+        lens = torch.tensor([ctx], dtype=torch.int32, device="cuda")
+        fn = lambda: ops.prefill_attn(q, cu, lens, bt, cache, hkv, gqa, ql)  # noqa: E731
+    elif c == "gemm_m1":
+        N, K = 34816, 5120  # gate_up: 89 MB of int4 weights
+        qw, sc = rand_int4(N, K)
+        x = torch.randn(1, K, device="cuda").bfloat16()
+        ws = torch.zeros(N, dtype=torch.float32, device="cuda")
+        fn = lambda: ops.wq_gemm(ops.W4A16, qw, sc, x, ws=ws, split=split_for(1, N, K))  # noqa: E731
+    elif c in ("gemm_prefill", "w4a8_prefill"):
+        N, K, M = 34816, 5120, 4224
+        qw, sc = rand_int4(N, K)
+        if c == "gemm_prefill":
+            x = torch.randn(M, K, device="cuda").bfloat16()
+            fn = lambda: ops.wq_gemm(ops.W4A16, qw, sc, x)  # noqa: E731
+        else:
+            xq = torch.randint(-127, 127, (M, K), dtype=torch.int8, device="cuda")
+            xs = torch.rand(M, device="cuda") * 0.01
+            fn = lambda: ops.wq_gemm(ops.W4A8, qw, sc, xq, xscale=xs)  # noqa: E731
+    else:
+        raise SystemExit("unknown case %s" % c)
+    for _ in range(a.reps):
+        fn()
+    torch.cuda.synchronize()
+    st = ops.status()
+    if st:
+        raise SystemExit("device status 0x%x" % st)
+    print("ok", c)
+
+
+if __name__ == "__main__":
+    main()
