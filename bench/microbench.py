@@ -38,23 +38,37 @@ HBM, TF, SRC = peaks()
 _flush = None
 
 
-def timeit(fn, iters=20, warmup=5):
+def timeit(fn, iters=20, warmup=3, graph=True):
+    """Median device time of ``fn``: captured in a CUDA graph and replayed
+    after an L2-flushing write, so neither host launch latency nor cached
+    weights enter the number."""
     global _flush
     if _flush is None:
         _flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
-    ts = []
+    run = fn
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            fn()
+        torch.cuda.current_stream().wait_stream(s)
+        with torch.cuda.graph(g, stream=s):
+            fn()
+        run = g.replay
+    evs = []
     for _ in range(iters):
-        _flush.fill_(1)
+        _flush.fill_(1)  # keeps the GPU busy while the host queues the next replay
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
-        fn()
+        run()
         b.record()
-        torch.cuda.synchronize()
-        ts.append(a.elapsed_time(b) / 1e3)
-    ts.sort()
+        evs.append((a, b))
+    torch.cuda.synchronize()
+    ts = sorted(a.elapsed_time(b) / 1e3 for a, b in evs)
     return ts[len(ts) // 2]
 
 

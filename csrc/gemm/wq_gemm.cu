@@ -44,7 +44,7 @@ struct Params {
   int k_per_split;             // multiple of 128
 };
 
-template <int MODE, int BT, int NCONV, int NACC, int STAGES, int RSTAGES>
+template <int MODE, int BT, int NCONV, int NACC, int STAGES, int RSTAGES, int BSTAGES>
 struct Cfg {
   static constexpr int BK = (MODE == W4A16) ? 64 : 128;    // k per stage (128-byte rows)
   static constexpr int KB_PER_GROUP = (MODE == W4A16) ? 2 : 1;  // stages per K group (W8: all)
@@ -53,12 +53,14 @@ struct Cfg {
   static constexpr int RAW_BYTES = (MODE == W8A8) ? 0 : (BK / 8) * 128 * 4;
   static constexpr int NWARPS = 2 + NCONV + NACC;
   static constexpr int NTHREADS = NWARPS * 32;
-  static constexpr int TMEM_COLS = (2 * BT < 32) ? 32 : 2 * BT;
+  static constexpr int NBUF = 4;                           // TMEM group partials in flight
+  static constexpr int TMEM_COLS = (NBUF * BT < 32) ? 32 : NBUF * BT;
+  static constexpr int MAXG = 144;                         // K groups whose scales fit the smem table
   static constexpr int ACC_SPLIT = NACC / 4;               // column slices per lane quadrant
   static constexpr int COLS = BT / ACC_SPLIT;              // columns per accumulator thread
   static constexpr int UMMA_K = (MODE == W4A16) ? 16 : 32;
   static constexpr int SMEM_BYTES =
-      1024 + STAGES * (A_BYTES + B_BYTES) + RSTAGES * RAW_BYTES + 1024;
+      1024 + STAGES * A_BYTES + BSTAGES * B_BYTES + RSTAGES * RAW_BYTES + 1024 + MAXG * 128 * 2;
   static_assert(NACC == 4 || NACC == 8, "accumulator warps cover the 4 lane quadrants");
   static_assert(COLS % 8 == 0, "columns per accumulator thread");
   static_assert(BT % 16 == 0 && BT >= 16 && BT <= 256, "MMA N");
@@ -98,26 +100,32 @@ __device__ __forceinline__ float i2f_small(uint32_t v) {
   return __int_as_float(static_cast<int>(v) + 0x4B400000) - 12582912.0f;
 }
 
-template <int MODE, int BT, int NCONV, int NACC, int STAGES, int RSTAGES>
-__global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES>::NTHREADS, 1)
+template <int MODE, int BT, int NCONV, int NACC, int STAGES, int RSTAGES, int BSTAGES>
+__global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BSTAGES>::NTHREADS, 1)
     wq_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                    const Params p) {
-  using C = Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES>;
+  using C = Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BSTAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = sA + STAGES * C::A_BYTES;
-  uint8_t* sR = sB + STAGES * C::B_BYTES;
+  uint8_t* sR = sB + BSTAGES * C::B_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sR + RSTAGES * C::RAW_BYTES);
+  // Three rings with their own depths: converted weights A (STAGES), token
+  // tiles B (BSTAGES) and raw int4 weights (RSTAGES). The producer only
+  // blocks on the raw and B rings, so weight bytes run RSTAGES k-blocks ahead
+  // of the tensor cores.
   uint64_t* a_full = bars;                 // converters (or TMA for W8) -> MMA
-  uint64_t* b_full = a_full + STAGES;      // TMA -> MMA
-  uint64_t* ab_empty = b_full + STAGES;    // MMA -> TMA / converters
-  uint64_t* r_full = ab_empty + STAGES;    // TMA -> converters
+  uint64_t* a_empty = a_full + STAGES;     // MMA -> converters (TMA for W8)
+  uint64_t* b_full = a_empty + STAGES;     // TMA -> MMA
+  uint64_t* b_empty = b_full + BSTAGES;    // MMA -> TMA
+  uint64_t* r_full = b_empty + BSTAGES;    // TMA -> converters
   uint64_t* r_empty = r_full + RSTAGES;    // converters -> TMA
-  uint64_t* acc_full = r_empty + RSTAGES;  // MMA -> accumulators (2)
-  uint64_t* acc_empty = acc_full + 2;      // accumulators -> MMA (2)
-  uint64_t* done_bar = acc_empty + 2;     // MMA drain on exit
+  uint64_t* acc_full = r_empty + RSTAGES;  // MMA -> accumulators (NBUF)
+  uint64_t* acc_empty = acc_full + C::NBUF;  // accumulators -> MMA (NBUF)
+  uint64_t* done_bar = acc_empty + C::NBUF;  // MMA drain on exit
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done_bar + 1);
+  __half* sScale = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(bars) + 1024);  // [MAXG][128]
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -133,14 +141,17 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES>::N
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&a_full[s], (MODE == W8A8) ? 1 : NCONV);
+      mbar_init(&a_empty[s], 1);
+    }
+    for (int s = 0; s < BSTAGES; ++s) {
       mbar_init(&b_full[s], 1);
-      mbar_init(&ab_empty[s], 1);
+      mbar_init(&b_empty[s], 1);
     }
     for (int s = 0; s < RSTAGES; ++s) {
       mbar_init(&r_full[s], 1);
       mbar_init(&r_empty[s], NCONV);
     }
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < C::NBUF; ++s) {
       mbar_init(&acc_full[s], 1);
       mbar_init(&acc_empty[s], NACC);
     }
@@ -164,8 +175,6 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES>::N
       prefetch_tmap(&tm_x);
       int rs = 0, rphase = 0, issued = 0, raw_issued = 0;
       for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
         const int k0 = kbeg + kb * C::BK;
         if (MODE != W8A8) {
           if (kb >= RSTAGES && !mbar_wait(&r_empty[rs], rphase ^ 1, abort_flag, 101)) break;
@@ -173,22 +182,25 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES>::N
           tma_load_2d(sR + rs * C::RAW_BYTES, &tm_w, &r_full[rs], n0, k0 / 8);
           ++raw_issued;
           if (++rs == RSTAGES) { rs = 0; rphase ^= 1; }
-        }
-        if (kb >= STAGES && !mbar_wait(&ab_empty[s], ph ^ 1, abort_flag, 102)) break;
-        if (MODE == W8A8) {
+        } else {
+          const int s = kb % STAGES;
+          if (kb >= STAGES && !mbar_wait(&a_empty[s], ((kb / STAGES) & 1) ^ 1, abort_flag, 102)) break;
           mbar_arrive_expect_tx(&a_full[s], C::A_BYTES);
           tma_load_2d(sA + s * C::A_BYTES, &tm_w, &a_full[s], k0, n0);
         }
-        mbar_arrive_expect_tx(&b_full[s], C::B_BYTES);
-        tma_load_2d(sB + s * C::B_BYTES, &tm_x, &b_full[s], k0, t0);
+        const int bs = kb % BSTAGES;
+        if (kb >= BSTAGES && !mbar_wait(&b_empty[bs], ((kb / BSTAGES) & 1) ^ 1, abort_flag, 109)) break;
+        mbar_arrive_expect_tx(&b_full[bs], C::B_BYTES);
+        tma_load_2d(sB + bs * C::B_BYTES, &tm_x, &b_full[bs], k0, t0);
         ++issued;
       }
       if (*abort_flag) {
         // Wait (bounded) for this CTA's own copies still in flight.
-        for (int kb = issued - 1; kb >= 0 && kb >= issued - STAGES; --kb) {
-          mbar_wait_drain(&b_full[kb % STAGES], (kb / STAGES) & 1);
-          if (MODE == W8A8) mbar_wait_drain(&a_full[kb % STAGES], (kb / STAGES) & 1);
-        }
+        for (int kb = issued - 1; kb >= 0 && kb >= issued - BSTAGES; --kb)
+          mbar_wait_drain(&b_full[kb % BSTAGES], (kb / BSTAGES) & 1);
+        if (MODE == W8A8)
+          for (int kb = issued - 1; kb >= 0 && kb >= issued - STAGES; --kb)
+            mbar_wait_drain(&a_full[kb % STAGES], (kb / STAGES) & 1);
         if (MODE != W8A8)
           for (int kb = raw_issued - 1; kb >= 0 && kb >= raw_issued - RSTAGES; --kb)
             mbar_wait_drain(&r_full[kb % RSTAGES], (kb / RSTAGES) & 1);
@@ -200,21 +212,21 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES>::N
       const uint32_t idesc = (MODE == W4A16) ? idesc_bf16(128, BT) : idesc_s8(128, BT);
       bool ok = true;
       for (int g = 0; g < ngroups && ok; ++g) {
-        const int buf = g & 1;
-        if (g >= 2 && !mbar_wait(&acc_empty[buf], ((g >> 1) - 1) & 1, abort_flag, 103)) break;
+        const int buf = g % C::NBUF;
+        if (g >= C::NBUF && !mbar_wait(&acc_empty[buf], ((g / C::NBUF) - 1) & 1, abort_flag, 103)) break;
         tc_fence_after();
         const uint32_t dtm = tmem + buf * BT;
         for (int j = 0; j < kb_per_group; ++j) {
           const int kb = g * kb_per_group + j;
-          const int s = kb % STAGES;
-          const uint32_t ph = (kb / STAGES) & 1;
-          if (!mbar_wait(&a_full[s], ph, abort_flag, 104) || !mbar_wait(&b_full[s], ph, abort_flag, 105)) {
+          const int s = kb % STAGES, bs = kb % BSTAGES;
+          if (!mbar_wait(&a_full[s], (kb / STAGES) & 1, abort_flag, 104) ||
+              !mbar_wait(&b_full[bs], (kb / BSTAGES) & 1, abort_flag, 105)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t a_base = smem_u32(sA + s * C::A_BYTES);
-          const uint32_t b_base = smem_u32(sB + s * C::B_BYTES);
+          const uint32_t b_base = smem_u32(sB + bs * C::B_BYTES);
 #pragma unroll
           for (int kk = 0; kk < C::BK / C::UMMA_K; ++kk) {
             const uint64_t ad = sdesc_sw128(a_base + kk * 32, 16, 1024);
@@ -224,7 +236,8 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES>::N
             else
               mma_i8(dtm, ad, bd, idesc, (j > 0 || kk > 0) ? 1u : 0u);
           }
-          mma_commit(&ab_empty[s]);
+          mma_commit(&a_empty[s]);
+          mma_commit(&b_empty[bs]);
         }
         if (ok) mma_commit(&acc_full[buf]);
       }
@@ -241,7 +254,7 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES>::N
         const int s = kb % STAGES;
         const uint32_t ph = (kb / STAGES) & 1;
         if (!mbar_wait_all(&r_full[rs], rphase, abort_flag, 106)) break;
-        if (kb >= STAGES && !mbar_wait_all(&ab_empty[s], ph ^ 1, abort_flag, 107)) break;
+        if (kb >= STAGES && !mbar_wait_all(&a_empty[s], ph ^ 1, abort_flag, 107)) break;
         const uint32_t* raw = reinterpret_cast<const uint32_t*>(sR + rs * C::RAW_BYTES);
         uint8_t* dst = sA + s * C::A_BYTES;
 #pragma unroll 4
@@ -281,23 +294,38 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES>::N
     float acc[C::COLS];
 #pragma unroll
     for (int i = 0; i < C::COLS; ++i) acc[i] = 0.f;
+    // Group scales of this CTA's K range staged once in shared memory
+    // (coalesced rows of 128 features) so no global load sits between an
+    // MMA's completion and the release of its TMEM buffer.
+    const bool staged = (MODE != W8A8) && ngroups <= C::MAXG;
+    if (staged) {
+      const int at = threadIdx.x - (2 + NCONV) * 32;
+      for (int i = at; i < ngroups * 128; i += NACC * 32)
+        sScale[i] = p.wscale[(size_t)((kbeg / 128) + (i >> 7)) * p.N + n0 + (i & 127)];
+      asm volatile("bar.sync 2, %0;" ::"r"(NACC * 32) : "memory");
+    }
     bool ok = nkb > 0;
     for (int g = 0; g < ngroups && ok; ++g) {
-      const int buf = g & 1;
-      if (!mbar_wait_all(&acc_full[buf], (g >> 1) & 1, abort_flag, 108)) { ok = false; break; }
+      const int buf = g % C::NBUF;
+      if (!mbar_wait_all(&acc_full[buf], (g / C::NBUF) & 1, abort_flag, 108)) { ok = false; break; }
       tc_fence_after();
       float gs = 1.f;
-      if (MODE != W8A8 && n < p.N) gs = __half2float(p.wscale[(size_t)((kbeg / 128) + g) * p.N + n]);
+      if (MODE != W8A8)
+        gs = staged ? __half2float(sScale[g * 128 + row])
+                    : (n < p.N ? __half2float(p.wscale[(size_t)((kbeg / 128) + g) * p.N + n]) : 0.f);
       const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + buf * BT + c0;
 #pragma unroll
-      for (int cc = 0; cc < C::COLS; cc += 8) {
-        uint32_t r[8];
-        tmem_ld8(taddr + cc, r);
+      for (int cc = 0; cc < C::COLS; cc += 16) {
+        uint32_t r[16];
+        tmem_ld8(taddr + cc, *reinterpret_cast<uint32_t(*)[8]>(&r[0]));
+        if (cc + 8 < C::COLS) tmem_ld8(taddr + cc + 8, *reinterpret_cast<uint32_t(*)[8]>(&r[8]));
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float v = (MODE == W4A16) ? __uint_as_float(r[i]) : ((MODE == W4A8) ? i2f_small(r[i]) : (float)(int)r[i]);
-          acc[cc + i] = fmaf(v, gs, acc[cc + i]);
+        for (int i = 0; i < 16; ++i) {
+          if (cc + i < C::COLS) {
+            const float v = (MODE == W4A16) ? __uint_as_float(r[i]) : ((MODE == W4A8) ? i2f_small(r[i]) : (float)(int)r[i]);
+            acc[cc + i] = fmaf(v, gs, acc[cc + i]);
+          }
         }
       }
       tc_fence_before();
@@ -365,9 +393,9 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int
   return r == CUDA_SUCCESS ? 0 : -2;
 }
 
-template <int MODE, int BT, int NCONV, int NACC, int STAGES, int RSTAGES>
+template <int MODE, int BT, int NCONV, int NACC, int STAGES, int RSTAGES, int BSTAGES>
 static int launch_cfg(const void* w, const void* x, const Params& p, int split, cudaStream_t st) {
-  using C = Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES>;
+  using C = Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BSTAGES>;
   CUtensorMap tw, tx;
   int rc;
   if (MODE == W8A8)
@@ -381,7 +409,7 @@ static int launch_cfg(const void* w, const void* x, const Params& p, int split, 
   else
     rc = make_tmap_2d(&tx, x, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.K, p.M, p.K, 128, BT, true);
   if (rc) return 200 + rc;
-  auto kern = wq_gemm_kernel<MODE, BT, NCONV, NACC, STAGES, RSTAGES>;
+  auto kern = wq_gemm_kernel<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BSTAGES>;
   static bool attr_set = false;
   if (!attr_set) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
@@ -424,18 +452,18 @@ extern "C" int k8v4_wq_gemm(int mode, const void* w, const void* wscale, const v
   split = cdiv(K, p.k_per_split);
   if (split > 1 && !ws) return 2;
   if (mode == W4A16) {
-    if (M <= 16) return launch_cfg<W4A16, 16, 8, 4, 4, 16>(w, x, p, split, st);
-    if (M <= 32) return launch_cfg<W4A16, 32, 8, 4, 4, 16>(w, x, p, split, st);
-    if (M <= 64) return launch_cfg<W4A16, 64, 8, 4, 4, 12>(w, x, p, split, st);
-    return launch_cfg<W4A16, 128, 4, 8, 4, 8>(w, x, p, split, st);
+    if (M <= 16) return launch_cfg<W4A16, 16, 8, 4, 4, 16, 16>(w, x, p, split, st);
+    if (M <= 32) return launch_cfg<W4A16, 32, 8, 4, 4, 12, 12>(w, x, p, split, st);
+    if (M <= 64) return launch_cfg<W4A16, 64, 8, 4, 4, 8, 8>(w, x, p, split, st);
+    return launch_cfg<W4A16, 128, 4, 8, 4, 8, 4>(w, x, p, split, st);
   }
   if (mode == W4A8) {
-    if (M <= 32) return launch_cfg<W4A8, 32, 8, 4, 4, 8>(w, x, p, split, st);
-    return launch_cfg<W4A8, 128, 4, 8, 4, 4>(w, x, p, split, st);
+    if (M <= 32) return launch_cfg<W4A8, 32, 8, 4, 4, 8, 12>(w, x, p, split, st);
+    return launch_cfg<W4A8, 128, 4, 8, 4, 4, 4>(w, x, p, split, st);
   }
   if (mode == W8A8) {
-    if (M <= 32) return launch_cfg<W8A8, 32, 4, 4, 6, 1>(w, x, p, split, st);
-    return launch_cfg<W8A8, 128, 4, 8, 4, 1>(w, x, p, split, st);
+    if (M <= 32) return launch_cfg<W8A8, 32, 4, 4, 6, 1, 6>(w, x, p, split, st);
+    return launch_cfg<W8A8, 128, 4, 8, 4, 1, 4>(w, x, p, split, st);
   }
   return 3;
 }

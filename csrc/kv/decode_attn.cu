@@ -45,11 +45,14 @@ struct DecodeParams {
 template <int NPAD>
 struct DCfg {
   static constexpr int STAGES = 4;
-  static constexpr int NTHREADS = 320;
+  static constexpr int NGRP = 2;  // softmax warpgroups, ping-pong over tiles
+  static constexpr int NWARPS = 2 + 4 + 4 * NGRP;
+  static constexpr int NTHREADS = 32 * NWARPS;
   static constexpr int Q_BYTES = NPAD * 128;
   static constexpr int PT_BYTES = 2 * NPAD * 128;   // P^T fp16: 2 K-atoms of NPAD rows
-  static constexpr int TMEM_COLS = (3 * NPAD <= 32) ? 32 : (3 * NPAD <= 64) ? 64 : (3 * NPAD <= 128) ? 128
-                                   : (3 * NPAD <= 256) ? 256 : 512;
+  static constexpr int TMEM_NEED = 4 * NPAD;        // S^T[2] + O^T[2]
+  static constexpr int TMEM_COLS = TMEM_NEED <= 32 ? 32 : TMEM_NEED <= 64 ? 64 : TMEM_NEED <= 128 ? 128
+                                   : TMEM_NEED <= 256 ? 256 : 512;
   // layout (offsets from the 1024-aligned base)
   static constexpr int OFF_K = 0;
   static constexpr int OFF_VT = OFF_K + STAGES * K_TILE_BYTES;
@@ -57,11 +60,15 @@ struct DCfg {
   static constexpr int OFF_Q = OFF_PT + 2 * PT_BYTES;
   static constexpr int OFF_VS = OFF_Q + ((Q_BYTES + 1023) / 1024) * 1024;
   static constexpr int OFF_MISC = OFF_VS + STAGES * VS_TILE_BYTES;
-  static constexpr int SMEM_BYTES = 1024 + OFF_MISC + 8192;
+  static constexpr int SMEM_BYTES = 1024 + OFF_MISC + 256 + 32 * NPAD * 4 + 64;
 };
 
+// Two softmax warpgroups take alternate tiles (group g owns tiles j = g mod 2)
+// with their own S^T / P^T / O^T buffers and their own running max and sums,
+// so one group's softmax overlaps the other's MMAs and handoffs. Their
+// (m, l, O) are merged in the epilogue like two splits.
 template <int NPAD>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(DCfg<NPAD>::NTHREADS, 1)
     decode_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const DecodeParams p) {
   using C = DCfg<NPAD>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -74,19 +81,20 @@ __global__ void __launch_bounds__(320, 1)
   uint8_t* misc = sm + C::OFF_MISC;
   uint64_t* kv_full = reinterpret_cast<uint64_t*>(misc);
   uint64_t* kv_empty = kv_full + C::STAGES;
-  uint64_t* s_full = kv_empty + C::STAGES;  // [2]
+  uint64_t* s_full = kv_empty + C::STAGES;  // [2] (buffer = owning group)
   uint64_t* p_full = s_full + 2;            // [2]
   uint64_t* v_full = p_full + 2;            // [2]
   uint64_t* pv_empty = v_full + 2;          // [2]
   uint64_t* done_bar = pv_empty + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  int* grp_ok = const_cast<int*>(abort_flag) + 1;            // [2]
   float* q_scale = reinterpret_cast<float*>(misc + 256);     // [NPAD] q scale * softmax scale
   int* row_end = reinterpret_cast<int*>(q_scale + NPAD);     // [NPAD] visible keys per row
-  float* m_ref = reinterpret_cast<float*>(row_end + NPAD);   // [4][NPAD] running max per softmax warp (log2)
-  float* alpha = m_ref + 4 * NPAD;                           // [4][NPAD] this tile's rescale per warp
-  float* red = alpha + 4 * NPAD;                             // [4][NPAD] cross-warp partials
-  int* flags = reinterpret_cast<int*>(red + 4 * NPAD);       // [1] rescale-needed flag
+  float* m_ref = reinterpret_cast<float*>(row_end + NPAD);   // [2][4][NPAD] running max per warp (log2)
+  float* alpha = m_ref + 8 * NPAD;                           // [2][4][NPAD] this tile's rescale per warp
+  float* red = alpha + 8 * NPAD;                             // [2][4][NPAD] cross-warp partials
+  float* fin = red + 8 * NPAD;                               // [2][2][NPAD] final (m, l) per group
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int split = blockIdx.x, h = blockIdx.y + p.head_offset, seq = blockIdx.z;
@@ -104,7 +112,7 @@ __global__ void __launch_bounds__(320, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1 + 4 + 4);
+      mbar_init(&kv_empty[s], 1 + 4 + 4);  // MMA commit + converter warps + owning group's warps
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
@@ -114,6 +122,7 @@ __global__ void __launch_bounds__(320, 1)
     }
     mbar_init(done_bar, 1);
     *abort_flag = 0;
+    grp_ok[0] = grp_ok[1] = 1;
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -121,7 +130,7 @@ __global__ void __launch_bounds__(320, 1)
     tmem_relinquish();
   }
   // ---- prologue: quantize the query rows into the Q8 tile (K-major SW128)
-  for (int r = warp; r < NPAD; r += 10) {
+  for (int r = warp; r < NPAD; r += C::NWARPS) {
     float x[4] = {0.f, 0.f, 0.f, 0.f};
     int end = 0;
     if (r < R) {
@@ -148,7 +157,7 @@ __global__ void __launch_bounds__(320, 1)
     if (lane == 0) {
       q_scale[r] = s * p.sm_scale_log2;
       row_end[r] = end;
-      for (int c = 0; c < 4; ++c) m_ref[c * NPAD + r] = -INFINITY;
+      for (int c = 0; c < 8; ++c) m_ref[c * NPAD + r] = -INFINITY;
     }
   }
   fence_async_smem();
@@ -157,7 +166,7 @@ __global__ void __launch_bounds__(320, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
   const uint32_t tm_s = tmem;                 // S^T buffers: cols [0, 2*NPAD)
-  const uint32_t tm_o = tmem + 2 * NPAD;      // O^T: cols [2*NPAD, 3*NPAD)
+  const uint32_t tm_o = tmem + 2 * NPAD;      // O^T buffers: cols [2*NPAD, 4*NPAD)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -216,7 +225,7 @@ __global__ void __launch_bounds__(320, 1)
           for (int kk = 0; kk < 8; ++kk) {
             const uint64_t ad = sdesc_sw128(vt_base + kk * 2048, VT_LBO, 1024);
             const uint64_t bd = sdesc_sw128(pt_base + (kk >> 2) * (NPAD * 128) + (kk & 3) * 32, 16, 1024);
-            mma_f16(tm_o, ad, bd, id_pv, (jj > 0 || kk > 0) ? 1u : 0u);
+            mma_f16(tm_o + b * NPAD, ad, bd, id_pv, (jj >= 2 || kk > 0) ? 1u : 0u);
           }
           mma_commit(&pv_empty[b]);
         }
@@ -257,18 +266,24 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else {
     // ------------------------------------------------------------- softmax
-    const int sw = warp - 6;                   // 0..3 (named-barrier group)
+    const int grp = (warp - 6) >> 2;           // warpgroup: owns tiles j = grp mod 2
+    const int sw = (warp - 6) & 3;             // warp within the group
     const int quad = warp & 3;                 // TMEM lane quadrant
     const int key_local = quad * 32 + lane;    // this thread's key (S^T lane) and dim (O^T lane)
+    const int bar_id = 1 + grp;
+    float* mw = m_ref + (grp * 4 + sw) * NPAD;
+    float* aw = alpha + (grp * 4 + sw) * NPAD;
+    float* rd = red + grp * 4 * NPAD;
+    const uint32_t tm_og = tm_o + grp * NPAD;
     float l_acc[NPAD];
 #pragma unroll
     for (int r = 0; r < NPAD; ++r) l_acc[r] = 0.f;
-    // Every softmax warp runs every iteration and every named barrier, even
-    // after a failed (timed-out) wait: a failure only turns the work off, so
-    // the four warps always meet at the same bar.sync.
+    // Every warp of a group runs every iteration and every named barrier,
+    // even after a failed (timed-out) wait: a failure only turns the work
+    // off, so the four warps always meet at the same bar.sync.
     bool ok = true;
-    for (int j = 0; j < nt; ++j) {
-      const int s = j % C::STAGES, b = j & 1;
+    for (int j = grp; j < nt; j += 2) {
+      const int s = j % C::STAGES, b = grp;
       if (ok && (!mbar_wait_all(&s_full[b], (j >> 1) & 1, abort_flag, 207) ||
                  !mbar_wait_all(&kv_full[s], (j / C::STAGES) & 1, abort_flag, 208)))
         ok = false;
@@ -299,22 +314,17 @@ __global__ void __launch_bounds__(320, 1)
             const float v = sc[r] * (q_scale[r] * ks);
             sc[r] = (key < row_end[r]) ? v : -INFINITY;
             const float wm = warp_max(sc[r]);
-            if (lane == 0) red[sw * NPAD + r] = wm;
+            if (lane == 0) rd[sw * NPAD + r] = wm;
           }
         }
       }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      // Every warp derives the same tile max / rescale decisions from the
-      // shared partial maxima and keeps its own copy of the running max and
-      // the rescale factors (m_w / a_w rows of this warp).
+      asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
       int any_rescale = 0;
-      float* mw = m_ref + sw * NPAD;
-      float* aw = alpha + sw * NPAD;
       if (ok) {
 #pragma unroll
         for (int r = 0; r < NPAD; ++r) {
           if (r < R) {
-            const float tmax = fmaxf(fmaxf(red[r], red[NPAD + r]), fmaxf(red[2 * NPAD + r], red[3 * NPAD + r]));
+            const float tmax = fmaxf(fmaxf(rd[r], rd[NPAD + r]), fmaxf(rd[2 * NPAD + r], rd[3 * NPAD + r]));
             const float mo = mw[r];
             float a = 1.f, mn = mo;
             if (tmax > mo + RESCALE_TAU || (mo == -INFINITY && tmax > -INFINITY)) {
@@ -333,30 +343,24 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
         __syncwarp();
-        // rescale O^T columns when a row's reference max moved (needs PV j-1 done)
-        if (any_rescale && j > 0) {
-          const int pb = (j - 1) & 1;
-          if (!mbar_wait_all(&pv_empty[pb], ((j - 1) >> 1) & 1, abort_flag, 209)) {
-            ok = false;
-          } else {
-            tc_fence_after();
-            const uint32_t ta = tm_o + ((uint32_t)(quad * 32) << 16);
-#pragma unroll
-            for (int c = 0; c < NPAD; c += 8) {
-              uint32_t r8[8];
-              tmem_ld8(ta + c, r8);
-              tmem_ld_wait();
-#pragma unroll
-              for (int i = 0; i < 8; ++i)
-                r8[i] = __float_as_uint(__uint_as_float(r8[i]) * (c + i < R ? aw[c + i] : 1.f));
-              tmem_st8(ta + c, r8);
-            }
-            tmem_st_wait();
-          }
-        }
       }
-      // P^T (fp16, K-major SW128): row r, key key_local
+      // this group's previous PV (tile j-2) read P^T[b] and wrote O^T[b]
       if (ok && j >= 2 && !mbar_wait_all(&pv_empty[b], ((j >> 1) - 1) & 1, abort_flag, 210)) ok = false;
+      if (ok && any_rescale && j >= 2) {
+        tc_fence_after();
+        const uint32_t ta = tm_og + ((uint32_t)(quad * 32) << 16);
+#pragma unroll
+        for (int c = 0; c < NPAD; c += 8) {
+          uint32_t r8[8];
+          tmem_ld8(ta + c, r8);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            r8[i] = __float_as_uint(__uint_as_float(r8[i]) * (c + i < R ? aw[c + i] : 1.f));
+          tmem_st8(ta + c, r8);
+        }
+        tmem_st_wait();
+      }
       if (ok) {
         uint8_t* pt = sPT + b * C::PT_BYTES + (key_local >> 6) * (NPAD * 128) + (key_local & 7) * 2;
         const int kc = (key_local & 63) >> 3;
@@ -373,53 +377,75 @@ __global__ void __launch_bounds__(320, 1)
           mbar_arrive(&kv_empty[s]);
         }
       }
-      asm volatile("bar.sync 1, 128;" ::: "memory");  // red / m / alpha reads done before the next tile
+      asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");  // rd / m reads done before the next tile
     }
     // ------------------------------------------------------------ epilogue
-    if (ok && nt > 0) {
-      const int lb = (nt - 1) & 1;
-      if (!mbar_wait_all(&pv_empty[lb], ((nt - 1) >> 1) & 1, abort_flag, 211)) ok = false;
+    const bool has = nt > grp;  // this group processed at least one tile
+    if (ok && has) {
+      const int jl = grp + 2 * ((nt - 1 - grp) / 2);  // this group's last tile
+      if (!mbar_wait_all(&pv_empty[grp], (jl >> 1) & 1, abort_flag, 211)) ok = false;
     }
-    // row sums across the 128 key-threads
 #pragma unroll
     for (int r = 0; r < NPAD; ++r) {
       if (r < R) {
         const float ws = warp_sum(l_acc[r]);
-        if (lane == 0) red[sw * NPAD + r] = ws;
+        if (lane == 0) rd[sw * NPAD + r] = ws;
       }
     }
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-    if (ok) {
+    asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
+    if (sw == 0) {
+      for (int r = lane; r < NPAD; r += 32) {
+        fin[(grp * 2) * NPAD + r] = has ? mw[r] : -INFINITY;
+        fin[(grp * 2 + 1) * NPAD + r] = rd[r] + rd[NPAD + r] + rd[2 * NPAD + r] + rd[3 * NPAD + r];
+      }
+      if (lane == 0 && !ok) grp_ok[grp] = 0;
+    }
+    asm volatile("bar.sync 3, 256;" ::: "memory");  // both groups' (m, l) published
+    if (grp == 0 && grp_ok[0] && grp_ok[1]) {
       tc_fence_after();
-      float o[NPAD];
+      float o0[NPAD], o1[NPAD];
+#pragma unroll
+      for (int r = 0; r < NPAD; ++r) o0[r] = o1[r] = 0.f;
+      const uint32_t lo = (uint32_t)(quad * 32) << 16;
       if (nt > 0) {
-        const uint32_t ta = tm_o + ((uint32_t)(quad * 32) << 16);
 #pragma unroll
         for (int c = 0; c < NPAD; c += 16) {
           uint32_t r16[16];
-          tmem_ld16(ta + c, r16);
+          tmem_ld16(tm_o + lo + c, r16);
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 16; ++i) o[c + i] = __uint_as_float(r16[i]);
+          for (int i = 0; i < 16; ++i) o0[c + i] = __uint_as_float(r16[i]);
         }
-      } else {
+      }
+      if (nt > 1) {
 #pragma unroll
-        for (int r = 0; r < NPAD; ++r) o[r] = 0.f;
+        for (int c = 0; c < NPAD; c += 16) {
+          uint32_t r16[16];
+          tmem_ld16(tm_o + NPAD + lo + c, r16);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o1[c + i] = __uint_as_float(r16[i]);
+        }
       }
       const int d = key_local;
       const int64_t wsi = (((int64_t)seq * gridDim.y + hl) * p.nsplit + split);
 #pragma unroll
       for (int r = 0; r < NPAD; ++r) {
         if (r < R) {
-          const float l = red[r] + red[NPAD + r] + red[2 * NPAD + r] + red[3 * NPAD + r];
+          const float m0 = fin[r], l0 = fin[NPAD + r], m1 = fin[2 * NPAD + r], l1 = fin[3 * NPAD + r];
+          const float M = fmaxf(m0, m1);
+          const float w0 = (m0 == -INFINITY) ? 0.f : exp2f(m0 - M);
+          const float w1 = (m1 == -INFINITY) ? 0.f : exp2f(m1 - M);
+          const float o = (w0 > 0.f ? w0 * o0[r] : 0.f) + (w1 > 0.f ? w1 * o1[r] : 0.f);
+          const float l = w0 * l0 + w1 * l1;
           if (p.nsplit == 1) {
             const int t = r / p.gqa, g = r % p.gqa;
-            const float v = l > 0.f ? o[r] / l : 0.f;
+            const float v = l > 0.f ? o / l : 0.f;
             p.out[((int64_t)(qb + t) * p.hq_total + (int64_t)h * p.gqa + g) * D + d] = __float2bfloat16_rn(v);
           } else {
-            p.ws_o[(wsi * NPAD + r) * D + d] = o[r];
+            p.ws_o[(wsi * NPAD + r) * D + d] = o;
             if (d == 0) {
-              p.ws_ml[(wsi * 2) * NPAD + r] = (nt > 0) ? m_ref[r] : -INFINITY;
+              p.ws_ml[(wsi * 2) * NPAD + r] = M;
               p.ws_ml[(wsi * 2 + 1) * NPAD + r] = l;
             }
           }

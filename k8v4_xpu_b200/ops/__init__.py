@@ -55,6 +55,10 @@ def available() -> bool:
 
 
 def _library_file() -> str | None:
+    """The in-tree build, or ``K8V4_LIB`` (an explicit .so path) when set."""
+    override = os.environ.get("K8V4_LIB")
+    if override:
+        return override if os.path.exists(override) else None
     pkg = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     found = sorted(glob.glob(os.path.join(pkg, "_C*.so")))
     return found[0] if found else None

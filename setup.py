@@ -17,7 +17,7 @@ NVCC = [
     "-O3", "-lineinfo", "-std=c++17",
     "--expt-relaxed-constexpr",
     "-diag-suppress", "20044",
-]
+] + os.environ.get("K8V4_NVCC_EXTRA", "").split()
 
 setup(
     name="k8v4_xpu_b200",
