@@ -63,6 +63,32 @@ def main():
             xq = torch.randint(-127, 127, (M, K), dtype=torch.int8, device="cuda")
             xs = torch.rand(M, device="cuda") * 0.01
             fn = lambda: ops.wq_gemm(ops.W4A8, qw, sc, xq, xscale=xs)  # noqa: E731
+    elif c in ("decode_step", "decode_step4"):
+        # two layers of the 27B decoder, 128K context written straight into
+        # the KV pool, one eager decode step per call (kernel launch lists)
+        from k8v4_xpu_b200.models.config import DENSE_27B
+        from k8v4_xpu_b200.models.dense import DenseModel, StepInputs
+        from k8v4_xpu_b200.runtime.workspace import Workspace
+        from k8v4_xpu_b200.runtime.engine import decode_splits
+        nseq = 4 if c == "decode_step4" else 1
+        ctx = 128197
+        m = DenseModel(DENSE_27B, device="cuda").random_init(seed=0, layers=2)
+        layout = m.layout
+        caches = []
+        for _ in m.layers:
+            _, cache, bt = fill_cache(ctx + 64, nseq, layout.hkv, layout.gqa)
+            caches.append(cache)
+        ws = Workspace("cuda", 64, nseq, bt.shape[1], 2 * DENSE_27B.intermediate, layout.hkv, layout.gqa, 1, 64)
+        pages_per = bt.shape[1]
+        pos = torch.full((nseq,), ctx, dtype=torch.int64, device="cuda")
+        inp = StepInputs(
+            input_ids=torch.randint(0, DENSE_27B.vocab, (nseq,), device="cuda"), positions=pos,
+            slots=torch.arange(nseq, device="cuda") * pages_per * 16 + ctx,
+            cu_q=torch.arange(nseq + 1, dtype=torch.int32, device="cuda"),
+            seq_lens=torch.full((nseq,), ctx + 1, dtype=torch.int32, device="cuda"), block_table=bt,
+            logit_rows=torch.arange(nseq, device="cuda"), max_q_len=1, is_decode=True,
+            nsplit=decode_splits(8200, nseq, layout.hkv))
+        fn = lambda: m.greedy(m.forward(inp, caches, ws))  # noqa: E731
     else:
         raise SystemExit("unknown case %s" % c)
     for _ in range(a.reps):

@@ -46,21 +46,39 @@ struct Params {
 
 template <int MODE, int BT, int NCONV, int NACC, int STAGES, int RSTAGES, int BSTAGES>
 struct Cfg {
-  static constexpr int BK = (MODE == W4A16) ? 64 : 128;    // k per stage (128-byte rows)
-  static constexpr int KB_PER_GROUP = (MODE == W4A16) ? 2 : 1;  // stages per K group (W8: all)
+  // Decode-sized tiles keep the converted weights in TMEM (the MMA reads A
+  // from TMEM): no shared-memory round trip for A, and 128-k stages so each
+  // wait / commit of the MMA thread covers eight MMAs.
+  static constexpr bool TA = (MODE == W4A16) && (BT <= 64);
+  static constexpr int BK = (MODE == W4A16 && !TA) ? 64 : 128;  // k per stage
+  static constexpr int KB_PER_GROUP = (BK == 64) ? 2 : 1;  // stages per K group (W8: all)
   static constexpr int A_BYTES = 128 * 128;                // 128 rows x 128 B
-  static constexpr int B_BYTES = BT * 128;
+  static constexpr int B_ATOMS = (MODE == W4A16) ? BK / 64 : 1;  // 128-byte k atoms per token row
+  static constexpr int B_BYTES = BT * 128 * B_ATOMS;
   static constexpr int RAW_BYTES = (MODE == W8A8) ? 0 : (BK / 8) * 128 * 4;
   static constexpr int NWARPS = 2 + NCONV + NACC;
   static constexpr int NTHREADS = NWARPS * 32;
   static constexpr int NBUF = 4;                           // TMEM group partials in flight
-  static constexpr int TMEM_COLS = (NBUF * BT < 32) ? 32 : NBUF * BT;
+  static constexpr int D_COLS = NBUF * BT;
+  static constexpr int A_COLS = BK / 2;                    // TMEM columns of one A stage
+  static constexpr int TSTAGES = TA ? ((512 - D_COLS) / A_COLS > 12 ? 12 : (512 - D_COLS) / A_COLS) : 0;
+  static constexpr int TMEM_NEED = D_COLS + TSTAGES * A_COLS;
+  static constexpr int TMEM_COLS = TMEM_NEED <= 32 ? 32 : TMEM_NEED <= 64 ? 64 : TMEM_NEED <= 128 ? 128
+                                   : TMEM_NEED <= 256 ? 256 : 512;
+  static constexpr int ASMEM = TA ? 0 : STAGES;            // A stages in shared memory
+  static constexpr int AR = TA ? TSTAGES : STAGES;         // A ring depth (either place)
+  // With A in TMEM the token ring shares the A ring's slots and its empty
+  // barrier (one commit per k-block); otherwise it has its own depth.
+  static constexpr int BR = TA ? TSTAGES : BSTAGES;
+  static constexpr int BAR_BYTES = 2048;
   static constexpr int MAXG = 144;                         // K groups whose scales fit the smem table
   static constexpr int ACC_SPLIT = NACC / 4;               // column slices per lane quadrant
   static constexpr int COLS = BT / ACC_SPLIT;              // columns per accumulator thread
   static constexpr int UMMA_K = (MODE == W4A16) ? 16 : 32;
   static constexpr int SMEM_BYTES =
-      1024 + STAGES * A_BYTES + BSTAGES * B_BYTES + RSTAGES * RAW_BYTES + 1024 + MAXG * 128 * 2;
+      1024 + ASMEM * A_BYTES + BR * B_BYTES + RSTAGES * RAW_BYTES + BAR_BYTES + MAXG * 128 * 2;
+  static_assert(TMEM_NEED <= 512, "TMEM budget");
+  static_assert(!TA || NCONV % 4 == 0, "TMEM converters work in teams of 4 warps (one per lane quadrant)");
   static_assert(NACC == 4 || NACC == 8, "accumulator warps cover the 4 lane quadrants");
   static_assert(COLS % 8 == 0, "columns per accumulator thread");
   static_assert(BT % 16 == 0 && BT >= 16 && BT <= 256, "MMA N");
@@ -100,32 +118,47 @@ __device__ __forceinline__ float i2f_small(uint32_t v) {
   return __int_as_float(static_cast<int>(v) + 0x4B400000) - 12582912.0f;
 }
 
+#ifdef K8V4_TRACE
+// Timeline of CTA (0,0,0) for pipeline studies (trace builds only):
+// row 0 producer issue, 1 converter done, 2 MMA issued, 3 accumulate done.
+__device__ uint64_t g_gemm_trace[8 * 256];
+#define K8V4_TRACE_EVENT(row, idx)                                                        \
+  do {                                                                                    \
+    if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (idx) < 256)             \
+      g_gemm_trace[(row) * 256 + (idx)] = globaltimer_ns();                               \
+  } while (0)
+#else
+#define K8V4_TRACE_EVENT(row, idx) do { } while (0)
+#endif
+
 template <int MODE, int BT, int NCONV, int NACC, int STAGES, int RSTAGES, int BSTAGES>
 __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BSTAGES>::NTHREADS, 1)
     wq_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
-                   const Params p) {
+                   const __grid_constant__ CUtensorMap tm_s, const Params p) {
   using C = Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BSTAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = sA + STAGES * C::A_BYTES;
-  uint8_t* sR = sB + BSTAGES * C::B_BYTES;
+  uint8_t* sB = sA + C::ASMEM * C::A_BYTES;
+  uint8_t* sR = sB + C::BR * C::B_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sR + RSTAGES * C::RAW_BYTES);
   // Three rings with their own depths: converted weights A (STAGES), token
   // tiles B (BSTAGES) and raw int4 weights (RSTAGES). The producer only
   // blocks on the raw and B rings, so weight bytes run RSTAGES k-blocks ahead
   // of the tensor cores.
   uint64_t* a_full = bars;                 // converters (or TMA for W8) -> MMA
-  uint64_t* a_empty = a_full + STAGES;     // MMA -> converters (TMA for W8)
-  uint64_t* b_full = a_empty + STAGES;     // TMA -> MMA
-  uint64_t* b_empty = b_full + BSTAGES;    // MMA -> TMA
-  uint64_t* r_full = b_empty + BSTAGES;    // TMA -> converters
+  uint64_t* a_empty = a_full + C::AR;      // MMA -> converters (TMA for W8)
+  uint64_t* b_full = a_empty + C::AR;      // TMA -> MMA (TMEM-A path: -> converters)
+  uint64_t* b_empty_own = b_full + C::BR;  // MMA -> TMA (own ring)
+  uint64_t* b_empty = C::TA ? a_empty : b_empty_own;
+  uint64_t* r_full = b_empty_own + C::BR;  // TMA -> converters
   uint64_t* r_empty = r_full + RSTAGES;    // converters -> TMA
   uint64_t* acc_full = r_empty + RSTAGES;  // MMA -> accumulators (NBUF)
   uint64_t* acc_empty = acc_full + C::NBUF;  // accumulators -> MMA (NBUF)
   uint64_t* done_bar = acc_empty + C::NBUF;  // MMA drain on exit
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done_bar + 1);
-  __half* sScale = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(bars) + 1024);  // [MAXG][128]
+  uint64_t* scale_bar = done_bar + 1;        // group-scale table loaded
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(scale_bar + 1);
+  __half* sScale = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(bars) + C::BAR_BYTES);  // [MAXG][128]
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -139,17 +172,18 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
   const int ngroups = (MODE == W8A8) ? 1 : nkb / kb_per_group;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&a_full[s], (MODE == W8A8) ? 1 : NCONV);
+    for (int s = 0; s < C::AR; ++s) {
+      mbar_init(&a_full[s], (MODE == W8A8) ? 1 : (C::TA ? 4 : NCONV));
       mbar_init(&a_empty[s], 1);
     }
-    for (int s = 0; s < BSTAGES; ++s) {
+    for (int s = 0; s < C::BR; ++s) {
       mbar_init(&b_full[s], 1);
-      mbar_init(&b_empty[s], 1);
+      mbar_init(&b_empty_own[s], 1);
     }
+    mbar_init(scale_bar, 1);
     for (int s = 0; s < RSTAGES; ++s) {
       mbar_init(&r_full[s], 1);
-      mbar_init(&r_empty[s], NCONV);
+      mbar_init(&r_empty[s], C::TA ? 4 : NCONV);
     }
     for (int s = 0; s < C::NBUF; ++s) {
       mbar_init(&acc_full[s], 1);
@@ -173,6 +207,13 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
     if (lane == 0 && nkb > 0) {
       prefetch_tmap(&tm_w);
       prefetch_tmap(&tm_x);
+      if (MODE != W8A8) prefetch_tmap(&tm_s);
+      if (MODE != W8A8 && p.k_per_split / 128 <= C::MAXG) {
+        // the CTA's scale block in one copy: the box always moves k_per_split/128
+        // rows (rows past K arrive zero-filled and are never read)
+        mbar_arrive_expect_tx(scale_bar, (p.k_per_split / 128) * 256);
+        tma_load_2d(sScale, &tm_s, scale_bar, n0, kbeg / 128);
+      }
       int rs = 0, rphase = 0, issued = 0, raw_issued = 0;
       for (int kb = 0; kb < nkb; ++kb) {
         const int k0 = kbeg + kb * C::BK;
@@ -188,16 +229,19 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
           mbar_arrive_expect_tx(&a_full[s], C::A_BYTES);
           tma_load_2d(sA + s * C::A_BYTES, &tm_w, &a_full[s], k0, n0);
         }
-        const int bs = kb % BSTAGES;
-        if (kb >= BSTAGES && !mbar_wait(&b_empty[bs], ((kb / BSTAGES) & 1) ^ 1, abort_flag, 109)) break;
+        const int bs = kb % C::BR;
+        if (kb >= C::BR && !mbar_wait(&b_empty[bs], ((kb / C::BR) & 1) ^ 1, abort_flag, 109)) break;
         mbar_arrive_expect_tx(&b_full[bs], C::B_BYTES);
-        tma_load_2d(sB + bs * C::B_BYTES, &tm_x, &b_full[bs], k0, t0);
+#pragma unroll
+        for (int at = 0; at < C::B_ATOMS; ++at)
+          tma_load_2d(sB + bs * C::B_BYTES + at * (BT * 128), &tm_x, &b_full[bs], k0 + at * 64, t0);
+        K8V4_TRACE_EVENT(0, kb);
         ++issued;
       }
       if (*abort_flag) {
         // Wait (bounded) for this CTA's own copies still in flight.
-        for (int kb = issued - 1; kb >= 0 && kb >= issued - BSTAGES; --kb)
-          mbar_wait_drain(&b_full[kb % BSTAGES], (kb / BSTAGES) & 1);
+        for (int kb = issued - 1; kb >= 0 && kb >= issued - C::BR; --kb)
+          mbar_wait_drain(&b_full[kb % C::BR], (kb / C::BR) & 1);
         if (MODE == W8A8)
           for (int kb = issued - 1; kb >= 0 && kb >= issued - STAGES; --kb)
             mbar_wait_drain(&a_full[kb % STAGES], (kb / STAGES) & 1);
@@ -213,31 +257,50 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
       bool ok = true;
       for (int g = 0; g < ngroups && ok; ++g) {
         const int buf = g % C::NBUF;
+#ifdef K8V4_TRACE
+        const uint64_t te0 = globaltimer_ns();
+#endif
         if (g >= C::NBUF && !mbar_wait(&acc_empty[buf], ((g / C::NBUF) - 1) & 1, abort_flag, 103)) break;
+#ifdef K8V4_TRACE
+        if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && g < 256)
+          g_gemm_trace[6 * 256 + g] = globaltimer_ns() - te0;
+#endif
         tc_fence_after();
         const uint32_t dtm = tmem + buf * BT;
         for (int j = 0; j < kb_per_group; ++j) {
           const int kb = g * kb_per_group + j;
-          const int s = kb % STAGES, bs = kb % BSTAGES;
-          if (!mbar_wait(&a_full[s], (kb / STAGES) & 1, abort_flag, 104) ||
-              !mbar_wait(&b_full[bs], (kb / BSTAGES) & 1, abort_flag, 105)) {
+          const int s = kb % C::AR, bs = kb % C::BR;
+          // TMEM-A path: the converters already waited for this stage's token tile
+          if (!mbar_wait(&a_full[s], (kb / C::AR) & 1, abort_flag, 104) ||
+              (!C::TA && !mbar_wait(&b_full[bs], (kb / C::BR) & 1, abort_flag, 105))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_base = smem_u32(sA + s * C::A_BYTES);
           const uint32_t b_base = smem_u32(sB + bs * C::B_BYTES);
+          if (C::TA) {
+            const uint32_t a_tm = tmem + C::D_COLS + s * C::A_COLS;
 #pragma unroll
-          for (int kk = 0; kk < C::BK / C::UMMA_K; ++kk) {
-            const uint64_t ad = sdesc_sw128(a_base + kk * 32, 16, 1024);
-            const uint64_t bd = sdesc_sw128(b_base + kk * 32, 16, 1024);
-            if (MODE == W4A16)
-              mma_f16(dtm, ad, bd, idesc, (j > 0 || kk > 0) ? 1u : 0u);
-            else
-              mma_i8(dtm, ad, bd, idesc, (j > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < C::BK / C::UMMA_K; ++kk)
+              mma_f16_ts(dtm, a_tm + kk * 8,
+                         sdesc_sw128(b_base + (kk >> 2) * (BT * 128) + (kk & 3) * 32, 16, 1024), idesc,
+                         (j > 0 || kk > 0) ? 1u : 0u);
+            mma_commit(&a_empty[s]);  // frees the TMEM A stage and the token stage
+          } else {
+            const uint32_t a_base = smem_u32(sA + s * C::A_BYTES);
+#pragma unroll
+            for (int kk = 0; kk < C::BK / C::UMMA_K; ++kk) {
+              const uint64_t ad = sdesc_sw128(a_base + kk * 32, 16, 1024);
+              const uint64_t bd = sdesc_sw128(b_base + kk * 32, 16, 1024);
+              if (MODE == W4A16)
+                mma_f16(dtm, ad, bd, idesc, (j > 0 || kk > 0) ? 1u : 0u);
+              else
+                mma_i8(dtm, ad, bd, idesc, (j > 0 || kk > 0) ? 1u : 0u);
+            }
+            mma_commit(&a_empty[s]);
+            mma_commit(&b_empty[bs]);
           }
-          mma_commit(&a_empty[s]);
-          mma_commit(&b_empty[bs]);
+          K8V4_TRACE_EVENT(2, kb);
         }
         if (ok) mma_commit(&acc_full[buf]);
       }
@@ -247,7 +310,48 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
     }
   } else if (warp < 2 + NCONV) {
     // ---------------------------------------------------------- converters
-    if (MODE != W8A8) {
+    if (C::TA) {
+      // Teams of 4 warps (one per TMEM lane quadrant) take alternate
+      // k-blocks; each thread converts one weight row (feature) of the block
+      // into 32 columns of bf16 pairs and stores them with one tcgen05.st.
+      const int cw = warp - 2;
+      const int team = cw >> 2, nteams = NCONV / 4;
+      const int quad = warp & 3;
+      const int f = quad * 32 + lane;
+      const uint32_t lane_base = tmem + C::D_COLS + ((uint32_t)(quad * 32) << 16);
+      for (int kb = team; kb < nkb; kb += nteams) {
+        const int rs = kb % RSTAGES, ts = kb % C::AR;
+        if (!mbar_wait_all(&r_full[rs], (kb / RSTAGES) & 1, abort_flag, 110)) break;
+        if (kb >= C::AR && !mbar_wait_all(&a_empty[ts], ((kb / C::AR) - 1) & 1, abort_flag, 111)) break;
+        const uint32_t* raw = reinterpret_cast<const uint32_t*>(sR + rs * C::RAW_BYTES);
+        const uint32_t dst = lane_base + ts * C::A_COLS;
+#pragma unroll
+        for (int half = 0; half < C::BK / 64; ++half) {
+          uint32_t v[32];
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            uint32_t o[4];
+            int4x8_to_bf16(raw[(half * 8 + c) * 128 + f], o);
+            v[4 * c] = o[0];
+            v[4 * c + 1] = o[1];
+            v[4 * c + 2] = o[2];
+            v[4 * c + 3] = o[3];
+          }
+          if (half == 0) tc_fence_after();  // the MMA that read this TMEM stage has completed
+          tmem_st32(dst + half * 32, v);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        // the MMA waits only on a_full: hand over once the token tile landed too
+        if (!mbar_wait_all(&b_full[ts], (kb / C::AR) & 1, abort_flag, 112)) break;
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&r_empty[rs]);
+          mbar_arrive(&a_full[ts]);
+          if (quad == 0) K8V4_TRACE_EVENT(1, kb);
+        }
+      }
+    } else if (MODE != W8A8) {
       const int ct = threadIdx.x - 64;  // 0 .. NCONV*32-1
       int rs = 0, rphase = 0;
       for (int kb = 0; kb < nkb; ++kb) {
@@ -294,17 +398,13 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
     float acc[C::COLS];
 #pragma unroll
     for (int i = 0; i < C::COLS; ++i) acc[i] = 0.f;
-    // Group scales of this CTA's K range staged once in shared memory
-    // (coalesced rows of 128 features) so no global load sits between an
+    // Group scales of this CTA's K range: one TMA copy into shared memory
+    // (issued by the producer at start), so no global load sits between an
     // MMA's completion and the release of its TMEM buffer.
-    const bool staged = (MODE != W8A8) && ngroups <= C::MAXG;
-    if (staged) {
-      const int at = threadIdx.x - (2 + NCONV) * 32;
-      for (int i = at; i < ngroups * 128; i += NACC * 32)
-        sScale[i] = p.wscale[(size_t)((kbeg / 128) + (i >> 7)) * p.N + n0 + (i & 127)];
-      asm volatile("bar.sync 2, %0;" ::"r"(NACC * 32) : "memory");
-    }
-    bool ok = nkb > 0;
+    const bool staged = (MODE != W8A8) && p.k_per_split / 128 <= C::MAXG && nkb > 0;
+    bool scales_ok = true;
+    if (staged) scales_ok = mbar_wait_all(scale_bar, 0, abort_flag, 113);
+    bool ok = nkb > 0 && scales_ok;
     for (int g = 0; g < ngroups && ok; ++g) {
       const int buf = g % C::NBUF;
       if (!mbar_wait_all(&acc_full[buf], (g / C::NBUF) & 1, abort_flag, 108)) { ok = false; break; }
@@ -331,6 +431,7 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      if (lane == 0 && aw == 0) K8V4_TRACE_EVENT(3, g);
     }
     if (ok && n < p.N) {
       const float rs = (MODE == W8A8) ? __half2float(p.wscale[n]) : 1.f;
@@ -395,6 +496,7 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int
 
 template <int MODE, int BT, int NCONV, int NACC, int STAGES, int RSTAGES, int BSTAGES>
 static int launch_cfg(const void* w, const void* x, const Params& p, int split, cudaStream_t st) {
+  const void* wscale_ptr = p.wscale;
   using C = Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BSTAGES>;
   CUtensorMap tw, tx;
   int rc;
@@ -409,6 +511,16 @@ static int launch_cfg(const void* w, const void* x, const Params& p, int split, 
   else
     rc = make_tmap_2d(&tx, x, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.K, p.M, p.K, 128, BT, true);
   if (rc) return 200 + rc;
+  CUtensorMap ts;
+  if (MODE != W8A8) {
+    // group scales [K/128, N] fp16: one box of (128 features x groups of one split)
+    const int groups = p.k_per_split / 128;
+    rc = make_tmap_2d(&ts, wscale_ptr, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.N, p.K / 128, (uint64_t)p.N * 2, 128,
+                      groups <= C::MAXG ? groups : 1, false);
+    if (rc) return 400 + rc;
+  } else {
+    ts = tx;  // unused
+  }
   auto kern = wq_gemm_kernel<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BSTAGES>;
   static bool attr_set = false;
   if (!attr_set) {
@@ -416,7 +528,7 @@ static int launch_cfg(const void* w, const void* x, const Params& p, int split, 
     attr_set = true;
   }
   dim3 grid(cdiv(p.N, 128), cdiv(p.M, BT), split);
-  kern<<<grid, C::NTHREADS, C::SMEM_BYTES, st>>>(tw, tx, p);
+  kern<<<grid, C::NTHREADS, C::SMEM_BYTES, st>>>(tw, tx, ts, p);
   return cudaGetLastError() == cudaSuccess ? 0 : 300;
 }
 
@@ -427,6 +539,17 @@ using namespace k8v4;
 using namespace k8v4::gemm;
 
 K8V4_STATUS_API(gemm)
+
+#ifdef K8V4_TRACE
+extern "C" int k8v4_gemm_trace(uint64_t* host, int clear) {
+  int rc = cudaMemcpyFromSymbol(host, g_gemm_trace, sizeof(uint64_t) * 8 * 256);
+  if (clear) {
+    static uint64_t zeros[8 * 256] = {0};
+    cudaMemcpyToSymbol(g_gemm_trace, zeros, sizeof(zeros));
+  }
+  return rc;
+}
+#endif
 
 // Tokens per CTA for a given M: small M streams weights (decode), large M
 // reuses each converted weight tile over 128 tokens (prefill).
@@ -453,7 +576,7 @@ extern "C" int k8v4_wq_gemm(int mode, const void* w, const void* wscale, const v
   if (split > 1 && !ws) return 2;
   if (mode == W4A16) {
     if (M <= 16) return launch_cfg<W4A16, 16, 8, 4, 4, 16, 16>(w, x, p, split, st);
-    if (M <= 32) return launch_cfg<W4A16, 32, 8, 4, 4, 12, 12>(w, x, p, split, st);
+    if (M <= 32) return launch_cfg<W4A16, 32, 8, 4, 4, 12, 16>(w, x, p, split, st);
     if (M <= 64) return launch_cfg<W4A16, 64, 8, 4, 4, 8, 8>(w, x, p, split, st);
     return launch_cfg<W4A16, 128, 4, 8, 4, 8, 4>(w, x, p, split, st);
   }

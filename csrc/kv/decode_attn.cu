@@ -42,6 +42,19 @@ struct DecodeParams {
   float sm_scale_log2;        // softmax scale * log2(e)
 };
 
+#ifdef K8V4_TRACE
+// Timeline of CTA (0,0,0) (trace builds only): rows = 0 producer issued,
+// 1 converters done, 2 QK issued, 3 softmax done (p_full), 4 PV issued.
+__device__ uint64_t g_attn_trace[5 * 256];
+#define K8V4_ATRACE(row, idx)                                                             \
+  do {                                                                                    \
+    if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (idx) < 256)             \
+      g_attn_trace[(row) * 256 + (idx)] = globaltimer_ns();                               \
+  } while (0)
+#else
+#define K8V4_ATRACE(row, idx) do { } while (0)
+#endif
+
 template <int NPAD>
 struct DCfg {
   static constexpr int STAGES = 4;
@@ -55,8 +68,11 @@ struct DCfg {
                                    : TMEM_NEED <= 256 ? 256 : 512;
   // layout (offsets from the 1024-aligned base)
   static constexpr int OFF_K = 0;
+  // fp16 V^T tiles: three when shared memory allows, so conversion of tile
+  // j+1 never waits for the PV MMA of tile j-2
+  static constexpr int NVT = (NPAD <= 32) ? 3 : 2;
   static constexpr int OFF_VT = OFF_K + STAGES * K_TILE_BYTES;
-  static constexpr int OFF_PT = OFF_VT + 2 * VT_BYTES;
+  static constexpr int OFF_PT = OFF_VT + NVT * VT_BYTES;
   static constexpr int OFF_Q = OFF_PT + 2 * PT_BYTES;
   static constexpr int OFF_VS = OFF_Q + ((Q_BYTES + 1023) / 1024) * 1024;
   static constexpr int OFF_MISC = OFF_VS + STAGES * VS_TILE_BYTES;
@@ -83,9 +99,10 @@ __global__ void __launch_bounds__(DCfg<NPAD>::NTHREADS, 1)
   uint64_t* kv_empty = kv_full + C::STAGES;
   uint64_t* s_full = kv_empty + C::STAGES;  // [2] (buffer = owning group)
   uint64_t* p_full = s_full + 2;            // [2]
-  uint64_t* v_full = p_full + 2;            // [2]
-  uint64_t* pv_empty = v_full + 2;          // [2]
-  uint64_t* done_bar = pv_empty + 2;
+  uint64_t* v_full = p_full + 2;            // [NVT] V^T tile converted
+  uint64_t* pv_empty = v_full + 3;          // [2] PV of the group's last tile done (P^T / O^T reusable)
+  uint64_t* vt_empty = pv_empty + 2;        // [NVT] PV that read the V^T tile done
+  uint64_t* done_bar = vt_empty + 3;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   int* grp_ok = const_cast<int*>(abort_flag) + 1;            // [2]
@@ -117,8 +134,11 @@ __global__ void __launch_bounds__(DCfg<NPAD>::NTHREADS, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
       mbar_init(&p_full[b], 4);
-      mbar_init(&v_full[b], 4);
       mbar_init(&pv_empty[b], 1);
+    }
+    for (int v = 0; v < C::NVT; ++v) {
+      mbar_init(&v_full[v], 4);
+      mbar_init(&vt_empty[v], 1);
     }
     mbar_init(done_bar, 1);
     *abort_flag = 0;
@@ -186,6 +206,7 @@ __global__ void __launch_bounds__(DCfg<NPAD>::NTHREADS, 1)
           bulk_load(sVS + s * VS_TILE_BYTES + i * VS_BYTES, p.cache + run * HEAD_BYTES + VS_OFF, VS_BYTES,
                     &kv_full[s]);
         }
+        K8V4_ATRACE(0, j);
         ++issued;
       }
       if (*abort_flag)
@@ -211,15 +232,18 @@ __global__ void __launch_bounds__(DCfg<NPAD>::NTHREADS, 1)
                    id_qk, kk > 0 ? 1u : 0u);
           mma_commit(&s_full[b]);
           mma_commit(&kv_empty[s]);
+          K8V4_ATRACE(2, j);
         }
         if (j >= 1) {
           const int jj = j - 1, b = jj & 1;
-          if (!mbar_wait(&p_full[b], (jj >> 1) & 1, abort_flag, 203) || !mbar_wait(&v_full[b], (jj >> 1) & 1, abort_flag, 204)) {
+          const int vb = jj % C::NVT;
+          if (!mbar_wait(&p_full[b], (jj >> 1) & 1, abort_flag, 203) ||
+              !mbar_wait(&v_full[vb], (jj / C::NVT) & 1, abort_flag, 204)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t vt_base = smem_u32(sVT + b * VT_BYTES);
+          const uint32_t vt_base = smem_u32(sVT + vb * VT_BYTES);
           const uint32_t pt_base = smem_u32(sPT + b * C::PT_BYTES);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
@@ -228,6 +252,8 @@ __global__ void __launch_bounds__(DCfg<NPAD>::NTHREADS, 1)
             mma_f16(tm_o + b * NPAD, ad, bd, id_pv, (jj >= 2 || kk > 0) ? 1u : 0u);
           }
           mma_commit(&pv_empty[b]);
+          mma_commit(&vt_empty[vb]);
+          K8V4_ATRACE(4, jj);
         }
       }
       mma_commit(done_bar);
@@ -239,11 +265,12 @@ __global__ void __launch_bounds__(DCfg<NPAD>::NTHREADS, 1)
     for (int j = 0; j < nt; ++j) {
       const int s = j % C::STAGES, b = j & 1;
       if (!mbar_wait_all(&kv_full[s], (j / C::STAGES) & 1, abort_flag, 205)) break;
-      if (j >= 2 && !mbar_wait_all(&pv_empty[b], ((j >> 1) - 1) & 1, abort_flag, 206)) break;
+      const int vb = j % C::NVT;
+      if (j >= C::NVT && !mbar_wait_all(&vt_empty[vb], ((j / C::NVT) - 1) & 1, abort_flag, 206)) break;
       const int key0 = (tile_beg + j) * TILE;
       const int nvalid = min(TILE, seq_len - key0);
       const uint8_t* vs = sVS + s * VS_TILE_BYTES;
-      uint8_t* vt = sVT + b * VT_BYTES;
+      uint8_t* vt = sVT + vb * VT_BYTES;
 #pragma unroll 4
       for (int item = ct; item < TILE * 16; item += 128) {
         const int key = item >> 4, chunk = item & 15;
@@ -260,8 +287,9 @@ __global__ void __launch_bounds__(DCfg<NPAD>::NTHREADS, 1)
       fence_async_smem();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&v_full[b]);
+        mbar_arrive(&v_full[vb]);
         mbar_arrive(&kv_empty[s]);
+        if (ct < 32) K8V4_ATRACE(1, j);
       }
     }
   } else {
@@ -375,6 +403,7 @@ __global__ void __launch_bounds__(DCfg<NPAD>::NTHREADS, 1)
         if (lane == 0) {
           mbar_arrive(&p_full[b]);
           mbar_arrive(&kv_empty[s]);
+          if (sw == 0) K8V4_ATRACE(3, j);
         }
       }
       asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");  // rd / m reads done before the next tile
@@ -462,26 +491,47 @@ __global__ void __launch_bounds__(DCfg<NPAD>::NTHREADS, 1)
   }
 }
 
-// Merge split partials: grid (rows, heads, seqs), 128 threads (dims).
-__global__ void decode_combine_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_ml,
-                                      const int32_t* cu_q, __nv_bfloat16* out, int nsplit, int npad, int gqa,
-                                      int hq_total, int head_offset) {
+// Merge split partials: grid (rows, heads, seqs), 128 threads (dims). The
+// per-split weights are computed once by the block; the O loads of all splits
+// are independent, so their latencies overlap.
+__global__ void __launch_bounds__(128) decode_combine_kernel(const float* __restrict__ ws_o,
+                                                             const float* __restrict__ ws_ml, const int32_t* cu_q,
+                                                             __nv_bfloat16* out, int nsplit, int npad, int gqa,
+                                                             int hq_total, int head_offset) {
+  __shared__ float wsh[128];
+  __shared__ float red[8];
   const int r = blockIdx.x, hl = blockIdx.y, seq = blockIdx.z, d = threadIdx.x;
   const int qb = cu_q[seq], q_len = cu_q[seq + 1] - qb;
   if (r >= q_len * gqa) return;
   const int64_t base = ((int64_t)seq * gridDim.y + hl) * nsplit;
-  float M = -INFINITY;
-  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, ws_ml[((base + s) * 2) * npad + r]);
-  float L = 0.f, acc = 0.f;
-  if (M > -INFINITY) {
-    for (int s = 0; s < nsplit; ++s) {
-      const float m = ws_ml[((base + s) * 2) * npad + r];
-      if (m == -INFINITY) continue;
-      const float w = exp2f(m - M);
-      L += w * ws_ml[((base + s) * 2 + 1) * npad + r];
-      acc += w * ws_o[((base + s) * npad + r) * D + d];
-    }
+  float m = -INFINITY, l = 0.f;
+  if (d < nsplit) {
+    m = ws_ml[((base + d) * 2) * npad + r];
+    l = ws_ml[((base + d) * 2 + 1) * npad + r];
   }
+  float M = warp_max(m);
+  if ((d & 31) == 0) red[d >> 5] = M;
+  __syncthreads();
+  M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  const float w = (m == -INFINITY || M == -INFINITY) ? 0.f : exp2f(m - M);
+  if (d < nsplit) wsh[d] = w;
+  float L = warp_sum(w * l);
+  __syncthreads();
+  if ((d & 31) == 0) red[4 + (d >> 5)] = L;
+  __syncthreads();
+  L = red[4] + red[5] + red[6] + red[7];
+  const float* o = ws_o + (base * npad + r) * D + d;
+  const int64_t stride = (int64_t)npad * D;
+  float acc = 0.f;
+  int s = 0;
+  for (; s + 8 <= nsplit; s += 8) {
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = o[(s + i) * stride];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc += wsh[s + i] > 0.f ? wsh[s + i] * v[i] : 0.f;
+  }
+  for (; s < nsplit; ++s) acc += wsh[s] > 0.f ? wsh[s] * o[s * stride] : 0.f;
   const int t = r / gqa, g = r % gqa, h = hl + head_offset;
   out[((int64_t)(qb + t) * hq_total + (int64_t)h * gqa + g) * D + d] = __float2bfloat16_rn(L > 0.f ? acc / L : 0.f);
 }
@@ -525,6 +575,12 @@ extern "C" int k8v4_make_kv_tmap(void* map_out, const void* cache, int64_t num_p
 
 K8V4_STATUS_API(decode)
 
+#ifdef K8V4_TRACE
+extern "C" int k8v4_attn_trace(uint64_t* host) {
+  return cudaMemcpyFromSymbol(host, g_attn_trace, sizeof(uint64_t) * 5 * 256);
+}
+#endif
+
 template <int NPAD>
 static int launch_decode(const CUtensorMap& tm, const DecodeParams& p, int heads, int nseq, cudaStream_t st) {
   using C = DCfg<NPAD>;
@@ -548,6 +604,7 @@ extern "C" int k8v4_decode_attn(const void* q, const int32_t* cu_q, const int32_
   const int rows = max_q_len * gqa;
   if (rows <= 0 || nseq <= 0) return 0;
   if (rows > 64) return 1;  // longer query runs use the prefill kernel
+  if (nsplit > 128) return 4;
   if (nsplit < 1) nsplit = 1;
   if (nsplit > 1 && (!ws_o || !ws_ml)) return 2;
   CUtensorMap tm;

@@ -66,9 +66,14 @@ class EngineConfig:
 
 
 def decode_splits(max_pages: int, nseq: int, heads: int) -> int:
-    """Split-K factor for decode attention: about two waves of CTAs."""
+    """Split-K factor for decode attention: one full wave of CTAs.
+
+    The kernel runs one CTA per SM, so splits * sequences * heads <= 148
+    keeps every CTA in the first wave (a second partial wave measured
+    slower than fewer, longer splits).
+    """
     tiles = max(1, (max_pages + 7) // 8)
-    want = max(1, (2 * NUM_SMS) // max(1, nseq * heads))
+    want = max(1, NUM_SMS // max(1, nseq * heads))
     return int(max(1, min(want, tiles, 64)))
 
 
