@@ -30,8 +30,8 @@ int k8v4_prefill_attn(const void* q, const int32_t* cu_q, const int32_t* seq_len
 int k8v4_wq_gemm(int mode, const void* w, const void* wscale, const void* x, const float* xscale,
                  const void* residual, void* out, float* ws, int M, int N, int K, int ldo, int split,
                  cudaStream_t st);
-int k8v4_rmsnorm(const void* x, void* residual, const void* w, void* y, void* yq, float* yscale, int rows, int n,
-                 float eps, cudaStream_t st);
+int k8v4_rmsnorm(const void* x, float* xf, void* residual, const void* w, void* y, void* yq, float* yscale,
+                 int rows, int n, float eps, cudaStream_t st);
 int k8v4_silu_mul(const void* gu, void* y, void* yq, float* yscale, int rows, int inter, cudaStream_t st);
 int k8v4_quant_rows(const void* x, void* q, float* scale, int rows, int n, cudaStream_t st);
 int k8v4_embed_int8(const int64_t* ids, const void* codes, const void* scales, void* out, int T, int n,
@@ -185,7 +185,7 @@ void prefill_attn(const at::Tensor& q, const at::Tensor& cu_q, const at::Tensor&
 // mode 0: W4A16 (x bf16), 1: W4A8 (x int8 + xscale), 2: W8A8 (w int8 [N,K] + per-row scale).
 void wq_gemm(int64_t mode, const at::Tensor& w, const at::Tensor& wscale, const at::Tensor& x,
              const c10::optional<at::Tensor>& xscale, const c10::optional<at::Tensor>& residual, at::Tensor& out,
-             const c10::optional<at::Tensor>& ws, int64_t split) {
+             const c10::optional<at::Tensor>& ws, int64_t split, bool finish) {
   check_contig(w, "weight");
   check_contig(wscale, "weight scale");
   check_contig(x, "x");
@@ -233,18 +233,20 @@ void wq_gemm(int64_t mode, const at::Tensor& w, const at::Tensor& wscale, const 
   check_rc(k8v4_wq_gemm((int)mode, w.data_ptr(), wscale.data_ptr(), x.data_ptr(), xs, res, out.data_ptr(), wsp,
                         (int)M, (int)N, (int)K, (int)N, (int)split, cur_stream()),
            "wq_gemm");
-  if (split > 1) {
+  if (split > 1 && finish) {
     check_rc(k8v4_splitk_finish(wsp, res, out.data_ptr(), M * N, 1, cur_stream()), "splitk_finish");
   }
 }
 
 // -------------------------------------------------------------- fused misc
-void rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual, const at::Tensor& w,
+void rmsnorm(at::Tensor& x, const c10::optional<at::Tensor>& residual, const at::Tensor& w,
              const c10::optional<at::Tensor>& y, const c10::optional<at::Tensor>& yq,
              const c10::optional<at::Tensor>& yscale, double eps) {
   check_contig(x, "x");
   check_contig(w, "weight");
-  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "bf16 inputs");
+  TORCH_CHECK((x.scalar_type() == at::kBFloat16 || x.scalar_type() == at::kFloat) && w.scalar_type() == at::kBFloat16,
+              "x bf16 (or fp32 split-K partials, zeroed after reading) and bf16 weight");
+  const bool f32 = x.scalar_type() == at::kFloat;
   const int64_t n = x.size(-1), rows = x.numel() / n;
   TORCH_CHECK(w.numel() == n, "weight size");
   void* r = nullptr;
@@ -269,7 +271,8 @@ void rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual, con
     sp = yscale->data_ptr<float>();
   }
   c10::cuda::CUDAGuard g(x.device());
-  check_rc(k8v4_rmsnorm(x.data_ptr(), r, w.data_ptr(), yp, qp, sp, (int)rows, (int)n, (float)eps, cur_stream()),
+  check_rc(k8v4_rmsnorm(f32 ? nullptr : x.data_ptr(), f32 ? x.data_ptr<float>() : nullptr, r, w.data_ptr(), yp, qp,
+                        sp, (int)rows, (int)n, (float)eps, cur_stream()),
            "rmsnorm");
 }
 
@@ -369,9 +372,9 @@ TORCH_LIBRARY(k8v4, m) {
       "int head_offset, int heads, int gqa, int max_q_len, float sm_scale, Tensor(a!) out) -> ()");
   m.def(
       "wq_gemm(int mode, Tensor w, Tensor wscale, Tensor x, Tensor? xscale, Tensor? residual, Tensor(a!) out, "
-      "Tensor(b!)? ws, int split) -> ()");
+      "Tensor(b!)? ws, int split, bool finish=True) -> ()");
   m.def(
-      "rmsnorm(Tensor x, Tensor(a!)? residual, Tensor w, Tensor(b!)? y, Tensor(c!)? yq, Tensor(d!)? yscale, "
+      "rmsnorm(Tensor(e!) x, Tensor(a!)? residual, Tensor w, Tensor(b!)? y, Tensor(c!)? yq, Tensor(d!)? yscale, "
       "float eps) -> ()");
   m.def("silu_mul(Tensor gate_up, Tensor(a!)? y, Tensor(b!)? yq, Tensor(c!)? yscale) -> ()");
   m.def("quant_rows(Tensor x, Tensor(a!) q, Tensor(b!) scale) -> ()");

@@ -87,7 +87,10 @@ __device__ __forceinline__ void quant_row(const float (&v)[VPT][8], int n, int8_
 // x: [T, n] bf16. If residual != nullptr: h = x + residual, residual <- h.
 // y = h * rsqrt(mean(h^2) + eps) * w. Outputs bf16 y and/or int8 y + scale.
 template <int VPT>
-__global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const __nv_bfloat16* __restrict__ x,
+// x may instead arrive as fp32 split-K partial sums `xf` (the finishing step
+// of a split-K GEMM fused into this norm); xf is zeroed after it is read so
+// the shared accumulator is clean for the next split-K GEMM.
+__global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, float* xf,
                                                            __nv_bfloat16* residual, const __nv_bfloat16* __restrict__ w,
                                                            __nv_bfloat16* y, int8_t* yq, float* yscale, int n,
                                                            float eps) {
@@ -99,7 +102,16 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const __nv_bfloat16* 
   for (int i = 0; i < VPT; ++i) {
     const int c = (threadIdx.x + i * kThreads) * 8;
     if (c < n) {
-      load8(x + row * n + c, v[i]);
+      if (xf) {
+        float4* p4 = reinterpret_cast<float4*>(xf + row * n + c);
+        const float4 a = p4[0], b = p4[1];
+        v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
+        v[i][4] = b.x; v[i][5] = b.y; v[i][6] = b.z; v[i][7] = b.w;
+        p4[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+        p4[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      } else {
+        load8(x + row * n + c, v[i]);
+      }
       if (residual) {
         float r[8];
         load8(residual + row * n + c, r);
@@ -155,6 +167,23 @@ __global__ void __launch_bounds__(kThreads) silu_mul_kernel(const __nv_bfloat16*
     }
   }
   if (yq) quant_row<VPT>(v, inter, yq + row * inter, yscale + row, red);
+}
+
+// bf16-only SiLU(gate)*up spread over the whole grid (one 8-wide vector per
+// thread), for the few-token decode rows where one CTA per row is too serial.
+__global__ void __launch_bounds__(256) silu_mul_wide_kernel(const __nv_bfloat16* __restrict__ gu,
+                                                            __nv_bfloat16* __restrict__ y, int inter, int64_t total) {
+  const int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (v >= total) return;
+  const int per_row = inter / 8;
+  const int64_t row = v / per_row;
+  const int c = (int)(v % per_row) * 8;
+  float g[8], u[8], o[8];
+  load8(gu + row * 2 * inter + c, g);
+  load8(gu + row * 2 * inter + inter + c, u);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) o[j] = g[j] / (1.f + __expf(-g[j])) * u[j];
+  store8(y + row * inter + c, o);
 }
 
 // Row-wise int8 quantization of bf16 rows.
@@ -235,11 +264,11 @@ K8V4_STATUS_API(misc)
     else return 2;                                                                \
   } while (0)
 
-extern "C" int k8v4_rmsnorm(const void* x, void* residual, const void* w, void* y, void* yq, float* yscale, int rows,
-                            int n, float eps, cudaStream_t st) {
+extern "C" int k8v4_rmsnorm(const void* x, float* xf, void* residual, const void* w, void* y, void* yq, float* yscale,
+                            int rows, int n, float eps, cudaStream_t st) {
   if (rows <= 0) return 0;
   if (n % 8) return 1;
-  K8V4_VPT_DISPATCH(n, rmsnorm_kernel, reinterpret_cast<const __nv_bfloat16*>(x),
+  K8V4_VPT_DISPATCH(n, rmsnorm_kernel, reinterpret_cast<const __nv_bfloat16*>(x), xf,
                     reinterpret_cast<__nv_bfloat16*>(residual), reinterpret_cast<const __nv_bfloat16*>(w),
                     reinterpret_cast<__nv_bfloat16*>(y), reinterpret_cast<int8_t*>(yq), yscale, n, eps);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
@@ -249,6 +278,12 @@ extern "C" int k8v4_silu_mul(const void* gu, void* y, void* yq, float* yscale, i
                              cudaStream_t st) {
   if (rows <= 0) return 0;
   if (inter % 8) return 1;
+  if (!yq && y && rows <= 16) {
+    const int64_t total = (int64_t)rows * (inter / 8);
+    silu_mul_wide_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
+        reinterpret_cast<const __nv_bfloat16*>(gu), reinterpret_cast<__nv_bfloat16*>(y), inter, total);
+    return cudaGetLastError() == cudaSuccess ? 0 : 3;
+  }
   K8V4_VPT_DISPATCH(inter, silu_mul_kernel, reinterpret_cast<const __nv_bfloat16*>(gu),
                     reinterpret_cast<__nv_bfloat16*>(y), reinterpret_cast<int8_t*>(yq), yscale, inter);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;

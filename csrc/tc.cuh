@@ -39,6 +39,7 @@ constexpr uint32_t kSuspendHintNs = K8V4_SUSPEND_HINT_NS;
 
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
+
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
 #if K8V4_SUSPEND_HINT_NS > 0

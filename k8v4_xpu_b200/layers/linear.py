@@ -59,15 +59,22 @@ class Int4Linear:
         self.in_features = qweight.shape[0] * 8
         self.out_features = qweight.shape[1]
 
+    def split(self, rows: int, ws) -> int:
+        return split_for(rows, self.out_features, self.in_features) if ws is not None else 1
+
     def __call__(self, x: torch.Tensor | None = None, xq: torch.Tensor | None = None,
                  xs: torch.Tensor | None = None, out: torch.Tensor | None = None,
-                 ws: torch.Tensor | None = None, split: int | None = None) -> torch.Tensor:
+                 ws: torch.Tensor | None = None, split: int | None = None, defer: bool = False) -> torch.Tensor:
+        """Run the GEMM. With ``defer`` and a split-K launch, returns the fp32
+        partial-sum view of ``ws`` (rows x out_features) for a fused consumer."""
         if xq is not None:
-            rows = xq.shape[0]
             return ops.wq_gemm(ops.W4A8, self.qweight, self.scales, xq, xscale=xs, out=out)
         rows = x.shape[0]
         if split is None:
-            split = split_for(rows, self.out_features, self.in_features) if ws is not None else 1
+            split = self.split(rows, ws)
+        if defer and split > 1:
+            ops.wq_gemm(ops.W4A16, self.qweight, self.scales, x, out=out, ws=ws, split=split, finish=False)
+            return ws[: rows * self.out_features].view(rows, self.out_features)
         return ops.wq_gemm(ops.W4A16, self.qweight, self.scales, x, out=out, ws=ws, split=split)
 
     def reference(self, x: torch.Tensor) -> torch.Tensor:

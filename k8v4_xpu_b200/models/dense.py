@@ -203,7 +203,8 @@ class DenseModel:
             else:
                 a = ops.prefill_attn(q, inp.cu_q, inp.seq_lens, inp.block_table, cache, hkv, sh.gqa_local,
                                      inp.max_q_len)
-            x = L.o(a.view(T, hq * D), ws=splitk_ws)
+            # single GPU: leave split-K partials for the fused norm below to finish
+            x = L.o(a.view(T, hq * D), ws=splitk_ws, defer=self.tp == 1)
             self._all_reduce(x)
             # ---- MLP block
             if uses_w4a8(L.gate_up.name, T, self.w4a8):
@@ -215,8 +216,12 @@ class DenseModel:
                 h = ops.rmsnorm(x, L.post_norm, cfg.rms_eps, residual=residual)
                 gu = L.gate_up(h, ws=splitk_ws)
                 act = ops.silu_mul(gu)
-                x = L.down(act, ws=splitk_ws)
+                x = L.down(act, ws=splitk_ws, defer=self.tp == 1)
             self._all_reduce(x)
+        if x.dtype == torch.float32:
+            # last layer's split-K partials: finish them in the final norm over all rows
+            h = ops.rmsnorm(x, self.final_norm, cfg.rms_eps, residual=residual)
+            return h.index_select(0, inp.logit_rows)
         rows = inp.logit_rows
         xs = x.index_select(0, rows)
         rs = residual.index_select(0, rows)

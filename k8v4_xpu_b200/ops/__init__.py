@@ -138,7 +138,10 @@ W4A16, W4A8, W8A8 = 0, 1, 2
 
 
 def wq_gemm(mode: int, w: torch.Tensor, wscale: torch.Tensor, x: torch.Tensor, xscale=None, residual=None,
-            out=None, ws=None, split: int = 1) -> torch.Tensor:
+            out=None, ws=None, split: int = 1, finish: bool = True) -> torch.Tensor:
+    """Quantized-weight GEMM. With ``split > 1`` and ``finish=False`` the fp32
+    partial sums stay in ``ws`` for a consumer that finishes them (the fused
+    RMSNorm); ``out`` is then not written."""
     require()
     n = w.shape[0] if mode == W8A8 else w.shape[1]
     if out is None:
@@ -147,14 +150,18 @@ def wq_gemm(mode: int, w: torch.Tensor, wscale: torch.Tensor, x: torch.Tensor, x
         ws = torch.zeros((x.shape[0], n), dtype=torch.float32, device=x.device)
     if x.shape[0] == 0:
         return out
-    torch.ops.k8v4.wq_gemm(mode, w, wscale, x, xscale, residual, out, ws, split)
-    _count(2 if split > 1 else 1)
+    torch.ops.k8v4.wq_gemm(mode, w, wscale, x, xscale, residual, out, ws, split, finish)
+    _count(2 if split > 1 and finish else 1)
     return out
 
 
 # ------------------------------------------------------------------- fused
 def rmsnorm(x, w, eps=1e-6, residual=None, out=None, quant=False):
-    """RMSNorm (optionally residual-add first); returns y, or (q, scale) with quant."""
+    """RMSNorm (optionally residual-add first); returns y, or (q, scale) with quant.
+
+    ``x`` may be the fp32 split-K accumulator of the preceding GEMM: it is
+    consumed (and zeroed) here, finishing that GEMM inside the norm.
+    """
     require()
     rows = x.numel() // x.shape[-1]
     if quant:
@@ -164,7 +171,7 @@ def rmsnorm(x, w, eps=1e-6, residual=None, out=None, quant=False):
         _count()
         return (out, q, s) if out is not None else (q, s)
     if out is None:
-        out = torch.empty_like(x)
+        out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
     torch.ops.k8v4.rmsnorm(x, residual, w, out, None, None, eps)
     _count()
     return out
