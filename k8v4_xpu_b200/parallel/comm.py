@@ -56,11 +56,11 @@ class TPComm:
     def all_gather(self, t: torch.Tensor, dim: int = 0) -> torch.Tensor:
         if self.world == 1:
             return t
-        out = torch.empty((self.world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
+        out = torch.empty((self.world * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
         dist.all_gather_into_tensor(out, t.contiguous(), group=self.group)
         if dim == 0:
-            return out.reshape((self.world * t.shape[0],) + tuple(t.shape[1:]))
-        return torch.cat(list(out.unbind(0)), dim=dim)
+            return out
+        return torch.cat(list(out.chunk(self.world, 0)), dim=dim)
 
     def reduce_scatter(self, t: torch.Tensor) -> torch.Tensor:
         if self.world == 1:
@@ -74,7 +74,7 @@ class TPComm:
         if self.world == 1:
             return val, idx
         packed = torch.stack([val.float(), idx.float()], 0)  # exact: vocab indices < 2^24
-        allp = self.all_gather(packed.unsqueeze(0)).view(self.world, 2, -1)
+        allp = self.all_gather(packed.unsqueeze(0)).view(self.world, 2, -1)  # [world, (val, idx), rows]
         vals, idxs = allp[:, 0], allp[:, 1]
         best = vals.max(dim=0).values
         cand = torch.where(vals == best.unsqueeze(0), idxs, torch.full_like(idxs, float("inf")))

@@ -1,0 +1,68 @@
+"""TP communicator on CPU: two ``gloo`` ranks as child processes."""
+import os
+import socket
+
+import torch
+import torch.multiprocessing as mp
+
+
+def _free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
+    import torch.distributed as dist
+    from k8v4_xpu_b200.parallel.comm import TPComm, init_from_env
+    import traceback
+    try:
+        r, w, _ = init_from_env(timeout_s=60, backend="gloo")
+        comm = TPComm()
+        res = {}
+        t = torch.full((4,), float(r + 1))
+        res["all_reduce"] = comm.all_reduce(t.clone()).tolist()
+        res["all_gather"] = comm.all_gather(torch.tensor([[r, r]], dtype=torch.float32)).tolist()
+        res["all_gather_d1"] = comm.all_gather(torch.tensor([[r], [r]], dtype=torch.float32), dim=1).tolist()
+        res["reduce_scatter"] = comm.reduce_scatter(torch.arange(4, dtype=torch.float32) * (r + 1)).tolist()
+        # row 0: rank 1 wins; row 1: tie -> lowest global index
+        val = torch.tensor([1.0, 5.0]) if r == 0 else torch.tensor([2.0, 5.0])
+        idx = torch.tensor([10, 30]) if r == 0 else torch.tensor([1010, 7])
+        bv, bi = comm.argmax_reduce(val, idx)
+        res["argmax"] = (bv.tolist(), bi.tolist())
+        res["max_scalar"] = comm.max_scalar(float(r) * 3.5)
+        comm.barrier()
+        q.put((r, res))
+    except Exception:
+        q.put((rank, {"error": traceback.format_exc()}))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def test_tp_comm_gloo_two_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in range(2):
+        res = out[r]
+        assert "error" not in res, res.get("error")
+        assert res["all_reduce"] == [3.0] * 4
+        assert res["all_gather"] == [[0.0, 0.0], [1.0, 1.0]]
+        assert res["all_gather_d1"] == [[0.0, 1.0], [0.0, 1.0]]
+        assert res["argmax"] == ([2.0, 5.0], [1010, 7])
+        assert res["max_scalar"] == 3.5
+    # sum = [0, 3, 6, 9]; rank r keeps elements 2r, 2r+1
+    assert out[0]["reduce_scatter"] == [0.0, 3.0]
+    assert out[1]["reduce_scatter"] == [6.0, 9.0]
