@@ -30,8 +30,8 @@ int k8v4_prefill_attn(const void* q, const int32_t* cu_q, const int32_t* seq_len
 int k8v4_wq_gemm(int mode, const void* w, const void* wscale, const void* x, const float* xscale,
                  const void* residual, void* out, float* ws, int M, int N, int K, int ldo, int split,
                  cudaStream_t st);
-int k8v4_rmsnorm(const void* x, float* xf, void* residual, const void* w, void* y, void* yq, float* yscale,
-                 int rows, int n, float eps, cudaStream_t st);
+int k8v4_rmsnorm(const void* x, float* xf, void* residual, const void* w, void* y, int64_t ldy, void* yq,
+                 float* yscale, int rows, int n, float eps, cudaStream_t st);
 int k8v4_silu_mul(const void* gu, void* y, void* yq, float* yscale, int rows, int inter, cudaStream_t st);
 int k8v4_quant_rows(const void* x, void* q, float* scale, int rows, int n, cudaStream_t st);
 int k8v4_embed_int8(const int64_t* ids, const void* codes, const void* scales, void* out, int T, int n,
@@ -256,9 +256,16 @@ void rmsnorm(at::Tensor& x, const c10::optional<at::Tensor>& residual, const at:
     r = residual->data_ptr();
   }
   void* yp = nullptr;
+  int64_t ldy = n;
   if (y.has_value()) {
-    check_contig(*y, "y");
-    TORCH_CHECK(y->numel() == x.numel() && y->scalar_type() == at::kBFloat16, "y");
+    // y may be a row-strided view (e.g. one half of a concatenated [rows, 2n] buffer)
+    check_cuda(*y, "y");
+    TORCH_CHECK(y->scalar_type() == at::kBFloat16 && y->numel() == x.numel() && y->size(-1) == n &&
+                    y->stride(-1) == 1 && (y->dim() == 1 || y->dim() == 2),
+                "y: bf16 [rows, n] with unit inner stride");
+    if (y->dim() == 2) ldy = y->stride(0);
+    TORCH_CHECK(ldy >= n && ldy % 8 == 0 && reinterpret_cast<uintptr_t>(y->data_ptr()) % 16 == 0,
+                "y rows must be 16-byte aligned");
     yp = y->data_ptr();
   }
   void* qp = nullptr;
@@ -271,8 +278,8 @@ void rmsnorm(at::Tensor& x, const c10::optional<at::Tensor>& residual, const at:
     sp = yscale->data_ptr<float>();
   }
   c10::cuda::CUDAGuard g(x.device());
-  check_rc(k8v4_rmsnorm(f32 ? nullptr : x.data_ptr(), f32 ? x.data_ptr<float>() : nullptr, r, w.data_ptr(), yp, qp,
-                        sp, (int)rows, (int)n, (float)eps, cur_stream()),
+  check_rc(k8v4_rmsnorm(f32 ? nullptr : x.data_ptr(), f32 ? x.data_ptr<float>() : nullptr, r, w.data_ptr(), yp, ldy,
+                        qp, sp, (int)rows, (int)n, (float)eps, cur_stream()),
            "rmsnorm");
 }
 

@@ -85,7 +85,8 @@ __device__ __forceinline__ void quant_row(const float (&v)[VPT][8], int n, int8_
 }
 
 // x: [T, n] bf16. If residual != nullptr: h = x + residual, residual <- h.
-// y = h * rsqrt(mean(h^2) + eps) * w. Outputs bf16 y and/or int8 y + scale.
+// y = h * rsqrt(mean(h^2) + eps) * w. Outputs bf16 y (row stride ldy, so two
+// norms can write the halves of one concatenated row) and/or int8 y + scale.
 template <int VPT>
 // x may instead arrive as fp32 split-K partial sums `xf` (the finishing step
 // of a split-K GEMM fused into this norm); xf is zeroed after it is read so
@@ -93,7 +94,7 @@ template <int VPT>
 __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, float* xf,
                                                            __nv_bfloat16* residual, const __nv_bfloat16* __restrict__ w,
                                                            __nv_bfloat16* y, int8_t* yq, float* yscale, int n,
-                                                           float eps) {
+                                                           int64_t ldy, float eps) {
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   float v[VPT][8];
@@ -138,7 +139,7 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const __nv_bfloat16* 
       for (int j = 0; j < 8; ++j) v[i][j] = __bfloat162float(__float2bfloat16_rn(v[i][j] * inv)) * g[j];
 #pragma unroll
       for (int j = 0; j < 8; ++j) v[i][j] = __bfloat162float(__float2bfloat16_rn(v[i][j]));
-      if (y) store8(y + row * n + c, v[i]);
+      if (y) store8(y + row * ldy + c, v[i]);
     }
   }
   if (yq) quant_row<VPT>(v, n, yq + row * n, yscale + row, red);
@@ -264,13 +265,13 @@ K8V4_STATUS_API(misc)
     else return 2;                                                                \
   } while (0)
 
-extern "C" int k8v4_rmsnorm(const void* x, float* xf, void* residual, const void* w, void* y, void* yq, float* yscale,
-                            int rows, int n, float eps, cudaStream_t st) {
+extern "C" int k8v4_rmsnorm(const void* x, float* xf, void* residual, const void* w, void* y, int64_t ldy, void* yq,
+                            float* yscale, int rows, int n, float eps, cudaStream_t st) {
   if (rows <= 0) return 0;
-  if (n % 8) return 1;
+  if (n % 8 || ldy < n || ldy % 8) return 1;
   K8V4_VPT_DISPATCH(n, rmsnorm_kernel, reinterpret_cast<const __nv_bfloat16*>(x), xf,
                     reinterpret_cast<__nv_bfloat16*>(residual), reinterpret_cast<const __nv_bfloat16*>(w),
-                    reinterpret_cast<__nv_bfloat16*>(y), reinterpret_cast<int8_t*>(yq), yscale, n, eps);
+                    reinterpret_cast<__nv_bfloat16*>(y), reinterpret_cast<int8_t*>(yq), yscale, n, ldy, eps);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 

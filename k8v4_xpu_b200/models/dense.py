@@ -58,6 +58,15 @@ class LayerWeights:
     down: Int4Linear
 
 
+@dataclasses.dataclass
+class MTPWeights:
+    enorm: torch.Tensor
+    hnorm: torch.Tensor
+    norm: torch.Tensor
+    eh_proj: Int4Linear
+    layer: LayerWeights
+
+
 def rope_table(max_pos: int, head_dim: int, theta: float, device) -> torch.Tensor:
     """fp32 ``[max_pos, head_dim]``: cos of the half-dim frequencies then sin."""
     inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim))
@@ -176,56 +185,124 @@ class DenseModel:
         x = ops.embed_int8(ids, self.embed_codes, self.embed_scales, start=self.vocab_start, out=out)
         return self._all_reduce(x)
 
-    def forward(self, inp: StepInputs, kv_caches: list[torch.Tensor], ws=None) -> torch.Tensor:
-        """Run every layer; returns the final-normed hidden rows ``inp.logit_rows``."""
+    def _layer(self, L: LayerWeights, x: torch.Tensor, residual: torch.Tensor | None, inp: StepInputs,
+               cache: torch.Tensor, ws, defer: bool) -> tuple[torch.Tensor, torch.Tensor]:
+        """One decoder layer. ``x`` may be fp32 split-K partials left by the
+        previous layer (finished inside the fused norm). Returns (x, residual)."""
         cfg, sh = self.cfg, self.shape
         T = inp.input_ids.shape[0]
-        H, D = cfg.hidden, cfg.head_dim
-        x = self.embed(inp.input_ids)
-        residual = None
+        D = cfg.head_dim
         hq, hkv = sh.hq_local, sh.hkv_local
         splitk_ws = ws.splitk if ws is not None else None
-        for li, L in enumerate(self.layers):
-            # ---- attention block
-            if residual is None:
-                residual = x.clone()
-                h = ops.rmsnorm(x, L.input_norm, cfg.rms_eps)
-            else:
-                h = ops.rmsnorm(x, L.input_norm, cfg.rms_eps, residual=residual)
-            qkv = L.qkv(h, ws=splitk_ws)
-            q = torch.empty((T, hq, D), dtype=torch.bfloat16, device=self.device)
-            cache = kv_caches[li]
-            ops.rope_store(qkv, self.rope, inp.positions, q, inp.slots, cache, hq, hkv)
-            if inp.is_decode:
-                a = ops.decode_attn(q, inp.cu_q, inp.seq_lens, inp.block_table, cache, hkv, sh.gqa_local,
-                                    inp.max_q_len, nsplit=inp.nsplit, q_ends=inp.q_ends,
-                                    ws=(ws.attn if ws is not None else None))
-            else:
-                a = ops.prefill_attn(q, inp.cu_q, inp.seq_lens, inp.block_table, cache, hkv, sh.gqa_local,
-                                     inp.max_q_len)
-            # single GPU: leave split-K partials for the fused norm below to finish
-            x = L.o(a.view(T, hq * D), ws=splitk_ws, defer=self.tp == 1)
-            self._all_reduce(x)
-            # ---- MLP block
-            if uses_w4a8(L.gate_up.name, T, self.w4a8):
-                hq8, hs = ops.rmsnorm(x, L.post_norm, cfg.rms_eps, residual=residual, quant=True)
-                gu = L.gate_up(xq=hq8, xs=hs)
-                aq, as_ = ops.silu_mul(gu, quant=True)
-                x = L.down(xq=aq, xs=as_)
-            else:
-                h = ops.rmsnorm(x, L.post_norm, cfg.rms_eps, residual=residual)
-                gu = L.gate_up(h, ws=splitk_ws)
-                act = ops.silu_mul(gu)
-                x = L.down(act, ws=splitk_ws, defer=self.tp == 1)
-            self._all_reduce(x)
-        if x.dtype == torch.float32:
-            # last layer's split-K partials: finish them in the final norm over all rows
-            h = ops.rmsnorm(x, self.final_norm, cfg.rms_eps, residual=residual)
-            return h.index_select(0, inp.logit_rows)
-        rows = inp.logit_rows
+        # ---- attention block
+        if residual is None:
+            residual = x.clone()
+            h = ops.rmsnorm(x, L.input_norm, cfg.rms_eps)
+        else:
+            h = ops.rmsnorm(x, L.input_norm, cfg.rms_eps, residual=residual)
+        qkv = L.qkv(h, ws=splitk_ws)
+        q = torch.empty((T, hq, D), dtype=torch.bfloat16, device=self.device)
+        ops.rope_store(qkv, self.rope, inp.positions, q, inp.slots, cache, hq, hkv)
+        if inp.is_decode:
+            a = ops.decode_attn(q, inp.cu_q, inp.seq_lens, inp.block_table, cache, hkv, sh.gqa_local,
+                                inp.max_q_len, nsplit=inp.nsplit, q_ends=inp.q_ends,
+                                ws=(ws.attn if ws is not None else None))
+        else:
+            a = ops.prefill_attn(q, inp.cu_q, inp.seq_lens, inp.block_table, cache, hkv, sh.gqa_local,
+                                 inp.max_q_len)
+        # single GPU: leave split-K partials for the fused norm below to finish
+        x = L.o(a.view(T, hq * D), ws=splitk_ws, defer=defer)
+        self._all_reduce(x)
+        # ---- MLP block
+        if uses_w4a8(L.gate_up.name, T, self.w4a8):
+            hq8, hs = ops.rmsnorm(x, L.post_norm, cfg.rms_eps, residual=residual, quant=True)
+            gu = L.gate_up(xq=hq8, xs=hs)
+            aq, as_ = ops.silu_mul(gu, quant=True)
+            x = L.down(xq=aq, xs=as_)
+        else:
+            h = ops.rmsnorm(x, L.post_norm, cfg.rms_eps, residual=residual)
+            gu = L.gate_up(h, ws=splitk_ws)
+            act = ops.silu_mul(gu)
+            x = L.down(act, ws=splitk_ws, defer=defer)
+        self._all_reduce(x)
+        return x, residual
+
+    def _final_norm(self, x, residual, norm_w, rows: torch.Tensor | None) -> torch.Tensor:
+        cfg = self.cfg
+        if x.dtype == torch.float32 or rows is None:
+            # split-K partials (or every row wanted): finish them in the norm over all rows
+            h = ops.rmsnorm(x, norm_w, cfg.rms_eps, residual=residual)
+            return h if rows is None else h.index_select(0, rows)
         xs = x.index_select(0, rows)
         rs = residual.index_select(0, rows)
-        return ops.rmsnorm(xs, self.final_norm, cfg.rms_eps, residual=rs)
+        return ops.rmsnorm(xs, norm_w, cfg.rms_eps, residual=rs)
+
+    def forward(self, inp: StepInputs, kv_caches: list[torch.Tensor], ws=None,
+                all_rows: bool = False) -> torch.Tensor:
+        """Run every layer; returns the final-normed hidden rows ``inp.logit_rows``
+        (every row with ``all_rows``, as the MTP drafter needs)."""
+        x = self.embed(inp.input_ids)
+        residual = None
+        defer = self.tp == 1
+        for li, L in enumerate(self.layers):
+            x, residual = self._layer(L, x, residual, inp, kv_caches[li], ws, defer)
+        return self._final_norm(x, residual, self.final_norm, None if all_rows else inp.logit_rows)
+
+    # ---------------------------------------------------------------- MTP
+    def init_mtp(self, seed: int = 1) -> "DenseModel":
+        """Random-init the MTP draft module (one decoder layer of the same shape).
+
+        Structure of the multi-token-prediction head served by the reference's
+        ``--speculative-config mtp/6`` (``k8v4_v030/launch.sh:193``): the
+        embedding of the next token and the target's final hidden state are
+        normed separately, concatenated and projected back to ``hidden``
+        (``eh_proj``, a column-parallel GPTQ linear), run through one decoder
+        layer with its own KV cache, normed, and scored by the shared lm_head.
+        """
+        cfg, sh = self.cfg, self.shape
+        dev = self.device
+        gen = torch.Generator(device=dev).manual_seed(seed + 7919)
+        H = cfg.hidden
+        # eh_proj: [2H -> H]; under TP every rank holds all of it (it feeds the replicated residual)
+        eh_q, eh_s = _rand_int4(2 * H, H, gen, dev)
+        qkv_q, qkv_s = self._shard_qkv(*_rand_int4(H, cfg.q_size + 2 * cfg.kv_size, gen, dev))
+        o_q, o_s = self._shard_rows(*_rand_int4(cfg.q_size, H, gen, dev), sh.hq_local * cfg.head_dim)
+        gu_q, gu_s = self._shard_gate_up(*_rand_int4(H, 2 * cfg.intermediate, gen, dev))
+        dn_q, dn_s = self._shard_rows(*_rand_int4(cfg.intermediate, H, gen, dev), sh.inter_local)
+        pre = "mtp.layers.0."
+
+        def nw():
+            return (1.0 + 0.02 * torch.randn(H, generator=gen, device=dev)).bfloat16()
+
+        self.mtp = MTPWeights(
+            enorm=nw(), hnorm=nw(), norm=nw(),
+            eh_proj=Int4Linear("mtp.eh_proj", eh_q, eh_s),
+            layer=LayerWeights(
+                input_norm=nw(), post_norm=nw(),
+                qkv=Int4Linear(pre + "self_attn.qkv_proj", qkv_q, qkv_s),
+                o=Int4Linear(pre + "self_attn.o_proj", o_q, o_s),
+                gate_up=Int4Linear(pre + "mlp.gate_up_proj", gu_q, gu_s),
+                down=Int4Linear(pre + "mlp.down_proj", dn_q, dn_s)),
+        )
+        return self
+
+    def mtp_forward(self, hidden: torch.Tensor, ids: torch.Tensor, inp: StepInputs, cache: torch.Tensor,
+                    ws=None) -> torch.Tensor:
+        """One MTP pass over ``T`` rows: ``hidden`` [T, H] (the target's, or the
+        previous draft's, final-normed state at position p) and ``ids`` [T] (the
+        token at p + 1). Writes the MTP KV at ``inp.slots``; returns the MTP's
+        final-normed hidden [T, H] (its next-token logits come from the lm_head)."""
+        cfg, M = self.cfg, self.mtp
+        T = ids.shape[0]
+        H = cfg.hidden
+        e = self.embed(ids)
+        cat = torch.empty((T, 2 * H), dtype=torch.bfloat16, device=self.device)
+        ops.rmsnorm(e, M.enorm, cfg.rms_eps, out=cat[:, :H])
+        ops.rmsnorm(hidden, M.hnorm, cfg.rms_eps, out=cat[:, H:])
+        splitk_ws = ws.splitk if ws is not None else None
+        x = M.eh_proj(cat, ws=splitk_ws)
+        x, residual = self._layer(M.layer, x, None, inp, cache, ws, defer=self.tp == 1)
+        return self._final_norm(x, residual, M.norm, None)
 
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
         """Local vocab shard logits ``[rows, V/tp]`` (bf16)."""

@@ -87,13 +87,18 @@ class LLMEngine:
         ops.require()
         self.model = DenseModel(model_cfg, tp=self.tp, rank=rank, device=self.device, comm=comm)
         self.model.random_init(seed=cfg.seed, layers=cfg.layers)
+        if cfg.speculative_tokens:
+            self.model.init_mtp(seed=cfg.seed)
         self.layout = self.model.layout
         self._alloc_cache()
         self.blocks = BlockManager(self.num_blocks, cfg.block_size, self.layout.page, cfg.enable_prefix_caching)
         width = 1 + cfg.speculative_tokens
+        spec = cfg.speculative_tokens > 0
         self.scheduler = Scheduler(self.blocks, cfg.max_num_seqs, cfg.max_num_batched_tokens, width,
-                                   cfg.max_model_len)
-        self.max_pages = (cfg.max_model_len + self.layout.page - 1) // self.layout.page + 1
+                                   cfg.max_model_len, lookahead=width if spec else 0,
+                                   mix_prefill_with_decode=not spec)
+        # a decoding sequence may write up to 2 * width slots past its length (verify + drafts)
+        self.max_pages = (cfg.max_model_len + 2 * width + self.layout.page - 1) // self.layout.page + 1
         self.max_q = max(1, width)
         self.max_tokens = max(cfg.max_num_batched_tokens, cfg.max_num_seqs * width)
         self.ws = Workspace(self.device, self.max_tokens, cfg.max_num_seqs, self.max_pages,
@@ -104,7 +109,7 @@ class LLMEngine:
         if cfg.speculative_tokens:
             from ..spec.mtp import MTPSpeculator
             self.mtp = MTPSpeculator(self, cfg.speculative_tokens, cfg.forced_accept_mean, cfg.seed)
-        if cfg.cuda_graphs:
+        if cfg.cuda_graphs and self.mtp is None:
             from .graphs import DecodeGraphs
             self.graphs = DecodeGraphs(self)
         # pinned host staging for the per-step copies
@@ -122,7 +127,8 @@ class LLMEngine:
     def _alloc_cache(self) -> None:
         cfg = self.cfg
         page_bytes = self.layout.page_bytes
-        n_layers = len(self.model.layers)
+        # the MTP draft layer keeps its own cache after the target's layers
+        n_layers = len(self.model.layers) + (1 if self.model.mtp is not None else 0)
         if cfg.num_kv_blocks is not None:
             blocks = int(cfg.num_kv_blocks)
         else:
@@ -233,6 +239,12 @@ class LLMEngine:
     def _plain_step(self, sched) -> list[Sequence]:
         if self.graphs is not None and sched.is_decode_only and self.graphs.can_run(sched):
             tokens = self.graphs.run(sched)
+        elif self.mtp is not None:
+            # speculative serving: the MTP layer catches up on every prefill row
+            inp, rows = self._build_inputs(sched)
+            hid_all = self.model.forward(inp, self.kv_caches, self.ws, all_rows=True)
+            tokens = self._sample(hid_all.index_select(0, inp.logit_rows)) if rows else np.zeros(0, np.int64)
+            self.mtp.after_prefill(sched, inp, hid_all, tokens)
         else:
             inp, rows = self._build_inputs(sched)
             hidden = self.model.forward(inp, self.kv_caches, self.ws)

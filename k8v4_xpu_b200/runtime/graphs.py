@@ -18,6 +18,85 @@ from .. import ops
 from ..models.dense import StepInputs
 
 
+def decode_inputs(ws, B: int, w: int, nsplit: int) -> StepInputs:
+    """StepInputs over the workspace's graph-stable buffers: B sequences x w tokens."""
+    T = B * w
+    return StepInputs(
+        input_ids=ws.input_ids[:T], positions=ws.positions[:T], slots=ws.slots[:T],
+        cu_q=ws.cu_q[: B + 1], seq_lens=ws.seq_lens[:B], block_table=ws.block_table[:B],
+        logit_rows=ws.logit_rows[:T], max_q_len=w, is_decode=True, nsplit=nsplit,
+    )
+
+
+def prepare_benign(eng, B: int, w: int) -> None:
+    """Capture-time metadata: every sequence one page long, no KV writes."""
+    ws = eng.ws
+    T = B * w
+    ws.cu_q[: B + 1].copy_(torch.arange(0, T + 1, w, dtype=torch.int32, device=eng.device))
+    ws.seq_lens[:B].fill_(w)
+    ws.block_table[:B].zero_()
+    ws.slots[:T].fill_(-1)  # capture must not write into live KV pages
+    ws.positions[:T].zero_()
+    ws.input_ids[:T].zero_()
+    ws.logit_rows[:T].copy_(torch.arange(T, device=eng.device))
+    ws.write_en[:B].zero_()
+    ws.forced_a[:B].zero_()
+
+
+def stage_decode_inputs(eng, sched, B: int, w: int, forced_a=None) -> None:
+    """Copy one decode step's metadata into the graph buffers.
+
+    Row i*w + j of the batch is token j of sequence i (its last token, then its
+    drafts). Padding sequences (B > real batch) repeat a one-page context with
+    every KV write dropped (slot -1, write_en 0).
+    """
+    ws = eng.ws
+    T = B * w
+    B_real = len(sched.chunks)
+    ids = np.zeros(T, np.int64)
+    pos = np.zeros(T, np.int64)
+    slots = np.full(T, -1, np.int64)
+    lens = np.zeros(B, np.int32)
+    tables = []
+    for i, c in enumerate(sched.chunks):
+        seq = c.seq
+        toks = [seq.tokens[-1]] + seq.draft
+        ids[i * w:(i + 1) * w] = toks[:w]
+        pos[i * w:(i + 1) * w] = np.arange(c.start, c.start + w)
+        for j in range(w):
+            slots[i * w + j] = eng.blocks.slot(seq.seq_id, c.start + j)
+        lens[i] = c.start + w
+        tables.append(eng.blocks.page_table(seq.seq_id))
+    for i in range(B_real, B):
+        lens[i] = w  # padding sequence: reads page 0, writes nothing
+        tables.append([0])
+    Wd = ws.block_table.shape[1]
+    n64 = 3 * T + 2 * B
+    pin64 = eng._pin_i64[:n64].numpy()
+    pin64[:T], pin64[T:2 * T], pin64[2 * T:3 * T] = ids, pos, slots
+    pin64[3 * T:3 * T + B] = [1 if i < B_real else 0 for i in range(B)]
+    pin64[3 * T + B:] = 0 if forced_a is None else np.concatenate([forced_a, np.zeros(B - len(forced_a), np.int64)])
+    n32 = (B + 1) + B + B * Wd
+    pin32 = eng._pin_i32[:n32].numpy()
+    pin32[: B + 1] = np.arange(0, T + 1, w)
+    pin32[B + 1: 2 * B + 1] = lens
+    bt = pin32[2 * B + 1:].reshape(B, Wd)
+    bt[:] = 0
+    for i, tb in enumerate(tables):
+        bt[i, :len(tb)] = tb
+    g64 = eng._pin_i64[:n64].to(eng.device, non_blocking=True)
+    g32 = eng._pin_i32[:n32].to(eng.device, non_blocking=True)
+    ws.input_ids[:T].copy_(g64[:T], non_blocking=True)
+    ws.positions[:T].copy_(g64[T:2 * T], non_blocking=True)
+    ws.slots[:T].copy_(g64[2 * T:3 * T], non_blocking=True)
+    ws.write_en[:B].copy_(g64[3 * T:3 * T + B], non_blocking=True)
+    ws.forced_a[:B].copy_(g64[3 * T + B:], non_blocking=True)
+    ws.cu_q[: B + 1].copy_(g32[: B + 1], non_blocking=True)
+    ws.seq_lens[:B].copy_(g32[B + 1: 2 * B + 1], non_blocking=True)
+    ws.block_table[:B].copy_(g32[2 * B + 1:].view(B, Wd), non_blocking=True)
+    eng.h2d_bytes += n64 * 8 + n32 * 4
+
+
 class DecodeGraphs:
     def __init__(self, engine, widths: tuple[int, ...] | None = None):
         self.engine = engine
@@ -35,15 +114,6 @@ class DecodeGraphs:
         widths = {c.num_tokens for c in sched.chunks}
         return len(widths) == 1 and next(iter(widths)) in (1, self.width) and B <= max(self.sizes)
 
-    def _inputs(self, B: int, w: int, nsplit: int) -> StepInputs:
-        ws = self.engine.ws
-        T = B * w
-        return StepInputs(
-            input_ids=ws.input_ids[:T], positions=ws.positions[:T], slots=ws.slots[:T],
-            cu_q=ws.cu_q[: B + 1], seq_lens=ws.seq_lens[:B], block_table=ws.block_table[:B],
-            logit_rows=ws.logit_rows[:T], max_q_len=w, is_decode=True, nsplit=nsplit,
-        )
-
     def capture(self, widths: tuple[int, ...] | None = None) -> None:
         eng = self.engine
         from .engine import decode_splits
@@ -53,16 +123,8 @@ class DecodeGraphs:
         for w in widths:
             for B in self.sizes:
                 nsplit = decode_splits(eng.max_pages, B, eng.layout.hkv)
-                T = B * w
-                # benign metadata: every sequence one page long
-                ws.cu_q[: B + 1].copy_(torch.arange(0, T + 1, w, dtype=torch.int32, device=eng.device))
-                ws.seq_lens[:B].fill_(w)
-                ws.block_table[:B].zero_()
-                ws.slots[:T].fill_(-1)  # capture must not write into live KV pages
-                ws.positions[:T].zero_()
-                ws.input_ids[:T].zero_()
-                ws.logit_rows[:T].copy_(torch.arange(T, device=eng.device))
-                inp = self._inputs(B, w, nsplit)
+                prepare_benign(eng, B, w)
+                inp = decode_inputs(ws, B, w, nsplit)
                 stream.wait_stream(torch.cuda.current_stream(eng.device))
                 with torch.cuda.stream(stream):
                     for _ in range(2):  # warm-up (kernel attributes, allocator)
@@ -95,43 +157,7 @@ class DecodeGraphs:
         w = sched.chunks[0].num_tokens
         B = next(s for s in self.sizes if s >= B_real)
         g, out, _nsplit = self.graphs[(B, w)]
-        T = B * w
-        ws = eng.ws
-        # host metadata (padding rows repeat sequence 0 with a dropped write)
-        ids = np.zeros(T, np.int64)
-        pos = np.zeros(T, np.int64)
-        slots = np.full(T, -1, np.int64)
-        lens = np.zeros(B, np.int32)
-        tables = []
-        for i, c in enumerate(sched.chunks):
-            seq = c.seq
-            toks = [seq.tokens[-1]] + seq.draft
-            ids[i * w:(i + 1) * w] = toks[:w]
-            pos[i * w:(i + 1) * w] = np.arange(c.start, c.start + w)
-            for j in range(w):
-                slots[i * w + j] = eng.blocks.slot(seq.seq_id, c.start + j)
-            lens[i] = c.start + w
-            tables.append(eng.blocks.page_table(seq.seq_id))
-        for i in range(B_real, B):
-            lens[i] = w  # padding sequence: reads page 0, writes nothing
-            tables.append([0])
-        Wd = ws.block_table.shape[1]
-        pin64 = eng._pin_i64[: 3 * T].numpy()
-        pin64[:T], pin64[T:2 * T], pin64[2 * T:] = ids, pos, slots
-        pin32 = eng._pin_i32[: B + B * Wd].numpy()
-        pin32[:B] = lens
-        bt = pin32[B:].reshape(B, Wd)
-        bt[:] = 0
-        for i, tb in enumerate(tables):
-            bt[i, :len(tb)] = tb
-        g64 = eng._pin_i64[: 3 * T].to(eng.device, non_blocking=True)
-        g32 = eng._pin_i32[: B + B * Wd].to(eng.device, non_blocking=True)
-        ws.input_ids[:T].copy_(g64[:T], non_blocking=True)
-        ws.positions[:T].copy_(g64[T:2 * T], non_blocking=True)
-        ws.slots[:T].copy_(g64[2 * T:], non_blocking=True)
-        ws.seq_lens[:B].copy_(g32[:B], non_blocking=True)
-        ws.block_table[:B].copy_(g32[B:].view(B, Wd), non_blocking=True)
-        eng.h2d_bytes += 3 * T * 8 + (B + B * Wd) * 4
+        stage_decode_inputs(eng, sched, B, w)
         g.replay()
         n = B_real * w
         host = eng._pin_out[:n]

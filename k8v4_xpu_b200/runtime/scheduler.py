@@ -85,7 +85,8 @@ class SchedulerOutput:
 
 class Scheduler:
     def __init__(self, blocks: BlockManager, max_num_seqs: int = 4, max_num_batched_tokens: int = 4224,
-                 decode_width: int = 1, max_model_len: int = 262144):
+                 decode_width: int = 1, max_model_len: int = 262144, lookahead: int = 0,
+                 mix_prefill_with_decode: bool = True):
         if max_num_batched_tokens < 1 or max_num_seqs < 1:
             raise ValueError("scheduler limits must be positive")
         self.blocks = blocks
@@ -93,6 +94,12 @@ class Scheduler:
         self.max_num_batched_tokens = max_num_batched_tokens
         self.decode_width = decode_width  # tokens per decoding sequence per step (1 + MTP drafts)
         self.max_model_len = max_model_len
+        # KV slots a decoding sequence may write past its verify window (MTP drafts)
+        self.lookahead = lookahead
+        # False: a step is either all decode or all prefill, alternating when both
+        # are pending (the speculative step is one graph over decode rows only)
+        self.mix = mix_prefill_with_decode
+        self._turn = 0
         self.waiting: collections.deque[Sequence] = collections.deque()
         self.running: list[Sequence] = []
         self._ids = itertools.count()
@@ -126,21 +133,31 @@ class Scheduler:
         budget = self.max_num_batched_tokens
         chunks: list[ScheduledChunk] = []
         preempted: list[Sequence] = []
+        do_decode = do_prefill = True
+        if not self.mix:
+            decoding = any(not s.in_prefill for s in self.running)
+            prefilling = any(s.in_prefill for s in self.running) or (
+                bool(self.waiting) and len(self.running) < self.max_num_seqs)
+            if decoding and prefilling:
+                self._turn ^= 1
+                do_decode, do_prefill = self._turn == 1, self._turn == 0
         # 1) decode tokens of generating sequences
-        for seq in list(self.running):
+        for seq in list(self.running) if do_decode else []:
             if seq.in_prefill:
                 continue
             width = 1 + len(seq.draft)
             if width > budget:
                 continue
             try:
-                self.blocks.ensure(seq.seq_id, seq.computed + width)
+                self.blocks.ensure(seq.seq_id, seq.computed + width + self.lookahead)
             except CapacityError:
                 self._preempt(seq)
                 preempted.append(seq)
                 continue
             chunks.append(ScheduledChunk(seq, seq.computed, width, False, True))
             budget -= width
+        if not do_prefill:
+            return SchedulerOutput(chunks, sum(c.num_tokens for c in chunks), bool(chunks), preempted)
         # 2) prefill chunks of admitted sequences, then admit new ones
         for seq in self.running:
             if budget <= 0:

@@ -36,6 +36,10 @@ class Workspace:
         self.block_table = torch.zeros((max_seqs, self.max_pages), dtype=torch.int32, device=self.device)
         self.logit_rows = torch.zeros(max_tokens, dtype=torch.int64, device=self.device)
         self.q_ends = torch.zeros(max_tokens, dtype=torch.int32, device=self.device)
+        # MTP step inputs: per-sequence KV-write enable (0 for padding rows) and
+        # the forced accepted-draft count of the benchmark acceptance mode
+        self.write_en = torch.zeros(max_seqs, dtype=torch.int64, device=self.device)
+        self.forced_a = torch.zeros(max_seqs, dtype=torch.int64, device=self.device)
 
     def splitk_view(self, rows: int, n: int) -> torch.Tensor:
         if rows * n > self.splitk.numel():

@@ -239,6 +239,21 @@ def test_rmsnorm_and_quant():
     assert (q.cpu().int() - q_ref.int()).abs().max().item() <= 1
 
 
+def test_rmsnorm_into_strided_halves():
+    """Two norms writing the halves of one concatenated row (the MTP input)."""
+    T, n = 7, 512
+    a = torch.randn(T, n, generator=_gen(24)).bfloat16().to(DEV)
+    b = torch.randn(T, n, generator=_gen(25)).bfloat16().to(DEV)
+    wa = (1 + 0.1 * torch.randn(n, generator=_gen(26))).bfloat16().to(DEV)
+    wb = (1 + 0.1 * torch.randn(n, generator=_gen(27))).bfloat16().to(DEV)
+    cat = torch.full((T, 2 * n), float("nan"), dtype=torch.bfloat16, device=DEV)
+    ops.rmsnorm(a, wa, 1e-6, out=cat[:, :n])
+    ops.rmsnorm(b, wb, 1e-6, out=cat[:, n:])
+    torch.cuda.synchronize()
+    assert torch.equal(cat[:, :n], ops.rmsnorm(a, wa, 1e-6))
+    assert torch.equal(cat[:, n:], ops.rmsnorm(b, wb, 1e-6))
+
+
 def test_silu_mul_and_quant():
     T, inter = 5, 2048
     gu = torch.randn(T, 2 * inter, generator=_gen(23)).bfloat16()
