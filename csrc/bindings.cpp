@@ -37,8 +37,8 @@ int k8v4_quant_rows(const void* x, void* q, float* scale, int rows, int n, cudaS
 int k8v4_embed_int8(const int64_t* ids, const void* codes, const void* scales, void* out, int T, int n,
                     int64_t start, int64_t rows, cudaStream_t st);
 int k8v4_splitk_finish(float* ws, const void* residual, void* out, int64_t total, int zero_ws, cudaStream_t st);
-int k8v4_argmax(const void* logits, int rows, int vocab, int64_t offset, float* best_val, int64_t* best_idx,
-                cudaStream_t st);
+int k8v4_argmax(const void* logits, int rows, int vocab, int64_t ld, int64_t offset, float* best_val,
+                int64_t* best_idx, cudaStream_t st);
 int k8v4_status_gemm(int clear);
 int k8v4_status_store(int clear);
 int k8v4_status_misc(int clear);
@@ -338,15 +338,16 @@ void embed_int8(const at::Tensor& ids, const at::Tensor& codes, const at::Tensor
 }
 
 void argmax(const at::Tensor& logits, int64_t offset, at::Tensor& best_val, at::Tensor& best_idx) {
-  check_contig(logits, "logits");
+  check_cuda(logits, "logits");
   check_contig(best_val, "best_val");
   check_contig(best_idx, "best_idx");
   TORCH_CHECK(logits.scalar_type() == at::kBFloat16 && logits.dim() == 2, "logits bf16 [rows, vocab]");
+  TORCH_CHECK(logits.stride(1) == 1 && logits.stride(0) >= logits.size(1), "logits rows must be unit-stride");
   TORCH_CHECK(best_val.scalar_type() == at::kFloat && best_idx.scalar_type() == at::kLong &&
                   best_val.numel() == logits.size(0) && best_idx.numel() == logits.size(0),
               "outputs");
   c10::cuda::CUDAGuard g(logits.device());
-  check_rc(k8v4_argmax(logits.data_ptr(), (int)logits.size(0), (int)logits.size(1), offset,
+  check_rc(k8v4_argmax(logits.data_ptr(), (int)logits.size(0), (int)logits.size(1), logits.stride(0), offset,
                        best_val.data_ptr<float>(), best_idx.data_ptr<int64_t>(), cur_stream()),
            "argmax");
 }

@@ -7,16 +7,19 @@
 namespace k8v4 {
 namespace sampler {
 
-__global__ void __launch_bounds__(1024) argmax_kernel(const __nv_bfloat16* __restrict__ logits, int vocab,
+// Row r of the logits starts at logits + r * ld (ld >= vocab: a lm_head shard
+// padded to the GEMM's 128-row tile is read only over its real columns).
+__global__ void __launch_bounds__(1024) argmax_kernel(const __nv_bfloat16* __restrict__ logits, int vocab, int64_t ld,
                                                       int64_t offset, float* best_val, int64_t* best_idx) {
   __shared__ float sv[32];
   __shared__ int si[32];
   const int64_t row = blockIdx.x;
-  const __nv_bfloat16* x = logits + row * vocab;
+  const __nv_bfloat16* x = logits + row * ld;
+  const bool vec = (ld & 7) == 0 && (reinterpret_cast<uintptr_t>(logits) & 15) == 0;
   float bv = -INFINITY;
   int bi = 0x7fffffff;
   for (int c = threadIdx.x * 8; c < vocab; c += blockDim.x * 8) {
-    if (c + 8 <= vocab && (vocab & 7) == 0) {
+    if (c + 8 <= vocab && vec) {
       const uint4 raw = *reinterpret_cast<const uint4*>(x + c);
       const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw);
 #pragma unroll
@@ -63,10 +66,11 @@ using namespace k8v4;
 
 K8V4_STATUS_API(sampler)
 
-extern "C" int k8v4_argmax(const void* logits, int rows, int vocab, int64_t offset, float* best_val,
+extern "C" int k8v4_argmax(const void* logits, int rows, int vocab, int64_t ld, int64_t offset, float* best_val,
                            int64_t* best_idx, cudaStream_t st) {
   if (rows <= 0) return 0;
-  sampler::argmax_kernel<<<rows, 1024, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(logits), vocab, offset,
+  if (ld < vocab) return 2;
+  sampler::argmax_kernel<<<rows, 1024, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(logits), vocab, ld, offset,
                                                  best_val, best_idx);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }

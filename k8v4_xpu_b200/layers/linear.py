@@ -83,13 +83,24 @@ class Int4Linear:
 
 
 class Int8RowLinear:
-    """Per-row INT8 weights ``[N, K]`` + fp16 scales ``[N]`` (the lm_head)."""
+    """Per-row INT8 weights ``[N, K]`` + fp16 scales ``[N]`` (the lm_head).
+
+    The GEMM tiles output features by 128, so the rows are zero-padded to a
+    multiple of 128 (a vocab shard under TP, e.g. 151936 / 2 = 75968, is not);
+    the call returns a view over the real rows.
+    """
 
     def __init__(self, name: str, weight: torch.Tensor, scale: torch.Tensor):
         self.name = name
-        self.weight = weight
-        self.scale = scale.reshape(-1)
-        self.out_features, self.in_features = weight.shape
+        n, k = weight.shape
+        pad = (-n) % 128
+        if pad:
+            weight = torch.cat([weight, weight.new_zeros(pad, k)])
+            scale = torch.cat([scale.reshape(-1), scale.new_zeros(pad)])
+        self.weight = weight.contiguous()
+        self.scale = scale.reshape(-1).contiguous()
+        self.out_features, self.in_features = n, k
 
     def __call__(self, xq: torch.Tensor, xs: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-        return ops.wq_gemm(ops.W8A8, self.weight, self.scale, xq, xscale=xs, out=out)
+        y = ops.wq_gemm(ops.W8A8, self.weight, self.scale, xq, xscale=xs, out=out)
+        return y if y.shape[1] == self.out_features else y[:, : self.out_features]
