@@ -31,7 +31,12 @@ int k8v4_wq_gemm(int mode, const void* w, const void* wscale, const void* x, con
                  const void* residual, void* out, float* ws, int M, int N, int K, int ldo, int split,
                  cudaStream_t st);
 int k8v4_rmsnorm(const void* x, float* xf, void* residual, const void* w, void* y, int64_t ldy, void* yq,
-                 float* yscale, int rows, int n, float eps, cudaStream_t st);
+                 float* yscale, int rows, int n, float eps, const unsigned long long* sync_flag,
+                 unsigned long long* sync_state, unsigned long long sync_expected, cudaStream_t st);
+int k8v4_wq_gemm_allreduce(int mode, const void* w, const void* wscale, const void* x, const float* xscale,
+                           float* ws_mc, unsigned long long* flag_mc, int M, int N, int K, int ldo, int split,
+                           cudaStream_t st);
+int k8v4_wq_gemm_ctas(int mode, int M, int N, int K, int split);
 int k8v4_silu_mul(const void* gu, void* y, void* yq, float* yscale, int rows, int inter, cudaStream_t st);
 int k8v4_quant_rows(const void* x, void* q, float* scale, int rows, int n, cudaStream_t st);
 int k8v4_embed_int8(const int64_t* ids, const void* codes, const void* scales, void* out, int T, int n,
@@ -241,7 +246,8 @@ void wq_gemm(int64_t mode, const at::Tensor& w, const at::Tensor& wscale, const 
 // -------------------------------------------------------------- fused misc
 void rmsnorm(at::Tensor& x, const c10::optional<at::Tensor>& residual, const at::Tensor& w,
              const c10::optional<at::Tensor>& y, const c10::optional<at::Tensor>& yq,
-             const c10::optional<at::Tensor>& yscale, double eps) {
+             const c10::optional<at::Tensor>& yscale, double eps, const c10::optional<at::Tensor>& sync_flag,
+             const c10::optional<at::Tensor>& sync_state, int64_t sync_expected) {
   check_contig(x, "x");
   check_contig(w, "weight");
   TORCH_CHECK((x.scalar_type() == at::kBFloat16 || x.scalar_type() == at::kFloat) && w.scalar_type() == at::kBFloat16,
@@ -278,8 +284,21 @@ void rmsnorm(at::Tensor& x, const c10::optional<at::Tensor>& residual, const at:
     sp = yscale->data_ptr<float>();
   }
   c10::cuda::CUDAGuard g(x.device());
+  const unsigned long long* sf = nullptr;
+  unsigned long long* ss = nullptr;
+  if (sync_flag.has_value()) {
+    // x is this rank's copy of a GEMM -> all-reduce buffer: wait for every rank's signals
+    TORCH_CHECK(f32, "an all-reduce consumer reads fp32 sums");
+    TORCH_CHECK(sync_state.has_value() && sync_state->scalar_type() == at::kLong && sync_state->numel() >= 2 &&
+                    sync_state->is_contiguous(),
+                "sync_state: int64 [2]");
+    TORCH_CHECK(sync_flag->scalar_type() == at::kLong && sync_flag->numel() >= 1, "sync_flag: int64 counter");
+    sf = reinterpret_cast<const unsigned long long*>(sync_flag->data_ptr());
+    ss = reinterpret_cast<unsigned long long*>(sync_state->data_ptr());
+  }
   check_rc(k8v4_rmsnorm(f32 ? nullptr : x.data_ptr(), f32 ? x.data_ptr<float>() : nullptr, r, w.data_ptr(), yp, ldy,
-                        qp, sp, (int)rows, (int)n, (float)eps, cur_stream()),
+                        qp, sp, (int)rows, (int)n, (float)eps, sf, ss, (unsigned long long)sync_expected,
+                        cur_stream()),
            "rmsnorm");
 }
 
@@ -352,6 +371,40 @@ void argmax(const at::Tensor& logits, int64_t offset, at::Tensor& best_val, at::
            "argmax");
 }
 
+// GEMM -> all-reduce: `ws` is this rank's copy of a symmetric fp32 [M, N]
+// buffer, `ws_mc` / `flag_mc` the multicast addresses of that buffer and of
+// the completion counter (from the symmetric-memory rendezvous).
+void wq_gemm_allreduce(int64_t mode, const at::Tensor& w, const at::Tensor& wscale, const at::Tensor& x,
+                       const c10::optional<at::Tensor>& xscale, at::Tensor& ws, int64_t ws_mc, int64_t flag_mc,
+                       int64_t split) {
+  check_contig(w, "weight");
+  check_contig(wscale, "weight scale");
+  check_contig(x, "x");
+  check_contig(ws, "ws");
+  TORCH_CHECK(mode == 0 || mode == 1, "all-reduce GEMMs are W4A16 or W4A8");
+  TORCH_CHECK(x.dim() == 2 && w.scalar_type() == at::kInt && w.size(0) * 8 == x.size(1), "W4 qweight [K/8, N]");
+  const int64_t M = x.size(0), K = x.size(1), N = w.size(1);
+  TORCH_CHECK(ws.scalar_type() == at::kFloat && ws.dim() == 2 && ws.size(0) == M && ws.size(1) == N, "ws fp32 [M, N]");
+  TORCH_CHECK(ws_mc != 0 && flag_mc != 0 && ws_mc % 16 == 0 && flag_mc % 8 == 0, "multicast addresses");
+  if (mode == 0) {
+    TORCH_CHECK(x.scalar_type() == at::kBFloat16, "W4A16 takes bf16 activations");
+  } else {
+    TORCH_CHECK(x.scalar_type() == at::kChar && xscale.has_value() && xscale->numel() == M &&
+                    xscale->scalar_type() == at::kFloat,
+                "W4A8 takes int8 activations + fp32 scales");
+  }
+  c10::cuda::CUDAGuard g(x.device());
+  check_rc(k8v4_wq_gemm_allreduce((int)mode, w.data_ptr(), wscale.data_ptr(), x.data_ptr(),
+                                  mode == 0 ? nullptr : xscale->data_ptr<float>(), reinterpret_cast<float*>(ws_mc),
+                                  reinterpret_cast<unsigned long long*>(flag_mc), (int)M, (int)N, (int)K, (int)N,
+                                  (int)split, cur_stream()),
+           "wq_gemm_allreduce");
+}
+
+int64_t wq_gemm_ctas(int64_t mode, int64_t M, int64_t N, int64_t K, int64_t split) {
+  return k8v4_wq_gemm_ctas((int)mode, (int)M, (int)N, (int)K, (int)split);
+}
+
 // Read (and optionally clear) the device status words of every kernel unit.
 int64_t status(bool clear) {
   int v = 0;
@@ -383,7 +436,11 @@ TORCH_LIBRARY(k8v4, m) {
       "Tensor(b!)? ws, int split, bool finish=True) -> ()");
   m.def(
       "rmsnorm(Tensor(e!) x, Tensor(a!)? residual, Tensor w, Tensor(b!)? y, Tensor(c!)? yq, Tensor(d!)? yscale, "
-      "float eps) -> ()");
+      "float eps, Tensor? sync_flag=None, Tensor(f!)? sync_state=None, int sync_expected=0) -> ()");
+  m.def(
+      "wq_gemm_allreduce(int mode, Tensor w, Tensor wscale, Tensor x, Tensor? xscale, Tensor(a!) ws, int ws_mc, "
+      "int flag_mc, int split) -> ()");
+  m.def("wq_gemm_ctas(int mode, int M, int N, int K, int split) -> int");
   m.def("silu_mul(Tensor gate_up, Tensor(a!)? y, Tensor(b!)? yq, Tensor(c!)? yscale) -> ()");
   m.def("quant_rows(Tensor x, Tensor(a!) q, Tensor(b!) scale) -> ()");
   m.def("embed_int8(Tensor ids, Tensor codes, Tensor scales, Tensor(a!) out, int start) -> ()");
@@ -397,6 +454,7 @@ TORCH_LIBRARY_IMPL(k8v4, CUDA, m) {
   m.impl("decode_attn", &decode_attn);
   m.impl("prefill_attn", &prefill_attn);
   m.impl("wq_gemm", &wq_gemm);
+  m.impl("wq_gemm_allreduce", &wq_gemm_allreduce);
   m.impl("rmsnorm", &rmsnorm);
   m.impl("silu_mul", &silu_mul);
   m.impl("quant_rows", &quant_rows);
@@ -406,5 +464,6 @@ TORCH_LIBRARY_IMPL(k8v4, CUDA, m) {
 
 TORCH_LIBRARY_IMPL(k8v4, CompositeExplicitAutograd, m) {
   m.impl("decode_ws_floats", &decode_ws_floats);
+  m.impl("wq_gemm_ctas", &wq_gemm_ctas);
   m.impl("status", &status);
 }

@@ -24,7 +24,17 @@
 //
 // Split-K: gridDim.z slices K; with more than one slice the CTA adds fp32
 // partial sums into `ws` with red.global.add and a finishing kernel converts.
+//
+// GEMM -> all-reduce (tensor parallel row-parallel projections): with
+// `ws_mc` set, the partial sums go to the multicast address of a symmetric
+// fp32 buffer instead (multimem.red: the NVSwitch adds them into every
+// rank's copy), and each CTA then adds 1 to the multicast counter `flag_mc`
+// with release semantics. The consumer (the fused RMSNorm) waits until its
+// local copy of the counter shows every rank's CTAs, then reads the reduced
+// sums from its own copy: the reduction and its broadcast happen inside the
+// GEMM's epilogue, overlapped with the other tiles' MMAs.
 #include "../tc.cuh"
+#include "../comm/peer.cuh"
 
 namespace k8v4 {
 namespace gemm {
@@ -40,6 +50,8 @@ struct Params {
   const __nv_bfloat16* residual;  // optional [M, ldo]
   __nv_bfloat16* out;          // [M, ldo] (split == 1)
   float* ws;                   // [M, ldo] fp32 accumulation (split > 1)
+  float* ws_mc;                // multicast alias of a symmetric [M, ldo] fp32 buffer (GEMM -> all-reduce)
+  unsigned long long* flag_mc; // multicast alias of the counter each CTA signals when its sums are out
   int M, N, K, ldo;
   int k_per_split;             // multiple of 128
 };
@@ -442,7 +454,9 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
           float v = acc[i] * rs;
           if (MODE != W4A16) v *= p.xscale[t];
           const size_t o = (size_t)t * p.ldo + n;
-          if (gridDim.z > 1) {
+          if (p.ws_mc) {
+            peer::mc_red_add_f32(p.ws_mc + o, v);
+          } else if (gridDim.z > 1) {
             atomicAdd(p.ws + o, v);
           } else {
             if (p.residual) v += __bfloat162float(p.residual[o]);
@@ -458,6 +472,13 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+  if (p.flag_mc && threadIdx.x == 0) {
+    // the CTA's multicast adds (ordered before this point by the barrier) are
+    // out: publish them to every rank
+    peer::fence_proxy_alias();
+    peer::fence_sys();
+    peer::mc_signal_add_u64(p.flag_mc, 1ull);
   }
 }
 
@@ -553,13 +574,22 @@ extern "C" int k8v4_gemm_trace(uint64_t* host, int clear) {
 
 // Tokens per CTA for a given M: small M streams weights (decode), large M
 // reuses each converted weight tile over 128 tokens (prefill).
-extern "C" int k8v4_wq_gemm(int mode, const void* w, const void* wscale, const void* x, const float* xscale,
-                            const void* residual, void* out, float* ws, int M, int N, int K, int ldo, int split,
-                            cudaStream_t st) {
-  if (N % 128 || K % 128 || M <= 0) return 1;
-  if (split < 1) split = 1;
+static int pick_bt(int mode, int M) {
+  if (mode == W4A16) return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
+  return M <= 32 ? 32 : 128;
+}
+
+static int k_per_split_for(int K, int split) {
   const int kgroups = K / 128;
+  if (split < 1) split = 1;
   if (split > kgroups) split = kgroups;
+  return cdiv(kgroups, split) * 128;
+}
+
+static int gemm_impl(int mode, const void* w, const void* wscale, const void* x, const float* xscale,
+                     const void* residual, void* out, float* ws, float* ws_mc, unsigned long long* flag_mc, int M,
+                     int N, int K, int ldo, int split, cudaStream_t st) {
+  if (N % 128 || K % 128 || M <= 0) return 1;
   Params p;
   p.qweight = reinterpret_cast<const int32_t*>(w);
   p.wscale = reinterpret_cast<const __half*>(wscale);
@@ -567,26 +597,53 @@ extern "C" int k8v4_wq_gemm(int mode, const void* w, const void* wscale, const v
   p.residual = reinterpret_cast<const __nv_bfloat16*>(residual);
   p.out = reinterpret_cast<__nv_bfloat16*>(out);
   p.ws = ws;
+  p.ws_mc = ws_mc;
+  p.flag_mc = flag_mc;
   p.M = M;
   p.N = N;
   p.K = K;
   p.ldo = ldo;
-  p.k_per_split = cdiv(kgroups, split) * 128;
+  p.k_per_split = k_per_split_for(K, split);
   split = cdiv(K, p.k_per_split);
-  if (split > 1 && !ws) return 2;
+  if (split > 1 && !ws && !ws_mc) return 2;
+  const int bt = pick_bt(mode, M);
   if (mode == W4A16) {
-    if (M <= 16) return launch_cfg<W4A16, 16, 8, 4, 4, 16, 16>(w, x, p, split, st);
-    if (M <= 32) return launch_cfg<W4A16, 32, 8, 4, 4, 12, 16>(w, x, p, split, st);
-    if (M <= 64) return launch_cfg<W4A16, 64, 8, 4, 4, 8, 8>(w, x, p, split, st);
+    if (bt == 16) return launch_cfg<W4A16, 16, 8, 4, 4, 16, 16>(w, x, p, split, st);
+    if (bt == 32) return launch_cfg<W4A16, 32, 8, 4, 4, 12, 16>(w, x, p, split, st);
+    if (bt == 64) return launch_cfg<W4A16, 64, 8, 4, 4, 8, 8>(w, x, p, split, st);
     return launch_cfg<W4A16, 128, 4, 8, 4, 8, 4>(w, x, p, split, st);
   }
   if (mode == W4A8) {
-    if (M <= 32) return launch_cfg<W4A8, 32, 8, 4, 4, 8, 12>(w, x, p, split, st);
+    if (bt == 32) return launch_cfg<W4A8, 32, 8, 4, 4, 8, 12>(w, x, p, split, st);
     return launch_cfg<W4A8, 128, 4, 8, 4, 4, 4>(w, x, p, split, st);
   }
   if (mode == W8A8) {
-    if (M <= 32) return launch_cfg<W8A8, 32, 4, 4, 6, 1, 6>(w, x, p, split, st);
+    if (bt == 32) return launch_cfg<W8A8, 32, 4, 4, 6, 1, 6>(w, x, p, split, st);
     return launch_cfg<W8A8, 128, 4, 8, 4, 1, 4>(w, x, p, split, st);
   }
   return 3;
+}
+
+extern "C" int k8v4_wq_gemm(int mode, const void* w, const void* wscale, const void* x, const float* xscale,
+                            const void* residual, void* out, float* ws, int M, int N, int K, int ldo, int split,
+                            cudaStream_t st) {
+  return gemm_impl(mode, w, wscale, x, xscale, residual, out, ws, nullptr, nullptr, M, N, K, ldo, split, st);
+}
+
+// GEMM -> all-reduce: fp32 sums into every rank's copy of a symmetric buffer
+// through its multicast address `ws_mc`, then one signal per CTA on the
+// multicast counter `flag_mc`. The consumer expects world x
+// k8v4_wq_gemm_ctas(...) signals for one call.
+extern "C" int k8v4_wq_gemm_allreduce(int mode, const void* w, const void* wscale, const void* x, const float* xscale,
+                                      float* ws_mc, unsigned long long* flag_mc, int M, int N, int K, int ldo,
+                                      int split, cudaStream_t st) {
+  if (!ws_mc || !flag_mc) return 4;
+  return gemm_impl(mode, w, wscale, x, xscale, nullptr, nullptr, nullptr, ws_mc, flag_mc, M, N, K, ldo, split, st);
+}
+
+// CTAs one call launches (the number of signals it sends per rank).
+extern "C" int k8v4_wq_gemm_ctas(int mode, int M, int N, int K, int split) {
+  if (N % 128 || K % 128 || M <= 0) return 0;
+  const int kps = k_per_split_for(K, split);
+  return (N / 128) * cdiv(M, pick_bt(mode, M)) * cdiv(K, kps);
 }

@@ -9,6 +9,7 @@
 //   * per-token int8 quantization of bf16 rows
 // One CTA per token row; 16-byte vector loads; fp32 math.
 #include "../common.cuh"
+#include "../comm/peer.cuh"
 
 namespace k8v4 {
 namespace misc {
@@ -84,6 +85,36 @@ __device__ __forceinline__ void quant_row(const float (&v)[VPT][8], int n, int8_
   if (threadIdx.x == 0) *scale = s;
 }
 
+// Completion tracking of a GEMM -> all-reduce consumed by one kernel launch.
+struct ReduceSync {
+  const unsigned long long* flag;  // this rank's copy of the multicast counter
+  unsigned long long* state;       // [0] signals consumed so far, [1] CTAs of this launch done
+  unsigned long long expected;     // signals one producer call sends (world x its CTAs)
+};
+
+__device__ __forceinline__ void sync_wait(const ReduceSync& s) {
+  if (threadIdx.x == 0) {
+    const unsigned long long target = *reinterpret_cast<volatile unsigned long long*>(s.state) + s.expected;
+    peer::wait_geq_u64(s.flag, target, 201);
+  }
+  __syncthreads();
+  peer::fence_proxy_alias();  // the sums arrived through the multicast alias
+}
+
+__device__ __forceinline__ void sync_done(const ReduceSync& s) {
+  peer::fence_proxy_alias();  // the zeroing stores precede later multicast adds
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned long long prev = atomicAdd(s.state + 1, 1ull);
+    if (prev == gridDim.x - 1) {
+      s.state[1] = 0;
+      s.state[0] += s.expected;
+      __threadfence();
+    }
+  }
+}
+
 // x: [T, n] bf16. If residual != nullptr: h = x + residual, residual <- h.
 // y = h * rsqrt(mean(h^2) + eps) * w. Outputs bf16 y (row stride ldy, so two
 // norms can write the halves of one concatenated row) and/or int8 y + scale.
@@ -91,12 +122,20 @@ template <int VPT>
 // x may instead arrive as fp32 split-K partial sums `xf` (the finishing step
 // of a split-K GEMM fused into this norm); xf is zeroed after it is read so
 // the shared accumulator is clean for the next split-K GEMM.
+//
+// Tensor parallel: xf may be this rank's copy of a symmetric buffer that a
+// GEMM -> all-reduce fills through its multicast address. Then `sync` is
+// given: the CTAs first wait until the counter `sync.flag` reaches
+// sync.state[0] + sync.expected (all ranks' GEMM CTAs have signalled), and the
+// last CTA to finish advances sync.state[0] by `expected` (a running count, so
+// a replayed CUDA graph needs no reset and calls may differ in size).
 __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, float* xf,
                                                            __nv_bfloat16* residual, const __nv_bfloat16* __restrict__ w,
                                                            __nv_bfloat16* y, int8_t* yq, float* yscale, int n,
-                                                           int64_t ldy, float eps) {
+                                                           int64_t ldy, float eps, ReduceSync sync) {
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
+  if (sync.flag) sync_wait(sync);
   float v[VPT][8];
   float ss = 0.f;
 #pragma unroll
@@ -143,6 +182,7 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const __nv_bfloat16* 
     }
   }
   if (yq) quant_row<VPT>(v, n, yq + row * n, yscale + row, red);
+  if (sync.flag) sync_done(sync);
 }
 
 // gu: [T, 2I] = [gate | up]. out = silu(gate) * up (bf16 and/or int8 + scale).
@@ -266,12 +306,15 @@ K8V4_STATUS_API(misc)
   } while (0)
 
 extern "C" int k8v4_rmsnorm(const void* x, float* xf, void* residual, const void* w, void* y, int64_t ldy, void* yq,
-                            float* yscale, int rows, int n, float eps, cudaStream_t st) {
+                            float* yscale, int rows, int n, float eps, const unsigned long long* sync_flag,
+                            unsigned long long* sync_state, unsigned long long sync_expected, cudaStream_t st) {
   if (rows <= 0) return 0;
   if (n % 8 || ldy < n || ldy % 8) return 1;
+  if (sync_flag && (!xf || !sync_state)) return 4;
+  ReduceSync sync{sync_flag, sync_state, sync_expected};
   K8V4_VPT_DISPATCH(n, rmsnorm_kernel, reinterpret_cast<const __nv_bfloat16*>(x), xf,
                     reinterpret_cast<__nv_bfloat16*>(residual), reinterpret_cast<const __nv_bfloat16*>(w),
-                    reinterpret_cast<__nv_bfloat16*>(y), reinterpret_cast<int8_t*>(yq), yscale, n, ldy, eps);
+                    reinterpret_cast<__nv_bfloat16*>(y), reinterpret_cast<int8_t*>(yq), yscale, n, ldy, eps, sync);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 

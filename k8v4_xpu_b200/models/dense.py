@@ -101,6 +101,7 @@ class DenseModel:
         self.rope = None
         self.w4a8 = w4a8_enabled()
         self.mtp = None
+        self.fused_ar = None  # parallel.fused_ar.FusedAllReduce when TP runs the fused path
 
     # ------------------------------------------------------------- weights
     def random_init(self, seed: int = 0, layers: int | None = None) -> "DenseModel":
@@ -186,20 +187,23 @@ class DenseModel:
         return self._all_reduce(x)
 
     def _layer(self, L: LayerWeights, x: torch.Tensor, residual: torch.Tensor | None, inp: StepInputs,
-               cache: torch.Tensor, ws, defer: bool) -> tuple[torch.Tensor, torch.Tensor]:
-        """One decoder layer. ``x`` may be fp32 split-K partials left by the
-        previous layer (finished inside the fused norm). Returns (x, residual)."""
+               cache: torch.Tensor, ws, defer: bool, sync=None):
+        """One decoder layer. ``x`` may be fp32 sums left by the previous
+        layer's GEMM (split-K partials, or this rank's copy of a fused
+        all-reduce, then ``sync`` says when they are complete); they are
+        finished inside the input norm. Returns (x, residual, sync)."""
         cfg, sh = self.cfg, self.shape
         T = inp.input_ids.shape[0]
         D = cfg.head_dim
         hq, hkv = sh.hq_local, sh.hkv_local
         splitk_ws = ws.splitk if ws is not None else None
+        far = self.fused_ar if (self.fused_ar is not None and self.fused_ar.fits(T, cfg.hidden)) else None
         # ---- attention block
         if residual is None:
             residual = x.clone()
             h = ops.rmsnorm(x, L.input_norm, cfg.rms_eps)
         else:
-            h = ops.rmsnorm(x, L.input_norm, cfg.rms_eps, residual=residual)
+            h = ops.rmsnorm(x, L.input_norm, cfg.rms_eps, residual=residual, sync=sync)
         qkv = L.qkv(h, ws=splitk_ws)
         q = torch.empty((T, hq, D), dtype=torch.bfloat16, device=self.device)
         ops.rope_store(qkv, self.rope, inp.positions, q, inp.slots, cache, hq, hkv)
@@ -210,28 +214,43 @@ class DenseModel:
         else:
             a = ops.prefill_attn(q, inp.cu_q, inp.seq_lens, inp.block_table, cache, hkv, sh.gqa_local,
                                  inp.max_q_len)
-        # single GPU: leave split-K partials for the fused norm below to finish
-        x = L.o(a.view(T, hq * D), ws=splitk_ws, defer=defer)
-        self._all_reduce(x)
+        a = a.view(T, hq * D)
+        if far is not None:
+            # TP: the all-reduce runs inside the GEMM epilogue (NVLS multicast adds)
+            x, sync_o = far.gemm(L.o, 0, x=a)
+        else:
+            # single GPU: leave split-K partials for the fused norm below to finish
+            x = L.o(a, ws=splitk_ws, defer=defer)
+            self._all_reduce(x)
+            sync_o = None
         # ---- MLP block
         if uses_w4a8(L.gate_up.name, T, self.w4a8):
-            hq8, hs = ops.rmsnorm(x, L.post_norm, cfg.rms_eps, residual=residual, quant=True)
+            hq8, hs = ops.rmsnorm(x, L.post_norm, cfg.rms_eps, residual=residual, quant=True, sync=sync_o)
             gu = L.gate_up(xq=hq8, xs=hs)
             aq, as_ = ops.silu_mul(gu, quant=True)
-            x = L.down(xq=aq, xs=as_)
+            if far is not None:
+                x, sync_d = far.gemm(L.down, 1, xq=aq, xs=as_)
+            else:
+                x = L.down(xq=aq, xs=as_)
+                self._all_reduce(x)
+                sync_d = None
         else:
-            h = ops.rmsnorm(x, L.post_norm, cfg.rms_eps, residual=residual)
+            h = ops.rmsnorm(x, L.post_norm, cfg.rms_eps, residual=residual, sync=sync_o)
             gu = L.gate_up(h, ws=splitk_ws)
             act = ops.silu_mul(gu)
-            x = L.down(act, ws=splitk_ws, defer=defer)
-        self._all_reduce(x)
-        return x, residual
+            if far is not None:
+                x, sync_d = far.gemm(L.down, 1, x=act)
+            else:
+                x = L.down(act, ws=splitk_ws, defer=defer)
+                self._all_reduce(x)
+                sync_d = None
+        return x, residual, sync_d
 
-    def _final_norm(self, x, residual, norm_w, rows: torch.Tensor | None) -> torch.Tensor:
+    def _final_norm(self, x, residual, norm_w, rows: torch.Tensor | None, sync=None) -> torch.Tensor:
         cfg = self.cfg
         if x.dtype == torch.float32 or rows is None:
-            # split-K partials (or every row wanted): finish them in the norm over all rows
-            h = ops.rmsnorm(x, norm_w, cfg.rms_eps, residual=residual)
+            # fp32 sums (or every row wanted): finish them in the norm over all rows
+            h = ops.rmsnorm(x, norm_w, cfg.rms_eps, residual=residual, sync=sync)
             return h if rows is None else h.index_select(0, rows)
         xs = x.index_select(0, rows)
         rs = residual.index_select(0, rows)
@@ -243,10 +262,11 @@ class DenseModel:
         (every row with ``all_rows``, as the MTP drafter needs)."""
         x = self.embed(inp.input_ids)
         residual = None
+        sync = None
         defer = self.tp == 1
         for li, L in enumerate(self.layers):
-            x, residual = self._layer(L, x, residual, inp, kv_caches[li], ws, defer)
-        return self._final_norm(x, residual, self.final_norm, None if all_rows else inp.logit_rows)
+            x, residual, sync = self._layer(L, x, residual, inp, kv_caches[li], ws, defer, sync)
+        return self._final_norm(x, residual, self.final_norm, None if all_rows else inp.logit_rows, sync)
 
     # ---------------------------------------------------------------- MTP
     def init_mtp(self, seed: int = 1) -> "DenseModel":
@@ -301,8 +321,8 @@ class DenseModel:
         ops.rmsnorm(hidden, M.hnorm, cfg.rms_eps, out=cat[:, H:])
         splitk_ws = ws.splitk if ws is not None else None
         x = M.eh_proj(cat, ws=splitk_ws)
-        x, residual = self._layer(M.layer, x, None, inp, cache, ws, defer=self.tp == 1)
-        return self._final_norm(x, residual, M.norm, None)
+        x, residual, sync = self._layer(M.layer, x, None, inp, cache, ws, defer=self.tp == 1)
+        return self._final_norm(x, residual, M.norm, None, sync)
 
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
         """Local vocab shard logits ``[rows, V/tp]`` (bf16)."""

@@ -156,23 +156,43 @@ def wq_gemm(mode: int, w: torch.Tensor, wscale: torch.Tensor, x: torch.Tensor, x
 
 
 # ------------------------------------------------------------------- fused
-def rmsnorm(x, w, eps=1e-6, residual=None, out=None, quant=False):
+def wq_gemm_allreduce(mode: int, w, wscale, x, ws, ws_mc: int, flag_mc: int, xscale=None, split: int = 1):
+    """GEMM -> all-reduce: fp32 sums land in every rank's copy of ``ws`` (a
+    symmetric buffer, multicast address ``ws_mc``); each CTA then signals the
+    multicast counter ``flag_mc``. Returns ``ws``."""
+    require()
+    if x.shape[0] == 0:
+        return ws
+    torch.ops.k8v4.wq_gemm_allreduce(mode, w, wscale, x, xscale, ws, int(ws_mc), int(flag_mc), int(split))
+    _count()
+    return ws
+
+
+def wq_gemm_ctas(mode: int, M: int, N: int, K: int, split: int = 1) -> int:
+    require()
+    return int(torch.ops.k8v4.wq_gemm_ctas(mode, M, N, K, split))
+
+
+def rmsnorm(x, w, eps=1e-6, residual=None, out=None, quant=False, sync=None):
     """RMSNorm (optionally residual-add first); returns y, or (q, scale) with quant.
 
     ``x`` may be the fp32 split-K accumulator of the preceding GEMM: it is
-    consumed (and zeroed) here, finishing that GEMM inside the norm.
+    consumed (and zeroed) here, finishing that GEMM inside the norm. With
+    ``sync = (flag, state, expected)`` x is this rank's copy of a GEMM ->
+    all-reduce buffer and the norm first waits for every rank's signals.
     """
     require()
     rows = x.numel() // x.shape[-1]
+    sf, ss, se = sync if sync is not None else (None, None, 0)
     if quant:
         q = torch.empty(x.shape, dtype=torch.int8, device=x.device)
         s = torch.empty(rows, dtype=torch.float32, device=x.device)
-        torch.ops.k8v4.rmsnorm(x, residual, w, out, q, s, eps)
+        torch.ops.k8v4.rmsnorm(x, residual, w, out, q, s, eps, sf, ss, int(se))
         _count()
         return (out, q, s) if out is not None else (q, s)
     if out is None:
         out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
-    torch.ops.k8v4.rmsnorm(x, residual, w, out, None, None, eps)
+    torch.ops.k8v4.rmsnorm(x, residual, w, out, None, None, eps, sf, ss, int(se))
     _count()
     return out
 

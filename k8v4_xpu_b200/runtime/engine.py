@@ -90,6 +90,9 @@ class LLMEngine:
         if cfg.speculative_tokens:
             self.model.init_mtp(seed=cfg.seed)
         self.layout = self.model.layout
+        self.tp_comm_mode = "single"
+        if self.tp > 1:
+            self._setup_tp_comm(comm)
         self._alloc_cache()
         self.blocks = BlockManager(self.num_blocks, cfg.block_size, self.layout.page, cfg.enable_prefix_caching)
         width = 1 + cfg.speculative_tokens
@@ -122,6 +125,23 @@ class LLMEngine:
         self._h2d_done = None
         self.stats = {"steps": 0, "prompt_tokens": 0, "generated_tokens": 0, "prefill_time": 0.0,
                       "decode_time": 0.0, "iteration_tokens": []}
+
+    def _setup_tp_comm(self, comm) -> None:
+        """Fused GEMM -> all-reduce (NVLS multicast) for decode-sized steps
+        when the box supports it; NCCL otherwise and for larger steps."""
+        from ..parallel.fused_ar import FusedAllReduce, fused_ar_mode
+        self.tp_comm_mode = "nccl"
+        if fused_ar_mode() != "fused":
+            return
+        rows = max(self.cfg.max_num_seqs * (1 + self.cfg.speculative_tokens), 1)
+        rows = min(64, max(rows, 8))
+        try:
+            self.model.fused_ar = FusedAllReduce(getattr(comm, "group", None), self.device, rows,
+                                                 self.mcfg.hidden)
+            self.tp_comm_mode = "fused"
+        except Exception as e:  # no multicast on this box: NCCL all-reduce
+            import logging
+            logging.getLogger("k8v4").warning("fused all-reduce unavailable (%s); using NCCL", e)
 
     # ---------------------------------------------------------------- cache
     def _alloc_cache(self) -> None:

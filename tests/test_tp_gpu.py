@@ -51,6 +51,7 @@ def _prefill_inputs(prompts, dev):
 
 
 PROMPTS = [list(range(3, 3 + 150)), list(range(100, 100 + 45))]
+SMALL_PROMPTS = [list(range(3, 3 + 40)), list(range(100, 100 + 17))]
 
 
 def _worker(rank, world, port, q):
@@ -73,11 +74,23 @@ def _worker(rank, world, port, q):
         hid = m.forward(inp, caches)
         ids = m.greedy(hid)
         res = {"hidden": hid.float().cpu(), "ids": ids.cpu(), "logits": m.logits(hid).float().cpu()}
+        # decode-sized batch (<= 64 rows): the GEMM -> all-reduce runs fused (NVLS multicast adds)
+        from k8v4_xpu_b200.parallel.fused_ar import FusedAllReduce
+        small = _prefill_inputs(SMALL_PROMPTS, dev)
+        caches = [torch.zeros(64, m.layout.page_bytes, dtype=torch.uint8, device=dev) for _ in m.layers]
+        res["small_nccl"] = m.forward(small, caches).float().cpu()
+        m.fused_ar = FusedAllReduce(None, dev, 64, TINY.hidden)
+        for _ in range(3):  # repeated uses: the running signal counts must keep matching
+            caches = [torch.zeros(64, m.layout.page_bytes, dtype=torch.uint8, device=dev) for _ in m.layers]
+            res["small_fused"] = m.forward(small, caches).float().cpu()
+        torch.cuda.synchronize(dev)
+        res["fused_calls"] = m.fused_ar.calls
         cfg = EngineConfig(model="tiny", tensor_parallel_size=world, max_model_len=2048, max_num_seqs=2,
                            max_num_batched_tokens=96, num_kv_blocks=128, device=str(dev))
         eng = LLMEngine(cfg, TINY, comm=comm, rank=rank)
         res["gen"] = eng.generate(PROMPTS, SamplingParams(max_tokens=8, ignore_eos=True))
         res["graph"] = bool(eng.graphs and eng.graphs.captured)
+        res["comm_mode"] = eng.tp_comm_mode
         res["status"] = ops.status()
         eng.graphs.release()
         comm.barrier()
@@ -107,6 +120,12 @@ def test_tp2_matches_tp1():
         assert out[r]["status"] == 0 and out[r]["graph"]
     # ranks agree exactly (replicated residual stream, reduced argmax)
     assert torch.equal(out[0]["hidden"], out[1]["hidden"])
+    assert torch.equal(out[0]["small_fused"], out[1]["small_fused"])
+    assert out[0]["fused_calls"] == 3 * 2 * TINY.num_layers
+    assert out[0]["comm_mode"] == "fused"
+    ref_small = out[0]["small_nccl"]
+    err = (out[0]["small_fused"] - ref_small).abs().max().item()
+    assert err <= 0.02 * ref_small.abs().max().item(), err
     assert out[0]["gen"] == out[1]["gen"]
     # TP2 vs TP1 on the same weights: reduction order differs, values agree closely
     dev = torch.device("cuda", 0)
