@@ -149,7 +149,7 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
                    const __grid_constant__ CUtensorMap tm_s, const Params p) {
   using C = Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BSTAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = align_smem_1024(smem_raw);
   uint8_t* sA = smem;
   uint8_t* sB = sA + C::ASMEM * C::A_BYTES;
   uint8_t* sR = sB + C::BR * C::B_BYTES;
@@ -477,7 +477,9 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
     // the CTA's multicast adds (ordered before this point by the barrier) are
     // out: publish them to every rank
     peer::fence_proxy_alias();
+#ifdef K8V4_AR_FENCE_SYS
     peer::fence_sys();
+#endif
     peer::mc_signal_add_u64(p.flag_mc, 1ull);
   }
 }

@@ -62,6 +62,14 @@ __device__ __forceinline__ void v_chunk_zero(uint8_t* vt, int key, int chunk) {
   *reinterpret_cast<uint4*>(vt + atom_m * VT_LBO + g * 1024 + r * 128 + ((c ^ r) << 4)) = make_uint4(0, 0, 0, 0);
 }
 
+// 2^x with the SFU's ex2.approx (flush-to-zero). Softmax arguments are <= 0
+// after max subtraction (<= tau with the lazy rescale), and -inf gives +0.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // Exact int32 -> fp32 for |v| < 2^22 (QK dot products are below 2^21).
 __device__ __forceinline__ float i2f_small(uint32_t v) {
   return __int_as_float(static_cast<int>(v) + 0x4B400000) - 12582912.0f;

@@ -1,23 +1,23 @@
 // Split-K paged decode / MTP-verify attention over int8-K / int4-V pages.
 //
 // One CTA per (split, KV head, sequence). Query rows are the (token, q-head)
-// pairs of the sequence that share this KV head (q_len * gqa <= NPAD); they
-// are quantized to int8 per row in the prologue (the reference's Q-once
-// quantization, k8v4_v030/native/xe2_kv_ops.cpp:205-257) and held as the
-// MMA B operand. Keys run on the MMA M dimension (TMEM lanes):
+// pairs of the sequence that share this KV head (q_len * gqa <= 64); they are
+// quantized to int8 per row in the prologue (the reference's Q-once
+// quantization, k8v4_v030/native/xe2_kv_ops.cpp:205-257). Rows run on the
+// TMEM lanes, keys / dims on the columns:
 //
-//   S^T[key, row]  = K_tile(int8, TMA) x Q8^T          tcgen05 kind::i8 -> TMEM
-//   softmax        : one thread per key, per-row max over the 128 keys via
-//                    warp shuffles, lazy rescale (tau = 8 in log2 units)
-//   O^T[dim, row] += V^T_tile(fp16) x P^T(fp16)       tcgen05 kind::f16 -> TMEM
+//   S[row, key]  = Q8 (A, smem) x K_tile^T (B, TMA)       tcgen05 kind::i8 -> TMEM
+//   softmax      : one thread per row over its 128 scores (tcgen05.ld),
+//                  lazy rescale (tau = 8 in log2 units), P -> TMEM (tcgen05.st)
+//   O[row, dim] += P (A, TMEM) x V_tile (B, fp16 smem)     tcgen05 kind::f16 -> TMEM
 //
 // V int4 is dequantized by converter warps into the MN-major fp16 tile the
 // PV MMA reads. Each split writes its (m, l, O) partial; k8v4_decode_combine
 // merges the splits (the reference's stage-2 merge, :847-1246). With one
 // split the CTA writes the normalized output directly.
 //
-// Warp roles: 0 = TMA producer, 1 = TMEM owner + MMA issuer, 2-5 = V
-// converters, 6-9 = softmax / epilogue.
+// Warp roles: 0 = TMA producer, 1 = TMEM owner + MMA issuer, 4-5 = softmax /
+// epilogue (lane quadrants 0-1 = rows 0-63), 2, 3, 6, 7 = V converters.
 #include "attn_common.cuh"
 
 namespace k8v4 {
@@ -58,66 +58,83 @@ __device__ uint64_t g_attn_trace[5 * 256];
 template <int NPAD>
 struct DCfg {
   static constexpr int STAGES = 4;
-  static constexpr int NGRP = 2;  // softmax warpgroups, ping-pong over tiles
-  static constexpr int NWARPS = 2 + 4 + 4 * NGRP;
+  static constexpr int NVT = 3;             // fp16 V tiles (conversion runs ahead of the PV MMAs)
+  // 0 TMA, 1 MMA, 4-7 softmax (one per TMEM lane quadrant), 2, 3, 8.. V converters
+#ifndef K8V4_DECODE_NCONV
+#define K8V4_DECODE_NCONV 6
+#endif
+  static constexpr int NCONV = K8V4_DECODE_NCONV;
+  static constexpr int NWARPS = 8 + (NCONV - 2);
   static constexpr int NTHREADS = 32 * NWARPS;
-  static constexpr int Q_BYTES = NPAD * 128;
-  static constexpr int PT_BYTES = 2 * NPAD * 128;   // P^T fp16: 2 K-atoms of NPAD rows
-  static constexpr int TMEM_NEED = 4 * NPAD;        // S^T[2] + O^T[2]
-  static constexpr int TMEM_COLS = TMEM_NEED <= 32 ? 32 : TMEM_NEED <= 64 ? 64 : TMEM_NEED <= 128 ? 128
-                                   : TMEM_NEED <= 256 ? 256 : 512;
-  // layout (offsets from the 1024-aligned base)
+  static constexpr int Q_BYTES = 128 * 128; // Q8 tile: 128 lanes (replicated rows) x 128 dims
+  // TMEM columns: S[2] (int32, 128 keys each), P[2] (fp16 pairs, 64 each), O (fp32, 128 dims)
+  static constexpr uint32_t COL_S = 0, COL_P = 256, COL_O = 384;
+  static constexpr int TMEM_COLS = 512;
   static constexpr int OFF_K = 0;
-  // fp16 V^T tiles: three when shared memory allows, so conversion of tile
-  // j+1 never waits for the PV MMA of tile j-2
-  static constexpr int NVT = (NPAD <= 32) ? 3 : 2;
   static constexpr int OFF_VT = OFF_K + STAGES * K_TILE_BYTES;
-  static constexpr int OFF_PT = OFF_VT + NVT * VT_BYTES;
-  static constexpr int OFF_Q = OFF_PT + 2 * PT_BYTES;
-  static constexpr int OFF_VS = OFF_Q + ((Q_BYTES + 1023) / 1024) * 1024;
-  static constexpr int OFF_MISC = OFF_VS + STAGES * VS_TILE_BYTES;
-  static constexpr int SMEM_BYTES = 1024 + OFF_MISC + 256 + 32 * NPAD * 4 + 64;
+  static constexpr int OFF_Q = OFF_VT + NVT * VT_BYTES;
+  static constexpr int OFF_VS = OFF_Q + Q_BYTES;
+  // k scales of a tile (fp32, one per key), copied out of the stage by the
+  // converters so the stage is released as soon as QK and conversion are done
+  static constexpr int OFF_KS = OFF_VS + STAGES * VS_TILE_BYTES;
+  static constexpr int OFF_MISC = OFF_KS + NVT * TILE * 4;
+  static constexpr int SMEM_BYTES = 1024 + OFF_MISC + 512 + 2 * 64 * 4 + 2 * 128 * 4 + 128 * 4;
+  // epilogue scratch (the K stages, idle by then): 128 lanes x 132 floats
+  static constexpr int EPI_STRIDE = 132;
+  static_assert(128 * EPI_STRIDE * 4 <= STAGES * K_TILE_BYTES + NVT * VT_BYTES, "epilogue scratch");
 };
 
-// Two softmax warpgroups take alternate tiles (group g owns tiles j = g mod 2)
-// with their own S^T / P^T / O^T buffers and their own running max and sums,
-// so one group's softmax overlaps the other's MMAs and handoffs. Their
-// (m, l, O) are merged in the epilogue like two splits.
+// Rows on TMEM lanes: the QK MMA puts query rows in lanes (A = Q8, M = 128)
+// and the tile's 128 keys in columns (B = K page tile, N = 128). The real
+// rows (R <= 64) are replicated NREP = 128 / LPR times down the lanes
+// (LPR = 32 lanes per replica for R <= 32, else 64), which costs the tensor
+// core nothing: replica e's threads own keys [e*KPR, (e+1)*KPR) of every
+// tile (KPR = 128 / NREP). The four softmax warps (one per lane quadrant,
+// so one per SM sub-partition) load only their key slice of S with
+// tcgen05.ld, exchange the slice maxima through an mbarrier, and write their
+// slice of P (fp16 pairs) into TMEM; a lane's P row is zero outside its
+// slice, so the PV MMA (A = P from TMEM, B = V fp16 MN-major) produces one
+// partial O row per replica, summed in the epilogue. O stays in TMEM across
+// tiles; each thread rescales its own row when the shared running max moves
+// (lazy, tau = 8 in log2 units).
 template <int NPAD>
 __global__ void __launch_bounds__(DCfg<NPAD>::NTHREADS, 1)
     decode_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const DecodeParams p) {
   using C = DCfg<NPAD>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sm = align_smem_1024(smem_raw);
   uint8_t* sK = sm + C::OFF_K;
   uint8_t* sVT = sm + C::OFF_VT;
-  uint8_t* sPT = sm + C::OFF_PT;
   uint8_t* sQ = sm + C::OFF_Q;
   uint8_t* sVS = sm + C::OFF_VS;
+  float* sKS = reinterpret_cast<float*>(sm + C::OFF_KS);
   uint8_t* misc = sm + C::OFF_MISC;
   uint64_t* kv_full = reinterpret_cast<uint64_t*>(misc);
-  uint64_t* kv_empty = kv_full + C::STAGES;
-  uint64_t* s_full = kv_empty + C::STAGES;  // [2] (buffer = owning group)
-  uint64_t* p_full = s_full + 2;            // [2]
-  uint64_t* v_full = p_full + 2;            // [NVT] V^T tile converted
-  uint64_t* pv_empty = v_full + 3;          // [2] PV of the group's last tile done (P^T / O^T reusable)
-  uint64_t* vt_empty = pv_empty + 2;        // [NVT] PV that read the V^T tile done
-  uint64_t* done_bar = vt_empty + 3;
+  uint64_t* kv_empty = kv_full + C::STAGES;  // QK commit + converter warps
+  uint64_t* s_full = kv_empty + C::STAGES;   // [2] QK done
+  uint64_t* s_empty = s_full + 2;            // [2] softmax read S
+  uint64_t* p_full = s_empty + 2;            // [2] softmax wrote P (and rescaled O)
+  uint64_t* pv_empty = p_full + 2;           // [2] PV that read P[b] done (O current)
+  uint64_t* v_full = pv_empty + 2;           // [NVT] V tile converted
+  uint64_t* vt_empty = v_full + C::NVT;      // [NVT] PV that read the V tile done
+  uint64_t* ks_full = vt_empty + C::NVT;     // [NVT] k scales copied out
+  uint64_t* mx_full = ks_full + C::NVT;      // [2] slice maxima of a tile published
+  uint64_t* done_bar = mx_full + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  int* grp_ok = const_cast<int*>(abort_flag) + 1;            // [2]
-  float* q_scale = reinterpret_cast<float*>(misc + 256);     // [NPAD] q scale * softmax scale
-  int* row_end = reinterpret_cast<int*>(q_scale + NPAD);     // [NPAD] visible keys per row
-  float* m_ref = reinterpret_cast<float*>(row_end + NPAD);   // [2][4][NPAD] running max per warp (log2)
-  float* alpha = m_ref + 8 * NPAD;                           // [2][4][NPAD] this tile's rescale per warp
-  float* red = alpha + 8 * NPAD;                             // [2][4][NPAD] cross-warp partials
-  float* fin = red + 8 * NPAD;                               // [2][2][NPAD] final (m, l) per group
+  float* q_scale = reinterpret_cast<float*>(misc + 512);  // [64] q scale * softmax scale (log2)
+  int* row_end = reinterpret_cast<int*>(q_scale + 64);     // [64] visible keys per row
+  float* mx_buf = reinterpret_cast<float*>(row_end + 64);  // [2][128] slice max per lane
+  float* l_buf = mx_buf + 2 * 128;                         // [128] partial row sums per lane
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int split = blockIdx.x, h = blockIdx.y + p.head_offset, seq = blockIdx.z;
   const int hl = blockIdx.y;  // head index within this launch's workspace
   const int qb = p.cu_q[seq], q_len = p.cu_q[seq + 1] - qb;
-  const int R = q_len * p.gqa;  // real rows
+  const int R = q_len * p.gqa;  // real rows (<= 64)
+  constexpr int LPR = NPAD > 32 ? 64 : 32;  // lanes per replica (rows R <= NPAD)
+  constexpr int NREP = 128 / LPR;
+  constexpr int KPR = TILE / NREP;          // keys per replica slice
   const int seq_len = p.seq_lens[seq];
   const int n_pages = (seq_len + PAGE - 1) / PAGE;
   const int n_tiles_all = (n_pages + TILE_PAGES - 1) / TILE_PAGES;
@@ -129,55 +146,58 @@ __global__ void __launch_bounds__(DCfg<NPAD>::NTHREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1 + 4 + 4);  // MMA commit + converter warps + owning group's warps
+      mbar_init(&kv_empty[s], 1 + C::NCONV);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
+      mbar_init(&s_empty[b], 4);
       mbar_init(&p_full[b], 4);
       mbar_init(&pv_empty[b], 1);
+      mbar_init(&mx_full[b], 4);
     }
     for (int v = 0; v < C::NVT; ++v) {
-      mbar_init(&v_full[v], 4);
+      mbar_init(&v_full[v], C::NCONV);
       mbar_init(&vt_empty[v], 1);
+      mbar_init(&ks_full[v], 4);
     }
     mbar_init(done_bar, 1);
     *abort_flag = 0;
-    grp_ok[0] = grp_ok[1] = 1;
     fence_mbar_init();
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, C::TMEM_COLS);
     tmem_relinquish();
   }
-  // ---- prologue: quantize the query rows into the Q8 tile (K-major SW128)
-  for (int r = warp; r < NPAD; r += C::NWARPS) {
-    float x[4] = {0.f, 0.f, 0.f, 0.f};
-    int end = 0;
-    if (r < R) {
-      const int t = r / p.gqa, g = r % p.gqa;
-      const __nv_bfloat16* src = p.q + ((int64_t)(qb + t) * p.hq_total + (int64_t)h * p.gqa + g) * D + lane * 4;
-      const uint2 raw = *reinterpret_cast<const uint2*>(src);
-      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
-      const float2 a = __bfloat1622float2(h2[0]), b = __bfloat1622float2(h2[1]);
-      x[0] = a.x; x[1] = a.y; x[2] = b.x; x[3] = b.y;
-      end = p.q_ends ? p.q_ends[qb + t] : (seq_len - q_len + t + 1);
-    }
+  // ---- prologue: zero the Q8 tile, then quantize the real rows into every replica (K-major SW128)
+  for (int i = threadIdx.x; i < C::Q_BYTES / 16; i += C::NTHREADS)
+    reinterpret_cast<uint4*>(sQ)[i] = make_uint4(0, 0, 0, 0);
+  if (threadIdx.x < 64) {
+    q_scale[threadIdx.x] = 0.f;
+    row_end[threadIdx.x] = 0;
+  }
+  __syncthreads();
+  for (int r = warp; r < R; r += C::NWARPS) {
+    const int t = r / p.gqa, g = r % p.gqa;
+    const __nv_bfloat16* src = p.q + ((int64_t)(qb + t) * p.hq_total + (int64_t)h * p.gqa + g) * D + lane * 4;
+    const uint2 raw = *reinterpret_cast<const uint2*>(src);
+    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+    const float2 a = __bfloat1622float2(h2[0]), b2 = __bfloat1622float2(h2[1]);
+    const float x[4] = {a.x, a.y, b2.x, b2.y};
     float amax = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
     amax = warp_max(amax);
-    const float s = amax / 127.f;
-    const float inv = s > 0.f ? 1.f / s : 0.f;
+    const float sc = amax / 127.f;
+    const float inv = sc > 0.f ? 1.f / sc : 0.f;
     uint32_t w = 0;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int qi = (int)fminf(fmaxf(rintf(x[j] * inv), -127.f), 127.f);
       w |= ((uint32_t)(uint8_t)(int8_t)qi) << (8 * j);
     }
-    // lane covers bytes [4*lane, 4*lane+4) of the 128-byte row: chunk lane/4
-    *reinterpret_cast<uint32_t*>(sQ + sw128_offset(r, lane >> 2) + (lane & 3) * 4) = w;
+    for (int e = 0; e < NREP; ++e)
+      *reinterpret_cast<uint32_t*>(sQ + sw128_offset(e * LPR + r, lane >> 2) + (lane & 3) * 4) = w;
     if (lane == 0) {
-      q_scale[r] = s * p.sm_scale_log2;
-      row_end[r] = end;
-      for (int c = 0; c < 8; ++c) m_ref[c * NPAD + r] = -INFINITY;
+      q_scale[r] = sc * p.sm_scale_log2;
+      row_end[r] = p.q_ends ? p.q_ends[qb + t] : (seq_len - q_len + t + 1);
     }
   }
   fence_async_smem();
@@ -185,58 +205,63 @@ __global__ void __launch_bounds__(DCfg<NPAD>::NTHREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  const uint32_t tm_s = tmem;                 // S^T buffers: cols [0, 2*NPAD)
-  const uint32_t tm_o = tmem + 2 * NPAD;      // O^T buffers: cols [2*NPAD, 4*NPAD)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      prefetch_tmap(&tm_k);
-      int issued = 0;
-      for (int j = 0; j < nt; ++j) {
-        const int s = j % C::STAGES;
-        if (j >= C::STAGES && !mbar_wait(&kv_empty[s], ((j / C::STAGES) - 1) & 1, abort_flag, 201)) break;
-        const int pg0 = (tile_beg + j) * TILE_PAGES;
-        const int npg = min(TILE_PAGES, n_pages - pg0);
-        mbar_arrive_expect_tx(&kv_full[s], npg * (K_BYTES + VS_BYTES));
-        for (int i = 0; i < npg; ++i) {
-          const int64_t page = bt[pg0 + i];
-          const int64_t run = page * p.hkv + h;
-          tma_load_3d(sK + s * K_TILE_BYTES + i * K_BYTES, &tm_k, &kv_full[s], 0, 0, (int)run);
-          bulk_load(sVS + s * VS_TILE_BYTES + i * VS_BYTES, p.cache + run * HEAD_BYTES + VS_OFF, VS_BYTES,
-                    &kv_full[s]);
-        }
-        K8V4_ATRACE(0, j);
-        ++issued;
+    // Lane i handles page i of a tile (8 pages): its page id is read one tile
+    // ahead, and it issues that page's K TMA and V + scales bulk copy itself.
+    if (lane == 0) prefetch_tmap(&tm_k);
+    auto page_of = [&](int jt) -> int64_t {
+      const int pg = (tile_beg + jt) * TILE_PAGES + lane;
+      return (jt < nt && lane < TILE_PAGES && pg < n_pages) ? (int64_t)bt[pg] : 0;
+    };
+    int64_t next_page = page_of(0);
+    int issued = 0;
+    for (int j = 0; j < nt; ++j) {
+      const int s = j % C::STAGES;
+      const int64_t page = next_page;
+      next_page = page_of(j + 1);
+      if (j >= C::STAGES && !mbar_wait_all(&kv_empty[s], ((j / C::STAGES) - 1) & 1, abort_flag, 201)) break;
+      const int pg0 = (tile_beg + j) * TILE_PAGES;
+      const int npg = min(TILE_PAGES, n_pages - pg0);
+      if (lane == 0) mbar_arrive_expect_tx(&kv_full[s], npg * (K_BYTES + VS_BYTES));
+      __syncwarp();
+      if (lane < npg) {
+        const int64_t run = page * p.hkv + h;
+        tma_load_3d(sK + s * K_TILE_BYTES + lane * K_BYTES, &tm_k, &kv_full[s], 0, 0, (int)run);
+        bulk_load(sVS + s * VS_TILE_BYTES + lane * VS_BYTES, p.cache + run * HEAD_BYTES + VS_OFF, VS_BYTES,
+                  &kv_full[s]);
       }
-      if (*abort_flag)
-        for (int j = issued - 1; j >= 0 && j >= issued - C::STAGES; --j)
-          mbar_wait_drain(&kv_full[j % C::STAGES], (j / C::STAGES) & 1);
+      if (lane == 0) K8V4_ATRACE(0, j);
+      ++issued;
     }
+    if (lane == 0 && *abort_flag)
+      for (int j = issued - 1; j >= 0 && j >= issued - C::STAGES; --j)
+        mbar_wait_drain(&kv_full[j % C::STAGES], (j / C::STAGES) & 1);
   } else if (warp == 1) {
     // ----------------------------------------------------------------- MMA
     if (lane == 0 && nt > 0) {
-      const uint32_t id_qk = idesc_s8(128, NPAD);
-      const uint32_t id_pv = idesc_f16(128, NPAD, true, false);
+      const uint32_t id_qk = idesc_s8(128, 128);
+      const uint32_t id_pv = idesc_f16(128, 128, false, true);
       const uint32_t q_base = smem_u32(sQ);
       bool ok = true;
       for (int j = 0; j <= nt && ok; ++j) {
         if (j < nt) {
           const int s = j % C::STAGES, b = j & 1;
           if (!mbar_wait(&kv_full[s], (j / C::STAGES) & 1, abort_flag, 202)) break;
+          if (j >= 2 && !mbar_wait(&s_empty[b], ((j >> 1) - 1) & 1, abort_flag, 209)) break;
           tc_fence_after();
           const uint32_t k_base = smem_u32(sK + s * K_TILE_BYTES);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma_i8(tm_s + b * NPAD, sdesc_sw128(k_base + kk * 32, 16, 1024), sdesc_sw128(q_base + kk * 32, 16, 1024),
-                   id_qk, kk > 0 ? 1u : 0u);
+            mma_i8(tmem + C::COL_S + b * 128, sdesc_sw128(q_base + kk * 32, 16, 1024),
+                   sdesc_sw128(k_base + kk * 32, 16, 1024), id_qk, kk > 0 ? 1u : 0u);
           mma_commit(&s_full[b]);
           mma_commit(&kv_empty[s]);
           K8V4_ATRACE(2, j);
         }
         if (j >= 1) {
-          const int jj = j - 1, b = jj & 1;
-          const int vb = jj % C::NVT;
+          const int jj = j - 1, b = jj & 1, vb = jj % C::NVT;
           if (!mbar_wait(&p_full[b], (jj >> 1) & 1, abort_flag, 203) ||
               !mbar_wait(&v_full[vb], (jj / C::NVT) & 1, abort_flag, 204)) {
             ok = false;
@@ -244,13 +269,10 @@ __global__ void __launch_bounds__(DCfg<NPAD>::NTHREADS, 1)
           }
           tc_fence_after();
           const uint32_t vt_base = smem_u32(sVT + vb * VT_BYTES);
-          const uint32_t pt_base = smem_u32(sPT + b * C::PT_BYTES);
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint64_t ad = sdesc_sw128(vt_base + kk * 2048, VT_LBO, 1024);
-            const uint64_t bd = sdesc_sw128(pt_base + (kk >> 2) * (NPAD * 128) + (kk & 3) * 32, 16, 1024);
-            mma_f16(tm_o + b * NPAD, ad, bd, id_pv, (jj >= 2 || kk > 0) ? 1u : 0u);
-          }
+          for (int kk = 0; kk < 8; ++kk)
+            mma_f16_ts(tmem + C::COL_O, tmem + C::COL_P + b * 64 + kk * 8,
+                       sdesc_sw128(vt_base + kk * 2048, VT_LBO, 1024), id_pv, (jj > 0 || kk > 0) ? 1u : 0u);
           mma_commit(&pv_empty[b]);
           mma_commit(&vt_empty[vb]);
           K8V4_ATRACE(4, jj);
@@ -259,11 +281,193 @@ __global__ void __launch_bounds__(DCfg<NPAD>::NTHREADS, 1)
       mma_commit(done_bar);
       mbar_wait_drain(done_bar, 0);
     }
-  } else if (warp < 6) {
-    // ---------------------------------------------------------- converters
-    const int ct = threadIdx.x - 64;  // 0..127
+  } else if (warp >= 4 && warp < 8) {
+    // ---------------------------------------- softmax (lane = replica x row)
+    const int quad = warp - 4;
+    const int lane_id = quad * 32 + lane;  // TMEM lane
+    const int rep = lane_id / LPR, r = lane_id % LPR;
+    const bool real = r < R;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const uint32_t tS = tmem + C::COL_S + lane_off, tP = tmem + C::COL_P + lane_off, tO = tmem + C::COL_O + lane_off;
+    const float qs = real ? q_scale[r] : 0.f;
+    const int end = real ? row_end[r] : 0;
+    const int kofs = rep * KPR;  // this lane's key slice within a tile
+    // P rows are zero outside the lane's slice: clear both P buffers once
+    {
+      uint32_t z[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) z[i] = 0u;
+#pragma unroll
+      for (int c = 0; c < 128; c += 32) tmem_st32(tP + c, z);
+      tmem_st_wait();
+    }
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    // Every softmax warp runs every iteration (the slice maxima are exchanged
+    // each tile); a failed wait only turns the work off.
     for (int j = 0; j < nt; ++j) {
-      const int s = j % C::STAGES, b = j & 1;
+      const int b = j & 1, vb = j % C::NVT;
+      if (ok && !mbar_wait_all(&s_full[b], (j >> 1) & 1, abort_flag, 207)) ok = false;
+      float sc[KPR];
+      if (ok) {
+        tc_fence_after();
+        uint32_t v[32];
+        tmem_ld32(tS + b * 128 + kofs, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sc[i] = i2f_small(v[i]);
+        if constexpr (KPR > 32) {
+          tmem_ld32(tS + b * 128 + kofs + 32, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) sc[32 + i] = i2f_small(v[i]);
+        }
+        tc_fence_before();
+      }
+      __syncwarp();
+      if (ok && lane == 0) mbar_arrive(&s_empty[b]);
+      if (ok && !mbar_wait_all(&ks_full[vb], (j / C::NVT) & 1, abort_flag, 208)) ok = false;
+      const int key0 = (tile_beg + j) * TILE + kofs;
+      float tmax = -INFINITY;
+      if (ok) {
+        const float4* ks4 = reinterpret_cast<const float4*>(sKS + vb * TILE + kofs);
+        const bool full = __all_sync(0xffffffffu, end >= key0 + KPR || !real);
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int k = 0; k < KPR; k += 4) {
+          {
+            const float4 kq = ks4[k >> 2];
+            float v0 = sc[k] * (qs * kq.x), v1 = sc[k + 1] * (qs * kq.y);
+            float v2 = sc[k + 2] * (qs * kq.z), v3 = sc[k + 3] * (qs * kq.w);
+            if (!full) {
+              v0 = (key0 + k < end) ? v0 : -INFINITY;
+              v1 = (key0 + k + 1 < end) ? v1 : -INFINITY;
+              v2 = (key0 + k + 2 < end) ? v2 : -INFINITY;
+              v3 = (key0 + k + 3 < end) ? v3 : -INFINITY;
+            }
+            sc[k] = v0; sc[k + 1] = v1; sc[k + 2] = v2; sc[k + 3] = v3;
+            mx[0] = fmaxf(mx[0], v0); mx[1] = fmaxf(mx[1], v1);
+            mx[2] = fmaxf(mx[2], v2); mx[3] = fmaxf(mx[3], v3);
+          }
+        }
+        tmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      }
+      // publish the slice max, combine the row's slices (all replicas of row r)
+      mx_buf[b * 128 + lane_id] = tmax;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&mx_full[b]);
+      if (ok && !mbar_wait_all(&mx_full[b], (j >> 1) & 1, abort_flag, 213)) ok = false;
+      if (ok) {
+        for (int e = 0; e < NREP; ++e) tmax = fmaxf(tmax, mx_buf[b * 128 + e * LPR + r]);
+        float alpha = 1.f;
+        if (tmax > m + RESCALE_TAU || (m == -INFINITY && tmax > -INFINITY)) {
+          alpha = (m == -INFINITY) ? 0.f : ex2_approx(m - tmax);
+          m = tmax;
+        }
+        l *= alpha;
+        // O holds PV(0..j-1) after PV(j-1): rescale it when any row of the warp moved its max
+        if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.f)) {
+          if (!mbar_wait_all(&pv_empty[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, 211)) {
+            ok = false;
+          } else {
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < D; c += 32) {
+              uint32_t v[32];
+              tmem_ld32(tO + c, v);
+              tmem_ld_wait();
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+              tmem_st32(tO + c, v);
+            }
+          }
+        }
+        // P[b] is free once the PV of tile j-2 finished
+        if (ok && j >= 2 && !mbar_wait_all(&pv_empty[b], ((j >> 1) - 1) & 1, abort_flag, 210)) ok = false;
+        if (ok) {
+          tc_fence_after();
+          // rows with no visible key keep m = -inf: exponentiate against 0 (all p = 0)
+          const float mref = (m == -INFINITY) ? 0.f : m;
+          float ls[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int hlf = 0; hlf < KPR; hlf += 32) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int k = 0; k < 32; k += 2) {
+              const float p0 = ex2_approx(sc[hlf + k] - mref);
+              const float p1 = ex2_approx(sc[hlf + k + 1] - mref);
+              ls[(k >> 1) & 3] += p0 + p1;
+              const __half2 hp = __floats2half2_rn(p0, p1);
+              pk[k >> 1] = *reinterpret_cast<const uint32_t*>(&hp);
+            }
+            tmem_st16(tP + b * 64 + ((kofs + hlf) >> 1), pk);
+          }
+          l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+          tmem_st_wait();
+          tc_fence_before();
+        }
+      }
+      __syncwarp();
+      if (ok && lane == 0) {
+        mbar_arrive(&p_full[b]);
+        if (quad == 0) K8V4_ATRACE(3, j);
+      }
+    }
+    // ------------------------------------------------------------ epilogue
+    // sum the replicas' partial O rows and row sums through shared memory
+    // (the K / V stage buffers are idle once the last PV finished)
+    if (ok && nt > 0 && !mbar_wait_all(&pv_empty[(nt - 1) & 1], ((nt - 1) >> 1) & 1, abort_flag, 212)) ok = false;
+    tc_fence_after();
+    float* epi = reinterpret_cast<float*>(sm);
+#pragma unroll
+    for (int c = 0; c < D; c += 32) {
+      uint32_t v[32];
+      if (ok && nt > 0) {
+        tmem_ld32(tO + c, v);
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0u;
+      }
+      float* row = epi + lane_id * C::EPI_STRIDE + c;
+#pragma unroll
+      for (int i = 0; i < 32; i += 4)
+        *reinterpret_cast<float4*>(row + i) = make_float4(__uint_as_float(v[i]), __uint_as_float(v[i + 1]),
+                                                          __uint_as_float(v[i + 2]), __uint_as_float(v[i + 3]));
+    }
+    l_buf[lane_id] = (ok && nt > 0) ? l : 0.f;
+    if (lane_id < 64) mx_buf[lane_id] = (ok && nt > 0) ? m : -INFINITY;  // replica 0 rows (lanes < LPR)
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    // thread d of the 128 softmax threads writes dim d of every real row
+    const int d = lane_id;
+    const int64_t wsi = (((int64_t)seq * gridDim.y + hl) * p.nsplit + split);
+    for (int rr = 0; rr < R; ++rr) {
+      float o = 0.f, lt = 0.f;
+      for (int e = 0; e < NREP; ++e) {
+        o += epi[(e * LPR + rr) * C::EPI_STRIDE + d];
+        lt += l_buf[e * LPR + rr];
+      }
+      if (p.nsplit == 1) {
+        const int t = rr / p.gqa, g = rr % p.gqa;
+        p.out[((int64_t)(qb + t) * p.hq_total + (int64_t)h * p.gqa + g) * D + d] =
+            __float2bfloat16_rn(lt > 0.f ? o / lt : 0.f);
+      } else {
+        p.ws_o[(wsi * NPAD + rr) * D + d] = o;
+        if (d == 0) {
+          p.ws_ml[(wsi * 2) * NPAD + rr] = mx_buf[rr];
+          p.ws_ml[(wsi * 2 + 1) * NPAD + rr] = lt;
+        }
+      }
+    }
+  } else {
+    // ---------------------------------------------------------- converters
+    // One item = 32 dims (one scale group) of one key: a 16-byte load of
+    // packed V and one scale feed four 16-byte stores of the fp16 tile.
+    const int cw = (warp < 4) ? warp - 2 : warp - 6;  // warps 2, 3, 8, 9, ... -> 0 .. NCONV-1
+    const int ct = cw * 32 + lane;
+    constexpr int CT = C::NCONV * 32;
+    for (int j = 0; j < nt; ++j) {
+      const int s = j % C::STAGES;
       if (!mbar_wait_all(&kv_full[s], (j / C::STAGES) & 1, abort_flag, 205)) break;
       const int vb = j % C::NVT;
       if (j >= C::NVT && !mbar_wait_all(&vt_empty[vb], ((j / C::NVT) - 1) & 1, abort_flag, 206)) break;
@@ -271,17 +475,29 @@ __global__ void __launch_bounds__(DCfg<NPAD>::NTHREADS, 1)
       const int nvalid = min(TILE, seq_len - key0);
       const uint8_t* vs = sVS + s * VS_TILE_BYTES;
       uint8_t* vt = sVT + vb * VT_BYTES;
-#pragma unroll 4
-      for (int item = ct; item < TILE * 16; item += 128) {
-        const int key = item >> 4, chunk = item & 15;
+      // k scales first: the softmax of this tile needs only these
+      if (cw < 4) {
+        sKS[vb * TILE + ct] = (ct < nvalid) ? __half2float(*reinterpret_cast<const __half*>(
+                                                  vs + (ct >> 4) * VS_BYTES + KS_OFF + (ct & 15) * 2))
+                                            : 0.f;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ks_full[vb]);
+      }
+#pragma unroll
+      for (int item = ct; item < TILE * 4; item += CT) {
+        const int key = item >> 2, grp = item & 3;
         if (key < nvalid) {
           const uint8_t* run = vs + (key >> 4) * VS_BYTES;
           const int kk = key & 15;
-          const uint32_t w = *reinterpret_cast<const uint32_t*>(run + kk * 64 + chunk * 4);
-          const __half sc = *reinterpret_cast<const __half*>(run + VSC_OFF + (kk * 4 + (chunk >> 2)) * 2);
-          v_chunk_to_f16(w, sc, vt, key, chunk);
+          const uint4 w = *reinterpret_cast<const uint4*>(run + kk * 64 + grp * 16);
+          const __half sc = *reinterpret_cast<const __half*>(run + VSC_OFF + (kk * 4 + grp) * 2);
+          v_chunk_to_f16(w.x, sc, vt, key, grp * 4);
+          v_chunk_to_f16(w.y, sc, vt, key, grp * 4 + 1);
+          v_chunk_to_f16(w.z, sc, vt, key, grp * 4 + 2);
+          v_chunk_to_f16(w.w, sc, vt, key, grp * 4 + 3);
         } else {
-          v_chunk_zero(vt, key, chunk);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) v_chunk_zero(vt, key, grp * 4 + q);
         }
       }
       fence_async_smem();
@@ -290,195 +506,6 @@ __global__ void __launch_bounds__(DCfg<NPAD>::NTHREADS, 1)
         mbar_arrive(&v_full[vb]);
         mbar_arrive(&kv_empty[s]);
         if (ct < 32) K8V4_ATRACE(1, j);
-      }
-    }
-  } else {
-    // ------------------------------------------------------------- softmax
-    const int grp = (warp - 6) >> 2;           // warpgroup: owns tiles j = grp mod 2
-    const int sw = (warp - 6) & 3;             // warp within the group
-    const int quad = warp & 3;                 // TMEM lane quadrant
-    const int key_local = quad * 32 + lane;    // this thread's key (S^T lane) and dim (O^T lane)
-    const int bar_id = 1 + grp;
-    float* mw = m_ref + (grp * 4 + sw) * NPAD;
-    float* aw = alpha + (grp * 4 + sw) * NPAD;
-    float* rd = red + grp * 4 * NPAD;
-    const uint32_t tm_og = tm_o + grp * NPAD;
-    float l_acc[NPAD];
-#pragma unroll
-    for (int r = 0; r < NPAD; ++r) l_acc[r] = 0.f;
-    // Every warp of a group runs every iteration and every named barrier,
-    // even after a failed (timed-out) wait: a failure only turns the work
-    // off, so the four warps always meet at the same bar.sync.
-    bool ok = true;
-    for (int j = grp; j < nt; j += 2) {
-      const int s = j % C::STAGES, b = grp;
-      if (ok && (!mbar_wait_all(&s_full[b], (j >> 1) & 1, abort_flag, 207) ||
-                 !mbar_wait_all(&kv_full[s], (j / C::STAGES) & 1, abort_flag, 208)))
-        ok = false;
-      const int key = (tile_beg + j) * TILE + key_local;
-      float sc[NPAD];
-#pragma unroll
-      for (int r = 0; r < NPAD; ++r) sc[r] = -INFINITY;
-      if (ok) {
-        tc_fence_after();
-        const uint8_t* vs = sVS + s * VS_TILE_BYTES;
-        const float ks = (key < seq_len)
-                             ? __half2float(*reinterpret_cast<const __half*>(vs + (key_local >> 4) * VS_BYTES + KS_OFF +
-                                                                             (key_local & 15) * 2))
-                             : 0.f;
-        const uint32_t ta = tm_s + b * NPAD + ((uint32_t)(quad * 32) << 16);
-#pragma unroll
-        for (int c = 0; c < NPAD; c += 16) {
-          uint32_t r16[16];
-          tmem_ld16(ta + c, r16);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) sc[c + i] = i2f_small(r16[i]);
-        }
-        // scores (log2 domain), masked, and this warp's per-row max
-#pragma unroll
-        for (int r = 0; r < NPAD; ++r) {
-          if (r < R) {
-            const float v = sc[r] * (q_scale[r] * ks);
-            sc[r] = (key < row_end[r]) ? v : -INFINITY;
-            const float wm = warp_max(sc[r]);
-            if (lane == 0) rd[sw * NPAD + r] = wm;
-          }
-        }
-      }
-      asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
-      int any_rescale = 0;
-      if (ok) {
-#pragma unroll
-        for (int r = 0; r < NPAD; ++r) {
-          if (r < R) {
-            const float tmax = fmaxf(fmaxf(rd[r], rd[NPAD + r]), fmaxf(rd[2 * NPAD + r], rd[3 * NPAD + r]));
-            const float mo = mw[r];
-            float a = 1.f, mn = mo;
-            if (tmax > mo + RESCALE_TAU || (mo == -INFINITY && tmax > -INFINITY)) {
-              mn = tmax;
-              a = (mo == -INFINITY) ? 0.f : exp2f(mo - mn);
-              any_rescale = 1;
-            }
-            l_acc[r] *= a;
-            sc[r] = (sc[r] == -INFINITY || mn == -INFINITY) ? 0.f : exp2f(sc[r] - mn);
-            l_acc[r] += sc[r];
-            __syncwarp();
-            if (lane == 0) {
-              mw[r] = mn;
-              aw[r] = a;
-            }
-          }
-        }
-        __syncwarp();
-      }
-      // this group's previous PV (tile j-2) read P^T[b] and wrote O^T[b]
-      if (ok && j >= 2 && !mbar_wait_all(&pv_empty[b], ((j >> 1) - 1) & 1, abort_flag, 210)) ok = false;
-      if (ok && any_rescale && j >= 2) {
-        tc_fence_after();
-        const uint32_t ta = tm_og + ((uint32_t)(quad * 32) << 16);
-#pragma unroll
-        for (int c = 0; c < NPAD; c += 8) {
-          uint32_t r8[8];
-          tmem_ld8(ta + c, r8);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-            r8[i] = __float_as_uint(__uint_as_float(r8[i]) * (c + i < R ? aw[c + i] : 1.f));
-          tmem_st8(ta + c, r8);
-        }
-        tmem_st_wait();
-      }
-      if (ok) {
-        uint8_t* pt = sPT + b * C::PT_BYTES + (key_local >> 6) * (NPAD * 128) + (key_local & 7) * 2;
-        const int kc = (key_local & 63) >> 3;
-#pragma unroll
-        for (int r = 0; r < NPAD; ++r) {
-          const __half hv = __float2half_rn(r < R ? sc[r] : 0.f);
-          *reinterpret_cast<__half*>(pt + r * 128 + ((kc ^ (r & 7)) << 4)) = hv;
-        }
-        fence_async_smem();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&p_full[b]);
-          mbar_arrive(&kv_empty[s]);
-          if (sw == 0) K8V4_ATRACE(3, j);
-        }
-      }
-      asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");  // rd / m reads done before the next tile
-    }
-    // ------------------------------------------------------------ epilogue
-    const bool has = nt > grp;  // this group processed at least one tile
-    if (ok && has) {
-      const int jl = grp + 2 * ((nt - 1 - grp) / 2);  // this group's last tile
-      if (!mbar_wait_all(&pv_empty[grp], (jl >> 1) & 1, abort_flag, 211)) ok = false;
-    }
-#pragma unroll
-    for (int r = 0; r < NPAD; ++r) {
-      if (r < R) {
-        const float ws = warp_sum(l_acc[r]);
-        if (lane == 0) rd[sw * NPAD + r] = ws;
-      }
-    }
-    asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
-    if (sw == 0) {
-      for (int r = lane; r < NPAD; r += 32) {
-        fin[(grp * 2) * NPAD + r] = has ? mw[r] : -INFINITY;
-        fin[(grp * 2 + 1) * NPAD + r] = rd[r] + rd[NPAD + r] + rd[2 * NPAD + r] + rd[3 * NPAD + r];
-      }
-      if (lane == 0 && !ok) grp_ok[grp] = 0;
-    }
-    asm volatile("bar.sync 3, 256;" ::: "memory");  // both groups' (m, l) published
-    if (grp == 0 && grp_ok[0] && grp_ok[1]) {
-      tc_fence_after();
-      float o0[NPAD], o1[NPAD];
-#pragma unroll
-      for (int r = 0; r < NPAD; ++r) o0[r] = o1[r] = 0.f;
-      const uint32_t lo = (uint32_t)(quad * 32) << 16;
-      if (nt > 0) {
-#pragma unroll
-        for (int c = 0; c < NPAD; c += 16) {
-          uint32_t r16[16];
-          tmem_ld16(tm_o + lo + c, r16);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) o0[c + i] = __uint_as_float(r16[i]);
-        }
-      }
-      if (nt > 1) {
-#pragma unroll
-        for (int c = 0; c < NPAD; c += 16) {
-          uint32_t r16[16];
-          tmem_ld16(tm_o + NPAD + lo + c, r16);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) o1[c + i] = __uint_as_float(r16[i]);
-        }
-      }
-      const int d = key_local;
-      const int64_t wsi = (((int64_t)seq * gridDim.y + hl) * p.nsplit + split);
-#pragma unroll
-      for (int r = 0; r < NPAD; ++r) {
-        if (r < R) {
-          const float m0 = fin[r], l0 = fin[NPAD + r], m1 = fin[2 * NPAD + r], l1 = fin[3 * NPAD + r];
-          const float M = fmaxf(m0, m1);
-          const float w0 = (m0 == -INFINITY) ? 0.f : exp2f(m0 - M);
-          const float w1 = (m1 == -INFINITY) ? 0.f : exp2f(m1 - M);
-          const float o = (w0 > 0.f ? w0 * o0[r] : 0.f) + (w1 > 0.f ? w1 * o1[r] : 0.f);
-          const float l = w0 * l0 + w1 * l1;
-          if (p.nsplit == 1) {
-            const int t = r / p.gqa, g = r % p.gqa;
-            const float v = l > 0.f ? o / l : 0.f;
-            p.out[((int64_t)(qb + t) * p.hq_total + (int64_t)h * p.gqa + g) * D + d] = __float2bfloat16_rn(v);
-          } else {
-            p.ws_o[(wsi * NPAD + r) * D + d] = o;
-            if (d == 0) {
-              p.ws_ml[(wsi * 2) * NPAD + r] = M;
-              p.ws_ml[(wsi * 2 + 1) * NPAD + r] = l;
-            }
-          }
-        }
       }
     }
   }

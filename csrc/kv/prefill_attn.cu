@@ -54,7 +54,7 @@ __global__ void __launch_bounds__(320, 1)
     prefill_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const PrefillParams p) {
   using C = PCfg;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sm = align_smem_1024(smem_raw);
   uint8_t* sK = sm + C::OFF_K;
   uint8_t* sVT = sm + C::OFF_VT;
   uint8_t* sP = sm + C::OFF_P;

@@ -17,6 +17,16 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 }
 
 // ------------------------------------------------------------------ mbarrier
+// The dynamic shared-memory window rounded up to 1024 bytes (the 128-byte
+// swizzle atom repeats every 1024 bytes). The offset is added to the
+// __shared__ array itself, so the compiler keeps treating every derived
+// pointer as shared memory (a round trip through an integer would turn all
+// of its loads and stores into generic ones).
+__device__ __forceinline__ uint8_t* align_smem_1024(uint8_t* smem_raw) {
+  const uint32_t base = smem_u32(smem_raw);
+  return smem_raw + (((base + 1023u) & ~1023u) - base);
+}
+
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
@@ -210,6 +220,14 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8])
                : "memory");
 }
 // 32 lanes x 32 bit, 32 consecutive columns from 32 registers per thread.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
