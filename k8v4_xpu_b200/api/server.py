@@ -1,0 +1,192 @@
+"""OpenAI-compatible HTTP server (FastAPI).
+
+Endpoints: ``POST /v1/chat/completions`` and ``POST /v1/completions``
+(streaming as server-sent events, ``stream_options.include_usage`` and
+``continuous_usage_stats``), ``GET /v1/models``, ``GET /health`` and
+``GET /metrics`` (Prometheus, ``vllm:*`` names). This is the surface the
+reference's clients use against stock vLLM (``bench/serve_coding.py:27-45``,
+``launch.sh:219-232``). Decoding is greedy (the benchmark path of the
+reference); ``temperature`` is accepted and ignored, ``n`` must be 1.
+"""
+from __future__ import annotations
+
+import asyncio
+import json
+import time
+import uuid
+from typing import Any
+
+from fastapi import FastAPI, HTTPException, Request
+from fastapi.responses import JSONResponse, Response, StreamingResponse
+from prometheus_client import CONTENT_TYPE_LATEST
+from pydantic import BaseModel, Field
+
+from ..runtime.scheduler import SamplingParams
+
+
+class StreamOptions(BaseModel):
+    include_usage: bool = False
+    continuous_usage_stats: bool = False
+
+
+class _Common(BaseModel):
+    model: str | None = None
+    max_tokens: int | None = None
+    max_completion_tokens: int | None = None
+    stream: bool = False
+    stream_options: StreamOptions | None = None
+    ignore_eos: bool = False
+    stop_token_ids: list[int] = Field(default_factory=list)
+    temperature: float | None = None
+    top_p: float | None = None
+    seed: int | None = None
+    n: int = 1
+
+
+class CompletionRequest(_Common):
+    prompt: str | list[int] | list[str]
+
+
+class ChatMessage(BaseModel):
+    role: str
+    content: Any = ""
+
+
+class ChatRequest(_Common):
+    messages: list[ChatMessage]
+
+
+def _usage(prompt: int, completion: int) -> dict:
+    return {"prompt_tokens": prompt, "completion_tokens": completion, "total_tokens": prompt + completion}
+
+
+def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, metrics=None) -> FastAPI:
+    app = FastAPI(title="k8v4_xpu_b200")
+    eos = getattr(tokenizer, "eos_token_id", None)
+
+    def params_for(req: _Common, prompt_len: int) -> SamplingParams:
+        if req.n != 1:
+            raise HTTPException(400, "only n=1 is supported")
+        mt = req.max_completion_tokens or req.max_tokens or 16
+        if mt < 1:
+            raise HTTPException(400, "max_tokens must be positive")
+        if prompt_len < 1:
+            raise HTTPException(400, "empty prompt")
+        if prompt_len + mt > max_model_len:
+            raise HTTPException(400, "prompt (%d) + max_tokens (%d) exceeds max_model_len %d"
+                                % (prompt_len, mt, max_model_len))
+        stops = tuple(req.stop_token_ids) + ((eos,) if eos is not None else ())
+        return SamplingParams(max_tokens=mt, ignore_eos=req.ignore_eos, stop_token_ids=stops,
+                              temperature=float(req.temperature or 0.0))
+
+    async def run(prompt: list[int], params: SamplingParams):
+        loop = asyncio.get_running_loop()
+        out: asyncio.Queue = asyncio.Queue()
+        try:
+            h = driver.submit(prompt, params, loop, out)
+        except RuntimeError as e:
+            raise HTTPException(503, str(e))
+        return h, out
+
+    @app.get("/health")
+    async def health():
+        if not driver.healthy:
+            return JSONResponse({"status": "error", "detail": (driver.error or "engine stopped")[-2000:]},
+                                status_code=503)
+        return {"status": "ok"}
+
+    @app.get("/v1/models")
+    async def models():
+        return {"object": "list", "data": [{"id": served_model_name, "object": "model", "created": 0,
+                                            "owned_by": "k8v4_xpu_b200", "max_model_len": max_model_len}]}
+
+    @app.get("/metrics")
+    async def metrics_ep():
+        body = metrics.render() if metrics is not None else b""
+        return Response(body, media_type=CONTENT_TYPE_LATEST)
+
+    async def generate(prompt: list[int], req: _Common, chat: bool, request: Request):
+        params = params_for(req, len(prompt))
+        h, out = await run(prompt, params)
+        rid = ("chatcmpl-" if chat else "cmpl-") + uuid.uuid4().hex[:24]
+        created = int(time.time())
+        obj = "chat.completion" if chat else "text_completion"
+        opts = req.stream_options or StreamOptions()
+
+        if not req.stream:
+            toks: list[int] = []
+            reason = None
+            while True:
+                new, fin, why = await out.get()
+                toks.extend(new)
+                if fin:
+                    reason = why
+                    break
+            if reason == "error":
+                raise HTTPException(500, "engine failed")
+            text = tokenizer.decode(toks)
+            choice = ({"index": 0, "message": {"role": "assistant", "content": text}, "finish_reason": reason}
+                      if chat else {"index": 0, "text": text, "finish_reason": reason, "logprobs": None})
+            choice["token_ids"] = toks
+            return {"id": rid, "object": obj, "created": created, "model": served_model_name,
+                    "choices": [choice], "usage": _usage(len(prompt), len(toks))}
+
+        async def events():
+            n_out = 0
+            chunk_obj = "chat.completion.chunk" if chat else "text_completion"
+            if chat:
+                first = {"id": rid, "object": chunk_obj, "created": created, "model": served_model_name,
+                         "choices": [{"index": 0, "delta": {"role": "assistant", "content": ""},
+                                      "finish_reason": None}]}
+                if opts.continuous_usage_stats:
+                    first["usage"] = _usage(len(prompt), 0)
+                yield "data: %s\n\n" % json.dumps(first)
+            try:
+                while True:
+                    if await request.is_disconnected():
+                        driver.abort(h)
+                        return
+                    new, fin, why = await out.get()
+                    n_out += len(new)
+                    if new or fin:
+                        text = tokenizer.decode(new) if new else ""
+                        ch = ({"index": 0, "delta": {"content": text}, "finish_reason": why if fin else None}
+                              if chat else {"index": 0, "text": text, "finish_reason": why if fin else None,
+                                            "logprobs": None})
+                        ch["token_ids"] = list(new)
+                        body = {"id": rid, "object": chunk_obj, "created": created, "model": served_model_name,
+                                "choices": [ch]}
+                        if opts.continuous_usage_stats:
+                            body["usage"] = _usage(len(prompt), n_out)
+                        yield "data: %s\n\n" % json.dumps(body)
+                    if fin:
+                        break
+                if opts.include_usage:
+                    yield "data: %s\n\n" % json.dumps({"id": rid, "object": chunk_obj, "created": created,
+                                                       "model": served_model_name, "choices": [],
+                                                       "usage": _usage(len(prompt), n_out)})
+                yield "data: [DONE]\n\n"
+            except asyncio.CancelledError:
+                driver.abort(h)
+                raise
+
+        return StreamingResponse(events(), media_type="text/event-stream")
+
+    @app.post("/v1/completions")
+    async def completions(req: CompletionRequest, request: Request):
+        if isinstance(req.prompt, str):
+            prompt = tokenizer.encode(req.prompt)
+        elif req.prompt and isinstance(req.prompt[0], str):
+            if len(req.prompt) != 1:
+                raise HTTPException(400, "one prompt per request")
+            prompt = tokenizer.encode(req.prompt[0])
+        else:
+            prompt = [int(t) for t in req.prompt]
+        return await generate(prompt, req, False, request)
+
+    @app.post("/v1/chat/completions")
+    async def chat(req: ChatRequest, request: Request):
+        prompt = tokenizer.apply_chat_template([m.model_dump() for m in req.messages])
+        return await generate(prompt, req, True, request)
+
+    return app

@@ -1,0 +1,73 @@
+"""Tokenizers for the server.
+
+Random-init checkpoints have no vocabulary, so the default is a byte-level
+tokenizer: UTF-8 bytes map to ids 3..258 (0 = pad, 1 = bos, 2 = eos), and
+ids outside the byte range decode to ``<|id|>`` placeholders. A checkpoint
+that ships a HuggingFace tokenizer directory loads it with ``transformers``
+(offline, ``local_files_only``).
+"""
+from __future__ import annotations
+
+import os
+
+
+class ByteTokenizer:
+    OFFSET = 3
+    pad_token_id, bos_token_id, eos_token_id = 0, 1, 2
+
+    def __init__(self, vocab_size: int = 151936):
+        self.vocab_size = vocab_size
+
+    def encode(self, text: str) -> list[int]:
+        return [b + self.OFFSET for b in text.encode("utf-8")]
+
+    def decode(self, ids) -> str:
+        out = bytearray()
+        parts: list[str] = []
+        for t in ids:
+            t = int(t)
+            if self.OFFSET <= t < self.OFFSET + 256:
+                out.append(t - self.OFFSET)
+            else:
+                if out:
+                    parts.append(out.decode("utf-8", errors="replace"))
+                    out = bytearray()
+                if t not in (self.pad_token_id, self.bos_token_id, self.eos_token_id):
+                    parts.append("<|%d|>" % t)
+        if out:
+            parts.append(out.decode("utf-8", errors="replace"))
+        return "".join(parts)
+
+    def apply_chat_template(self, messages: list[dict]) -> list[int]:
+        text = "".join("<|%s|>\n%s\n" % (m.get("role", "user"), _content(m)) for m in messages)
+        return self.encode(text + "<|assistant|>\n")
+
+
+def _content(m: dict) -> str:
+    c = m.get("content", "")
+    if isinstance(c, list):  # OpenAI content parts: keep the text parts
+        return "".join(p.get("text", "") for p in c if isinstance(p, dict))
+    return str(c)
+
+
+class HFTokenizer:
+    def __init__(self, path: str):
+        from transformers import AutoTokenizer
+        self.tok = AutoTokenizer.from_pretrained(path, local_files_only=True)
+        self.eos_token_id = self.tok.eos_token_id
+
+    def encode(self, text: str) -> list[int]:
+        return list(self.tok.encode(text, add_special_tokens=False))
+
+    def decode(self, ids) -> str:
+        return self.tok.decode(list(ids), skip_special_tokens=True)
+
+    def apply_chat_template(self, messages: list[dict]) -> list[int]:
+        msgs = [{"role": m.get("role", "user"), "content": _content(m)} for m in messages]
+        return list(self.tok.apply_chat_template(msgs, add_generation_prompt=True, tokenize=True))
+
+
+def load_tokenizer(path: str | None, vocab_size: int):
+    if path and os.path.isdir(path):
+        return HFTokenizer(path)
+    return ByteTokenizer(vocab_size)

@@ -1,0 +1,152 @@
+"""``python -m k8v4_xpu_b200 serve ...``: launch the OpenAI-compatible server.
+
+The launcher equivalent of the reference's ``launch.sh`` (T1) and
+``tools/launch_tp1.py`` (T2):
+
+* ``--dry-run`` prints the resolved configuration and every rank's launch
+  (environment + argv) as JSON and exits (``launch.sh:196-200``);
+* TP x CP > 1 starts one process per GPU (RANK / LOCAL_RANK / WORLD_SIZE,
+  rendezvous on 127.0.0.1); rank 0 serves HTTP, the others mirror its steps;
+* a KV-capacity error at start-up (the pool cannot hold ``--max-model-len``)
+  is retried once at the fitted length; any other failure is reported and
+  never retried (``launch_tp1.py:15-69``).
+"""
+from __future__ import annotations
+
+import json
+import os
+import signal
+import socket
+import subprocess
+import sys
+
+from .config import ServeConfig, resolve
+
+
+def _free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def launch_plan(cfg: ServeConfig, argv: list[str], master_port: int | None = None) -> dict:
+    world = cfg.world_size
+    port = master_port or 29500
+    ranks = []
+    for r in range(world):
+        env = {"RANK": str(r), "LOCAL_RANK": str(r), "WORLD_SIZE": str(world), "MASTER_ADDR": "127.0.0.1",
+               "MASTER_PORT": str(port)} if world > 1 else {}
+        ranks.append({"rank": r, "role": "server" if r == 0 else "follower", "env": env,
+                      "argv": [sys.executable, "-m", "k8v4_xpu_b200", "serve"] + [a for a in argv if a != "--dry-run"]})
+    return {"config": cfg.to_dict(), "engine": _engine_dict(cfg), "ranks": ranks,
+            "endpoint": "http://%s:%d/v1" % (cfg.host, cfg.port)}
+
+
+def _engine_dict(cfg: ServeConfig) -> dict:
+    import dataclasses
+    d = dataclasses.asdict(cfg.engine_config())
+    d["capture_sizes"] = list(d["capture_sizes"])
+    return d
+
+
+def build_engine(cfg: ServeConfig, comm=None, rank: int = 0, device: str = "cuda"):
+    """Engine with the capacity-fit retry: only a CapacityError is retried."""
+    from .models.config import PRESETS
+    from .runtime.block_manager import CapacityError
+    from .runtime.engine import LLMEngine
+    mcfg = PRESETS.get(cfg.model)
+    if mcfg is None:
+        from .models.checkpoint import read_model_config
+        mcfg = read_model_config(cfg.checkpoint or cfg.model)
+    ecfg = cfg.engine_config(device)
+    try:
+        eng = LLMEngine(ecfg, mcfg, comm=comm, rank=rank)
+    except CapacityError as e:
+        if not cfg.fit_capacity or not e.fit_tokens:
+            raise
+        fit = (e.fit_tokens // cfg.block_size) * cfg.block_size
+        print("[k8v4] %s; retrying at max_model_len=%d" % (e, fit), file=sys.stderr, flush=True)
+        cfg.max_model_len = fit
+        ecfg = cfg.engine_config(device)
+        eng = LLMEngine(ecfg, mcfg, comm=comm, rank=rank)
+    if cfg.checkpoint:
+        from .models.checkpoint import load_checkpoint
+        load_checkpoint(eng.model, cfg.checkpoint)
+    return eng
+
+
+def run_rank(cfg: ServeConfig) -> int:
+    import torch
+    import torch.distributed as dist
+
+    from .api.driver import EngineDriver, TPControl, follower_loop
+    from .parallel.comm import TPComm, init_from_env
+    rank, world, local = init_from_env(timeout_s=600)
+    device = "cuda:%d" % local
+    comm = TPComm() if world > 1 else None
+    control = TPControl(dist.new_group(backend="gloo")) if world > 1 else None
+    eng = build_engine(cfg, comm=comm, rank=rank, device=device)
+    try:
+        if rank == 0:
+            import uvicorn
+
+            from .api.metrics import ServingMetrics
+            from .api.server import build_app
+            from .api.tokenizer import load_tokenizer
+            metrics = ServingMetrics(cfg.served_model_name or cfg.model)
+            driver = EngineDriver(eng, metrics=metrics, control=control).start()
+            app = build_app(driver, load_tokenizer(cfg.tokenizer, eng.mcfg.vocab), cfg.served_model_name or cfg.model,
+                            cfg.max_model_len, metrics)
+            uvicorn.run(app, host=cfg.host, port=cfg.port, log_level="info")
+            driver.stop()
+        else:
+            follower_loop(eng, control)
+    finally:
+        if eng.graphs is not None:
+            eng.graphs.release()
+        if eng.mtp is not None:
+            eng.mtp.release()
+        torch.cuda.synchronize()
+        if world > 1 and dist.is_initialized():
+            dist.destroy_process_group()
+    return 0
+
+
+def serve(argv: list[str]) -> int:
+    cfg = resolve(argv)
+    if cfg.dry_run:
+        print(json.dumps(launch_plan(cfg, argv), indent=2))
+        return 0
+    if cfg.world_size == 1 or "RANK" in os.environ:
+        return run_rank(cfg)
+    plan = launch_plan(cfg, argv, _free_port())
+    procs = []
+    for r in plan["ranks"]:
+        env = dict(os.environ)
+        env.update(r["env"])
+        procs.append(subprocess.Popen(r["argv"], env=env))
+
+    def forward(sig, _frame):
+        for p in procs:
+            if p.poll() is None:
+                p.send_signal(sig)
+    signal.signal(signal.SIGINT, forward)
+    signal.signal(signal.SIGTERM, forward)
+    rc = 0
+    for p in procs:
+        rc = p.wait() or rc
+    return rc
+
+
+def main(argv: list[str] | None = None) -> int:
+    argv = list(sys.argv[1:] if argv is None else argv)
+    if not argv or argv[0] in ("-h", "--help"):
+        print("usage: python -m k8v4_xpu_b200 serve [options]   (serve --help for options)")
+        return 0
+    cmd, rest = argv[0], argv[1:]
+    if cmd == "serve":
+        return serve(rest)
+    print("unknown command %r" % cmd, file=sys.stderr)
+    return 2

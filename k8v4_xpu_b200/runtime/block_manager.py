@@ -20,7 +20,15 @@ import struct
 
 
 class CapacityError(RuntimeError):
-    """Raised when the KV pool cannot hold a request (the launcher's fit signal)."""
+    """Raised when the KV pool cannot hold a request (the launcher's fit signal).
+
+    ``fit_tokens`` (when known) is the longest context the pool can hold; the
+    launcher retries at that length, and only after this error.
+    """
+
+    def __init__(self, msg: str, fit_tokens: int | None = None):
+        super().__init__(msg)
+        self.fit_tokens = fit_tokens
 
 
 def chain_hash(parent: bytes | None, tokens) -> bytes:

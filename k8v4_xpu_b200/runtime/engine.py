@@ -158,7 +158,11 @@ class LLMEngine:
             need = ((cfg.max_model_len + cfg.block_size - 1) // cfg.block_size + 1) * cfg.max_num_seqs
             blocks = max(1, min(blocks, need))
         if blocks < 1:
-            raise CapacityError("no memory left for the KV cache")
+            raise CapacityError("no memory left for the KV cache", fit_tokens=0)
+        if blocks * cfg.block_size < cfg.max_model_len:
+            fit = blocks * cfg.block_size - 2 * (1 + cfg.speculative_tokens)
+            raise CapacityError("max_model_len %d exceeds the KV cache capacity of %d tokens"
+                                % (cfg.max_model_len, blocks * cfg.block_size), fit_tokens=max(0, fit))
         self.num_blocks = blocks
         pages = blocks * (cfg.block_size // self.layout.page)
         self.kv_pool = torch.empty((n_layers, pages, page_bytes), dtype=torch.uint8, device=self.device)
@@ -171,6 +175,9 @@ class LLMEngine:
 
     def has_unfinished(self) -> bool:
         return self.scheduler.has_work()
+
+    def abort(self, seq_id: int) -> None:
+        self.scheduler.abort(seq_id)
 
     # ----------------------------------------------------------------- step
     def _build_inputs(self, sched) -> tuple[StepInputs, list]:

@@ -196,6 +196,16 @@ class Scheduler:
         self.waiting.appendleft(seq)
         self.num_preemptions += 1
 
+    def abort(self, seq_id: int) -> Sequence | None:
+        """Finish a waiting or running sequence with reason ``abort``."""
+        for seq in list(self.waiting) + list(self.running):
+            if seq.seq_id == seq_id:
+                if seq in self.waiting:
+                    self.waiting.remove(seq)
+                self.finish(seq, "abort")
+                return seq
+        return None
+
     def finish(self, seq: Sequence, reason: str) -> None:
         seq.status = SeqStatus.FINISHED
         seq.finish_reason = reason

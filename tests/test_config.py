@@ -1,0 +1,75 @@
+"""Config resolution (CLI > env > profile > defaults) and the launcher dry run (CPU)."""
+import json
+import subprocess
+import sys
+
+import pytest
+
+from k8v4_xpu_b200.config import parse_compilation, parse_speculative, resolve
+
+
+def test_defaults_match_the_reference_deployment():
+    cfg = resolve([], env={})
+    assert cfg.kv_cache_dtype == "int8_k_int4_v"
+    assert cfg.max_num_batched_tokens == 4224
+    assert cfg.max_num_seqs == 4 and cfg.enable_prefix_caching
+    assert cfg.default_capture_sizes() == (1, 2, 3, 4)
+    e = cfg.engine_config("cpu")
+    assert e.max_num_batched_tokens == 4224 and e.capture_sizes == (1, 2, 3, 4)
+
+
+def test_precedence_cli_over_env_over_profile():
+    env = {"K8V4_MAX_NUM_SEQS": "3", "K8V4_PREFIX_CACHING": "0", "K8V4_TP": "4"}
+    cfg = resolve(["--profile", "tp2"], env=env)
+    assert (cfg.tensor_parallel_size, cfg.max_num_seqs, cfg.enable_prefix_caching) == (4, 3, False)
+    cfg = resolve(["--profile", "tp2", "--max-num-seqs", "2", "-tp", "8"], env=env)
+    assert (cfg.tensor_parallel_size, cfg.max_num_seqs) == (8, 2)
+    cfg = resolve(["--profile", "tp1"], env={})
+    assert (cfg.tensor_parallel_size, cfg.max_num_seqs, cfg.enable_prefix_caching) == (1, 1, False)
+
+
+def test_speculative_and_compilation_configs():
+    assert parse_speculative("mtp/6") == 6
+    assert parse_speculative('{"method": "mtp", "num_speculative_tokens": 3}') == 3
+    assert parse_speculative("none") == 0
+    with pytest.raises(ValueError):
+        parse_speculative("eagle/3")
+    with pytest.raises(ValueError):
+        parse_speculative("mtp/12")
+    assert parse_compilation("FULL_DECODE_ONLY") == (True, ())
+    assert parse_compilation('{"cudagraph_mode": "FULL_DECODE_ONLY", "cudagraph_capture_sizes": [7, 14]}') == (
+        True, (7, 14))
+    assert parse_compilation("NONE") == (False, ())
+    cfg = resolve(["--speculative-config", "mtp/6"], env={})
+    assert cfg.default_capture_sizes() == (7, 14, 21, 28)
+    assert cfg.engine_config("cpu").capture_sizes == (1, 2, 3, 4)
+    cfg = resolve(["--speculative-config", "mtp/6", "--compilation-config",
+                   '{"cudagraph_capture_sizes": [7, 28]}'], env={})
+    assert cfg.engine_config("cpu").capture_sizes == (1, 4)
+    with pytest.raises(ValueError):
+        resolve(["--speculative-config", "mtp/6", "--compilation-config", '{"cudagraph_capture_sizes": [8]}'],
+                env={})
+    assert not resolve(["--enforce-eager"], env={}).cuda_graphs
+
+
+def test_validation_errors():
+    with pytest.raises(ValueError):
+        resolve(["--kv-cache-dtype", "fp8"], env={})
+    with pytest.raises(ValueError):
+        resolve(["-tp", "3"], env={})
+    with pytest.raises(ValueError):
+        resolve(["-tp", "8", "-cp", "2"], env={})
+    with pytest.raises(ValueError):
+        resolve(["--block-size", "24"], env={})
+
+
+def test_dry_run_prints_every_rank():
+    out = subprocess.run([sys.executable, "-m", "k8v4_xpu_b200", "serve", "--profile", "tp2", "--speculative-config",
+                          "mtp/6", "--dry-run", "--port", "8123"], capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0, out.stderr
+    plan = json.loads(out.stdout)
+    assert plan["config"]["tensor_parallel_size"] == 2 and plan["config"]["capture_sizes"] == [7, 14, 21, 28]
+    assert [r["role"] for r in plan["ranks"]] == ["server", "follower"]
+    assert plan["ranks"][1]["env"]["RANK"] == "1" and plan["ranks"][1]["env"]["MASTER_ADDR"] == "127.0.0.1"
+    assert "--dry-run" not in plan["ranks"][0]["argv"]
+    assert plan["endpoint"].endswith(":8123/v1")

@@ -1,0 +1,102 @@
+"""OpenAI-compatible server against a CPU engine stand-in (CPU)."""
+import json
+
+import pytest
+from fastapi.testclient import TestClient
+
+from fakes import FakeEngine
+from k8v4_xpu_b200.api.driver import EngineDriver
+from k8v4_xpu_b200.api.metrics import ServingMetrics
+from k8v4_xpu_b200.api.server import build_app
+from k8v4_xpu_b200.api.tokenizer import ByteTokenizer
+
+
+@pytest.fixture
+def client():
+    eng = FakeEngine(max_model_len=512)
+    metrics = ServingMetrics("tiny")
+    driver = EngineDriver(eng, metrics=metrics).start()
+    app = build_app(driver, ByteTokenizer(1000), "tiny", 512, metrics)
+    with TestClient(app) as c:
+        yield c, eng, driver
+    driver.stop()
+
+
+def test_health_models_metrics(client):
+    c, eng, driver = client
+    assert c.get("/health").json() == {"status": "ok"}
+    m = c.get("/v1/models").json()
+    assert m["data"][0]["id"] == "tiny" and m["data"][0]["max_model_len"] == 512
+    r = c.post("/v1/completions", json={"prompt": [5, 6, 7], "max_tokens": 4, "ignore_eos": True})
+    assert r.status_code == 200
+    body = c.get("/metrics").text
+    for name in ("vllm:prompt_tokens_total", "vllm:generation_tokens_total", "vllm:num_requests_running",
+                 "vllm:kv_cache_usage_perc", "vllm:time_to_first_token_seconds_bucket",
+                 "vllm:e2e_request_latency_seconds_count", "vllm:prefix_cache_queries_total"):
+        assert name in body, name
+    assert 'vllm:generation_tokens_total{model_name="tiny"} 4.0' in body
+
+
+def test_completion_tokens_and_usage(client):
+    c, *_ = client
+    r = c.post("/v1/completions", json={"prompt": [10, 11], "max_tokens": 5, "ignore_eos": True}).json()
+    assert r["choices"][0]["token_ids"] == [12, 13, 14, 15, 16]
+    assert r["choices"][0]["finish_reason"] == "length"
+    assert r["usage"] == {"prompt_tokens": 2, "completion_tokens": 5, "total_tokens": 7}
+    # text prompts go through the byte tokenizer
+    r = c.post("/v1/completions", json={"prompt": "ab", "max_tokens": 2, "ignore_eos": True}).json()
+    assert r["usage"]["prompt_tokens"] == 2
+    # stop tokens end the request early
+    r = c.post("/v1/completions", json={"prompt": [10], "max_tokens": 9, "stop_token_ids": [13]}).json()
+    assert r["choices"][0]["token_ids"] == [11, 12, 13] and r["choices"][0]["finish_reason"] == "stop"
+
+
+def test_streaming_chat_with_usage(client):
+    c, *_ = client
+    with c.stream("POST", "/v1/chat/completions",
+                  json={"messages": [{"role": "user", "content": "hi"}], "max_tokens": 6, "stream": True,
+                        "ignore_eos": True,
+                        "stream_options": {"include_usage": True, "continuous_usage_stats": True}}) as r:
+        lines = [ln for ln in r.iter_lines() if ln.startswith("data: ")]
+    assert lines[-1] == "data: [DONE]"
+    chunks = [json.loads(ln[6:]) for ln in lines[:-1]]
+    assert chunks[0]["choices"][0]["delta"]["role"] == "assistant"
+    toks = [t for ch in chunks for choice in ch["choices"] for t in choice.get("token_ids", [])]
+    assert len(toks) == 6
+    assert chunks[-1]["choices"] == [] and chunks[-1]["usage"]["completion_tokens"] == 6
+    assert all("usage" in ch for ch in chunks)  # continuous usage stats
+    fins = [choice["finish_reason"] for ch in chunks for choice in ch["choices"] if choice["finish_reason"]]
+    assert fins == ["length"]
+
+
+def test_concurrent_requests_and_limits(client):
+    c, eng, driver = client
+    import concurrent.futures as cf
+    with cf.ThreadPoolExecutor(4) as ex:
+        futs = [ex.submit(c.post, "/v1/completions",
+                          json={"prompt": list(range(100 * i, 100 * i + 20)), "max_tokens": 8, "ignore_eos": True})
+                for i in range(1, 7)]
+        outs = [f.result().json() for f in futs]
+    for i, o in enumerate(outs, 1):
+        assert o["choices"][0]["token_ids"][0] == 100 * i + 20
+    assert c.post("/v1/completions", json={"prompt": [1] * 500, "max_tokens": 20}).status_code == 400
+    assert c.post("/v1/completions", json={"prompt": [1], "max_tokens": 2, "n": 2}).status_code == 400
+    eng.blocks.check_invariants()
+    assert driver.healthy
+
+
+def test_engine_failure_turns_health_red():
+    eng = FakeEngine()
+
+    def boom():
+        raise RuntimeError("device status 0x201: mbarrier wait timed out")
+    eng.step = boom
+    driver = EngineDriver(eng).start()
+    app = build_app(driver, ByteTokenizer(1000), "tiny", 512)
+    with TestClient(app) as c:
+        r = c.post("/v1/completions", json={"prompt": [1, 2], "max_tokens": 2})
+        assert r.status_code == 500
+        h = c.get("/health")
+        assert h.status_code == 503 and "mbarrier" in h.json()["detail"]
+        assert c.post("/v1/completions", json={"prompt": [1, 2], "max_tokens": 2}).status_code == 503
+    driver.stop()
