@@ -66,8 +66,9 @@ def apply_commands(engine, cmds, seqs: dict, handles: dict | None = None) -> Non
 
 class EngineDriver:
     def __init__(self, engine, metrics=None, control: TPControl | None = None, idle_s: float = 0.05,
-                 status_every: int = 16):
+                 status_every: int = 16, watchdog=None):
         self.engine = engine
+        self.watchdog = watchdog
         self.metrics = metrics
         self.control = control
         self.idle_s = idle_s
@@ -159,6 +160,8 @@ class EngineDriver:
                 if self.control is not None:
                     cmds = self.control.exchange(cmds + ([("stop",)] if self._stop.is_set() else []))
                 apply_commands(eng, cmds, self._seqs, self._handles)
+                if self.watchdog is not None:
+                    self.watchdog.guard()  # a lost rank stops us before the next launch
                 if eng.has_unfinished():
                     finished = eng.step()
                     self.steps += 1
@@ -195,7 +198,7 @@ class DeviceStatusError(RuntimeError):
         self.status = status
 
 
-def follower_loop(engine, control: TPControl) -> None:
+def follower_loop(engine, control: TPControl, watchdog=None) -> None:
     """Ranks > 0: mirror rank 0's commands and steps until it says stop."""
     seqs: dict = {}
     while True:
@@ -203,6 +206,8 @@ def follower_loop(engine, control: TPControl) -> None:
         if any(c[0] == "stop" for c in cmds):
             return
         apply_commands(engine, cmds, seqs)
+        if watchdog is not None:
+            watchdog.guard()
         for rid in [r for r, q in seqs.items() if q.done]:
             del seqs[rid]
         if engine.has_unfinished():

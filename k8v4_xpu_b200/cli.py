@@ -88,6 +88,11 @@ def run_rank(cfg: ServeConfig) -> int:
     comm = TPComm() if world > 1 else None
     control = TPControl(dist.new_group(backend="gloo")) if world > 1 else None
     eng = build_engine(cfg, comm=comm, rank=rank, device=device)
+    watchdog = hb = None
+    if world > 1:
+        from .parallel.health import Heartbeat, Watchdog
+        hb = Heartbeat(dist.distributed_c10d._get_default_store(), rank, world).start()
+        watchdog = Watchdog(hb, timeout=float(os.environ.get("K8V4_HEARTBEAT_TIMEOUT", "30")))
     try:
         if rank == 0:
             import uvicorn
@@ -96,14 +101,16 @@ def run_rank(cfg: ServeConfig) -> int:
             from .api.server import build_app
             from .api.tokenizer import load_tokenizer
             metrics = ServingMetrics(cfg.served_model_name or cfg.model)
-            driver = EngineDriver(eng, metrics=metrics, control=control).start()
+            driver = EngineDriver(eng, metrics=metrics, control=control, watchdog=watchdog).start()
             app = build_app(driver, load_tokenizer(cfg.tokenizer, eng.mcfg.vocab), cfg.served_model_name or cfg.model,
                             cfg.max_model_len, metrics)
             uvicorn.run(app, host=cfg.host, port=cfg.port, log_level="info")
             driver.stop()
         else:
-            follower_loop(eng, control)
+            follower_loop(eng, control, watchdog)
     finally:
+        if hb is not None:
+            hb.stop()
         if eng.graphs is not None:
             eng.graphs.release()
         if eng.mtp is not None:
