@@ -50,6 +50,9 @@ int k8v4_status_misc(int clear);
 int k8v4_status_decode(int clear);
 int k8v4_status_prefill(int clear);
 int k8v4_status_sampler(int clear);
+int k8v4_status_gather(int clear);
+int k8v4_gather_dequant(const void* cache, int64_t num_pages, const int32_t* block_table, int hkv, int head,
+                        int seq_len, int out_dtype, void* k_out, void* v_out, cudaStream_t st);
 }
 
 namespace {
@@ -405,13 +408,34 @@ int64_t wq_gemm_ctas(int64_t mode, int64_t M, int64_t N, int64_t K, int64_t spli
   return k8v4_wq_gemm_ctas((int)mode, (int)M, (int)N, (int)K, (int)split);
 }
 
+// Gather + dequantize one KV head of a sequence's pages into dense [seq_len, 128] K and V.
+void gather_dequant(const at::Tensor& cache, const at::Tensor& block_table, int64_t hkv, int64_t head,
+                    int64_t seq_len, at::Tensor& k_out, at::Tensor& v_out) {
+  check_contig(cache, "cache");
+  check_contig(block_table, "block_table");
+  check_contig(k_out, "k_out");
+  check_contig(v_out, "v_out");
+  TORCH_CHECK(cache.scalar_type() == at::kByte && cache.dim() == 2 && cache.size(1) == hkv * 3232,
+              "cache: uint8 [pages, hkv * 3232] (b200 format)");
+  TORCH_CHECK(block_table.scalar_type() == at::kInt && block_table.numel() * 16 >= seq_len, "block_table int32");
+  TORCH_CHECK(k_out.scalar_type() == v_out.scalar_type() &&
+                  (k_out.scalar_type() == at::kFloat || k_out.scalar_type() == at::kBFloat16),
+              "outputs fp32 or bf16");
+  TORCH_CHECK(k_out.numel() >= seq_len * 128 && v_out.numel() >= seq_len * 128, "outputs [seq_len, 128]");
+  c10::cuda::CUDAGuard g(cache.device());
+  check_rc(k8v4_gather_dequant(cache.data_ptr(), cache.size(0), block_table.data_ptr<int32_t>(), (int)hkv, (int)head,
+                               (int)seq_len, k_out.scalar_type() == at::kFloat ? 0 : 1, k_out.data_ptr(),
+                               v_out.data_ptr(), cur_stream()),
+           "gather_dequant");
+}
+
 // Read (and optionally clear) the device status words of every kernel unit.
 int64_t status(bool clear) {
   int v = 0;
   const int c = clear ? 1 : 0;
-  int s[6] = {k8v4_status_gemm(c), k8v4_status_store(c), k8v4_status_misc(c), k8v4_status_decode(c),
-              k8v4_status_prefill(c), k8v4_status_sampler(c)};
-  for (int i = 0; i < 6; ++i)
+  int s[7] = {k8v4_status_gemm(c), k8v4_status_store(c), k8v4_status_misc(c), k8v4_status_decode(c),
+              k8v4_status_prefill(c), k8v4_status_sampler(c), k8v4_status_gather(c)};
+  for (int i = 0; i < 7; ++i)
     if (s[i]) v = s[i];
   return v;
 }
@@ -446,6 +470,9 @@ TORCH_LIBRARY(k8v4, m) {
   m.def("embed_int8(Tensor ids, Tensor codes, Tensor scales, Tensor(a!) out, int start) -> ()");
   m.def("argmax(Tensor logits, int offset, Tensor(a!) best_val, Tensor(b!) best_idx) -> ()");
   m.def("status(bool clear) -> int");
+  m.def(
+      "gather_dequant(Tensor cache, Tensor block_table, int hkv, int head, int seq_len, Tensor(a!) k_out, "
+      "Tensor(b!) v_out) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(k8v4, CUDA, m) {
@@ -460,6 +487,7 @@ TORCH_LIBRARY_IMPL(k8v4, CUDA, m) {
   m.impl("quant_rows", &quant_rows);
   m.impl("embed_int8", &embed_int8);
   m.impl("argmax", &argmax);
+  m.impl("gather_dequant", &gather_dequant);
 }
 
 TORCH_LIBRARY_IMPL(k8v4, CompositeExplicitAutograd, m) {

@@ -238,3 +238,13 @@ def argmax(logits, offset=0):
     torch.ops.k8v4.argmax(logits, int(offset), v, i)
     _count()
     return v, i
+
+
+def gather_dequant(cache, block_table, hkv: int, head: int, seq_len: int, dtype=torch.float32):
+    """Dense ``[seq_len, 128]`` K and V of one KV head from its pages (b200 format)."""
+    require()
+    k = torch.empty((seq_len, 128), dtype=dtype, device=cache.device)
+    v = torch.empty((seq_len, 128), dtype=dtype, device=cache.device)
+    torch.ops.k8v4.gather_dequant(cache, block_table.to(torch.int32).contiguous(), hkv, head, seq_len, k, v)
+    _count()
+    return k, v
