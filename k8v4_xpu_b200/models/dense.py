@@ -27,6 +27,8 @@ import torch
 from .. import ops
 from ..kv.layout import PageLayout, b200_layout
 from ..layers.linear import Int4Linear, Int8RowLinear, uses_w4a8, w4a8_enabled
+from ..obs.attn_time import attention_span
+from ..obs.stage_profile import stage
 from . import gptq
 from .config import ModelConfig, TPShape
 
@@ -187,7 +189,7 @@ class DenseModel:
         return self._all_reduce(x)
 
     def _layer(self, L: LayerWeights, x: torch.Tensor, residual: torch.Tensor | None, inp: StepInputs,
-               cache: torch.Tensor, ws, defer: bool, sync=None):
+               cache: torch.Tensor, ws, defer: bool, sync=None, tag: str = "layers"):
         """One decoder layer. ``x`` may be fp32 sums left by the previous
         layer's GEMM (split-K partials, or this rank's copy of a fused
         all-reduce, then ``sync`` says when they are complete); they are
@@ -199,51 +201,69 @@ class DenseModel:
         splitk_ws = ws.splitk if ws is not None else None
         far = self.fused_ar if (self.fused_ar is not None and self.fused_ar.fits(T, cfg.hidden)) else None
         # ---- attention block
-        if residual is None:
-            residual = x.clone()
-            h = ops.rmsnorm(x, L.input_norm, cfg.rms_eps)
-        else:
-            h = ops.rmsnorm(x, L.input_norm, cfg.rms_eps, residual=residual, sync=sync)
-        qkv = L.qkv(h, ws=splitk_ws)
+        with stage(tag + ".input_norm"):
+            if residual is None:
+                residual = x.clone()
+                h = ops.rmsnorm(x, L.input_norm, cfg.rms_eps)
+            else:
+                h = ops.rmsnorm(x, L.input_norm, cfg.rms_eps, residual=residual, sync=sync)
+        with stage(tag + ".gemm_qkv"):
+            qkv = L.qkv(h, ws=splitk_ws)
         q = torch.empty((T, hq, D), dtype=torch.bfloat16, device=self.device)
-        ops.rope_store(qkv, self.rope, inp.positions, q, inp.slots, cache, hq, hkv)
-        if inp.is_decode:
-            a = ops.decode_attn(q, inp.cu_q, inp.seq_lens, inp.block_table, cache, hkv, sh.gqa_local,
-                                inp.max_q_len, nsplit=inp.nsplit, q_ends=inp.q_ends,
-                                ws=(ws.attn if ws is not None else None))
-        else:
-            a = ops.prefill_attn(q, inp.cu_q, inp.seq_lens, inp.block_table, cache, hkv, sh.gqa_local,
-                                 inp.max_q_len)
+        with stage(tag + ".rope_store"):
+            ops.rope_store(qkv, self.rope, inp.positions, q, inp.slots, cache, hq, hkv)
+        with stage(tag + ".attn"):
+            if inp.is_decode:
+                with attention_span("decode"):
+                    a = ops.decode_attn(q, inp.cu_q, inp.seq_lens, inp.block_table, cache, hkv, sh.gqa_local,
+                                        inp.max_q_len, nsplit=inp.nsplit, q_ends=inp.q_ends,
+                                        ws=(ws.attn if ws is not None else None))
+            else:
+                with attention_span("prefill"):
+                    a = ops.prefill_attn(q, inp.cu_q, inp.seq_lens, inp.block_table, cache, hkv, sh.gqa_local,
+                                         inp.max_q_len)
         a = a.view(T, hq * D)
-        if far is not None:
-            # TP: the all-reduce runs inside the GEMM epilogue (NVLS multicast adds)
-            x, sync_o = far.gemm(L.o, 0, x=a)
-        else:
-            # single GPU: leave split-K partials for the fused norm below to finish
-            x = L.o(a, ws=splitk_ws, defer=defer)
-            self._all_reduce(x)
-            sync_o = None
+        with stage(tag + ".o_proj"):
+            if far is not None:
+                # TP: the all-reduce runs inside the GEMM epilogue (NVLS multicast adds)
+                x, sync_o = far.gemm(L.o, 0, x=a)
+            else:
+                # single GPU: leave split-K partials for the fused norm below to finish
+                x = L.o(a, ws=splitk_ws, defer=defer)
+                sync_o = None
+        if far is None:
+            with stage(tag + ".all_reduce"):
+                self._all_reduce(x)
         # ---- MLP block
         if uses_w4a8(L.gate_up.name, T, self.w4a8):
-            hq8, hs = ops.rmsnorm(x, L.post_norm, cfg.rms_eps, residual=residual, quant=True, sync=sync_o)
-            gu = L.gate_up(xq=hq8, xs=hs)
-            aq, as_ = ops.silu_mul(gu, quant=True)
-            if far is not None:
-                x, sync_d = far.gemm(L.down, 1, xq=aq, xs=as_)
-            else:
-                x = L.down(xq=aq, xs=as_)
-                self._all_reduce(x)
-                sync_d = None
+            with stage(tag + ".post_norm"):
+                hq8, hs = ops.rmsnorm(x, L.post_norm, cfg.rms_eps, residual=residual, quant=True, sync=sync_o)
+            with stage(tag + ".gate_up"):
+                gu = L.gate_up(xq=hq8, xs=hs)
+            with stage(tag + ".act"):
+                aq, as_ = ops.silu_mul(gu, quant=True)
+            with stage(tag + ".down"):
+                if far is not None:
+                    x, sync_d = far.gemm(L.down, 1, xq=aq, xs=as_)
+                else:
+                    x = L.down(xq=aq, xs=as_)
+                    sync_d = None
         else:
-            h = ops.rmsnorm(x, L.post_norm, cfg.rms_eps, residual=residual, sync=sync_o)
-            gu = L.gate_up(h, ws=splitk_ws)
-            act = ops.silu_mul(gu)
-            if far is not None:
-                x, sync_d = far.gemm(L.down, 1, x=act)
-            else:
-                x = L.down(act, ws=splitk_ws, defer=defer)
+            with stage(tag + ".post_norm"):
+                h = ops.rmsnorm(x, L.post_norm, cfg.rms_eps, residual=residual, sync=sync_o)
+            with stage(tag + ".gate_up"):
+                gu = L.gate_up(h, ws=splitk_ws)
+            with stage(tag + ".act"):
+                act = ops.silu_mul(gu)
+            with stage(tag + ".down"):
+                if far is not None:
+                    x, sync_d = far.gemm(L.down, 1, x=act)
+                else:
+                    x = L.down(act, ws=splitk_ws, defer=defer)
+                    sync_d = None
+        if far is None:
+            with stage(tag + ".all_reduce"):
                 self._all_reduce(x)
-                sync_d = None
         return x, residual, sync_d
 
     def _final_norm(self, x, residual, norm_w, rows: torch.Tensor | None, sync=None) -> torch.Tensor:
@@ -260,13 +280,15 @@ class DenseModel:
                 all_rows: bool = False) -> torch.Tensor:
         """Run every layer; returns the final-normed hidden rows ``inp.logit_rows``
         (every row with ``all_rows``, as the MTP drafter needs)."""
-        x = self.embed(inp.input_ids)
+        with stage("embed"):
+            x = self.embed(inp.input_ids)
         residual = None
         sync = None
         defer = self.tp == 1
         for li, L in enumerate(self.layers):
-            x, residual, sync = self._layer(L, x, residual, inp, kv_caches[li], ws, defer, sync)
-        return self._final_norm(x, residual, self.final_norm, None if all_rows else inp.logit_rows, sync)
+            x, residual, sync = self._layer(L, x, residual, inp, kv_caches[li], ws, defer, sync, "layers.%d" % li)
+        with stage("final_norm"):
+            return self._final_norm(x, residual, self.final_norm, None if all_rows else inp.logit_rows, sync)
 
     # ---------------------------------------------------------------- MTP
     def init_mtp(self, seed: int = 1) -> "DenseModel":
@@ -321,20 +343,22 @@ class DenseModel:
         ops.rmsnorm(hidden, M.hnorm, cfg.rms_eps, out=cat[:, H:])
         splitk_ws = ws.splitk if ws is not None else None
         x = M.eh_proj(cat, ws=splitk_ws)
-        x, residual, sync = self._layer(M.layer, x, None, inp, cache, ws, defer=self.tp == 1)
+        x, residual, sync = self._layer(M.layer, x, None, inp, cache, ws, defer=self.tp == 1, tag="mtp")
         return self._final_norm(x, residual, M.norm, None, sync)
 
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
         """Local vocab shard logits ``[rows, V/tp]`` (bf16)."""
-        q, s = ops.quant_rows(hidden)
-        return self.lm_head(q, s)
+        with stage("lm_head"):
+            q, s = ops.quant_rows(hidden)
+            return self.lm_head(q, s)
 
     def greedy(self, hidden: torch.Tensor) -> torch.Tensor:
         """Greedy token ids ``[rows]`` (int64), reduced over vocab shards."""
         lg = self.logits(hidden)
-        val, idx = ops.argmax(lg, offset=self.vocab_start)
-        if self.tp > 1:
-            val, idx = self.comm.argmax_reduce(val, idx)
+        with stage("sampler.argmax"):
+            val, idx = ops.argmax(lg, offset=self.vocab_start)
+            if self.tp > 1:
+                val, idx = self.comm.argmax_reduce(val, idx)
         return idx
 
     # ------------------------------------------------------------ reference

@@ -103,7 +103,13 @@ class MTPSpeculator:
         self.graphs: dict[int, tuple[torch.cuda.CUDAGraph, torch.Tensor]] = {}
         self.pool = None
         self.kernels: dict[int, int] = {}
-        self.topk_log = None  # optional spec.topk_log.TopKLogger
+        from .topk_log import TopKLogger
+        self.topk_log = TopKLogger.from_env()  # draft top-k logging (eager drafting, TP1)
+        if self.topk_log is not None:
+            if engine.tp > 1:
+                raise ValueError("MTP top-k logging runs at tensor parallel size 1")
+            self.use_graphs = False
+        self._topk: list = []  # (ids [B, 8], vals [B, 8]) per draft position of the current call
         self.lookahead = self.w  # KV slots past the verify window that drafting writes
 
     # ------------------------------------------------------------ forced mode
@@ -113,6 +119,17 @@ class MTPSpeculator:
         return np.cumprod(draws, axis=1).sum(axis=1).astype(np.int64)
 
     # ------------------------------------------------------------ device body
+    def _propose(self, h: torch.Tensor) -> torch.Tensor:
+        """Next draft ids from MTP hidden rows (greedy; with top-k logging the
+        drafter's top-8 of each position is kept too)."""
+        m = self.eng.model
+        if self.topk_log is None:
+            return m.greedy(h)
+        vals, ids = torch.topk(m.logits(h).float(), 8, dim=-1)
+        ids = ids + m.vocab_start
+        self._topk.append((ids, vals))
+        return ids[:, 0].contiguous()
+
     def _draft_loop(self, h: torch.Tensor, d1: torch.Tensor, base: torch.Tensor, bt: torch.Tensor,
                     write_en: torch.Tensor, nsplit: int) -> torch.Tensor:
         """Drafts 2..k: one MTP row per sequence per step. ``base`` [B] is the
@@ -131,7 +148,7 @@ class MTPSpeculator:
             inp = StepInputs(input_ids=d, positions=pos, slots=slot, cu_q=cu, seq_lens=(pos + 1).to(torch.int32),
                              block_table=bt, logit_rows=rows, max_q_len=1, is_decode=True, nsplit=nsplit)
             h = m.mtp_forward(h, d, inp, eng.kv_caches[-1], eng.ws)
-            d = m.greedy(h)
+            d = self._propose(h)
             drafts.append(d)
         return torch.stack(drafts, 1)
 
@@ -157,7 +174,7 @@ class MTPSpeculator:
         mh = m.mtp_forward(hid, catch_ids, inp, eng.kv_caches[-1], ws)
         rows = torch.arange(B, device=eng.device) * w + a
         h = mh.index_select(0, rows)
-        d1 = m.greedy(h)
+        d1 = self._propose(h)
         base = inp.positions.index_select(0, rows)
         drafts = self._draft_loop(h, d1, base, inp.block_table, ws.write_en[:B], nsplit)
         return torch.cat([t.reshape(T), a, drafts.reshape(B * k)])
@@ -206,6 +223,7 @@ class MTPSpeculator:
             self.capture()  # before staging: capture fills the buffers with benign metadata
         forced = self.forced_counts(B_real) if self.forced else None
         stage_decode_inputs(eng, sched, B, self.w, forced)
+        self._topk = []
         if self.use_graphs:
             g, out = self.graphs[B]
             g.replay()
@@ -222,8 +240,23 @@ class MTPSpeculator:
         acc = res[B * w: B * w + B]
         nd = res[B * w + B:].reshape(B, k)
         if self.topk_log is not None:
-            self.topk_log.record_step(sched, t[:B_real], acc[:B_real])
+            for i, c in enumerate(sched.chunks):
+                prev = getattr(c.seq, "draft_topk", None)
+                if prev is not None:
+                    self.topk_log.record(c.seq.seq_id, c.seq.draft, prev[0], prev[1], t[i].tolist(), int(acc[i]))
+            self.topk_log.end_step()
+            self._stash_topk([c.seq for c in sched.chunks])
         return self.commit(sched, t, acc, nd)
+
+    def _stash_topk(self, seqs) -> None:
+        """Keep each sequence's draft top-k for the next verify step's log line."""
+        if not self._topk:
+            return
+        ids = torch.stack([a for a, _ in self._topk], 1).cpu()   # [B, k, 8]
+        vals = torch.stack([b for _, b in self._topk], 1).cpu()
+        for i, seq in enumerate(seqs):
+            seq.draft_topk = (ids[i].tolist(), vals[i].tolist())
+        self._topk = []
 
     def commit(self, sched, t: np.ndarray, acc: np.ndarray, drafts: np.ndarray) -> list:
         eng = self.eng
@@ -302,7 +335,8 @@ class MTPSpeculator:
         B = len(live)
         rows = torch.tensor([row for _, row in live], dtype=torch.int64, device=eng.device)
         h = mh.index_select(0, rows)
-        d1 = m.greedy(h)
+        self._topk = []
+        d1 = self._propose(h)
         base = torch.tensor([c.start + c.num_tokens - 1 for c, _ in live], dtype=torch.int64, device=eng.device)
         tables = [eng.blocks.page_table(c.seq.seq_id) for c, _ in live]
         W = max(len(tb) for tb in tables)
@@ -317,3 +351,5 @@ class MTPSpeculator:
         eng.d2h_bytes += host.size * 8
         for i, (c, _) in enumerate(live):
             c.seq.draft = [int(x) for x in host[i]]
+        if self.topk_log is not None:
+            self._stash_topk([c.seq for c, _ in live])
