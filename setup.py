@@ -32,4 +32,8 @@ setup(
         )
     ],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+    entry_points={
+        "vllm.general_plugins": ["k8v4_int8_k_int4_v = k8v4_xpu_b200.registry:register_vllm"],
+        "console_scripts": ["k8v4-serve = k8v4_xpu_b200.cli:main", "k8v4-bake = k8v4_xpu_b200.tools.bake:main"],
+    },
 )
