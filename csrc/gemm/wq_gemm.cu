@@ -68,7 +68,12 @@ struct Cfg {
   static constexpr int B_ATOMS = (MODE == W4A16) ? BK / 64 : 1;  // 128-byte k atoms per token row
   static constexpr int B_BYTES = BT * 128 * B_ATOMS;
   static constexpr int RAW_BYTES = (MODE == W8A8) ? 0 : (BK / 8) * 128 * 4;
-  static constexpr int NWARPS = 2 + NCONV + NACC;
+  // Two MMA-issuing warps on the TMEM-A path (even / odd K groups, separate
+  // accumulator buffers): at N <= 64 one tcgen05.mma costs its issuing thread
+  // ~50 cycles regardless of N, and a second issuer overlaps that cost
+  // (measured 28 cycles per MMA aggregate with two issuers, 52 with one).
+  static constexpr int NMMA = TA ? 2 : 1;
+  static constexpr int NWARPS = 2 + NCONV + NACC + (NMMA - 1);
   static constexpr int NTHREADS = NWARPS * 32;
   static constexpr int NBUF = 4;                           // TMEM group partials in flight
   static constexpr int D_COLS = NBUF * BT;
@@ -169,7 +174,8 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
   uint64_t* acc_empty = acc_full + C::NBUF;  // accumulators -> MMA (NBUF)
   uint64_t* done_bar = acc_empty + C::NBUF;  // MMA drain on exit
   uint64_t* scale_bar = done_bar + 1;        // group-scale table loaded
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(scale_bar + 1);
+  uint64_t* done_bar2 = scale_bar + 1;       // second MMA issuer's drain
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done_bar2 + 1);
   __half* sScale = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(bars) + C::BAR_BYTES);  // [MAXG][128]
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -202,6 +208,7 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
       mbar_init(&acc_empty[s], NACC);
     }
     mbar_init(done_bar, 1);
+    mbar_init(done_bar2, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -262,12 +269,16 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
             mbar_wait_drain(&r_full[kb % RSTAGES], (kb / RSTAGES) & 1);
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == 1 || (C::NMMA > 1 && warp == C::NWARPS - 1)) {
     // ----------------------------------------------------------------- MMA
+    // issuer 0 (warp 1) takes K groups 0, 2, 4, ..., issuer 1 (the last warp)
+    // groups 1, 3, 5, ...; a group's accumulator buffer is g % NBUF, so the
+    // two never share one.
     if (lane == 0 && nkb > 0) {
+      const int issuer = (warp == 1) ? 0 : 1;
       const uint32_t idesc = (MODE == W4A16) ? idesc_bf16(128, BT) : idesc_s8(128, BT);
       bool ok = true;
-      for (int g = 0; g < ngroups && ok; ++g) {
+      for (int g = issuer; g < ngroups && ok; g += C::NMMA) {
         const int buf = g % C::NBUF;
 #ifdef K8V4_TRACE
         const uint64_t te0 = globaltimer_ns();
@@ -283,11 +294,18 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
           const int kb = g * kb_per_group + j;
           const int s = kb % C::AR, bs = kb % C::BR;
           // TMEM-A path: the converters already waited for this stage's token tile
+#ifdef K8V4_TRACE
+          const uint64_t tw0 = globaltimer_ns();
+#endif
           if (!mbar_wait(&a_full[s], (kb / C::AR) & 1, abort_flag, 104) ||
               (!C::TA && !mbar_wait(&b_full[bs], (kb / C::BR) & 1, abort_flag, 105))) {
             ok = false;
             break;
           }
+#ifdef K8V4_TRACE
+          if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && kb < 256)
+            g_gemm_trace[4 * 256 + kb] = globaltimer_ns() - tw0;
+#endif
           tc_fence_after();
           const uint32_t b_base = smem_u32(sB + bs * C::B_BYTES);
           if (C::TA) {
@@ -317,8 +335,9 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
         if (ok) mma_commit(&acc_full[buf]);
       }
       // Every MMA this thread issued must finish before TMEM is released.
-      mma_commit(done_bar);
-      mbar_wait_drain(done_bar, 0);
+      uint64_t* dbar = issuer == 0 ? done_bar : done_bar2;
+      mma_commit(dbar);
+      mbar_wait_drain(dbar, 0);
     }
   } else if (warp < 2 + NCONV) {
     // ---------------------------------------------------------- converters
