@@ -7,6 +7,7 @@
 // batched decode over every request in one launch) and adds the GEMM, norm,
 // activation, embedding and prefill-attention ops the reference took from
 // libraries.
+#include <vector>
 #include <torch/library.h>
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
@@ -51,6 +52,13 @@ int k8v4_status_decode(int clear);
 int k8v4_status_prefill(int clear);
 int k8v4_status_sampler(int clear);
 int k8v4_status_gather(int clear);
+int k8v4_prefill_attn_multi(const void* q, const int32_t* cu_q, const int32_t* seq_lens, const int32_t* block_table,
+                            int bt_stride, const void* const* caches, int nsrc, int64_t num_pages, const int32_t* q_pos,
+                            int hkv, int head_offset, int heads, int gqa, int hq_total, int nseq, int max_q_len,
+                            float sm_scale, void* out, cudaStream_t st);
+int k8v4_decode_combine_ranks(const float* ws_all, int64_t rank_floats, const int32_t* cu_q, void* out, int nrank,
+                              int nsplit, int nseq, int heads, int head_offset, int gqa, int hq_total, int max_q_len,
+                              cudaStream_t st);
 int k8v4_gather_dequant(const void* cache, int64_t num_pages, const int32_t* block_table, int hkv, int head,
                         int seq_len, int out_dtype, void* k_out, void* v_out, cudaStream_t st);
 }
@@ -429,6 +437,54 @@ void gather_dequant(const at::Tensor& cache, const at::Tensor& block_table, int6
            "gather_dequant");
 }
 
+// Context-parallel prefill: pages from several caches (this GPU's and peers'
+// mapped into this process), block-table entries (source << 24) | page, and
+// optional per-token global positions.
+void prefill_attn_cp(const at::Tensor& q, const at::Tensor& cu_q, const at::Tensor& seq_lens,
+                     const at::Tensor& block_table, at::TensorList caches, const c10::optional<at::Tensor>& q_pos,
+                     int64_t hkv, int64_t head_offset, int64_t heads, int64_t gqa, int64_t max_q_len, double sm_scale,
+                     at::Tensor& out) {
+  check_contig(q, "q");
+  check_contig(block_table, "block_table");
+  check_contig(out, "out");
+  TORCH_CHECK(!caches.empty() && caches.size() <= 8, "1 to 8 KV sources");
+  std::vector<const void*> ptrs;
+  const int64_t pages = caches[0].size(0);
+  for (const auto& c : caches) {
+    TORCH_CHECK(c.scalar_type() == at::kByte && c.dim() == 2 && c.size(1) == hkv * 3232 && c.is_contiguous(),
+                "caches: uint8 [pages, hkv * 3232]");
+    TORCH_CHECK(c.size(0) == pages, "every KV source has the same page count");
+    ptrs.push_back(c.data_ptr());
+  }
+  const int32_t* qp = nullptr;
+  if (q_pos.has_value()) {
+    check_contig(*q_pos, "q_pos");
+    TORCH_CHECK(q_pos->scalar_type() == at::kInt && q_pos->numel() == q.size(0), "q_pos int32 [T]");
+    qp = q_pos->data_ptr<int32_t>();
+  }
+  c10::cuda::CUDAGuard g(q.device());
+  check_rc(k8v4_prefill_attn_multi(q.data_ptr(), cu_q.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(),
+                                   block_table.data_ptr<int32_t>(), (int)block_table.stride(0), ptrs.data(),
+                                   (int)ptrs.size(), pages, qp, (int)hkv, (int)head_offset, (int)heads, (int)gqa,
+                                   (int)q.size(1), (int)seq_lens.numel(), (int)max_q_len, (float)sm_scale,
+                                   out.data_ptr(), cur_stream()),
+           "prefill_attn_cp");
+}
+
+// Merge every rank's split-K decode partials (all-gathered workspaces).
+void decode_combine_ranks(const at::Tensor& ws_all, int64_t rank_floats, const at::Tensor& cu_q, int64_t nrank,
+                          int64_t nsplit, int64_t heads, int64_t head_offset, int64_t gqa, int64_t max_q_len,
+                          at::Tensor& out) {
+  check_contig(ws_all, "ws_all");
+  check_contig(out, "out");
+  TORCH_CHECK(ws_all.scalar_type() == at::kFloat && ws_all.numel() >= nrank * rank_floats, "ws_all fp32");
+  c10::cuda::CUDAGuard g(out.device());
+  check_rc(k8v4_decode_combine_ranks(ws_all.data_ptr<float>(), rank_floats, cu_q.data_ptr<int32_t>(), out.data_ptr(),
+                                     (int)nrank, (int)nsplit, (int)(cu_q.numel() - 1), (int)heads, (int)head_offset,
+                                     (int)gqa, (int)out.size(1), (int)max_q_len, cur_stream()),
+           "decode_combine_ranks");
+}
+
 // Read (and optionally clear) the device status words of every kernel unit.
 int64_t status(bool clear) {
   int v = 0;
@@ -471,6 +527,12 @@ TORCH_LIBRARY(k8v4, m) {
   m.def("argmax(Tensor logits, int offset, Tensor(a!) best_val, Tensor(b!) best_idx) -> ()");
   m.def("status(bool clear) -> int");
   m.def(
+      "prefill_attn_cp(Tensor q, Tensor cu_q, Tensor seq_lens, Tensor block_table, Tensor[] caches, Tensor? q_pos, "
+      "int hkv, int head_offset, int heads, int gqa, int max_q_len, float sm_scale, Tensor(a!) out) -> ()");
+  m.def(
+      "decode_combine_ranks(Tensor ws_all, int rank_floats, Tensor cu_q, int nrank, int nsplit, int heads, "
+      "int head_offset, int gqa, int max_q_len, Tensor(a!) out) -> ()");
+  m.def(
       "gather_dequant(Tensor cache, Tensor block_table, int hkv, int head, int seq_len, Tensor(a!) k_out, "
       "Tensor(b!) v_out) -> ()");
 }
@@ -488,6 +550,8 @@ TORCH_LIBRARY_IMPL(k8v4, CUDA, m) {
   m.impl("embed_int8", &embed_int8);
   m.impl("argmax", &argmax);
   m.impl("gather_dequant", &gather_dequant);
+  m.impl("prefill_attn_cp", &prefill_attn_cp);
+  m.impl("decode_combine_ranks", &decode_combine_ranks);
 }
 
 TORCH_LIBRARY_IMPL(k8v4, CompositeExplicitAutograd, m) {

@@ -72,7 +72,10 @@ struct Cfg {
   // accumulator buffers): at N <= 64 one tcgen05.mma costs its issuing thread
   // ~50 cycles regardless of N, and a second issuer overlaps that cost
   // (measured 28 cycles per MMA aggregate with two issuers, 52 with one).
-  static constexpr int NMMA = TA ? 2 : 1;
+#ifndef K8V4_GEMM_NMMA
+#define K8V4_GEMM_NMMA 3
+#endif
+  static constexpr int NMMA = TA ? K8V4_GEMM_NMMA : 1;
   static constexpr int NWARPS = 2 + NCONV + NACC + (NMMA - 1);
   static constexpr int NTHREADS = NWARPS * 32;
   static constexpr int NBUF = 4;                           // TMEM group partials in flight
@@ -174,8 +177,8 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
   uint64_t* acc_empty = acc_full + C::NBUF;  // accumulators -> MMA (NBUF)
   uint64_t* done_bar = acc_empty + C::NBUF;  // MMA drain on exit
   uint64_t* scale_bar = done_bar + 1;        // group-scale table loaded
-  uint64_t* done_bar2 = scale_bar + 1;       // second MMA issuer's drain
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done_bar2 + 1);
+  uint64_t* done_more = scale_bar + 1;       // [NMMA-1] drains of the other MMA issuers
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done_more + C::NMMA);
   __half* sScale = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(bars) + C::BAR_BYTES);  // [MAXG][128]
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -208,7 +211,7 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
       mbar_init(&acc_empty[s], NACC);
     }
     mbar_init(done_bar, 1);
-    mbar_init(done_bar2, 1);
+    for (int i = 0; i < C::NMMA - 1; ++i) mbar_init(&done_more[i], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -269,13 +272,13 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
             mbar_wait_drain(&r_full[kb % RSTAGES], (kb / RSTAGES) & 1);
       }
     }
-  } else if (warp == 1 || (C::NMMA > 1 && warp == C::NWARPS - 1)) {
+  } else if (warp == 1 || warp >= 2 + NCONV + NACC) {
     // ----------------------------------------------------------------- MMA
-    // issuer 0 (warp 1) takes K groups 0, 2, 4, ..., issuer 1 (the last warp)
-    // groups 1, 3, 5, ...; a group's accumulator buffer is g % NBUF, so the
-    // two never share one.
+    // issuer i (warp 1, then the last NMMA-1 warps) takes K groups g with
+    // g % NMMA == i; group g accumulates into buffer g % NBUF, whose reuse
+    // waits on the accumulators whichever issuer filled it last.
     if (lane == 0 && nkb > 0) {
-      const int issuer = (warp == 1) ? 0 : 1;
+      const int issuer = (warp == 1) ? 0 : warp - (2 + NCONV + NACC) + 1;
       const uint32_t idesc = (MODE == W4A16) ? idesc_bf16(128, BT) : idesc_s8(128, BT);
       bool ok = true;
       for (int g = issuer; g < ngroups && ok; g += C::NMMA) {
@@ -335,7 +338,7 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
         if (ok) mma_commit(&acc_full[buf]);
       }
       // Every MMA this thread issued must finish before TMEM is released.
-      uint64_t* dbar = issuer == 0 ? done_bar : done_bar2;
+      uint64_t* dbar = issuer == 0 ? done_bar : &done_more[issuer - 1];
       mma_commit(dbar);
       mbar_wait_drain(dbar, 0);
     }
@@ -595,6 +598,11 @@ extern "C" int k8v4_gemm_trace(uint64_t* host, int clear) {
 
 // Tokens per CTA for a given M: small M streams weights (decode), large M
 // reuses each converted weight tile over 128 tokens (prefill).
+// converter warps of the decode (TMEM-A) configurations: teams of 4
+#ifndef K8V4_GEMM_NCONV
+#define K8V4_GEMM_NCONV 12
+#endif
+
 static int pick_bt(int mode, int M) {
   if (mode == W4A16) return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
   return M <= 32 ? 32 : 128;
@@ -629,9 +637,9 @@ static int gemm_impl(int mode, const void* w, const void* wscale, const void* x,
   if (split > 1 && !ws && !ws_mc) return 2;
   const int bt = pick_bt(mode, M);
   if (mode == W4A16) {
-    if (bt == 16) return launch_cfg<W4A16, 16, 8, 4, 4, 16, 16>(w, x, p, split, st);
-    if (bt == 32) return launch_cfg<W4A16, 32, 8, 4, 4, 12, 16>(w, x, p, split, st);
-    if (bt == 64) return launch_cfg<W4A16, 64, 8, 4, 4, 8, 8>(w, x, p, split, st);
+    if (bt == 16) return launch_cfg<W4A16, 16, K8V4_GEMM_NCONV, 4, 4, 16, 16>(w, x, p, split, st);
+    if (bt == 32) return launch_cfg<W4A16, 32, K8V4_GEMM_NCONV, 4, 4, 12, 16>(w, x, p, split, st);
+    if (bt == 64) return launch_cfg<W4A16, 64, K8V4_GEMM_NCONV, 4, 4, 8, 8>(w, x, p, split, st);
     return launch_cfg<W4A16, 128, 4, 8, 4, 8, 4>(w, x, p, split, st);
   }
   if (mode == W4A8) {

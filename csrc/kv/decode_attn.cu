@@ -520,45 +520,55 @@ __global__ void __launch_bounds__(DCfg<NPAD>::NTHREADS, 1)
 
 // Merge split partials: grid (rows, heads, seqs), 128 threads (dims). The
 // per-split weights are computed once by the block; the O loads of all splits
-// are independent, so their latencies overlap.
+// are independent, so their latencies overlap. Context parallelism adds a
+// rank dimension: split index s of the merged set is (rank s / nsplit, split
+// s % nsplit), each rank's partials `rank_stride_*` floats apart (the
+// all-gathered workspaces of every rank).
 __global__ void __launch_bounds__(128) decode_combine_kernel(const float* __restrict__ ws_o,
                                                              const float* __restrict__ ws_ml, const int32_t* cu_q,
                                                              __nv_bfloat16* out, int nsplit, int npad, int gqa,
-                                                             int hq_total, int head_offset) {
+                                                             int hq_total, int head_offset, int nrank,
+                                                             int64_t rank_stride_o, int64_t rank_stride_ml) {
   __shared__ float wsh[128];
   __shared__ float red[8];
   const int r = blockIdx.x, hl = blockIdx.y, seq = blockIdx.z, d = threadIdx.x;
   const int qb = cu_q[seq], q_len = cu_q[seq + 1] - qb;
   if (r >= q_len * gqa) return;
   const int64_t base = ((int64_t)seq * gridDim.y + hl) * nsplit;
+  const int ntot = nsplit * nrank;  // <= 128
   float m = -INFINITY, l = 0.f;
-  if (d < nsplit) {
-    m = ws_ml[((base + d) * 2) * npad + r];
-    l = ws_ml[((base + d) * 2 + 1) * npad + r];
+  if (d < ntot) {
+    const int rk = d / nsplit, sp = d % nsplit;
+    const float* ml = ws_ml + rk * rank_stride_ml;
+    m = ml[((base + sp) * 2) * npad + r];
+    l = ml[((base + sp) * 2 + 1) * npad + r];
   }
   float M = warp_max(m);
   if ((d & 31) == 0) red[d >> 5] = M;
   __syncthreads();
   M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
   const float w = (m == -INFINITY || M == -INFINITY) ? 0.f : exp2f(m - M);
-  if (d < nsplit) wsh[d] = w;
+  if (d < ntot) wsh[d] = w;
   float L = warp_sum(w * l);
   __syncthreads();
   if ((d & 31) == 0) red[4 + (d >> 5)] = L;
   __syncthreads();
   L = red[4] + red[5] + red[6] + red[7];
-  const float* o = ws_o + (base * npad + r) * D + d;
   const int64_t stride = (int64_t)npad * D;
   float acc = 0.f;
-  int s = 0;
-  for (; s + 8 <= nsplit; s += 8) {
-    float v[8];
+  for (int rk = 0; rk < nrank; ++rk) {
+    const float* o = ws_o + rk * rank_stride_o + (base * npad + r) * D + d;
+    const float* wr = wsh + rk * nsplit;
+    int s = 0;
+    for (; s + 8 <= nsplit; s += 8) {
+      float v[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = o[(s + i) * stride];
+      for (int i = 0; i < 8; ++i) v[i] = o[(s + i) * stride];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc += wsh[s + i] > 0.f ? wsh[s + i] * v[i] : 0.f;
+      for (int i = 0; i < 8; ++i) acc += wr[s + i] > 0.f ? wr[s + i] * v[i] : 0.f;
+    }
+    for (; s < nsplit; ++s) acc += wr[s] > 0.f ? wr[s] * o[s * stride] : 0.f;
   }
-  for (; s < nsplit; ++s) acc += wsh[s] > 0.f ? wsh[s] * o[s * stride] : 0.f;
   const int t = r / gqa, g = r % gqa, h = hl + head_offset;
   out[((int64_t)(qb + t) * hq_total + (int64_t)h * gqa + g) * D + d] = __float2bfloat16_rn(L > 0.f ? acc / L : 0.f);
 }
@@ -660,7 +670,25 @@ extern "C" int k8v4_decode_attn(const void* q, const int32_t* cu_q, const int32_
   else { npad = 64; rc = launch_decode<64>(tm, p, heads, nseq, st); }
   if (rc || nsplit == 1) return rc;
   decode_combine_kernel<<<dim3(rows, heads, nseq), D, 0, st>>>(ws_o, ws_ml, cu_q, reinterpret_cast<__nv_bfloat16*>(out),
-                                                               nsplit, npad, gqa, hq_total, head_offset);
+                                                               nsplit, npad, gqa, hq_total, head_offset, 1, 0, 0);
+  return cudaGetLastError() == cudaSuccess ? 0 : 11;
+}
+
+// Merge the split partials of `nrank` ranks (context parallelism): `ws_all`
+// holds every rank's decode workspace back to back, `rank_floats` apart (one
+// launch shape's partials: (m, l) first, then O, as k8v4_decode_attn lays
+// them out).
+extern "C" int k8v4_decode_combine_ranks(const float* ws_all, int64_t rank_floats, const int32_t* cu_q, void* out,
+                                         int nrank, int nsplit, int nseq, int heads, int head_offset, int gqa,
+                                         int hq_total, int max_q_len, cudaStream_t st) {
+  const int rows = max_q_len * gqa;
+  if (rows <= 0 || nseq <= 0) return 0;
+  if (rows > 64 || nrank < 1 || nsplit < 1 || nrank * nsplit > 128) return 1;
+  const int npad = rows <= 16 ? 16 : rows <= 32 ? 32 : rows <= 48 ? 48 : 64;
+  const int64_t ml_floats = (int64_t)nseq * heads * nsplit * 2 * npad;
+  decode_combine_kernel<<<dim3(rows, heads, nseq), D, 0, st>>>(
+      ws_all + ml_floats, ws_all, cu_q, reinterpret_cast<__nv_bfloat16*>(out), nsplit, npad, gqa, hq_total,
+      head_offset, nrank, rank_floats, rank_floats);
   return cudaGetLastError() == cudaSuccess ? 0 : 11;
 }
 

@@ -23,12 +23,24 @@ namespace attn {
 
 using namespace tc;
 
+constexpr int MAX_SRC = 8;  // KV page sources: this GPU plus context-parallel peers
+
+// Context parallelism: a block-table entry is (source << 24) | page, source
+// 0 .. nsrc-1 indexing `caches` (this GPU's cache or a peer's, mapped into
+// this process) and the matching TMA map. With one source the entry is the
+// page number itself.
+struct KVMaps {
+  CUtensorMap m[MAX_SRC];
+};
+
 struct PrefillParams {
   const __nv_bfloat16* q;      // [T, hq_total, D]
   const int32_t* cu_q;         // [nseq + 1]
   const int32_t* seq_lens;     // [nseq]
   const int32_t* block_table;  // [nseq, bt_stride]
-  const uint8_t* cache;
+  const int32_t* q_pos;        // optional [T] global position of each query token (CP: strided tokens)
+  const uint8_t* caches[MAX_SRC];
+  int nsrc;
   __nv_bfloat16* out;          // [T, hq_total, D]
   int bt_stride;
   int hkv, gqa, hq_total, head_offset;
@@ -51,7 +63,7 @@ struct PCfg {
 };
 
 __global__ void __launch_bounds__(320, 1)
-    prefill_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const PrefillParams p) {
+    prefill_attn_kernel(const __grid_constant__ KVMaps maps, const PrefillParams p) {
   using C = PCfg;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* sm = align_smem_1024(smem_raw);
@@ -84,9 +96,11 @@ __global__ void __launch_bounds__(320, 1)
   const int R = tq * p.gqa;
   const int seq_len = p.seq_lens[seq];
   const int ctx = seq_len - q_len;
-  const int n_keys = ctx + t0 + tq;  // keys the last token of the tile sees
+  // without positions the chunk is the sequence's last q_len tokens (bottom-right causal)
+  const int32_t* qpos = p.q_pos ? p.q_pos + qb : nullptr;
+  const int n_keys = qpos ? qpos[t0 + tq - 1] + 1 : ctx + t0 + tq;  // keys the last token of the tile sees
   const int nt = (n_keys + TILE - 1) / TILE;
-  const int full_keys = ctx + t0 + 1;  // keys every row of the tile sees
+  const int full_keys = qpos ? qpos[t0] + 1 : ctx + t0 + 1;        // keys every row of the tile sees
   const int32_t* bt = p.block_table + (int64_t)seq * p.bt_stride;
 
   if (threadIdx.x == 0) {
@@ -119,7 +133,7 @@ __global__ void __launch_bounds__(320, 1)
       const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
       const float2 a = __bfloat1622float2(h2[0]), b = __bfloat1622float2(h2[1]);
       x[0] = a.x; x[1] = a.y; x[2] = b.x; x[3] = b.y;
-      end = ctx + t + 1;
+      end = qpos ? qpos[t] + 1 : ctx + t + 1;
     }
     float amax = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
     amax = warp_max(amax);
@@ -149,7 +163,7 @@ __global__ void __launch_bounds__(320, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      prefetch_tmap(&tm_k);
+      for (int i = 0; i < p.nsrc; ++i) prefetch_tmap(&maps.m[i]);
       int issued = 0;
       for (int j = 0; j < nt; ++j) {
         const int s = j % C::STAGES;
@@ -158,9 +172,11 @@ __global__ void __launch_bounds__(320, 1)
         const int npg = min(TILE_PAGES, n_pages - pg0);
         mbar_arrive_expect_tx(&kv_full[s], npg * (K_BYTES + VS_BYTES));
         for (int i = 0; i < npg; ++i) {
-          const int64_t run = (int64_t)bt[pg0 + i] * p.hkv + h;
-          tma_load_3d(sK + s * K_TILE_BYTES + i * K_BYTES, &tm_k, &kv_full[s], 0, 0, (int)run);
-          bulk_load(sVS + s * VS_TILE_BYTES + i * VS_BYTES, p.cache + run * HEAD_BYTES + VS_OFF, VS_BYTES,
+          const uint32_t e = (uint32_t)bt[pg0 + i];
+          const int src = (int)(e >> 24) < p.nsrc ? (int)(e >> 24) : 0;  // a bad source reads source 0
+          const int64_t run = (int64_t)(e & 0xFFFFFFu) * p.hkv + h;
+          tma_load_3d(sK + s * K_TILE_BYTES + i * K_BYTES, &maps.m[src], &kv_full[s], 0, 0, (int)run);
+          bulk_load(sVS + s * VS_TILE_BYTES + i * VS_BYTES, p.caches[src] + run * HEAD_BYTES + VS_OFF, VS_BYTES,
                     &kv_full[s]);
         }
         ++issued;
@@ -392,21 +408,35 @@ extern "C" int k8v4_make_kv_tmap(void* map_out, const void* cache, int64_t num_p
 
 K8V4_STATUS_API(prefill)
 
-// Paged causal prefill over `heads` KV heads starting at head_offset.
-extern "C" int k8v4_prefill_attn(const void* q, const int32_t* cu_q, const int32_t* seq_lens,
-                                 const int32_t* block_table, int bt_stride, const void* cache, int64_t num_pages,
-                                 int hkv, int head_offset, int heads, int gqa, int hq_total, int nseq, int max_q_len,
-                                 float sm_scale, void* out, cudaStream_t st) {
+// Paged causal prefill over `heads` KV heads starting at head_offset. With
+// `nsrc` > 1 the pages come from several caches (context parallelism: this
+// GPU's and its peers', block-table entries (source << 24) | page), and
+// `q_pos` gives each query token's global position (the tokens of a rank are
+// then not contiguous). All caches share num_pages and the head layout.
+extern "C" int k8v4_prefill_attn_multi(const void* q, const int32_t* cu_q, const int32_t* seq_lens,
+                                       const int32_t* block_table, int bt_stride, const void* const* caches,
+                                       int nsrc, int64_t num_pages, const int32_t* q_pos, int hkv, int head_offset,
+                                       int heads, int gqa, int hq_total, int nseq, int max_q_len, float sm_scale,
+                                       void* out, cudaStream_t st) {
   if (nseq <= 0 || max_q_len <= 0) return 0;
   if (gqa < 1 || 128 / gqa < 1) return 1;
-  CUtensorMap tm;
-  if (k8v4_make_kv_tmap(&tm, cache, num_pages, hkv)) return 3;
+  if (nsrc < 1 || nsrc > MAX_SRC) return 2;
+  KVMaps maps;
   PrefillParams p;
+  for (int i = 0; i < nsrc; ++i) {
+    if (k8v4_make_kv_tmap(&maps.m[i], caches[i], num_pages, hkv)) return 3;
+    p.caches[i] = reinterpret_cast<const uint8_t*>(caches[i]);
+  }
+  for (int i = nsrc; i < MAX_SRC; ++i) {
+    maps.m[i] = maps.m[0];
+    p.caches[i] = p.caches[0];
+  }
+  p.nsrc = nsrc;
   p.q = reinterpret_cast<const __nv_bfloat16*>(q);
   p.cu_q = cu_q;
   p.seq_lens = seq_lens;
   p.block_table = block_table;
-  p.cache = reinterpret_cast<const uint8_t*>(cache);
+  p.q_pos = q_pos;
   p.out = reinterpret_cast<__nv_bfloat16*>(out);
   p.bt_stride = bt_stride;
   p.hkv = hkv;
@@ -421,6 +451,15 @@ extern "C" int k8v4_prefill_attn(const void* q, const int32_t* cu_q, const int32
     set = true;
   }
   dim3 grid(p.n_qtiles, heads, nseq);
-  prefill_attn_kernel<<<grid, PCfg::NTHREADS, PCfg::SMEM_BYTES, st>>>(tm, p);
+  prefill_attn_kernel<<<grid, PCfg::NTHREADS, PCfg::SMEM_BYTES, st>>>(maps, p);
   return cudaGetLastError() == cudaSuccess ? 0 : 10;
+}
+
+extern "C" int k8v4_prefill_attn(const void* q, const int32_t* cu_q, const int32_t* seq_lens,
+                                 const int32_t* block_table, int bt_stride, const void* cache, int64_t num_pages,
+                                 int hkv, int head_offset, int heads, int gqa, int hq_total, int nseq, int max_q_len,
+                                 float sm_scale, void* out, cudaStream_t st) {
+  const void* caches[1] = {cache};
+  return k8v4_prefill_attn_multi(q, cu_q, seq_lens, block_table, bt_stride, caches, 1, num_pages, nullptr, hkv,
+                                 head_offset, heads, gqa, hq_total, nseq, max_q_len, sm_scale, out, st);
 }

@@ -248,3 +248,29 @@ def gather_dequant(cache, block_table, hkv: int, head: int, seq_len: int, dtype=
     torch.ops.k8v4.gather_dequant(cache, block_table.to(torch.int32).contiguous(), hkv, head, seq_len, k, v)
     _count()
     return k, v
+
+
+def prefill_attn_cp(q, cu_q, seq_lens, block_table, caches, hkv, gqa, max_q_len, q_pos=None, out=None,
+                    head_offset=0, heads=None, sm_scale=None):
+    """Paged causal prefill reading pages from several KV caches (context
+    parallelism): entry ``(source << 24) | page`` of the block table addresses
+    ``caches[source]``; ``q_pos`` gives each query token's global position."""
+    require()
+    heads = hkv if heads is None else heads
+    if out is None:
+        out = torch.empty_like(q)
+    scale = (1.0 / math.sqrt(q.shape[-1])) if sm_scale is None else sm_scale
+    torch.ops.k8v4.prefill_attn_cp(q, cu_q, seq_lens, block_table, list(caches), q_pos, hkv, head_offset, heads, gqa,
+                                   max_q_len, float(scale), out)
+    _count()
+    return out
+
+
+def decode_combine_ranks(ws_all, rank_floats: int, cu_q, nrank: int, nsplit: int, heads: int, gqa: int,
+                         max_q_len: int, out, head_offset: int = 0):
+    """Merge the split-K partials of every context-parallel rank into ``out``."""
+    require()
+    torch.ops.k8v4.decode_combine_ranks(ws_all, int(rank_floats), cu_q, nrank, nsplit, heads, head_offset, gqa,
+                                        max_q_len, out)
+    _count()
+    return out
