@@ -115,9 +115,16 @@ def main() -> int:
     ap.add_argument("--model", default="dense-27b")
     ap.add_argument("--layers", type=int, default=None, help="debug only: fewer layers is not a valid number")
     ap.add_argument("--no-c4", action="store_true")
+    ap.add_argument("--mode", default="decode", choices=("decode", "cp", "mtp"),
+                    help="decode: the headline (128K prefill + decode c=1/c=4); cp: 262K context-parallel prefill "
+                         "cold and cached-prefix TTFT; mtp: 4 x 200K contexts, MTP6 with forced acceptance 3.0")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm()
+    if args.mode == "cp":
+        return cp_mode(args)
+    if args.mode == "mtp":
+        return mtp_mode(args)
     args.warmup = max(3, args.warmup)
 
     import numpy as np
@@ -257,6 +264,136 @@ def main() -> int:
         print(json.dumps(line), flush=True)
     if eng.graphs is not None:
         eng.graphs.release()
+    comm.barrier()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+def _emit(rank: int, line: dict) -> None:
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def cp_mode(args) -> int:
+    """262,144-token prefill with context parallelism over
+    the ranks (KV pages sharded, peer pages read inside prefill attention),
+    cold TTFT, then a request sharing the first 131,072 tokens (prefix hit)."""
+    import numpy as np
+    import torch
+
+    from k8v4_xpu_b200.models.config import PRESETS
+    from k8v4_xpu_b200.parallel.comm import TPComm, init_from_env
+    from k8v4_xpu_b200.parallel.cp import CPGroup
+    from k8v4_xpu_b200.runtime.cp_engine import CPEngine
+    from k8v4_xpu_b200.runtime.engine import EngineConfig, LLMEngine
+    from k8v4_xpu_b200.runtime.scheduler import SamplingParams
+    rank, world, local = init_from_env(timeout_s=900)
+    dev = torch.device("cuda", local)
+    ctx = 262144 if args.ctx == 128197 else args.ctx
+    shared = ctx // 2
+    mcfg = PRESETS[args.model]
+    blk = 16 * world
+    blocks = 2 * ((ctx + 64 + blk - 1) // blk) + 8
+    ecfg = EngineConfig(model=args.model, context_parallel_size=world, max_model_len=ctx + 64, max_num_seqs=2,
+                        max_num_batched_tokens=args.chunk, num_kv_blocks=blocks, layers=args.layers,
+                        device=str(dev), cuda_graphs=False)
+    comm = TPComm()
+    eng = CPEngine(ecfg, mcfg, CPGroup()) if world > 1 else LLMEngine(ecfg, mcfg)
+    rng = np.random.default_rng(0)
+    prompt = rng.integers(0, mcfg.vocab, size=ctx).tolist()
+    second = prompt[:shared] + rng.integers(0, mcfg.vocab, size=ctx - shared).tolist()
+    params = SamplingParams(max_tokens=1, ignore_eos=True)
+
+    def ttft(p):
+        torch.cuda.synchronize(dev)
+        comm.barrier()
+        seq = eng.add_request(p, params)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        w = time.perf_counter()
+        a.record()
+        while not seq.done:
+            eng.step()
+        b.record()
+        torch.cuda.synchronize(dev)
+        return comm.max_scalar(a.elapsed_time(b) / 1e3), comm.max_scalar(time.perf_counter() - w), seq
+
+    cold_dev, cold_wall, s1 = ttft(prompt)
+    hot_dev, hot_wall, s2 = ttft(second)
+    line = {"metric": "context-parallel prefill TTFT @262K (cold, 131K cached prefix), 27B K8V4",
+            "value": round(cold_dev, 3), "unit": "s", "higher_is_better": False, "n_gpus": world,
+            "parallelism": "cp%d" % world, "ctx": ctx, "cold_ttft_s": round(cold_dev, 3),
+            "cold_prefill_tok_s": round(ctx / cold_dev, 1), "cached_ttft_s": round(hot_dev, 3),
+            "cached_prefix_tokens": s2.cached_tokens, "wall": {"cold_s": round(cold_wall, 3),
+                                                               "cached_s": round(hot_wall, 3)},
+            "dtype": "bf16", "data": "synthetic (uniform-random tokens; random-init weights)"}
+    if args.layers is not None:
+        line["invalid"] = "debug run (layers=%s)" % args.layers
+    _emit(rank, line)
+    comm.barrier()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+def mtp_mode(args) -> int:
+    """4 sequences holding 200,000-token contexts, MTP with 6
+    drafts, 7-token verify under the speculative CUDA graph, acceptance forced
+    to a seeded Bernoulli chain with mean accepted length 3.0."""
+    import numpy as np
+    import torch
+
+    from k8v4_xpu_b200.models.config import PRESETS
+    from k8v4_xpu_b200.parallel.comm import TPComm, init_from_env
+    from k8v4_xpu_b200.runtime.engine import EngineConfig, LLMEngine
+    from k8v4_xpu_b200.runtime.scheduler import SamplingParams
+    rank, world, local = init_from_env(timeout_s=900)
+    dev = torch.device("cuda", local)
+    ctx = 200000 if args.ctx == 128197 else args.ctx
+    mcfg = PRESETS[args.model]
+    budget = 8 * (args.warmup + args.steps) + 64
+    blocks_per_seq = (ctx + budget + 15) // 16 + 4
+    comm = TPComm()
+    ecfg = EngineConfig(model=args.model, tensor_parallel_size=world, max_model_len=ctx + budget + 16,
+                        max_num_seqs=4, max_num_batched_tokens=args.chunk, num_kv_blocks=4 * blocks_per_seq + 8,
+                        enable_prefix_caching=False, layers=args.layers, device=str(dev), speculative_tokens=6,
+                        forced_accept_mean=3.0)
+    eng = LLMEngine(ecfg, mcfg, comm=comm, rank=rank)
+    rng = np.random.default_rng(0)
+    seq = eng.add_request(rng.integers(0, mcfg.vocab, size=ctx).tolist(),
+                          SamplingParams(max_tokens=budget, ignore_eos=True))
+    while not seq.output:
+        eng.step()
+    for _ in range(3):
+        eng.clone_sequence_private(seq)
+    for _ in range(args.warmup):
+        eng.step()
+    torch.cuda.synchronize(dev)
+    comm.barrier()
+    gen0 = eng.stats["generated_tokens"]
+    acc0 = (eng.mtp.stats.num_drafts, eng.mtp.stats.num_accepted_tokens)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        eng.step()
+    b.record()
+    torch.cuda.synchronize(dev)
+    dt = comm.max_scalar(a.elapsed_time(b) / 1e3)
+    gen = eng.stats["generated_tokens"] - gen0
+    nd = eng.mtp.stats.num_drafts - acc0[0]
+    na = eng.mtp.stats.num_accepted_tokens - acc0[1]
+    line = {"metric": "MTP6 decode tok/s, 4 x 200K contexts, forced acceptance mean 3.0, 27B K8V4",
+            "value": round(gen / dt, 2), "unit": "tok/s", "higher_is_better": True, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * dt / args.steps, 3),
+            "mean_accepted_length": round(1 + na / max(1, nd), 3), "ctx": ctx, "concurrency": 4,
+            "parallelism": "tp%d" % world, "timing": "engine steps (host scheduling included) between CUDA events",
+            "dtype": "bf16", "data": "synthetic (uniform-random tokens; random-init weights)"}
+    if args.layers is not None:
+        line["invalid"] = "debug run (layers=%s)" % args.layers
+    _emit(rank, line)
+    eng.mtp.release()
     comm.barrier()
     if world > 1:
         import torch.distributed as dist

@@ -48,6 +48,11 @@ class StepInputs:
     is_decode: bool              # every sequence has q_len <= the decode tile
     q_ends: torch.Tensor | None = None  # [T] int32 per-token visible end (MTP trees)
     nsplit: int = 1              # decode split-K factor
+    # context parallelism: global positions of this rank's rows (prefill), and
+    # this rank's own pages of every sequence with the keys they hold (decode)
+    q_pos: torch.Tensor | None = None        # [T] int32
+    cp_local_bt: torch.Tensor | None = None  # [B, W] int32
+    cp_local_lens: torch.Tensor | None = None  # [B] int32
 
 
 @dataclasses.dataclass
@@ -104,6 +109,7 @@ class DenseModel:
         self.w4a8 = w4a8_enabled()
         self.mtp = None
         self.fused_ar = None  # parallel.fused_ar.FusedAllReduce when TP runs the fused path
+        self.cp = None        # parallel.cp.CPGroup under context parallelism
 
     # ------------------------------------------------------------- weights
     def random_init(self, seed: int = 0, layers: int | None = None) -> "DenseModel":
@@ -188,8 +194,26 @@ class DenseModel:
         x = ops.embed_int8(ids, self.embed_codes, self.embed_scales, start=self.vocab_start, out=out)
         return self._all_reduce(x)
 
+    def _cp_attention(self, q: torch.Tensor, inp: StepInputs, cache: torch.Tensor, layer: int) -> torch.Tensor:
+        """Attention under context parallelism (see ``parallel.cp``)."""
+        sh, cp = self.shape, self.cp
+        hkv, gqa = sh.hkv_local, sh.gqa_local
+        if not inp.is_decode:
+            cp.sync(self.device)  # every rank's KV of this chunk is written
+            return ops.prefill_attn_cp(q, inp.cu_q, inp.seq_lens, inp.block_table, cp.layer_caches(layer), hkv, gqa,
+                                       inp.max_q_len, q_pos=inp.q_pos)
+        B = inp.cu_q.numel() - 1
+        nsplit = max(2, inp.nsplit)
+        rank_floats = ops.decode_ws_floats(B, hkv, nsplit, inp.max_q_len, gqa)
+        ws = torch.empty(rank_floats, dtype=torch.float32, device=self.device)
+        ops.decode_attn(q, inp.cu_q, inp.cp_local_lens, inp.cp_local_bt, cache, hkv, gqa, inp.max_q_len,
+                        nsplit=nsplit, ws=ws)
+        out = torch.empty_like(q)
+        return ops.decode_combine_ranks(cp.all_gather(ws), rank_floats, inp.cu_q, cp.world, nsplit, hkv, gqa,
+                                        inp.max_q_len, out)
+
     def _layer(self, L: LayerWeights, x: torch.Tensor, residual: torch.Tensor | None, inp: StepInputs,
-               cache: torch.Tensor, ws, defer: bool, sync=None, tag: str = "layers"):
+               cache: torch.Tensor, ws, defer: bool, sync=None, tag: str = "layers", layer: int = -1):
         """One decoder layer. ``x`` may be fp32 sums left by the previous
         layer's GEMM (split-K partials, or this rank's copy of a fused
         all-reduce, then ``sync`` says when they are complete); they are
@@ -213,7 +237,9 @@ class DenseModel:
         with stage(tag + ".rope_store"):
             ops.rope_store(qkv, self.rope, inp.positions, q, inp.slots, cache, hq, hkv)
         with stage(tag + ".attn"):
-            if inp.is_decode:
+            if self.cp is not None:
+                a = self._cp_attention(q, inp, cache, layer)
+            elif inp.is_decode:
                 with attention_span("decode"):
                     a = ops.decode_attn(q, inp.cu_q, inp.seq_lens, inp.block_table, cache, hkv, sh.gqa_local,
                                         inp.max_q_len, nsplit=inp.nsplit, q_ends=inp.q_ends,
@@ -286,7 +312,8 @@ class DenseModel:
         sync = None
         defer = self.tp == 1
         for li, L in enumerate(self.layers):
-            x, residual, sync = self._layer(L, x, residual, inp, kv_caches[li], ws, defer, sync, "layers.%d" % li)
+            x, residual, sync = self._layer(L, x, residual, inp, kv_caches[li], ws, defer, sync, "layers.%d" % li,
+                                            li)
         with stage("final_norm"):
             return self._final_norm(x, residual, self.final_norm, None if all_rows else inp.logit_rows, sync)
 

@@ -1,0 +1,109 @@
+"""Context parallelism (CP): the KV cache sharded by page across ranks.
+
+The reference has no context parallelism; this is the long-context mechanism
+of this framework (a KV-gather design, not ring attention):
+
+* every CP rank holds the whole model (weights replicated) and a shard of
+  every sequence's KV pages. A CP block is C pages, page j of block b on
+  rank j at physical page b, so every rank's block manager (they all run the
+  same one) agrees on where a page lives, and prefix caching works unchanged
+  across the shard map;
+* prefill: each rank runs the model on the chunk tokens whose pages it owns
+  (so its KV writes stay local), then, in every layer, all ranks synchronize
+  and the prefill attention kernel reads every page straight from its owner's
+  cache (peer memory mapped into this process, per-source TMA maps; no
+  multicast). The chunk's GEMMs are split C ways;
+* decode: every rank runs the model on the new token (replicated GEMMs); the
+  owner of the token's page writes its KV; each rank's decode attention
+  covers its own pages and the (m, l, O) split partials of all ranks are
+  all-gathered and merged, so every rank continues with the same attention
+  output.
+
+Peer caches are mapped with CUDA IPC (torch's tensor reduction over the
+process group's object all-gather); synchronization and the partial exchange
+use NCCL.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+PAGE = 16
+
+
+def entry(src: int, page: int) -> int:
+    """Block-table entry of a page on rank ``src``."""
+    return (src << 24) | page
+
+
+class CPGroup:
+    def __init__(self, group=None):
+        self.group = group if group is not None else dist.group.WORLD
+        self.rank = dist.get_rank(self.group)
+        self.world = dist.get_world_size(self.group)
+        if self.world > 8:
+            raise ValueError("context parallel size must be at most 8")
+        self._peer_pools = None
+        self._flag = None
+
+    # ----------------------------------------------------------- peer memory
+    def share_pool(self, pool: torch.Tensor) -> list[torch.Tensor]:
+        """Every rank's KV pool (``[layers, pages, page_bytes]``) as tensors of
+        this process: its own, and the peers' mapped through CUDA IPC."""
+        from torch.multiprocessing.reductions import reduce_tensor
+        handle = reduce_tensor(pool)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle, group=self.group)
+        pools = []
+        for r, (fn, args) in enumerate(handles):
+            pools.append(pool if r == self.rank else fn(*args))
+        for p in pools:
+            if p.shape != pool.shape:
+                raise RuntimeError("context-parallel ranks must allocate identical KV pools")
+        self._peer_pools = pools
+        return pools
+
+    def layer_caches(self, layer: int) -> list[torch.Tensor]:
+        return [p[layer] for p in self._peer_pools]
+
+    # ------------------------------------------------------------ collectives
+    def sync(self, device) -> None:
+        """Stream-ordered barrier: KV pages written before it are readable by every rank after it."""
+        if self._flag is None or self._flag.device != torch.device(device):
+            self._flag = torch.zeros(1, dtype=torch.float32, device=device)
+        dist.all_reduce(self._flag, group=self.group)
+
+    def all_gather(self, t: torch.Tensor) -> torch.Tensor:
+        out = torch.empty((self.world * t.numel(),), dtype=t.dtype, device=t.device)
+        dist.all_gather_into_tensor(out, t.reshape(-1).contiguous(), group=self.group)
+        return out
+
+    def sum_(self, t: torch.Tensor) -> torch.Tensor:
+        dist.all_reduce(t, group=self.group)
+        return t
+
+    # ------------------------------------------------------------- page maps
+    def owner(self, pos: int) -> int:
+        return (pos // PAGE) % self.world
+
+    def encoded_pages(self, blocks: list[int], n_tokens: int) -> list[int]:
+        """Kernel block table of a sequence: logical page i -> (i % C, blocks[i // C])."""
+        n_pages = (n_tokens + PAGE - 1) // PAGE
+        C = self.world
+        return [entry(i % C, blocks[i // C]) for i in range(n_pages)]
+
+    def local_pages(self, blocks: list[int], n_tokens: int) -> tuple[list[int], int]:
+        """This rank's pages of a sequence (physical ids, in order) and the keys they hold."""
+        C, r = self.world, self.rank
+        n_pages = (n_tokens + PAGE - 1) // PAGE
+        pages, keys = [], 0
+        for i in range(r, n_pages, C):
+            pages.append(blocks[i // C])
+            keys += min(PAGE, n_tokens - i * PAGE)
+        return pages, keys
+
+    def slot(self, blocks: list[int], pos: int) -> int:
+        """Local slot of the token at ``pos`` on its owner, -1 on the other ranks."""
+        if self.owner(pos) != self.rank:
+            return -1
+        return blocks[pos // (PAGE * self.world)] * PAGE + pos % PAGE

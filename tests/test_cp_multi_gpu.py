@@ -1,0 +1,71 @@
+"""Context-parallel serving on 2 GPUs: page-sharded KV, peer-page prefill (GPU)."""
+import os
+import socket
+import traceback
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+PROMPTS = [list(range(5, 5 + 333)), list(range(900, 900 + 70))]
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    try:
+        from k8v4_xpu_b200 import ops
+        from k8v4_xpu_b200.models.config import TINY
+        from k8v4_xpu_b200.parallel.comm import init_from_env
+        from k8v4_xpu_b200.parallel.cp import CPGroup
+        from k8v4_xpu_b200.runtime.cp_engine import CPEngine
+        from k8v4_xpu_b200.runtime.engine import EngineConfig
+        from k8v4_xpu_b200.runtime.scheduler import SamplingParams
+        init_from_env(timeout_s=120)
+        cfg = EngineConfig(model="tiny", context_parallel_size=world, max_model_len=2048, max_num_seqs=2,
+                           max_num_batched_tokens=96, num_kv_blocks=96, device="cuda:%d" % rank)
+        eng = CPEngine(cfg, TINY, CPGroup())
+        outs = eng.generate(PROMPTS, SamplingParams(max_tokens=10, ignore_eos=True))
+        torch.cuda.synchronize()
+        q.put((rank, {"outs": outs, "status": ops.status()}))
+        dist.barrier()
+    except Exception:
+        q.put((rank, {"error": traceback.format_exc()}))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_cp2_generation_matches_tp1_greedy():
+    from test_mtp_gpu import _teacher_forced_margin
+    from k8v4_xpu_b200.models.config import TINY
+    from k8v4_xpu_b200.models.dense import DenseModel
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = dict(q.get(timeout=600) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+    for r in range(2):
+        assert "error" not in out[r], out[r].get("error")
+        assert out[r]["status"] == 0
+    assert out[0]["outs"] == out[1]["outs"]
+    m = DenseModel(TINY, device="cuda:0").random_init(seed=0)
+    for p, o in zip(PROMPTS, out[0]["outs"]):
+        assert len(o) == 10
+        assert _teacher_forced_margin(m, p, o) < 0.05
