@@ -485,6 +485,25 @@ void decode_combine_ranks(const at::Tensor& ws_all, int64_t rank_floats, const a
            "decode_combine_ranks");
 }
 
+// Let kernels on the current device read and write `peer`'s memory (context
+// parallelism maps peer KV pools through CUDA IPC; the mapping alone does not
+// grant this device access). Returns false when the pair cannot peer.
+bool enable_peer_access(int64_t peer) {
+  int here = -1;
+  C10_CUDA_CHECK(cudaGetDevice(&here));
+  if (peer == here) return true;
+  int can = 0;
+  C10_CUDA_CHECK(cudaDeviceCanAccessPeer(&can, here, (int)peer));
+  if (!can) return false;
+  const cudaError_t e = cudaDeviceEnablePeerAccess((int)peer, 0);
+  if (e == cudaErrorPeerAccessAlreadyEnabled) {
+    (void)cudaGetLastError();
+    return true;
+  }
+  C10_CUDA_CHECK(e);
+  return true;
+}
+
 // Read (and optionally clear) the device status words of every kernel unit.
 int64_t status(bool clear) {
   int v = 0;
@@ -526,6 +545,7 @@ TORCH_LIBRARY(k8v4, m) {
   m.def("embed_int8(Tensor ids, Tensor codes, Tensor scales, Tensor(a!) out, int start) -> ()");
   m.def("argmax(Tensor logits, int offset, Tensor(a!) best_val, Tensor(b!) best_idx) -> ()");
   m.def("status(bool clear) -> int");
+  m.def("enable_peer_access(int peer) -> bool");
   m.def(
       "prefill_attn_cp(Tensor q, Tensor cu_q, Tensor seq_lens, Tensor block_table, Tensor[] caches, Tensor? q_pos, "
       "int hkv, int head_offset, int heads, int gqa, int max_q_len, float sm_scale, Tensor(a!) out) -> ()");
@@ -558,4 +578,5 @@ TORCH_LIBRARY_IMPL(k8v4, CompositeExplicitAutograd, m) {
   m.impl("decode_ws_floats", &decode_ws_floats);
   m.impl("wq_gemm_ctas", &wq_gemm_ctas);
   m.impl("status", &status);
+  m.impl("enable_peer_access", &enable_peer_access);
 }

@@ -274,3 +274,9 @@ def decode_combine_ranks(ws_all, rank_floats: int, cu_q, nrank: int, nsplit: int
                                         max_q_len, out)
     _count()
     return out
+
+
+def enable_peer_access(peer_device: int) -> bool:
+    """Grant the current device access to ``peer_device``'s memory."""
+    require()
+    return bool(torch.ops.k8v4.enable_peer_access(int(peer_device)))

@@ -51,6 +51,15 @@ class CPGroup:
         """Every rank's KV pool (``[layers, pages, page_bytes]``) as tensors of
         this process: its own, and the peers' mapped through CUDA IPC."""
         from torch.multiprocessing.reductions import reduce_tensor
+
+        from .. import ops
+        # kernels on this GPU read the peers' pools: grant this device access to theirs first
+        devices = [None] * self.world
+        dist.all_gather_object(devices, pool.device.index, group=self.group)
+        with torch.cuda.device(pool.device):
+            for d in devices:
+                if d != pool.device.index and not ops.enable_peer_access(d):
+                    raise RuntimeError("GPU %d cannot access GPU %d's memory (no peer path)" % (pool.device.index, d))
         handle = reduce_tensor(pool)
         handles = [None] * self.world
         dist.all_gather_object(handles, handle, group=self.group)

@@ -344,11 +344,13 @@ class LLMEngine:
         pages (so concurrent decodes read distinct memory).
         """
         child = Sequence(next(self.scheduler._ids), list(seq.prompt), seq.params, list(seq.output))
+        child.draft = list(seq.draft)
         self.blocks.tables[child.seq_id] = []
         self.blocks.keys[child.seq_id] = []
         self.blocks.ensure(child.seq_id, seq.computed)
-        src = torch.tensor(self.blocks.page_table(seq.seq_id), device=self.device)
-        dst = torch.tensor(self.blocks.page_table(child.seq_id), device=self.device)
+        n = (seq.computed + self.layout.page - 1) // self.layout.page  # pages with written KV
+        src = torch.tensor(self.blocks.page_table(seq.seq_id)[:n], device=self.device)
+        dst = torch.tensor(self.blocks.page_table(child.seq_id)[:n], device=self.device)
         for layer in self.kv_caches:
             layer.index_copy_(0, dst, layer.index_select(0, src))
         child.computed = seq.computed
