@@ -19,9 +19,9 @@ of this framework (a KV-gather design, not ring attention):
   all-gathered and merged, so every rank continues with the same attention
   output.
 
-Peer caches are mapped with CUDA IPC (torch's tensor reduction over the
-process group's object all-gather); synchronization and the partial exchange
-use NCCL.
+Every rank's KV pool lives in symmetric memory and is mapped into every
+process (torch's symmetric-memory rendezvous does the handle exchange and
+grants access); synchronization and the partial exchange use NCCL.
 """
 from __future__ import annotations
 
@@ -47,30 +47,20 @@ class CPGroup:
         self._flag = None
 
     # ----------------------------------------------------------- peer memory
-    def share_pool(self, pool: torch.Tensor) -> list[torch.Tensor]:
-        """Every rank's KV pool (``[layers, pages, page_bytes]``) as tensors of
-        this process: its own, and the peers' mapped through CUDA IPC."""
-        from torch.multiprocessing.reductions import reduce_tensor
-
-        from .. import ops
-        # kernels on this GPU read the peers' pools: grant this device access to theirs first
-        devices = [None] * self.world
-        dist.all_gather_object(devices, pool.device.index, group=self.group)
-        with torch.cuda.device(pool.device):
-            for d in devices:
-                if d != pool.device.index and not ops.enable_peer_access(d):
-                    raise RuntimeError("GPU %d cannot access GPU %d's memory (no peer path)" % (pool.device.index, d))
-        handle = reduce_tensor(pool)
-        handles = [None] * self.world
-        dist.all_gather_object(handles, handle, group=self.group)
-        pools = []
-        for r, (fn, args) in enumerate(handles):
-            pools.append(pool if r == self.rank else fn(*args))
-        for p in pools:
-            if p.shape != pool.shape:
-                raise RuntimeError("context-parallel ranks must allocate identical KV pools")
-        self._peer_pools = pools
-        return pools
+    def alloc_pool(self, shape: tuple[int, ...], device) -> torch.Tensor:
+        """This rank's KV pool in symmetric memory, with every rank's pool
+        mapped into this process (torch's symmetric-memory rendezvous grants
+        this GPU access to the peers' allocations)."""
+        import torch.distributed._symmetric_memory as symm_mem
+        pool = symm_mem.empty(*shape, dtype=torch.uint8, device=device)
+        pool.zero_()
+        h = symm_mem.rendezvous(pool, self.group.group_name)
+        self._handle = h
+        self._peer_pools = [pool if r == self.rank else h.get_buffer(r, tuple(shape), torch.uint8, 0)
+                            for r in range(self.world)]
+        torch.cuda.synchronize(device)
+        dist.barrier(group=self.group)
+        return pool
 
     def layer_caches(self, layer: int) -> list[torch.Tensor]:
         return [p[layer] for p in self._peer_pools]

@@ -58,10 +58,9 @@ class CPEngine(LLMEngine):
                                 % (cfg.max_model_len, blocks * cfg.block_size),
                                 fit_tokens=blocks * cfg.block_size - 2)
         self.num_blocks = blocks
-        self.kv_pool = torch.zeros((n_layers, blocks, page_bytes), dtype=torch.uint8, device=self.device)
+        self.kv_pool = self.cp.alloc_pool((n_layers, blocks, page_bytes), self.device)
         self.kv_caches = [self.kv_pool[i] for i in range(n_layers)]
         self.kv_capacity_tokens = blocks * cfg.block_size
-        self.cp.share_pool(self.kv_pool)
 
     # ------------------------------------------------------------- inputs
     def _build_inputs(self, sched):

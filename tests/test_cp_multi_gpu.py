@@ -20,9 +20,16 @@ def _port():
     return p
 
 
+def _log(rank, msg):
+    """Progress of a rank, flushed to a file (a stalled rank shows where it stopped)."""
+    os.makedirs("gpurun_out", exist_ok=True)
+    with open("gpurun_out/cp_rank%d.log" % rank, "a") as f:
+        f.write(msg + "\n")
+
+
 def _worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
-                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+                      LOCAL_RANK=str(rank))
     import torch.distributed as dist
     try:
         from k8v4_xpu_b200 import ops
@@ -32,15 +39,25 @@ def _worker(rank, world, port, q):
         from k8v4_xpu_b200.runtime.cp_engine import CPEngine
         from k8v4_xpu_b200.runtime.engine import EngineConfig
         from k8v4_xpu_b200.runtime.scheduler import SamplingParams
-        init_from_env(timeout_s=120)
+        init_from_env(timeout_s=60)
+        _log(rank, "init")
         cfg = EngineConfig(model="tiny", context_parallel_size=world, max_model_len=2048, max_num_seqs=2,
                            max_num_batched_tokens=96, num_kv_blocks=96, device="cuda:%d" % rank)
         eng = CPEngine(cfg, TINY, CPGroup())
-        outs = eng.generate(PROMPTS, SamplingParams(max_tokens=10, ignore_eos=True))
+        _log(rank, "engine")
+        seqs = [eng.add_request(p, SamplingParams(max_tokens=10, ignore_eos=True)) for p in PROMPTS]
+        n = 0
+        while eng.has_unfinished():
+            eng.step()
+            torch.cuda.synchronize()
+            n += 1
+            _log(rank, "step %d status %d" % (n, ops.status(clear=False)))
+        outs = [s.output for s in seqs]
         torch.cuda.synchronize()
         q.put((rank, {"outs": outs, "status": ops.status()}))
         dist.barrier()
     except Exception:
+        _log(rank, traceback.format_exc())
         q.put((rank, {"error": traceback.format_exc()}))
     finally:
         if dist.is_initialized():
@@ -58,7 +75,7 @@ def test_cp2_generation_matches_tp1_greedy():
     procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
-    out = dict(q.get(timeout=600) for _ in procs)
+    out = dict(q.get(timeout=180) for _ in procs)
     for p in procs:
         p.join(timeout=120)
     for r in range(2):
