@@ -178,6 +178,10 @@ def main() -> int:
 
     # ----------------------------------------------------------------- decode
     def decode_phase(nseq: int) -> dict:
+        # nvidia-smi needs ~1 s to start reporting: start it during the warm-up so
+        # its samples cover the timed region (median over samples under load)
+        sampler = ClockSampler(local)
+        sampler.start()
         for _ in range(args.warmup):  # through the engine; captures graphs on first use
             eng.step()
         sync_all()
@@ -186,8 +190,6 @@ def main() -> int:
         for _ in range(3):
             graph.replay()
         sync_all()
-        sampler = ClockSampler(local)
-        sampler.start()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         for _ in range(args.steps):
