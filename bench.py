@@ -376,6 +376,7 @@ def mtp_mode(args) -> int:
     comm.barrier()
     gen0 = eng.stats["generated_tokens"]
     acc0 = (eng.mtp.stats.num_drafts, eng.mtp.stats.num_accepted_tokens)
+    pos0 = list(eng.mtp.stats.accepted_per_pos)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for _ in range(args.steps):
@@ -389,7 +390,9 @@ def mtp_mode(args) -> int:
     line = {"metric": "MTP6 decode tok/s, 4 x 200K contexts, forced acceptance mean 3.0, 27B K8V4",
             "value": round(gen / dt, 2), "unit": "tok/s", "higher_is_better": True, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * dt / args.steps, 3),
-            "mean_accepted_length": round(1 + na / max(1, nd), 3), "ctx": ctx, "concurrency": 4,
+            "mean_accepted_length": round(1 + na / max(1, nd), 3), "verify_rows": nd,
+            "accepted_per_pos": [a - b for a, b in zip(eng.mtp.stats.accepted_per_pos, pos0)],
+            "ctx": ctx, "concurrency": 4,
             "parallelism": "tp%d" % world, "timing": "engine steps (host scheduling included) between CUDA events",
             "dtype": "bf16", "data": "synthetic (uniform-random tokens; random-init weights)"}
     if args.layers is not None:

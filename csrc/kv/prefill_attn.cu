@@ -11,11 +11,13 @@
 // the chunk's tokens are the last q_len tokens of the sequence.
 //
 //   S[row, key]  = Q8(int8, per-row scale) x K_tile^T      tcgen05 kind::i8
-//   softmax      : one thread per row, lazy rescale (tau 8, log2 units)
-//   O[row, dim] += P(fp16) x V_tile(fp16, MN-major)         tcgen05 kind::f16
+//   softmax      : two threads per row (64 keys each), lazy rescale (tau 8, log2 units)
+//   O[row, dim] += P(fp16, TMEM) x V_tile(fp16, MN-major)   tcgen05 kind::f16, A from TMEM
 //
-// Warp roles: 0 = TMA producer, 1 = TMEM owner + MMA issuer, 2-5 = V
-// converters, 6-9 = softmax / epilogue (thread = TMEM lane = row).
+// Warp roles: 0 = TMA producer, 1 = TMEM owner + MMA issuer, 2, 3, 12, 13 =
+// V converters, 4-11 = softmax / epilogue (lane quadrant = warp & 3, key and
+// O-column half = (warp - 4) >> 2). S and P are double-buffered in TMEM, so
+// the softmax of tile j overlaps QK(j + 1) and PV(j - 1).
 #include "attn_common.cuh"
 
 namespace k8v4 {
@@ -49,41 +51,50 @@ struct PrefillParams {
 };
 
 struct PCfg {
-  static constexpr int STAGES = 3;
-  static constexpr int NTHREADS = 320;
-  static constexpr int P_BYTES = 128 * 256;  // P fp16: 2 K-atoms of 128 rows
+  static constexpr int STAGES = 4;
+  static constexpr int NWARPS = 14;
+  static constexpr int NTHREADS = NWARPS * 32;
+  static constexpr int NCONV = 4;   // warps 2, 3, 12, 13
+  static constexpr int NSOFT = 8;   // warps 4-11: quadrant = warp & 3, key half = (warp - 4) >> 2
   static constexpr int TMEM_COLS = 512;
+  static constexpr uint32_t COL_S = 0, COL_P = 256, COL_O = 384;  // S [2 x 128], P fp16 pairs [2 x 64], O [128]
   static constexpr int OFF_K = 0;
   static constexpr int OFF_VT = OFF_K + STAGES * K_TILE_BYTES;
-  static constexpr int OFF_P = OFF_VT + 2 * VT_BYTES;
-  static constexpr int OFF_Q = OFF_P + P_BYTES;
+  static constexpr int OFF_Q = OFF_VT + 2 * VT_BYTES;
   static constexpr int OFF_VS = OFF_Q + 128 * 128;
   static constexpr int OFF_MISC = OFF_VS + STAGES * VS_TILE_BYTES;
-  static constexpr int SMEM_BYTES = 1024 + OFF_MISC + 2048;
+  static constexpr int MISC_BYTES = 5120;
+  static constexpr int SMEM_BYTES = 1024 + OFF_MISC + MISC_BYTES;
 };
+static_assert(PCfg::SMEM_BYTES <= 232448, "prefill shared memory");
+static_assert(PCfg::OFF_VS % 16 == 0 && VS_TILE_BYTES % 16 == 0, "16-byte k-scale loads");
 
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(PCfg::NTHREADS, 1)
     prefill_attn_kernel(const __grid_constant__ KVMaps maps, const PrefillParams p) {
   using C = PCfg;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* sm = align_smem_1024(smem_raw);
   uint8_t* sK = sm + C::OFF_K;
   uint8_t* sVT = sm + C::OFF_VT;
-  uint8_t* sP = sm + C::OFF_P;
   uint8_t* sQ = sm + C::OFF_Q;
   uint8_t* sVS = sm + C::OFF_VS;
   uint8_t* misc = sm + C::OFF_MISC;
   uint64_t* kv_full = reinterpret_cast<uint64_t*>(misc);
-  uint64_t* kv_empty = kv_full + C::STAGES;
-  uint64_t* s_full = kv_empty + C::STAGES;  // [2]
-  uint64_t* p_full = s_full + 2;            // [1] P tile written
-  uint64_t* v_full = p_full + 1;            // [2]
-  uint64_t* pv_empty = v_full + 2;          // [2] PV of tile j (buffer j&1) finished
-  uint64_t* done_bar = pv_empty + 2;
+  uint64_t* kv_empty = kv_full + C::STAGES;  // QK commit + converter warps + softmax warps (k scales read)
+  uint64_t* s_full = kv_empty + C::STAGES;   // [2] QK of the tile in S[b] done
+  uint64_t* s_empty = s_full + 2;            // [2] every softmax warp loaded S[b]
+  uint64_t* p_full = s_empty + 2;            // [2] P[b] written (and O rescaled)
+  uint64_t* v_full = p_full + 2;             // [2] V tile converted
+  uint64_t* pv_empty = v_full + 2;           // [2] PV that read P[b] / V[b] done
+  uint64_t* mx_full = pv_empty + 2;          // [2][4] both key halves of quadrant q published their max
+  uint64_t* l_full = mx_full + 8;            // [4] both halves published their row sum
+  uint64_t* done_bar = l_full + 4;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  float* q_scale = reinterpret_cast<float*>(misc + 256);  // [128]
-  int* row_end = reinterpret_cast<int*>(q_scale + 128);   // [128]
+  float* q_scale = reinterpret_cast<float*>(misc + 512);   // [128]
+  int* row_end = reinterpret_cast<int*>(misc + 1024);       // [128]
+  float* mx_buf = reinterpret_cast<float*>(misc + 1536);    // [2 buffers][2 halves][128 rows]
+  float* l_buf = reinterpret_cast<float*>(misc + 3584);     // [2 halves][128 rows]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = p.n_qtiles - 1 - blockIdx.x;  // longest tiles first
@@ -100,20 +111,22 @@ __global__ void __launch_bounds__(320, 1)
   const int32_t* qpos = p.q_pos ? p.q_pos + qb : nullptr;
   const int n_keys = qpos ? qpos[t0 + tq - 1] + 1 : ctx + t0 + tq;  // keys the last token of the tile sees
   const int nt = (n_keys + TILE - 1) / TILE;
-  const int full_keys = qpos ? qpos[t0] + 1 : ctx + t0 + 1;        // keys every row of the tile sees
   const int32_t* bt = p.block_table + (int64_t)seq * p.bt_stride;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1 + 4 + 4);
+      mbar_init(&kv_empty[s], 1 + C::NCONV + C::NSOFT);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
-      mbar_init(&v_full[b], 4);
+      mbar_init(&s_empty[b], C::NSOFT);
+      mbar_init(&p_full[b], C::NSOFT);
+      mbar_init(&v_full[b], C::NCONV);
       mbar_init(&pv_empty[b], 1);
     }
-    mbar_init(p_full, 4);
+    for (int i = 0; i < 8; ++i) mbar_init(&mx_full[i], 2);
+    for (int i = 0; i < 4; ++i) mbar_init(&l_full[i], 2);
     mbar_init(done_bar, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -123,7 +136,7 @@ __global__ void __launch_bounds__(320, 1)
     tmem_relinquish();
   }
   // ---- prologue: quantized query rows (A operand, K-major SW128)
-  for (int r = warp; r < 128; r += 10) {
+  for (int r = warp; r < 128; r += C::NWARPS) {
     float x[4] = {0.f, 0.f, 0.f, 0.f};
     int end = 0;
     if (r < R) {
@@ -156,8 +169,6 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  const uint32_t tm_s = tmem;         // S buffers: cols [0, 256)
-  const uint32_t tm_o = tmem + 256;   // O: cols [256, 384)
   const int n_pages = (n_keys + PAGE - 1) / PAGE;
 
   if (warp == 0) {
@@ -187,48 +198,54 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else if (warp == 1) {
     // ----------------------------------------------------------------- MMA
+    // QK(j) into S[j & 1] once the softmax loaded S of tile j - 2; PV(j - 1)
+    // with P[(j - 1) & 1] read from TMEM (TS form) once the softmax wrote it.
     if (lane == 0) {
       const uint32_t id_qk = idesc_s8(128, 128);
       const uint32_t id_pv = idesc_f16(128, 128, false, true);
       const uint32_t q_base = smem_u32(sQ);
-      const uint32_t p_base = smem_u32(sP);
       bool ok = true;
       for (int j = 0; j <= nt && ok; ++j) {
         if (j < nt) {
           const int s = j % C::STAGES, b = j & 1;
-          if (!mbar_wait(&kv_full[s], (j / C::STAGES) & 1, abort_flag, 302)) break;
+          if (!mbar_wait(&kv_full[s], (j / C::STAGES) & 1, abort_flag, 302) ||
+              (j >= 2 && !mbar_wait(&s_empty[b], ((j >> 1) - 1) & 1, abort_flag, 311)))
+            break;
           tc_fence_after();
           const uint32_t k_base = smem_u32(sK + s * K_TILE_BYTES);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma_i8(tm_s + b * 128, sdesc_sw128(q_base + kk * 32, 16, 1024), sdesc_sw128(k_base + kk * 32, 16, 1024),
-                   id_qk, kk > 0 ? 1u : 0u);
+            mma_i8(tmem + C::COL_S + b * 128, sdesc_sw128(q_base + kk * 32, 16, 1024),
+                   sdesc_sw128(k_base + kk * 32, 16, 1024), id_qk, kk > 0 ? 1u : 0u);
           mma_commit(&s_full[b]);
           mma_commit(&kv_empty[s]);
         }
         if (j >= 1) {
           const int jj = j - 1, b = jj & 1;
-          if (!mbar_wait(p_full, jj & 1, abort_flag, 303) || !mbar_wait(&v_full[b], (jj >> 1) & 1, abort_flag, 304)) {
+          if (!mbar_wait(&p_full[b], (jj >> 1) & 1, abort_flag, 303) ||
+              !mbar_wait(&v_full[b], (jj >> 1) & 1, abort_flag, 304)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t vt_base = smem_u32(sVT + b * VT_BYTES);
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint64_t ad = sdesc_sw128(p_base + (kk >> 2) * (128 * 128) + (kk & 3) * 32, 16, 1024);
-            const uint64_t bd = sdesc_sw128(vt_base + kk * 2048, VT_LBO, 1024);
-            mma_f16(tm_o, ad, bd, id_pv, (jj > 0 || kk > 0) ? 1u : 0u);
-          }
+          for (int kk = 0; kk < 8; ++kk)
+            mma_f16_ts(tmem + C::COL_O, tmem + C::COL_P + b * 64 + kk * 8,
+                       sdesc_sw128(vt_base + kk * 2048, VT_LBO, 1024), id_pv, (jj > 0 || kk > 0) ? 1u : 0u);
           mma_commit(&pv_empty[b]);
         }
       }
       mma_commit(done_bar);
       mbar_wait_drain(done_bar, 0);
     }
-  } else if (warp < 6) {
+  } else if (warp < 4 || warp >= 4 + C::NSOFT) {
     // ---------------------------------------------------------- converters
-    const int ct = threadIdx.x - 64;
+    // One item = 32 dims (one scale group) of one key: a 16-byte load of
+    // packed V and one scale feed four 16-byte stores of the fp16 tile.
+    const int cw = (warp < 4) ? warp - 2 : warp - 2 - C::NSOFT;  // 0 .. NCONV-1
+    const int ct = cw * 32 + lane;
+    constexpr int CT = C::NCONV * 32;
     for (int j = 0; j < nt; ++j) {
       const int s = j % C::STAGES, b = j & 1;
       if (!mbar_wait_all(&kv_full[s], (j / C::STAGES) & 1, abort_flag, 305)) break;
@@ -237,17 +254,21 @@ __global__ void __launch_bounds__(320, 1)
       const int nvalid = min(TILE, n_keys - j * TILE);
       const uint8_t* vs = sVS + s * VS_TILE_BYTES;
       uint8_t* vt = sVT + b * VT_BYTES;
-#pragma unroll 4
-      for (int item = ct; item < TILE * 16; item += 128) {
-        const int key = item >> 4, chunk = item & 15;
+#pragma unroll
+      for (int item = ct; item < TILE * 4; item += CT) {
+        const int key = item >> 2, grp = item & 3;
         if (key < nvalid) {
           const uint8_t* run = vs + (key >> 4) * VS_BYTES;
           const int kk = key & 15;
-          const uint32_t w = *reinterpret_cast<const uint32_t*>(run + kk * 64 + chunk * 4);
-          const __half sc = *reinterpret_cast<const __half*>(run + VSC_OFF + (kk * 4 + (chunk >> 2)) * 2);
-          v_chunk_to_f16(w, sc, vt, key, chunk);
+          const uint4 w = *reinterpret_cast<const uint4*>(run + kk * 64 + grp * 16);
+          const __half sc = *reinterpret_cast<const __half*>(run + VSC_OFF + (kk * 4 + grp) * 2);
+          v_chunk_to_f16(w.x, sc, vt, key, grp * 4);
+          v_chunk_to_f16(w.y, sc, vt, key, grp * 4 + 1);
+          v_chunk_to_f16(w.z, sc, vt, key, grp * 4 + 2);
+          v_chunk_to_f16(w.w, sc, vt, key, grp * 4 + 3);
         } else {
-          v_chunk_zero(vt, key, chunk);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) v_chunk_zero(vt, key, grp * 4 + q);
         }
       }
       fence_async_smem();
@@ -259,119 +280,158 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else {
     // ------------------------------------------------------------- softmax
-    const int quad = warp & 3;
+    // Two warps per TMEM lane quadrant: each owns 32 rows x 64 keys of every
+    // tile (scores held in registers, one pass) and 64 columns of O. The two
+    // halves of a row agree on the running max through shared memory.
+    const int quad = warp & 3, hf = (warp - 4) >> 2;
     const int row = quad * 32 + lane;
     const bool live = row < R;
-    const float qs = q_scale[row];
+    // a zero query row (scale 0) keeps finite scores: scores x qs stay 0 and masked keys -inf
+    const float qs = fmaxf(q_scale[row], 1e-30f);
     const int end = row_end[row];
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    float m_run = -INFINITY, l_run = 0.f;
+    const uint32_t tS = tmem + C::COL_S + lane_off + hf * 64;
+    const uint32_t tP = tmem + C::COL_P + lane_off + hf * 32;
+    const uint32_t tO = tmem + C::COL_O + lane_off + hf * 64;
+    float m = -INFINITY, l = 0.f;
     bool ok = true;
+    // Every softmax warp runs every iteration (the halves exchange maxima each
+    // tile); a failed wait only turns the work off.
     for (int j = 0; j < nt; ++j) {
       const int s = j % C::STAGES, b = j & 1;
-      if (!mbar_wait_all(&s_full[b], (j >> 1) & 1, abort_flag, 307) ||
-          !mbar_wait_all(&kv_full[s], (j / C::STAGES) & 1, abort_flag, 308)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const uint8_t* vs = sVS + s * VS_TILE_BYTES;
-      const int key0 = j * TILE;
-      const bool masked_tile = key0 + TILE > full_keys;
-      const uint32_t s_addr = tm_s + b * 128 + lane_off;
-      // pass 1: row max of the scaled, masked scores (TMEM is read twice
-      // instead of holding 128 scores in registers)
-      float tmax = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < TILE; c += 32) {
-        uint32_t r32[32];
-        tmem_ld32(s_addr + c, r32);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int kl = c + i;
-          const float ks = __half2float(*reinterpret_cast<const __half*>(vs + (kl >> 4) * VS_BYTES + KS_OFF + (kl & 15) * 2));
-          float v = i2f_small(r32[i]) * (qs * ks);
-          if (masked_tile && key0 + kl >= end) v = -INFINITY;
-          tmax = fmaxf(tmax, v);
-        }
-      }
-      float mn = m_run, a = 1.f;
-      if (tmax > m_run + RESCALE_TAU || (m_run == -INFINITY && tmax > -INFINITY)) {
-        mn = tmax;
-        a = (m_run == -INFINITY) ? 0.f : exp2f(m_run - mn);
-      }
-      float lsum = 0.f;
-      // P (fp16) must not overwrite the buffer PV j-1 is still reading
-      if (j >= 1 && !mbar_wait_all(&pv_empty[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, 309)) { ok = false; break; }
-      // tcgen05.ld/st are warp-collective: the warp rescales together when any
-      // of its rows needs it (rows that do not use a == 1).
-      if (__any_sync(0xffffffffu, a != 1.f && j > 0 && live)) {
+      if (ok && !mbar_wait_all(&s_full[b], (j >> 1) & 1, abort_flag, 307)) ok = false;
+      float sc[64];
+      if (ok) {
         tc_fence_after();
-        // rescale this row of O
-#pragma unroll
-        for (int c = 0; c < D; c += 8) {
-          uint32_t r8[8];
-          tmem_ld8(tm_o + lane_off + c, r8);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 8; ++i) r8[i] = __float_as_uint(__uint_as_float(r8[i]) * a);
-          tmem_st8(tm_o + lane_off + c, r8);
-        }
-        tmem_st_wait();
-      }
-      // pass 2: probabilities -> P (fp16, K-major SW128, this thread's row)
-      uint8_t* prow = sP + row * 128;
-#pragma unroll
-      for (int c = 0; c < TILE; c += 32) {
-        uint32_t r32[32];
-        tmem_ld32(s_addr + c, r32);
+        uint32_t v[32];
+        tmem_ld32(tS + b * 128, v);
         tmem_ld_wait();
 #pragma unroll
-        for (int c8 = 0; c8 < 32; c8 += 8) {
-          uint32_t w[4];
+        for (int i = 0; i < 32; ++i) sc[i] = i2f_small(v[i]);
+        tmem_ld32(tS + b * 128 + 32, v);
+        tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            float pv[2];
+        for (int i = 0; i < 32; ++i) sc[32 + i] = i2f_small(v[i]);
+        tc_fence_before();
+      }
+      __syncwarp();
+      if (ok && lane == 0) mbar_arrive(&s_empty[b]);
+      if (ok && !mbar_wait_all(&kv_full[s], (j / C::STAGES) & 1, abort_flag, 308)) ok = false;
+      const int key0 = j * TILE + hf * 64;
+      float tmax = -INFINITY;
+      if (ok) {
+        // k scales of this half: 4 pages x 16 fp16, two 16-byte loads per page
+        const uint8_t* vs = sVS + s * VS_TILE_BYTES + hf * 4 * VS_BYTES + KS_OFF;
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int kl = c + c8 + 2 * i + e;
-              const float ks = __half2float(*reinterpret_cast<const __half*>(vs + (kl >> 4) * VS_BYTES + KS_OFF + (kl & 15) * 2));
-              const float v = i2f_small(r32[c8 + 2 * i + e]) * (qs * ks);
-              const bool vis = !(masked_tile && key0 + kl >= end) && mn != -INFINITY && live;
-              pv[e] = vis ? exp2f(v - mn) : 0.f;
+        for (int pg = 0; pg < 4; ++pg) {
+#pragma unroll
+          for (int hq = 0; hq < 2; ++hq) {
+            const uint4 kw = *reinterpret_cast<const uint4*>(vs + pg * VS_BYTES + hq * 16);
+            const __half2* k2 = reinterpret_cast<const __half2*>(&kw);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 kf = __half22float2(k2[e]);
+              const int k = pg * 16 + hq * 8 + 2 * e;
+              sc[k] *= kf.x;
+              sc[k + 1] *= kf.y;
             }
-            lsum += pv[0] + pv[1];
-            __half2 h2 = __floats2half2_rn(pv[0], pv[1]);
-            w[i] = *reinterpret_cast<uint32_t*>(&h2);
           }
-          const int cc = c + c8;
-          const int atom = cc >> 6, ch = (cc & 63) >> 3;
-          *reinterpret_cast<uint4*>(prow + atom * (128 * 128) + ((ch ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
-      tc_fence_before();
-      // S buffer b and the k_scale reads are done
       __syncwarp();
-      if (lane == 0) mbar_arrive(&kv_empty[s]);
-      l_run = l_run * a + lsum;
-      m_run = mn;
-      fence_async_smem();
-      tc_fence_before();
+      if (ok && lane == 0) mbar_arrive(&kv_empty[s]);
+      if (ok) {
+        const bool full = __all_sync(0xffffffffu, end >= key0 + 64 || !live);
+        if (!full) {
+#pragma unroll
+          for (int k = 0; k < 64; ++k) sc[k] = (key0 + k < end) ? sc[k] : -INFINITY;
+        }
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int k = 0; k < 64; k += 4) {
+          mx[0] = fmaxf(mx[0], sc[k]);
+          mx[1] = fmaxf(mx[1], sc[k + 1]);
+          mx[2] = fmaxf(mx[2], sc[k + 2]);
+          mx[3] = fmaxf(mx[3], sc[k + 3]);
+        }
+        tmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * qs;
+      }
+      // publish this half's max, combine with the other half of the same rows
+      mx_buf[(b * 2 + hf) * 128 + row] = tmax;
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(&mx_full[b * 4 + quad]);
+      if (ok && !mbar_wait_all(&mx_full[b * 4 + quad], (j >> 1) & 1, abort_flag, 309)) ok = false;
+      if (ok) {
+        tmax = fmaxf(tmax, mx_buf[(b * 2 + (hf ^ 1)) * 128 + row]);
+        float alpha = 1.f;
+        if (tmax > m + RESCALE_TAU || (m == -INFINITY && tmax > -INFINITY)) {
+          alpha = (m == -INFINITY) ? 0.f : ex2_approx(m - tmax);
+          m = tmax;
+        }
+        l *= alpha;
+        // O holds PV(0..j-1) after PV(j-1): rescale this half's columns when any row of the warp moved its max
+        if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.f)) {
+          if (!mbar_wait_all(&pv_empty[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, 310)) {
+            ok = false;
+          } else {
+            tc_fence_after();
+            // 16 columns at a time: the 64 scores stay live in registers meanwhile
+#pragma unroll
+            for (int c = 0; c < 64; c += 16) {
+              uint32_t v[16];
+              tmem_ld16(tO + c, v);
+              tmem_ld_wait();
+#pragma unroll
+              for (int i = 0; i < 16; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+              tmem_st16(tO + c, v);
+            }
+          }
+        }
+        // P[b] is free once the PV of tile j-2 finished
+        if (ok && j >= 2 && !mbar_wait_all(&pv_empty[b], ((j >> 1) - 1) & 1, abort_flag, 312)) ok = false;
+        if (ok) {
+          tc_fence_after();
+          // rows with no visible key keep m = -inf: exponentiate against 0 (all p = 0)
+          const float nm = (m == -INFINITY) ? 0.f : -m;
+          float ls[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int hh = 0; hh < 64; hh += 32) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int k = 0; k < 32; k += 2) {
+              const float p0 = ex2_approx(fmaf(sc[hh + k], qs, nm));
+              const float p1 = ex2_approx(fmaf(sc[hh + k + 1], qs, nm));
+              ls[(k >> 1) & 3] += p0 + p1;
+              const __half2 hp = __floats2half2_rn(p0, p1);
+              pk[k >> 1] = *reinterpret_cast<const uint32_t*>(&hp);
+            }
+            tmem_st16(tP + b * 64 + (hh >> 1), pk);
+          }
+          l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+          tmem_st_wait();
+          tc_fence_before();
+        }
+      }
+      __syncwarp();
+      if (ok && lane == 0) mbar_arrive(&p_full[b]);
     }
     // ------------------------------------------------------------ epilogue
-    if (ok && nt > 0 && !mbar_wait_all(&pv_empty[(nt - 1) & 1], ((nt - 1) >> 1) & 1, abort_flag, 310)) ok = false;
-    if (ok) {  // warp-uniform (voted waits): every lane joins the TMEM loads
+    // each warp writes its 64 columns of its 32 rows; the row sum is the sum of both halves
+    l_buf[hf * 128 + row] = l;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&l_full[quad]);
+    if (ok && nt > 0 && !mbar_wait_all(&pv_empty[(nt - 1) & 1], ((nt - 1) >> 1) & 1, abort_flag, 313)) ok = false;
+    if (ok && !mbar_wait_all(&l_full[quad], 0, abort_flag, 314)) ok = false;
+    if (ok && nt > 0) {  // warp-uniform (voted waits): every lane joins the TMEM loads
       tc_fence_after();
+      const float lt = l + l_buf[(hf ^ 1) * 128 + row];
       const int t = t0 + (live ? row : 0) / p.gqa, g = (live ? row : 0) % p.gqa;
-      __nv_bfloat16* dst = p.out + ((int64_t)(qb + t) * p.hq_total + (int64_t)h * p.gqa + g) * D;
-      const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
+      __nv_bfloat16* dst = p.out + ((int64_t)(qb + t) * p.hq_total + (int64_t)h * p.gqa + g) * D + hf * 64;
+      const float inv_l = lt > 0.f ? 1.f / lt : 0.f;
 #pragma unroll
-      for (int c = 0; c < D; c += 32) {
+      for (int c = 0; c < 64; c += 32) {
         uint32_t r32[32];
-        tmem_ld32(tm_o + lane_off + c, r32);
+        tmem_ld32(tO + c, r32);
         tmem_ld_wait();
 #pragma unroll
         for (int i = 0; i < 32; i += 8) {

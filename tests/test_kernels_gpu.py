@@ -148,7 +148,7 @@ def test_gemm_residual():
 
 
 # ---------------------------------------------------------------- attention
-def _paged_setup(lens, hkv, gqa, seed, q_lens=None, pages_extra=3):
+def _paged_setup(lens, hkv, gqa, seed, q_lens=None, pages_extra=3, k_ramp=0.0):
     layout = b200_layout(hkv, gqa)
     g = _gen(seed)
     D = 128
@@ -165,7 +165,10 @@ def _paged_setup(lens, hkv, gqa, seed, q_lens=None, pages_extra=3):
         pages = perm[off:off + np_]
         off += np_
         bt[i, :np_] = pages.to(torch.int32)
-        k = torch.randn(n, hkv, D, generator=g).bfloat16()
+        k = torch.randn(n, hkv, D, generator=g)
+        if k_ramp:  # keys grow along the sequence: the running max keeps moving
+            k = k * (1.0 + k_ramp * torch.arange(n).view(n, 1, 1) / max(1, n))
+        k = k.bfloat16()
         v = torch.randn(n, hkv, D, generator=g).bfloat16()
         slots = (pages.repeat_interleave(16) * 16 + torch.arange(16).repeat(np_))[:n].to(torch.int64)
         store_tokens(cache, slots, k, v, layout)
@@ -210,6 +213,34 @@ def test_prefill_attn(ctx, q_len, gqa, hkv):
     layout, cache, bt, seqs = _paged_setup(lens, hkv, gqa, 13, q_lens)
     ref = _reference(layout, cache, seqs, lens, q_lens)
     q = torch.cat([s[0] for s in seqs], 0).to(DEV)
+    cu = torch.tensor([0, q_len, 2 * q_len], dtype=torch.int32, device=DEV)
+    out = ops.prefill_attn(q, cu, torch.tensor(lens, dtype=torch.int32, device=DEV), bt.to(DEV), cache.to(DEV),
+                           hkv, gqa, q_len)
+    torch.cuda.synchronize()
+    st = ops.status()
+    assert st == 0, "device status 0x%x (code | site<<8)" % st
+    err = (out.float().cpu() - ref).abs().max().item()
+    assert err < 2e-2, err
+
+
+@pytest.mark.parametrize("ctx,q_len", [(700, 40), (1500, 130)])
+def test_prefill_attn_sharp_rescale(ctx, q_len):
+    """Large logits that grow along the sequence (several online-softmax
+    rescales per row). Query rows are exact int8 x 2^-5 values holding a 127,
+    so the kernel's per-row query quantization is lossless and the reference
+    can be tight."""
+    gqa, hkv = 6, 4
+    lens = [ctx + q_len, ctx // 3 + q_len]
+    q_lens = [q_len, q_len]
+    layout, cache, bt, seqs = _paged_setup(lens, hkv, gqa, 14, q_lens, k_ramp=2.0)
+    g = _gen(15)
+    sharp = []
+    for q, pages in seqs:
+        qi = torch.randint(-127, 128, q.shape, generator=g).float()
+        qi[..., 0] = 127.0
+        sharp.append(((qi / 32.0).bfloat16(), pages))
+    ref = _reference(layout, cache, sharp, lens, q_lens)
+    q = torch.cat([s[0] for s in sharp], 0).to(DEV)
     cu = torch.tensor([0, q_len, 2 * q_len], dtype=torch.int32, device=DEV)
     out = ops.prefill_attn(q, cu, torch.tensor(lens, dtype=torch.int32, device=DEV), bt.to(DEV), cache.to(DEV),
                            hkv, gqa, q_len)
