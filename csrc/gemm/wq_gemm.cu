@@ -140,7 +140,9 @@ __device__ __forceinline__ float i2f_small(uint32_t v) {
 
 #ifdef K8V4_TRACE
 // Timeline of CTA (0,0,0) for pipeline studies (trace builds only):
-// row 0 producer issue, 1 converter done, 2 MMA issued, 3 accumulate done.
+// row 0 producer issue, 1 converter done, 2 MMA issued, 3 accumulate done,
+// 4 MMA wait for the converted stage (ns), 5 converter past its waits,
+// 6 MMA wait for a free accumulator buffer (ns), 7 converter stores issued.
 __device__ uint64_t g_gemm_trace[8 * 256];
 #define K8V4_TRACE_EVENT(row, idx)                                                        \
   do {                                                                                    \
@@ -357,6 +359,7 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
         const int rs = kb % RSTAGES, ts = kb % C::AR;
         if (!mbar_wait_all(&r_full[rs], (kb / RSTAGES) & 1, abort_flag, 110)) break;
         if (kb >= C::AR && !mbar_wait_all(&a_empty[ts], ((kb / C::AR) - 1) & 1, abort_flag, 111)) break;
+        if (quad == 0 && lane == 0) K8V4_TRACE_EVENT(5, kb);
         const uint32_t* raw = reinterpret_cast<const uint32_t*>(sR + rs * C::RAW_BYTES);
         const uint32_t dst = lane_base + ts * C::A_COLS;
 #pragma unroll
@@ -374,6 +377,7 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
           if (half == 0) tc_fence_after();  // the MMA that read this TMEM stage has completed
           tmem_st32(dst + half * 32, v);
         }
+        if (quad == 0 && lane == 0) K8V4_TRACE_EVENT(7, kb);
         tmem_st_wait();
         tc_fence_before();
         // the MMA waits only on a_full: hand over once the token tile landed too

@@ -83,6 +83,7 @@ class SpecStats:
 
 
 class MTPSpeculator:
+    _GOLDEN = 0.6180339887498949  # fractional part of the golden ratio
     def __init__(self, engine, k: int, forced_accept_mean: float | None = None, seed: int = 0):
         if k < 1:
             raise ValueError("MTP needs at least one draft token")
@@ -92,6 +93,8 @@ class MTPSpeculator:
         self.forced = forced_accept_mean is not None
         self.p = forced_accept_prob(forced_accept_mean, k) if self.forced else None
         self.rng = np.random.default_rng(seed)
+        self._u0 = float(self.rng.random())  # forced mode: start of the golden-ratio sequence
+        self._n = 0
         self.stats = SpecStats(k)
         self.use_graphs = engine.cfg.cuda_graphs
         cfg = engine.cfg
@@ -114,9 +117,19 @@ class MTPSpeculator:
 
     # ------------------------------------------------------------ forced mode
     def forced_counts(self, n: int) -> np.ndarray:
-        """Accepted-draft counts of ``n`` sequences for one step (seeded chain)."""
-        draws = self.rng.random((n, self.k)) < self.p
-        return np.cumprod(draws, axis=1).sum(axis=1).astype(np.int64)
+        """Accepted-draft counts of ``n`` sequences for one step.
+
+        The count has the Bernoulli chain's distribution (``P(count >= i) =
+        p^i``), drawn by inverting that tail at a quasi-random uniform ``u``
+        (the additive golden-ratio sequence from a seeded start): ``count =
+        #{i <= k : u < p^i}``. The sequence fills [0, 1) evenly, so the
+        realized mean over a benchmark's few hundred rows sits on the
+        configured mean instead of drifting by the sampling noise of
+        independent draws."""
+        u = (self._u0 + self._GOLDEN * (self._n + np.arange(n))) % 1.0
+        self._n += n
+        tails = self.p ** np.arange(1, self.k + 1)
+        return (u[:, None] < tails[None, :]).sum(axis=1).astype(np.int64)
 
     # ------------------------------------------------------------ device body
     def _propose(self, h: torch.Tensor) -> torch.Tensor:

@@ -105,6 +105,26 @@ def test_w4a16_gemm(M, split):
     assert err <= 2e-2 * ref.abs().max().item() + 1e-3, err
 
 
+@pytest.mark.parametrize("M", [1, 5, 16, 32])
+@pytest.mark.parametrize("split", [1, 4])
+def test_w4a16_decode_precision(M, split):
+    """Decode tile sizes (int8 MMAs on two activation limbs): within bf16
+    output rounding of the fp32 reference, with activation outliers."""
+    N, K = 256, 5120
+    qw, sc = _int4_weights(N, K, 30)
+    x = torch.randn(M, K, generator=_gen(31))
+    x[:, 7] = 60.0   # an outlier 60x the typical value sets each row's fixed-point step
+    x[0, 100] = -1e-3
+    x = x.bfloat16()
+    ref = gptq.w4a16_ref(x, qw, sc)
+    out = ops.wq_gemm(ops.W4A16, qw.to(DEV), sc.to(DEV), x.to(DEV), split=split)
+    torch.cuda.synchronize()
+    st = ops.status()
+    assert st == 0, "device status 0x%x (code | site<<8)" % st
+    err = (out.float().cpu() - ref).abs().max().item()
+    assert err <= 4e-3 * ref.abs().max().item() + 1e-4, err
+
+
 @pytest.mark.parametrize("M", [1, 28, 130, 300])
 def test_w4a8_gemm(M):
     N, K = 256, 1280
