@@ -26,8 +26,10 @@ int k8v4_decode_attn(const void* q, const int32_t* cu_q, const int32_t* seq_lens
                      float sm_scale, void* out, float* ws_o, float* ws_ml, cudaStream_t st);
 int64_t k8v4_decode_ws_floats(int nseq, int heads, int nsplit, int max_q_len, int gqa);
 int k8v4_prefill_attn(const void* q, const int32_t* cu_q, const int32_t* seq_lens, const int32_t* block_table,
-                      int bt_stride, const void* cache, int64_t num_pages, int hkv, int head_offset, int heads,
-                      int gqa, int hq_total, int nseq, int max_q_len, float sm_scale, void* out, cudaStream_t st);
+                      int bt_stride, int bt_width, const void* cache, int64_t num_pages, int hkv, int head_offset,
+                      int heads, int gqa, int hq_total, int nseq, int max_q_len, float sm_scale, void* stage,
+                      void* out, cudaStream_t st);
+int64_t k8v4_prefill_stage_bytes(int nseq, int bt_width, int heads);
 int k8v4_wq_gemm(int mode, const void* w, const void* wscale, const void* x, const float* xscale,
                  const void* residual, void* out, float* ws, int M, int N, int K, int ldo, int split,
                  cudaStream_t st);
@@ -53,9 +55,9 @@ int k8v4_status_prefill(int clear);
 int k8v4_status_sampler(int clear);
 int k8v4_status_gather(int clear);
 int k8v4_prefill_attn_multi(const void* q, const int32_t* cu_q, const int32_t* seq_lens, const int32_t* block_table,
-                            int bt_stride, const void* const* caches, int nsrc, int64_t num_pages, const int32_t* q_pos,
-                            int hkv, int head_offset, int heads, int gqa, int hq_total, int nseq, int max_q_len,
-                            float sm_scale, void* out, cudaStream_t st);
+                            int bt_stride, int bt_width, const void* const* caches, int nsrc, int64_t num_pages,
+                            const int32_t* q_pos, int hkv, int head_offset, int heads, int gqa, int hq_total, int nseq,
+                            int max_q_len, float sm_scale, void* stage, void* out, cudaStream_t st);
 int k8v4_decode_combine_ranks(const float* ws_all, int64_t rank_floats, const int32_t* cu_q, void* out, int nrank,
                               int nsplit, int nseq, int heads, int head_offset, int gqa, int hq_total, int max_q_len,
                               cudaStream_t st);
@@ -190,10 +192,13 @@ void prefill_attn(const at::Tensor& q, const at::Tensor& cu_q, const at::Tensor&
   check_attn_common(q, cu_q, seq_lens, block_table, cache, out, hkv);
   TORCH_CHECK(head_offset >= 0 && heads >= 1 && head_offset + heads <= hkv, "head range");
   c10::cuda::CUDAGuard g(cache.device());
+  const int nseq = (int)seq_lens.numel(), width = (int)block_table.size(1);
+  // scratch for the once-dequantized V tiles (stream-ordered caching allocator)
+  at::Tensor stage = at::empty({k8v4_prefill_stage_bytes(nseq, width, (int)heads)}, cache.options());
   check_rc(k8v4_prefill_attn(q.data_ptr(), cu_q.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(),
-                             block_table.data_ptr<int32_t>(), (int)block_table.stride(0), cache.data_ptr(),
-                             cache.size(0), (int)hkv, (int)head_offset, (int)heads, (int)gqa, (int)q.size(1),
-                             (int)seq_lens.numel(), (int)max_q_len, (float)sm_scale, out.data_ptr(), cur_stream()),
+                             block_table.data_ptr<int32_t>(), (int)block_table.stride(0), width, cache.data_ptr(),
+                             cache.size(0), (int)hkv, (int)head_offset, (int)heads, (int)gqa, (int)q.size(1), nseq,
+                             (int)max_q_len, (float)sm_scale, stage.data_ptr(), out.data_ptr(), cur_stream()),
            "prefill_attn");
 }
 
@@ -463,10 +468,12 @@ void prefill_attn_cp(const at::Tensor& q, const at::Tensor& cu_q, const at::Tens
     qp = q_pos->data_ptr<int32_t>();
   }
   c10::cuda::CUDAGuard g(q.device());
+  const int nseq = (int)seq_lens.numel(), width = (int)block_table.size(1);
+  at::Tensor stage = at::empty({k8v4_prefill_stage_bytes(nseq, width, (int)heads)}, q.options().dtype(at::kByte));
   check_rc(k8v4_prefill_attn_multi(q.data_ptr(), cu_q.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(),
-                                   block_table.data_ptr<int32_t>(), (int)block_table.stride(0), ptrs.data(),
+                                   block_table.data_ptr<int32_t>(), (int)block_table.stride(0), width, ptrs.data(),
                                    (int)ptrs.size(), pages, qp, (int)hkv, (int)head_offset, (int)heads, (int)gqa,
-                                   (int)q.size(1), (int)seq_lens.numel(), (int)max_q_len, (float)sm_scale,
+                                   (int)q.size(1), nseq, (int)max_q_len, (float)sm_scale, stage.data_ptr(),
                                    out.data_ptr(), cur_stream()),
            "prefill_attn_cp");
 }

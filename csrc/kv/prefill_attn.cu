@@ -44,30 +44,83 @@ struct PrefillParams {
   const uint8_t* caches[MAX_SRC];
   int nsrc;
   __nv_bfloat16* out;          // [T, hq_total, D]
+  uint8_t* vstage;             // staged tiles [nseq][stage_tiles][heads] x STAGE_TILE_BYTES
+  int stage_tiles;             // tiles per sequence in the staging buffer
   int bt_stride;
   int hkv, gqa, hq_total, head_offset;
   int n_qtiles;
   float sm_scale_log2;
 };
 
+// Every query tile of a KV head reads the same V pages, so V is dequantized
+// once per (sequence, 128-key tile, KV head) by prefill_stage_kernel instead
+// of in each of the ~128 / TQ-times-more attention CTAs. A staged tile is the
+// fp16 MN-major SW128 image the PV MMA reads (32 KB) followed by the tile's
+// 128 k-scales as fp32 (512 B); keys past the sequence are zero. The
+// attention kernel moves it with two plain bulk copies.
+constexpr int STAGE_V_BYTES = VT_BYTES;
+constexpr int STAGE_KS_BYTES = TILE * 4;
+constexpr int STAGE_TILE_BYTES = STAGE_V_BYTES + STAGE_KS_BYTES;
+
+__device__ __forceinline__ uint8_t* stage_tile(const PrefillParams& p, int seq, int j, int hl, int heads) {
+  return p.vstage + (((size_t)seq * p.stage_tiles + j) * heads + hl) * STAGE_TILE_BYTES;
+}
+
+__global__ void __launch_bounds__(256) prefill_stage_kernel(const PrefillParams p) {
+  __shared__ __align__(1024) uint8_t sV[VT_BYTES];
+  const int j = blockIdx.x, hl = blockIdx.y, h = hl + p.head_offset, seq = blockIdx.z;
+  const int seq_len = p.seq_lens[seq];
+  const int key0 = j * TILE;
+  if (key0 >= seq_len) return;  // uniform for the CTA
+  const int nvalid = min(TILE, seq_len - key0);
+  const int32_t* bt = p.block_table + (int64_t)seq * p.bt_stride + j * TILE_PAGES;
+  uint8_t* dst = stage_tile(p, seq, j, hl, gridDim.y);
+  float* ks_out = reinterpret_cast<float*>(dst + STAGE_V_BYTES);
+  // one item = 32 dims (one scale group) of one key: a 16-byte load of packed
+  // V and one scale feed four 16-byte stores of the fp16 tile
+  for (int item = threadIdx.x; item < TILE * 4; item += 256) {
+    const int key = item >> 2, grp = item & 3;
+    if (key < nvalid) {
+      const uint32_t e = (uint32_t)bt[key >> 4];
+      const int src = (int)(e >> 24) < p.nsrc ? (int)(e >> 24) : 0;  // a bad source reads source 0
+      const uint8_t* run = p.caches[src] + ((int64_t)(e & 0xFFFFFFu) * p.hkv + h) * HEAD_BYTES + VS_OFF;
+      const int kk = key & 15;
+      const uint4 w = *reinterpret_cast<const uint4*>(run + kk * 64 + grp * 16);
+      const __half sc = *reinterpret_cast<const __half*>(run + VSC_OFF + (kk * 4 + grp) * 2);
+      v_chunk_to_f16(w.x, sc, sV, key, grp * 4);
+      v_chunk_to_f16(w.y, sc, sV, key, grp * 4 + 1);
+      v_chunk_to_f16(w.z, sc, sV, key, grp * 4 + 2);
+      v_chunk_to_f16(w.w, sc, sV, key, grp * 4 + 3);
+      if (grp == 0) ks_out[key] = __half2float(*reinterpret_cast<const __half*>(run + KS_OFF + kk * 2));
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) v_chunk_zero(sV, key, grp * 4 + q);
+      if (grp == 0) ks_out[key] = 0.f;
+    }
+  }
+  __syncthreads();
+  const uint4* s4 = reinterpret_cast<const uint4*>(sV);
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+  for (int i = threadIdx.x; i < VT_BYTES / 16; i += 256) d4[i] = s4[i];
+}
+
 struct PCfg {
   static constexpr int STAGES = 4;
-  static constexpr int NWARPS = 14;
+  static constexpr int NWARPS = 10;
   static constexpr int NTHREADS = NWARPS * 32;
-  static constexpr int NCONV = 4;   // warps 2, 3, 12, 13
-  static constexpr int NSOFT = 8;   // warps 4-11: quadrant = warp & 3, key half = (warp - 4) >> 2
+  static constexpr int NSOFT = 8;   // warps 2-9: quadrant = warp & 3, key half = (warp - 2) >> 2
   static constexpr int TMEM_COLS = 512;
   static constexpr uint32_t COL_S = 0, COL_P = 256, COL_O = 384;  // S [2 x 128], P fp16 pairs [2 x 64], O [128]
-  static constexpr int OFF_K = 0;
-  static constexpr int OFF_VT = OFF_K + STAGES * K_TILE_BYTES;
-  static constexpr int OFF_Q = OFF_VT + 2 * VT_BYTES;
-  static constexpr int OFF_VS = OFF_Q + 128 * 128;
-  static constexpr int OFF_MISC = OFF_VS + STAGES * VS_TILE_BYTES;
+  static constexpr int OFF_K = 0;                                  // [STAGES] int8 K tiles (TMA, SW128)
+  static constexpr int OFF_V = OFF_K + STAGES * K_TILE_BYTES;      // [STAGES] staged fp16 V tiles
+  static constexpr int OFF_KS = OFF_V + STAGES * STAGE_V_BYTES;    // [STAGES] k-scales (fp32)
+  static constexpr int OFF_Q = OFF_KS + STAGES * STAGE_KS_BYTES;
+  static constexpr int OFF_MISC = OFF_Q + 128 * 128;
   static constexpr int MISC_BYTES = 5120;
   static constexpr int SMEM_BYTES = 1024 + OFF_MISC + MISC_BYTES;
 };
 static_assert(PCfg::SMEM_BYTES <= 232448, "prefill shared memory");
-static_assert(PCfg::OFF_VS % 16 == 0 && VS_TILE_BYTES % 16 == 0, "16-byte k-scale loads");
+static_assert(PCfg::OFF_V % 1024 == 0 && PCfg::OFF_Q % 1024 == 0, "SW128 operands on 1 KB boundaries");
 
 __global__ void __launch_bounds__(PCfg::NTHREADS, 1)
     prefill_attn_kernel(const __grid_constant__ KVMaps maps, const PrefillParams p) {
@@ -75,17 +128,16 @@ __global__ void __launch_bounds__(PCfg::NTHREADS, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* sm = align_smem_1024(smem_raw);
   uint8_t* sK = sm + C::OFF_K;
-  uint8_t* sVT = sm + C::OFF_VT;
+  uint8_t* sV = sm + C::OFF_V;
+  const float* sKS = reinterpret_cast<const float*>(sm + C::OFF_KS);
   uint8_t* sQ = sm + C::OFF_Q;
-  uint8_t* sVS = sm + C::OFF_VS;
   uint8_t* misc = sm + C::OFF_MISC;
   uint64_t* kv_full = reinterpret_cast<uint64_t*>(misc);
-  uint64_t* kv_empty = kv_full + C::STAGES;  // QK commit + converter warps + softmax warps (k scales read)
+  uint64_t* kv_empty = kv_full + C::STAGES;  // PV of the stage's tile done (K, V and k-scales all read)
   uint64_t* s_full = kv_empty + C::STAGES;   // [2] QK of the tile in S[b] done
   uint64_t* s_empty = s_full + 2;            // [2] every softmax warp loaded S[b]
   uint64_t* p_full = s_empty + 2;            // [2] P[b] written (and O rescaled)
-  uint64_t* v_full = p_full + 2;             // [2] V tile converted
-  uint64_t* pv_empty = v_full + 2;           // [2] PV that read P[b] / V[b] done
+  uint64_t* pv_empty = p_full + 2;           // [2] PV that read P[b] done
   uint64_t* mx_full = pv_empty + 2;          // [2][4] both key halves of quadrant q published their max
   uint64_t* l_full = mx_full + 8;            // [4] both halves published their row sum
   uint64_t* done_bar = l_full + 4;
@@ -116,13 +168,12 @@ __global__ void __launch_bounds__(PCfg::NTHREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1 + C::NCONV + C::NSOFT);
+      mbar_init(&kv_empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
       mbar_init(&s_empty[b], C::NSOFT);
       mbar_init(&p_full[b], C::NSOFT);
-      mbar_init(&v_full[b], C::NCONV);
       mbar_init(&pv_empty[b], 1);
     }
     for (int i = 0; i < 8; ++i) mbar_init(&mx_full[i], 2);
@@ -173,6 +224,8 @@ __global__ void __launch_bounds__(PCfg::NTHREADS, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
+    // per tile: the K pages by TMA (one 3D map per source), the staged V
+    // image and k-scales by two bulk copies
     if (lane == 0) {
       for (int i = 0; i < p.nsrc; ++i) prefetch_tmap(&maps.m[i]);
       int issued = 0;
@@ -181,15 +234,16 @@ __global__ void __launch_bounds__(PCfg::NTHREADS, 1)
         if (j >= C::STAGES && !mbar_wait(&kv_empty[s], ((j / C::STAGES) - 1) & 1, abort_flag, 301)) break;
         const int pg0 = j * TILE_PAGES;
         const int npg = min(TILE_PAGES, n_pages - pg0);
-        mbar_arrive_expect_tx(&kv_full[s], npg * (K_BYTES + VS_BYTES));
+        mbar_arrive_expect_tx(&kv_full[s], npg * K_BYTES + STAGE_TILE_BYTES);
         for (int i = 0; i < npg; ++i) {
           const uint32_t e = (uint32_t)bt[pg0 + i];
           const int src = (int)(e >> 24) < p.nsrc ? (int)(e >> 24) : 0;  // a bad source reads source 0
           const int64_t run = (int64_t)(e & 0xFFFFFFu) * p.hkv + h;
           tma_load_3d(sK + s * K_TILE_BYTES + i * K_BYTES, &maps.m[src], &kv_full[s], 0, 0, (int)run);
-          bulk_load(sVS + s * VS_TILE_BYTES + i * VS_BYTES, p.caches[src] + run * HEAD_BYTES + VS_OFF, VS_BYTES,
-                    &kv_full[s]);
         }
+        const uint8_t* st = stage_tile(p, seq, j, hl, gridDim.y);
+        bulk_load(sV + s * STAGE_V_BYTES, st, STAGE_V_BYTES, &kv_full[s]);
+        bulk_load(sm + C::OFF_KS + s * STAGE_KS_BYTES, st + STAGE_V_BYTES, STAGE_KS_BYTES, &kv_full[s]);
         ++issued;
       }
       if (*abort_flag)
@@ -218,72 +272,32 @@ __global__ void __launch_bounds__(PCfg::NTHREADS, 1)
             mma_i8(tmem + C::COL_S + b * 128, sdesc_sw128(q_base + kk * 32, 16, 1024),
                    sdesc_sw128(k_base + kk * 32, 16, 1024), id_qk, kk > 0 ? 1u : 0u);
           mma_commit(&s_full[b]);
-          mma_commit(&kv_empty[s]);
         }
         if (j >= 1) {
-          const int jj = j - 1, b = jj & 1;
-          if (!mbar_wait(&p_full[b], (jj >> 1) & 1, abort_flag, 303) ||
-              !mbar_wait(&v_full[b], (jj >> 1) & 1, abort_flag, 304)) {
+          const int jj = j - 1, b = jj & 1, s = jj % C::STAGES;
+          if (!mbar_wait(&p_full[b], (jj >> 1) & 1, abort_flag, 303)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t vt_base = smem_u32(sVT + b * VT_BYTES);
+          const uint32_t v_base = smem_u32(sV + s * STAGE_V_BYTES);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
             mma_f16_ts(tmem + C::COL_O, tmem + C::COL_P + b * 64 + kk * 8,
-                       sdesc_sw128(vt_base + kk * 2048, VT_LBO, 1024), id_pv, (jj > 0 || kk > 0) ? 1u : 0u);
+                       sdesc_sw128(v_base + kk * 2048, VT_LBO, 1024), id_pv, (jj > 0 || kk > 0) ? 1u : 0u);
           mma_commit(&pv_empty[b]);
+          mma_commit(&kv_empty[s]);  // the stage's K, V and k-scales are all consumed
         }
       }
       mma_commit(done_bar);
       mbar_wait_drain(done_bar, 0);
-    }
-  } else if (warp < 4 || warp >= 4 + C::NSOFT) {
-    // ---------------------------------------------------------- converters
-    // One item = 32 dims (one scale group) of one key: a 16-byte load of
-    // packed V and one scale feed four 16-byte stores of the fp16 tile.
-    const int cw = (warp < 4) ? warp - 2 : warp - 2 - C::NSOFT;  // 0 .. NCONV-1
-    const int ct = cw * 32 + lane;
-    constexpr int CT = C::NCONV * 32;
-    for (int j = 0; j < nt; ++j) {
-      const int s = j % C::STAGES, b = j & 1;
-      if (!mbar_wait_all(&kv_full[s], (j / C::STAGES) & 1, abort_flag, 305)) break;
-      // V^T buffer b was last read by PV of tile j-2
-      if (j >= 2 && !mbar_wait_all(&pv_empty[b], ((j >> 1) - 1) & 1, abort_flag, 306)) break;
-      const int nvalid = min(TILE, n_keys - j * TILE);
-      const uint8_t* vs = sVS + s * VS_TILE_BYTES;
-      uint8_t* vt = sVT + b * VT_BYTES;
-#pragma unroll
-      for (int item = ct; item < TILE * 4; item += CT) {
-        const int key = item >> 2, grp = item & 3;
-        if (key < nvalid) {
-          const uint8_t* run = vs + (key >> 4) * VS_BYTES;
-          const int kk = key & 15;
-          const uint4 w = *reinterpret_cast<const uint4*>(run + kk * 64 + grp * 16);
-          const __half sc = *reinterpret_cast<const __half*>(run + VSC_OFF + (kk * 4 + grp) * 2);
-          v_chunk_to_f16(w.x, sc, vt, key, grp * 4);
-          v_chunk_to_f16(w.y, sc, vt, key, grp * 4 + 1);
-          v_chunk_to_f16(w.z, sc, vt, key, grp * 4 + 2);
-          v_chunk_to_f16(w.w, sc, vt, key, grp * 4 + 3);
-        } else {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) v_chunk_zero(vt, key, grp * 4 + q);
-        }
-      }
-      fence_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&v_full[b]);
-        mbar_arrive(&kv_empty[s]);
-      }
     }
   } else {
     // ------------------------------------------------------------- softmax
     // Two warps per TMEM lane quadrant: each owns 32 rows x 64 keys of every
     // tile (scores held in registers, one pass) and 64 columns of O. The two
     // halves of a row agree on the running max through shared memory.
-    const int quad = warp & 3, hf = (warp - 4) >> 2;
+    const int quad = warp & 3, hf = (warp - 2) >> 2;
     const int row = quad * 32 + lane;
     const bool live = row < R;
     // a zero query row (scale 0) keeps finite scores: scores x qs stay 0 and masked keys -inf
@@ -316,31 +330,20 @@ __global__ void __launch_bounds__(PCfg::NTHREADS, 1)
       }
       __syncwarp();
       if (ok && lane == 0) mbar_arrive(&s_empty[b]);
+      // the stage's k-scales (landed with its K tile; QK completing implies it)
       if (ok && !mbar_wait_all(&kv_full[s], (j / C::STAGES) & 1, abort_flag, 308)) ok = false;
       const int key0 = j * TILE + hf * 64;
       float tmax = -INFINITY;
       if (ok) {
-        // k scales of this half: 4 pages x 16 fp16, two 16-byte loads per page
-        const uint8_t* vs = sVS + s * VS_TILE_BYTES + hf * 4 * VS_BYTES + KS_OFF;
+        const float4* ks4 = reinterpret_cast<const float4*>(sKS + s * TILE + hf * 64);
 #pragma unroll
-        for (int pg = 0; pg < 4; ++pg) {
-#pragma unroll
-          for (int hq = 0; hq < 2; ++hq) {
-            const uint4 kw = *reinterpret_cast<const uint4*>(vs + pg * VS_BYTES + hq * 16);
-            const __half2* k2 = reinterpret_cast<const __half2*>(&kw);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 kf = __half22float2(k2[e]);
-              const int k = pg * 16 + hq * 8 + 2 * e;
-              sc[k] *= kf.x;
-              sc[k + 1] *= kf.y;
-            }
-          }
+        for (int k = 0; k < 64; k += 4) {
+          const float4 kq = ks4[k >> 2];
+          sc[k] *= kq.x;
+          sc[k + 1] *= kq.y;
+          sc[k + 2] *= kq.z;
+          sc[k + 3] *= kq.w;
         }
-      }
-      __syncwarp();
-      if (ok && lane == 0) mbar_arrive(&kv_empty[s]);
-      if (ok) {
         const bool full = __all_sync(0xffffffffu, end >= key0 + 64 || !live);
         if (!full) {
 #pragma unroll
@@ -468,19 +471,29 @@ extern "C" int k8v4_make_kv_tmap(void* map_out, const void* cache, int64_t num_p
 
 K8V4_STATUS_API(prefill)
 
+// Bytes of the V staging buffer for `nseq` sequences whose block-table rows
+// hold `bt_width` pages, over `heads` KV heads.
+extern "C" int64_t k8v4_prefill_stage_bytes(int nseq, int bt_width, int heads) {
+  return (int64_t)nseq * cdiv(bt_width, TILE_PAGES) * heads * STAGE_TILE_BYTES;
+}
+
 // Paged causal prefill over `heads` KV heads starting at head_offset. With
 // `nsrc` > 1 the pages come from several caches (context parallelism: this
 // GPU's and its peers', block-table entries (source << 24) | page), and
 // `q_pos` gives each query token's global position (the tokens of a rank are
 // then not contiguous). All caches share num_pages and the head layout.
+// `stage` holds k8v4_prefill_stage_bytes(nseq, bt_width, heads) bytes of
+// scratch for the dequantized V tiles.
 extern "C" int k8v4_prefill_attn_multi(const void* q, const int32_t* cu_q, const int32_t* seq_lens,
-                                       const int32_t* block_table, int bt_stride, const void* const* caches,
-                                       int nsrc, int64_t num_pages, const int32_t* q_pos, int hkv, int head_offset,
-                                       int heads, int gqa, int hq_total, int nseq, int max_q_len, float sm_scale,
+                                       const int32_t* block_table, int bt_stride, int bt_width,
+                                       const void* const* caches, int nsrc, int64_t num_pages,
+                                       const int32_t* q_pos, int hkv, int head_offset, int heads, int gqa,
+                                       int hq_total, int nseq, int max_q_len, float sm_scale, void* stage,
                                        void* out, cudaStream_t st) {
   if (nseq <= 0 || max_q_len <= 0) return 0;
   if (gqa < 1 || 128 / gqa < 1) return 1;
   if (nsrc < 1 || nsrc > MAX_SRC) return 2;
+  if (!stage || bt_width < 1) return 4;
   KVMaps maps;
   PrefillParams p;
   for (int i = 0; i < nsrc; ++i) {
@@ -498,6 +511,8 @@ extern "C" int k8v4_prefill_attn_multi(const void* q, const int32_t* cu_q, const
   p.block_table = block_table;
   p.q_pos = q_pos;
   p.out = reinterpret_cast<__nv_bfloat16*>(out);
+  p.vstage = reinterpret_cast<uint8_t*>(stage);
+  p.stage_tiles = cdiv(bt_width, TILE_PAGES);
   p.bt_stride = bt_stride;
   p.hkv = hkv;
   p.gqa = gqa;
@@ -510,16 +525,17 @@ extern "C" int k8v4_prefill_attn_multi(const void* q, const int32_t* cu_q, const
     cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PCfg::SMEM_BYTES);
     set = true;
   }
+  prefill_stage_kernel<<<dim3(p.stage_tiles, heads, nseq), 256, 0, st>>>(p);
   dim3 grid(p.n_qtiles, heads, nseq);
   prefill_attn_kernel<<<grid, PCfg::NTHREADS, PCfg::SMEM_BYTES, st>>>(maps, p);
   return cudaGetLastError() == cudaSuccess ? 0 : 10;
 }
 
 extern "C" int k8v4_prefill_attn(const void* q, const int32_t* cu_q, const int32_t* seq_lens,
-                                 const int32_t* block_table, int bt_stride, const void* cache, int64_t num_pages,
-                                 int hkv, int head_offset, int heads, int gqa, int hq_total, int nseq, int max_q_len,
-                                 float sm_scale, void* out, cudaStream_t st) {
+                                 const int32_t* block_table, int bt_stride, int bt_width, const void* cache,
+                                 int64_t num_pages, int hkv, int head_offset, int heads, int gqa, int hq_total,
+                                 int nseq, int max_q_len, float sm_scale, void* stage, void* out, cudaStream_t st) {
   const void* caches[1] = {cache};
-  return k8v4_prefill_attn_multi(q, cu_q, seq_lens, block_table, bt_stride, caches, 1, num_pages, nullptr, hkv,
-                                 head_offset, heads, gqa, hq_total, nseq, max_q_len, sm_scale, out, st);
+  return k8v4_prefill_attn_multi(q, cu_q, seq_lens, block_table, bt_stride, bt_width, caches, 1, num_pages, nullptr,
+                                 hkv, head_offset, heads, gqa, hq_total, nseq, max_q_len, sm_scale, stage, out, st);
 }
