@@ -26,6 +26,18 @@ constexpr int VS_TILE_BYTES = TILE_PAGES * VS_BYTES;
 constexpr int VT_BYTES = TILE * D * 2; // fp16 V tile, 32 KB
 constexpr int VT_LBO = 16 * 1024;      // MN-major: next 64 dims
 constexpr float LOG2E = 1.4426950408889634f;
+
+// TMA maps of one KV cache: `page` moves one (page, head) K block (2 KB);
+// `k8` moves the K blocks of 8 consecutive pages of one head (16 KB, the
+// whole tile) and `vs8` their V + scale blocks (9,472 B). A tile whose pages
+// are consecutive (the usual case: the block manager hands out pages in
+// order) then costs 2 copy requests instead of 16; the TMA's per-request
+// issue cost, not bandwidth, set the tile rate with one request per page.
+struct KVTileMaps {
+  CUtensorMap page;
+  CUtensorMap k8;
+  CUtensorMap vs8;
+};
 // Lazy rescale threshold (log2 units): the running max used for exp2 only
 // moves when a new score exceeds it by more than this, so p <= 2^8.
 constexpr float RESCALE_TAU = 8.0f;

@@ -99,7 +99,7 @@ struct DCfg {
 // (lazy, tau = 8 in log2 units).
 template <int NPAD>
 __global__ void __launch_bounds__(DCfg<NPAD>::NTHREADS, 1)
-    decode_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const DecodeParams p) {
+    decode_attn_kernel(const __grid_constant__ KVTileMaps tm, const DecodeParams p) {
   using C = DCfg<NPAD>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* sm = align_smem_1024(smem_raw);
@@ -208,9 +208,14 @@ __global__ void __launch_bounds__(DCfg<NPAD>::NTHREADS, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    // Lane i handles page i of a tile (8 pages): its page id is read one tile
-    // ahead, and it issues that page's K TMA and V + scales bulk copy itself.
-    if (lane == 0) prefetch_tmap(&tm_k);
+    // Lane i holds page i of a tile (8 pages), its id read one tile ahead.
+    // Consecutive pages: lane 0 moves the tile with two TMA boxes; otherwise
+    // each lane issues its page's K TMA and V + scales bulk copy.
+    if (lane == 0) {
+      prefetch_tmap(&tm.page);
+      prefetch_tmap(&tm.k8);
+      prefetch_tmap(&tm.vs8);
+    }
     auto page_of = [&](int jt) -> int64_t {
       const int pg = (tile_beg + jt) * TILE_PAGES + lane;
       return (jt < nt && lane < TILE_PAGES && pg < n_pages) ? (int64_t)bt[pg] : 0;
@@ -224,13 +229,24 @@ __global__ void __launch_bounds__(DCfg<NPAD>::NTHREADS, 1)
       if (j >= C::STAGES && !mbar_wait_all(&kv_empty[s], ((j / C::STAGES) - 1) & 1, abort_flag, 201)) break;
       const int pg0 = (tile_beg + j) * TILE_PAGES;
       const int npg = min(TILE_PAGES, n_pages - pg0);
-      if (lane == 0) mbar_arrive_expect_tx(&kv_full[s], npg * (K_BYTES + VS_BYTES));
-      __syncwarp();
-      if (lane < npg) {
-        const int64_t run = page * p.hkv + h;
-        tma_load_3d(sK + s * K_TILE_BYTES + lane * K_BYTES, &tm_k, &kv_full[s], 0, 0, (int)run);
-        bulk_load(sVS + s * VS_TILE_BYTES + lane * VS_BYTES, p.cache + run * HEAD_BYTES + VS_OFF, VS_BYTES,
-                  &kv_full[s]);
+      const int64_t page0 = __shfl_sync(0xffffffffu, page, 0);
+      if (__all_sync(0xffffffffu, lane >= npg || page == page0 + lane)) {
+        // 8-page boxes (pages past the cache arrive zero-filled; pages past
+        // the sequence are masked like any key beyond its end)
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&kv_full[s], TILE_PAGES * (K_BYTES + VS_BYTES));
+          tma_load_4d(sK + s * K_TILE_BYTES, &tm.k8, &kv_full[s], 0, 0, h, (int)page0);
+          tma_load_3d(sVS + s * VS_TILE_BYTES, &tm.vs8, &kv_full[s], 0, h, (int)page0);
+        }
+      } else {
+        if (lane == 0) mbar_arrive_expect_tx(&kv_full[s], npg * (K_BYTES + VS_BYTES));
+        __syncwarp();
+        if (lane < npg) {
+          const int64_t run = page * p.hkv + h;
+          tma_load_3d(sK + s * K_TILE_BYTES + lane * K_BYTES, &tm.page, &kv_full[s], 0, 0, (int)run);
+          bulk_load(sVS + s * VS_TILE_BYTES + lane * VS_BYTES, p.cache + run * HEAD_BYTES + VS_OFF, VS_BYTES,
+                    &kv_full[s]);
+        }
       }
       if (lane == 0) K8V4_ATRACE(0, j);
       ++issued;
@@ -610,6 +626,38 @@ extern "C" int k8v4_make_kv_tmap(void* map_out, const void* cache, int64_t num_p
   return r == CUDA_SUCCESS ? 0 : -2;
 }
 
+// All three maps of a cache (KVTileMaps).
+extern "C" int k8v4_make_kv_maps(void* maps_out, const void* cache, int64_t num_pages, int hkv) {
+  KVTileMaps* m = reinterpret_cast<KVTileMaps*>(maps_out);
+  if (k8v4_make_kv_tmap(&m->page, cache, num_pages, hkv)) return -3;
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return -1;
+  {
+    // K: (128 bytes, 16 rows, hkv heads, pages), box = one head's rows of 8 pages
+    cuuint64_t dims[4] = {128, 16, (cuuint64_t)hkv, (cuuint64_t)num_pages};
+    cuuint64_t strides[3] = {128, HEAD_BYTES, (cuuint64_t)hkv * HEAD_BYTES};
+    cuuint32_t box[4] = {128, 16, 1, TILE_PAGES};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = enc(&m->k8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(cache), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return -4;
+  }
+  {
+    // V + scales: (148 x 8 bytes, hkv heads, pages) from VS_OFF, box = 8 pages of one head
+    cuuint64_t dims[3] = {VS_BYTES / 8, (cuuint64_t)hkv, (cuuint64_t)num_pages};
+    cuuint64_t strides[2] = {HEAD_BYTES, (cuuint64_t)hkv * HEAD_BYTES};
+    cuuint32_t box[3] = {VS_BYTES / 8, 1, TILE_PAGES};
+    cuuint32_t estr[3] = {1, 1, 1};
+    void* base = const_cast<uint8_t*>(reinterpret_cast<const uint8_t*>(cache)) + VS_OFF;
+    CUresult r = enc(&m->vs8, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, base, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return -5;
+  }
+  return 0;
+}
+
 K8V4_STATUS_API(decode)
 
 #ifdef K8V4_TRACE
@@ -619,7 +667,7 @@ extern "C" int k8v4_attn_trace(uint64_t* host) {
 #endif
 
 template <int NPAD>
-static int launch_decode(const CUtensorMap& tm, const DecodeParams& p, int heads, int nseq, cudaStream_t st) {
+static int launch_decode(const KVTileMaps& tm, const DecodeParams& p, int heads, int nseq, cudaStream_t st) {
   using C = DCfg<NPAD>;
   static bool set = false;
   if (!set) {
@@ -644,8 +692,8 @@ extern "C" int k8v4_decode_attn(const void* q, const int32_t* cu_q, const int32_
   if (nsplit > 128) return 4;
   if (nsplit < 1) nsplit = 1;
   if (nsplit > 1 && (!ws_o || !ws_ml)) return 2;
-  CUtensorMap tm;
-  if (k8v4_make_kv_tmap(&tm, cache, num_pages, hkv)) return 3;
+  KVTileMaps tm;
+  if (k8v4_make_kv_maps(&tm, cache, num_pages, hkv)) return 3;
   DecodeParams p;
   p.q = reinterpret_cast<const __nv_bfloat16*>(q);
   p.cu_q = cu_q;

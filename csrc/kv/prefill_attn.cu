@@ -32,7 +32,7 @@ constexpr int MAX_SRC = 8;  // KV page sources: this GPU plus context-parallel p
 // this process) and the matching TMA map. With one source the entry is the
 // page number itself.
 struct KVMaps {
-  CUtensorMap m[MAX_SRC];
+  KVTileMaps m[MAX_SRC];
 };
 
 struct PrefillParams {
@@ -224,32 +224,57 @@ __global__ void __launch_bounds__(PCfg::NTHREADS, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    // per tile: the K pages by TMA (one 3D map per source), the staged V
-    // image and k-scales by two bulk copies
-    if (lane == 0) {
-      for (int i = 0; i < p.nsrc; ++i) prefetch_tmap(&maps.m[i]);
-      int issued = 0;
-      for (int j = 0; j < nt; ++j) {
-        const int s = j % C::STAGES;
-        if (j >= C::STAGES && !mbar_wait(&kv_empty[s], ((j / C::STAGES) - 1) & 1, abort_flag, 301)) break;
-        const int pg0 = j * TILE_PAGES;
-        const int npg = min(TILE_PAGES, n_pages - pg0);
-        mbar_arrive_expect_tx(&kv_full[s], npg * K_BYTES + STAGE_TILE_BYTES);
-        for (int i = 0; i < npg; ++i) {
-          const uint32_t e = (uint32_t)bt[pg0 + i];
+    // per tile: the K pages by TMA (one 3D map per source; lane i issues
+    // page i, its block-table entry read STAGES tiles ahead in a register
+    // ring), the staged V image and k-scales by two bulk copies (lane 0)
+    if (lane == 0)
+      for (int i = 0; i < p.nsrc; ++i) {
+        prefetch_tmap(&maps.m[i].page);
+        prefetch_tmap(&maps.m[i].k8);
+      }
+    auto entry_of = [&](int jt) -> uint32_t {
+      const int pg = jt * TILE_PAGES + lane;
+      return (jt < nt && lane < TILE_PAGES && pg < n_pages) ? (uint32_t)bt[pg] : 0u;
+    };
+    static_assert(C::STAGES == 4, "page-id ring depth");
+    uint32_t eq0 = entry_of(0), eq1 = entry_of(1), eq2 = entry_of(2), eq3 = entry_of(3);
+    int issued = 0;
+    for (int j = 0; j < nt; ++j) {
+      const int s = j % C::STAGES;
+      const uint32_t e = eq0;
+      eq0 = eq1;
+      eq1 = eq2;
+      eq2 = eq3;
+      eq3 = entry_of(j + 4);
+      if (j >= C::STAGES && !mbar_wait_all(&kv_empty[s], ((j / C::STAGES) - 1) & 1, abort_flag, 301)) break;
+      const int npg = min(TILE_PAGES, n_pages - j * TILE_PAGES);
+      const uint32_t e0 = __shfl_sync(0xffffffffu, e, 0);
+      if (__all_sync(0xffffffffu, lane >= npg || e == e0 + (uint32_t)lane)) {
+        // 8 consecutive pages of one source: one box for the tile's K
+        if (lane == 0) {
+          const int src = (int)(e0 >> 24) < p.nsrc ? (int)(e0 >> 24) : 0;  // a bad source reads source 0
+          mbar_arrive_expect_tx(&kv_full[s], TILE_PAGES * K_BYTES + STAGE_TILE_BYTES);
+          tma_load_4d(sK + s * K_TILE_BYTES, &maps.m[src].k8, &kv_full[s], 0, 0, h, (int)(e0 & 0xFFFFFFu));
+        }
+      } else {
+        if (lane == 0) mbar_arrive_expect_tx(&kv_full[s], npg * K_BYTES + STAGE_TILE_BYTES);
+        __syncwarp();
+        if (lane < npg) {
           const int src = (int)(e >> 24) < p.nsrc ? (int)(e >> 24) : 0;  // a bad source reads source 0
           const int64_t run = (int64_t)(e & 0xFFFFFFu) * p.hkv + h;
-          tma_load_3d(sK + s * K_TILE_BYTES + i * K_BYTES, &maps.m[src], &kv_full[s], 0, 0, (int)run);
+          tma_load_3d(sK + s * K_TILE_BYTES + lane * K_BYTES, &maps.m[src].page, &kv_full[s], 0, 0, (int)run);
         }
+      }
+      if (lane == 0) {
         const uint8_t* st = stage_tile(p, seq, j, hl, gridDim.y);
         bulk_load(sV + s * STAGE_V_BYTES, st, STAGE_V_BYTES, &kv_full[s]);
         bulk_load(sm + C::OFF_KS + s * STAGE_KS_BYTES, st + STAGE_V_BYTES, STAGE_KS_BYTES, &kv_full[s]);
-        ++issued;
       }
-      if (*abort_flag)
-        for (int j = issued - 1; j >= 0 && j >= issued - C::STAGES; --j)
-          mbar_wait_drain(&kv_full[j % C::STAGES], (j / C::STAGES) & 1);
+      ++issued;
     }
+    if (lane == 0 && *abort_flag)
+      for (int j = issued - 1; j >= 0 && j >= issued - C::STAGES; --j)
+        mbar_wait_drain(&kv_full[j % C::STAGES], (j / C::STAGES) & 1);
   } else if (warp == 1) {
     // ----------------------------------------------------------------- MMA
     // QK(j) into S[j & 1] once the softmax loaded S of tile j - 2; PV(j - 1)
@@ -467,7 +492,7 @@ __global__ void __launch_bounds__(PCfg::NTHREADS, 1)
 using namespace k8v4;
 using namespace k8v4::attn;
 
-extern "C" int k8v4_make_kv_tmap(void* map_out, const void* cache, int64_t num_pages, int hkv);
+extern "C" int k8v4_make_kv_maps(void* maps_out, const void* cache, int64_t num_pages, int hkv);
 
 K8V4_STATUS_API(prefill)
 
@@ -497,7 +522,7 @@ extern "C" int k8v4_prefill_attn_multi(const void* q, const int32_t* cu_q, const
   KVMaps maps;
   PrefillParams p;
   for (int i = 0; i < nsrc; ++i) {
-    if (k8v4_make_kv_tmap(&maps.m[i], caches[i], num_pages, hkv)) return 3;
+    if (k8v4_make_kv_maps(&maps.m[i], caches[i], num_pages, hkv)) return 3;
     p.caches[i] = reinterpret_cast<const uint8_t*>(caches[i]);
   }
   for (int i = nsrc; i < MAX_SRC; ++i) {

@@ -168,13 +168,14 @@ def test_gemm_residual():
 
 
 # ---------------------------------------------------------------- attention
-def _paged_setup(lens, hkv, gqa, seed, q_lens=None, pages_extra=3, k_ramp=0.0):
+def _paged_setup(lens, hkv, gqa, seed, q_lens=None, pages_extra=3, k_ramp=0.0, contiguous=False):
     layout = b200_layout(hkv, gqa)
     g = _gen(seed)
     D = 128
     q_lens = q_lens or [1] * len(lens)
     total_pages = sum((n + 15) // 16 for n in lens) + pages_extra
-    perm = torch.randperm(total_pages, generator=g)
+    # shuffled pages exercise the per-page copies; pages in order the 8-page TMA boxes
+    perm = torch.arange(total_pages) if contiguous else torch.randperm(total_pages, generator=g)
     width = max((n + 15) // 16 for n in lens)
     bt = torch.zeros(len(lens), width, dtype=torch.int32)
     cache = torch.zeros(total_pages, layout.page_bytes, dtype=torch.uint8)
@@ -209,10 +210,11 @@ def _reference(layout, cache, seqs, lens, q_lens):
 @pytest.mark.parametrize("q_len", [1, 7])
 @pytest.mark.parametrize("nsplit", [1, 4])
 @pytest.mark.parametrize("gqa,hkv", [(6, 4), (3, 1)])
-def test_decode_attn(q_len, nsplit, gqa, hkv):
+@pytest.mark.parametrize("contiguous", [False, True])
+def test_decode_attn(q_len, nsplit, gqa, hkv, contiguous):
     lens = [37, 300, 1024, 16]
     q_lens = [q_len] * len(lens)
-    layout, cache, bt, seqs = _paged_setup(lens, hkv, gqa, 12, q_lens)
+    layout, cache, bt, seqs = _paged_setup(lens, hkv, gqa, 12, q_lens, contiguous=contiguous)
     ref = _reference(layout, cache, seqs, lens, q_lens)
     q = torch.cat([s[0] for s in seqs], 0).to(DEV)
     cu = torch.tensor([0] + list(torch.cumsum(torch.tensor(q_lens), 0)), dtype=torch.int32, device=DEV)
@@ -227,10 +229,11 @@ def test_decode_attn(q_len, nsplit, gqa, hkv):
 
 @pytest.mark.parametrize("ctx,q_len", [(0, 50), (200, 300), (1000, 21)])
 @pytest.mark.parametrize("gqa,hkv", [(6, 4), (3, 2)])
-def test_prefill_attn(ctx, q_len, gqa, hkv):
+@pytest.mark.parametrize("contiguous", [False, True])
+def test_prefill_attn(ctx, q_len, gqa, hkv, contiguous):
     lens = [ctx + q_len, ctx // 2 + q_len]
     q_lens = [q_len, q_len]
-    layout, cache, bt, seqs = _paged_setup(lens, hkv, gqa, 13, q_lens)
+    layout, cache, bt, seqs = _paged_setup(lens, hkv, gqa, 13, q_lens, contiguous=contiguous)
     ref = _reference(layout, cache, seqs, lens, q_lens)
     q = torch.cat([s[0] for s in seqs], 0).to(DEV)
     cu = torch.tensor([0, q_len, 2 * q_len], dtype=torch.int32, device=DEV)
