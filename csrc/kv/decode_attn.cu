@@ -260,38 +260,63 @@ __global__ void __launch_bounds__(DCfg<NPAD>::NTHREADS, 1)
       const uint32_t id_qk = idesc_s8(128, 128);
       const uint32_t id_pv = idesc_f16(128, 128, false, true);
       const uint32_t q_base = smem_u32(sQ);
-      bool ok = true;
-      for (int j = 0; j <= nt && ok; ++j) {
-        if (j < nt) {
-          const int s = j % C::STAGES, b = j & 1;
-          if (!mbar_wait(&kv_full[s], (j / C::STAGES) & 1, abort_flag, 202)) break;
-          if (j >= 2 && !mbar_wait(&s_empty[b], ((j >> 1) - 1) & 1, abort_flag, 209)) break;
-          tc_fence_after();
-          const uint32_t k_base = smem_u32(sK + s * K_TILE_BYTES);
+      // One thread feeds the in-order tensor pipe from two queues: QK(jq)
+      // as soon as its K stage landed and the softmax has loaded S of tile
+      // jq - 2, PV(jp) as soon as P and V of tile jp are ready. QK thus runs
+      // up to two tiles ahead instead of queueing behind PV(jq - 2), which
+      // waits for the softmax. The polls are bounded like every wait.
+      int jq = 0, jp = 0, idle = 0;
+      uint64_t t_idle = globaltimer_ns();
+      while (jp < nt) {
+        bool progressed = false;
+        if (jq < nt) {
+          const int s = jq % C::STAGES, b = jq & 1;
+          if (mbar_test_wait(&kv_full[s], (jq / C::STAGES) & 1) &&
+              (jq < 2 || mbar_test_wait(&s_empty[b], ((jq >> 1) - 1) & 1))) {
+            tc_fence_after();
+            const uint32_t k_base = smem_u32(sK + s * K_TILE_BYTES);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_i8(tmem + C::COL_S + b * 128, sdesc_sw128(q_base + kk * 32, 16, 1024),
-                   sdesc_sw128(k_base + kk * 32, 16, 1024), id_qk, kk > 0 ? 1u : 0u);
-          mma_commit(&s_full[b]);
-          mma_commit(&kv_empty[s]);
-          K8V4_ATRACE(2, j);
-        }
-        if (j >= 1) {
-          const int jj = j - 1, b = jj & 1, vb = jj % C::NVT;
-          if (!mbar_wait(&p_full[b], (jj >> 1) & 1, abort_flag, 203) ||
-              !mbar_wait(&v_full[vb], (jj / C::NVT) & 1, abort_flag, 204)) {
-            ok = false;
-            break;
+            for (int kk = 0; kk < 4; ++kk)
+              mma_i8(tmem + C::COL_S + b * 128, sdesc_sw128(q_base + kk * 32, 16, 1024),
+                     sdesc_sw128(k_base + kk * 32, 16, 1024), id_qk, kk > 0 ? 1u : 0u);
+            mma_commit(&s_full[b]);
+            mma_commit(&kv_empty[s]);
+            K8V4_ATRACE(2, jq);
+            ++jq;
+            progressed = true;
           }
-          tc_fence_after();
-          const uint32_t vt_base = smem_u32(sVT + vb * VT_BYTES);
+        }
+        if (jp < jq) {
+          const int b = jp & 1, vb = jp % C::NVT;
+          if (mbar_test_wait(&p_full[b], (jp >> 1) & 1) && mbar_test_wait(&v_full[vb], (jp / C::NVT) & 1)) {
+            tc_fence_after();
+            const uint32_t vt_base = smem_u32(sVT + vb * VT_BYTES);
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            mma_f16_ts(tmem + C::COL_O, tmem + C::COL_P + b * 64 + kk * 8,
-                       sdesc_sw128(vt_base + kk * 2048, VT_LBO, 1024), id_pv, (jj > 0 || kk > 0) ? 1u : 0u);
-          mma_commit(&pv_empty[b]);
-          mma_commit(&vt_empty[vb]);
-          K8V4_ATRACE(4, jj);
+            for (int kk = 0; kk < 8; ++kk)
+              mma_f16_ts(tmem + C::COL_O, tmem + C::COL_P + b * 64 + kk * 8,
+                         sdesc_sw128(vt_base + kk * 2048, VT_LBO, 1024), id_pv, (jp > 0 || kk > 0) ? 1u : 0u);
+            mma_commit(&pv_empty[b]);
+            mma_commit(&vt_empty[vb]);
+            K8V4_ATRACE(4, jp);
+            ++jp;
+            progressed = true;
+          }
+        }
+        if (progressed) {
+          idle = 0;
+        } else {
+          // idle: yield the issue slots to this sub-partition's other warps,
+          // look at the clock and the abort flag every 64 polls
+          __nanosleep(20);
+          if (++idle == 1) t_idle = globaltimer_ns();
+          if ((idle & 63) == 0) {
+            if (*abort_flag) break;
+            if (globaltimer_ns() - t_idle > K8V4_WAIT_LIMIT_NS) {
+              *abort_flag = 1;
+              record_error(kErrMbarTimeout, 203);
+              break;
+            }
+          }
         }
       }
       mma_commit(done_bar);
