@@ -1,6 +1,8 @@
 // Shared device helpers for the k8v4 sm_100a kernel library.
 #pragma once
 #include <cstdint>
+#include <cstdlib>
+#include <utility>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -71,5 +73,42 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 
 K8V4_HOST_DEVICE inline int cdiv(int a, int b) { return (a + b - 1) / b; }
+
+// ------------------------------------------------ programmatic dependent launch
+// Kernels are launched with programmatic stream serialization (decode runs
+// ~11 dependent kernels per layer inside a CUDA graph): the next kernel's
+// CTAs may start once every CTA of the current one has started, set up
+// barriers / TMEM and stream inputs that no earlier kernel writes (weights),
+// and wait for the previous grid's completion and memory only where they
+// first touch its results. Both instructions are no-ops in a kernel launched
+// without the attribute.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// K8V4_PDL=0 in the environment turns the attribute off (plain stream order).
+inline bool pdl_enabled() {
+  static const int on = [] {
+    const char* e = getenv("K8V4_PDL");
+    return (e && e[0] == '0') ? 0 : 1;
+  }();
+  return on != 0;
+}
+
+// kern<<<grid, block, smem, st>>>(args...) with the programmatic attribute.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                           Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 }  // namespace k8v4

@@ -158,6 +158,7 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
     wq_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                    const __grid_constant__ CUtensorMap tm_s, const Params p) {
   using C = Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BSTAGES>;
+  pdl_trigger();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = align_smem_1024(smem_raw);
   uint8_t* sA = smem;
@@ -238,15 +239,27 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
         mbar_arrive_expect_tx(scale_bar, (p.k_per_split / 128) * 256);
         tma_load_2d(sScale, &tm_s, scale_bar, n0, kbeg / 128);
       }
-      int rs = 0, rphase = 0, issued = 0, raw_issued = 0;
+      int issued = 0, raw_issued = 0;
+      // The weights (and their scales) come from no earlier kernel: the raw
+      // ring fills before this grid waits for the previous one (programmatic
+      // dependent launch), so the first weight bytes overlap its tail.
+      const int pre = (MODE != W8A8) ? min(RSTAGES, nkb) : 0;
+      for (int kb = 0; kb < pre; ++kb) {
+        mbar_arrive_expect_tx(&r_full[kb], C::RAW_BYTES);
+        tma_load_2d(sR + kb * C::RAW_BYTES, &tm_w, &r_full[kb], n0, (kbeg + kb * C::BK) / 8);
+        ++raw_issued;
+      }
+      pdl_wait();
       for (int kb = 0; kb < nkb; ++kb) {
         const int k0 = kbeg + kb * C::BK;
         if (MODE != W8A8) {
-          if (kb >= RSTAGES && !mbar_wait(&r_empty[rs], rphase ^ 1, abort_flag, 101)) break;
-          mbar_arrive_expect_tx(&r_full[rs], C::RAW_BYTES);
-          tma_load_2d(sR + rs * C::RAW_BYTES, &tm_w, &r_full[rs], n0, k0 / 8);
-          ++raw_issued;
-          if (++rs == RSTAGES) { rs = 0; rphase ^= 1; }
+          if (kb >= pre) {
+            const int rs = kb % RSTAGES;
+            if (kb >= RSTAGES && !mbar_wait(&r_empty[rs], ((kb / RSTAGES) & 1) ^ 1, abort_flag, 101)) break;
+            mbar_arrive_expect_tx(&r_full[rs], C::RAW_BYTES);
+            tma_load_2d(sR + rs * C::RAW_BYTES, &tm_w, &r_full[rs], n0, k0 / 8);
+            ++raw_issued;
+          }
         } else {
           const int s = kb % STAGES;
           if (kb >= STAGES && !mbar_wait(&a_empty[s], ((kb / STAGES) & 1) ^ 1, abort_flag, 102)) break;
@@ -577,8 +590,7 @@ static int launch_cfg(const void* w, const void* x, const Params& p, int split, 
     attr_set = true;
   }
   dim3 grid(cdiv(p.N, 128), cdiv(p.M, BT), split);
-  kern<<<grid, C::NTHREADS, C::SMEM_BYTES, st>>>(tw, tx, ts, p);
-  return cudaGetLastError() == cudaSuccess ? 0 : 300;
+  return launch_k(kern, grid, dim3(C::NTHREADS), C::SMEM_BYTES, st, tw, tx, ts, p) == cudaSuccess ? 0 : 300;
 }
 
 }  // namespace gemm

@@ -100,6 +100,8 @@ struct DCfg {
 template <int NPAD>
 __global__ void __launch_bounds__(DCfg<NPAD>::NTHREADS, 1)
     decode_attn_kernel(const __grid_constant__ KVTileMaps tm, const DecodeParams p) {
+  pdl_trigger();
+  pdl_wait();  // Q, the KV pages and the block table may come from the previous kernels
   using C = DCfg<NPAD>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* sm = align_smem_1024(smem_raw);
@@ -570,6 +572,8 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const float* __rest
                                                              __nv_bfloat16* out, int nsplit, int npad, int gqa,
                                                              int hq_total, int head_offset, int nrank,
                                                              int64_t rank_stride_o, int64_t rank_stride_ml) {
+  pdl_trigger();
+  pdl_wait();  // everything this kernel reads may come from the previous one
   __shared__ float wsh[128];
   __shared__ float red[8];
   const int r = blockIdx.x, hl = blockIdx.y, seq = blockIdx.z, d = threadIdx.x;
@@ -700,8 +704,7 @@ static int launch_decode(const KVTileMaps& tm, const DecodeParams& p, int heads,
     set = true;
   }
   dim3 grid(p.nsplit, heads, nseq);
-  decode_attn_kernel<NPAD><<<grid, C::NTHREADS, C::SMEM_BYTES, st>>>(tm, p);
-  return cudaGetLastError() == cudaSuccess ? 0 : 10;
+  return launch_k(decode_attn_kernel<NPAD>, grid, dim3(C::NTHREADS), C::SMEM_BYTES, st, tm, p) == cudaSuccess ? 0 : 10;
 }
 
 // Paged decode attention (b200 format). `heads` KV heads starting at
@@ -742,9 +745,11 @@ extern "C" int k8v4_decode_attn(const void* q, const int32_t* cu_q, const int32_
   else if (rows <= 48) { npad = 48; rc = launch_decode<48>(tm, p, heads, nseq, st); }
   else { npad = 64; rc = launch_decode<64>(tm, p, heads, nseq, st); }
   if (rc || nsplit == 1) return rc;
-  decode_combine_kernel<<<dim3(rows, heads, nseq), D, 0, st>>>(ws_o, ws_ml, cu_q, reinterpret_cast<__nv_bfloat16*>(out),
-                                                               nsplit, npad, gqa, hq_total, head_offset, 1, 0, 0);
-  return cudaGetLastError() == cudaSuccess ? 0 : 11;
+  return launch_k(decode_combine_kernel, dim3(rows, heads, nseq), dim3(D), 0, st, (const float*)ws_o,
+                  (const float*)ws_ml, cu_q, reinterpret_cast<__nv_bfloat16*>(out), nsplit, npad, gqa, hq_total,
+                  head_offset, 1, (int64_t)0, (int64_t)0) == cudaSuccess
+             ? 0
+             : 11;
 }
 
 // Merge the split partials of `nrank` ranks (context parallelism): `ws_all`
@@ -759,10 +764,11 @@ extern "C" int k8v4_decode_combine_ranks(const float* ws_all, int64_t rank_float
   if (rows > 64 || nrank < 1 || nsplit < 1 || nrank * nsplit > 128) return 1;
   const int npad = rows <= 16 ? 16 : rows <= 32 ? 32 : rows <= 48 ? 48 : 64;
   const int64_t ml_floats = (int64_t)nseq * heads * nsplit * 2 * npad;
-  decode_combine_kernel<<<dim3(rows, heads, nseq), D, 0, st>>>(
-      ws_all + ml_floats, ws_all, cu_q, reinterpret_cast<__nv_bfloat16*>(out), nsplit, npad, gqa, hq_total,
-      head_offset, nrank, rank_floats, rank_floats);
-  return cudaGetLastError() == cudaSuccess ? 0 : 11;
+  return launch_k(decode_combine_kernel, dim3(rows, heads, nseq), dim3(D), 0, st, ws_all + ml_floats, ws_all, cu_q,
+                  reinterpret_cast<__nv_bfloat16*>(out), nsplit, npad, gqa, hq_total, head_offset, nrank,
+                  rank_floats, rank_floats) == cudaSuccess
+             ? 0
+             : 11;
 }
 
 // Workspace floats needed for a given launch shape.

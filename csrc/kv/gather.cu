@@ -36,6 +36,8 @@ __global__ void __launch_bounds__(256) gather_dequant_kernel(const uint8_t* __re
                                                              const int32_t* __restrict__ block_table, int hkv,
                                                              int head, int seq_len, int64_t num_pages,
                                                              OutT* __restrict__ k_out, OutT* __restrict__ v_out) {
+  pdl_trigger();
+  pdl_wait();  // everything this kernel reads may come from the previous one
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= seq_len) return;
@@ -77,11 +79,11 @@ extern "C" int k8v4_gather_dequant(const void* cache, int64_t num_pages, const i
   if (head < 0 || head >= hkv) return 1;
   const int blocks = (seq_len * 32 + 255) / 256;
   if (out_dtype == 0)
-    gather_dequant_kernel<float><<<blocks, 256, 0, st>>>(reinterpret_cast<const uint8_t*>(cache), block_table, hkv,
+    launch_k(gather_dequant_kernel<float>, dim3(blocks), dim3(256), 0, st, reinterpret_cast<const uint8_t*>(cache), block_table, hkv,
                                                          head, seq_len, num_pages, reinterpret_cast<float*>(k_out),
                                                          reinterpret_cast<float*>(v_out));
   else
-    gather_dequant_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
+    launch_k(gather_dequant_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, st, 
         reinterpret_cast<const uint8_t*>(cache), block_table, hkv, head, seq_len, num_pages,
         reinterpret_cast<__nv_bfloat16*>(k_out), reinterpret_cast<__nv_bfloat16*>(v_out));
   return cudaGetLastError() == cudaSuccess ? 0 : 2;

@@ -67,6 +67,8 @@ __device__ __forceinline__ uint8_t* stage_tile(const PrefillParams& p, int seq, 
 }
 
 __global__ void __launch_bounds__(256) prefill_stage_kernel(const PrefillParams p) {
+  pdl_trigger();
+  pdl_wait();  // everything this kernel reads may come from the previous one
   __shared__ __align__(1024) uint8_t sV[VT_BYTES];
   const int j = blockIdx.x, hl = blockIdx.y, h = hl + p.head_offset, seq = blockIdx.z;
   const int seq_len = p.seq_lens[seq];
@@ -124,6 +126,8 @@ static_assert(PCfg::OFF_V % 1024 == 0 && PCfg::OFF_Q % 1024 == 0, "SW128 operand
 
 __global__ void __launch_bounds__(PCfg::NTHREADS, 1)
     prefill_attn_kernel(const __grid_constant__ KVMaps maps, const PrefillParams p) {
+  pdl_trigger();
+  pdl_wait();  // Q, the KV pages and the block table may come from the previous kernels
   using C = PCfg;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* sm = align_smem_1024(smem_raw);
@@ -550,10 +554,10 @@ extern "C" int k8v4_prefill_attn_multi(const void* q, const int32_t* cu_q, const
     cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PCfg::SMEM_BYTES);
     set = true;
   }
-  prefill_stage_kernel<<<dim3(p.stage_tiles, heads, nseq), 256, 0, st>>>(p);
+  if (launch_k(prefill_stage_kernel, dim3(p.stage_tiles, heads, nseq), dim3(256), 0, st, p) != cudaSuccess) return 10;
   dim3 grid(p.n_qtiles, heads, nseq);
-  prefill_attn_kernel<<<grid, PCfg::NTHREADS, PCfg::SMEM_BYTES, st>>>(maps, p);
-  return cudaGetLastError() == cudaSuccess ? 0 : 10;
+  return launch_k(prefill_attn_kernel, grid, dim3(PCfg::NTHREADS), PCfg::SMEM_BYTES, st, maps, p) == cudaSuccess ? 0
+                                                                                                              : 10;
 }
 
 extern "C" int k8v4_prefill_attn(const void* q, const int32_t* cu_q, const int32_t* seq_lens,

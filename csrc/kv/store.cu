@@ -39,6 +39,8 @@ __device__ __forceinline__ float rint_f(float x) { return rintf(x); }
 // [K 16x128 int8][V 16x64 u8][k_scale 16 fp16][v_scale 16x4 fp16].
 template <bool ROPE>
 __global__ void store_b200_kernel(StoreArgs a) {
+  pdl_trigger();
+  pdl_wait();  // everything this kernel reads may come from the previous one
   constexpr int D = 128, PAGE = 16, HEAD_BYTES = 3232;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -145,6 +147,8 @@ __global__ void store_b200_kernel(StoreArgs a) {
 // ------------------------------------------------------------------ ref
 // D = 256, page 64, token-major regions, fp32 scales, affine V.
 __global__ void store_ref_kernel(StoreArgs a) {
+  pdl_trigger();
+  pdl_wait();  // everything this kernel reads may come from the previous one
   constexpr int D = 256, PAGE = 64;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -231,9 +235,9 @@ extern "C" int k8v4_kv_store(int fmt, const void* k, int64_t k_stride_t, const v
   const int warps = T * hkv;
   const int blocks = cdiv(warps, 4);
   if (fmt == 0)
-    store_ref_kernel<<<blocks, 128, 0, st>>>(a);
+    launch_k(store_ref_kernel, dim3(blocks), dim3(128), 0, st, a);
   else
-    store_b200_kernel<false><<<blocks, 128, 0, st>>>(a);
+    launch_k(store_b200_kernel<false>, dim3(blocks), dim3(128), 0, st, a);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }
 
@@ -255,6 +259,6 @@ extern "C" int k8v4_rope_store(const void* qkv, const float* cos_sin, const int6
   a.hkv = hkv;
   a.hq = hq;
   const int warps = T * (hq + hkv);
-  store_b200_kernel<true><<<cdiv(warps, 4), 128, 0, st>>>(a);
+  launch_k(store_b200_kernel<true>, dim3(cdiv(warps, 4)), dim3(128), 0, st, a);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }

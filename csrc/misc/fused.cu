@@ -133,6 +133,8 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const __nv_bfloat16* 
                                                            __nv_bfloat16* residual, const __nv_bfloat16* __restrict__ w,
                                                            __nv_bfloat16* y, int8_t* yq, float* yscale, int n,
                                                            int64_t ldy, float eps, ReduceSync sync) {
+  pdl_trigger();
+  pdl_wait();  // everything this kernel reads may come from the previous one
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   if (sync.flag) sync_wait(sync);
@@ -189,6 +191,8 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const __nv_bfloat16* 
 template <int VPT>
 __global__ void __launch_bounds__(kThreads) silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* y,
                                                             int8_t* yq, float* yscale, int inter) {
+  pdl_trigger();
+  pdl_wait();  // everything this kernel reads may come from the previous one
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   float v[VPT][8];
@@ -214,6 +218,8 @@ __global__ void __launch_bounds__(kThreads) silu_mul_kernel(const __nv_bfloat16*
 // thread), for the few-token decode rows where one CTA per row is too serial.
 __global__ void __launch_bounds__(256) silu_mul_wide_kernel(const __nv_bfloat16* __restrict__ gu,
                                                             __nv_bfloat16* __restrict__ y, int inter, int64_t total) {
+  pdl_trigger();
+  pdl_wait();  // everything this kernel reads may come from the previous one
   const int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (v >= total) return;
   const int per_row = inter / 8;
@@ -231,6 +237,8 @@ __global__ void __launch_bounds__(256) silu_mul_wide_kernel(const __nv_bfloat16*
 template <int VPT>
 __global__ void __launch_bounds__(kThreads) quant_rows_kernel(const __nv_bfloat16* __restrict__ x, int8_t* q, float* scale,
                                                               int n) {
+  pdl_trigger();
+  pdl_wait();  // everything this kernel reads may come from the previous one
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   float v[VPT][8];
@@ -246,6 +254,8 @@ __global__ void __launch_bounds__(kThreads) quant_rows_kernel(const __nv_bfloat1
 __global__ void embed_int8_kernel(const int64_t* __restrict__ ids, const int8_t* __restrict__ codes,
                                   const __half* __restrict__ scales, __nv_bfloat16* out, int n, int64_t start,
                                   int64_t rows) {
+  pdl_trigger();
+  pdl_wait();  // everything this kernel reads may come from the previous one
   const int64_t t = blockIdx.x;
   const int64_t id = ids[t] - start;
   const bool in = id >= 0 && id < rows;
@@ -270,6 +280,8 @@ __global__ void embed_int8_kernel(const int64_t* __restrict__ ids, const int8_t*
 // out = bf16(ws (+ residual)); optionally zero ws for the next accumulation.
 __global__ void splitk_finish_kernel(float* ws, const __nv_bfloat16* residual, __nv_bfloat16* out, int64_t total,
                                      int zero_ws) {
+  pdl_trigger();
+  pdl_wait();  // everything this kernel reads may come from the previous one
   const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
   if (i >= total) return;
   float4 a = *reinterpret_cast<float4*>(ws + i);
@@ -298,10 +310,10 @@ K8V4_STATUS_API(misc)
 #define K8V4_VPT_DISPATCH(n, KERNEL, ...)                                         \
   do {                                                                            \
     const int vpt_ = cdiv(cdiv((n), 8), kThreads);                                \
-    if (vpt_ <= 1) KERNEL<1><<<rows, kThreads, 0, st>>>(__VA_ARGS__);             \
-    else if (vpt_ <= 2) KERNEL<2><<<rows, kThreads, 0, st>>>(__VA_ARGS__);        \
-    else if (vpt_ <= 4) KERNEL<4><<<rows, kThreads, 0, st>>>(__VA_ARGS__);        \
-    else if (vpt_ <= 9) KERNEL<9><<<rows, kThreads, 0, st>>>(__VA_ARGS__);        \
+    if (vpt_ <= 1) launch_k(KERNEL<1>, dim3(rows), dim3(kThreads), 0, st, __VA_ARGS__);             \
+    else if (vpt_ <= 2) launch_k(KERNEL<2>, dim3(rows), dim3(kThreads), 0, st, __VA_ARGS__);        \
+    else if (vpt_ <= 4) launch_k(KERNEL<4>, dim3(rows), dim3(kThreads), 0, st, __VA_ARGS__);        \
+    else if (vpt_ <= 9) launch_k(KERNEL<9>, dim3(rows), dim3(kThreads), 0, st, __VA_ARGS__);        \
     else return 2;                                                                \
   } while (0)
 
@@ -324,7 +336,7 @@ extern "C" int k8v4_silu_mul(const void* gu, void* y, void* yq, float* yscale, i
   if (inter % 8) return 1;
   if (!yq && y && rows <= 16) {
     const int64_t total = (int64_t)rows * (inter / 8);
-    silu_mul_wide_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
+    launch_k(silu_mul_wide_kernel, dim3((unsigned)((total + 255) / 256)), dim3(256), 0, st,
         reinterpret_cast<const __nv_bfloat16*>(gu), reinterpret_cast<__nv_bfloat16*>(y), inter, total);
     return cudaGetLastError() == cudaSuccess ? 0 : 3;
   }
@@ -345,7 +357,7 @@ extern "C" int k8v4_embed_int8(const int64_t* ids, const void* codes, const void
                                int64_t start, int64_t rows, cudaStream_t st) {
   if (T <= 0) return 0;
   if (n % 8) return 1;
-  embed_int8_kernel<<<T, 128, 0, st>>>(ids, reinterpret_cast<const int8_t*>(codes),
+  launch_k(embed_int8_kernel, dim3(T), dim3(128), 0, st, ids, reinterpret_cast<const int8_t*>(codes),
                                        reinterpret_cast<const __half*>(scales), reinterpret_cast<__nv_bfloat16*>(out),
                                        n, start, rows);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
@@ -356,7 +368,7 @@ extern "C" int k8v4_splitk_finish(float* ws, const void* residual, void* out, in
   if (total <= 0) return 0;
   if (total % 4) return 1;
   const int64_t threads = total / 4;
-  splitk_finish_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
+  launch_k(splitk_finish_kernel, dim3((unsigned)((threads + 255) / 256)), dim3(256), 0, st,
       ws, reinterpret_cast<const __nv_bfloat16*>(residual), reinterpret_cast<__nv_bfloat16*>(out), total, zero_ws);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }

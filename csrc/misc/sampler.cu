@@ -11,6 +11,8 @@ namespace sampler {
 // padded to the GEMM's 128-row tile is read only over its real columns).
 __global__ void __launch_bounds__(1024) argmax_kernel(const __nv_bfloat16* __restrict__ logits, int vocab, int64_t ld,
                                                       int64_t offset, float* best_val, int64_t* best_idx) {
+  pdl_trigger();
+  pdl_wait();  // everything this kernel reads may come from the previous one
   __shared__ float sv[32];
   __shared__ int si[32];
   const int64_t row = blockIdx.x;
@@ -70,7 +72,7 @@ extern "C" int k8v4_argmax(const void* logits, int rows, int vocab, int64_t ld, 
                            int64_t* best_idx, cudaStream_t st) {
   if (rows <= 0) return 0;
   if (ld < vocab) return 2;
-  sampler::argmax_kernel<<<rows, 1024, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(logits), vocab, ld, offset,
+  launch_k(sampler::argmax_kernel, dim3(rows), dim3(1024), 0, st, reinterpret_cast<const __nv_bfloat16*>(logits), vocab, ld, offset,
                                                  best_val, best_idx);
   return cudaGetLastError() == cudaSuccess ? 0 : 1;
 }
