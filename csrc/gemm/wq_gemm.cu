@@ -240,10 +240,12 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
         tma_load_2d(sScale, &tm_s, scale_bar, n0, kbeg / 128);
       }
       int issued = 0, raw_issued = 0;
-      // The weights (and their scales) come from no earlier kernel: the raw
-      // ring fills before this grid waits for the previous one (programmatic
-      // dependent launch), so the first weight bytes overlap its tail.
-      const int pre = (MODE != W8A8) ? min(RSTAGES, nkb) : 0;
+      // The weights (and their scales) come from no earlier kernel: a few raw
+      // stages go out before this grid waits for the previous one
+      // (programmatic dependent launch), so the first weight bytes overlap its
+      // tail. Only a few: the token tiles issued after the wait queue behind
+      // them in the TMA unit.
+      const int pre = (MODE != W8A8) ? min(min(RSTAGES, 4), nkb) : 0;
       for (int kb = 0; kb < pre; ++kb) {
         mbar_arrive_expect_tx(&r_full[kb], C::RAW_BYTES);
         tma_load_2d(sR + kb * C::RAW_BYTES, &tm_w, &r_full[kb], n0, (kbeg + kb * C::BK) / 8);
