@@ -45,6 +45,7 @@ int k8v4_quant_rows(const void* x, void* q, float* scale, int rows, int n, cudaS
 int k8v4_embed_int8(const int64_t* ids, const void* codes, const void* scales, void* out, int T, int n,
                     int64_t start, int64_t rows, cudaStream_t st);
 int k8v4_splitk_finish(float* ws, const void* residual, void* out, int64_t total, int zero_ws, cudaStream_t st);
+int k8v4_int8_dequant(const void* q, const void* scale, void* out, int N, int K, cudaStream_t st);
 int k8v4_argmax(const void* logits, int rows, int vocab, int64_t ld, int64_t offset, float* best_val,
                 int64_t* best_idx, cudaStream_t st);
 int k8v4_status_gemm(int clear);
@@ -355,6 +356,21 @@ void quant_rows(const at::Tensor& x, at::Tensor& q, at::Tensor& scale) {
            "quant_rows");
 }
 
+// INT8 island weights -> bf16 (per-row scales).
+void int8_dequant(const at::Tensor& q, const at::Tensor& scale, at::Tensor& out) {
+  check_contig(q, "q");
+  check_contig(scale, "scale");
+  check_contig(out, "out");
+  TORCH_CHECK(q.scalar_type() == at::kChar && q.dim() == 2, "q int8 [N, K]");
+  TORCH_CHECK(scale.scalar_type() == at::kBFloat16 && scale.numel() == q.size(0), "scale bf16 [N]");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.numel() >= q.numel(), "out bf16, at least N * K");
+  TORCH_CHECK(q.size(1) % 8 == 0, "K must be a multiple of 8");
+  c10::cuda::CUDAGuard g(q.device());
+  check_rc(k8v4_int8_dequant(q.data_ptr(), scale.data_ptr(), out.data_ptr(), (int)q.size(0), (int)q.size(1),
+                             cur_stream()),
+           "int8_dequant");
+}
+
 void embed_int8(const at::Tensor& ids, const at::Tensor& codes, const at::Tensor& scales, at::Tensor& out,
                 int64_t start) {
   check_contig(ids, "ids");
@@ -549,6 +565,7 @@ TORCH_LIBRARY(k8v4, m) {
   m.def("wq_gemm_ctas(int mode, int M, int N, int K, int split) -> int");
   m.def("silu_mul(Tensor gate_up, Tensor(a!)? y, Tensor(b!)? yq, Tensor(c!)? yscale) -> ()");
   m.def("quant_rows(Tensor x, Tensor(a!) q, Tensor(b!) scale) -> ()");
+  m.def("int8_dequant(Tensor q, Tensor scale, Tensor(a!) out) -> ()");
   m.def("embed_int8(Tensor ids, Tensor codes, Tensor scales, Tensor(a!) out, int start) -> ()");
   m.def("argmax(Tensor logits, int offset, Tensor(a!) best_val, Tensor(b!) best_idx) -> ()");
   m.def("status(bool clear) -> int");
@@ -574,6 +591,7 @@ TORCH_LIBRARY_IMPL(k8v4, CUDA, m) {
   m.impl("rmsnorm", &rmsnorm);
   m.impl("silu_mul", &silu_mul);
   m.impl("quant_rows", &quant_rows);
+  m.impl("int8_dequant", &int8_dequant);
   m.impl("embed_int8", &embed_int8);
   m.impl("argmax", &argmax);
   m.impl("gather_dequant", &gather_dequant);

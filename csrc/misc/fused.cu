@@ -134,7 +134,14 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const __nv_bfloat16* 
                                                            __nv_bfloat16* y, int8_t* yq, float* yscale, int n,
                                                            int64_t ldy, float eps, ReduceSync sync) {
   pdl_trigger();
-  pdl_wait();  // everything this kernel reads may come from the previous one
+  // the norm weights come from no earlier kernel: load them before waiting
+  uint4 gw[VPT];
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = (threadIdx.x + i * kThreads) * 8;
+    gw[i] = c < n ? *reinterpret_cast<const uint4*>(w + c) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  pdl_wait();  // x / xf / residual may come from the previous kernel
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   if (sync.flag) sync_wait(sync);
@@ -174,8 +181,14 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const __nv_bfloat16* 
   for (int i = 0; i < VPT; ++i) {
     const int c = (threadIdx.x + i * kThreads) * 8;
     if (c < n) {
+      const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gw[i]);
       float g[8];
-      load8(w + c, g);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(g2[j]);
+        g[2 * j] = f.x;
+        g[2 * j + 1] = f.y;
+      }
 #pragma unroll
       for (int j = 0; j < 8; ++j) v[i][j] = __bfloat162float(__float2bfloat16_rn(v[i][j] * inv)) * g[j];
 #pragma unroll
@@ -299,6 +312,24 @@ __global__ void splitk_finish_kernel(float* ws, const __nv_bfloat16* residual, _
   if (zero_ws) *reinterpret_cast<float4*>(ws + i) = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
+// INT8 island weights: out[n, k] = q[n, k] * scale[n] in bf16 (8 values a thread).
+__global__ void __launch_bounds__(256) int8_dequant_kernel(const int8_t* __restrict__ q,
+                                                          const __nv_bfloat16* __restrict__ scale,
+                                                          __nv_bfloat16* __restrict__ out, int K, int64_t total8) {
+  pdl_trigger();
+  pdl_wait();  // the scratch it overwrites may still be read by the previous kernel
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total8) return;
+  const int64_t e = i * 8;
+  const float s = __bfloat162float(scale[e / K]);
+  const uint2 raw = *reinterpret_cast<const uint2*>(q + e);
+  const int8_t* b = reinterpret_cast<const int8_t*>(&raw);
+  float f[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) f[j] = (float)b[j] * s;
+  store8(out + e, f);
+}
+
 }  // namespace misc
 }  // namespace k8v4
 
@@ -371,4 +402,16 @@ extern "C" int k8v4_splitk_finish(float* ws, const void* residual, void* out, in
   launch_k(splitk_finish_kernel, dim3((unsigned)((threads + 255) / 256)), dim3(256), 0, st,
       ws, reinterpret_cast<const __nv_bfloat16*>(residual), reinterpret_cast<__nv_bfloat16*>(out), total, zero_ws);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+// q [N, K] int8 with per-row bf16 scales -> bf16 [N, K]; K % 8 == 0.
+extern "C" int k8v4_int8_dequant(const void* q, const void* scale, void* out, int N, int K, cudaStream_t st) {
+  if (N <= 0 || K <= 0) return 0;
+  if (K % 8) return 1;
+  const int64_t total8 = (int64_t)N * K / 8;
+  return launch_k(int8_dequant_kernel, dim3((unsigned)((total8 + 255) / 256)), dim3(256), 0, st,
+                  reinterpret_cast<const int8_t*>(q), reinterpret_cast<const __nv_bfloat16*>(scale),
+                  reinterpret_cast<__nv_bfloat16*>(out), K, total8) == cudaSuccess
+             ? 0
+             : 3;
 }

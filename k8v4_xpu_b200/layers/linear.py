@@ -50,6 +50,8 @@ def split_for(rows: int, n: int, k: int, sms: int = NUM_SMS) -> int:
 class Int4Linear:
     """GPTQ INT4 weights ``qweight`` [K/8, N] int32 + ``scales`` [K/128, N] fp16."""
 
+    supports_w4a8 = True  # takes int8 activations on the MLP prefill path
+
     def __init__(self, name: str, qweight: torch.Tensor, scales: torch.Tensor):
         if qweight.dim() != 2 or scales.dim() != 2:
             raise ValueError("qweight / scales must be 2D")
@@ -81,6 +83,11 @@ class Int4Linear:
         from ..models.gptq import dequant_int4
         return x.float() @ dequant_int4(self.qweight, self.scales)
 
+    def dense_t(self) -> torch.Tensor:
+        """The dequantized weight [K, N] in fp32 on the CPU (torch reference paths)."""
+        from ..models.gptq import dequant_int4
+        return dequant_int4(self.qweight.cpu(), self.scales.cpu())
+
 
 class Int8RowLinear:
     """Per-row INT8 weights ``[N, K]`` + fp16 scales ``[N]`` (the lm_head).
@@ -104,3 +111,81 @@ class Int8RowLinear:
     def __call__(self, xq: torch.Tensor, xs: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         y = ops.wq_gemm(ops.W8A8, self.weight, self.scale, xq, xscale=xs, out=out)
         return y if y.shape[1] == self.out_features else y[:, : self.out_features]
+
+
+# ------------------------------------------------------------------ INT8 islands
+def island_suffixes(env=None) -> tuple[str, ...]:
+    """Module-name suffixes listed in ``K8V4_INT8_ISLANDS`` (comma separated),
+    the reference's switch (``k8v4_v030/int8_island.py:50-53``)."""
+    raw = (os.environ if env is None else env).get("K8V4_INT8_ISLANDS", "")
+    return tuple(x.strip() for x in raw.split(",") if x.strip())
+
+
+def is_island(name: str, suffixes: tuple[str, ...]) -> bool:
+    return any(name.endswith(suf) for suf in suffixes)
+
+
+_SCRATCH: dict = {}
+
+
+def _island_scratch(numel: int, device) -> torch.Tensor:
+    """One bf16 buffer per device for the dequantized island weight (grows,
+    never shrinks, so a captured graph keeps its address)."""
+    key = str(device)
+    buf = _SCRATCH.get(key)
+    if buf is None or buf.numel() < numel:
+        buf = torch.empty(numel, dtype=torch.bfloat16, device=device)
+        _SCRATCH[key] = buf
+    return buf
+
+
+class Int8IslandLinear:
+    """A dense linear kept resident as per-output-row symmetric int8 weights
+    ``q`` [N, K] with bf16 scales [N] (the reference's INT8 island,
+    ``k8v4_v030/int8_island.py:60-130``: ``s = max(amax / 127, 1e-12)``,
+    ``q = round(w / s)`` clamped to +-127). The product is W8A16: bf16
+    activations against the weights dequantized by ``k8v4.int8_dequant`` into
+    a shared scratch, then a library bf16 GEMM. Islands halve the weight
+    memory of the dense layers they replace; they are not a hot path.
+    """
+
+    supports_w4a8 = False
+
+    def __init__(self, name: str, q: torch.Tensor, scale: torch.Tensor):
+        if q.dtype != torch.int8 or q.dim() != 2:
+            raise ValueError("island weights must be int8 [N, K]")
+        self.name = name
+        self.q = q.contiguous()
+        self.scale = scale.reshape(-1).to(torch.bfloat16).contiguous()
+        self.out_features, self.in_features = q.shape
+
+    @staticmethod
+    def quantize(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """Dense [N, K] -> (int8 [N, K], bf16 [N])."""
+        w = w.float()
+        s = (w.abs().amax(dim=1, keepdim=True) / 127.0).clamp_min(1e-12)
+        q = torch.round(w / s).clamp_(-127, 127).to(torch.int8)
+        return q, s.reshape(-1).to(torch.bfloat16)
+
+    @classmethod
+    def from_dense(cls, name: str, w: torch.Tensor, device=None) -> "Int8IslandLinear":
+        q, s = cls.quantize(w)
+        return cls(name, q.to(device) if device is not None else q, s.to(device) if device is not None else s)
+
+    def __call__(self, x: torch.Tensor | None = None, xq=None, xs=None, out: torch.Tensor | None = None,
+                 ws=None, split=None, defer: bool = False) -> torch.Tensor:
+        if x is None:
+            raise ValueError("%s: INT8 islands take bf16 activations" % self.name)
+        w = ops.int8_dequant(self.q, self.scale, _island_scratch(self.q.numel(), self.q.device))
+        y = torch.matmul(x, w.t())
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+
+    def reference(self, x: torch.Tensor) -> torch.Tensor:
+        return x.float() @ (self.q.float() * self.scale.float()[:, None]).t()
+
+    def dense_t(self) -> torch.Tensor:
+        """The dequantized weight [K, N] in fp32 on the CPU (torch reference paths)."""
+        return (self.q.float().cpu() * self.scale.float().cpu()[:, None]).t()

@@ -87,6 +87,9 @@ def save_checkpoint(model, path: str, shard_layers: int = 8) -> None:
     q/k/v and gate/up unfused)."""
     if model.tp != 1:
         raise ValueError("save a tensor-parallel size 1 model")
+    from ..layers.linear import Int4Linear
+    if any(not isinstance(lin, Int4Linear) for L in model.layers for lin in (L.qkv, L.o, L.gate_up, L.down)):
+        raise ValueError("INT8 islands are chosen when loading (K8V4_INT8_ISLANDS); save the GPTQ model")
     cfg = model.cfg
     os.makedirs(path, exist_ok=True)
     with open(os.path.join(path, "config.json"), "w") as f:
@@ -174,9 +177,18 @@ class _Reader:
         return qw, sc
 
 
+def _rows_k(wt: torch.Tensor, rank: int, k_local: int) -> torch.Tensor:
+    """Row-parallel shard of a dense [K, N] weight: this rank's K rows."""
+    return wt[rank * k_local:(rank + 1) * k_local]
+
+
 def load_checkpoint(model, path: str) -> None:
-    """Load a GPTQ + side-file checkpoint into ``model`` (its TP rank's shard)."""
-    from ..layers.linear import Int4Linear, Int8RowLinear
+    """Load a GPTQ + side-file checkpoint into ``model`` (its TP rank's shard).
+
+    Linears whose fused module name ends with a ``K8V4_INT8_ISLANDS`` suffix
+    are read from dense ``<part>.weight`` tensors instead and kept as INT8
+    islands."""
+    from ..layers.linear import Int4Linear, Int8IslandLinear, Int8RowLinear, is_island, island_suffixes
     from .dense import LayerWeights, MTPWeights, rope_table
     cfg = read_model_config(path)
     mc = model.cfg
@@ -188,20 +200,48 @@ def load_checkpoint(model, path: str) -> None:
     r = _Reader(path)
     sh = model.shape
 
+    islands = island_suffixes()
+
+    def dense_t(pre: str, parts) -> torch.Tensor:
+        # dense HF weights [N_part, K] of the parts, fused along N, as [K, N]
+        return torch.cat([r.get(pre + "%s.weight" % p).float() for p in parts], 0).t()
+
+    def island(mod: str, wt_local: torch.Tensor) -> Int8IslandLinear:
+        return Int8IslandLinear.from_dense(mod, wt_local.t().contiguous(), dev)
+
     def layer(pre: str, name: str) -> LayerWeights:
-        qs = [r.linear(pre + "self_attn.%s_proj" % p) for p in ("q", "k", "v")]
-        qkv_q, qkv_s = model._shard_qkv(torch.cat([a for a, _ in qs], 1), torch.cat([b for _, b in qs], 1))
-        o_q, o_s = model._shard_rows(*r.linear(pre + "self_attn.o_proj"), sh.hq_local * cfg.head_dim)
-        gu = [r.linear(pre + "mlp.%s_proj" % p) for p in ("gate", "up")]
-        gu_q, gu_s = model._shard_gate_up(torch.cat([a for a, _ in gu], 1), torch.cat([b for _, b in gu], 1))
-        dn_q, dn_s = model._shard_rows(*r.linear(pre + "mlp.down_proj"), sh.inter_local)
+        # INT8 islands (K8V4_INT8_ISLANDS suffixes of the fused module names)
+        # come from dense weights, quantized per output row after sharding
+        qkv_name, o_name = name + "self_attn.qkv_proj", name + "self_attn.o_proj"
+        gu_name, dn_name = name + "mlp.gate_up_proj", name + "mlp.down_proj"
+        if is_island(qkv_name, islands):
+            wt = dense_t(pre + "self_attn.", ("q_proj", "k_proj", "v_proj"))
+            qkv = island(qkv_name, model._shard_qkv(wt, wt[:1])[0])
+        else:
+            qs = [r.linear(pre + "self_attn.%s_proj" % p) for p in ("q", "k", "v")]
+            qkv_q, qkv_s = model._shard_qkv(torch.cat([a for a, _ in qs], 1), torch.cat([b for _, b in qs], 1))
+            qkv = Int4Linear(qkv_name, qkv_q.to(dev).contiguous(), qkv_s.to(dev).contiguous())
+        if is_island(o_name, islands):
+            o = island(o_name, _rows_k(dense_t(pre + "self_attn.", ("o_proj",)), model.rank, sh.hq_local * cfg.head_dim))
+        else:
+            o_q, o_s = model._shard_rows(*r.linear(pre + "self_attn.o_proj"), sh.hq_local * cfg.head_dim)
+            o = Int4Linear(o_name, o_q.to(dev).contiguous(), o_s.to(dev).contiguous())
+        if is_island(gu_name, islands):
+            wt = dense_t(pre + "mlp.", ("gate_proj", "up_proj"))
+            gate_up = island(gu_name, model._shard_gate_up(wt, wt[:1])[0])
+        else:
+            gu = [r.linear(pre + "mlp.%s_proj" % p) for p in ("gate", "up")]
+            gu_q, gu_s = model._shard_gate_up(torch.cat([a for a, _ in gu], 1), torch.cat([b for _, b in gu], 1))
+            gate_up = Int4Linear(gu_name, gu_q.to(dev).contiguous(), gu_s.to(dev).contiguous())
+        if is_island(dn_name, islands):
+            down = island(dn_name, _rows_k(dense_t(pre + "mlp.", ("down_proj",)), model.rank, sh.inter_local))
+        else:
+            dn_q, dn_s = model._shard_rows(*r.linear(pre + "mlp.down_proj"), sh.inter_local)
+            down = Int4Linear(dn_name, dn_q.to(dev).contiguous(), dn_s.to(dev).contiguous())
         return LayerWeights(
             input_norm=r.get(pre + "input_layernorm.weight").to(dev, torch.bfloat16),
             post_norm=r.get(pre + "post_attention_layernorm.weight").to(dev, torch.bfloat16),
-            qkv=Int4Linear(name + "self_attn.qkv_proj", qkv_q.to(dev).contiguous(), qkv_s.to(dev).contiguous()),
-            o=Int4Linear(name + "self_attn.o_proj", o_q.to(dev).contiguous(), o_s.to(dev).contiguous()),
-            gate_up=Int4Linear(name + "mlp.gate_up_proj", gu_q.to(dev).contiguous(), gu_s.to(dev).contiguous()),
-            down=Int4Linear(name + "mlp.down_proj", dn_q.to(dev).contiguous(), dn_s.to(dev).contiguous()))
+            qkv=qkv, o=o, gate_up=gate_up, down=down)
 
     n_layers = len(model.layers) or cfg.num_layers
     model.layers = [layer("model.layers.%d." % i, "model.layers.%d." % i) for i in range(n_layers)]

@@ -223,7 +223,9 @@ class DenseModel:
         D = cfg.head_dim
         hq, hkv = sh.hq_local, sh.hkv_local
         splitk_ws = ws.splitk if ws is not None else None
-        far = self.fused_ar if (self.fused_ar is not None and self.fused_ar.fits(T, cfg.hidden)) else None
+        # the fused all-reduce epilogue belongs to the int4 GEMM (INT8 islands use NCCL)
+        far = self.fused_ar if (self.fused_ar is not None and self.fused_ar.fits(T, cfg.hidden)
+                                and isinstance(L.o, Int4Linear) and isinstance(L.down, Int4Linear)) else None
         # ---- attention block
         with stage(tag + ".input_norm"):
             if residual is None:
@@ -261,7 +263,7 @@ class DenseModel:
             with stage(tag + ".all_reduce"):
                 self._all_reduce(x)
         # ---- MLP block
-        if uses_w4a8(L.gate_up.name, T, self.w4a8):
+        if uses_w4a8(L.gate_up.name, T, self.w4a8) and L.gate_up.supports_w4a8 and L.down.supports_w4a8:
             with stage(tag + ".post_norm"):
                 hq8, hs = ops.rmsnorm(x, L.post_norm, cfg.rms_eps, residual=residual, quant=True, sync=sync_o)
             with stage(tag + ".gate_up"):
@@ -420,7 +422,7 @@ class DenseModel:
 
         for li, L in enumerate(self.layers):
             h, residual = norm(x, L.input_norm, residual) if residual is not None else (norm(x, L.input_norm, None)[0], x)
-            qkv = (h.float() @ gptq.dequant_int4(L.qkv.qweight.cpu(), L.qkv.scales.cpu())).bfloat16()
+            qkv = (h.float() @ L.qkv.dense_t()).bfloat16()
             T = qkv.shape[0]
             qkv = qkv.view(T, sh.hq_local + 2 * sh.hkv_local, D)
             q = rot(qkv[:, : sh.hq_local])
@@ -436,12 +438,12 @@ class DenseModel:
                 ends = [lens[b] - ql + t + 1 for t in range(ql)]
                 outs.append(attention_ref(qs.float(), kd, vd, ends, sh.gqa_local))
             a = torch.cat(outs, 0).bfloat16().view(T, -1)
-            x = (a.float() @ gptq.dequant_int4(L.o.qweight.cpu(), L.o.scales.cpu())).bfloat16()
+            x = (a.float() @ L.o.dense_t()).bfloat16()
             h, residual = norm(x, L.post_norm, residual)
-            gu = (h.float() @ gptq.dequant_int4(L.gate_up.qweight.cpu(), L.gate_up.scales.cpu())).bfloat16()
+            gu = (h.float() @ L.gate_up.dense_t()).bfloat16()
             I = gu.shape[1] // 2
             act = (torch.nn.functional.silu(gu[:, :I].float()) * gu[:, I:].float()).bfloat16()
-            x = (act.float() @ gptq.dequant_int4(L.down.qweight.cpu(), L.down.scales.cpu())).bfloat16()
+            x = (act.float() @ L.down.dense_t()).bfloat16()
         rows = inp.logit_rows.cpu()
         y, _ = norm(x[rows], self.final_norm, residual[rows])
         return y

@@ -197,6 +197,14 @@ def rmsnorm(x, w, eps=1e-6, residual=None, out=None, quant=False, sync=None):
     return out
 
 
+def int8_dequant(q, scale, out):
+    """INT8 island weights ``q`` [N, K] x per-row ``scale`` [N] -> bf16 into ``out`` (>= N*K elements)."""
+    require()
+    torch.ops.k8v4.int8_dequant(q, scale, out)
+    _count()
+    return out[: q.numel()].view(q.shape)
+
+
 def silu_mul(gu, out=None, quant=False):
     require()
     rows, inter = gu.shape[0], gu.shape[1] // 2
