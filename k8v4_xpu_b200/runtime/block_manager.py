@@ -54,6 +54,10 @@ class BlockManager:
         self.enable_prefix_caching = enable_prefix_caching
         self.info = [BlockInfo() for _ in range(self.num_blocks)]
         self.free: collections.deque[int] = collections.deque(range(self.num_blocks))
+        # per-sequence table version: bumped whenever entries already handed
+        # out may change (new table, replaced block, truncation, free), so a
+        # device copy of a table can be extended instead of rewritten
+        self.version: dict[int, int] = {}
         self.cached: dict[bytes, int] = {}
         self.evictable: collections.OrderedDict[int, None] = collections.OrderedDict()
         self.tables: dict[int, list[int]] = {}
@@ -140,6 +144,7 @@ class BlockManager:
             self._ref(b)
         self.tables[seq_id] = list(hit)
         self.keys[seq_id] = list(keys)
+        self._bump(seq_id)
         cached = len(hit) * self.block_size
         self.prefix_hits += cached
         return cached
@@ -175,11 +180,14 @@ class BlockManager:
                 self._ref(other)
                 table[i] = other
                 self._unref(b)
+                self._bump(seq_id)
 
     def truncate(self, seq_id: int, tokens: int) -> None:
         """Drop blocks past ``tokens`` (speculative rollback)."""
         table = self.tables[seq_id]
         keep = self.blocks_for(tokens)
+        if len(table) > keep:
+            self._bump(seq_id)
         while len(table) > keep:
             self._unref(table.pop())
         keys = self.keys[seq_id]
@@ -205,19 +213,32 @@ class BlockManager:
             table.append(nb)
         self.tables[child] = table
         self.keys[child] = list(self.keys[parent][:n_full])
+        self._bump(child)
         return copies
 
     def free_seq(self, seq_id: int) -> None:
         for b in reversed(self.tables.pop(seq_id, [])):
             self._unref(b)
         self.keys.pop(seq_id, None)
+        self._bump(seq_id)
+
+    def _bump(self, seq_id: int) -> None:
+        self.version[seq_id] = self.version.get(seq_id, 0) + 1
 
     def page_table(self, seq_id: int) -> list[int]:
         """Kernel pages of the sequence (block ids expanded by the page ratio)."""
+        return self.pages_from(seq_id, 0)
+
+    def num_pages(self, seq_id: int) -> int:
+        return len(self.tables[seq_id]) * self.ratio
+
+    def pages_from(self, seq_id: int, start: int) -> list[int]:
+        """Kernel pages of the sequence from page ``start`` on."""
         r = self.ratio
+        table = self.tables[seq_id]
         if r == 1:
-            return list(self.tables[seq_id])
-        return [b * r + i for b in self.tables[seq_id] for i in range(r)]
+            return table[start:]
+        return [b * r + i for b in table[start // r:] for i in range(r)][start % r:]
 
     def slot(self, seq_id: int, pos: int) -> int:
         table = self.tables[seq_id]

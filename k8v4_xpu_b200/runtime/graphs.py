@@ -35,6 +35,10 @@ def prepare_benign(eng, B: int, w: int) -> None:
     ws.cu_q[: B + 1].copy_(torch.arange(0, T + 1, w, dtype=torch.int32, device=eng.device))
     ws.seq_lens[:B].fill_(w)
     ws.block_table[:B].zero_()
+    rows = eng.__dict__.get("_bt_rows")
+    if rows:  # the zeroed rows no longer hold the tables stage_decode_inputs copied
+        for i in range(B):
+            rows.pop(i, None)
     ws.slots[:T].fill_(-1)  # capture must not write into live KV pages
     ws.positions[:T].zero_()
     ws.input_ids[:T].zero_()
@@ -48,7 +52,13 @@ def stage_decode_inputs(eng, sched, B: int, w: int, forced_a=None) -> None:
 
     Row i*w + j of the batch is token j of sequence i (its last token, then its
     drafts). Padding sequences (B > real batch) repeat a one-page context with
-    every KV write dropped (slot -1, write_en 0).
+    every KV write dropped (slot -1, write_en 0); their block-table row keeps
+    whatever valid page ids it held.
+
+    Block-table rows are copied incrementally: the device row of batch slot i
+    remembers (sequence, table version, pages copied), and a step sends only
+    the pages appended since (a decode step usually sends none). A changed
+    table (new sequence in the slot, replaced block, truncation) is rewritten.
     """
     ws = eng.ws
     T = B * w
@@ -56,34 +66,42 @@ def stage_decode_inputs(eng, sched, B: int, w: int, forced_a=None) -> None:
     ids = np.zeros(T, np.int64)
     pos = np.zeros(T, np.int64)
     slots = np.full(T, -1, np.int64)
-    lens = np.zeros(B, np.int32)
-    tables = []
+    lens = np.full(B, w, np.int32)  # padding sequences: one page
+    blocks = eng.blocks
+    rows = eng.__dict__.setdefault("_bt_rows", {})
+    updates = []  # (row, first page, pages)
     for i, c in enumerate(sched.chunks):
         seq = c.seq
-        toks = [seq.tokens[-1]] + seq.draft
+        toks = [seq.last_token] + seq.draft
         ids[i * w:(i + 1) * w] = toks[:w]
         pos[i * w:(i + 1) * w] = np.arange(c.start, c.start + w)
         for j in range(w):
-            slots[i * w + j] = eng.blocks.slot(seq.seq_id, c.start + j)
+            slots[i * w + j] = blocks.slot(seq.seq_id, c.start + j)
         lens[i] = c.start + w
-        tables.append(eng.blocks.page_table(seq.seq_id))
-    for i in range(B_real, B):
-        lens[i] = w  # padding sequence: reads page 0, writes nothing
-        tables.append([0])
-    Wd = ws.block_table.shape[1]
+        ver = blocks.version.get(seq.seq_id, 0)
+        n = blocks.num_pages(seq.seq_id)
+        st = rows.get(i)
+        start = st[2] if (st is not None and st[0] == seq.seq_id and st[1] == ver and st[2] <= n) else 0
+        if n > start:
+            updates.append((i, start, blocks.pages_from(seq.seq_id, start)))
+        rows[i] = (seq.seq_id, ver, n)
     n64 = 3 * T + 2 * B
     pin64 = eng._pin_i64[:n64].numpy()
     pin64[:T], pin64[T:2 * T], pin64[2 * T:3 * T] = ids, pos, slots
     pin64[3 * T:3 * T + B] = [1 if i < B_real else 0 for i in range(B)]
     pin64[3 * T + B:] = 0 if forced_a is None else np.concatenate([forced_a, np.zeros(B - len(forced_a), np.int64)])
-    n32 = (B + 1) + B + B * Wd
-    pin32 = eng._pin_i32[:n32].numpy()
+    n32 = (B + 1) + B
+    pin32 = eng._pin_i32.numpy()
     pin32[: B + 1] = np.arange(0, T + 1, w)
     pin32[B + 1: 2 * B + 1] = lens
-    bt = pin32[2 * B + 1:].reshape(B, Wd)
-    bt[:] = 0
-    for i, tb in enumerate(tables):
-        bt[i, :len(tb)] = tb
+    off = n32
+    table_bytes = 0
+    for i, first, pages in updates:
+        k = len(pages)
+        pin32[off:off + k] = pages
+        ws.block_table[i, first:first + k].copy_(eng._pin_i32[off:off + k], non_blocking=True)
+        off += k
+        table_bytes += 4 * k
     g64 = eng._pin_i64[:n64].to(eng.device, non_blocking=True)
     g32 = eng._pin_i32[:n32].to(eng.device, non_blocking=True)
     ws.input_ids[:T].copy_(g64[:T], non_blocking=True)
@@ -93,8 +111,7 @@ def stage_decode_inputs(eng, sched, B: int, w: int, forced_a=None) -> None:
     ws.forced_a[:B].copy_(g64[3 * T + B:], non_blocking=True)
     ws.cu_q[: B + 1].copy_(g32[: B + 1], non_blocking=True)
     ws.seq_lens[:B].copy_(g32[B + 1: 2 * B + 1], non_blocking=True)
-    ws.block_table[:B].copy_(g32[2 * B + 1:].view(B, Wd), non_blocking=True)
-    eng.h2d_bytes += n64 * 8 + n32 * 4
+    eng.h2d_bytes += n64 * 8 + n32 * 4 + table_bytes
 
 
 class DecodeGraphs:

@@ -50,8 +50,14 @@ class Sequence:
     prefill_start: float | None = None
 
     @property
-    def tokens(self) -> list[int]:
-        return self.prompt + self.output
+    def tokens(self) -> "TokenView":
+        """prompt + output without copying either (a 128K-token prompt made the
+        concatenation a per-step cost): len(), indexing, slices (lists)."""
+        return TokenView(self.prompt, self.output)
+
+    @property
+    def last_token(self) -> int:
+        return self.output[-1] if self.output else self.prompt[-1]
 
     @property
     def num_tokens(self) -> int:
@@ -64,6 +70,42 @@ class Sequence:
     @property
     def done(self) -> bool:
         return self.status == SeqStatus.FINISHED
+
+
+class TokenView:
+    """Read-only concatenation of two token lists."""
+
+    __slots__ = ("a", "b")
+
+    def __init__(self, a: list[int], b: list[int]):
+        self.a, self.b = a, b
+
+    def __len__(self) -> int:
+        return len(self.a) + len(self.b)
+
+    def __iter__(self):
+        yield from self.a
+        yield from self.b
+
+    def __eq__(self, other) -> bool:
+        return list(self) == list(other)
+
+    def __getitem__(self, i):
+        na = len(self.a)
+        if isinstance(i, slice):
+            start, stop, step = i.indices(len(self))
+            if step != 1:
+                return list(self)[i]
+            if stop <= na:
+                return self.a[start:stop]
+            if start >= na:
+                return self.b[start - na:stop - na]
+            return self.a[start:] + self.b[:stop - na]
+        if i < 0:
+            i += len(self)
+        if not 0 <= i < len(self):
+            raise IndexError("token index out of range")
+        return self.a[i] if i < na else self.b[i - na]
 
 
 @dataclasses.dataclass
