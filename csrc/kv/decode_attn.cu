@@ -567,36 +567,46 @@ __global__ void __launch_bounds__(DCfg<NPAD>::NTHREADS, 1)
 // rank dimension: split index s of the merged set is (rank s / nsplit, split
 // s % nsplit), each rank's partials `rank_stride_*` floats apart (the
 // all-gathered workspaces of every rank).
-__global__ void __launch_bounds__(128) decode_combine_kernel(const float* __restrict__ ws_o,
-                                                             const float* __restrict__ ws_ml, const int32_t* cu_q,
-                                                             __nv_bfloat16* out, int nsplit, int npad, int gqa,
-                                                             int hq_total, int head_offset, int nrank,
-                                                             int64_t rank_stride_o, int64_t rank_stride_ml) {
+// Merge the split partials of one query row: threads (group g, dim d), group
+// g takes splits g, g + 4, ... so every O load of the row is in flight at
+// once; the groups' sums meet in shared memory.
+constexpr int COMBINE_GROUPS = 4;
+__global__ void __launch_bounds__(128 * COMBINE_GROUPS) decode_combine_kernel(
+    const float* __restrict__ ws_o, const float* __restrict__ ws_ml, const int32_t* cu_q, __nv_bfloat16* out,
+    int nsplit, int npad, int gqa, int hq_total, int head_offset, int nrank, int64_t rank_stride_o,
+    int64_t rank_stride_ml) {
   pdl_trigger();
   pdl_wait();  // everything this kernel reads may come from the previous one
   __shared__ float wsh[128];
   __shared__ float red[8];
-  const int r = blockIdx.x, hl = blockIdx.y, seq = blockIdx.z, d = threadIdx.x;
+  __shared__ float part[COMBINE_GROUPS - 1][D];
+  const int r = blockIdx.x, hl = blockIdx.y, seq = blockIdx.z;
+  const int d = threadIdx.x & (D - 1), grp = threadIdx.x / D;
   const int qb = cu_q[seq], q_len = cu_q[seq + 1] - qb;
-  if (r >= q_len * gqa) return;
+  if (r >= q_len * gqa) return;  // uniform for the CTA
   const int64_t base = ((int64_t)seq * gridDim.y + hl) * nsplit;
   const int ntot = nsplit * nrank;  // <= 128
+  // (m, l) of every split: threads of group 0, one split each
   float m = -INFINITY, l = 0.f;
-  if (d < ntot) {
+  if (grp == 0 && d < ntot) {
     const int rk = d / nsplit, sp = d % nsplit;
     const float* ml = ws_ml + rk * rank_stride_ml;
     m = ml[((base + sp) * 2) * npad + r];
     l = ml[((base + sp) * 2 + 1) * npad + r];
   }
-  float M = warp_max(m);
-  if ((d & 31) == 0) red[d >> 5] = M;
+  if (grp == 0) {
+    const float M0 = warp_max(m);
+    if ((d & 31) == 0) red[d >> 5] = M0;
+  }
   __syncthreads();
-  M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-  const float w = (m == -INFINITY || M == -INFINITY) ? 0.f : exp2f(m - M);
-  if (d < ntot) wsh[d] = w;
-  float L = warp_sum(w * l);
-  __syncthreads();
-  if ((d & 31) == 0) red[4 + (d >> 5)] = L;
+  const float M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  float L = 0.f;
+  if (grp == 0) {
+    const float w = (m == -INFINITY || M == -INFINITY) ? 0.f : exp2f(m - M);
+    if (d < ntot) wsh[d] = w;
+    const float Lw = warp_sum(w * l);
+    if ((d & 31) == 0) red[4 + (d >> 5)] = Lw;
+  }
   __syncthreads();
   L = red[4] + red[5] + red[6] + red[7];
   const int64_t stride = (int64_t)npad * D;
@@ -604,18 +614,27 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const float* __rest
   for (int rk = 0; rk < nrank; ++rk) {
     const float* o = ws_o + rk * rank_stride_o + (base * npad + r) * D + d;
     const float* wr = wsh + rk * nsplit;
-    int s = 0;
-    for (; s + 8 <= nsplit; s += 8) {
+    int s = grp;
+    for (; s + 7 * COMBINE_GROUPS < nsplit; s += 8 * COMBINE_GROUPS) {
       float v[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = o[(s + i) * stride];
+      for (int i = 0; i < 8; ++i) v[i] = o[(s + i * COMBINE_GROUPS) * stride];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc += wr[s + i] > 0.f ? wr[s + i] * v[i] : 0.f;
+      for (int i = 0; i < 8; ++i) {
+        const float wi = wr[s + i * COMBINE_GROUPS];
+        acc += wi > 0.f ? wi * v[i] : 0.f;
+      }
     }
-    for (; s < nsplit; ++s) acc += wr[s] > 0.f ? wr[s] * o[s * stride] : 0.f;
+    for (; s < nsplit; s += COMBINE_GROUPS) acc += wr[s] > 0.f ? wr[s] * o[s * stride] : 0.f;
   }
-  const int t = r / gqa, g = r % gqa, h = hl + head_offset;
-  out[((int64_t)(qb + t) * hq_total + (int64_t)h * gqa + g) * D + d] = __float2bfloat16_rn(L > 0.f ? acc / L : 0.f);
+  if (grp > 0) part[grp - 1][d] = acc;
+  __syncthreads();
+  if (grp == 0) {
+#pragma unroll
+    for (int g = 0; g < COMBINE_GROUPS - 1; ++g) acc += part[g][d];
+    const int t = r / gqa, g = r % gqa, h = hl + head_offset;
+    out[((int64_t)(qb + t) * hq_total + (int64_t)h * gqa + g) * D + d] = __float2bfloat16_rn(L > 0.f ? acc / L : 0.f);
+  }
 }
 
 }  // namespace attn
@@ -745,7 +764,7 @@ extern "C" int k8v4_decode_attn(const void* q, const int32_t* cu_q, const int32_
   else if (rows <= 48) { npad = 48; rc = launch_decode<48>(tm, p, heads, nseq, st); }
   else { npad = 64; rc = launch_decode<64>(tm, p, heads, nseq, st); }
   if (rc || nsplit == 1) return rc;
-  return launch_k(decode_combine_kernel, dim3(rows, heads, nseq), dim3(D), 0, st, (const float*)ws_o,
+  return launch_k(decode_combine_kernel, dim3(rows, heads, nseq), dim3(D * COMBINE_GROUPS), 0, st, (const float*)ws_o,
                   (const float*)ws_ml, cu_q, reinterpret_cast<__nv_bfloat16*>(out), nsplit, npad, gqa, hq_total,
                   head_offset, 1, (int64_t)0, (int64_t)0) == cudaSuccess
              ? 0
@@ -764,7 +783,7 @@ extern "C" int k8v4_decode_combine_ranks(const float* ws_all, int64_t rank_float
   if (rows > 64 || nrank < 1 || nsplit < 1 || nrank * nsplit > 128) return 1;
   const int npad = rows <= 16 ? 16 : rows <= 32 ? 32 : rows <= 48 ? 48 : 64;
   const int64_t ml_floats = (int64_t)nseq * heads * nsplit * 2 * npad;
-  return launch_k(decode_combine_kernel, dim3(rows, heads, nseq), dim3(D), 0, st, ws_all + ml_floats, ws_all, cu_q,
+  return launch_k(decode_combine_kernel, dim3(rows, heads, nseq), dim3(D * COMBINE_GROUPS), 0, st, ws_all + ml_floats, ws_all, cu_q,
                   reinterpret_cast<__nv_bfloat16*>(out), nsplit, npad, gqa, hq_total, head_offset, nrank,
                   rank_floats, rank_floats) == cudaSuccess
              ? 0

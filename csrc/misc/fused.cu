@@ -146,26 +146,37 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const __nv_bfloat16* 
   const int64_t row = blockIdx.x;
   if (sync.flag) sync_wait(sync);
   float v[VPT][8];
+  float rs[VPT][8];
   float ss = 0.f;
+  // every load first: the zeroing and residual stores below would otherwise
+  // order each later load behind them (the pointers may alias)
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = (threadIdx.x + i * kThreads) * 8;
+    if (c < n) {
+      if (xf) {
+        const float4* p4 = reinterpret_cast<const float4*>(xf + row * n + c);
+        const float4 a = p4[0], b = p4[1];
+        v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
+        v[i][4] = b.x; v[i][5] = b.y; v[i][6] = b.z; v[i][7] = b.w;
+      } else {
+        load8(x + row * n + c, v[i]);
+      }
+      if (residual) load8(residual + row * n + c, rs[i]);
+    }
+  }
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int c = (threadIdx.x + i * kThreads) * 8;
     if (c < n) {
       if (xf) {
         float4* p4 = reinterpret_cast<float4*>(xf + row * n + c);
-        const float4 a = p4[0], b = p4[1];
-        v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
-        v[i][4] = b.x; v[i][5] = b.y; v[i][6] = b.z; v[i][7] = b.w;
         p4[0] = make_float4(0.f, 0.f, 0.f, 0.f);
         p4[1] = make_float4(0.f, 0.f, 0.f, 0.f);
-      } else {
-        load8(x + row * n + c, v[i]);
       }
       if (residual) {
-        float r[8];
-        load8(residual + row * n + c, r);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[i][j] += r[j];
+        for (int j = 0; j < 8; ++j) v[i][j] += rs[i][j];
         // the residual stream is kept in bf16
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[i][j] = __bfloat162float(__float2bfloat16_rn(v[i][j]));
