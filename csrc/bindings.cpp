@@ -17,7 +17,7 @@
 extern "C" {
 int k8v4_kv_store(int fmt, const void* k, int64_t k_stride_t, const void* v, int64_t v_stride_t, const int64_t* slots,
                   void* cache, int64_t num_pages, int page_bytes, int T, int hkv, cudaStream_t st);
-int k8v4_rope_store(const void* qkv, const float* cos_sin, const int64_t* positions, void* q_out,
+int k8v4_rope_store(const void* qkv, int qkv_fp32, const float* cos_sin, const int64_t* positions, void* q_out,
                     const int64_t* slots, void* cache, int64_t num_pages, int page_bytes, int T, int hq, int hkv,
                     cudaStream_t st);
 int k8v4_decode_attn(const void* q, const int32_t* cu_q, const int32_t* seq_lens, const int32_t* q_ends,
@@ -112,7 +112,10 @@ void rope_store(const at::Tensor& qkv, const at::Tensor& cos_sin, const at::Tens
   check_contig(q_out, "q_out");
   check_contig(slots, "slot_mapping");
   check_contig(cache, "cache");
-  TORCH_CHECK(qkv.scalar_type() == at::kBFloat16 && q_out.scalar_type() == at::kBFloat16, "qkv/q_out bf16");
+  // qkv: bf16 rows, or the qkv GEMM's fp32 split-K sums (finished and zeroed here)
+  TORCH_CHECK((qkv.scalar_type() == at::kBFloat16 || qkv.scalar_type() == at::kFloat) &&
+                  q_out.scalar_type() == at::kBFloat16,
+              "qkv bf16 or fp32 split-K sums, q_out bf16");
   TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.size(-1) == 128, "cos_sin fp32 [pos, 128]");
   TORCH_CHECK(positions.scalar_type() == at::kLong && slots.scalar_type() == at::kLong, "positions/slots int64");
   const int64_t T = qkv.size(0);
@@ -121,7 +124,8 @@ void rope_store(const at::Tensor& qkv, const at::Tensor& cos_sin, const at::Tens
   TORCH_CHECK(positions.numel() == T && slots.numel() == T, "positions/slots length");
   TORCH_CHECK(cache.scalar_type() == at::kByte && cache.size(1) == 16 * hkv * 202, "b200 cache layout");
   c10::cuda::CUDAGuard g(cache.device());
-  check_rc(k8v4_rope_store(qkv.data_ptr(), cos_sin.data_ptr<float>(), positions.data_ptr<int64_t>(), q_out.data_ptr(),
+  check_rc(k8v4_rope_store(qkv.data_ptr(), qkv.scalar_type() == at::kFloat ? 1 : 0, cos_sin.data_ptr<float>(),
+                           positions.data_ptr<int64_t>(), q_out.data_ptr(),
                            slots.data_ptr<int64_t>(), cache.data_ptr(), cache.size(0), (int)cache.size(1), (int)T,
                            (int)hq, (int)hkv, cur_stream()),
            "rope_store");

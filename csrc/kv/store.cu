@@ -18,6 +18,7 @@ namespace kv {
 
 struct StoreArgs {
   const __nv_bfloat16* qkv;  // fused rows [T, (hq + 2*hkv) * D] (b200) or nullptr
+  float* qkv_f;              // or the same rows as the qkv GEMM's fp32 split-K sums (read, then zeroed)
   const __nv_bfloat16* k;    // separate K rows [T, hkv, D] when qkv == nullptr
   const __nv_bfloat16* v;
   int64_t k_stride_t, v_stride_t;  // token strides (elements) of k / v
@@ -50,17 +51,35 @@ __global__ void store_b200_kernel(StoreArgs a) {
   const int hh = gw % heads_per_tok;
   const int d0 = lane * 4;
 
-  float x[4];
-  const __nv_bfloat16* src;
+  float x[4], y[4];
   const int row = a.hq + 2 * a.hkv;
+  // 4 values of a fused qkv row: bf16, or the GEMM's fp32 split-K sums, which
+  // are rounded to bf16 as the split-K finish would and zeroed for the next
+  // split-K GEMM (every element of the row is read by exactly one warp)
+  auto load_row4 = [&](int64_t off, float (&f)[4]) {
+    if (a.qkv_f) {
+      float4* p4 = reinterpret_cast<float4*>(a.qkv_f + off);
+      const float4 v = *p4;
+      *p4 = make_float4(0.f, 0.f, 0.f, 0.f);
+      f[0] = __bfloat162float(__float2bfloat16_rn(v.x));
+      f[1] = __bfloat162float(__float2bfloat16_rn(v.y));
+      f[2] = __bfloat162float(__float2bfloat16_rn(v.z));
+      f[3] = __bfloat162float(__float2bfloat16_rn(v.w));
+    } else {
+      const uint2 raw = *reinterpret_cast<const uint2*>(a.qkv + off);
+      const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+      const float2 f0 = __bfloat1622float2(p2[0]), f1 = __bfloat1622float2(p2[1]);
+      f[0] = f0.x; f[1] = f0.y; f[2] = f1.x; f[3] = f1.y;
+    }
+  };
   if (ROPE) {
-    // head hh < hq: a query head; otherwise KV head hh - hq
+    // head hh < hq: a query head; otherwise KV head hh - hq, whose V columns
+    // are read here too (before any early return, so they are always consumed)
     const int col = (hh < a.hq) ? hh * D : (a.hq + (hh - a.hq)) * D;
-    src = a.qkv + (int64_t)t * row * D + col;
+    load_row4((int64_t)t * row * D + col + d0, x);
+    if (hh >= a.hq) load_row4((int64_t)t * row * D + (a.hq + a.hkv + (hh - a.hq)) * D + d0, y);
   } else {
-    src = a.k + (int64_t)t * a.k_stride_t + (int64_t)hh * D;
-  }
-  {
+    const __nv_bfloat16* src = a.k + (int64_t)t * a.k_stride_t + (int64_t)hh * D;
     const uint2 raw = *reinterpret_cast<const uint2*>(src + d0);
     const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
     const float2 f0 = __bfloat1622float2(p2[0]), f1 = __bfloat1622float2(p2[1]);
@@ -118,10 +137,8 @@ __global__ void store_b200_kernel(StoreArgs a) {
   if (lane == 0) *reinterpret_cast<__half*>(base + 3072 + off * 2) = ks;
 
   // ---- V: int4 symmetric per 32-dim group (8 lanes), fp16 scale
-  const __nv_bfloat16* vsrc = ROPE ? (a.qkv + (int64_t)t * row * D + (a.hq + a.hkv + h) * D)
-                                   : (a.v + (int64_t)t * a.v_stride_t + (int64_t)h * D);
-  float y[4];
-  {
+  if (!ROPE) {
+    const __nv_bfloat16* vsrc = a.v + (int64_t)t * a.v_stride_t + (int64_t)h * D;
     const uint2 raw = *reinterpret_cast<const uint2*>(vsrc + d0);
     const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
     const float2 f0 = __bfloat1622float2(p2[0]), f1 = __bfloat1622float2(p2[1]);
@@ -242,12 +259,17 @@ extern "C" int k8v4_kv_store(int fmt, const void* k, int64_t k_stride_t, const v
 }
 
 // b200 format, fused: rotate q/k of the qkv rows, write q_out, store K/V.
-extern "C" int k8v4_rope_store(const void* qkv, const float* cos_sin, const int64_t* positions, void* q_out,
-                               const int64_t* slots, void* cache, int64_t num_pages, int page_bytes, int T, int hq,
-                               int hkv, cudaStream_t st) {
+// `qkv_fp32` = 1: qkv holds the qkv GEMM's fp32 split-K sums, which this
+// call finishes (bf16 rounding) and leaves zeroed.
+extern "C" int k8v4_rope_store(const void* qkv, int qkv_fp32, const float* cos_sin, const int64_t* positions,
+                               void* q_out, const int64_t* slots, void* cache, int64_t num_pages, int page_bytes,
+                               int T, int hq, int hkv, cudaStream_t st) {
   if (T <= 0) return 0;
   StoreArgs a{};
-  a.qkv = reinterpret_cast<const __nv_bfloat16*>(qkv);
+  if (qkv_fp32)
+    a.qkv_f = reinterpret_cast<float*>(const_cast<void*>(qkv));
+  else
+    a.qkv = reinterpret_cast<const __nv_bfloat16*>(qkv);
   a.cos_sin = cos_sin;
   a.positions = positions;
   a.q_out = reinterpret_cast<__nv_bfloat16*>(q_out);

@@ -234,7 +234,9 @@ class DenseModel:
             else:
                 h = ops.rmsnorm(x, L.input_norm, cfg.rms_eps, residual=residual, sync=sync)
         with stage(tag + ".gemm_qkv"):
-            qkv = L.qkv(h, ws=splitk_ws)
+            # split-K at decode sizes: the fp32 sums go straight to rope_store,
+            # which finishes them (bf16 rounding) and zeroes the accumulator
+            qkv = L.qkv(h, ws=splitk_ws, defer=True)
         q = torch.empty((T, hq, D), dtype=torch.bfloat16, device=self.device)
         with stage(tag + ".rope_store"):
             ops.rope_store(qkv, self.rope, inp.positions, q, inp.slots, cache, hq, hkv)

@@ -90,6 +90,9 @@ def kv_store(k: torch.Tensor, v: torch.Tensor, slots: torch.Tensor, cache: torch
 
 def rope_store(qkv: torch.Tensor, cos_sin: torch.Tensor, positions: torch.Tensor, q_out: torch.Tensor,
                slots: torch.Tensor, cache: torch.Tensor, hq: int, hkv: int) -> None:
+    """RoPE on the q / k heads of fused qkv rows, q written to ``q_out``, K and V
+    quantized into their pages. ``qkv`` may be bf16 rows or the qkv GEMM's fp32
+    split-K sums (then finished here and left zeroed for the next GEMM)."""
     require()
     torch.ops.k8v4.rope_store(qkv, cos_sin, positions, q_out, slots, cache, hq, hkv)
     _count()

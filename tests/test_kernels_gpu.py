@@ -81,6 +81,31 @@ def test_rope_store_matches_oracle():
     assert torch.equal(cache.cpu(), ref)
 
 
+def test_rope_store_finishes_fp32_split_k_sums():
+    """fp32 split-K sums in: same q and pages as their bf16 rounding, and the
+    accumulator left zeroed, also for a token whose KV write is skipped."""
+    hq, hkv, D = 12, 2, 128
+    layout = b200_layout(hkv)
+    g = _gen(3)
+    T, pages = 9, 4
+    sums = torch.randn(T, (hq + 2 * hkv) * D, generator=g)
+    pos = torch.randint(0, 4000, (T,), generator=g)
+    slots = torch.randperm(pages * 16, generator=g)[:T].to(torch.int64)
+    slots[4] = -1  # padding row: no KV write, its sums are still consumed
+    table = _rope_table(4096).to(DEV)
+    q_a = torch.empty(T, hq, D, dtype=torch.bfloat16, device=DEV)
+    q_b = torch.empty_like(q_a)
+    cache_a = torch.zeros(pages, layout.page_bytes, dtype=torch.uint8, device=DEV)
+    cache_b = torch.zeros_like(cache_a)
+    ws = sums.to(DEV)
+    ops.rope_store(ws, table, pos.to(DEV), q_a, slots.to(DEV), cache_a, hq, hkv)
+    ops.rope_store(sums.bfloat16().to(DEV), table, pos.to(DEV), q_b, slots.to(DEV), cache_b, hq, hkv)
+    torch.cuda.synchronize()
+    assert ops.status() == 0
+    assert torch.equal(q_a, q_b) and torch.equal(cache_a, cache_b)
+    assert ws.abs().max().item() == 0.0
+
+
 # --------------------------------------------------------------------- GEMM
 def _int4_weights(N, K, seed):
     g = _gen(seed)
