@@ -132,3 +132,36 @@ def test_bake_cli_random_and_verify(tmp_path):
     assert out.returncode == 0, out.stderr
     rep = json.loads(out.stdout.strip().splitlines()[-1])
     assert rep["layers"] == 1 and rep["mtp"] and rep["lm_head_rows"] == TINY.vocab
+
+
+def test_tp8_shards_replicate_kv_heads_and_tile_the_full_model():
+    """TP 8 on the 27B head structure (24 Q heads, 4 KV heads): every rank
+    holds 3 Q heads and KV head rank // 2 (two ranks per KV head), and the
+    ranks' shards are exact slices of the TP 1 weights."""
+    from k8v4_xpu_b200.models.config import ModelConfig
+    cfg = ModelConfig(name="tp8-shape", num_layers=1, hidden=512, num_heads=24, num_kv_heads=4, head_dim=128,
+                      intermediate=2048, vocab=4096, max_position=1024)
+    D = cfg.head_dim
+    full = DenseModel(cfg, device="cpu").random_init(seed=11)
+    F = full.layers[0]
+    fq = F.qkv.dense_t()            # [K, q | k | v]
+    fo, fg, fd = F.o.dense_t(), F.gate_up.dense_t(), F.down.dense_t()
+    q_sz, kv_sz, I = cfg.q_size, cfg.kv_size, cfg.intermediate
+    for rank in range(8):
+        m = DenseModel(cfg, tp=8, rank=rank, device="cpu").random_init(seed=11)
+        sh = m.shape
+        assert (sh.hq_local, sh.hkv_local, sh.kv_replicas, sh.gqa_local) == (3, 1, 2, 3)
+        L = m.layers[0]
+        kvh = rank // 2
+        want_qkv = torch.cat([fq[:, rank * 3 * D:(rank + 1) * 3 * D],
+                              fq[:, q_sz + kvh * D:q_sz + (kvh + 1) * D],
+                              fq[:, q_sz + kv_sz + kvh * D:q_sz + kv_sz + (kvh + 1) * D]], 1)
+        assert torch.equal(L.qkv.dense_t(), want_qkv), rank
+        assert torch.equal(L.o.dense_t(), fo[rank * 3 * D:(rank + 1) * 3 * D]), rank
+        il = I // 8
+        assert torch.equal(L.gate_up.dense_t(), torch.cat([fg[:, rank * il:(rank + 1) * il],
+                                                           fg[:, I + rank * il:I + (rank + 1) * il]], 1)), rank
+        assert torch.equal(L.down.dense_t(), fd[rank * il:(rank + 1) * il]), rank
+        v = cfg.vocab // 8
+        assert torch.equal(m.lm_head.weight[:v], full.lm_head.weight[rank * v:(rank + 1) * v]), rank
+        assert torch.equal(m.embed_codes, full.embed_codes[rank * v:(rank + 1) * v]), rank
