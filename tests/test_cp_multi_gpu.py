@@ -1,6 +1,7 @@
 """Context-parallel serving on 2 GPUs: page-sharded KV, peer-page prefill (GPU)."""
 import os
 import socket
+import tempfile
 import traceback
 
 import pytest
@@ -21,9 +22,11 @@ def _port():
 
 
 def _log(rank, msg):
-    """Progress of a rank, flushed to a file (a stalled rank shows where it stopped)."""
-    os.makedirs("gpurun_out", exist_ok=True)
-    with open("gpurun_out/cp_rank%d.log" % rank, "a") as f:
+    """Progress of a rank, flushed to a file (a stalled rank shows where it
+    stopped) in $K8V4_TEST_LOG_DIR, else the system temporary directory."""
+    d = os.environ.get("K8V4_TEST_LOG_DIR") or tempfile.gettempdir()
+    os.makedirs(d, exist_ok=True)
+    with open(os.path.join(d, "k8v4_cp_rank%d.log" % rank), "a") as f:
         f.write(msg + "\n")
 
 
