@@ -2,8 +2,10 @@
 //
 // Replaces the reference's per-KV-head gather + oneDNN SDPA pipeline
 // (k8v4_v030/onednn_prefill.py:188-241, native/k8v4_sdpa.cpp:83-228 and the
-// Triton gather prefill_gather_triton.py:15-66): no fp16 copy of the prefix is
-// materialized, nothing is compiled per shape and there are no host waits.
+// Triton gather prefill_gather_triton.py:15-66): K stays int8 (read by TMA
+// straight from the pages), only V is dequantized, once per tile and KV head
+// into a staging buffer in the MMA's own layout (prefill_stage_kernel);
+// nothing is compiled per shape and there are no host waits.
 //
 // One CTA per (query tile, KV head, sequence). A query tile is TQ = 128/gqa
 // consecutive tokens x the gqa query heads of this KV head = up to 128 rows,
@@ -14,10 +16,11 @@
 //   softmax      : two threads per row (64 keys each), lazy rescale (tau 8, log2 units)
 //   O[row, dim] += P(fp16, TMEM) x V_tile(fp16, MN-major)   tcgen05 kind::f16, A from TMEM
 //
-// Warp roles: 0 = TMA producer, 1 = TMEM owner + MMA issuer, 2, 3, 12, 13 =
-// V converters, 4-11 = softmax / epilogue (lane quadrant = warp & 3, key and
-// O-column half = (warp - 4) >> 2). S and P are double-buffered in TMEM, so
-// the softmax of tile j overlaps QK(j + 1) and PV(j - 1).
+// Warp roles: 0 = producer (K pages by TMA, staged V and k-scales by bulk
+// copies), 1 = TMEM owner + MMA issuer, 2-9 = softmax / epilogue (lane
+// quadrant = warp & 3, key and O-column half = (warp - 2) >> 2). S and P are
+// double-buffered in TMEM, so the softmax of tile j overlaps QK(j + 1) and
+// PV(j - 1).
 #include "attn_common.cuh"
 
 namespace k8v4 {
