@@ -7,7 +7,9 @@
 // TMEM lanes, keys / dims on the columns:
 //
 //   S[row, key]  = Q8 (A, smem) x K_tile^T (B, TMA)       tcgen05 kind::i8 -> TMEM
-//   softmax      : one thread per row over its 128 scores (tcgen05.ld),
+//   softmax      : the rows are replicated down the 128 lanes; each lane
+//                  quadrant's warp takes its slice of every tile's keys
+//                  (tcgen05.ld), slice maxima meet through shared memory,
 //                  lazy rescale (tau = 8 in log2 units), P -> TMEM (tcgen05.st)
 //   O[row, dim] += P (A, TMEM) x V_tile (B, fp16 smem)     tcgen05 kind::f16 -> TMEM
 //
@@ -16,8 +18,10 @@
 // merges the splits (the reference's stage-2 merge, :847-1246). With one
 // split the CTA writes the normalized output directly.
 //
-// Warp roles: 0 = TMA producer, 1 = TMEM owner + MMA issuer, 4-5 = softmax /
-// epilogue (lane quadrants 0-1 = rows 0-63), 2, 3, 6, 7 = V converters.
+// Warp roles: 0 = producer (a tile of 8 consecutive pages in two TMA boxes,
+// else per-page copies), 1 = TMEM owner + MMA issuer (polls its QK and PV
+// queues), 4-7 = softmax / epilogue (one per TMEM lane quadrant), 2, 3, 8..
+// = V converters.
 #include "attn_common.cuh"
 
 namespace k8v4 {
