@@ -18,12 +18,16 @@
 //                tile goes straight from TMA into the MMA, one group = all K.
 //
 // Roles: warp 0 issues TMA, warp 1 owns TMEM and issues MMAs (one elected
-// thread), the next NCONV warps convert raw weights, the last NACC warps
-// accumulate TMEM partials and write the output. TMEM partials are double
-// buffered so group g+1's MMAs overlap group g's rescale.
+// thread; at decode sizes two more warps issue too, each taking every third
+// K group into its own accumulator buffers), the next NCONV warps convert
+// raw weights, the NACC accumulator warps fold TMEM partials into fp32 and
+// write the output. NBUF TMEM partial buffers let group g+1's MMAs overlap
+// group g's rescale.
 //
 // Split-K: gridDim.z slices K; with more than one slice the CTA adds fp32
-// partial sums into `ws` with red.global.add and a finishing kernel converts.
+// partial sums into `ws` with red.global.add, and a consumer finishes them
+// (the splitk_finish kernel, the fused RMSNorm, or the RoPE / cache-store
+// kernel for the qkv projection), zeroing `ws` for the next GEMM.
 //
 // GEMM -> all-reduce (tensor parallel row-parallel projections): with
 // `ws_mc` set, the partial sums go to the multicast address of a symmetric
