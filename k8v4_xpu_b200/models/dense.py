@@ -3,8 +3,8 @@
 Per layer (one rank of a TP group):
 
     residual, h = rmsnorm(x + residual)            fused add + norm
-    qkv         = h @ Wqkv                         W4A16 (tcgen05)
-    q, K/V      = rope_store(qkv)                  RoPE + K8/V4 quantized page write
+    qkv         = h @ Wqkv                         W4A16 (tcgen05); decode: fp32 split-K sums
+    q, K/V      = rope_store(qkv)                  (finish split-K +) RoPE + K8/V4 page write
     a           = paged attention(q, pages)        decode: split-K; prefill: causal tiles
     x           = a @ Wo                           W4A16, then TP all-reduce
     residual, h = rmsnorm(x + residual)            (+ int8 quant when W4A8 runs)
