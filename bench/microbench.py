@@ -6,7 +6,7 @@ L2 flush (a 256 MB write) between iterations so weights and KV come from
 HBM. Fractions are against MEASURED_PEAKS.json (STREAM copy GB/s and cuBLAS
 bf16 TFLOP/s) when present, else the pool's fallback (6,650 GB/s, 1,590 TF).
 
-    python bench/microbench.py [--only gemm|attn|misc] [--ctx 128197]
+    python bench/microbench.py [--only gemm|mlp|attn|misc] [--ctx 128197]
 """
 from __future__ import annotations
 
@@ -124,6 +124,34 @@ def bench_gemm():
         report("w8a8 lm_head M=%d" % M, t, bytes_=V * H + V * 2)
 
 
+def bench_mlp():
+    """BASELINE config 2 at TP1: the W4A8 MLP layer (int8 activations with a
+    per-token scale; gate_up -> SiLU-mul + int8 quant -> down) at M = 1, 7,
+    28, 4224 and 16384 tokens; each GEMM and the whole layer."""
+    H, I = 5120, 17408
+    gq, gs = rand_int4(2 * I, H)
+    dq, ds = rand_int4(H, I)
+    for M in (1, 7, 28, 4224, 16384):
+        xq = torch.randint(-127, 127, (M, H), dtype=torch.int8, device="cuda")
+        xs = torch.rand(M, device="cuda") * 0.01
+        gu = torch.empty(M, 2 * I, dtype=torch.bfloat16, device="cuda")
+        out = torch.empty(M, H, dtype=torch.bfloat16, device="cuda")
+        aq, as_ = ops.silu_mul(ops.wq_gemm(ops.W4A8, gq, gs, xq, xscale=xs, out=gu), quant=True)
+        iters = 5 if M >= 4224 else 20
+        t_gu = timeit(lambda: ops.wq_gemm(ops.W4A8, gq, gs, xq, xscale=xs, out=gu), iters=iters)
+        t_dn = timeit(lambda: ops.wq_gemm(ops.W4A8, dq, ds, aq, xscale=as_, out=out), iters=iters)
+
+        def layer():
+            ops.wq_gemm(ops.W4A8, gq, gs, xq, xscale=xs, out=gu)
+            a8, a8s = ops.silu_mul(gu, quant=True)
+            ops.wq_gemm(ops.W4A8, dq, ds, a8, xscale=a8s, out=out)
+        t_l = timeit(layer, iters=iters)
+        wbytes = gq.numel() * 4 + gs.numel() * 2 + dq.numel() * 4 + ds.numel() * 2
+        report("w4a8 mlp gate_up M=%d" % M, t_gu, flops=2 * M * 2 * I * H)
+        report("w4a8 mlp down M=%d" % M, t_dn, flops=2 * M * H * I)
+        report("w4a8 mlp layer M=%d" % M, t_l, bytes_=wbytes, flops=2 * M * 3 * I * H)
+
+
 def fill_cache(ctx, nseq, hkv, gqa):
     layout = b200_layout(hkv, gqa)
     pages_per = (ctx + 15) // 16
@@ -189,6 +217,8 @@ def main():
     print(json.dumps({"peaks": {"hbm_gbs": HBM, "bf16_tflops": TF, "source": SRC}}))
     if a.only in (None, "gemm"):
         bench_gemm()
+    if a.only in (None, "mlp"):
+        bench_mlp()
     if a.only in (None, "attn"):
         bench_attn(a.ctx)
     if a.only in (None, "misc"):
