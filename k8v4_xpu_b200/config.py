@@ -23,6 +23,7 @@ import os
 from typing import Any, Mapping, Sequence
 
 from .kv.layout import CACHE_DTYPE
+from .kv.skip_layers import parse_layers, resolve_skip_dtype
 
 PROFILES: dict[str, dict[str, Any]] = {
     # launch.sh:10-32
@@ -138,6 +139,8 @@ class ServeConfig:
     dry_run: bool = False
     profile: str | None = None
     fit_capacity: bool = True
+    kv_cache_dtype_skip_layers: tuple[int, ...] = ()
+    kv_skip_dtype: str | None = None
 
     @property
     def world_size(self) -> int:
@@ -164,7 +167,8 @@ class ServeConfig:
             block_size=self.block_size, gpu_memory_utilization=self.gpu_memory_utilization,
             num_kv_blocks=self.num_kv_blocks, speculative_tokens=self.speculative_tokens,
             cuda_graphs=self.cuda_graphs, capture_sizes=seqs, seed=self.seed, layers=self.layers,
-            forced_accept_mean=self.forced_accept_mean, device=device)
+            forced_accept_mean=self.forced_accept_mean, device=device,
+            kv_cache_dtype_skip_layers=self.kv_cache_dtype_skip_layers, kv_skip_dtype=self.kv_skip_dtype)
 
     def validate(self) -> None:
         if self.kv_cache_dtype != CACHE_DTYPE:
@@ -181,6 +185,10 @@ class ServeConfig:
             raise ValueError("--block-size must be a multiple of the 16-token page")
         if not 0.0 < self.gpu_memory_utilization <= 1.0:
             raise ValueError("--gpu-memory-utilization must lie in (0, 1]")
+        if self.kv_cache_dtype_skip_layers:
+            if self.context_parallel_size > 1:
+                raise ValueError("--kv-cache-dtype-skip-layers is not supported with --context-parallel-size")
+            resolve_skip_dtype(self.kv_skip_dtype or "auto")
         w = self.decode_width
         for s in self.capture_sizes:
             if s % w:
@@ -222,6 +230,9 @@ def build_parser() -> argparse.ArgumentParser:
     a("--tokenizer", help="tokenizer directory (default: byte-level)")
     a("--dry-run", action="store_true", default=None)
     a("--no-fit-capacity", action="store_false", dest="fit_capacity", default=None)
+    a("--kv-cache-dtype-skip-layers", help="comma-separated layers whose KV stays in --kv-skip-dtype "
+      "(the MTP layer's index is the layer count)")
+    a("--kv-skip-dtype", help="skip layers' KV dtype: auto (bf16), bfloat16, fp8, fp8_e4m3, fp8_e5m2")
     return ap
 
 
@@ -249,6 +260,11 @@ def resolve(argv: Sequence[str] | None = None, env: Mapping[str, str] | None = N
         values["cuda_graphs"], values["capture_sizes"] = parse_compilation(cc)
     if cli.pop("enforce_eager", False):
         values["cuda_graphs"] = False
+    skip = cli.pop("kv_cache_dtype_skip_layers", None) or env.get("K8V4_KV_SKIP_LAYERS")
+    if skip:
+        values["kv_cache_dtype_skip_layers"] = parse_layers(skip)
+        # the reference deployment's VLLM_KV_SKIP_DTYPE is honoured after K8V4_KV_SKIP_DTYPE
+        values["kv_skip_dtype"] = resolve_skip_dtype(cli.pop("kv_skip_dtype", None), env)
     values.update(cli)
     if values.get("served_model_name") is None:
         values["served_model_name"] = str(values.get("model", ServeConfig.model))

@@ -15,7 +15,10 @@ Per layer (one rank of a TP group):
 The embedding is the INT8 side-file lookup (vocab sharded under TP), the
 lm_head is INT8 per-row with int8 activations, sampling is a per-rank argmax
 reduced across ranks. Attention metadata (slots, block tables, lengths) comes
-in a :class:`StepInputs`.
+in a :class:`StepInputs`. A layer listed in ``skip_kv`` (set by the engine
+from ``kv_cache_dtype_skip_layers``) keeps its KV in plain fp8 / bf16 pages
+and runs RoPE, store and attention through ``kv.skip_layers`` instead of
+``rope_store`` and the K8/V4 attention kernels.
 """
 from __future__ import annotations
 
@@ -25,6 +28,7 @@ import math
 import torch
 
 from .. import ops
+from ..kv import skip_layers
 from ..kv.layout import PageLayout, b200_layout
 from ..layers.linear import Int4Linear, Int8RowLinear, uses_w4a8, w4a8_enabled
 from ..obs.attn_time import attention_span
@@ -108,6 +112,8 @@ class DenseModel:
         self.rope = None
         self.w4a8 = w4a8_enabled()
         self.mtp = None
+        # layer index (the MTP layer: len(layers)) -> plain fp8 / bf16 cache layout
+        self.skip_kv: dict[int, skip_layers.SkipLayout] = {}
         self.fused_ar = None  # parallel.fused_ar.FusedAllReduce when TP runs the fused path
         self.cp = None        # parallel.cp.CPGroup under context parallelism
 
@@ -194,6 +200,18 @@ class DenseModel:
         x = ops.embed_int8(ids, self.embed_codes, self.embed_scales, start=self.vocab_start, out=out)
         return self._all_reduce(x)
 
+    def _skip_attention(self, qkv: torch.Tensor, inp: StepInputs, cache: torch.Tensor,
+                        lay: skip_layers.SkipLayout) -> torch.Tensor:
+        """A skip layer's attention (``kv.skip_layers``): RoPE, the plain-dtype
+        store and the paged attention in torch, on the same page ids and
+        causal rule as the K8/V4 kernels. ``qkv`` is ``[T, hq + 2 hkv, D]``."""
+        hq, hkv = self.shape.hq_local, self.shape.hkv_local
+        q = skip_layers.apply_rope(qkv[:, :hq], self.rope, inp.positions)
+        k = skip_layers.apply_rope(qkv[:, hq:hq + hkv], self.rope, inp.positions)
+        skip_layers.store(cache, lay, inp.slots, k, qkv[:, hq + hkv:])
+        return skip_layers.paged_attention(q, cache, lay, inp.block_table, inp.seq_lens, inp.cu_q, inp.positions,
+                                           inp.max_q_len, self.shape.gqa_local, q_ends=inp.q_ends)
+
     def _cp_attention(self, q: torch.Tensor, inp: StepInputs, cache: torch.Tensor, layer: int) -> torch.Tensor:
         """Attention under context parallelism (see ``parallel.cp``)."""
         sh, cp = self.shape, self.cp
@@ -233,15 +251,19 @@ class DenseModel:
                 h = ops.rmsnorm(x, L.input_norm, cfg.rms_eps)
             else:
                 h = ops.rmsnorm(x, L.input_norm, cfg.rms_eps, residual=residual, sync=sync)
+        skip = self.skip_kv.get(layer) if self.skip_kv else None
         with stage(tag + ".gemm_qkv"):
             # split-K at decode sizes: the fp32 sums go straight to rope_store,
             # which finishes them (bf16 rounding) and zeroes the accumulator
-            qkv = L.qkv(h, ws=splitk_ws, defer=True)
-        q = torch.empty((T, hq, D), dtype=torch.bfloat16, device=self.device)
-        with stage(tag + ".rope_store"):
-            ops.rope_store(qkv, self.rope, inp.positions, q, inp.slots, cache, hq, hkv)
+            qkv = L.qkv(h, ws=splitk_ws, defer=skip is None)
+        if skip is None:
+            q = torch.empty((T, hq, D), dtype=torch.bfloat16, device=self.device)
+            with stage(tag + ".rope_store"):
+                ops.rope_store(qkv, self.rope, inp.positions, q, inp.slots, cache, hq, hkv)
         with stage(tag + ".attn"):
-            if self.cp is not None:
+            if skip is not None:
+                a = self._skip_attention(qkv.reshape(T, hq + 2 * hkv, D), inp, cache, skip)
+            elif self.cp is not None:
                 a = self._cp_attention(q, inp, cache, layer)
             elif inp.is_decode:
                 with attention_span("decode"):
@@ -374,7 +396,8 @@ class DenseModel:
         ops.rmsnorm(hidden, M.hnorm, cfg.rms_eps, out=cat[:, H:])
         splitk_ws = ws.splitk if ws is not None else None
         x = M.eh_proj(cat, ws=splitk_ws)
-        x, residual, sync = self._layer(M.layer, x, None, inp, cache, ws, defer=self.tp == 1, tag="mtp")
+        x, residual, sync = self._layer(M.layer, x, None, inp, cache, ws, defer=self.tp == 1, tag="mtp",
+                                        layer=len(self.layers))
         return self._final_norm(x, residual, M.norm, None, sync)
 
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:

@@ -1,8 +1,10 @@
 """The serving engine: requests in, tokens out.
 
 ``LLMEngine`` owns one TP rank's model, its K8/V4 cache (one uint8 page
-pool per layer), the block manager, the scheduler, the decode CUDA-graph
-runner and the optional MTP speculator. ``step()`` runs one scheduler step:
+pool per layer; layers named in ``kv_cache_dtype_skip_layers`` get a plain
+fp8 / bf16 pool on the same page ids, ``kv.skip_layers``), the block
+manager, the scheduler, the decode CUDA-graph runner and the optional MTP
+speculator. ``step()`` runs one scheduler step:
 
 1. the scheduler picks decode tokens and prefill chunks (token budget 4,224);
 2. the host builds the step's metadata (ids, positions, slots, block tables,
@@ -25,6 +27,7 @@ import numpy as np
 import torch
 
 from .. import ops
+from ..kv import skip_layers
 from ..kv.layout import ATTN_TILE_ROWS
 from ..models.config import ModelConfig
 from ..models.dense import DenseModel, StepInputs
@@ -57,12 +60,30 @@ class EngineConfig:
     layers: int | None = None         # override (tests / smoke)
     forced_accept_mean: float | None = None  # MTP forced-acceptance benchmark mode
     device: str = "cuda"
+    # layers whose KV stays in a plain dtype (the MTP layer's index is the
+    # target's layer count); the dtype name is resolved from the environment
+    # when None (K8V4_KV_SKIP_DTYPE, then VLLM_KV_SKIP_DTYPE, else auto)
+    kv_cache_dtype_skip_layers: tuple[int, ...] = ()
+    kv_skip_dtype: str | None = None
 
     def __post_init__(self):
         if self.kv_cache_dtype != "int8_k_int4_v":
             raise ValueError("kv_cache_dtype must be int8_k_int4_v")
         if self.max_num_batched_tokens < 1:
             raise ValueError("max_num_batched_tokens must be positive")
+        self.kv_cache_dtype_skip_layers = skip_layers.parse_layers(self.kv_cache_dtype_skip_layers)
+        if self.kv_cache_dtype_skip_layers or self.kv_skip_dtype is not None:
+            self.kv_skip_dtype = skip_layers.resolve_skip_dtype(self.kv_skip_dtype)
+        if self.kv_cache_dtype_skip_layers and self.context_parallel_size > 1:
+            raise ValueError("skip layers are not supported under context parallelism")
+
+    def skip_layouts(self, n_layers: int, hkv_local: int) -> dict[int, "skip_layers.SkipLayout"]:
+        """Layer index -> plain-dtype cache layout; raises on an index outside
+        the ``n_layers`` layers that hold a cache."""
+        bad = [i for i in self.kv_cache_dtype_skip_layers if i >= n_layers]
+        if bad:
+            raise ValueError("skip layers %s outside the %d cached layers" % (bad, n_layers))
+        return {i: skip_layers.SkipLayout(hkv_local, self.kv_skip_dtype) for i in self.kv_cache_dtype_skip_layers}
 
 
 def decode_splits(max_pages: int, nseq: int, heads: int) -> int:
@@ -149,12 +170,14 @@ class LLMEngine:
         page_bytes = self.layout.page_bytes
         # the MTP draft layer keeps its own cache after the target's layers
         n_layers = len(self.model.layers) + (1 if self.model.mtp is not None else 0)
+        skip = cfg.skip_layouts(n_layers, self.model.shape.hkv_local)
+        per_page = skip_layers.pool_bytes_per_page(page_bytes, n_layers, skip)
         if cfg.num_kv_blocks is not None:
             blocks = int(cfg.num_kv_blocks)
         else:
             free, total = torch.cuda.mem_get_info(self.device)
             budget = free - (1 - cfg.gpu_memory_utilization) * total - (4 << 30)
-            blocks = int(budget // (page_bytes * n_layers * (cfg.block_size // self.layout.page)))
+            blocks = int(budget // (per_page * (cfg.block_size // self.layout.page)))
             need = ((cfg.max_model_len + cfg.block_size - 1) // cfg.block_size + 1) * cfg.max_num_seqs
             blocks = max(1, min(blocks, need))
         if blocks < 1:
@@ -165,8 +188,11 @@ class LLMEngine:
                                 % (cfg.max_model_len, blocks * cfg.block_size), fit_tokens=max(0, fit))
         self.num_blocks = blocks
         pages = blocks * (cfg.block_size // self.layout.page)
-        self.kv_pool = torch.empty((n_layers, pages, page_bytes), dtype=torch.uint8, device=self.device)
-        self.kv_caches = [self.kv_pool[i] for i in range(n_layers)]
+        self.kv_pool = torch.empty((n_layers - len(skip), pages, page_bytes), dtype=torch.uint8, device=self.device)
+        dense = iter(range(n_layers - len(skip)))
+        self.kv_caches = [skip[i].alloc(pages, self.device) if i in skip else self.kv_pool[next(dense)]
+                          for i in range(n_layers)]
+        self.model.skip_kv = skip
         self.kv_capacity_tokens = blocks * cfg.block_size
 
     # ------------------------------------------------------------- requests
