@@ -25,6 +25,14 @@ int k8v4_decode_attn(const void* q, const int32_t* cu_q, const int32_t* seq_lens
                      int head_offset, int heads, int gqa, int hq_total, int nseq, int max_q_len, int nsplit,
                      float sm_scale, void* out, float* ws_o, float* ws_ml, cudaStream_t st);
 int64_t k8v4_decode_ws_floats(int nseq, int heads, int nsplit, int max_q_len, int gqa);
+int k8v4_decode_attn_push(const void* q, const int32_t* cu_q, const int32_t* seq_lens, const int32_t* q_ends,
+                          const int32_t* block_table, int bt_stride, const void* cache, int64_t num_pages, int hkv,
+                          int head_offset, int heads, int gqa, int hq_total, int nseq, int max_q_len, int nsplit,
+                          float sm_scale, float* slot_mc, unsigned long long* flag_mc, cudaStream_t st);
+int k8v4_decode_combine_ranks_sync(const float* ws_all, int64_t rank_floats, const int32_t* cu_q, void* out,
+                                   int nrank, int nsplit, int nseq, int heads, int head_offset, int gqa, int hq_total,
+                                   int max_q_len, const unsigned long long* sync_flag, unsigned long long* sync_state,
+                                   unsigned long long sync_expected, cudaStream_t st);
 int k8v4_prefill_attn(const void* q, const int32_t* cu_q, const int32_t* seq_lens, const int32_t* block_table,
                       int bt_stride, int bt_width, const void* cache, int64_t num_pages, int hkv, int head_offset,
                       int heads, int gqa, int hq_total, int nseq, int max_q_len, float sm_scale, void* stage,
@@ -189,6 +197,34 @@ void decode_attn(const at::Tensor& q, const at::Tensor& cu_q, const at::Tensor& 
 
 int64_t decode_ws_floats(int64_t nseq, int64_t heads, int64_t nsplit, int64_t max_q_len, int64_t gqa) {
   return k8v4_decode_ws_floats((int)nseq, (int)heads, (int)nsplit, (int)max_q_len, (int)gqa);
+}
+
+// Context parallelism: decode attention whose partials go straight into
+// every rank's copy of this rank's gather slot (multicast address `slot_mc`),
+// then one signal per CTA on the multicast counter `flag_mc`.
+void decode_attn_push(const at::Tensor& q, const at::Tensor& cu_q, const at::Tensor& seq_lens,
+                      const c10::optional<at::Tensor>& q_ends, const at::Tensor& block_table, const at::Tensor& cache,
+                      int64_t hkv, int64_t head_offset, int64_t heads, int64_t gqa, int64_t max_q_len, int64_t nsplit,
+                      double sm_scale, int64_t slot_mc, int64_t flag_mc) {
+  check_attn_common(q, cu_q, seq_lens, block_table, cache, q, hkv);
+  TORCH_CHECK(max_q_len * gqa <= 64, "decode tile holds at most 64 query rows per KV head");
+  TORCH_CHECK(head_offset >= 0 && heads >= 1 && head_offset + heads <= hkv, "head range");
+  TORCH_CHECK(q.size(1) == hkv * gqa || q.size(1) == heads * gqa, "q heads vs layout");
+  TORCH_CHECK(slot_mc != 0 && flag_mc != 0 && slot_mc % 16 == 0 && flag_mc % 8 == 0, "multicast addresses");
+  const int32_t* qe = nullptr;
+  if (q_ends.has_value()) {
+    check_contig(*q_ends, "q_ends");
+    TORCH_CHECK(q_ends->scalar_type() == at::kInt && q_ends->numel() == q.size(0), "q_ends int32 [T]");
+    qe = q_ends->data_ptr<int32_t>();
+  }
+  c10::cuda::CUDAGuard g(cache.device());
+  check_rc(k8v4_decode_attn_push(q.data_ptr(), cu_q.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(), qe,
+                                 block_table.data_ptr<int32_t>(), (int)block_table.stride(0), cache.data_ptr(),
+                                 cache.size(0), (int)hkv, (int)head_offset, (int)heads, (int)gqa, (int)q.size(1),
+                                 (int)seq_lens.numel(), (int)max_q_len, (int)nsplit, (float)sm_scale,
+                                 reinterpret_cast<float*>(slot_mc), reinterpret_cast<unsigned long long*>(flag_mc),
+                                 cur_stream()),
+           "decode_attn_push");
 }
 
 void prefill_attn(const at::Tensor& q, const at::Tensor& cu_q, const at::Tensor& seq_lens,
@@ -499,13 +535,31 @@ void prefill_attn_cp(const at::Tensor& q, const at::Tensor& cu_q, const at::Tens
 }
 
 // Merge every rank's split-K decode partials (all-gathered workspaces).
+// With sync_flag: ws_all is this rank's copy of the gather buffer that
+// decode_attn_push fills; the merge first waits for every rank's signals.
 void decode_combine_ranks(const at::Tensor& ws_all, int64_t rank_floats, const at::Tensor& cu_q, int64_t nrank,
                           int64_t nsplit, int64_t heads, int64_t head_offset, int64_t gqa, int64_t max_q_len,
-                          at::Tensor& out) {
+                          at::Tensor& out, const c10::optional<at::Tensor>& sync_flag,
+                          const c10::optional<at::Tensor>& sync_state, int64_t sync_expected) {
   check_contig(ws_all, "ws_all");
   check_contig(out, "out");
   TORCH_CHECK(ws_all.scalar_type() == at::kFloat && ws_all.numel() >= nrank * rank_floats, "ws_all fp32");
   c10::cuda::CUDAGuard g(out.device());
+  if (sync_flag.has_value()) {
+    TORCH_CHECK(sync_state.has_value() && sync_state->scalar_type() == at::kLong && sync_state->numel() >= 2 &&
+                    sync_state->is_contiguous(),
+                "sync_state: int64 [2]");
+    TORCH_CHECK(sync_flag->scalar_type() == at::kLong && sync_flag->numel() >= 1, "sync_flag: int64 counter");
+    TORCH_CHECK(sync_expected > 0, "sync_expected: signals of one exchange");
+    check_rc(k8v4_decode_combine_ranks_sync(
+                 ws_all.data_ptr<float>(), rank_floats, cu_q.data_ptr<int32_t>(), out.data_ptr(), (int)nrank,
+                 (int)nsplit, (int)(cu_q.numel() - 1), (int)heads, (int)head_offset, (int)gqa, (int)out.size(1),
+                 (int)max_q_len, reinterpret_cast<const unsigned long long*>(sync_flag->data_ptr()),
+                 reinterpret_cast<unsigned long long*>(sync_state->data_ptr()), (unsigned long long)sync_expected,
+                 cur_stream()),
+             "decode_combine_ranks");
+    return;
+  }
   check_rc(k8v4_decode_combine_ranks(ws_all.data_ptr<float>(), rank_floats, cu_q.data_ptr<int32_t>(), out.data_ptr(),
                                      (int)nrank, (int)nsplit, (int)(cu_q.numel() - 1), (int)heads, (int)head_offset,
                                      (int)gqa, (int)out.size(1), (int)max_q_len, cur_stream()),
@@ -579,7 +633,12 @@ TORCH_LIBRARY(k8v4, m) {
       "int hkv, int head_offset, int heads, int gqa, int max_q_len, float sm_scale, Tensor(a!) out) -> ()");
   m.def(
       "decode_combine_ranks(Tensor ws_all, int rank_floats, Tensor cu_q, int nrank, int nsplit, int heads, "
-      "int head_offset, int gqa, int max_q_len, Tensor(a!) out) -> ()");
+      "int head_offset, int gqa, int max_q_len, Tensor(a!) out, Tensor? sync_flag=None, "
+      "Tensor(b!)? sync_state=None, int sync_expected=0) -> ()");
+  m.def(
+      "decode_attn_push(Tensor q, Tensor cu_q, Tensor seq_lens, Tensor? q_ends, Tensor block_table, Tensor cache, "
+      "int hkv, int head_offset, int heads, int gqa, int max_q_len, int nsplit, float sm_scale, int slot_mc, "
+      "int flag_mc) -> ()");
   m.def(
       "gather_dequant(Tensor cache, Tensor block_table, int hkv, int head, int seq_len, Tensor(a!) k_out, "
       "Tensor(b!) v_out) -> ()");
@@ -601,6 +660,7 @@ TORCH_LIBRARY_IMPL(k8v4, CUDA, m) {
   m.impl("gather_dequant", &gather_dequant);
   m.impl("prefill_attn_cp", &prefill_attn_cp);
   m.impl("decode_combine_ranks", &decode_combine_ranks);
+  m.impl("decode_attn_push", &decode_attn_push);
 }
 
 TORCH_LIBRARY_IMPL(k8v4, CompositeExplicitAutograd, m) {

@@ -24,6 +24,11 @@ __device__ __forceinline__ void mc_signal_add_u64(unsigned long long* mc_addr, u
   asm volatile("multimem.red.release.sys.global.add.u64 [%0], %1;" ::"l"(mc_addr), "l"(v) : "memory");
 }
 
+// v is stored into every rank's copy of the element (the switch fans it out).
+__device__ __forceinline__ void mc_st_f32(float* mc_addr, float v) {
+  asm volatile("multimem.st.relaxed.sys.global.f32 [%0], %1;" ::"l"(mc_addr), "f"(v) : "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_alias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
 
 __device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
@@ -47,6 +52,45 @@ __device__ __forceinline__ bool wait_geq_u64(const unsigned long long* p, unsign
       return false;
     }
     __nanosleep(64);
+  }
+}
+
+// Completion tracking of a producer -> consumer exchange through symmetric
+// memory: the producer's CTAs (on every rank) each add 1 to a counter, and
+// one consumer launch waits until its copy of the counter holds one more
+// call's worth of signals.
+struct ReduceSync {
+  const unsigned long long* flag;  // this rank's copy of the multicast counter
+  unsigned long long* state;       // [0] signals consumed so far, [1] CTAs of this launch done
+  unsigned long long expected;     // signals one producer call sends (world x its CTAs)
+};
+
+// Every thread of the CTA returns once the counter reached state[0] +
+// expected (or the wait gave up and recorded kErrPeerTimeout at `site`).
+__device__ __forceinline__ void sync_wait(const ReduceSync& s, int site) {
+  if (threadIdx.x == 0) {
+    const unsigned long long target = *reinterpret_cast<volatile unsigned long long*>(s.state) + s.expected;
+    wait_geq_u64(s.flag, target, site);
+  }
+  __syncthreads();
+  fence_proxy_alias();  // the data arrived through the multicast alias
+}
+
+// Every CTA of the consumer launch calls this once; the last one advances
+// state[0] by `expected` (a running count: a replayed CUDA graph needs no
+// reset, and calls may differ in size).
+__device__ __forceinline__ void sync_done(const ReduceSync& s) {
+  fence_proxy_alias();  // this CTA's reads and writes precede later multicast traffic
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned long long ctas = (unsigned long long)gridDim.x * gridDim.y * gridDim.z;
+    const unsigned long long prev = atomicAdd(s.state + 1, 1ull);
+    if (prev == ctas - 1) {
+      s.state[1] = 0;
+      s.state[0] += s.expected;
+      __threadfence();
+    }
   }
 }
 

@@ -23,6 +23,7 @@
 // queues), 4-7 = softmax / epilogue (one per TMEM lane quadrant), 2, 3, 8..
 // = V converters.
 #include "attn_common.cuh"
+#include "../comm/peer.cuh"
 
 namespace k8v4 {
 namespace attn {
@@ -44,6 +45,12 @@ struct DecodeParams {
   int head_offset;            // first KV head of this launch (for replicated layouts)
   int nsplit;
   float sm_scale_log2;        // softmax scale * log2(e)
+  // context parallelism, fused exchange: ws_o / ws_ml are multicast addresses
+  // (this rank's slot in every rank's copy of a symmetric gather buffer), the
+  // partials go out with multimem stores even when nsplit == 1, and each CTA
+  // then adds 1 to the multicast counter flag_mc
+  int push;
+  unsigned long long* flag_mc;
 };
 
 #ifdef K8V4_TRACE
@@ -494,7 +501,13 @@ __global__ void __launch_bounds__(DCfg<NPAD>::NTHREADS, 1)
         o += epi[(e * LPR + rr) * C::EPI_STRIDE + d];
         lt += l_buf[e * LPR + rr];
       }
-      if (p.nsplit == 1) {
+      if (p.push) {
+        peer::mc_st_f32(p.ws_o + (wsi * NPAD + rr) * D + d, o);
+        if (d == 0) {
+          peer::mc_st_f32(p.ws_ml + (wsi * 2) * NPAD + rr, mx_buf[rr]);
+          peer::mc_st_f32(p.ws_ml + (wsi * 2 + 1) * NPAD + rr, lt);
+        }
+      } else if (p.nsplit == 1) {
         const int t = rr / p.gqa, g = rr % p.gqa;
         p.out[((int64_t)(qb + t) * p.hq_total + (int64_t)h * p.gqa + g) * D + d] =
             __float2bfloat16_rn(lt > 0.f ? o / lt : 0.f);
@@ -563,6 +576,12 @@ __global__ void __launch_bounds__(DCfg<NPAD>::NTHREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
+  if (p.push && threadIdx.x == 0) {
+    // the CTA's multicast stores (ordered before this point by the barrier)
+    // are out: publish them to every rank
+    peer::fence_proxy_alias();
+    peer::mc_signal_add_u64(p.flag_mc, 1ull);
+  }
 }
 
 // Merge split partials: grid (rows, heads, seqs), 128 threads (dims). The
@@ -575,19 +594,23 @@ __global__ void __launch_bounds__(DCfg<NPAD>::NTHREADS, 1)
 // g takes splits g, g + 4, ... so every O load of the row is in flight at
 // once; the groups' sums meet in shared memory.
 constexpr int COMBINE_GROUPS = 4;
-__global__ void __launch_bounds__(128 * COMBINE_GROUPS) decode_combine_kernel(
-    const float* __restrict__ ws_o, const float* __restrict__ ws_ml, const int32_t* cu_q, __nv_bfloat16* out,
-    int nsplit, int npad, int gqa, int hq_total, int head_offset, int nrank, int64_t rank_stride_o,
-    int64_t rank_stride_ml) {
-  pdl_trigger();
-  pdl_wait();  // everything this kernel reads may come from the previous one
+// NC: the partials were written before this launch (read-only data path);
+// otherwise they arrived from peers during it (plain coherent loads).
+template <bool NC>
+__device__ __forceinline__ float ld_part(const float* p) {
+  if constexpr (NC) return __ldg(p);
+  else return *p;
+}
+
+template <bool NC>
+__device__ __forceinline__ void combine_row(const float* ws_o, const float* ws_ml, __nv_bfloat16* out, int r, int hl,
+                                            int seq, int qb, int nsplit, int npad, int gqa, int hq_total,
+                                            int head_offset, int nrank, int64_t rank_stride_o,
+                                            int64_t rank_stride_ml) {
   __shared__ float wsh[128];
   __shared__ float red[8];
   __shared__ float part[COMBINE_GROUPS - 1][D];
-  const int r = blockIdx.x, hl = blockIdx.y, seq = blockIdx.z;
   const int d = threadIdx.x & (D - 1), grp = threadIdx.x / D;
-  const int qb = cu_q[seq], q_len = cu_q[seq + 1] - qb;
-  if (r >= q_len * gqa) return;  // uniform for the CTA
   const int64_t base = ((int64_t)seq * gridDim.y + hl) * nsplit;
   const int ntot = nsplit * nrank;  // <= 128
   // (m, l) of every split: threads of group 0, one split each
@@ -595,8 +618,8 @@ __global__ void __launch_bounds__(128 * COMBINE_GROUPS) decode_combine_kernel(
   if (grp == 0 && d < ntot) {
     const int rk = d / nsplit, sp = d % nsplit;
     const float* ml = ws_ml + rk * rank_stride_ml;
-    m = ml[((base + sp) * 2) * npad + r];
-    l = ml[((base + sp) * 2 + 1) * npad + r];
+    m = ld_part<NC>(ml + ((base + sp) * 2) * npad + r);
+    l = ld_part<NC>(ml + ((base + sp) * 2 + 1) * npad + r);
   }
   if (grp == 0) {
     const float M0 = warp_max(m);
@@ -622,14 +645,14 @@ __global__ void __launch_bounds__(128 * COMBINE_GROUPS) decode_combine_kernel(
     for (; s + 7 * COMBINE_GROUPS < nsplit; s += 8 * COMBINE_GROUPS) {
       float v[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = o[(s + i * COMBINE_GROUPS) * stride];
+      for (int i = 0; i < 8; ++i) v[i] = ld_part<NC>(o + (s + i * COMBINE_GROUPS) * stride);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float wi = wr[s + i * COMBINE_GROUPS];
         acc += wi > 0.f ? wi * v[i] : 0.f;
       }
     }
-    for (; s < nsplit; s += COMBINE_GROUPS) acc += wr[s] > 0.f ? wr[s] * o[s * stride] : 0.f;
+    for (; s < nsplit; s += COMBINE_GROUPS) acc += wr[s] > 0.f ? wr[s] * ld_part<NC>(o + s * stride) : 0.f;
   }
   if (grp > 0) part[grp - 1][d] = acc;
   __syncthreads();
@@ -639,6 +662,37 @@ __global__ void __launch_bounds__(128 * COMBINE_GROUPS) decode_combine_kernel(
     const int t = r / gqa, g = r % gqa, h = hl + head_offset;
     out[((int64_t)(qb + t) * hq_total + (int64_t)h * gqa + g) * D + d] = __float2bfloat16_rn(L > 0.f ? acc / L : 0.f);
   }
+}
+
+__global__ void __launch_bounds__(128 * COMBINE_GROUPS) decode_combine_kernel(
+    const float* __restrict__ ws_o, const float* __restrict__ ws_ml, const int32_t* cu_q, __nv_bfloat16* out,
+    int nsplit, int npad, int gqa, int hq_total, int head_offset, int nrank, int64_t rank_stride_o,
+    int64_t rank_stride_ml) {
+  pdl_trigger();
+  pdl_wait();  // everything this kernel reads may come from the previous one
+  const int r = blockIdx.x, hl = blockIdx.y, seq = blockIdx.z;
+  const int qb = cu_q[seq], q_len = cu_q[seq + 1] - qb;
+  if (r >= q_len * gqa) return;  // uniform for the CTA
+  combine_row<true>(ws_o, ws_ml, out, r, hl, seq, qb, nsplit, npad, gqa, hq_total, head_offset, nrank,
+                    rank_stride_o, rank_stride_ml);
+}
+
+// The same merge over every rank's slot of a symmetric gather buffer that
+// the ranks' decode kernels fill with multicast stores (`ws_all` is this
+// rank's copy). Every CTA, rows past a sequence's end included, waits until
+// all ranks' CTAs have signalled; the last CTA advances the running count.
+__global__ void __launch_bounds__(128 * COMBINE_GROUPS) decode_combine_sync_kernel(
+    const float* ws_o, const float* ws_ml, const int32_t* cu_q, __nv_bfloat16* out, int nsplit, int npad, int gqa,
+    int hq_total, int head_offset, int nrank, int64_t rank_stride, peer::ReduceSync sync) {
+  pdl_trigger();
+  pdl_wait();
+  const int r = blockIdx.x, hl = blockIdx.y, seq = blockIdx.z;
+  const int qb = cu_q[seq], q_len = cu_q[seq + 1] - qb;
+  peer::sync_wait(sync, 213);
+  if (r < q_len * gqa)  // uniform for the CTA
+    combine_row<false>(ws_o, ws_ml, out, r, hl, seq, qb, nsplit, npad, gqa, hq_total, head_offset, nrank,
+                       rank_stride, rank_stride);
+  peer::sync_done(sync);
 }
 
 }  // namespace attn
@@ -730,19 +784,15 @@ static int launch_decode(const KVTileMaps& tm, const DecodeParams& p, int heads,
   return launch_k(decode_attn_kernel<NPAD>, grid, dim3(C::NTHREADS), C::SMEM_BYTES, st, tm, p) == cudaSuccess ? 0 : 10;
 }
 
-// Paged decode attention (b200 format). `heads` KV heads starting at
-// `head_offset` are processed; q/out rows hold hq_total query heads.
-// ws_o / ws_ml must hold nseq*heads*nsplit*npad*(D+2) floats when nsplit > 1.
-extern "C" int k8v4_decode_attn(const void* q, const int32_t* cu_q, const int32_t* seq_lens, const int32_t* q_ends,
-                                const int32_t* block_table, int bt_stride, const void* cache, int64_t num_pages,
-                                int hkv, int head_offset, int heads, int gqa, int hq_total, int nseq, int max_q_len,
-                                int nsplit, float sm_scale, void* out, float* ws_o, float* ws_ml, cudaStream_t st) {
+namespace {
+// Builds the parameters and launches the decode kernel; the npad the launch
+// used comes back in *npad_out.
+int decode_core(const void* q, const int32_t* cu_q, const int32_t* seq_lens, const int32_t* q_ends,
+                const int32_t* block_table, int bt_stride, const void* cache, int64_t num_pages, int hkv,
+                int head_offset, int heads, int gqa, int hq_total, int nseq, int max_q_len, int nsplit,
+                float sm_scale, void* out, float* ws_o, float* ws_ml, unsigned long long* flag_mc, int* npad_out,
+                cudaStream_t st) {
   const int rows = max_q_len * gqa;
-  if (rows <= 0 || nseq <= 0) return 0;
-  if (rows > 64) return 1;  // longer query runs use the prefill kernel
-  if (nsplit > 128) return 4;
-  if (nsplit < 1) nsplit = 1;
-  if (nsplit > 1 && (!ws_o || !ws_ml)) return 2;
   KVTileMaps tm;
   if (k8v4_make_kv_maps(&tm, cache, num_pages, hkv)) return 3;
   DecodeParams p;
@@ -762,17 +812,71 @@ extern "C" int k8v4_decode_attn(const void* q, const int32_t* cu_q, const int32_
   p.head_offset = head_offset;
   p.nsplit = nsplit;
   p.sm_scale_log2 = sm_scale * LOG2E;
+  p.push = flag_mc != nullptr;
+  p.flag_mc = flag_mc;
   int npad, rc;
   if (rows <= 16) { npad = 16; rc = launch_decode<16>(tm, p, heads, nseq, st); }
   else if (rows <= 32) { npad = 32; rc = launch_decode<32>(tm, p, heads, nseq, st); }
   else if (rows <= 48) { npad = 48; rc = launch_decode<48>(tm, p, heads, nseq, st); }
   else { npad = 64; rc = launch_decode<64>(tm, p, heads, nseq, st); }
+  *npad_out = npad;
+  return rc;
+}
+
+int npad_of(int rows) { return rows <= 16 ? 16 : rows <= 32 ? 32 : rows <= 48 ? 48 : 64; }
+}  // namespace
+
+// Paged decode attention (b200 format). `heads` KV heads starting at
+// `head_offset` are processed; q/out rows hold hq_total query heads.
+// ws_o / ws_ml must hold nseq*heads*nsplit*npad*(D+2) floats when nsplit > 1.
+extern "C" int k8v4_decode_attn(const void* q, const int32_t* cu_q, const int32_t* seq_lens, const int32_t* q_ends,
+                                const int32_t* block_table, int bt_stride, const void* cache, int64_t num_pages,
+                                int hkv, int head_offset, int heads, int gqa, int hq_total, int nseq, int max_q_len,
+                                int nsplit, float sm_scale, void* out, float* ws_o, float* ws_ml, cudaStream_t st) {
+  const int rows = max_q_len * gqa;
+  if (rows <= 0 || nseq <= 0) return 0;
+  if (rows > 64) return 1;  // longer query runs use the prefill kernel
+  if (nsplit > 128) return 4;
+  if (nsplit < 1) nsplit = 1;
+  if (nsplit > 1 && (!ws_o || !ws_ml)) return 2;
+  int npad = 0;
+  const int rc = decode_core(q, cu_q, seq_lens, q_ends, block_table, bt_stride, cache, num_pages, hkv, head_offset,
+                             heads, gqa, hq_total, nseq, max_q_len, nsplit, sm_scale, out, ws_o, ws_ml, nullptr,
+                             &npad, st);
   if (rc || nsplit == 1) return rc;
   return launch_k(decode_combine_kernel, dim3(rows, heads, nseq), dim3(D * COMBINE_GROUPS), 0, st, (const float*)ws_o,
                   (const float*)ws_ml, cu_q, reinterpret_cast<__nv_bfloat16*>(out), nsplit, npad, gqa, hq_total,
                   head_offset, 1, (int64_t)0, (int64_t)0) == cudaSuccess
              ? 0
              : 11;
+}
+
+// Context parallelism, exchange fused into the decode kernel: each CTA stores
+// its (m, l, O) partial through `slot_mc`, the multicast address of this
+// rank's slot in a symmetric gather buffer (the slot lands in every rank's
+// copy; (m, l) first, then O, k8v4_decode_ws_floats floats), then adds 1 to
+// the multicast counter `flag_mc`. k8v4_decode_combine_ranks_sync merges the
+// slots. Every rank must launch the same shape (nseq, heads, nsplit, rows).
+extern "C" int k8v4_decode_attn_push(const void* q, const int32_t* cu_q, const int32_t* seq_lens,
+                                     const int32_t* q_ends, const int32_t* block_table, int bt_stride,
+                                     const void* cache, int64_t num_pages, int hkv, int head_offset, int heads,
+                                     int gqa, int hq_total, int nseq, int max_q_len, int nsplit, float sm_scale,
+                                     float* slot_mc, unsigned long long* flag_mc, cudaStream_t st) {
+  const int rows = max_q_len * gqa;
+  if (rows <= 0 || nseq <= 0) return 0;
+  if (rows > 64) return 1;
+  if (nsplit < 1 || nsplit > 128) return 4;
+  if (!slot_mc || !flag_mc) return 2;
+  const int64_t ml_floats = (int64_t)nseq * heads * nsplit * 2 * npad_of(rows);
+  int npad = 0;
+  return decode_core(q, cu_q, seq_lens, q_ends, block_table, bt_stride, cache, num_pages, hkv, head_offset, heads,
+                     gqa, hq_total, nseq, max_q_len, nsplit, sm_scale, nullptr, slot_mc + ml_floats, slot_mc, flag_mc,
+                     &npad, st);
+}
+
+// CTAs one k8v4_decode_attn_push launch signals with (per rank).
+extern "C" int64_t k8v4_decode_push_ctas(int nseq, int heads, int nsplit) {
+  return (int64_t)nseq * heads * nsplit;
 }
 
 // Merge the split partials of `nrank` ranks (context parallelism): `ws_all`
@@ -790,6 +894,30 @@ extern "C" int k8v4_decode_combine_ranks(const float* ws_all, int64_t rank_float
   return launch_k(decode_combine_kernel, dim3(rows, heads, nseq), dim3(D * COMBINE_GROUPS), 0, st, ws_all + ml_floats, ws_all, cu_q,
                   reinterpret_cast<__nv_bfloat16*>(out), nsplit, npad, gqa, hq_total, head_offset, nrank,
                   rank_floats, rank_floats) == cudaSuccess
+             ? 0
+             : 11;
+}
+
+// Merge every rank's slot of the gather buffer that k8v4_decode_attn_push
+// fills (`ws_all`: this rank's copy, slots `rank_floats` apart). The kernel
+// waits until the counter `sync_flag` (this rank's copy) reaches
+// sync_state[0] + sync_expected, then the last CTA adds sync_expected to
+// sync_state[0]; sync_expected = ranks x k8v4_decode_push_ctas.
+extern "C" int k8v4_decode_combine_ranks_sync(const float* ws_all, int64_t rank_floats, const int32_t* cu_q,
+                                              void* out, int nrank, int nsplit, int nseq, int heads, int head_offset,
+                                              int gqa, int hq_total, int max_q_len,
+                                              const unsigned long long* sync_flag, unsigned long long* sync_state,
+                                              unsigned long long sync_expected, cudaStream_t st) {
+  const int rows = max_q_len * gqa;
+  if (rows <= 0 || nseq <= 0) return 0;
+  if (rows > 64 || nrank < 1 || nsplit < 1 || nrank * nsplit > 128) return 1;
+  if (!sync_flag || !sync_state) return 2;
+  const int npad = npad_of(rows);
+  const int64_t ml_floats = (int64_t)nseq * heads * nsplit * 2 * npad;
+  peer::ReduceSync sync{sync_flag, sync_state, sync_expected};
+  return launch_k(decode_combine_sync_kernel, dim3(rows, heads, nseq), dim3(D * COMBINE_GROUPS), 0, st,
+                  (const float*)(ws_all + ml_floats), ws_all, cu_q, reinterpret_cast<__nv_bfloat16*>(out), nsplit,
+                  npad, gqa, hq_total, head_offset, nrank, rank_floats, sync) == cudaSuccess
              ? 0
              : 11;
 }

@@ -85,36 +85,6 @@ __device__ __forceinline__ void quant_row(const float (&v)[VPT][8], int n, int8_
   if (threadIdx.x == 0) *scale = s;
 }
 
-// Completion tracking of a GEMM -> all-reduce consumed by one kernel launch.
-struct ReduceSync {
-  const unsigned long long* flag;  // this rank's copy of the multicast counter
-  unsigned long long* state;       // [0] signals consumed so far, [1] CTAs of this launch done
-  unsigned long long expected;     // signals one producer call sends (world x its CTAs)
-};
-
-__device__ __forceinline__ void sync_wait(const ReduceSync& s) {
-  if (threadIdx.x == 0) {
-    const unsigned long long target = *reinterpret_cast<volatile unsigned long long*>(s.state) + s.expected;
-    peer::wait_geq_u64(s.flag, target, 201);
-  }
-  __syncthreads();
-  peer::fence_proxy_alias();  // the sums arrived through the multicast alias
-}
-
-__device__ __forceinline__ void sync_done(const ReduceSync& s) {
-  peer::fence_proxy_alias();  // the zeroing stores precede later multicast adds
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const unsigned long long prev = atomicAdd(s.state + 1, 1ull);
-    if (prev == gridDim.x - 1) {
-      s.state[1] = 0;
-      s.state[0] += s.expected;
-      __threadfence();
-    }
-  }
-}
-
 // x: [T, n] bf16. If residual != nullptr: h = x + residual, residual <- h.
 // y = h * rsqrt(mean(h^2) + eps) * w. Outputs bf16 y (row stride ldy, so two
 // norms can write the halves of one concatenated row) and/or int8 y + scale.
@@ -132,7 +102,7 @@ template <int VPT>
 __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, float* xf,
                                                            __nv_bfloat16* residual, const __nv_bfloat16* __restrict__ w,
                                                            __nv_bfloat16* y, int8_t* yq, float* yscale, int n,
-                                                           int64_t ldy, float eps, ReduceSync sync) {
+                                                           int64_t ldy, float eps, peer::ReduceSync sync) {
   pdl_trigger();
   // the norm weights come from no earlier kernel: load them before waiting
   uint4 gw[VPT];
@@ -144,7 +114,7 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const __nv_bfloat16* 
   pdl_wait();  // x / xf / residual may come from the previous kernel
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
-  if (sync.flag) sync_wait(sync);
+  if (sync.flag) peer::sync_wait(sync, 201);
   float v[VPT][8];
   float rs[VPT][8];
   float ss = 0.f;
@@ -208,7 +178,7 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const __nv_bfloat16* 
     }
   }
   if (yq) quant_row<VPT>(v, n, yq + row * n, yscale + row, red);
-  if (sync.flag) sync_done(sync);
+  if (sync.flag) peer::sync_done(sync);
 }
 
 // gu: [T, 2I] = [gate | up]. out = silu(gate) * up (bf16 and/or int8 + scale).
@@ -365,7 +335,7 @@ extern "C" int k8v4_rmsnorm(const void* x, float* xf, void* residual, const void
   if (rows <= 0) return 0;
   if (n % 8 || ldy < n || ldy % 8) return 1;
   if (sync_flag && (!xf || !sync_state)) return 4;
-  ReduceSync sync{sync_flag, sync_state, sync_expected};
+  peer::ReduceSync sync{sync_flag, sync_state, sync_expected};
   K8V4_VPT_DISPATCH(n, rmsnorm_kernel, reinterpret_cast<const __nv_bfloat16*>(x), xf,
                     reinterpret_cast<__nv_bfloat16*>(residual), reinterpret_cast<const __nv_bfloat16*>(w),
                     reinterpret_cast<__nv_bfloat16*>(y), reinterpret_cast<int8_t*>(yq), yscale, n, ldy, eps, sync);

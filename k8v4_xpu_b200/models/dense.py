@@ -223,6 +223,10 @@ class DenseModel:
         B = inp.cu_q.numel() - 1
         nsplit = max(2, inp.nsplit)
         rank_floats = ops.decode_ws_floats(B, hkv, nsplit, inp.max_q_len, gqa)
+        if cp.peer is not None and cp.peer.fits(rank_floats):
+            # partials exchanged by the attention kernel itself (multicast stores)
+            return cp.peer.attention(q, inp.cu_q, inp.cp_local_lens, inp.cp_local_bt, cache, hkv, gqa,
+                                     inp.max_q_len, nsplit)
         ws = torch.empty(rank_floats, dtype=torch.float32, device=self.device)
         ops.decode_attn(q, inp.cu_q, inp.cp_local_lens, inp.cp_local_bt, cache, hkv, gqa, inp.max_q_len,
                         nsplit=nsplit, ws=ws)

@@ -278,13 +278,38 @@ def prefill_attn_cp(q, cu_q, seq_lens, block_table, caches, hkv, gqa, max_q_len,
 
 
 def decode_combine_ranks(ws_all, rank_floats: int, cu_q, nrank: int, nsplit: int, heads: int, gqa: int,
-                         max_q_len: int, out, head_offset: int = 0):
-    """Merge the split-K partials of every context-parallel rank into ``out``."""
+                         max_q_len: int, out, head_offset: int = 0, sync=None):
+    """Merge the split-K partials of every context-parallel rank into ``out``.
+
+    ``sync`` = (counter, state, expected) when ``ws_all`` is this rank's copy
+    of the gather buffer that :func:`decode_attn_push` fills: the kernel first
+    waits until the counter holds ``expected`` more signals (bounded)."""
     require()
+    flag, state, expected = sync if sync is not None else (None, None, 0)
     torch.ops.k8v4.decode_combine_ranks(ws_all, int(rank_floats), cu_q, nrank, nsplit, heads, head_offset, gqa,
-                                        max_q_len, out)
+                                        max_q_len, out, flag, state, int(expected))
     _count()
     return out
+
+
+def decode_attn_push(q, cu_q, seq_lens, block_table, cache, hkv, gqa, max_q_len, nsplit, slot_mc: int,
+                     flag_mc: int, q_ends=None, head_offset=0, heads=None, sm_scale=None):
+    """Split-K decode attention whose partials go straight into every rank's
+    copy of this rank's gather slot (``slot_mc``: its multicast address),
+    then one signal per CTA on the multicast counter ``flag_mc``."""
+    require()
+    heads = hkv if heads is None else heads
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(q.shape[-1])
+    torch.ops.k8v4.decode_attn_push(q, cu_q, seq_lens, q_ends, block_table, cache, hkv, head_offset, heads, gqa,
+                                    max_q_len, nsplit, float(sm_scale), int(slot_mc), int(flag_mc))
+    _count()
+    return q
+
+
+def decode_push_ctas(nseq: int, heads: int, nsplit: int) -> int:
+    """Signals one :func:`decode_attn_push` launch sends (its CTAs)."""
+    return int(nseq) * int(heads) * int(nsplit)
 
 
 def enable_peer_access(peer_device: int) -> bool:

@@ -16,12 +16,13 @@ of this framework (a KV-gather design, not ring attention):
 * decode: every rank runs the model on the new token (replicated GEMMs); the
   owner of the token's page writes its KV; each rank's decode attention
   covers its own pages and the (m, l, O) split partials of all ranks are
-  all-gathered and merged, so every rank continues with the same attention
-  output.
+  exchanged and merged, so every rank continues with the same attention
+  output. The exchange is an NCCL all-gather, or (``K8V4_CP_COMBINE=peer``)
+  multicast stores from the attention kernel itself (``parallel.cp_combine``).
 
 Every rank's KV pool lives in symmetric memory and is mapped into every
 process (torch's symmetric-memory rendezvous does the handle exchange and
-grants access); synchronization and the partial exchange use NCCL.
+grants access); synchronization uses NCCL.
 """
 from __future__ import annotations
 
@@ -45,6 +46,7 @@ class CPGroup:
             raise ValueError("context parallel size must be at most 8")
         self._peer_pools = None
         self._flag = None
+        self.peer = None  # PeerCombine when the decode exchange runs through multicast stores
 
     # ----------------------------------------------------------- peer memory
     def alloc_pool(self, shape: tuple[int, ...], device) -> torch.Tensor:

@@ -13,8 +13,10 @@ same steps. What differs per rank (see ``parallel.cp``):
 * a decode step feeds every rank the new tokens (replicated GEMMs), the owner
   writes each token's KV, and attention merges every rank's partials.
 
-Decode runs eagerly here (the per-layer partial all-gather is stream-ordered
-NCCL); MTP and tensor parallelism inside a CP group are not supported yet.
+Decode runs eagerly here. The per-layer partial exchange is an NCCL
+all-gather, or with ``K8V4_CP_COMBINE=peer`` multicast stores from the decode
+attention kernel (``parallel.cp_combine``). MTP and tensor parallelism
+inside a CP group are not supported yet.
 """
 from __future__ import annotations
 
@@ -23,6 +25,7 @@ import torch
 
 from ..models.dense import StepInputs
 from ..parallel.cp import PAGE, CPGroup
+from ..parallel.cp_combine import PeerCombine, cp_combine_mode, max_slot_floats
 from .block_manager import BlockManager, CapacityError
 from .engine import LLMEngine, decode_splits
 
@@ -40,6 +43,14 @@ class CPEngine(LLMEngine):
         super().__init__(cfg, model_cfg, comm=None, rank=0)
         self.model.cp = cp
         self.cp_rank = cp.rank
+        if cp_combine_mode() == "peer" and cp.world > 1:
+            sh = self.model.shape
+            try:
+                cp.peer = PeerCombine(cp.group, self.device,
+                                      max_slot_floats(cfg.max_num_seqs, sh.hkv_local, 1, sh.gqa_local))
+            except Exception as e:  # no multicast on this box: NCCL all-gather
+                import logging
+                logging.getLogger("k8v4").warning("peer partial exchange unavailable (%s); using NCCL", e)
 
     def _alloc_cache(self) -> None:
         cfg = self.cfg

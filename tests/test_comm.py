@@ -1,7 +1,9 @@
-"""TP communicator on CPU: two ``gloo`` ranks as child processes."""
+"""TP communicator on CPU (two ``gloo`` ranks as child processes) and the
+host side of the context-parallel partial exchange."""
 import os
 import socket
 
+import pytest
 import torch
 import torch.multiprocessing as mp
 
@@ -66,3 +68,34 @@ def test_tp_comm_gloo_two_ranks():
     # sum = [0, 3, 6, 9]; rank r keeps elements 2r, 2r+1
     assert out[0]["reduce_scatter"] == [0.0, 3.0]
     assert out[1]["reduce_scatter"] == [6.0, 9.0]
+
+
+def test_cp_peer_exchange_slots_and_bounds(monkeypatch):
+    """Context-parallel decode exchange through multicast stores: mode switch,
+    slot size bound and the two alternating buffers' layout."""
+    from k8v4_xpu_b200.parallel import cp_combine as X
+    monkeypatch.delenv("K8V4_CP_COMBINE", raising=False)
+    assert X.cp_combine_mode() == "nccl"
+    monkeypatch.setenv("K8V4_CP_COMBINE", "peer")
+    assert X.cp_combine_mode() == "peer"
+    monkeypatch.setenv("K8V4_CP_COMBINE", "ring")
+    with pytest.raises(ValueError):
+        X.cp_combine_mode()
+    # the largest launch the CP engine makes fits: one wave of CTAs, >= 2 splits
+    from k8v4_xpu_b200.runtime.engine import decode_splits
+    hkv, gqa = 4, 6
+    cap = X.max_slot_floats(4, hkv, 1, gqa)
+    for B in range(1, 5):
+        for pages in (1, 100, 8192, 16384):
+            nsplit = max(2, decode_splits(pages, B, hkv))
+            assert B * hkv * nsplit * 16 * 130 <= cap
+    # buffers alternate; ranks' slots are packed at this call's size
+    world, rf, sf = 4, 2080, 10400
+    assert X.slot_layout(0, world, 0, rf, sf) == (0, 0, 0)
+    assert X.slot_layout(0, world, 3, rf, sf) == (0, 0, 3 * rf)
+    assert X.slot_layout(1, world, 2, rf, sf) == (1, world * sf, world * sf + 2 * rf)
+    assert X.slot_layout(2, world, 1, rf, sf) == (0, 0, rf)
+    # 16-byte aligned multicast addresses (the store kernel's requirement)
+    assert all(X.slot_layout(c, world, r, rf, sf)[2] % 4 == 0 for c in range(3) for r in range(world))
+    with pytest.raises(ValueError):
+        X.slot_layout(0, world, 0, sf + 1, sf)

@@ -30,9 +30,9 @@ def _log(rank, msg):
         f.write(msg + "\n")
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, combine="nccl"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
-                      LOCAL_RANK=str(rank))
+                      LOCAL_RANK=str(rank), K8V4_CP_COMBINE=combine)
     import torch.distributed as dist
     try:
         from k8v4_xpu_b200 import ops
@@ -57,7 +57,7 @@ def _worker(rank, world, port, q):
             _log(rank, "step %d status %d" % (n, ops.status(clear=False)))
         outs = [s.output for s in seqs]
         torch.cuda.synchronize()
-        q.put((rank, {"outs": outs, "status": ops.status()}))
+        q.put((rank, {"outs": outs, "status": ops.status(), "peer": eng.cp.peer is not None}))
         dist.barrier()
     except Exception:
         _log(rank, traceback.format_exc())
@@ -68,14 +68,17 @@ def _worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_cp2_generation_matches_tp1_greedy():
+@pytest.mark.parametrize("combine", ["nccl", "peer"])
+def test_cp2_generation_matches_tp1_greedy(combine):
+    """Both decode partial exchanges: NCCL all-gather, and multicast stores
+    from the attention kernel with a bounded wait in the merge."""
     from test_mtp_gpu import _teacher_forced_margin
     from k8v4_xpu_b200.models.config import TINY
     from k8v4_xpu_b200.models.dense import DenseModel
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, combine)) for r in range(2)]
     for p in procs:
         p.start()
     out = dict(q.get(timeout=180) for _ in procs)
@@ -84,6 +87,7 @@ def test_cp2_generation_matches_tp1_greedy():
     for r in range(2):
         assert "error" not in out[r], out[r].get("error")
         assert out[r]["status"] == 0
+        assert out[r]["peer"] == (combine == "peer")
     assert out[0]["outs"] == out[1]["outs"]
     m = DenseModel(TINY, device="cuda:0").random_init(seed=0)
     for p, o in zip(PROMPTS, out[0]["outs"]):
