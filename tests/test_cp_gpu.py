@@ -81,3 +81,48 @@ def test_cp_decode_partials_merge_across_ranks(C):
     err = (merged.float().cpu() - ref).abs().max().item()
     assert err < 2e-2, err
     assert ops.status() == 0
+
+
+def test_cp_push_exchange_one_rank_matches_the_workspace_path():
+    """The partial exchange fused into the decode kernel (multicast stores,
+    one signal per CTA, merge behind a bounded wait), on a one-rank group:
+    the merge's wait is met by the attention kernel before it in the stream.
+    Its output equals the workspace path's bit for bit, and the running
+    counts advance by one call's signals per use of each buffer."""
+    import socket
+    import torch.distributed as dist
+    from k8v4_xpu_b200.parallel.cp_combine import PeerCombine, max_slot_floats
+    n = 3001
+    lay, caches, table, kd, vd = _sharded(n, 1, seed=5)
+    g = torch.Generator().manual_seed(6)
+    q = torch.randn(2, lay.hkv * lay.gqa, 128, generator=g).bfloat16().cuda()
+    cu = torch.tensor([0, 1, 2], dtype=torch.int32, device="cuda")
+    lens = torch.tensor([n, n - 700], dtype=torch.int32, device="cuda")
+    bt = table.cuda().view(1, -1).repeat(2, 1).contiguous()
+    nsplit = 5
+    ref = ops.decode_attn(q, cu, lens, bt, caches[0], lay.hkv, lay.gqa, 1, nsplit=nsplit)
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    own_group = not dist.is_initialized()
+    if own_group:
+        dist.init_process_group("nccl", init_method="tcp://127.0.0.1:%d" % port, rank=0, world_size=1,
+                                device_id=torch.device("cuda", 0))
+    try:
+        try:
+            peer = PeerCombine(dist.group.WORLD, torch.device("cuda", 0), max_slot_floats(2, lay.hkv, 1, lay.gqa))
+        except RuntimeError as e:  # no multicast object on this box
+            pytest.skip(str(e))
+        expected = ops.decode_push_ctas(2, lay.hkv, nsplit)
+        for call in range(3):  # buffers 0, 1, 0
+            out = peer.attention(q, cu, lens, bt, caches[0], lay.hkv, lay.gqa, 1, nsplit)
+            torch.cuda.synchronize()
+            assert ops.status() == 0
+            assert torch.equal(out, ref), call
+        assert peer.state[:, 0].tolist() == [2 * expected, expected]
+        assert peer.state[:, 1].tolist() == [0, 0]
+        del peer
+    finally:
+        if own_group:
+            dist.destroy_process_group()
