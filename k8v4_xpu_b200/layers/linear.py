@@ -35,6 +35,22 @@ def uses_w4a8(name: str, rows: int, enabled: bool = True) -> bool:
     return enabled and ".mlp." in name and rows > SMALL_M_MAX
 
 
+_NOTED: set = set()
+
+
+def note_gemm_branch(name: str, rows: int, branch: str, env=None) -> None:
+    """``K8V4_GEMM_DIAGNOSTICS=1``: log which GEMM path a linear took, once
+    per (linear, path) (the reference's switch, ``w4a8_prefill.py:227,240-244``)."""
+    if (os.environ if env is None else env).get("K8V4_GEMM_DIAGNOSTICS", "0") in ("", "0"):
+        return
+    key = (name, branch)
+    if key in _NOTED:
+        return
+    _NOTED.add(key)
+    import logging
+    logging.getLogger("k8v4").info("gemm %s: %s (first at %d rows)", name, branch, rows)
+
+
 def split_for(rows: int, n: int, k: int, sms: int = NUM_SMS) -> int:
     """Split-K factor that fills the GPU for skinny (decode) GEMMs."""
     if rows > 64:

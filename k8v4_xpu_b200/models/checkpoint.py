@@ -70,8 +70,18 @@ def read_model_config(path: str) -> ModelConfig:
 
 
 def _save(tensors: dict, path: str) -> None:
+    """Atomic: written to ``path.partial``, then renamed over ``path``."""
     from safetensors.torch import save_file
-    save_file({k: v.contiguous().cpu() for k, v in tensors.items()}, path)
+    tmp = path + ".partial"
+    save_file({k: v.contiguous().cpu() for k, v in tensors.items()}, tmp)
+    os.replace(tmp, path)
+
+
+def _save_json(obj, path: str, indent: int = 2) -> None:
+    tmp = path + ".partial"
+    with open(tmp, "w") as f:
+        json.dump(obj, f, indent=indent)
+    os.replace(tmp, path)
 
 
 def _linear_tensors(prefix: str, qweight: torch.Tensor, scales: torch.Tensor) -> dict:
@@ -84,7 +94,11 @@ def _linear_tensors(prefix: str, qweight: torch.Tensor, scales: torch.Tensor) ->
 
 def save_checkpoint(model, path: str, shard_layers: int = 8) -> None:
     """Write a TP1 ``DenseModel`` in the GPTQ + side-file format (HF names,
-    q/k/v and gate/up unfused)."""
+    q/k/v and gate/up unfused).
+
+    Every file is written atomically (``.partial``, then renamed; the
+    reference's bake tools do the same, ``tools/assemble_swift_bake.py:203-217``)
+    and ``config.json`` comes last, so a directory holding one is complete."""
     if model.tp != 1:
         raise ValueError("save a tensor-parallel size 1 model")
     from ..layers.linear import Int4Linear
@@ -92,8 +106,6 @@ def save_checkpoint(model, path: str, shard_layers: int = 8) -> None:
         raise ValueError("INT8 islands are chosen when loading (K8V4_INT8_ISLANDS); save the GPTQ model")
     cfg = model.cfg
     os.makedirs(path, exist_ok=True)
-    with open(os.path.join(path, "config.json"), "w") as f:
-        json.dump(config_to_hf(cfg), f, indent=2)
     q_sz, kv_sz = cfg.q_size, cfg.kv_size
     shard: dict = {}
     idx = 0
@@ -137,10 +149,10 @@ def save_checkpoint(model, path: str, shard_layers: int = 8) -> None:
     shard["lm_head.weight"] = lm.weight[: lm.out_features].cpu()
     shard["lm_head.weight_scale"] = lm.scale[: lm.out_features].view(-1, 1).cpu()
     flush(final=True)
-    with open(os.path.join(path, "model.safetensors.index.json"), "w") as f:
-        json.dump(index, f, indent=1)
+    _save_json(index, os.path.join(path, "model.safetensors.index.json"), indent=1)
     _save({"embed_tokens.int8": model.embed_codes.cpu(), "embed_tokens.scale": model.embed_scales.view(-1, 1).cpu()},
           os.path.join(path, SIDE_FILE))
+    _save_json(config_to_hf(cfg), os.path.join(path, "config.json"))
 
 
 class _Reader:

@@ -30,7 +30,7 @@ import torch
 from .. import ops
 from ..kv import skip_layers
 from ..kv.layout import PageLayout, b200_layout
-from ..layers.linear import Int4Linear, Int8RowLinear, uses_w4a8, w4a8_enabled
+from ..layers.linear import Int4Linear, Int8RowLinear, note_gemm_branch, uses_w4a8, w4a8_enabled
 from ..obs.attn_time import attention_span
 from ..obs.stage_profile import stage
 from . import gptq
@@ -291,7 +291,9 @@ class DenseModel:
             with stage(tag + ".all_reduce"):
                 self._all_reduce(x)
         # ---- MLP block
-        if uses_w4a8(L.gate_up.name, T, self.w4a8) and L.gate_up.supports_w4a8 and L.down.supports_w4a8:
+        w4a8 = uses_w4a8(L.gate_up.name, T, self.w4a8) and L.gate_up.supports_w4a8 and L.down.supports_w4a8
+        note_gemm_branch(L.gate_up.name, T, "w4a8" if w4a8 else "w4a16")
+        if w4a8:
             with stage(tag + ".post_norm"):
                 hq8, hs = ops.rmsnorm(x, L.post_norm, cfg.rms_eps, residual=residual, quant=True, sync=sync_o)
             with stage(tag + ".gate_up"):

@@ -194,6 +194,11 @@ class LLMEngine:
                           for i in range(n_layers)]
         self.model.skip_kv = skip
         self.kv_capacity_tokens = blocks * cfg.block_size
+        import logging
+        logging.getLogger("k8v4").info(
+            "KV cache size: %d tokens (%d blocks of %d, %.2f GiB over %d layers%s)", self.kv_capacity_tokens, blocks,
+            cfg.block_size, pages * per_page / 2 ** 30, n_layers,
+            ", skip layers %s in %s" % (sorted(skip), cfg.kv_skip_dtype) if skip else "")
 
     # ------------------------------------------------------------- requests
     def add_request(self, prompt: list[int], params: SamplingParams | None = None) -> Sequence:

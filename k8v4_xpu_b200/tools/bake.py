@@ -32,7 +32,7 @@ import sys
 import torch
 
 from ..models import gptq
-from ..models.checkpoint import SIDE_FILE, _linear_tensors, _save, config_from_hf, config_to_hf
+from ..models.checkpoint import SIDE_FILE, _linear_tensors, _save, _save_json, config_from_hf, config_to_hf
 
 LINEARS = ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "self_attn.o_proj", "mlp.gate_proj",
            "mlp.up_proj", "mlp.down_proj")
@@ -134,8 +134,7 @@ def bake_dense(src: str, out: str, hessians: dict | None = None, layers: int | N
     eq, es = gptq.quantize_int8_rows(t["model.embed_tokens.weight"].float())
     _save({"embed_tokens.int8": eq, "embed_tokens.scale": es}, os.path.join(out, SIDE_FILE))
     new_cfg = config_to_hf(cfg if layers is None else cfg.__class__(**{**cfg.__dict__, "num_layers": L}))
-    with open(os.path.join(out, "config.json"), "w") as f:
-        json.dump(new_cfg, f, indent=2)
+    _save_json(new_cfg, os.path.join(out, "config.json"))  # last: the directory is complete
     return {"linears_gptq": n_gptq, "linears_rtn": n_rtn, "layers": L}
 
 

@@ -165,3 +165,31 @@ def test_tp8_shards_replicate_kv_heads_and_tile_the_full_model():
         v = cfg.vocab // 8
         assert torch.equal(m.lm_head.weight[:v], full.lm_head.weight[rank * v:(rank + 1) * v]), rank
         assert torch.equal(m.embed_codes, full.embed_codes[rank * v:(rank + 1) * v]), rank
+
+
+def test_checkpoint_files_are_written_atomically_config_last(tmp_path, monkeypatch):
+    """A save that dies part way leaves no file under its final name and no
+    config.json (the marker of a complete directory)."""
+    import os
+    from k8v4_xpu_b200.models import checkpoint as C
+    m = _model()
+    real = C._save
+    calls = []
+
+    def dying(tensors, path):
+        calls.append(path)
+        if path.endswith(C.SIDE_FILE):
+            raise OSError("disk full")
+        real(tensors, path)
+
+    monkeypatch.setattr(C, "_save", dying)
+    with pytest.raises(OSError):
+        save_checkpoint(m, str(tmp_path / "a"))
+    names = set(os.listdir(tmp_path / "a"))
+    assert "config.json" not in names and C.SIDE_FILE not in names
+    assert not any(n.endswith(".partial") for n in names)
+    monkeypatch.setattr(C, "_save", real)
+    save_checkpoint(m, str(tmp_path / "b"))
+    names = set(os.listdir(tmp_path / "b"))
+    assert "config.json" in names and C.SIDE_FILE in names
+    assert not any(n.endswith(".partial") for n in names)

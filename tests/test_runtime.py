@@ -256,3 +256,18 @@ def test_split_k_policy_fills_the_gpu():
     assert LIN.split_for(200, 6144, 5120) == 1
     s = LIN.split_for(1, 5120, 17408)
     assert 1 < s and s * 40 <= 148 and (17408 // 128) // s >= 4
+
+
+def test_gemm_diagnostics_log_each_branch_once(caplog):
+    import logging
+    from k8v4_xpu_b200.layers import linear
+    linear._NOTED.clear()
+    env = {"K8V4_GEMM_DIAGNOSTICS": "1"}
+    with caplog.at_level(logging.INFO, logger="k8v4"):
+        linear.note_gemm_branch("layers.0.mlp.gate_up", 4224, "w4a8", env)
+        linear.note_gemm_branch("layers.0.mlp.gate_up", 2000, "w4a8", env)
+        linear.note_gemm_branch("layers.0.mlp.gate_up", 1, "w4a16", env)
+        linear.note_gemm_branch("layers.1.mlp.gate_up", 1, "w4a16", {})  # switch off: nothing
+    msgs = [r.getMessage() for r in caplog.records if r.name == "k8v4"]
+    assert msgs == ["gemm layers.0.mlp.gate_up: w4a8 (first at 4224 rows)",
+                    "gemm layers.0.mlp.gate_up: w4a16 (first at 1 rows)"]
