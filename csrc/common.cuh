@@ -20,7 +20,7 @@ enum : int {
   kErrMbarTimeout = 1,     // an mbarrier wait ran past its time limit
   kErrPeerTimeout = 2,     // a wait on a peer GPU's flag ran past its limit
   kErrBadShape = 3,        // device-side shape guard tripped
-  kErrBadIndex = 4,        // device-side bounds guard tripped (debug builds)
+  kErrBadIndex = 4,        // device-side bounds guard tripped (the access was skipped)
 };
 
 // Nanoseconds a device-side wait may spin before it records a timeout.

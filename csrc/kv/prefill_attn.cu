@@ -46,6 +46,7 @@ struct PrefillParams {
   const int32_t* q_pos;        // optional [T] global position of each query token (CP: strided tokens)
   const uint8_t* caches[MAX_SRC];
   int nsrc;
+  int64_t num_pages;           // pages of every source cache
   __nv_bfloat16* out;          // [T, hq_total, D]
   uint8_t* vstage;             // staged tiles [nseq][stage_tiles][heads] x STAGE_TILE_BYTES
   int stage_tiles;             // tiles per sequence in the staging buffer
@@ -85,8 +86,10 @@ __global__ void __launch_bounds__(256) prefill_stage_kernel(const PrefillParams 
   // V and one scale feed four 16-byte stores of the fp16 tile
   for (int item = threadIdx.x; item < TILE * 4; item += 256) {
     const int key = item >> 2, grp = item & 3;
-    if (key < nvalid) {
-      const uint32_t e = (uint32_t)bt[key >> 4];
+    const uint32_t e = key < nvalid ? (uint32_t)bt[key >> 4] : 0u;
+    const bool in_pool = (int64_t)(e & 0xFFFFFFu) < p.num_pages;
+    if (key < nvalid && !in_pool && grp == 0 && (key & 15) == 0) record_error(kErrBadIndex, 301);
+    if (key < nvalid && in_pool) {  // a page outside the pool reads as zeros (and is reported)
       const int src = (int)(e >> 24) < p.nsrc ? (int)(e >> 24) : 0;  // a bad source reads source 0
       const uint8_t* run = p.caches[src] + ((int64_t)(e & 0xFFFFFFu) * p.hkv + h) * HEAD_BYTES + VS_OFF;
       const int kk = key & 15;
@@ -537,6 +540,7 @@ extern "C" int k8v4_prefill_attn_multi(const void* q, const int32_t* cu_q, const
     p.caches[i] = p.caches[0];
   }
   p.nsrc = nsrc;
+  p.num_pages = num_pages;
   p.q = reinterpret_cast<const __nv_bfloat16*>(q);
   p.cu_q = cu_q;
   p.seq_lens = seq_lens;
