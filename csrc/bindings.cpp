@@ -7,6 +7,7 @@
 // batched decode over every request in one launch) and adds the GEMM, norm,
 // activation, embedding and prefill-attention ops the reference took from
 // libraries.
+#include <string>
 #include <vector>
 #include <torch/library.h>
 #include <ATen/ATen.h>
@@ -566,6 +567,12 @@ void decode_combine_ranks(const at::Tensor& ws_all, int64_t rank_floats, const a
            "decode_combine_ranks");
 }
 
+#ifndef K8V4_SOURCE_HASH
+#define K8V4_SOURCE_HASH "unknown"
+#endif
+// Hash of the csrc/ tree this library was built from (setup.py passes it).
+std::string source_hash() { return K8V4_SOURCE_HASH; }
+
 // Let kernels on the current device read and write `peer`'s memory (context
 // parallelism maps peer KV pools through CUDA IPC; the mapping alone does not
 // grant this device access). Returns false when the pair cannot peer.
@@ -627,6 +634,7 @@ TORCH_LIBRARY(k8v4, m) {
   m.def("embed_int8(Tensor ids, Tensor codes, Tensor scales, Tensor(a!) out, int start) -> ()");
   m.def("argmax(Tensor logits, int offset, Tensor(a!) best_val, Tensor(b!) best_idx) -> ()");
   m.def("status(bool clear) -> int");
+  m.def("source_hash() -> str");
   m.def("enable_peer_access(int peer) -> bool");
   m.def(
       "prefill_attn_cp(Tensor q, Tensor cu_q, Tensor seq_lens, Tensor block_table, Tensor[] caches, Tensor? q_pos, "
@@ -667,5 +675,6 @@ TORCH_LIBRARY_IMPL(k8v4, CompositeExplicitAutograd, m) {
   m.impl("decode_ws_floats", &decode_ws_floats);
   m.impl("wq_gemm_ctas", &wq_gemm_ctas);
   m.impl("status", &status);
+  m.impl("source_hash", &source_hash);
   m.impl("enable_peer_access", &enable_peer_access);
 }

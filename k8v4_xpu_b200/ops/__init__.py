@@ -35,11 +35,26 @@ def load() -> bool:
             raise ImportError("no built k8v4_xpu_b200/_C*.so")
         torch.ops.load_library(path)
         _ = torch.ops.k8v4.status
+        _check_sources(path)
         _LOADED = True
         _ERROR = None
     except Exception as exc:  # pragma: no cover - depends on the build
         _ERROR = "%s: %s" % (type(exc).__name__, exc)
     return _LOADED
+
+
+def _check_sources(path: str) -> None:
+    """Refuse an in-tree library built from other sources than the csrc/
+    tree beside the package (an explicit ``K8V4_LIB`` is taken as given)."""
+    if os.environ.get("K8V4_LIB"):
+        return
+    from ..buildhash import source_hash
+    csrc = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))), "csrc")
+    if not os.path.isdir(csrc):
+        return  # an installed package without sources
+    built, tree = str(torch.ops.k8v4.source_hash()), source_hash(csrc)
+    if built != tree:
+        raise ImportError("%s was built from other sources (%s) than csrc/ (%s); rebuild it" % (path, built, tree))
 
 
 def require() -> None:

@@ -11,6 +11,18 @@ from setuptools import setup
 from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
+
+
+def _source_hash() -> str:
+    # the package module, loaded by path (importing the package needs torch's extension first)
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("_k8v4_buildhash", os.path.join(ROOT, "k8v4_xpu_b200", "buildhash.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod.source_hash(os.path.join(ROOT, "csrc"))
+
+
+SOURCE_HASH = ['-DK8V4_SOURCE_HASH="%s"' % _source_hash()]
 SOURCES = ["csrc/bindings.cpp"] + sorted(glob.glob("csrc/**/*.cu", recursive=True))
 NVCC = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -28,7 +40,7 @@ setup(
             name="k8v4_xpu_b200._C",
             sources=SOURCES,
             include_dirs=[os.path.join(ROOT, "csrc")],
-            extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC},
+            extra_compile_args={"cxx": ["-O3", "-std=c++17"] + SOURCE_HASH, "nvcc": NVCC},
         )
     ],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},

@@ -139,3 +139,29 @@ def test_public_surface_names():
 @pytest.mark.parametrize("f", CUDA_FILES, ids=lambda p: p.name)
 def test_cuda_sources_have_a_header_comment(f):
     assert f.read_text().lstrip().startswith("//"), f
+
+
+def test_source_hash_tracks_every_native_source(tmp_path):
+    import shutil
+    from k8v4_xpu_b200.buildhash import source_hash
+    tree = tmp_path / "csrc"
+    shutil.copytree(CSRC, tree)
+    h0 = source_hash(str(tree))
+    assert h0 == source_hash(str(CSRC)) and len(h0) == 16
+    f = tree / "kv" / "store.cu"
+    f.write_text(f.read_text() + "\n")
+    h1 = source_hash(str(tree))
+    assert h1 != h0
+    (tree / "kv" / "store.cu").rename(tree / "kv" / "store2.cu")
+    assert source_hash(str(tree)) not in (h0, h1)
+
+
+def test_the_in_tree_library_was_built_from_this_tree():
+    """A stale build (sources edited since) is refused by the loader."""
+    from k8v4_xpu_b200 import ops
+    from k8v4_xpu_b200.buildhash import source_hash
+    if ops._library_file() is None:
+        pytest.skip("no in-tree build")
+    assert ops.load(), ops._ERROR
+    import torch
+    assert str(torch.ops.k8v4.source_hash()) == source_hash(str(CSRC))
