@@ -10,6 +10,10 @@ The launcher equivalent of the reference's ``launch.sh`` (T1) and
 * a KV-capacity error at start-up (the pool cannot hold ``--max-model-len``)
   is retried once at the fitted length; any other failure is reported and
   never retried (``launch_tp1.py:15-69``).
+
+``python -m k8v4_xpu_b200 doctor`` prints installation checks as JSON (the
+reference image's build-time checks, T3): library load, source-hash match,
+page-layout asserts, devices.
 """
 from __future__ import annotations
 
@@ -147,13 +151,55 @@ def serve(argv: list[str]) -> int:
     return rc
 
 
+def doctor() -> dict:
+    """Installation checks (the reference image's build-time checks,
+    ``Dockerfile.unified:18-24``: library load, layout asserts). Returns a
+    report; ``ok`` is False when something a GPU run needs is missing."""
+    import torch
+
+    from . import ops
+    from .buildhash import source_hash
+    from .kv.layout import CACHE_DTYPE, b200_layout
+    rep: dict = {"torch": torch.__version__, "cuda_build": torch.version.cuda, "cache_dtype": CACHE_DTYPE}
+    lay = b200_layout(4, 6)
+    # the b200 page: 16 tokens x (128 int8 K + 64 packed V + scales) per head
+    rep["page_bytes_4kv"] = lay.page_bytes
+    rep["layout_ok"] = lay.page_bytes == 16 * 4 * 202 and lay.page == 16 and lay.head_dim == 128
+    rep["library"] = ops._library_file()
+    rep["library_loads"] = ops.load()
+    if not rep["library_loads"]:
+        rep["library_error"] = ops._ERROR
+    else:
+        rep["library_source_hash"] = str(torch.ops.k8v4.source_hash())
+    csrc = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "csrc")
+    if os.path.isdir(csrc):
+        rep["tree_source_hash"] = source_hash(csrc)
+    rep["gpus"] = torch.cuda.device_count() if torch.cuda.is_available() else 0
+    devs = []
+    for i in range(rep["gpus"]):
+        p = torch.cuda.get_device_properties(i)
+        devs.append({"name": p.name, "sm": "%d.%d" % (p.major, p.minor), "sms": p.multi_processor_count,
+                     "mem_gib": round(p.total_memory / 2 ** 30, 1)})
+    rep["devices"] = devs
+    rep["sm100"] = bool(devs) and all(d["sm"] == "10.0" for d in devs)
+    if torch.distributed.is_available() and torch.distributed.is_nccl_available():
+        rep["nccl"] = ".".join(str(x) for x in torch.cuda.nccl.version()) if rep["gpus"] else "available"
+    rep["ok"] = bool(rep["layout_ok"] and rep["library_loads"] and (rep["gpus"] == 0 or rep["sm100"]))
+    return rep
+
+
 def main(argv: list[str] | None = None) -> int:
     argv = list(sys.argv[1:] if argv is None else argv)
     if not argv or argv[0] in ("-h", "--help"):
-        print("usage: python -m k8v4_xpu_b200 serve [options]   (serve --help for options)")
+        print("usage: python -m k8v4_xpu_b200 serve [options]   (serve --help for options)\n"
+              "       python -m k8v4_xpu_b200 doctor            (installation checks, JSON)")
         return 0
     cmd, rest = argv[0], argv[1:]
     if cmd == "serve":
         return serve(rest)
+    if cmd == "doctor":
+        rep = doctor()
+        print(json.dumps(rep, indent=2))
+        return 0 if rep["ok"] else 1
     print("unknown command %r" % cmd, file=sys.stderr)
     return 2

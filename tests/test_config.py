@@ -73,3 +73,14 @@ def test_dry_run_prints_every_rank():
     assert plan["ranks"][1]["env"]["RANK"] == "1" and plan["ranks"][1]["env"]["MASTER_ADDR"] == "127.0.0.1"
     assert "--dry-run" not in plan["ranks"][0]["argv"]
     assert plan["endpoint"].endswith(":8123/v1")
+
+
+def test_doctor_reports_layout_library_and_devices():
+    from k8v4_xpu_b200 import cli
+    rep = cli.doctor()
+    assert rep["layout_ok"] and rep["cache_dtype"] == "int8_k_int4_v"
+    if rep["library"] is not None:  # an in-tree build must load and match its sources
+        assert rep["library_loads"], rep.get("library_error")
+        assert rep["library_source_hash"] == rep["tree_source_hash"]
+    assert rep["ok"] == (rep["library_loads"] and (rep["gpus"] == 0 or rep["sm100"]))
+    assert cli.main(["doctor"]) == (0 if rep["ok"] else 1)
