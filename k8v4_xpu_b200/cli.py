@@ -55,8 +55,12 @@ def _engine_dict(cfg: ServeConfig) -> dict:
     return d
 
 
-def build_engine(cfg: ServeConfig, comm=None, rank: int = 0, device: str = "cuda"):
-    """Engine with the capacity-fit retry: only a CapacityError is retried."""
+def build_engine(cfg: ServeConfig, comm=None, rank: int = 0, device: str = "cuda", cp_group=None):
+    """Engine with the capacity-fit retry: only a CapacityError is retried.
+
+    ``rank`` is the TP rank and ``comm`` the TP group's communicator; with
+    ``--context-parallel-size`` > 1, ``cp_group`` is this rank's CP group
+    (``parallel.groups``) and the engine is the context-parallel one."""
     from .models.config import PRESETS
     from .runtime.block_manager import CapacityError
     from .runtime.engine import LLMEngine
@@ -64,17 +68,23 @@ def build_engine(cfg: ServeConfig, comm=None, rank: int = 0, device: str = "cuda
     if mcfg is None:
         from .models.checkpoint import read_model_config
         mcfg = read_model_config(cfg.checkpoint or cfg.model)
-    ecfg = cfg.engine_config(device)
+
+    def make(ecfg):
+        if cfg.context_parallel_size > 1:
+            from .parallel.cp import CPGroup
+            from .runtime.cp_engine import CPEngine
+            return CPEngine(ecfg, mcfg, CPGroup(cp_group), rank=rank, comm=comm)
+        return LLMEngine(ecfg, mcfg, comm=comm, rank=rank)
+
     try:
-        eng = LLMEngine(ecfg, mcfg, comm=comm, rank=rank)
+        eng = make(cfg.engine_config(device))
     except CapacityError as e:
         if not cfg.fit_capacity or not e.fit_tokens:
             raise
         fit = (e.fit_tokens // cfg.block_size) * cfg.block_size
         print("[k8v4] %s; retrying at max_model_len=%d" % (e, fit), file=sys.stderr, flush=True)
         cfg.max_model_len = fit
-        ecfg = cfg.engine_config(device)
-        eng = LLMEngine(ecfg, mcfg, comm=comm, rank=rank)
+        eng = make(cfg.engine_config(device))
     if cfg.checkpoint:
         from .models.checkpoint import load_checkpoint
         load_checkpoint(eng.model, cfg.checkpoint)
@@ -86,12 +96,14 @@ def run_rank(cfg: ServeConfig) -> int:
     import torch.distributed as dist
 
     from .api.driver import EngineDriver, TPControl, follower_loop
+    from .parallel import groups
     from .parallel.comm import TPComm, init_from_env
     rank, world, local = init_from_env(timeout_s=600)
     device = "cuda:%d" % local
-    comm = TPComm() if world > 1 else None
+    pg = groups.build(cfg.tensor_parallel_size, cfg.context_parallel_size)
+    comm = TPComm(pg.tp_group) if pg.tp > 1 else None
     control = TPControl(dist.new_group(backend="gloo")) if world > 1 else None
-    eng = build_engine(cfg, comm=comm, rank=rank, device=device)
+    eng = build_engine(cfg, comm=comm, rank=pg.tp_rank, device=device, cp_group=pg.cp_group)
     watchdog = hb = None
     if world > 1:
         from .parallel.health import Heartbeat, Watchdog

@@ -33,6 +33,8 @@ PROFILES: dict[str, dict[str, Any]] = {
     "tp8": {"tensor_parallel_size": 8, "max_num_seqs": 4, "enable_prefix_caching": True},
     "cp8": {"tensor_parallel_size": 1, "context_parallel_size": 8, "max_num_seqs": 4,
             "enable_prefix_caching": True},
+    "cp4tp2": {"tensor_parallel_size": 2, "context_parallel_size": 4, "max_num_seqs": 4,
+               "enable_prefix_caching": True},
 }
 
 # field -> (env var, type)
@@ -185,6 +187,8 @@ class ServeConfig:
             raise ValueError("--block-size must be a multiple of the 16-token page")
         if not 0.0 < self.gpu_memory_utilization <= 1.0:
             raise ValueError("--gpu-memory-utilization must lie in (0, 1]")
+        if self.context_parallel_size > 1 and self.speculative_tokens:
+            raise ValueError("--speculative-config (MTP) is not supported with --context-parallel-size")
         if self.kv_cache_dtype_skip_layers:
             if self.context_parallel_size > 1:
                 raise ValueError("--kv-cache-dtype-skip-layers is not supported with --context-parallel-size")
@@ -205,7 +209,7 @@ def build_parser() -> argparse.ArgumentParser:
     ap = argparse.ArgumentParser(prog="k8v4-serve", description="Serve a K8/V4 model (OpenAI-compatible API).")
     a = ap.add_argument
     a("--model", help="model preset (dense-27b, small, tiny) or a checkpoint directory")
-    a("--profile", choices=sorted(PROFILES), help="launcher profile defaults (tp2, tp1, tp4, tp8, cp8)")
+    a("--profile", choices=sorted(PROFILES), help="launcher profile defaults (tp2, tp1, tp4, tp8, cp8, cp4tp2)")
     a("--tensor-parallel-size", "-tp", type=int, dest="tensor_parallel_size")
     a("--context-parallel-size", "-cp", type=int, dest="context_parallel_size")
     a("--kv-cache-dtype")

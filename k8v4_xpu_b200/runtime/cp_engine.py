@@ -15,8 +15,10 @@ same steps. What differs per rank (see ``parallel.cp``):
 
 Decode runs eagerly here. The per-layer partial exchange is an NCCL
 all-gather, or with ``K8V4_CP_COMBINE=peer`` multicast stores from the decode
-attention kernel (``parallel.cp_combine``). MTP and tensor parallelism
-inside a CP group are not supported yet.
+attention kernel (``parallel.cp_combine``). Tensor parallelism inside each
+CP rank (CP x TP, ``parallel.groups``) shards the model over the TP group as
+in the plain engine; the CP exchange then runs between the ranks that hold
+the same KV heads. MTP under CP is not supported yet.
 """
 from __future__ import annotations
 
@@ -31,16 +33,22 @@ from .engine import LLMEngine, decode_splits
 
 
 class CPEngine(LLMEngine):
-    def __init__(self, cfg, model_cfg, cp: CPGroup, rank: int = 0):
-        if cfg.tensor_parallel_size != 1 or cfg.speculative_tokens:
-            raise NotImplementedError("context parallelism runs with tensor parallel size 1 and without MTP")
+    """``cp``: this rank's CP group. With TP inside each CP rank
+    (``tensor_parallel_size`` > 1), ``comm`` is the TP group's communicator
+    and ``rank`` this process's TP rank (``parallel.groups``)."""
+
+    def __init__(self, cfg, model_cfg, cp: CPGroup, rank: int = 0, comm=None):
+        if cfg.speculative_tokens:
+            raise NotImplementedError("context parallelism runs without MTP")
+        if cfg.tensor_parallel_size > 1 and comm is None:
+            raise ValueError("tensor parallelism inside a CP group needs the TP group's communicator")
         if cfg.context_parallel_size != cp.world:
             raise ValueError("context_parallel_size %d != CP group size %d" % (cfg.context_parallel_size, cp.world))
         self.cp = cp
         cfg.cuda_graphs = False
         if cfg.block_size != PAGE * cp.world:
             cfg.block_size = PAGE * cp.world  # one CP block = one page on every rank
-        super().__init__(cfg, model_cfg, comm=None, rank=0)
+        super().__init__(cfg, model_cfg, comm=comm, rank=rank)
         self.model.cp = cp
         self.cp_rank = cp.rank
         if cp_combine_mode() == "peer" and cp.world > 1:

@@ -99,3 +99,63 @@ def test_cp_peer_exchange_slots_and_bounds(monkeypatch):
     assert all(X.slot_layout(c, world, r, rf, sf)[2] % 4 == 0 for c in range(3) for r in range(world))
     with pytest.raises(ValueError):
         X.slot_layout(0, world, 0, sf + 1, sf)
+
+
+def test_tp_cp_group_layout():
+    from k8v4_xpu_b200.parallel import groups as G
+    assert G.tp_members(2, 2) == [[0, 1], [2, 3]] and G.cp_members(2, 2) == [[0, 2], [1, 3]]
+    assert G.tp_members(2, 4) == [[0, 1], [2, 3], [4, 5], [6, 7]]
+    assert G.cp_members(2, 4) == [[0, 2, 4, 6], [1, 3, 5, 7]]
+    assert G.cp_members(1, 8) == [list(range(8))] and G.tp_members(8, 1) == [list(range(8))]
+    for tp, cp in ((2, 2), (2, 4), (4, 2)):
+        seen = set()
+        for r in range(tp * cp):
+            t, c = G.coords(r, tp)
+            assert r in G.tp_members(tp, cp)[c] and r in G.cp_members(tp, cp)[t]
+            assert G.tp_members(tp, cp)[c].index(r) == t and G.cp_members(tp, cp)[t].index(r) == c
+            seen.add((t, c))
+        assert len(seen) == tp * cp
+
+
+def _groups_worker(rank, world, port, tp, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
+    import traceback
+    import torch.distributed as dist
+    from k8v4_xpu_b200.parallel import groups as G
+    from k8v4_xpu_b200.parallel.comm import TPComm, init_from_env
+    from k8v4_xpu_b200.parallel.cp import CPGroup
+    try:
+        r, w, _ = init_from_env(timeout_s=60, backend="gloo")
+        pg = G.build(tp, w // tp)
+        # the TP communicator and the CP group see their own members only
+        tp_sum = TPComm(pg.tp_group).all_reduce(torch.tensor([float(2 ** r)])).item()
+        cp = CPGroup(pg.cp_group)
+        cp_sum = cp.sum_(torch.tensor([float(2 ** r)])).item()
+        q.put((r, {"tp_rank": pg.tp_rank, "cp_rank": pg.cp_rank, "cp_group_rank": cp.rank, "cp_world": cp.world,
+                   "tp_sum": tp_sum, "cp_sum": cp_sum}))
+    except Exception:
+        q.put((rank, {"error": traceback.format_exc()}))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def test_cp2_by_tp2_groups_on_four_gloo_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_groups_worker, args=(r, 4, port, 2, q)) for r in range(4)]
+    for p in procs:
+        p.start()
+    out = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in range(4):
+        o = out[r]
+        assert "error" not in o, o.get("error")
+        t, c = r % 2, r // 2
+        assert (o["tp_rank"], o["cp_rank"], o["cp_group_rank"], o["cp_world"]) == (t, c, c, 2)
+        assert o["tp_sum"] == sum(2 ** m for m in (2 * c, 2 * c + 1))
+        assert o["cp_sum"] == sum(2 ** m for m in (t, t + 2))

@@ -84,3 +84,43 @@ def test_doctor_reports_layout_library_and_devices():
         assert rep["library_source_hash"] == rep["tree_source_hash"]
     assert rep["ok"] == (rep["library_loads"] and (rep["gpus"] == 0 or rep["sm100"]))
     assert cli.main(["doctor"]) == (0 if rep["ok"] else 1)
+
+
+def test_build_engine_picks_the_context_parallel_engine(monkeypatch):
+    """--context-parallel-size > 1 builds the CP engine on this rank's CP
+    group, with the TP communicator and TP rank (CP x TP); otherwise the
+    plain engine."""
+    import pytest
+    from k8v4_xpu_b200 import cli, config
+    from k8v4_xpu_b200.parallel import cp as cp_mod
+    from k8v4_xpu_b200.runtime import cp_engine, engine
+    made = []
+
+    class FakeCPGroup:
+        def __init__(self, group=None):
+            self.group = group
+
+    class FakeEngine:
+        def __init__(self, ecfg, mcfg, *args, **kw):
+            made.append((type(self).__name__, ecfg, args, kw))
+            self.model = None
+
+    class CPEngine(FakeEngine):
+        pass
+
+    class LLMEngine(FakeEngine):
+        pass
+
+    monkeypatch.setattr(cp_mod, "CPGroup", FakeCPGroup)
+    monkeypatch.setattr(cp_engine, "CPEngine", CPEngine)
+    monkeypatch.setattr(engine, "LLMEngine", LLMEngine)
+    cfg = config.resolve(["--model", "tiny", "--context-parallel-size", "2", "--tensor-parallel-size", "2"], env={})
+    cli.build_engine(cfg, comm="tp-comm", rank=1, device="cpu", cp_group="cp-group")
+    name, ecfg, args, kw = made[-1]
+    assert name == "CPEngine" and kw == {"rank": 1, "comm": "tp-comm"} and args[0].group == "cp-group"
+    assert ecfg.context_parallel_size == 2 and ecfg.tensor_parallel_size == 2
+    cfg = config.resolve(["--model", "tiny", "--tensor-parallel-size", "2"], env={})
+    cli.build_engine(cfg, comm="tp-comm", rank=1, device="cpu")
+    assert made[-1][0] == "LLMEngine" and made[-1][3] == {"comm": "tp-comm", "rank": 1}
+    with pytest.raises(ValueError):
+        config.resolve(["--context-parallel-size", "2", "--speculative-config", "mtp/6"], env={})
