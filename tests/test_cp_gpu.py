@@ -112,8 +112,8 @@ def test_cp_push_exchange_one_rank_matches_the_workspace_path():
     try:
         try:
             peer = PeerCombine(dist.group.WORLD, torch.device("cuda", 0), max_slot_floats(2, lay.hkv, 1, lay.gqa))
-        except RuntimeError as e:  # no multicast object on this box
-            pytest.skip(str(e))
+        except (RuntimeError, ValueError, NotImplementedError) as e:  # no one-rank multicast object here
+            pytest.skip("symmetric-memory multicast at one rank: %s" % e)
         expected = ops.decode_push_ctas(2, lay.hkv, nsplit)
         for call in range(3):  # buffers 0, 1, 0
             out = peer.attention(q, cu, lens, bt, caches[0], lay.hkv, lay.gqa, 1, nsplit)
