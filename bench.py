@@ -82,9 +82,15 @@ class ClockSampler:
             self.proc.kill()
         if self.thread:
             self.thread.join(timeout=2)
+        return self.summarize(self.lines)
+
+    @staticmethod
+    def summarize(lines: list[str]) -> dict:
+        """Median SM clock under load (power draw above 300 W; all samples if
+        none), the max clock, and every throttle reason seen active."""
         sm, mx, reasons, loaded = [], None, set(), []
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for ln in self.lines:
+        for ln in lines:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
