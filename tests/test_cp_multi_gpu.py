@@ -93,3 +93,63 @@ def test_cp2_generation_matches_tp1_greedy(combine):
     for p, o in zip(PROMPTS, out[0]["outs"]):
         assert len(o) == 10
         assert _teacher_forced_margin(m, p, o) < 0.05
+
+
+def _worker_cp_tp(rank, world, port, q, tp):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    import torch.distributed as dist
+    try:
+        from k8v4_xpu_b200 import ops
+        from k8v4_xpu_b200.models.config import TINY
+        from k8v4_xpu_b200.parallel import groups
+        from k8v4_xpu_b200.parallel.comm import TPComm, init_from_env
+        from k8v4_xpu_b200.parallel.cp import CPGroup
+        from k8v4_xpu_b200.runtime.cp_engine import CPEngine
+        from k8v4_xpu_b200.runtime.engine import EngineConfig
+        from k8v4_xpu_b200.runtime.scheduler import SamplingParams
+        init_from_env(timeout_s=60)
+        pg = groups.build(tp, world // tp)
+        cfg = EngineConfig(model="tiny", tensor_parallel_size=tp, context_parallel_size=world // tp,
+                           max_model_len=2048, max_num_seqs=2, max_num_batched_tokens=96, num_kv_blocks=96,
+                           device="cuda:%d" % rank)
+        eng = CPEngine(cfg, TINY, CPGroup(pg.cp_group), rank=pg.tp_rank, comm=TPComm(pg.tp_group))
+        _log(rank, "engine cp%d x tp%d" % (world // tp, tp))
+        seqs = [eng.add_request(p, SamplingParams(max_tokens=10, ignore_eos=True)) for p in PROMPTS]
+        while eng.has_unfinished():
+            eng.step()
+        torch.cuda.synchronize()
+        q.put((rank, {"outs": [s.output for s in seqs], "status": ops.status()}))
+        dist.barrier()
+    except Exception:
+        _log(rank, traceback.format_exc())
+        q.put((rank, {"error": traceback.format_exc()}))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs 4 GPUs")
+def test_cp2_by_tp2_generation_matches_tp1_greedy():
+    """Context parallelism with tensor parallelism inside each CP rank: the
+    TP groups shard the model, the CP groups exchange attention partials."""
+    from test_mtp_gpu import _teacher_forced_margin
+    from k8v4_xpu_b200.models.config import TINY
+    from k8v4_xpu_b200.models.dense import DenseModel
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker_cp_tp, args=(r, 4, port, q, 2)) for r in range(4)]
+    for p in procs:
+        p.start()
+    out = dict(q.get(timeout=240) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+    for r in range(4):
+        assert "error" not in out[r], out[r].get("error")
+        assert out[r]["status"] == 0
+        assert out[r]["outs"] == out[0]["outs"]
+    m = DenseModel(TINY, device="cuda:0").random_init(seed=0)
+    for p, o in zip(PROMPTS, out[0]["outs"]):
+        assert len(o) == 10
+        assert _teacher_forced_margin(m, p, o) < 0.05
