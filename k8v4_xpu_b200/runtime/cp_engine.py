@@ -22,6 +22,8 @@ the same KV heads. MTP under CP is not supported yet.
 """
 from __future__ import annotations
 
+import os
+
 import numpy as np
 import torch
 
@@ -51,6 +53,9 @@ class CPEngine(LLMEngine):
         super().__init__(cfg, model_cfg, comm=comm, rank=rank)
         self.model.cp = cp
         self.cp_rank = cp.rank
+        self.cp_graphs = CPDecodeGraphs(self) if cp_graphs_enabled() else None
+        # shutdown paths release `graphs` before the process group goes
+        self.graphs = self.cp_graphs
         if cp_combine_mode() == "peer" and cp.world > 1:
             sh = self.model.shape
             try:
@@ -138,6 +143,8 @@ class CPEngine(LLMEngine):
         return inp, owned_logit
 
     def _plain_step(self, sched):
+        if self.cp_graphs is not None and sched.is_decode_only and self.cp_graphs.can_run(sched):
+            return self._commit(sched, self.cp_graphs.run(sched))
         inp, owned = self._build_inputs(sched)
         n_logit = sum(1 for c in sched.chunks if c.needs_logits)
         hidden = self.model.forward(inp, self.kv_caches, self.ws)
@@ -154,3 +161,132 @@ class CPEngine(LLMEngine):
             self.d2h_bytes += all_tok.size * 8
             tokens = np.array([all_tok[i] for i, c in enumerate(sched.chunks) if c.needs_logits], np.int64)
         return self._commit(sched, tokens)
+
+
+def cp_graphs_enabled() -> bool:
+    """``K8V4_CP_GRAPHS=1``: decode steps under CP replay captured CUDA graphs
+    (off by default until the multi-GPU tests have run them)."""
+    return os.environ.get("K8V4_CP_GRAPHS", "0") not in ("", "0")
+
+
+class CPDecodeGraphs:
+    """CUDA graphs of the CP decode step, one per batch size.
+
+    Per step the host stages into graph-stable buffers the new tokens, their
+    positions, this rank's KV slot of each (-1 where another rank owns the
+    page), and this rank's page list and key count of each sequence. The
+    split count is fixed per batch size (one wave of CTAs at the longest
+    local page list), and the partial exchange (NCCL all-gather or the
+    attention kernel's multicast stores) is captured with the rest of the
+    step; every rank captures and replays the same graphs in the same order.
+    Padding sequences hold no keys on any rank and write no KV.
+    """
+
+    def __init__(self, eng: "CPEngine"):
+        self.eng = eng
+        cfg = eng.cfg
+        dev = eng.device
+        self.sizes = list(range(1, cfg.max_num_seqs + 1))
+        self.local_w = (eng.max_pages + eng.cp.world - 1) // eng.cp.world + 1
+        B = cfg.max_num_seqs
+        self.ids = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.pos = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.slots = torch.full((B,), -1, dtype=torch.int64, device=dev)
+        self.cu = torch.arange(B + 1, dtype=torch.int32, device=dev)
+        self.lens = torch.ones(B, dtype=torch.int32, device=dev)
+        self.table = torch.zeros((B, 1), dtype=torch.int32, device=dev)
+        self.rows = torch.arange(B, dtype=torch.int64, device=dev)
+        self.local_bt = torch.zeros((B, self.local_w), dtype=torch.int32, device=dev)
+        self.local_lens = torch.zeros(B, dtype=torch.int32, device=dev)
+        self._pin64 = torch.zeros(3 * B, dtype=torch.int64, pin_memory=True)
+        self._pin32 = torch.zeros(2 * B + B * self.local_w, dtype=torch.int32, pin_memory=True)
+        self.graphs: dict[int, tuple] = {}
+        self.pool = None
+
+    def can_run(self, sched) -> bool:
+        # the multicast exchange alternates two buffers per call; a captured
+        # step keeps that alternation across replays only with an even count
+        if self.eng.cp.peer is not None and len(self.eng.model.layers) % 2:
+            return False
+        return len(sched.chunks) <= len(self.sizes) and all(c.num_tokens == 1 for c in sched.chunks)
+
+    def _inputs(self, B: int, nsplit: int) -> StepInputs:
+        return StepInputs(
+            input_ids=self.ids[:B], positions=self.pos[:B], slots=self.slots[:B], cu_q=self.cu[:B + 1],
+            seq_lens=self.lens[:B], block_table=self.table[:B], logit_rows=self.rows[:B], max_q_len=1,
+            is_decode=True, cp_local_bt=self.local_bt[:B], cp_local_lens=self.local_lens[:B], nsplit=nsplit)
+
+    def _benign(self, B: int) -> None:
+        self.slots[:B].fill_(-1)
+        self.pos[:B].zero_()
+        self.ids[:B].zero_()
+        self.lens[:B].fill_(1)
+        self.local_lens[:B].zero_()
+        self.local_bt[:B].zero_()
+
+    def capture(self, B: int) -> None:
+        eng = self.eng
+        nsplit = max(2, decode_splits(self.local_w, B, eng.layout.hkv))
+        self._benign(B)
+        inp = self._inputs(B, nsplit)
+        stream = torch.cuda.Stream(device=eng.device)
+        stream.wait_stream(torch.cuda.current_stream(eng.device))
+        with torch.cuda.stream(stream):
+            for _ in range(2):  # warm-up: kernel attributes, allocator, communicator
+                out = eng.model.greedy(eng.model.forward(inp, eng.kv_caches, eng.ws))
+        torch.cuda.current_stream(eng.device).wait_stream(stream)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, pool=self.pool, stream=stream):
+            out = eng.model.greedy(eng.model.forward(inp, eng.kv_caches, eng.ws))
+        if self.pool is None:
+            self.pool = g.pool()
+        torch.cuda.synchronize(eng.device)
+        self.graphs[B] = (g, out)
+
+    def run(self, sched) -> np.ndarray:
+        eng, cp = self.eng, self.eng.cp
+        B_real = len(sched.chunks)
+        B = next(s for s in self.sizes if s >= B_real)
+        if B not in self.graphs:
+            self.capture(B)
+        W = self.local_w
+        p64 = self._pin64.numpy()
+        p32 = self._pin32.numpy()
+        p64[:3 * B] = 0
+        p64[2 * B:3 * B] = -1
+        p32[:2 * B + B * W] = 0
+        p32[:B] = 1  # padding sequences: one key, none of it on this rank
+        for i, c in enumerate(sched.chunks):
+            seq = c.seq
+            blocks = eng.blocks.tables[seq.seq_id]
+            end = c.start + 1
+            p64[i] = seq.tokens[-1]
+            p64[B + i] = c.start
+            p64[2 * B + i] = cp.slot(blocks, c.start)
+            p32[i] = end
+            pages, keys = cp.local_pages(blocks, end)
+            if len(pages) > W:
+                raise RuntimeError("sequence holds %d local pages, the graphs %d" % (len(pages), W))
+            p32[B + i] = keys
+            p32[2 * B + i * W: 2 * B + i * W + len(pages)] = pages
+        g64 = self._pin64[:3 * B].to(eng.device, non_blocking=True)
+        g32 = self._pin32[:2 * B + B * W].to(eng.device, non_blocking=True)
+        self.ids[:B].copy_(g64[:B], non_blocking=True)
+        self.pos[:B].copy_(g64[B:2 * B], non_blocking=True)
+        self.slots[:B].copy_(g64[2 * B:3 * B], non_blocking=True)
+        self.lens[:B].copy_(g32[:B], non_blocking=True)
+        self.local_lens[:B].copy_(g32[B:2 * B], non_blocking=True)
+        self.local_bt[:B].copy_(g32[2 * B:].view(B, W), non_blocking=True)
+        eng.h2d_bytes += 3 * B * 8 + (2 * B + B * W) * 4
+        g, out = self.graphs[B]
+        g.replay()
+        tokens = eng._pin_out[:B]
+        tokens.copy_(out, non_blocking=True)
+        torch.cuda.current_stream(eng.device).synchronize()
+        eng.d2h_bytes += B_real * 8
+        return tokens.numpy()[:B_real].copy()
+
+    def release(self) -> None:
+        """Drop every graph (they hold NCCL calls: before the process group goes)."""
+        self.graphs.clear()
+        self.pool = None

@@ -30,9 +30,9 @@ def _log(rank, msg):
         f.write(msg + "\n")
 
 
-def _worker(rank, world, port, q, combine="nccl"):
+def _worker(rank, world, port, q, combine="nccl", graphs=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
-                      LOCAL_RANK=str(rank), K8V4_CP_COMBINE=combine)
+                      LOCAL_RANK=str(rank), K8V4_CP_COMBINE=combine, K8V4_CP_GRAPHS="1" if graphs else "0")
     import torch.distributed as dist
     try:
         from k8v4_xpu_b200 import ops
@@ -57,7 +57,11 @@ def _worker(rank, world, port, q, combine="nccl"):
             _log(rank, "step %d status %d" % (n, ops.status(clear=False)))
         outs = [s.output for s in seqs]
         torch.cuda.synchronize()
-        q.put((rank, {"outs": outs, "status": ops.status(), "peer": eng.cp.peer is not None}))
+        res = {"outs": outs, "status": ops.status(), "peer": eng.cp.peer is not None,
+               "graphs": sorted(eng.cp_graphs.graphs) if eng.cp_graphs is not None else None}
+        if eng.graphs is not None:
+            eng.graphs.release()  # graphs holding NCCL calls go before the process group
+        q.put((rank, res))
         dist.barrier()
     except Exception:
         _log(rank, traceback.format_exc())
@@ -68,17 +72,18 @@ def _worker(rank, world, port, q, combine="nccl"):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("combine", ["nccl", "peer"])
-def test_cp2_generation_matches_tp1_greedy(combine):
-    """Both decode partial exchanges: NCCL all-gather, and multicast stores
-    from the attention kernel with a bounded wait in the merge."""
+@pytest.mark.parametrize("combine,graphs", [("nccl", False), ("peer", False), ("nccl", True), ("peer", True)])
+def test_cp2_generation_matches_tp1_greedy(combine, graphs):
+    """Both decode partial exchanges (NCCL all-gather, and multicast stores
+    from the attention kernel with a bounded wait in the merge), eager and
+    in captured decode graphs."""
     from test_mtp_gpu import _teacher_forced_margin
     from k8v4_xpu_b200.models.config import TINY
     from k8v4_xpu_b200.models.dense import DenseModel
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, combine)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, combine, graphs)) for r in range(2)]
     for p in procs:
         p.start()
     out = dict(q.get(timeout=180) for _ in procs)
@@ -88,6 +93,10 @@ def test_cp2_generation_matches_tp1_greedy(combine):
         assert "error" not in out[r], out[r].get("error")
         assert out[r]["status"] == 0
         assert out[r]["peer"] == (combine == "peer")
+        if graphs:  # decode steps ran as replays (one graph per batch size seen)
+            assert out[r]["graphs"] and set(out[r]["graphs"]) <= {1, 2}
+        else:
+            assert out[r]["graphs"] is None
     assert out[0]["outs"] == out[1]["outs"]
     m = DenseModel(TINY, device="cuda:0").random_init(seed=0)
     for p, o in zip(PROMPTS, out[0]["outs"]):
