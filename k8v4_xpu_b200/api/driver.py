@@ -8,7 +8,8 @@ step's commands over a CPU (gloo) group before applying them, so every rank
 schedules identically and issues the same collectives in the same order. The
 broadcast also runs while idle (every ``idle_s``), which doubles as a
 heartbeat: a follower whose rank 0 died ends with the group's timeout
-instead of waiting forever.
+instead of waiting forever. (In the reference this is vLLM's own engine
+loop and TP workers, ``k8v4_v030/launch.sh:176-194``.)
 """
 from __future__ import annotations
 

@@ -3,7 +3,9 @@
 ``setup.py`` compiles ``source_hash(csrc)`` into the library and the loader
 compares it with the tree next to the package, so a library built from other
 sources (a stale in-tree build that travelled with a snapshot, or sources
-edited since) is refused instead of being run.
+edited since) is refused instead of being run. The reference namespaces its
+compile caches by configuration for the same reason, so that stale
+artefacts cannot bypass a changed hook (``k8v4_v030/launch.sh:29,161``).
 """
 from __future__ import annotations
 

@@ -1,7 +1,8 @@
 """GPTQ INT4 + INT8 side-file checkpoints: read, write, load with TP sharding.
 
 On-disk format (the reference's baked checkpoint, ``tools/bake_gptq_resume.py
-:51-75`` and ``tools/assemble_swift_bake.py:58-147,256-289``):
+:51-75``, ``tools/assemble_swift_bake.py:58-147`` with the side-file entry at
+``:118,135``, read back by ``k8v4_v030/embed_int8_runtime.py:20-50``):
 
 * ``config.json``: HF-style architecture keys, ``quantization_config``
   (``quant_method: gptq, bits: 4, group_size: 128, sym: true, desc_act:
@@ -97,7 +98,7 @@ def save_checkpoint(model, path: str, shard_layers: int = 8) -> None:
     q/k/v and gate/up unfused).
 
     Every file is written atomically (``.partial``, then renamed; the
-    reference's bake tools do the same, ``tools/assemble_swift_bake.py:203-217``)
+    reference's bake tools do the same, ``tools/assemble_swift_bake.py:41-55``, ``tools/calibrate_swift_bake.py:105-106``)
     and ``config.json`` comes last, so a directory holding one is complete."""
     if model.tp != 1:
         raise ValueError("save a tensor-parallel size 1 model")

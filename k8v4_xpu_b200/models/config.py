@@ -4,6 +4,9 @@
 / 4 KV heads of dim 128, SiLU-gated MLP 17408, RMSNorm, RoPE theta 1e6, vocab
 151936, INT8 embedding and lm_head (per-row scaled), GPTQ INT4 g128 linears,
 one MTP draft layer. Smaller presets keep the same structure for tests.
+The reference serves the same shape (hidden 5120, its embedding partitions
+``(124160, 5120)`` per TP2 rank, ``huggingface/swift-baked/README.md:88``;
+MTP6 and the served flags at ``k8v4_v030/launch.sh:176-194``).
 """
 from __future__ import annotations
 

@@ -19,6 +19,12 @@ in a :class:`StepInputs`. A layer listed in ``skip_kv`` (set by the engine
 from ``kv_cache_dtype_skip_layers``) keeps its KV in plain fp8 / bf16 pages
 and runs RoPE, store and attention through ``kv.skip_layers`` instead of
 ``rope_store`` and the K8/V4 attention kernels.
+
+Reference counterparts: the K8/V4 attention backend
+(``k8v4_v030/backend.py:79-486``), the MLP-only W4A8 prefill hook
+(``k8v4_v030/w4a8_prefill.py:146-157,382-392``) and the INT8 embedding
+runtime (``k8v4_v030/embed_int8_runtime.py:11-56``); the rest of the decoder
+is stock vLLM there.
 """
 from __future__ import annotations
 

@@ -9,7 +9,7 @@ Checkpoint format (the reference's bake, ``tools/bake_gptq_resume.py:51-75``):
   ``desc_act`` false.
 
 INT8 per-row (embedding side file and lm_head, ``tools/assemble_swift_bake.py
-:256-289``): codes int8 ``[V, H]`` = ``round(w / s)`` clamped to
+:100-106``): codes int8 ``[V, H]`` = ``round(w / s)`` clamped to
 [-128, 127] with ``s = amax(|row|) / 127`` stored fp16 ``[V, 1]``.
 
 This module holds the CPU/torch reference of both formats: quantizers (round

@@ -1,7 +1,9 @@
 """Python entry points of the sm_100a kernel library (``torch.ops.k8v4``).
 
 The extension ``k8v4_xpu_b200._C`` is built in-tree by ``setup.py
-build_ext --inplace``. On a machine with a CUDA device a missing or broken
+build_ext --inplace`` (the reference loads its prebuilt ``libxe2_kv.so`` from
+``XE2_KV_LIB`` the same way, ``k8v4_v030/ops_api.py:10-25``; ``K8V4_LIB`` is
+the equivalent override here). On a machine with a CUDA device a missing or broken
 extension raises instead of falling back to slower code: every op here runs
 the CUDA kernel or fails loudly.
 """

@@ -21,6 +21,8 @@ of the call that read buffer ``s``. So no rank still reads a slot that is
 being overwritten.
 
 ``K8V4_CP_COMBINE`` = ``nccl`` (default) or ``peer`` selects the exchange.
+The reference has no context parallelism, so this module has no counterpart
+there.
 """
 from __future__ import annotations
 

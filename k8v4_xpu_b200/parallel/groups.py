@@ -6,7 +6,9 @@ shards), and a CP group holds the ranks with the same TP rank, one per CP
 rank (the same KV heads, page-sharded by sequence position). With both
 degrees above one, every rank creates every group, in the same order, as
 ``torch.distributed.new_group`` requires; with one of them, the other's group
-is the whole world. A degree of one has no group (``None``).
+is the whole world. A degree of one has no group (``None``). The reference
+gets TP from vLLM (``k8v4_v030/launch.sh:184``) and has no CP, so there is no
+counterpart for the CP x TP layout.
 """
 from __future__ import annotations
 

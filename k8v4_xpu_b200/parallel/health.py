@@ -13,6 +13,10 @@ Three layers, none of which needs a GPU fault to be exercised:
   rendezvous store; :class:`Watchdog` checks the others' counters before each
   step and raises :class:`CommTimeout` naming the ranks that stopped, so the
   survivors learn of a lost rank before their next launch.
+
+The reference has a launcher health wait with a deadline and container-exit
+detection (``k8v4_v030/launch.sh:219-232``) and nothing between ranks; these
+layers are what a one-process-per-GPU job needs in its place.
 """
 from __future__ import annotations
 

@@ -14,7 +14,9 @@ speculator. ``step()`` runs one scheduler step:
 
 Every TP rank runs the same engine on the same request stream (rank 0 drives
 the API; the others follow with identical scheduling decisions), so ranks
-issue the same collectives in the same order.
+issue the same collectives in the same order. The reference runs stock
+vLLM's engine with these settings (``k8v4_v030/launch.sh:176-194``: 4,224
+batched tokens, prefix caching, MTP6, FULL_DECODE_ONLY graphs).
 """
 from __future__ import annotations
 
