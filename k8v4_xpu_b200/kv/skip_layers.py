@@ -4,11 +4,11 @@ paged cache next to the K8/V4 layers.
 Reference behaviour (``tools/patch_vllm_skip_fp8.py:1-188``): the layers
 listed in ``kv_cache_dtype_skip_layers`` take the dtype that
 ``VLLM_KV_SKIP_DTYPE`` names (default ``auto``, the model dtype) instead of
-K8/V4 and run the stock attention backend (``:53-58``, ``:123-140``). In vLLM
-all KV groups share one page size, so a skipped layer's page is padded up to
-the K8/V4 page, its block is the largest 64-token multiple that divides that
-page with a 16-byte token stride, and the padding is spread over the tokens
-(``:81-117``, ``:160-186``).
+K8/V4 and run the stock attention backend (``:62-70``, ``:123-140``). In
+vLLM all KV groups share one page size, so a skipped layer's page is padded
+up to the K8/V4 page, its block is the largest 64-token multiple that divides
+that page with a 16-byte token stride, and the padding is spread over the
+tokens (``:47-61``, ``:81-117``, ``:160-186``).
 
 Here every layer's cache is its own tensor indexed by the same page ids, so a
 skip layer needs neither a second block table nor padding: its page holds the

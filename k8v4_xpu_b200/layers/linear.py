@@ -23,7 +23,11 @@ NUM_SMS = 148
 
 
 def w4a8_enabled() -> bool:
-    """``K8V4_PREFILL_GEMM`` = ``w4a8`` (default) or ``w4a16`` (MLP keeps W4A16)."""
+    """``K8V4_PREFILL_GEMM`` = ``w4a8`` (default) or ``w4a16`` (MLP keeps W4A16).
+
+    The default is the reference deployment's (``k8v4_v030/launch.sh:160``
+    sets ``w4a8``; the module's own fallback is ``w4a16``,
+    ``k8v4_v030/w4a8_prefill.py:385``)."""
     mode = os.environ.get("K8V4_PREFILL_GEMM", "w4a8").strip().lower()
     if mode not in ("w4a8", "w4a16"):
         raise ValueError("K8V4_PREFILL_GEMM must be w4a8 or w4a16, got %r" % mode)
