@@ -67,7 +67,8 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
     def params_for(req: _Common, prompt_len: int) -> SamplingParams:
         if req.n != 1:
             raise HTTPException(400, "only n=1 is supported")
-        mt = req.max_completion_tokens or req.max_tokens or 16
+        mt = req.max_completion_tokens if req.max_completion_tokens is not None else req.max_tokens
+        mt = 16 if mt is None else mt  # an explicit 0 is refused below, not defaulted
         if mt < 1:
             raise HTTPException(400, "max_tokens must be positive")
         if prompt_len < 1:

@@ -100,3 +100,23 @@ def test_engine_failure_turns_health_red():
         assert h.status_code == 503 and "mbarrier" in h.json()["detail"]
         assert c.post("/v1/completions", json={"prompt": [1, 2], "max_tokens": 2}).status_code == 503
     driver.stop()
+
+
+def test_request_validation_and_non_streaming_chat(client):
+    c, eng, _ = client
+    bad = [
+        {"prompt": [1, 2], "max_tokens": 0},          # max_tokens must be positive
+        {"prompt": [], "max_tokens": 2},              # empty prompt
+        {"prompt": ["a", "b"], "max_tokens": 2},      # one prompt per request
+    ]
+    for body in bad:
+        assert c.post("/v1/completions", json=body).status_code == 400, body
+    assert c.post("/v1/completions", json={"max_tokens": 2}).status_code == 422  # no prompt at all
+    r = c.post("/v1/completions", json={"prompt": ["ab"], "max_tokens": 1, "ignore_eos": True}).json()
+    assert r["usage"]["prompt_tokens"] == 2 and r["object"] == "text_completion"
+    r = c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "hi"}], "max_tokens": 3,
+                                            "ignore_eos": True}).json()
+    msg = r["choices"][0]["message"]
+    assert msg["role"] == "assistant" and isinstance(msg["content"], str)
+    assert r["usage"]["completion_tokens"] == 3 and r["object"] == "chat.completion"
+    eng.blocks.check_invariants()
