@@ -358,7 +358,8 @@ class LLMEngine:
 
     def fork_sequence(self, seq: Sequence) -> Sequence:
         """A new running sequence with the same tokens and its own copy of the KV tail."""
-        child = Sequence(next(self.scheduler._ids), list(seq.prompt), seq.params, list(seq.output))
+        child = Sequence(next(self.scheduler._ids), list(seq.prompt), seq.params, list(seq.output),
+                         prefill_len=seq.prefill_len)
         copies = self.blocks.fork(seq.seq_id, child.seq_id, seq.computed)
         r = self.blocks.ratio
         for src, dst in copies:
@@ -376,7 +377,8 @@ class LLMEngine:
         Used to build several long contexts from one prefill without sharing
         pages (so concurrent decodes read distinct memory).
         """
-        child = Sequence(next(self.scheduler._ids), list(seq.prompt), seq.params, list(seq.output))
+        child = Sequence(next(self.scheduler._ids), list(seq.prompt), seq.params, list(seq.output),
+                         prefill_len=seq.prefill_len)
         child.draft = list(seq.draft)
         self.blocks.tables[child.seq_id] = []
         self.blocks.keys[child.seq_id] = []

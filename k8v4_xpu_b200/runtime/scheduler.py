@@ -48,6 +48,9 @@ class Sequence:
     finish_reason: str | None = None
     draft: list[int] = dataclasses.field(default_factory=list)  # MTP proposals for the next step
     prefill_start: float | None = None
+    # tokens to prefill: the prompt, or after a recompute preemption every
+    # token the sequence held (prompt + output so far)
+    prefill_len: int | None = None
 
     @property
     def tokens(self) -> "TokenView":
@@ -64,8 +67,12 @@ class Sequence:
         return len(self.prompt) + len(self.output)
 
     @property
+    def prefill_target(self) -> int:
+        return len(self.prompt) if self.prefill_len is None else self.prefill_len
+
+    @property
     def in_prefill(self) -> bool:
-        return self.computed < len(self.prompt)
+        return self.computed < self.prefill_target
 
     @property
     def done(self) -> bool:
@@ -161,9 +168,17 @@ class Scheduler:
         return bool(self.waiting or self.running)
 
     def _admit(self, seq: Sequence) -> bool:
+        """Admit the queue head if the pool holds its whole prefill. The blocks
+        are reserved now, so the later chunks of a chunked prefill never find
+        the pool emptied by decoding sequences in between."""
         try:
-            cached = self.blocks.allocate(seq.seq_id, seq.prompt)
+            cached = self.blocks.allocate(seq.seq_id, seq.tokens[:seq.prefill_target])
         except CapacityError:
+            return False
+        try:
+            self.blocks.ensure(seq.seq_id, seq.prefill_target)
+        except CapacityError:  # allocate checked the same count; kept as a guard
+            self.blocks.free_seq(seq.seq_id)
             return False
         seq.cached_tokens = cached
         seq.computed = cached
@@ -206,9 +221,9 @@ class Scheduler:
                 break
             if not seq.in_prefill or any(c.seq is seq for c in chunks):
                 continue
-            n = min(budget, len(seq.prompt) - seq.computed)
+            n = min(budget, seq.prefill_target - seq.computed)
             self.blocks.ensure(seq.seq_id, seq.computed + n)
-            last = seq.computed + n == len(seq.prompt)
+            last = seq.computed + n == seq.prefill_target
             chunks.append(ScheduledChunk(seq, seq.computed, n, True, last))
             budget -= n
         while budget > 0 and self.waiting and len(self.running) < self.max_num_seqs:
@@ -217,9 +232,9 @@ class Scheduler:
                 break
             self.waiting.popleft()
             seq.prefill_start = time.monotonic()
-            n = min(budget, len(seq.prompt) - seq.computed)
+            n = min(budget, seq.prefill_target - seq.computed)
             self.blocks.ensure(seq.seq_id, seq.computed + n)
-            last = seq.computed + n == len(seq.prompt)
+            last = seq.computed + n == seq.prefill_target
             chunks.append(ScheduledChunk(seq, seq.computed, n, True, last))
             budget -= n
         total = sum(c.num_tokens for c in chunks)
@@ -227,12 +242,16 @@ class Scheduler:
         return SchedulerOutput(chunks, total, decode_only, preempted)
 
     def _preempt(self, seq: Sequence) -> None:
-        """Recompute-style preemption: free the blocks and requeue at the front."""
+        """Recompute-style preemption: free the blocks and requeue at the front.
+
+        Prompt and output stay as they are (the output already streamed to the
+        client, and ``max_tokens`` counts it); on readmission the sequence
+        prefills every token it held and samples its next one from that
+        prefill's last row."""
         self.blocks.free_seq(seq.seq_id)
         self.running.remove(seq)
         seq.status = SeqStatus.WAITING
-        seq.prompt = seq.prompt + seq.output
-        seq.output = []
+        seq.prefill_len = seq.num_tokens
         seq.computed = 0
         seq.draft = []
         self.waiting.appendleft(seq)

@@ -321,8 +321,10 @@ class MTPSpeculator:
             else:
                 tok = None
             if c.is_prefill:
-                nxt = seq.prompt[c.start + 1:end + 1] if end < len(seq.prompt) else seq.prompt[c.start + 1:end]
-                if end >= len(seq.prompt):
+                # the prefilled tokens are the prompt, or after a preemption prompt + output
+                L = seq.prefill_target
+                nxt = seq.tokens[c.start + 1:min(end + 1, L)]
+                if end >= L:
                     nxt = list(nxt) + [tok]
                 ids[r:r + n] = nxt
                 if c.needs_logits:

@@ -165,21 +165,38 @@ def test_scheduler_chunked_prefill_then_decode_first():
 
 
 def test_scheduler_limits_and_preemption():
-    bm = BlockManager(4, block_size=16)
-    sch = Scheduler(bm, max_num_seqs=1, max_num_batched_tokens=64, max_model_len=100)
+    bm = BlockManager(5, block_size=16)  # 80 tokens: one max_model_len sequence fits the pool
+    sch = Scheduler(bm, max_num_seqs=2, max_num_batched_tokens=64, max_model_len=80)
     with pytest.raises(ValueError):
         sch.add([])
     with pytest.raises(ValueError):
-        sch.add(list(range(90)), SamplingParams(max_tokens=20))
+        sch.add(list(range(70)), SamplingParams(max_tokens=20))
     a = sch.add(list(range(40)), SamplingParams(max_tokens=40))
     b = sch.add(list(range(100, 110)))
     out = sch.schedule()
-    assert [c.seq for c in out.chunks] == [a]  # max_num_seqs=1 holds b back
-    a.output = [7] * 25  # 65 tokens, 64 written: the next write needs a 5th block
+    assert [c.seq for c in out.chunks] == [a, b]
+    a.output = [7] * 25  # 65 tokens, 64 written: the next write needs two more blocks, one is free
     a.computed = 64
+    b.output = [1]
+    b.computed = 10
     out = sch.schedule()
     assert out.preempted == [a] and sch.num_preemptions == 1
-    assert a.prompt[-1] == 7 and a.computed == 0 and a.output == []
+    # recompute preemption keeps prompt and output (max_tokens counts the output)
+    assert len(a.prompt) == 40 and a.output == [7] * 25 and a.computed == 0
+    assert a.prefill_target == 65 and a.in_prefill
+    assert [c.seq for c in out.chunks] == [b]
+    bm.check_invariants()
+    sch.finish(b, "length")
+    out = sch.schedule()  # readmitted: prefill every token it held, in budget-sized chunks
+    assert [(c.seq, c.start, c.num_tokens, c.is_prefill, c.needs_logits) for c in out.chunks] == [(a, 0, 64, True, False)]
+    a.computed = 64
+    out = sch.schedule()
+    assert [(c.start, c.num_tokens, c.needs_logits) for c in out.chunks] == [(64, 1, True)]
+    a.computed = 65
+    a.output.append(8)  # sampled from the recompute prefill's last row
+    assert not a.in_prefill
+    out = sch.schedule()
+    assert [(c.start, c.num_tokens, c.is_prefill) for c in out.chunks] == [(65, 1, False)]
     bm.check_invariants()
 
 

@@ -1,0 +1,56 @@
+"""Randomised scheduler + block manager runs (CPU): adds with shared
+prefixes (prefix caching), aborts, chunked prefill and preemption on a small
+pool. After every step the block invariants hold, every sequence's output
+follows the fake model's rule (next = last + 1), no sequence exceeds its
+budget, and once adds stop every request drains."""
+import random
+
+import pytest
+
+from fakes import FakeEngine
+from k8v4_xpu_b200.runtime.scheduler import SamplingParams
+
+
+preemptions: list[int] = []
+
+
+@pytest.mark.parametrize("seed", range(12))
+def test_random_add_abort_step_keeps_invariants(seed):
+    rng = random.Random(seed)
+    eng = FakeEngine(max_num_seqs=rng.choice([1, 2, 4]), budget=rng.choice([16, 40, 64]),
+                     num_blocks=rng.choice([8, 10, 24]), max_model_len=128)
+    prefixes = [[rng.randrange(900) for _ in range(rng.randrange(8, 40))] for _ in range(3)]
+    live, done = [], []
+    for step in range(200 + 5000):
+        if step < 200 and rng.random() < 0.3:
+            prompt = list(rng.choice(prefixes)) + [rng.randrange(900) for _ in range(rng.randrange(0, 20))]
+            seq = eng.add_request(prompt, SamplingParams(max_tokens=rng.randrange(1, 64), ignore_eos=True))
+            live.append(seq)
+        if step < 200 and live and rng.random() < 0.05:
+            victim = rng.choice(live)
+            eng.abort(victim.seq_id)
+            live.remove(victim)
+        if eng.has_unfinished():
+            for seq in eng.step():
+                done.append(seq)
+                if seq in live:
+                    live.remove(seq)
+        eng.blocks.check_invariants()
+        for seq in live + done:
+            assert len(seq.output) <= seq.params.max_tokens
+            toks = seq.prompt + seq.output
+            for i, t in enumerate(seq.output):  # the fake model's rule
+                assert t == (toks[len(seq.prompt) + i - 1] + 1) % eng.vocab, (seq.seq_id, i)
+        if step >= 200 and not eng.has_unfinished():
+            break
+    assert not eng.has_unfinished(), "requests did not drain"
+    preemptions.append(eng.scheduler.num_preemptions)
+    for seq in done:
+        assert len(seq.output) == seq.params.max_tokens
+
+
+def test_the_random_runs_reached_preemption():
+    """The runs above (same module, run first) exercised recompute preemption."""
+    if len(preemptions) < 12:
+        pytest.skip("run with the parametrised test")
+    assert sum(1 for n in preemptions if n > 0) >= 3, preemptions
