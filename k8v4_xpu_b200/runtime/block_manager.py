@@ -202,6 +202,8 @@ class BlockManager:
         """
         ptable = self.tables[parent]
         n_full = int(tokens) // self.block_size
+        if len(ptable) > n_full and self.num_free < 1:  # fail before any refcount moves
+            raise CapacityError("KV cache out of blocks")
         table = []
         for b in ptable[:n_full]:
             self._ref(b)
