@@ -288,3 +288,23 @@ def test_gemm_diagnostics_log_each_branch_once(caplog):
     msgs = [r.getMessage() for r in caplog.records if r.name == "k8v4"]
     assert msgs == ["gemm layers.0.mlp.gate_up: w4a8 (first at 4224 rows)",
                     "gemm layers.0.mlp.gate_up: w4a16 (first at 1 rows)"]
+
+
+def test_token_view_matches_list_concatenation():
+    import random
+    from k8v4_xpu_b200.runtime.scheduler import TokenView
+    rng = random.Random(0)
+    for _ in range(2000):
+        a = [rng.randrange(100) for _ in range(rng.randrange(0, 6))]
+        b = [rng.randrange(100) for _ in range(rng.randrange(0, 6))]
+        v, ref = TokenView(a, b), a + b
+        assert len(v) == len(ref) and list(v) == ref
+        i = rng.randrange(-len(ref) - 2, len(ref) + 2)
+        if -len(ref) <= i < len(ref):
+            assert v[i] == ref[i]
+        else:
+            with pytest.raises(IndexError):
+                v[i]
+        s = slice(rng.choice([None] + list(range(-8, 9))), rng.choice([None] + list(range(-8, 9))),
+                  rng.choice([None, 1, 2, -1]))
+        assert list(v[s]) == ref[s]
