@@ -120,3 +120,28 @@ def test_request_validation_and_non_streaming_chat(client):
     assert msg["role"] == "assistant" and isinstance(msg["content"], str)
     assert r["usage"]["completion_tokens"] == 3 and r["object"] == "chat.completion"
     eng.blocks.check_invariants()
+
+
+def test_concurrent_requests_under_kv_pressure_keep_every_token():
+    """A pool too small for all requests at once forces recompute preemption
+    mid-generation; every response still carries exactly max_tokens tokens
+    that follow the fake model's rule (next = last + 1)."""
+    import concurrent.futures as cf
+    eng = FakeEngine(max_num_seqs=4, budget=48, num_blocks=10, max_model_len=160)
+    driver = EngineDriver(eng).start()
+    app = build_app(driver, ByteTokenizer(1000), "tiny", 160)
+    with TestClient(app) as c:
+        def one(i):
+            prompt = list(range(10 * i, 10 * i + 30))
+            r = c.post("/v1/completions", json={"prompt": prompt, "max_tokens": 40, "ignore_eos": True})
+            return prompt, r.json()
+        with cf.ThreadPoolExecutor(6) as ex:
+            results = list(ex.map(one, range(1, 9)))
+        for prompt, r in results:
+            toks = r["choices"][0]["token_ids"]
+            assert len(toks) == 40 and r["usage"]["completion_tokens"] == 40
+            seq = prompt + toks
+            assert all(seq[len(prompt) + j] == (seq[len(prompt) + j - 1] + 1) % 1000 for j in range(40))
+    assert eng.scheduler.num_preemptions > 0
+    eng.blocks.check_invariants()
+    driver.stop()
