@@ -108,3 +108,39 @@ def test_token_view():
     assert v[1:4] == [2, 3, 4] and v[:2] == [1, 2] and v[3:] == [4, 5] and v[::2] == [1, 3, 5]
     assert list(v) == [1, 2, 3, 4, 5] and v == [1, 2, 3, 4, 5]
     assert np.array_equal(np.asarray(v[0:5]), np.arange(1, 6))
+
+
+def test_random_serving_keeps_every_staged_row_equal_to_its_table():
+    """Sequences come and go (adds with shared prompts, aborts, preemption on
+    a small pool, identical blocks swapped in by publish), so batch slots
+    change hands; after every staging each slot's device row equals its
+    sequence's page table."""
+    import random
+    for seed in range(8):
+        rng = random.Random(seed)
+        eng = _engine(num_blocks=rng.choice([10, 16, 40]), seqs=4, width=64)
+        sch, bm = eng.scheduler, eng.blocks
+        stems = [[rng.randrange(500) for _ in range(rng.randrange(20, 60))] for _ in range(2)]
+        for step in range(250):
+            if step < 150 and rng.random() < 0.25:
+                prompt = list(rng.choice(stems)) + [rng.randrange(500) for _ in range(rng.randrange(0, 20))]
+                sch.add(prompt, SamplingParams(max_tokens=rng.randrange(5, 60), ignore_eos=True))
+            if step < 150 and sch.running and rng.random() < 0.05:
+                sch.abort(rng.choice(list(sch.running)).seq_id)
+            s = sch.schedule()
+            if not s.chunks:
+                continue
+            if s.is_decode_only:
+                stage_decode_inputs(eng, s, len(s.chunks), 1)
+                for i, c in enumerate(s.chunks):
+                    pages = bm.page_table(c.seq.seq_id)
+                    assert eng.ws.block_table[i, :len(pages)].tolist() == pages, (seed, step, i)
+            for c in s.chunks:
+                seq = c.seq
+                seq.computed = c.start + c.num_tokens
+                if c.needs_logits:
+                    seq.output.append((seq.tokens[-1] + 1) % 500)
+                bm.publish(seq.seq_id, seq.tokens, seq.computed)
+                if len(seq.output) >= seq.params.max_tokens:
+                    sch.finish(seq, "length")
+            bm.check_invariants()
