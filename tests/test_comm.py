@@ -159,3 +159,40 @@ def test_cp2_by_tp2_groups_on_four_gloo_ranks():
         assert (o["tp_rank"], o["cp_rank"], o["cp_group_rank"], o["cp_world"]) == (t, c, c, 2)
         assert o["tp_sum"] == sum(2 ** m for m in (2 * c, 2 * c + 1))
         assert o["cp_sum"] == sum(2 ** m for m in (t, t + 2))
+
+
+def test_cp_page_maps_against_a_brute_force_shard_model():
+    """CP block b = C pages: logical page i of a sequence lives on rank i % C
+    at physical page blocks[i // C]. Every token's owner, slot, the encoded
+    table and each rank's local page list agree with that model."""
+    import random
+    from k8v4_xpu_b200.parallel.cp import CPGroup, entry
+    rng = random.Random(0)
+    for _ in range(200):
+        C = rng.choice([1, 2, 4, 8])
+        n = rng.randrange(1, 400)
+        n_pages = (n + 15) // 16
+        blocks = rng.sample(range(1000), (n_pages + C - 1) // C)
+        groups = []
+        for r in range(C):
+            g = object.__new__(CPGroup)
+            g.rank, g.world = r, C
+            groups.append(g)
+        for g in groups:
+            assert g.encoded_pages(blocks, n) == [entry(i % C, blocks[i // C]) for i in range(n_pages)]
+        owned = {r: [] for r in range(C)}
+        for p in range(n):
+            i = p // 16
+            owner = i % C
+            for g in groups:
+                assert g.owner(p) == owner
+                want = blocks[i // C] * 16 + p % 16 if g.rank == owner else -1
+                assert g.slot(blocks, p) == want
+            owned[owner].append(p)
+        for g in groups:
+            pages, keys = g.local_pages(blocks, n)
+            assert keys == len(owned[g.rank])
+            assert pages == [blocks[i // C] for i in range(g.rank, n_pages, C)]
+            # local key k of this rank is global token owned[k]: pages in order, 16 per page
+            for k, p in enumerate(owned[g.rank]):
+                assert pages[k // 16] * 16 + k % 16 == g.slot(blocks, p)
