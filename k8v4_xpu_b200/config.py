@@ -187,6 +187,19 @@ class ServeConfig:
             raise ValueError("--block-size must be a multiple of the 16-token page")
         if not 0.0 < self.gpu_memory_utilization <= 1.0:
             raise ValueError("--gpu-memory-utilization must lie in (0, 1]")
+        if self.num_kv_blocks is not None and self.num_kv_blocks < 1:
+            raise ValueError("--num-kv-blocks must be positive")
+        if self.layers is not None and self.layers < 1:
+            raise ValueError("--layers must be positive")
+        if not 0 <= self.port <= 65535:
+            raise ValueError("--port must lie in [0, 65535]")
+        if self.seed < 0:
+            raise ValueError("--seed must be non-negative")
+        if self.forced_accept_mean is not None:
+            if not self.speculative_tokens:
+                raise ValueError("--forced-accept-mean needs --speculative-config")
+            if not 1.0 <= self.forced_accept_mean <= self.speculative_tokens + 1:
+                raise ValueError("--forced-accept-mean must lie in [1, %d]" % (self.speculative_tokens + 1))
         if self.context_parallel_size > 1 and self.speculative_tokens:
             raise ValueError("--speculative-config (MTP) is not supported with --context-parallel-size")
         if self.kv_cache_dtype_skip_layers:

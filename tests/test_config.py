@@ -124,3 +124,15 @@ def test_build_engine_picks_the_context_parallel_engine(monkeypatch):
     assert made[-1][0] == "LLMEngine" and made[-1][3] == {"comm": "tp-comm", "rank": 1}
     with pytest.raises(ValueError):
         config.resolve(["--context-parallel-size", "2", "--speculative-config", "mtp/6"], env={})
+
+
+def test_out_of_range_values_are_refused_up_front():
+    import pytest
+    from k8v4_xpu_b200 import config
+    for argv in (["--num-kv-blocks", "-3"], ["--port", "70000"], ["--seed", "-1"], ["--layers", "0"],
+                 ["--forced-accept-mean", "3.0"],
+                 ["--forced-accept-mean", "0.5", "--speculative-config", "mtp/6"],
+                 ["--forced-accept-mean", "8.0", "--speculative-config", "mtp/6"]):
+        with pytest.raises(ValueError):
+            config.resolve(argv, env={})
+    assert config.resolve(["--forced-accept-mean", "3.0", "--speculative-config", "mtp/6"], env={}).forced_accept_mean == 3.0
