@@ -22,6 +22,7 @@ from prometheus_client import CONTENT_TYPE_LATEST
 from pydantic import BaseModel, Field
 
 from ..runtime.scheduler import SamplingParams
+from .tokenizer import IncrementalDecoder
 
 
 class StreamOptions(BaseModel):
@@ -134,6 +135,7 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
 
         async def events():
             n_out = 0
+            detok = IncrementalDecoder(tokenizer)
             chunk_obj = "chat.completion.chunk" if chat else "text_completion"
             if chat:
                 first = {"id": rid, "object": chunk_obj, "created": created, "model": served_model_name,
@@ -150,7 +152,7 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
                     new, fin, why = await out.get()
                     n_out += len(new)
                     if new or fin:
-                        text = tokenizer.decode(new) if new else ""
+                        text = detok.push(new, final=fin)
                         ch = ({"index": 0, "delta": {"content": text}, "finish_reason": why if fin else None}
                               if chat else {"index": 0, "text": text, "finish_reason": why if fin else None,
                                             "logprobs": None})

@@ -43,6 +43,36 @@ class ByteTokenizer:
         return self.encode(text + "<|assistant|>\n")
 
 
+class IncrementalDecoder:
+    """Text deltas of a growing token list, for streaming.
+
+    Decoding each delta alone splits multi-byte characters (and, for
+    subword tokenizers, spacing that depends on the previous token). Instead
+    the window of tokens since the last emission is decoded twice, with and
+    without the new tokens, and the difference is emitted; while the window
+    ends in an incomplete character (U+FFFD), nothing is emitted until more
+    tokens complete it or the stream ends. The concatenated deltas equal one
+    decode of all tokens."""
+
+    def __init__(self, tokenizer):
+        self.tok = tokenizer
+        self.ids: list[int] = []
+        self.prefix = 0  # window start: tokens before it are emitted for good
+        self.read = 0    # tokens up to here are emitted
+
+    def push(self, new, final: bool = False) -> str:
+        self.ids.extend(int(t) for t in new)
+        before = self.tok.decode(self.ids[self.prefix:self.read])
+        now = self.tok.decode(self.ids[self.prefix:])
+        if len(now) > len(before) and (final or not now.endswith("\ufffd")):
+            self.prefix, self.read = self.read, len(self.ids)
+            return now[len(before):]
+        if final:
+            self.prefix = self.read = len(self.ids)
+            return now[len(before):]
+        return ""
+
+
 def _content(m: dict) -> str:
     c = m.get("content", "")
     if isinstance(c, list):  # OpenAI content parts: keep the text parts

@@ -145,3 +145,44 @@ def test_concurrent_requests_under_kv_pressure_keep_every_token():
     assert eng.scheduler.num_preemptions > 0
     eng.blocks.check_invariants()
     driver.stop()
+
+
+def test_incremental_decoder_never_splits_a_character():
+    import random
+    from k8v4_xpu_b200.api.tokenizer import IncrementalDecoder
+    tok = ByteTokenizer(1000)
+    text = "héllo wörld, 日本語のテキスト 🎉🚀 ok"
+    ids = tok.encode(text)
+    rng = random.Random(0)
+    for _ in range(200):
+        dec, out, i = IncrementalDecoder(tok), [], 0
+        while i < len(ids):
+            n = rng.randrange(0, 4)
+            piece = dec.push(ids[i:i + n], final=i + n >= len(ids))
+            assert "�" not in piece
+            out.append(piece)
+            i += n
+        out.append(dec.push([], final=True))
+        assert "".join(out) == text
+    # bytes that never form a character still come out, at the end at the latest
+    bad = tok.encode("a") + [0xE6 + 3, 0x97 + 3] + tok.encode("b")
+    dec = IncrementalDecoder(tok)
+    streamed = "".join(dec.push([t]) for t in bad) + dec.push([], final=True)
+    assert streamed == tok.decode(bad)
+
+
+def test_streamed_text_equals_one_decode_of_the_streamed_tokens(client):
+    c, *_ = client
+    # ids 0xC3+3, 0xA9+3 ... : the fake model counts up through multi-byte UTF-8 lead/continuation bytes
+    texts, ids = [], []
+    with c.stream("POST", "/v1/completions", json={"prompt": [0xC2 + 3], "max_tokens": 12, "ignore_eos": True,
+                                                   "stream": True}) as r:
+        for line in r.iter_lines():
+            if not line.startswith("data: ") or line == "data: [DONE]":
+                continue
+            ch = json.loads(line[6:])["choices"]
+            if ch:
+                texts.append(ch[0]["text"])
+                ids += ch[0]["token_ids"]
+    assert len(ids) == 12
+    assert "".join(texts) == ByteTokenizer(1000).decode(ids)
