@@ -49,13 +49,21 @@ class TPControl:
         return obj[0]
 
 
-def apply_commands(engine, cmds, seqs: dict, handles: dict | None = None) -> None:
+def apply_commands(engine, cmds, seqs: dict, handles: dict | None = None, on_reject=None) -> None:
     """Apply one step's commands in order. ``seqs`` maps request id -> sequence
-    on every rank (followers add requests in the same order, so ids agree)."""
+    on every rank (followers add requests in the same order, so ids agree).
+    A request the engine refuses (``ValueError``: empty, too long) is
+    dropped on every rank alike and reported through ``on_reject``; it does
+    not stop the engine."""
     for c in cmds:
         if c[0] == "add":
             _, rid, prompt, params = c
-            seq = engine.add_request(prompt, SamplingParams(**params))
+            try:
+                seq = engine.add_request(prompt, SamplingParams(**params))
+            except ValueError as e:
+                if on_reject is not None:
+                    on_reject(rid, str(e))
+                continue
             seqs[rid] = seq
             if handles is not None and rid in handles:
                 handles[rid].seq = seq
@@ -147,6 +155,11 @@ class EngineDriver:
                 del self._handles[rid]
                 self._seqs.pop(rid, None)
 
+    def _reject(self, rid: int, msg: str) -> None:
+        h = self._handles.pop(rid, None)
+        if h is not None:
+            self._emit(h, [], True, "rejected: " + msg)
+
     def _fail_all(self, msg: str) -> None:
         for rid, h in list(self._handles.items()):
             self._emit(h, [], True, "error")
@@ -160,7 +173,7 @@ class EngineDriver:
                 cmds = self._drain(block=idle)
                 if self.control is not None:
                     cmds = self.control.exchange(cmds + ([("stop",)] if self._stop.is_set() else []))
-                apply_commands(eng, cmds, self._seqs, self._handles)
+                apply_commands(eng, cmds, self._seqs, self._handles, on_reject=self._reject)
                 if self.watchdog is not None:
                     self.watchdog.guard()  # a lost rank stops us before the next launch
                 if eng.has_unfinished():

@@ -126,6 +126,8 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
                     break
             if reason == "error":
                 raise HTTPException(500, "engine failed")
+            if reason and reason.startswith("rejected: "):
+                raise HTTPException(400, reason[len("rejected: "):])
             text = tokenizer.decode(toks)
             choice = ({"index": 0, "message": {"role": "assistant", "content": text}, "finish_reason": reason}
                       if chat else {"index": 0, "text": text, "finish_reason": reason, "logprobs": None})
@@ -150,6 +152,10 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
                         driver.abort(h)
                         return
                     new, fin, why = await out.get()
+                    if fin and why and why.startswith("rejected: "):
+                        yield "data: %s\n\n" % json.dumps({"error": {"message": why[len("rejected: "):],
+                                                                      "type": "invalid_request_error"}})
+                        break
                     n_out += len(new)
                     if new or fin:
                         text = detok.push(new, final=fin)

@@ -186,3 +186,23 @@ def test_streamed_text_equals_one_decode_of_the_streamed_tokens(client):
                 ids += ch[0]["token_ids"]
     assert len(ids) == 12
     assert "".join(texts) == ByteTokenizer(1000).decode(ids)
+
+
+def test_a_request_the_engine_refuses_fails_alone():
+    """The engine enforces a shorter max_model_len than the HTTP layer knows:
+    the refused request gets a 400 (or an error event when streaming) and the
+    server keeps serving."""
+    eng = FakeEngine(max_model_len=64)
+    driver = EngineDriver(eng).start()
+    app = build_app(driver, ByteTokenizer(1000), "tiny", 512)
+    with TestClient(app) as c:
+        r = c.post("/v1/completions", json={"prompt": list(range(3, 103)), "max_tokens": 4})
+        assert r.status_code == 400 and "max_model_len" in r.json()["detail"]
+        with c.stream("POST", "/v1/completions", json={"prompt": list(range(3, 103)), "max_tokens": 4,
+                                                       "stream": True}) as s:
+            lines = [ln for ln in s.iter_lines() if ln.startswith("data: ")]
+        assert "error" in json.loads(lines[0][6:])
+        ok = c.post("/v1/completions", json={"prompt": [10, 11], "max_tokens": 3, "ignore_eos": True})
+        assert ok.status_code == 200 and ok.json()["choices"][0]["token_ids"] == [12, 13, 14]
+        assert driver.healthy
+    driver.stop()
