@@ -3,7 +3,8 @@
 ``bench/serve_coding.py:27-45`` and ``bench/held_curve.py`` of the reference
 read vLLM's ``/metrics``; the names here are the same so those clients work
 unchanged: request gauges, token counters, TTFT / e2e latency histograms,
-KV-cache usage, prefix-cache queries and hits, preemptions, and the
+KV-cache usage, prefix-cache queries and hits, preemptions, per-request
+prefill / decode time, cached and computed prompt tokens, and the
 speculative-decoding counters (drafts, draft tokens, accepted tokens,
 accepted tokens per position).
 """
@@ -41,6 +42,16 @@ class ServingMetrics:
         self.iter_tokens = Histogram("vllm:iteration_tokens_total", "Tokens per engine step", L,
                                      buckets=(1, 8, 16, 32, 64, 128, 256, 512, 1024, 2048, 4096, 8192),
                                      registry=r)
+        # per finished request (the reference's clients read these:
+        # bench/held_curve.py:36-47, bench/serve_coding.py:32-45)
+        self.prefill_time = Histogram("vllm:request_prefill_time_seconds", "Admission to first token", L,
+                                      buckets=_LAT, registry=r)
+        self.decode_time = Histogram("vllm:request_decode_time_seconds", "First token to finish", L,
+                                     buckets=_LAT, registry=r)
+        self.prompt_cached = Counter("vllm:prompt_tokens_cached", "Prompt tokens served from the prefix cache",
+                                     L, registry=r)
+        self.kv_computed = Histogram("vllm:request_prefill_kv_computed_tokens", "Prompt tokens computed (not cached)",
+                                     L, buckets=(16, 256, 1024, 4096, 16384, 65536, 262144), registry=r)
         self.spec_drafts = Counter("vllm:spec_decode_num_drafts", "Speculative steps x sequences", L, registry=r)
         self.spec_draft_tokens = Counter("vllm:spec_decode_num_draft_tokens", "Draft tokens proposed", L,
                                          registry=r)
@@ -94,6 +105,14 @@ class ServingMetrics:
                     max(0.0, (seq.finish_time - seq.first_token_time) / (len(seq.output) - 1)))
         if seq.finish_time is not None:
             self.e2e.labels(m).observe(max(0.0, seq.finish_time - seq.arrival))
+        start = getattr(seq, "prefill_start", None)
+        if start is not None and seq.first_token_time is not None:
+            self.prefill_time.labels(m).observe(max(0.0, seq.first_token_time - start))
+            if seq.finish_time is not None:
+                self.decode_time.labels(m).observe(max(0.0, seq.finish_time - seq.first_token_time))
+        cached = int(getattr(seq, "cached_tokens", 0) or 0)
+        self.prompt_cached.labels(m).inc(cached)
+        self.kv_computed.labels(m).observe(max(0, len(seq.prompt) - cached))
 
     def render(self) -> bytes:
         return generate_latest(self.registry)

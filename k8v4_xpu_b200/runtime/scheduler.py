@@ -231,7 +231,8 @@ class Scheduler:
             if not self._admit(seq):
                 break
             self.waiting.popleft()
-            seq.prefill_start = time.monotonic()
+            if seq.prefill_start is None:  # first admission (a preempted request keeps it)
+                seq.prefill_start = time.monotonic()
             n = min(budget, seq.prefill_target - seq.computed)
             self.blocks.ensure(seq.seq_id, seq.computed + n)
             last = seq.computed + n == seq.prefill_target

@@ -32,9 +32,12 @@ def test_health_models_metrics(client):
     body = c.get("/metrics").text
     for name in ("vllm:prompt_tokens_total", "vllm:generation_tokens_total", "vllm:num_requests_running",
                  "vllm:kv_cache_usage_perc", "vllm:time_to_first_token_seconds_bucket",
-                 "vllm:e2e_request_latency_seconds_count", "vllm:prefix_cache_queries_total"):
+                 "vllm:e2e_request_latency_seconds_count", "vllm:prefix_cache_queries_total",
+                 "vllm:request_prefill_time_seconds_sum", "vllm:request_decode_time_seconds_count",
+                 "vllm:prompt_tokens_cached_total", "vllm:request_prefill_kv_computed_tokens_sum"):
         assert name in body, name
     assert 'vllm:generation_tokens_total{model_name="tiny"} 4.0' in body
+    assert 'vllm:request_prefill_kv_computed_tokens_sum{model_name="tiny"} 3.0' in body
 
 
 def test_completion_tokens_and_usage(client):
