@@ -81,11 +81,11 @@ class ServingMetrics:
         self.preemptions.labels(m).inc(self._delta("preempt", sch.num_preemptions))
         self.prefix_queries.labels(m).inc(self._delta("pq", engine.blocks.prefix_queries))
         self.prefix_hits.labels(m).inc(self._delta("ph", engine.blocks.prefix_hits))
-        its = st.get("iteration_tokens", [])
-        n_seen = self._last.get("iters", 0)
-        for t in its[n_seen:]:
-            self.iter_tokens.labels(m).observe(t)
-        self._last["iters"] = len(its)
+        its = st.get("iteration_tokens")
+        if its:  # drained here (same thread as the engine), so the list stays short
+            for t in its:
+                self.iter_tokens.labels(m).observe(t)
+            its.clear()
         mtp = getattr(engine, "mtp", None)
         if mtp is not None:
             s = mtp.stats

@@ -289,7 +289,10 @@ class LLMEngine:
             finished = self._plain_step(sched)
         dt = time.perf_counter() - t0
         self.stats["steps"] += 1
-        self.stats["iteration_tokens"].append(sched.num_tokens)
+        its = self.stats["iteration_tokens"]  # the metrics exporter drains it
+        its.append(sched.num_tokens)
+        if len(its) > 65536:  # nothing drains it: keep the recent half
+            del its[:32768]
         if sched.is_decode_only:
             self.stats["decode_time"] += dt
         else:

@@ -209,3 +209,13 @@ def test_a_request_the_engine_refuses_fails_alone():
         assert ok.status_code == 200 and ok.json()["choices"][0]["token_ids"] == [12, 13, 14]
         assert driver.healthy
     driver.stop()
+
+
+def test_iteration_token_history_is_drained_by_the_exporter(client):
+    c, eng, driver = client
+    for i in range(3):
+        assert c.post("/v1/completions", json={"prompt": [5 + i], "max_tokens": 3, "ignore_eos": True}).status_code == 200
+    body = c.get("/metrics").text
+    count = [ln for ln in body.splitlines() if ln.startswith("vllm:iteration_tokens_total_count")]
+    assert count and float(count[0].split()[-1]) >= 3
+    assert len(eng.stats["iteration_tokens"]) <= 1  # drained after each step (one may be in flight)
