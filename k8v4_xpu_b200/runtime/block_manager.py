@@ -58,6 +58,7 @@ class BlockManager:
         # out may change (new table, replaced block, truncation, free), so a
         # device copy of a table can be extended instead of rewritten
         self.version: dict[int, int] = {}
+        self._clock = 0
         self.cached: dict[bytes, int] = {}
         self.evictable: collections.OrderedDict[int, None] = collections.OrderedDict()
         self.tables: dict[int, list[int]] = {}
@@ -222,10 +223,13 @@ class BlockManager:
         for b in reversed(self.tables.pop(seq_id, [])):
             self._unref(b)
         self.keys.pop(seq_id, None)
-        self._bump(seq_id)
+        # versions come from one clock, so a sequence allocated again (after
+        # a preemption) never repeats an old version: dropping the entry is safe
+        self.version.pop(seq_id, None)
 
     def _bump(self, seq_id: int) -> None:
-        self.version[seq_id] = self.version.get(seq_id, 0) + 1
+        self._clock += 1
+        self.version[seq_id] = self._clock
 
     def page_table(self, seq_id: int) -> list[int]:
         """Kernel pages of the sequence (block ids expanded by the page ratio)."""

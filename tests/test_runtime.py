@@ -308,3 +308,18 @@ def test_token_view_matches_list_concatenation():
         s = slice(rng.choice([None] + list(range(-8, 9))), rng.choice([None] + list(range(-8, 9))),
                   rng.choice([None, 1, 2, -1]))
         assert list(v[s]) == ref[s]
+
+
+def test_block_manager_keeps_no_state_for_finished_sequences():
+    bm = BlockManager(64, block_size=16)
+    seen = set()
+    for sid in range(500):
+        bm.allocate(sid, list(range(sid % 7, sid % 7 + 40)))
+        bm.ensure(sid, 40)
+        seen.add(bm.version[sid])
+        bm.free_seq(sid)
+    assert bm.version == {} and bm.tables == {} and bm.keys == {}
+    # a sequence allocated again (after a preemption) gets a version it never had
+    bm.allocate(7, [1, 2, 3])
+    assert bm.version[7] not in seen
+    bm.check_invariants()
