@@ -106,3 +106,26 @@ def test_tiled_online_softmax_equals_dense():
     sc = sc.masked_fill(torch.arange(S).view(1, 1, -1) >= ends.view(3, 1, 1), float("-inf"))
     ref = torch.einsum("tgs,sd->tgd", torch.softmax(sc, -1), v)
     assert (tiled - ref).abs().max().item() < 1e-4
+
+
+def test_workspace_sizing_matches_the_native_library():
+    """The host's split-K workspace sizes (decode plan, CP exchange slots)
+    follow the native kernels' own formula."""
+    import pytest
+    from k8v4_xpu_b200 import ops
+    from k8v4_xpu_b200.attention import plan as P
+    from k8v4_xpu_b200.parallel.cp_combine import max_slot_floats
+    from k8v4_xpu_b200.runtime.engine import decode_splits
+    if not ops.load():
+        pytest.skip("native library not built")
+    for nseq in (1, 3, 4):
+        for hkv in (1, 2, 4):
+            for q in (1, 2, 7, 10):
+                for gqa in (3, 6):
+                    if q * gqa > 64:
+                        continue
+                    for nsplit in (1, 5, 37, 64):
+                        assert P.decode_workspace_floats(nseq, hkv, nsplit, q, gqa) == \
+                            ops.decode_ws_floats(nseq, hkv, nsplit, q, gqa)
+                    ns = max(2, decode_splits(8192, nseq, hkv))
+                    assert ops.decode_ws_floats(nseq, hkv, ns, q, gqa) <= max_slot_floats(nseq, hkv, q, gqa)
