@@ -70,6 +70,9 @@ class FusedAllReduce:
         self.flag_mc = int(hf.multicast_ptr)
         if self.data_mc == 0 or self.flag_mc == 0:
             raise RuntimeError("no multicast address for the all-reduce buffers")
+        if self.data_mc == self.data.data_ptr() or self.flag_mc == self.flags.data_ptr():
+            # multimem instructions need a real multicast mapping, not the unicast buffer
+            raise RuntimeError("the multicast address is the local buffer (no multicast object)")
         # per slot: [signals consumed so far, consumer CTAs done] (local to this rank)
         self.state = torch.zeros((self.SLOTS, 2), dtype=torch.int64, device=self.device)
         torch.cuda.synchronize(self.device)
