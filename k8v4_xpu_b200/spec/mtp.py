@@ -38,6 +38,17 @@ from ..runtime.block_manager import CapacityError
 from ..runtime.graphs import decode_inputs, prepare_benign, stage_decode_inputs
 
 
+def next_token_rows(tokens, start: int, end: int, prefill_len: int, sampled: int | None) -> list[int]:
+    """The MTP input of prefill rows ``start .. end-1``: the token at p + 1
+    for row p, and for the last row of the whole prefill (``end ==
+    prefill_len``) the token sampled there. The prefilled tokens are the
+    prompt, or after a recompute preemption prompt + output."""
+    nxt = list(tokens[start + 1:min(end + 1, prefill_len)])
+    if end >= prefill_len:
+        nxt.append(sampled)
+    return nxt
+
+
 def forced_accept_prob(mean_len: float, k: int) -> float:
     """Per-position acceptance probability p of a Bernoulli chain (stop at the
     first rejection, at most k accepted) whose mean accepted LENGTH
@@ -321,12 +332,7 @@ class MTPSpeculator:
             else:
                 tok = None
             if c.is_prefill:
-                # the prefilled tokens are the prompt, or after a preemption prompt + output
-                L = seq.prefill_target
-                nxt = seq.tokens[c.start + 1:min(end + 1, L)]
-                if end >= L:
-                    nxt = list(nxt) + [tok]
-                ids[r:r + n] = nxt
+                ids[r:r + n] = next_token_rows(seq.tokens, c.start, end, seq.prefill_target, tok)
                 if c.needs_logits:
                     finals.append((c, r + n - 1))
             r += n

@@ -95,3 +95,16 @@ def test_spec_stats_mean():
         s.record(a)
     assert s.num_draft_tokens == 18 and s.accepted_per_pos == [2, 2, 1, 1, 1, 1]
     assert abs(s.mean_accepted_length - (1 + 8 / 3)) < 1e-12
+
+
+def test_mtp_catch_up_rows_for_prompt_chunks_and_recompute_prefill():
+    from k8v4_xpu_b200.runtime.scheduler import TokenView
+    from k8v4_xpu_b200.spec.mtp import next_token_rows
+    prompt, output = [10, 11, 12, 13, 14], [20, 21, 22]
+    toks = TokenView(prompt, [])
+    assert next_token_rows(toks, 0, 3, 5, None) == [11, 12, 13]          # a middle chunk
+    assert next_token_rows(toks, 3, 5, 5, 99) == [14, 99]                # last chunk: the sampled token
+    # after a preemption the prefill covers prompt + output; the sampled token follows the last output
+    toks = TokenView(prompt, output)
+    assert next_token_rows(toks, 0, 6, 8, None) == [11, 12, 13, 14, 20, 21]
+    assert next_token_rows(toks, 6, 8, 8, 77) == [22, 77]
