@@ -54,3 +54,60 @@ def test_the_random_runs_reached_preemption():
     if len(preemptions) < 12:
         pytest.skip("run with the parametrised test")
     assert sum(1 for n in preemptions if n > 0) >= 3, preemptions
+
+
+@pytest.mark.parametrize("seed", range(8))
+def test_mtp_shaped_scheduling_keeps_invariants(seed):
+    """The scheduler as MTP6 drives it: decode rows of width 1 + drafts with a
+    KV lookahead, decode and prefill steps alternating; a fake verify accepts
+    a random number of drafts and emits them plus one token (rollback by
+    length, as the real commit does)."""
+    from k8v4_xpu_b200.runtime.block_manager import BlockManager
+    from k8v4_xpu_b200.runtime.scheduler import Scheduler
+    rng = random.Random(seed)
+    k, V = 6, 1000
+    bm = BlockManager(rng.choice([12, 20, 48]), block_size=16)
+    sch = Scheduler(bm, max_num_seqs=4, max_num_batched_tokens=rng.choice([32, 64]), decode_width=k + 1,
+                    max_model_len=200, lookahead=k, mix_prefill_with_decode=False)
+    seqs = []
+    for step in range(3000):
+        if step < 150 and rng.random() < 0.3:
+            prompt = [rng.randrange(V) for _ in range(rng.randrange(1, 60))]
+            seqs.append(sch.add(prompt, SamplingParams(max_tokens=rng.randrange(1, 80), ignore_eos=True)))
+        if not sch.has_work():
+            if step >= 150:
+                break
+            continue
+        out = sch.schedule()
+        for c in out.chunks:
+            seq = c.seq
+            if c.is_prefill:
+                seq.computed = c.start + c.num_tokens
+                bm.publish(seq.seq_id, seq.tokens, seq.computed)
+                if not c.needs_logits:
+                    continue
+                emitted = [(seq.tokens[-1] + 1) % V]
+            else:
+                assert c.num_tokens == 1 + len(seq.draft)
+                a = rng.randrange(0, len(seq.draft) + 1)
+                seq.computed = c.start + a + 1
+                emitted = []
+                for _ in range(a + 1):
+                    emitted.append(((emitted[-1] if emitted else seq.tokens[-1]) + 1) % V)
+            for t in emitted:
+                seq.output.append(t)
+                if len(seq.output) >= seq.params.max_tokens:
+                    sch.finish(seq, "length")
+                    break
+            if not seq.done:
+                seq.draft = [rng.randrange(V) for _ in range(k)]
+                bm.publish(seq.seq_id, seq.tokens, seq.computed)
+        bm.check_invariants()
+    assert not sch.has_work()
+    for seq in seqs:
+        if seq.finish_reason == "abort":
+            continue
+        assert len(seq.output) == seq.params.max_tokens
+        toks = seq.prompt + seq.output
+        assert all(toks[len(seq.prompt) + j] == (toks[len(seq.prompt) + j - 1] + 1) % V
+                   for j in range(len(seq.output)))
