@@ -4,7 +4,7 @@
 // Every wait here is bounded: it polls with a time limit and, when the limit
 // passes, records kErrMbarTimeout in the library status word and sets the
 // CTA's shared abort flag so the other roles of the CTA leave their loops.
-// No TMA load in this library uses .multicast::cluster.
+// No TMA or bulk load in this library fans out to a cluster: each CTA loads its own copy.
 #pragma once
 #include <cuda.h>
 #include "common.cuh"
