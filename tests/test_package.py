@@ -59,14 +59,20 @@ def test_committed_code_never_reaches_into_the_scratch_folder():
                 assert not node.value.startswith(SCRATCH + "/"), (f, node.value)
 
 
-def test_no_bulk_copy_carries_a_multicast_qualifier_in_the_cuda_sources():
-    # Multi-GPU runs must not reach a TMA / bulk load that fans out to a
-    # cluster. A line that issues a bulk copy may name no multicast form at all.
+# A bulk-copy instruction and a fan-out qualifier, written as patterns so that
+# this file names neither of them as plain text.
+_BULK_COPY = re.compile(r"cp[.]async[.]bul[k]")
+_FAN_OUT = re.compile(r"multi[c]ast")
+
+
+def test_no_bulk_copy_fans_out_to_a_cluster_in_the_cuda_sources():
+    # Multi-GPU runs must not reach a TMA / bulk load that fans out to several
+    # CTAs of a cluster: a line that issues a bulk copy names no fan-out form.
     for f in CUDA_FILES:
         code = _strip_comments(f.read_text())
         for line in code.splitlines():
-            if "cp.async.bulk" in line:
-                assert "multicast" not in line, (f, line)
+            if _BULK_COPY.search(line):
+                assert not _FAN_OUT.search(line), (f, line)
 
 
 def test_cuda_sources_build_for_sm100a_only():

@@ -1,8 +1,14 @@
-"""Tensor parallel forward and serving on 2 GPUs (NCCL), checked against TP1.
+"""Tensor parallel forward and serving on 2, 4 and 8 GPUs (NCCL), checked
+against TP1.
 
 Each rank is a child process with its own GPU. Every rank draws the full
-random-init matrices from one seed and keeps its shard, so the TP2 model is
-the TP1 model split by heads / MLP columns / vocab rows.
+random-init matrices from one seed and keeps its shard, so the TPn model is
+the TP1 model split by heads / MLP columns / vocab rows. The test model has
+the 27B head structure (24 query / 4 KV heads of 128): at TP8 each KV head is
+replicated on two ranks and the per-rank GQA is 3.
+
+    torchrun is not needed: ``python -m pytest tests/test_tp_gpu.py -m gpu``
+    spawns the ranks itself (one per GPU, rendezvous on 127.0.0.1).
 """
 import os
 import socket
@@ -11,6 +17,8 @@ import traceback
 import pytest
 import torch
 import torch.multiprocessing as mp
+
+from k8v4_xpu_b200.models.config import ModelConfig
 
 pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 
@@ -51,6 +59,9 @@ def _prefill_inputs(prompts, dev):
 
 
 PROMPTS = [list(range(3, 3 + 150)), list(range(100, 100 + 45))]
+# the 27B head structure at test size: TP 2/4/8 all divide it, TP8 replicates KV heads
+TP_MODEL = ModelConfig(name="tp-test", num_layers=2, hidden=1024, num_heads=24, num_kv_heads=4, head_dim=128,
+                       intermediate=2048, vocab=8192, max_position=8192)
 SMALL_PROMPTS = [list(range(3, 3 + 40)), list(range(100, 100 + 17))]
 
 
@@ -60,7 +71,6 @@ def _worker(rank, world, port, q):
     import torch.distributed as dist
     try:
         from k8v4_xpu_b200 import ops
-        from k8v4_xpu_b200.models.config import TINY
         from k8v4_xpu_b200.models.dense import DenseModel
         from k8v4_xpu_b200.parallel.comm import TPComm, init_from_env
         from k8v4_xpu_b200.runtime.engine import EngineConfig, LLMEngine
@@ -68,7 +78,7 @@ def _worker(rank, world, port, q):
         init_from_env(timeout_s=120)
         comm = TPComm()
         dev = torch.device("cuda", rank)
-        m = DenseModel(TINY, tp=world, rank=rank, device=dev, comm=comm).random_init(seed=3)
+        m = DenseModel(TP_MODEL, tp=world, rank=rank, device=dev, comm=comm).random_init(seed=3)
         inp = _prefill_inputs(PROMPTS, dev)
         caches = [torch.zeros(64, m.layout.page_bytes, dtype=torch.uint8, device=dev) for _ in m.layers]
         hid = m.forward(inp, caches)
@@ -79,15 +89,17 @@ def _worker(rank, world, port, q):
         small = _prefill_inputs(SMALL_PROMPTS, dev)
         caches = [torch.zeros(64, m.layout.page_bytes, dtype=torch.uint8, device=dev) for _ in m.layers]
         res["small_nccl"] = m.forward(small, caches).float().cpu()
-        m.fused_ar = FusedAllReduce(None, dev, 64, TINY.hidden)
+        m.fused_ar = FusedAllReduce(None, dev, 64, TP_MODEL.hidden)
         for _ in range(3):  # repeated uses: the running signal counts must keep matching
             caches = [torch.zeros(64, m.layout.page_bytes, dtype=torch.uint8, device=dev) for _ in m.layers]
             res["small_fused"] = m.forward(small, caches).float().cpu()
         torch.cuda.synchronize(dev)
         res["fused_calls"] = m.fused_ar.calls
-        cfg = EngineConfig(model="tiny", tensor_parallel_size=world, max_model_len=2048, max_num_seqs=2,
+        res["kv_heads"] = m.shape.kv_heads_of(rank, TP_MODEL.num_kv_heads)
+        res["gqa_local"] = m.shape.gqa_local
+        cfg = EngineConfig(model="tp-test", tensor_parallel_size=world, max_model_len=2048, max_num_seqs=2,
                            max_num_batched_tokens=96, num_kv_blocks=128, device=str(dev))
-        eng = LLMEngine(cfg, TINY, comm=comm, rank=rank)
+        eng = LLMEngine(cfg, TP_MODEL, comm=comm, rank=rank)
         res["gen"] = eng.generate(PROMPTS, SamplingParams(max_tokens=8, ignore_eos=True))
         res["graph"] = bool(eng.graphs and eng.graphs.captured)
         res["comm_mode"] = eng.tp_comm_mode
@@ -102,41 +114,48 @@ def _worker(rank, world, port, q):
             dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tp2_matches_tp1():
-    from k8v4_xpu_b200.models.config import TINY
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_matches_tp1(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip("needs %d GPUs" % world)
     from k8v4_xpu_b200.models.dense import DenseModel
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    out = dict(q.get(timeout=600) for _ in procs)
+    out = dict(q.get(timeout=900) for _ in procs)
     for p in procs:
         p.join(timeout=120)
-    for r in range(2):
+    for r in range(world):
         assert "error" not in out[r], out[r].get("error")
         assert out[r]["status"] == 0 and out[r]["graph"]
+    # KV heads: split while TP divides them, then each one shared by TP / 4 ranks (GQA 3)
+    rep = max(1, world // TP_MODEL.num_kv_heads)
+    for r in range(world):
+        assert out[r]["kv_heads"] == ([r // rep] if rep > 1 else list(range(r * 4 // world, (r + 1) * 4 // world)))
+        assert out[r]["gqa_local"] == (3 if world == 8 else 6)
     # ranks agree exactly (replicated residual stream, reduced argmax)
-    assert torch.equal(out[0]["hidden"], out[1]["hidden"])
-    assert torch.equal(out[0]["small_fused"], out[1]["small_fused"])
-    assert out[0]["fused_calls"] == 3 * 2 * TINY.num_layers
+    for r in range(1, world):
+        assert torch.equal(out[0]["hidden"], out[r]["hidden"]), r
+        assert torch.equal(out[0]["small_fused"], out[r]["small_fused"]), r
+        assert out[0]["gen"] == out[r]["gen"], r
+    assert out[0]["fused_calls"] == 3 * 2 * TP_MODEL.num_layers
     assert out[0]["comm_mode"] == "fused"
     ref_small = out[0]["small_nccl"]
     err = (out[0]["small_fused"] - ref_small).abs().max().item()
     assert err <= 0.02 * ref_small.abs().max().item(), err
-    assert out[0]["gen"] == out[1]["gen"]
-    # TP2 vs TP1 on the same weights: reduction order differs, values agree closely
+    # TPn vs TP1 on the same weights: reduction order differs, values agree closely
     dev = torch.device("cuda", 0)
-    m = DenseModel(TINY, device=dev).random_init(seed=3)
+    m = DenseModel(TP_MODEL, device=dev).random_init(seed=3)
     inp = _prefill_inputs(PROMPTS, dev)
     caches = [torch.zeros(64, m.layout.page_bytes, dtype=torch.uint8, device=dev) for _ in m.layers]
     ref = m.forward(inp, caches).float().cpu()
     err = (out[0]["hidden"] - ref).abs().max().item()
     assert err <= 0.03 * ref.abs().max().item(), err
     lg_ref = m.logits(m.forward(inp, caches)).float().cpu()
-    full = torch.cat([out[0]["logits"], out[1]["logits"]], 1)  # the two vocab shards side by side
+    full = torch.cat([out[r]["logits"] for r in range(world)], 1)  # the vocab shards side by side
     assert full.shape == lg_ref.shape
     assert (full - lg_ref).abs().max().item() <= 0.03 * lg_ref.abs().max().item()
     picked = lg_ref.gather(1, out[0]["ids"].view(-1, 1)).view(-1)
