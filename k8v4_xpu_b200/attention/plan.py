@@ -19,7 +19,7 @@ from __future__ import annotations
 
 from collections.abc import Sequence
 
-from ..kv.layout import PageLayout, b200_layout
+from ..kv.layout import B200_FORMAT, PageLayout, b200_layout
 
 DECODE_MAX_ROWS = 64  # query rows (tokens x GQA) one decode CTA holds
 
@@ -59,9 +59,8 @@ def decode_workspace_floats(nseq: int, hkv: int, nsplit: int, q_len: int, gqa: i
 
 
 def layout_for_heads(num_heads: int, num_kv_heads: int) -> PageLayout:
-    if num_kv_heads < 1 or num_heads % num_kv_heads:
-        raise ValueError("query heads (%d) must be a multiple of KV heads (%d)" % (num_heads, num_kv_heads))
-    return b200_layout(num_kv_heads, num_heads // num_kv_heads)
+    """The b200-format layout of a rank with these local heads."""
+    return PageLayout.for_rank(num_heads, num_kv_heads, B200_FORMAT)
 
 
 def require_decoder(head_size: int, num_heads: int, num_kv_heads: int, sliding_window: int | None = None,

@@ -24,6 +24,7 @@ Nothing here reads the environment; byte-level code carries an explicit
 from __future__ import annotations
 
 import dataclasses
+import functools
 
 CACHE_DTYPE = "int8_k_int4_v"
 HISTORIC_MTP_LEN = 59500
@@ -96,6 +97,35 @@ DECODE_MAX_T = PAGE // GQA  # 10
 
 
 @dataclasses.dataclass(frozen=True)
+class Region:
+    """One typed plane of a page, with the byte steps that address it.
+
+    Element ``(token, head, col)`` of page ``p`` sits at byte
+    ``p * page_bytes + offset + token * token_step + head * head_step + col * elem``.
+    ``cols`` is 1 for a per-(token, head) scalar such as ``k_scale``.
+    """
+
+    name: str
+    dtype: str
+    cols: int
+    offset: int
+    token_step: int
+    head_step: int
+
+    @property
+    def elem(self) -> int:
+        return _ELEM_BYTES[self.dtype]
+
+    @property
+    def row_bytes(self) -> int:
+        """Bytes of one (token, head) entry."""
+        return self.cols * self.elem
+
+
+_ELEM_BYTES = {"int8": 1, "uint8": 1, "float32": 4, "float16": 2}
+
+
+@dataclasses.dataclass(frozen=True)
 class PageLayout:
     """Per-rank head layout plus the page format it is stored in.
 
@@ -110,34 +140,21 @@ class PageLayout:
     fmt: KVFormat = REF_FORMAT
 
     def __post_init__(self) -> None:
-        if self.fmt.name == "ref":
-            if self.hkv not in (2, 4) or self.gqa != GQA:
-                raise ValueError(
-                    "unsupported per-GPU KV head count %r (ref K8/V4 serves 2 or 4, GQA 6)"
-                    % (self.hkv,)
-                )
-        else:
-            if self.hkv not in (1, 2, 4):
-                raise ValueError("unsupported per-GPU KV head count %r" % (self.hkv,))
-            if self.gqa not in (3, 6):
-                raise ValueError("unsupported per-rank GQA %r" % (self.gqa,))
+        allowed = ({2, 4}, {GQA}) if self.fmt.name == "ref" else ({1, 2, 4}, {3, 6})
+        if self.hkv not in allowed[0] or self.gqa not in allowed[1]:
+            raise ValueError(
+                "the %s page format stores %s KV heads per rank at GQA %s; asked for %r KV heads at GQA %r"
+                % (self.fmt.name, sorted(allowed[0]), sorted(allowed[1]), self.hkv, self.gqa))
 
     @classmethod
-    def for_heads(cls, num_heads: int, num_kv_heads: int, fmt: KVFormat | str = REF_FORMAT) -> "PageLayout":
-        """Layout for one rank's local heads; a mismatched pair fails loudly."""
-        if isinstance(fmt, str):
-            fmt = FORMATS[fmt]
-        num_heads = int(num_heads)
-        num_kv_heads = int(num_kv_heads)
-        if num_kv_heads < 1 or num_heads % num_kv_heads:
-            raise ValueError("%d Q heads do not group over %d KV heads" % (num_heads, num_kv_heads))
-        gqa = num_heads // num_kv_heads
-        if fmt.name == "ref" and (num_kv_heads not in (2, 4) or gqa != GQA):
-            raise ValueError(
-                "K8/V4 serves 12/2 (TP2) or 24/4 (single GPU) local heads, got %d Q / %d KV"
-                % (num_heads, num_kv_heads)
-            )
-        return cls(num_kv_heads, gqa, fmt)
+    def for_rank(cls, hq_local: int, hkv_local: int, fmt: KVFormat | str = REF_FORMAT) -> "PageLayout":
+        """Layout of a rank holding ``hq_local`` query and ``hkv_local`` KV
+        heads; the constructor refuses a pair its format does not store."""
+        fmt = FORMATS[fmt] if isinstance(fmt, str) else fmt
+        groups, rest = divmod(int(hq_local), max(1, int(hkv_local)))
+        if int(hkv_local) < 1 or rest:
+            raise ValueError("%d query heads do not share %d KV heads evenly" % (hq_local, hkv_local))
+        return cls(int(hkv_local), groups, fmt)
 
     # ------------------------------------------------------------------ sizes
     @property
@@ -198,6 +215,67 @@ class PageLayout:
     def bf16_bytes_per_token(self) -> int:
         return self.hkv * 4 * self.head_dim
 
+    # ---------------------------------------------------------------- regions
+    @functools.cached_property
+    def regions(self) -> tuple[Region, ...]:
+        """The page's planes in storage order.
+
+        The planes are K codes, V nibbles, K scales, V scales and (affine V
+        only) V zero points. Token-major pages stack each plane for all heads
+        (``[token][head][cols]``); head-major pages give every head one run
+        holding all of its planes (``[head][plane][token][cols]``).
+        """
+        f = self.fmt
+        sdt = f.scale_dtype
+        planes = [("k", "int8", f.head_dim), ("v", "uint8", f.v_cols), ("k_scale", sdt, 1), ("v_scale", sdt, f.v_groups)]
+        if f.has_v_zero:
+            planes.append(("v_zero", sdt, 1))
+        out, at = [], 0
+        for name, dt, cols in planes:
+            row = cols * _ELEM_BYTES[dt]
+            if f.order == "token_major":
+                out.append(Region(name, dt, cols, at, self.hkv * row, row))
+                at += self.page * self.hkv * row
+            else:  # offsets inside head 0's run; heads follow each other
+                out.append(Region(name, dt, cols, at, row, self.head_page_bytes))
+                at += self.page * row
+        return tuple(out)
+
+    def region(self, name: str) -> Region:
+        for r in self.regions:
+            if r.name == name:
+                return r
+        raise KeyError("no %r plane in the %s format" % (name, self.fmt.name))
+
+    def byte_of(self, name: str, page: int, token: int, head: int, col: int = 0) -> int:
+        """Address (from the start of page 0) of one element of a plane."""
+        r = self.region(name)
+        for what, i, n in (("token", token, self.page), ("head", head, self.hkv), ("col", col, r.cols)):
+            if not 0 <= int(i) < n:
+                raise IndexError("%s %d outside 0..%d" % (what, i, n - 1))
+        if int(page) < 0:
+            raise IndexError("page %d" % page)
+        return int(page) * self.page_bytes + r.offset + int(token) * r.token_step + int(head) * r.head_step + int(col) * r.elem
+
+    def extents(self, head: int | None = None) -> list[tuple[str, int, int]]:
+        """``(plane, start, length)`` byte runs inside one page: one per plane
+        for token-major pages, one per plane of ``head`` (every head when
+        ``None``) for head-major pages."""
+        if self.fmt.order == "token_major":
+            return [(r.name, r.offset, self.page * self.hkv * r.row_bytes) for r in self.regions]
+        heads = range(self.hkv) if head is None else [int(head)]
+        return [(r.name, r.offset + h * r.head_step, self.page * r.row_bytes) for h in heads for r in self.regions]
+
+    def regions_fill_page(self) -> bool:
+        """The planes' runs cover ``[0, page_bytes)`` exactly once."""
+        runs = sorted((start, length) for _n, start, length in self.extents())
+        at = 0
+        for start, length in runs:
+            if start != at:
+                return False
+            at += length
+        return at == self.page_bytes
+
 
 def b200_layout(hkv: int, gqa: int = 6) -> PageLayout:
     return PageLayout(hkv, gqa, B200_FORMAT)
@@ -228,215 +306,132 @@ def n_valid(seq_len: int, logical_page: int, page: int = PAGE) -> int:
     return max(0, min(page, int(seq_len) - int(logical_page) * page))
 
 
+@dataclasses.dataclass(frozen=True)
+class TableGeometry:
+    """What one block-table entry stands for in kernel pages.
+
+    The block manager hands out ``manager_block``-token blocks. A table given
+    to the kernels is either still in those blocks (``kernel_block=None``) or
+    re-expressed in ``kernel_block``-token entries; either way an entry covers
+    ``entry_tokens`` tokens = ``pages_per_entry`` consecutive pages, and entry
+    ``e`` names pages ``e * pages_per_entry ...`` (the pages ``slot // page``
+    writes).
+    """
+
+    manager_block: int
+    kernel_block: int | None = None
+    page: int = PAGE
+
+    def __post_init__(self) -> None:
+        for what, n in (("manager block", self.manager_block), ("kernel block", self.kernel_block)):
+            if n is not None and (int(n) < self.page or int(n) % self.page):
+                raise ValueError("%s of %s tokens is not a whole number of %d-token pages" % (what, n, self.page))
+
+    @property
+    def entry_tokens(self) -> int:
+        return int(self.manager_block if self.kernel_block is None else self.kernel_block)
+
+    @property
+    def pages_per_entry(self) -> int:
+        return self.entry_tokens // self.page
+
+    def pages(self, entries) -> list[int]:
+        """Kernel pages of a list of table entries, in order."""
+        n = self.pages_per_entry
+        return [int(e) * n + i for e in entries for i in range(n)]
+
+    def max_pages(self, max_model_len: int) -> int:
+        """Pages a table wide enough for ``max_model_len`` tokens addresses."""
+        entries = max(1, -(-int(max_model_len) // self.entry_tokens))
+        return entries * self.pages_per_entry
+
+
 def expand_block_ids(block_ids: list[int], ratio: int) -> list[int]:
     """Manager block id -> kernel pages (``block_id * ratio + sub``)."""
-    ratio = int(ratio)
-    if ratio < 1:
-        raise ValueError("pages_per_block must be >= 1")
-    out: list[int] = []
-    for block_id in block_ids:
-        base = int(block_id) * ratio
-        out.extend(base + sub for sub in range(ratio))
-    return out
-
-
-def visible_lens(seq_len: int, q_len: int, max_t: int = DECODE_MAX_T) -> list[int]:
-    """Per-query causal ends for one MTP step.
-
-    Index 0 is the longest end (the page-valid length); index ``1+j`` is the
-    end for query ``j``: ``seq_len - (q_len - 1 - j)``, clamped at 1. Lengths
-    are full integers; a length near 59.5K must not be narrowed to 16 bits.
-    Behaviour of ``k8v4_v030/layout.py:124-139``.
-    """
-    q_len = int(q_len)
-    seq_len = int(seq_len)
-    if q_len < 1 or q_len > max_t:
-        raise ValueError("q_len %d outside packed decode tile" % q_len)
-    rows = []
-    for j in range(q_len):
-        end = seq_len - (q_len - 1 - j)
-        rows.append(end if end >= 1 else 1)
-    return [max(rows)] + rows
-
-
-def builtin_q_end(seq_len: int, q_len: int, q_tok: int) -> int:
-    """Causal end of query ``q_tok`` of the last ``q_len`` tokens."""
-    return int(seq_len) - int(q_len) + int(q_tok) + 1
-
-
-def as_int16(value: int) -> int:
-    """The reference's historic ABI bug: a length narrowed to signed 16 bits."""
-    masked = int(value) & 0xFFFF
-    return masked - 0x10000 if masked >= 0x8000 else masked
-
-
-# -------------------------------------------------------------------- regions
-def page_regions(page_index: int, layout: PageLayout, head: int | None = None) -> dict[str, tuple[int, int]]:
-    """Byte offset and length of each region of one page.
-
-    Token-major pages have one region per kind for all heads. Head-major pages
-    have one run per head; pass ``head`` to get that head's regions (without it
-    the first head's run is described together with the page extent).
-    """
-    base = int(page_index) * layout.page_bytes
-    fmt = layout.fmt
-    if fmt.order == "token_major":
-        k0 = base
-        v0 = k0 + layout.k_bytes_per_page
-        s0 = v0 + layout.v_bytes_per_page
-        out = {
-            "k": (k0, layout.k_bytes_per_page),
-            "v": (v0, layout.v_bytes_per_page),
-            "k_scale": (s0, layout.scale_bytes_per_page),
-            "v_scale": (s0 + layout.scale_bytes_per_page, layout.v_scale_bytes_per_page),
-        }
-        if fmt.has_v_zero:
-            out["v_zero"] = (s0 + layout.scale_bytes_per_page + layout.v_scale_bytes_per_page,
-                             layout.scale_bytes_per_page)
-        return out
-    h = 0 if head is None else int(head)
-    if h < 0 or h >= layout.hkv:
-        raise IndexError(h)
-    hb = base + h * layout.head_page_bytes
-    kb = layout.page * fmt.head_dim
-    vb = layout.page * fmt.v_cols
-    sb = layout.page * fmt.scale_bytes
-    out = {
-        "k": (hb, kb),
-        "v": (hb + kb, vb),
-        "k_scale": (hb + kb + vb, sb),
-        "v_scale": (hb + kb + vb + sb, sb * fmt.v_groups),
-    }
-    if fmt.has_v_zero:
-        out["v_zero"] = (hb + kb + vb + sb * (1 + fmt.v_groups), sb)
-    return out
-
-
-def block_byte_span(block_id: int, block_size: int, layout: PageLayout) -> tuple[int, int]:
-    """Start and length of one manager block in the packed blob."""
-    ratio = pages_per_block(block_size, layout.page)
-    start = int(block_id) * ratio * layout.page_bytes
-    return start, ratio * layout.page_bytes
+    if int(ratio) < 1:
+        raise ValueError("a block spans at least one page, got %s" % ratio)
+    return TableGeometry(int(ratio), None, 1).pages(block_ids)
 
 
 def attention_pages_per_block(manager_block: int, kernel_block: int | None, page: int = PAGE) -> int:
-    """How many kernel pages one block-table entry stands for.
-
-    A ``page``-token kernel block is one page; a larger entry expands as
-    ``block_id * ratio + page_in_block`` (the page ``slot // page`` writes).
-    ``kernel_block is None`` means the table is still in manager blocks.
-    """
-    manager_block = int(manager_block)
-    if manager_block < page or manager_block % page != 0:
-        raise ValueError("manager block %s is not a multiple of %s" % (manager_block, page))
-    if kernel_block is None:
-        return manager_block // page
-    kernel_block = int(kernel_block)
-    if kernel_block == page:
-        return 1
-    if kernel_block < page or kernel_block % page != 0:
-        raise ValueError("kernel block %s is not a multiple of %s" % (kernel_block, page))
-    return kernel_block // page
-
-
-def table_block_size(manager_block: int, kernel_block: int | None) -> int:
-    """Token width of one block-table entry."""
-    if kernel_block is None:
-        return int(manager_block)
-    return int(kernel_block)
+    """How many kernel pages one block-table entry stands for."""
+    return TableGeometry(manager_block, kernel_block, page).pages_per_entry
 
 
 def max_kernel_pages(max_model_len: int, manager_block: int, kernel_block: int | None, page: int = PAGE) -> int:
     """Kernel pages addressable by a full-length block table."""
-    unit = table_block_size(manager_block, kernel_block)
-    ratio = attention_pages_per_block(manager_block, kernel_block, page)
-    width = (int(max_model_len) + unit - 1) // unit
-    if width < 1:
-        width = 1
-    return width * ratio
+    return TableGeometry(manager_block, kernel_block, page).max_pages(max_model_len)
 
 
-def region_view_specs(num_pages: int, layout: PageLayout) -> dict[str, dict[str, object]]:
-    """``as_strided`` specs for one contiguous run of pages.
+# ------------------------------------------------------- MTP causal query ends
+def builtin_q_end(seq_len: int, q_len: int, q_tok: int) -> int:
+    """Keys visible to query row ``q_tok`` of a ``q_len``-row step whose last
+    row is token ``seq_len - 1``: its own position plus one."""
+    return (int(seq_len) - int(q_len)) + int(q_tok) + 1
 
-    Strides are in elements of that region's dtype; ``byte_offset`` is from the
-    start of page 0. Shapes are ``(pages, page, hkv, cols)`` for K/V/v_scale
-    with more than one group and ``(pages, page, hkv)`` for per-row scales,
-    whichever the page order, so callers index ``[page, token, head]``.
+
+def visible_lens(seq_len: int, q_len: int, max_t: int = DECODE_MAX_T) -> list[int]:
+    """The packed decode kernel's length vector for one MTP step.
+
+    Entry 0 is the longest causal end (the page-valid length), then one end
+    per query row, each at least 1. Lengths stay full integers: a length near
+    59.5K must not be narrowed to 16 bits (``as_int16``).
     """
-    num_pages = int(num_pages)
-    if num_pages < 1:
-        raise ValueError("num_pages")
-    fmt = layout.fmt
-    sdt = fmt.scale_dtype
-    sb = fmt.scale_bytes
-    P, T, H, Dh, Vc, G = num_pages, layout.page, layout.hkv, fmt.head_dim, fmt.v_cols, fmt.v_groups
-    pb = layout.page_bytes
-    if pb % sb:
-        raise ValueError("page bytes not a multiple of the scale size")
-    specs: dict[str, dict[str, object]] = {}
-    if fmt.order == "token_major":
-        s0 = layout.k_bytes_per_page + layout.v_bytes_per_page
-        specs["k"] = {"dtype": "int8", "shape": (P, T, H, Dh), "stride": (pb, H * Dh, Dh, 1), "byte_offset": 0}
-        specs["v"] = {"dtype": "uint8", "shape": (P, T, H, Vc), "stride": (pb, H * Vc, Vc, 1),
-                      "byte_offset": layout.k_bytes_per_page}
-        specs["k_scale"] = {"dtype": sdt, "shape": (P, T, H), "stride": (pb // sb, H, 1), "byte_offset": s0}
-        if G == 1:
-            specs["v_scale"] = {"dtype": sdt, "shape": (P, T, H), "stride": (pb // sb, H, 1),
-                                "byte_offset": s0 + layout.scale_bytes_per_page}
-        else:
-            specs["v_scale"] = {"dtype": sdt, "shape": (P, T, H, G), "stride": (pb // sb, H * G, G, 1),
-                                "byte_offset": s0 + layout.scale_bytes_per_page}
-        if fmt.has_v_zero:
-            specs["v_zero"] = {"dtype": sdt, "shape": (P, T, H), "stride": (pb // sb, H, 1),
-                               "byte_offset": s0 + layout.scale_bytes_per_page + layout.v_scale_bytes_per_page}
-        return specs
-    hp = layout.head_page_bytes
-    kb, vb, ssb = T * Dh, T * Vc, T * sb
-    specs["k"] = {"dtype": "int8", "shape": (P, T, H, Dh), "stride": (pb, Dh, hp, 1), "byte_offset": 0}
-    specs["v"] = {"dtype": "uint8", "shape": (P, T, H, Vc), "stride": (pb, Vc, hp, 1), "byte_offset": kb}
-    specs["k_scale"] = {"dtype": sdt, "shape": (P, T, H), "stride": (pb // sb, 1, hp // sb),
-                        "byte_offset": kb + vb}
-    if G == 1:
-        specs["v_scale"] = {"dtype": sdt, "shape": (P, T, H), "stride": (pb // sb, 1, hp // sb),
-                            "byte_offset": kb + vb + ssb}
+    if not 1 <= int(q_len) <= int(max_t):
+        raise ValueError("a packed decode step holds 1..%d query rows, got %s" % (max_t, q_len))
+    ends = [max(1, builtin_q_end(seq_len, q_len, r)) for r in range(int(q_len))]
+    return [ends[-1]] + ends  # ends ascend, so the last row's is the longest
+
+
+def as_int16(value: int) -> int:
+    """``value`` as a two's-complement 16-bit integer: the historic ABI bug
+    that narrowed sequence lengths (lengths above 32,767 turn negative)."""
+    return ((int(value) + 0x8000) & 0xFFFF) - 0x8000
+
+
+# -------------------------------------------------------------------- regions
+def page_regions(page_index: int, layout: PageLayout, head: int | None = None) -> dict[str, tuple[int, int]]:
+    """``{plane: (byte offset, length)}`` of one page (absolute offsets).
+
+    Token-major pages have one run per plane for all heads; head-major pages
+    one run per plane and head, so ``head`` picks the head (default 0).
+    """
+    base = int(page_index) * layout.page_bytes
+    if layout.fmt.order == "head_major":
+        h = 0 if head is None else int(head)
+        if not 0 <= h < layout.hkv:
+            raise IndexError(h)
+        runs = layout.extents(h)
     else:
-        specs["v_scale"] = {"dtype": sdt, "shape": (P, T, H, G), "stride": (pb // sb, G, hp // sb, 1),
-                            "byte_offset": kb + vb + ssb}
-    if fmt.has_v_zero:
-        specs["v_zero"] = {"dtype": sdt, "shape": (P, T, H), "stride": (pb // sb, 1, hp // sb),
-                           "byte_offset": kb + vb + ssb * (1 + G)}
-    return specs
-
-
-_ELEM = {"int8": 1, "uint8": 1, "float32": 4, "float16": 2}
-
-
-def element_byte(spec: dict[str, object], index: tuple[int, ...]) -> int:
-    """Byte address of one element of a region spec."""
-    shape = spec["shape"]
-    stride = spec["stride"]
-    if len(index) != len(shape) or len(stride) != len(shape):
-        raise ValueError("index rank")
-    elem = _ELEM[str(spec["dtype"])]
-    off = int(spec["byte_offset"])
-    for i, size, step in zip(index, shape, stride):
-        i = int(i)
-        if i < 0 or i >= int(size):
-            raise IndexError(i)
-        off += i * int(step) * elem
-    return off
+        runs = layout.extents()
+    return {name: (base + start, length) for name, start, length in runs}
 
 
 def region_stays_inside_block(block_size: int, layout: PageLayout) -> bool:
-    """K, V and scales of every page sit inside that manager block."""
-    ratio = pages_per_block(block_size, layout.page)
-    start, length = block_byte_span(0, block_size, layout)
-    end = start + length
-    heads = range(layout.hkv) if layout.fmt.order == "head_major" else (None,)
-    for page in range(ratio):
-        for head in heads:
-            for off, nbytes in page_regions(page, layout, head).values():
-                if off < start or off + nbytes > end:
-                    return False
-    return True
+    """Every plane of every page of a ``block_size``-token manager block lies
+    inside that block's bytes: the block holds whole pages and each page's
+    planes tile the page."""
+    whole = int(block_size) >= layout.page and int(block_size) % layout.page == 0
+    return whole and layout.regions_fill_page()
+
+
+def region_view_specs(num_pages: int, layout: PageLayout) -> dict[str, dict[str, object]]:
+    """``as_strided`` arguments of each plane over ``num_pages`` pages.
+
+    Shapes are ``(pages, page, hkv[, cols])`` (the column axis only when a
+    plane holds more than one element per token and head), strides are in the
+    plane's own elements, ``byte_offset`` counts from page 0.
+    """
+    if int(num_pages) < 1:
+        raise ValueError("num_pages must be positive")
+    specs: dict[str, dict[str, object]] = {}
+    for r in layout.regions:
+        e = r.elem
+        if layout.page_bytes % e or r.token_step % e or r.head_step % e or r.offset % e:
+            raise ValueError("plane %s is not aligned to its %d-byte elements" % (r.name, e))
+        shape = (int(num_pages), layout.page, layout.hkv)
+        stride = (layout.page_bytes // e, r.token_step // e, r.head_step // e)
+        if r.cols > 1:
+            shape, stride = shape + (r.cols,), stride + (1,)
+        specs[r.name] = {"dtype": r.dtype, "shape": shape, "stride": stride, "byte_offset": r.offset}
+    return specs

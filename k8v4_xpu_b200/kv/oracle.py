@@ -28,123 +28,76 @@ kernel's Q-once quantization (``xe2_kv_ops.cpp:205-257``).
 from __future__ import annotations
 
 import math
-import random
 
 import torch
 
-from .layout import D, GQA, PageLayout, builtin_q_end, ref_layout
+from .layout import D, REF_FORMAT, PageLayout, builtin_q_end, ref_layout
 
 # ------------------------------------------------------------ scalar (lists)
+# Python-list entry points for the reference format. Each one converts to
+# tensors, runs the tensor oracle below and converts back, so there is one
+# implementation of every rule.
 
 
-def _rint(value: float) -> int:
-    """Round half to even, like ``rintf`` / ``__float2int_rn``."""
-    return int(round(value))
-
-
-def _f32(x: float) -> float:
-    return float(torch.tensor(x, dtype=torch.float32))
+def _row(values, what: str) -> torch.Tensor:
+    t = torch.tensor(values, dtype=torch.float32)
+    if t.shape != (D,):
+        raise ValueError("a reference-format %s row holds %d values, got shape %s" % (what, D, tuple(t.shape)))
+    return t
 
 
 def quant_k(row: list[float]) -> tuple[list[int], float]:
-    """Reference-format K row (fp32 scale)."""
-    if len(row) != D:
-        raise ValueError("K row must be %d" % D)
-    q, s = quant_k_t(torch.tensor(row, dtype=torch.float32), "float32")
-    return [int(v) for v in q.tolist()], float(s)
+    """Reference-format K row: int8 codes and the fp32 scale."""
+    q, s = quant_k_t(_row(row, "K"), "float32")
+    return q.tolist(), float(s)
 
 
 def dequant_k(packed: list[int], scale: float) -> list[float]:
-    return [q * scale for q in packed]
+    return dequant_k_t(torch.tensor(packed), torch.tensor(scale)).tolist()
 
 
 def quant_v(row: list[float]) -> tuple[list[int], float, float]:
-    """Reference-format V row: affine uint4, low nibble = even dim."""
-    if len(row) != D:
-        raise ValueError("V row must be %d" % D)
-    nib, s, z = quant_v_affine_t(torch.tensor(row, dtype=torch.float32))
-    packed = (nib[0::2] | (nib[1::2] << 4)).tolist()
-    return [int(b) for b in packed], float(s), float(z)
+    """Reference-format V row: packed affine uint4 bytes (low nibble = even
+    dim), scale and zero point."""
+    nib, s, z = quant_v_affine_t(_row(row, "V"))
+    return pack_nibbles(nib).tolist(), float(s), float(z)
 
 
 def dequant_v(packed: list[int], scale: float, zero: float) -> list[float]:
-    out: list[float] = []
-    for byte in packed:
-        out.append((float(byte & 0xF) - zero) * scale)
-        out.append((float(byte >> 4) - zero) * scale)
-    return out
-
-
-def _softmax(scores: list[float]) -> list[float]:
-    finite = [s for s in scores if s != float("-inf")]
-    if not finite:
-        return [0.0] * len(scores)
-    peak = max(finite)
-    exps = [0.0 if s == float("-inf") else math.exp(s - peak) for s in scores]
-    total = sum(exps)
-    if total == 0.0:
-        return [0.0] * len(scores)
-    inv = 1.0 / total
-    return [e * inv for e in exps]
+    nib = unpack_nibbles(torch.tensor(packed, dtype=torch.uint8))
+    return dequant_v_affine_t(nib, torch.tensor(scale), torch.tensor(zero)).tolist()
 
 
 def causal_gqa(query, key, value, seq_len: int, q_len: int):
     """Quantized causal GQA over Python lists, reference format.
 
-    ``query`` is ``[q_len][HQ][D]`` (the last ``q_len`` tokens), ``key`` and
-    ``value`` are ``[seq_len][HKV][D]`` floats quantized here with the store
-    rules. Behaviour of ``k8v4_v030/oracle.py:100-163``.
+    ``query`` is ``[q_len][HQ][D]`` (the last ``q_len`` tokens of the
+    sequence), ``key`` and ``value`` ``[>= seq_len][HKV][D]`` floats, which
+    go through the store rules first. Returns ``[q_len][HQ][D]``. The same
+    computation as ``attention_ref`` (behaviour of
+    ``k8v4_v030/oracle.py:100-163``).
     """
-    if len(query) != q_len:
-        raise ValueError("query width")
-    if len(key) < seq_len or len(value) < seq_len:
-        raise ValueError("cache shorter than seq_len")
-    if q_len == 0:
+    if int(q_len) == 0:
+        if len(query):
+            raise ValueError("q_len 0 with %d query rows" % len(query))
         return []
-    kv_heads = len(key[0]) if key else len(query[0]) // GQA
-    layout = PageLayout.for_heads(len(query[0]), kv_heads)
-    hkv, hq = layout.hkv, layout.hq
-    kq, vq = [], []
-    for t in range(seq_len):
-        k_heads, v_heads = [], []
-        for h in range(hkv):
-            k_heads.append(quant_k(key[t][h]))
-            vp, vs, vz = quant_v(value[t][h])
-            v_heads.append(dequant_v(vp, vs, vz))
-        kq.append(k_heads)
-        vq.append(v_heads)
-    out = []
-    inv_sqrt = 1.0 / math.sqrt(D)
-    for q_tok in range(q_len):
-        end = builtin_q_end(seq_len, q_len, q_tok)
-        heads = []
-        for h in range(hq):
-            kv_head = h // GQA
-            q_packed, q_scale = quant_k(query[q_tok][h])
-            scores = []
-            for t in range(seq_len):
-                if t >= end:
-                    scores.append(float("-inf"))
-                    continue
-                k_packed, k_scale = kq[t][kv_head]
-                dot = sum(a * b for a, b in zip(q_packed, k_packed))
-                scores.append(dot * q_scale * k_scale * inv_sqrt)
-            probs = _softmax(scores)
-            acc = [0.0] * D
-            for t, prob in enumerate(probs):
-                if prob == 0.0:
-                    continue
-                row = vq[t][kv_head]
-                for d in range(D):
-                    acc[d] += prob * row[d]
-            heads.append(acc)
-        out.append(heads)
-    return out
+    q = torch.tensor(query, dtype=torch.float32)
+    if q.dim() != 3 or q.shape[0] != q_len or q.shape[2] != D:
+        raise ValueError("query must be [%d][HQ][%d], got %s" % (q_len, D, tuple(q.shape)))
+    k = torch.tensor(key, dtype=torch.float32)
+    v = torch.tensor(value, dtype=torch.float32)
+    if k.shape[0] < seq_len or v.shape[0] < seq_len or k.shape[1:] != v.shape[1:]:
+        raise ValueError("key/value must hold at least %d tokens of the same heads" % seq_len)
+    layout = PageLayout.for_rank(q.shape[1], k.shape[1], REF_FORMAT)
+    kd, vd = quant_dequant_kv(k[:seq_len], v[:seq_len], layout)
+    ends = [builtin_q_end(seq_len, q_len, r) for r in range(q_len)]
+    return attention_ref(q, kd, vd, ends, layout.gqa).tolist()
 
 
 def deterministic_rows(n: int, heads: int, seed: int, dim: int = D):
-    rng = random.Random(seed)
-    return [[[rng.uniform(-1.0, 1.0) for _d in range(dim)] for _h in range(heads)] for _ in range(n)]
+    """``[n][heads][dim]`` floats, uniform in [-1, 1), reproducible from ``seed``."""
+    gen = torch.Generator().manual_seed(int(seed))
+    return (torch.rand(n, heads, dim, generator=gen, dtype=torch.float64) * 2.0 - 1.0).tolist()
 
 
 # ------------------------------------------------------------ torch (tensors)

@@ -11,7 +11,7 @@ import struct
 
 import torch
 
-from .layout import PageLayout, element_byte, kernel_page_and_offset, region_view_specs
+from .layout import PageLayout, kernel_page_and_offset
 from .oracle import (
     dequant_k_t,
     dequant_v_affine_t,
@@ -47,24 +47,23 @@ def write_token(blob: bytearray, slot: int, keys, values, layout: PageLayout) ->
     if len(blob) < (page + 1) * layout.page_bytes:
         raise ValueError("blob shorter than page %d" % page)
     fmt = layout.fmt
-    specs = region_view_specs(page + 1, layout)
     k = torch.tensor(keys, dtype=torch.float32)
     v = torch.tensor(values, dtype=torch.float32)
     kq, ks = quant_k_t(k, fmt.scale_dtype)
     for head in range(layout.hkv):
-        base = element_byte(specs["k"], (page, off, head, 0))
+        base = layout.byte_of("k", page, off, head)
         blob[base:base + fmt.head_dim] = kq[head].numpy().tobytes()
-        _put_scale(blob, element_byte(specs["k_scale"], (page, off, head)), float(ks[head]), fmt.scale_dtype)
+        _put_scale(blob, layout.byte_of("k_scale", page, off, head), float(ks[head]), fmt.scale_dtype)
         if fmt.v_mode == "affine_row":
             nib, vs, vz = quant_v_affine_t(v[head])
-            _put_scale(blob, element_byte(specs["v_scale"], (page, off, head)), float(vs), fmt.scale_dtype)
-            _put_scale(blob, element_byte(specs["v_zero"], (page, off, head)), float(vz), fmt.scale_dtype)
+            _put_scale(blob, layout.byte_of("v_scale", page, off, head), float(vs), fmt.scale_dtype)
+            _put_scale(blob, layout.byte_of("v_zero", page, off, head), float(vz), fmt.scale_dtype)
         else:
             nib, vs = quant_v_sym_t(v[head], fmt.v_group)
             for g in range(fmt.v_groups):
-                at = element_byte(specs["v_scale"], (page, off, head, g))
+                at = layout.byte_of("v_scale", page, off, head, g)
                 _put_scale(blob, at, float(vs[g]), fmt.scale_dtype)
-        vb = element_byte(specs["v"], (page, off, head, 0))
+        vb = layout.byte_of("v", page, off, head)
         blob[vb:vb + fmt.v_cols] = pack_nibbles(nib).numpy().tobytes()
 
 
@@ -74,21 +73,20 @@ def read_token(blob: bytearray, slot: int, layout: PageLayout):
     if page < 0:
         raise ValueError("negative slot")
     fmt = layout.fmt
-    specs = region_view_specs(page + 1, layout)
     keys, values = [], []
     for head in range(layout.hkv):
-        base = element_byte(specs["k"], (page, off, head, 0))
+        base = layout.byte_of("k", page, off, head)
         kq = torch.frombuffer(bytearray(blob[base:base + fmt.head_dim]), dtype=torch.int8)
-        ks = _get_scale(blob, element_byte(specs["k_scale"], (page, off, head)), fmt.scale_dtype)
+        ks = _get_scale(blob, layout.byte_of("k_scale", page, off, head), fmt.scale_dtype)
         keys.append((kq.float() * ks).tolist())
-        vb = element_byte(specs["v"], (page, off, head, 0))
+        vb = layout.byte_of("v", page, off, head)
         nib = unpack_nibbles(torch.frombuffer(bytearray(blob[vb:vb + fmt.v_cols]), dtype=torch.uint8))
         if fmt.v_mode == "affine_row":
-            vs = _get_scale(blob, element_byte(specs["v_scale"], (page, off, head)), fmt.scale_dtype)
-            vz = _get_scale(blob, element_byte(specs["v_zero"], (page, off, head)), fmt.scale_dtype)
+            vs = _get_scale(blob, layout.byte_of("v_scale", page, off, head), fmt.scale_dtype)
+            vz = _get_scale(blob, layout.byte_of("v_zero", page, off, head), fmt.scale_dtype)
             values.append(((nib.float() - vz) * vs).tolist())
         else:
-            scales = torch.tensor([_get_scale(blob, element_byte(specs["v_scale"], (page, off, head, g)),
+            scales = torch.tensor([_get_scale(blob, layout.byte_of("v_scale", page, off, head, g),
                                               fmt.scale_dtype) for g in range(fmt.v_groups)])
             values.append(dequant_v_sym_t(nib, scales, fmt.v_group).tolist())
     return keys, values

@@ -1,79 +1,92 @@
-"""Typed region views over a K8/V4 byte cache, without copies.
+"""Typed plane views over a K8/V4 byte cache, without copies.
 
-The cache of one layer is a byte tensor whose address order is the page
-order. It can arrive as ``[num_pages, page_bytes]`` (this framework's own
+A layer's cache is a byte tensor whose address order is the page order. It
+arrives either as ``[num_pages, page_bytes]`` (this framework's own
 allocation) or as a vLLM-style logical ``[block, head, token, cell]`` tensor
-whose memory order differs from its logical order. Either way the bytes must
-form one dense span; a gapped, overlapping or negatively strided tensor is
-refused (behaviour of ``k8v4_v030/cache_views.py:28-109``).
+whose memory order differs from its logical order. The views are built from
+the layout's own plane table (``PageLayout.regions``) over the tensor's bytes
+in address order, so they work for both. Capability of the reference's
+``k8v4_v030/cache_views.py:28-109``: only a tensor whose bytes form one dense,
+forward run is accepted, and a head count other than the layout's is refused.
 """
 from __future__ import annotations
 
 import torch
 
-from .layout import PageLayout, region_view_specs
+from .layout import PageLayout
 
-_BYTE = (torch.uint8, torch.int8)
-_DT = {"int8": torch.int8, "uint8": torch.uint8, "float32": torch.float32, "float16": torch.float16}
-
-
-def _dense_reason(kv_cache: torch.Tensor) -> str:
-    return "K8/V4 layer cache is not a dense byte span (shape=%s stride=%s)" % (
-        tuple(kv_cache.shape), tuple(kv_cache.stride()))
+_TORCH_DTYPE = {"int8": torch.int8, "uint8": torch.uint8, "float32": torch.float32, "float16": torch.float16}
+# Plane views start on a 16-byte boundary: the widest element and every TMA
+# or bulk copy of a page need no more.
+_BASE_ALIGN = 16
 
 
-def memory_order_bytes(kv_cache: torch.Tensor) -> torch.Tensor:
-    """One uint8 vector of ``kv_cache`` in address order (no copy)."""
-    if kv_cache.dtype not in _BYTE:
-        raise RuntimeError("K8/V4 cache dtype %s is not a byte tensor" % kv_cache.dtype)
-    if kv_cache.numel() == 0:
-        raise RuntimeError("K8/V4 cache tensor is empty")
-    dims = [(int(n), int(s)) for n, s in zip(kv_cache.shape, kv_cache.stride()) if int(n) != 1]
-    for _n, s in dims:
-        if s <= 0:
-            raise RuntimeError(_dense_reason(kv_cache))
-    covered = 1
-    for n, s in sorted(dims, key=lambda item: item[1]):
-        if s != covered:
-            raise RuntimeError(_dense_reason(kv_cache))
-        covered *= n
-    if covered != int(kv_cache.numel()):
-        raise RuntimeError(_dense_reason(kv_cache))
-    base = int(kv_cache.storage_offset())
-    if base % 16 != 0:
-        raise RuntimeError("K8/V4 cache storage is not 16-byte aligned")
-    flat = torch.as_strided(kv_cache, size=(int(kv_cache.numel()),), stride=(1,), storage_offset=base)
-    return flat if flat.dtype == torch.uint8 else flat.view(torch.uint8)
+def span_problem(t: torch.Tensor) -> str | None:
+    """Why ``t``'s bytes are not one dense, forward, non-overlapping run, or
+    ``None`` when they are.
+
+    Taking the dimensions longer than 1 from the fastest stride to the
+    slowest, each stride must equal the number of bytes the faster ones
+    span. That one rule refuses gaps, overlaps (stride 0 or a repeated
+    stride) and negative strides alike.
+    """
+    if t.dtype not in (torch.uint8, torch.int8):
+        return "a K8/V4 cache is a byte tensor, got %s" % t.dtype
+    if t.numel() == 0:
+        return "the K8/V4 cache tensor holds no bytes"
+    spanned = 1
+    for size, stride in sorted(((n, s) for n, s in zip(t.shape, t.stride()) if n > 1), key=lambda d: d[1]):
+        if stride != spanned:
+            return ("the K8/V4 cache bytes are not one dense run: a dimension of %d has stride %d where %d "
+                    "would continue the run (shape %s, strides %s)"
+                    % (size, stride, spanned, tuple(t.shape), tuple(t.stride())))
+        spanned *= size
+    if t.storage_offset() % _BASE_ALIGN:
+        return "the K8/V4 cache starts %d bytes into its storage, not on a %d-byte boundary" % (
+            t.storage_offset(), _BASE_ALIGN)
+    return None
+
+
+def byte_run(t: torch.Tensor) -> torch.Tensor:
+    """``t``'s bytes as one uint8 vector in address order (shares storage)."""
+    why = span_problem(t)
+    if why:
+        raise RuntimeError(why)
+    run = t.as_strided((t.numel(),), (1,), t.storage_offset())
+    return run.view(torch.uint8)
+
+
+def _head_axis_problem(t: torch.Tensor, layout: PageLayout) -> str | None:
+    """A vLLM-style ``[block, head, token, cell]`` tensor names its head count
+    on axis 1: it must be the layout's, whatever the memory order."""
+    if t.dim() == 4 and t.shape[-1] == layout.fmt.slot_bytes_per_head and t.shape[1] != layout.hkv:
+        return "the cache tensor holds %d KV heads per block but this rank's layout stores %d" % (
+            t.shape[1], layout.hkv)
+    return None
 
 
 def bind_regions(kv_cache: torch.Tensor, layout: PageLayout) -> dict[str, torch.Tensor]:
-    """Region views (``k``, ``v``, ``k_scale``, ``v_scale`` [, ``v_zero``]) sharing storage."""
-    if kv_cache.dim() == 4 and kv_cache.shape[1] > 1 and kv_cache.shape[1] != layout.hkv:
-        raise RuntimeError("K8/V4 cache has %d KV heads, layout serves %d"
-                           % (int(kv_cache.shape[1]), layout.hkv))
-    raw = memory_order_bytes(kv_cache)
-    if raw.numel() % layout.page_bytes != 0:
-        raise RuntimeError("K8/V4 cache has %d bytes, not a multiple of the %d-byte page"
-                           % (raw.numel(), layout.page_bytes))
-    num_pages = raw.numel() // layout.page_bytes
-    specs = region_view_specs(num_pages, layout)
-    base = int(raw.storage_offset())
+    """One view per plane (``k``, ``v``, ``k_scale``, ``v_scale`` [, ``v_zero``]),
+    indexed ``[page, token, head(, col)]`` and sharing the cache's storage."""
+    why = _head_axis_problem(kv_cache, layout)
+    if why:
+        raise RuntimeError(why)
+    run = byte_run(kv_cache)
+    pages, rest = divmod(run.numel(), layout.page_bytes)
+    if rest:
+        raise RuntimeError("%d cache bytes are not a whole number of %d-byte pages" % (run.numel(), layout.page_bytes))
     views: dict[str, torch.Tensor] = {}
-    for name, spec in specs.items():
-        dt = _DT[str(spec["dtype"])]
-        storage = raw.view(dt)
-        esz = storage.element_size()
-        off = base + int(spec["byte_offset"])
-        if off % esz:
-            raise RuntimeError("region %s misaligned for %s" % (name, dt))
-        views[name] = torch.as_strided(storage, size=spec["shape"], stride=spec["stride"],
-                                       storage_offset=off // esz)
+    for r in layout.regions:
+        typed = run.view(_TORCH_DTYPE[r.dtype])
+        e = r.elem
+        size = (pages, layout.page, layout.hkv) + ((r.cols,) if r.cols > 1 else ())
+        stride = (layout.page_bytes // e, r.token_step // e, r.head_step // e) + ((1,) if r.cols > 1 else ())
+        views[r.name] = typed.as_strided(size, stride, (run.storage_offset() + r.offset) // e)
     return views
 
 
 def allocate_cache(num_pages: int, layout: PageLayout, device="cpu", zero: bool = True) -> torch.Tensor:
     """A ``[num_pages, page_bytes]`` uint8 cache for one layer."""
     shape = (int(num_pages), layout.page_bytes)
-    if zero:
-        return torch.zeros(shape, dtype=torch.uint8, device=device)
-    return torch.empty(shape, dtype=torch.uint8, device=device)
+    make = torch.zeros if zero else torch.empty
+    return make(shape, dtype=torch.uint8, device=device)

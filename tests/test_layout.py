@@ -30,10 +30,13 @@ def test_reference_format_rejects_other_heads():
         with pytest.raises(ValueError):
             L.ref_layout(bad)
     with pytest.raises(ValueError):
-        L.PageLayout.for_heads(12, 4)
+        L.PageLayout.for_rank(12, 4)  # GQA 3 is not a reference deployment
     with pytest.raises(ValueError):
-        L.PageLayout.for_heads(24, 2)
-    assert L.PageLayout.for_heads(12, 2).hkv == 2
+        L.PageLayout.for_rank(24, 2)  # GQA 12
+    with pytest.raises(ValueError):
+        L.PageLayout.for_rank(13, 2)  # heads do not group
+    assert L.PageLayout.for_rank(12, 2).hkv == 2
+    assert L.PageLayout.for_rank(12, 4, "b200").gqa == 3
 
 
 def test_b200_format_geometry():
@@ -61,19 +64,23 @@ def test_b200_format_geometry():
 def test_region_specs_address_every_byte_once(lay):
     pages = 3
     specs = L.region_view_specs(pages, lay)
+    assert lay.regions_fill_page()
     seen = set()
     import itertools
     for name, spec in specs.items():
-        ranges = [range(n) for n in spec["shape"]]
         elem = {"int8": 1, "uint8": 1, "float32": 4, "float16": 2}[spec["dtype"]]
-        for idx in itertools.product(*ranges):
-            b = L.element_byte(spec, idx)
+        for idx in itertools.product(*[range(n) for n in spec["shape"]]):
+            b = lay.byte_of(name, *idx)
+            # the as_strided spec and the plane table address the same byte
+            assert b == spec["byte_offset"] + elem * sum(i * s for i, s in zip(idx, spec["stride"]))
             for k in range(elem):
                 assert b + k not in seen, (name, idx)
                 seen.add(b + k)
     assert seen == set(range(pages * lay.page_bytes))
     with pytest.raises(IndexError):
-        L.element_byte(specs["k"], (pages, 0, 0, 0))
+        lay.byte_of("k", 0, lay.page, 0)
+    with pytest.raises(IndexError):
+        lay.byte_of("k", 0, 0, lay.hkv)
 
 
 def test_slot_addressing_and_block_expansion():
@@ -89,6 +96,11 @@ def test_slot_addressing_and_block_expansion():
     assert L.attention_pages_per_block(2112, 64) == 1
     assert L.attention_pages_per_block(2112, 128) == 2
     assert L.max_kernel_pages(262144, 2112, None) == ((262144 + 2111) // 2112) * 33
+    assert L.max_kernel_pages(262144, 2112, 128) == 262144 // 64
+    geo = L.TableGeometry(2112, 128)
+    assert geo.entry_tokens == 128 and geo.pages([5, 0]) == [10, 11, 0, 1]
+    with pytest.raises(ValueError):
+        L.TableGeometry(2112, 100)
     for lay in (REF2, L.b200_layout(2)):
         assert L.region_stays_inside_block(lay.page * 4, lay)
 
@@ -99,6 +111,7 @@ def test_visible_lens_and_int16_wrap():
     assert vis[0] == n and vis[1:] == [n - 6 + j for j in range(7)]
     assert all(v > 32767 for v in vis)
     assert L.as_int16(n) != n and L.as_int16(n) < 0  # the historic narrowing would corrupt it
+    assert [L.as_int16(x) for x in (0, 32767, 32768, 65535, 65536, -1)] == [0, 32767, -32768, -1, 0, -1]
     assert L.visible_lens(3, 7)[1:5] == [1, 1, 1, 1]
     with pytest.raises(ValueError):
         L.visible_lens(100, 11)

@@ -7,7 +7,7 @@ import torch
 from k8v4_xpu_b200.kv import layout as L
 from k8v4_xpu_b200.kv import oracle as O
 from k8v4_xpu_b200.kv.pack import gather_sequence, read_token, store_tokens, write_token
-from k8v4_xpu_b200.kv.views import allocate_cache, bind_regions, memory_order_bytes
+from k8v4_xpu_b200.kv.views import allocate_cache, bind_regions, byte_run, span_problem
 
 
 @pytest.mark.parametrize("lay", [L.ref_layout(2), L.ref_layout(4), L.b200_layout(4), L.b200_layout(1, 3)])
@@ -93,7 +93,7 @@ def test_views_refuse_bad_layouts():
     views = bind_regions(cache, lay)
     assert views["k"].shape == (3, 64, 2, 256) and views["k_scale"].dtype == torch.float32
     views["k_scale"][1, 5, 1] = 3.25
-    off = L.element_byte(L.region_view_specs(3, lay)["k_scale"], (1, 5, 1))
+    off = lay.byte_of("k_scale", 1, 5, 1)
     assert struct.unpack("<f", cache.flatten()[off:off + 4].numpy().tobytes())[0] == 3.25
     # vLLM-style logical [block, head, token, cell] with memory order [block, token, head, cell]
     blocks = torch.zeros(2, 64, 2, 396, dtype=torch.uint8).permute(0, 2, 1, 3)
@@ -101,10 +101,15 @@ def test_views_refuse_bad_layouts():
     with pytest.raises(RuntimeError):
         bind_regions(torch.zeros(2, 4, 64, 396, dtype=torch.uint8), lay)  # 4 heads, layout serves 2
     with pytest.raises(RuntimeError):
-        memory_order_bytes(torch.zeros(4, 8, dtype=torch.uint8)[:, ::2])  # gapped
+        byte_run(torch.zeros(4, 8, dtype=torch.uint8)[:, ::2])  # gapped
     with pytest.raises(RuntimeError):
-        memory_order_bytes(torch.zeros(1, 8, dtype=torch.uint8).expand(4, 8))  # overlapping (stride 0)
+        byte_run(torch.zeros(1, 8, dtype=torch.uint8).expand(4, 8))  # overlapping (stride 0)
     with pytest.raises(RuntimeError):
-        memory_order_bytes(torch.zeros(4, 8, dtype=torch.float32))  # not bytes
+        byte_run(torch.zeros(4, 8, dtype=torch.float32))  # not bytes
     with pytest.raises(RuntimeError):
         bind_regions(torch.zeros(lay.page_bytes + 16, dtype=torch.uint8), lay)  # not whole pages
+    with pytest.raises(RuntimeError):
+        byte_run(torch.zeros(16, dtype=torch.uint8).as_strided((4, 4), (2, 1)))  # rows overlap
+    with pytest.raises(RuntimeError):
+        byte_run(torch.zeros(64, dtype=torch.uint8)[1:])  # not 16-byte aligned
+    assert span_problem(torch.zeros(2, 3, 16, dtype=torch.uint8).permute(2, 0, 1)) is None  # dense, any order
