@@ -1,5 +1,6 @@
 // Shared device helpers for the k8v4 sm_100a kernel library.
 #pragma once
+#include <atomic>
 #include <cstdint>
 #include <cstdlib>
 #include <utility>
@@ -53,6 +54,22 @@ static __device__ int g_k8v4_site;
     }                                                                      \
     return v ? (v | (site << 8)) : 0;                                      \
   }
+
+// Raises Kernel's dynamic shared-memory limit to `bytes` on the current
+// device. The attribute belongs to the device, so it is set once per
+// (kernel, device): a process that drives several GPUs sets it on each.
+template <auto Kernel>
+inline cudaError_t ensure_smem_limit(int bytes) {
+  static std::atomic<unsigned long long> done{0};  // bit d: set on device d
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = dev < 64 ? 1ull << dev : 0ull;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  e = cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_release);
+  return e;
+}
 
 __device__ __forceinline__ void record_error(int code, int site = 0) {
   if (atomicCAS(&g_k8v4_status, 0, code) == 0) g_k8v4_site = site;

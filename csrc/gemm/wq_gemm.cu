@@ -590,11 +590,8 @@ static int launch_cfg(const void* w, const void* x, const Params& p, int split, 
     ts = tx;  // unused
   }
   auto kern = wq_gemm_kernel<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BSTAGES>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
-    attr_set = true;
-  }
+  if (ensure_smem_limit<wq_gemm_kernel<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BSTAGES>>(C::SMEM_BYTES) != cudaSuccess)
+    return 300;
   dim3 grid(cdiv(p.N, 128), cdiv(p.M, BT), split);
   return launch_k(kern, grid, dim3(C::NTHREADS), C::SMEM_BYTES, st, tw, tx, ts, p) == cudaSuccess ? 0 : 300;
 }

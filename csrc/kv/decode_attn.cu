@@ -24,6 +24,7 @@
 // = V converters.
 #include "attn_common.cuh"
 #include "../comm/peer.cuh"
+#include "../k8v4_c_api.h"
 
 namespace k8v4 {
 namespace attn {
@@ -775,11 +776,7 @@ extern "C" int k8v4_attn_trace(uint64_t* host) {
 template <int NPAD>
 static int launch_decode(const KVTileMaps& tm, const DecodeParams& p, int heads, int nseq, cudaStream_t st) {
   using C = DCfg<NPAD>;
-  static bool set = false;
-  if (!set) {
-    cudaFuncSetAttribute(decode_attn_kernel<NPAD>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
-    set = true;
-  }
+  if (ensure_smem_limit<decode_attn_kernel<NPAD>>(C::SMEM_BYTES) != cudaSuccess) return 10;
   dim3 grid(p.nsplit, heads, nseq);
   return launch_k(decode_attn_kernel<NPAD>, grid, dim3(C::NTHREADS), C::SMEM_BYTES, st, tm, p) == cudaSuccess ? 0 : 10;
 }

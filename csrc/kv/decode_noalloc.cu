@@ -1,7 +1,7 @@
 // Split-K decode attention without any allocation by the library.
 //
-// Declaration: this entry point has no counterpart in the reference; it is an
-// addition of this library.
+// Declared in ../k8v4_c_api.h. This entry point has no counterpart in the
+// reference; it is an addition of this library.
 //
 // Who needs it: callers that cannot allocate device memory at the point where
 // they run attention -- code running inside a host thread that must not call
@@ -28,9 +28,11 @@
 //     race on the array and corrupt each other's output; serialize them.
 //   * The call allocates nothing: no cudaMalloc, cudaFree or allocating
 //     library routine.
+#include <atomic>
 #include <cstdio>
 
 #include "../common.cuh"
+#include "../k8v4_c_api.h"
 
 #ifndef K8V4_NOALLOC_SCRATCH_FLOATS
 #define K8V4_NOALLOC_SCRATCH_FLOATS (1 << 20)
@@ -38,15 +40,12 @@
 
 static __device__ __align__(256) float g_decode_noalloc_scratch[K8V4_NOALLOC_SCRATCH_FLOATS];
 
-extern "C" int k8v4_decode_attn(const void* q, const int32_t* cu_q, const int32_t* seq_lens, const int32_t* q_ends,
-                                const int32_t* block_table, int bt_stride, const void* cache, int64_t num_pages,
-                                int hkv, int head_offset, int heads, int gqa, int hq_total, int nseq, int max_q_len,
-                                int nsplit, float sm_scale, void* out, float* ws_o, float* ws_ml, cudaStream_t st);
-extern "C" int64_t k8v4_decode_ws_floats(int nseq, int heads, int nsplit, int max_q_len, int gqa);
-
 namespace {
 constexpr int kMaxDevices = 64;
-float* g_scratch_addr[kMaxDevices] = {nullptr};
+// Device address of the array on each device. Two host threads making their
+// first call on one device at the same time both look it up and store the
+// same value; the atomics make that well defined.
+std::atomic<float*> g_scratch_addr[kMaxDevices];
 
 // Device address of the scratch array on the current device (looked up once).
 float* scratch_for_current_device(int* err) {
@@ -55,7 +54,8 @@ float* scratch_for_current_device(int* err) {
     *err = 21;
     return nullptr;
   }
-  if (!g_scratch_addr[dev]) {
+  float* known = g_scratch_addr[dev].load(std::memory_order_acquire);
+  if (!known) {
     void* p = nullptr;
     const cudaError_t rc = cudaGetSymbolAddress(&p, g_decode_noalloc_scratch);
     if (rc != cudaSuccess || p == nullptr) {
@@ -64,14 +64,15 @@ float* scratch_for_current_device(int* err) {
       *err = 22;
       return nullptr;
     }
-    g_scratch_addr[dev] = static_cast<float*>(p);
+    known = static_cast<float*>(p);
+    g_scratch_addr[dev].store(known, std::memory_order_release);
   }
-  return g_scratch_addr[dev];
+  return known;
 }
 }  // namespace
 
 // Capacity of the built-in scratch, in floats.
-extern "C" int64_t k8v4_decode_attn_noalloc_max_floats() { return K8V4_NOALLOC_SCRATCH_FLOATS; }
+extern "C" int64_t k8v4_decode_attn_noalloc_max_floats(void) { return K8V4_NOALLOC_SCRATCH_FLOATS; }
 
 // Same arguments and results as k8v4_decode_attn, minus the two workspace
 // pointers. Returns 0 on success, 20 when the launch needs more scratch than

@@ -556,11 +556,7 @@ extern "C" int k8v4_prefill_attn_multi(const void* q, const int32_t* cu_q, const
   p.head_offset = head_offset;
   p.n_qtiles = cdiv(max_q_len, 128 / gqa);
   p.sm_scale_log2 = sm_scale * LOG2E;
-  static bool set = false;
-  if (!set) {
-    cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PCfg::SMEM_BYTES);
-    set = true;
-  }
+  if (ensure_smem_limit<prefill_attn_kernel>(PCfg::SMEM_BYTES) != cudaSuccess) return 10;
   if (launch_k(prefill_stage_kernel, dim3(p.stage_tiles, heads, nseq), dim3(256), 0, st, p) != cudaSuccess) return 10;
   dim3 grid(p.n_qtiles, heads, nseq);
   return launch_k(prefill_attn_kernel, grid, dim3(PCfg::NTHREADS), PCfg::SMEM_BYTES, st, maps, p) == cudaSuccess ? 0

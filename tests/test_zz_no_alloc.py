@@ -4,8 +4,11 @@
 memory when they run attention (threads that must not call cudaMalloc,
 embedders whose memory belongs to another allocator, hosts that forbid
 allocations after start-up): its split-K scratch is a fixed array inside the
-library. This test calls it through ctypes, exactly as such a caller would,
-and checks two consecutive calls against the allocating entry point.
+library (declared in ``csrc/k8v4_c_api.h``). This test calls it through its
+exported C symbol with ctypes, exactly as such a caller would, and checks two
+consecutive calls: bit for bit against the allocating entry point (the same
+kernels on the same data), and against the fp32 torch attention reference of
+the dequantized cache within the tolerance of the other decode tests.
 
 The file name sorts last so that a run stopping at the first failure has run
 every other test before this one.
@@ -18,7 +21,8 @@ import torch
 
 from k8v4_xpu_b200 import ops
 from k8v4_xpu_b200.kv.layout import b200_layout
-from k8v4_xpu_b200.kv.pack import store_tokens
+from k8v4_xpu_b200.kv.oracle import attention_ref
+from k8v4_xpu_b200.kv.pack import gather_sequence, store_tokens
 
 pytestmark = pytest.mark.gpu
 
@@ -37,6 +41,8 @@ def _lib():
 
 
 def _case(seed, hkv=4, gqa=6, lens=(700, 1500, 33), q_len=1):
+    """Device inputs ``(q, cu, lens, bt, cache, hkv, gqa, q_len)`` of a paged
+    decode step and the fp32 reference output on the CPU."""
     g = torch.Generator().manual_seed(seed)
     layout = b200_layout(hkv, gqa)
     pages = [(n + 15) // 16 for n in lens]
@@ -55,9 +61,16 @@ def _case(seed, hkv=4, gqa=6, lens=(700, 1500, 33), q_len=1):
         store_tokens(cache, slots, k, v, layout)
     q = torch.randn(len(lens) * q_len, hkv * gqa, 128, generator=g).bfloat16()
     cu = torch.arange(0, len(lens) * q_len + 1, q_len, dtype=torch.int32)
+    # fp32 reference of what the kernels compute: attention over the dequantized cache
+    refs = []
+    for i, n in enumerate(lens):
+        kd, vd = gather_sequence(cache, bt[i, :pages[i]].tolist(), n, layout)
+        ends = [n - q_len + 1 + t for t in range(q_len)]
+        refs.append(attention_ref(q[i * q_len:(i + 1) * q_len].float(), kd, vd, ends, gqa))
     dev = "cuda"
-    return (q.to(dev), cu.to(dev), torch.tensor(lens, dtype=torch.int32, device=dev), bt.to(dev), cache.to(dev),
+    args = (q.to(dev), cu.to(dev), torch.tensor(lens, dtype=torch.int32, device=dev), bt.to(dev), cache.to(dev),
             hkv, gqa, q_len)
+    return args, torch.cat(refs, 0)
 
 
 def _call_noalloc(lib, q, cu, lens, bt, cache, hkv, gqa, q_len, nsplit, out):
@@ -69,26 +82,27 @@ def _call_noalloc(lib, q, cu, lens, bt, cache, hkv, gqa, q_len, nsplit, out):
     return rc
 
 
+@pytest.mark.parametrize("nsplit", [1, 5])
 @pytest.mark.parametrize("q_len", [1, 7])
-def test_noalloc_matches_allocating_entry_point_twice(q_len):
+def test_noalloc_matches_allocating_entry_point_twice(q_len, nsplit):
     lib = _lib()
-    nsplit = 5
     for seed in (101, 202):  # two calls in a row on different data
-        q, cu, lens, bt, cache, hkv, gqa, ql = _case(seed, q_len=q_len)
+        (q, cu, lens, bt, cache, hkv, gqa, ql), fp32_ref = _case(seed, q_len=q_len)
         ref = ops.decode_attn(q, cu, lens, bt, cache, hkv, gqa, ql, nsplit=nsplit)
         out = torch.full_like(q, float("nan"))
         rc = _call_noalloc(lib, q, cu, lens, bt, cache, hkv, gqa, ql, nsplit, out)
         torch.cuda.synchronize()
         assert rc == 0
         assert ops.status() == 0
-        assert torch.isfinite(out.float()).all()
-        err = (out.float() - ref.float()).abs().max().item()
+        # the same kernels on the same data: equal bit for bit
+        assert torch.equal(out, ref)
+        err = (out.float().cpu() - fp32_ref).abs().max().item()
         assert err < 2e-2, err
 
 
 def test_noalloc_rejects_oversized_launch():
     lib = _lib()
-    q, cu, lens, bt, cache, hkv, gqa, ql = _case(7)
+    (q, cu, lens, bt, cache, hkv, gqa, ql), _ = _case(7)
     cap = lib.k8v4_decode_attn_noalloc_max_floats()
     # pick a split count whose scratch exceeds the built-in array
     nsplit = 1
