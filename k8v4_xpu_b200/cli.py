@@ -200,16 +200,53 @@ def doctor() -> dict:
     return rep
 
 
+def build_checks() -> dict:
+    """The deployment image's build-time checks, which need no GPU (behaviour
+    of the reference's ``Dockerfile.unified:18-24``: byte-compile, patcher
+    run, library load, layout asserts). Every module of the package
+    byte-compiles; the in-tree library loads and was built from the ``csrc/``
+    tree beside it; its op registry is complete; the cache dtype and the vLLM
+    plugin register; the page layouts tile their pages. ``ok`` is the
+    conjunction."""
+    import compileall
+
+    import torch
+
+    from . import registry
+    from .kv.layout import CACHE_DTYPE, b200_layout, ref_layout
+    rep = doctor()
+    pkg = os.path.dirname(os.path.abspath(__file__))
+    rep["byte_compiled"] = bool(compileall.compile_dir(pkg, quiet=1, force=True))
+    rep["hash_matches"] = bool(rep.get("library_loads")) and rep.get("library_source_hash") == rep.get(
+        "tree_source_hash", rep.get("library_source_hash"))
+    want_ops = ("kv_store", "rope_store", "decode_attn", "prefill_attn", "wq_gemm", "wq_gemm_allreduce", "rmsnorm",
+                "silu_mul", "quant_rows", "embed_int8", "argmax", "gather_dequant", "prefill_attn_cp",
+                "decode_combine_ranks", "decode_attn_push")
+    rep["missing_ops"] = [o for o in want_ops if not (rep.get("library_loads") and hasattr(torch.ops.k8v4, o))]
+    rep["registry"] = registry.kv_cache_torch_dtype(CACHE_DTYPE) == torch.uint8
+    rep["pages_tile"] = all(lay.regions_fill_page() for lay in
+                            (b200_layout(4), b200_layout(2), b200_layout(1, 3), ref_layout(2), ref_layout(4)))
+    rep["build_ok"] = bool(rep["byte_compiled"] and rep["library_loads"] and rep["hash_matches"]
+                           and not rep["missing_ops"] and rep["registry"] and rep["pages_tile"]
+                           and rep["layout_ok"])
+    return rep
+
+
 def main(argv: list[str] | None = None) -> int:
     argv = list(sys.argv[1:] if argv is None else argv)
     if not argv or argv[0] in ("-h", "--help"):
         print("usage: python -m k8v4_xpu_b200 serve [options]   (serve --help for options)\n"
-              "       python -m k8v4_xpu_b200 doctor            (installation checks, JSON)")
+              "       python -m k8v4_xpu_b200 doctor            (installation checks, JSON)\n"
+              "       python -m k8v4_xpu_b200 doctor --build    (image build-time checks, no GPU needed)")
         return 0
     cmd, rest = argv[0], argv[1:]
     if cmd == "serve":
         return serve(rest)
     if cmd == "doctor":
+        if "--build" in rest:
+            rep = build_checks()
+            print(json.dumps(rep, indent=2))
+            return 0 if rep["build_ok"] else 1
         rep = doctor()
         print(json.dumps(rep, indent=2))
         return 0 if rep["ok"] else 1
