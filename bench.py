@@ -13,8 +13,10 @@ one, so each sequence reads its own KV pages every step).
 
 ``value`` is decode tok/s at c=1 timed on the device (K back-to-back replays
 of the captured decode step between CUDA events, max over ranks); ``e2e`` is
-the same metric through the engine's public ``step()`` (host scheduling, H2D
-of the step inputs from pinned memory, D2H of the sampled tokens).
+the same metric through the engine's public ``step()`` over 512 decode steps
+(BASELINE config 3's decode length; ``--e2e-steps``), each one growing every
+context by a token, with host scheduling, the H2D of the step inputs from
+pinned memory and the D2H of the sampled tokens inside the timed region.
 """
 from __future__ import annotations
 
@@ -121,6 +123,8 @@ def main() -> int:
     ap.add_argument("--model", default="dense-27b")
     ap.add_argument("--layers", type=int, default=None, help="debug only: fewer layers is not a valid number")
     ap.add_argument("--no-c4", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=512,
+                    help="engine steps of the end-to-end decode (BASELINE config 3: 512 decode tokens)")
     ap.add_argument("--mode", default="decode", choices=("decode", "cp", "mtp"),
                     help="decode: the headline (128K prefill + decode c=1/c=4); cp: 262K context-parallel prefill "
                          "cold and cached-prefix TTFT; mtp: 4 x 200K contexts, MTP6 with forced acceptance 3.0")
@@ -151,7 +155,7 @@ def main() -> int:
     ops.require()
     mcfg = PRESETS[args.model]
     ctx = args.ctx
-    decode_budget = 2 * (args.warmup + args.steps) + 64
+    decode_budget = 2 * (args.warmup + args.steps + args.e2e_steps) + 64
     blocks_per_seq = (ctx + decode_budget + 15) // 16 + 2
     ecfg = EngineConfig(model=args.model, tensor_parallel_size=world, max_model_len=ctx + decode_budget + 16,
                         max_num_seqs=4, max_num_batched_tokens=args.chunk, num_kv_blocks=4 * blocks_per_seq + 8,
@@ -203,15 +207,20 @@ def main() -> int:
         b.record()
         sync_all()
         dev_s = comm.max_scalar(a.elapsed_time(b) / 1e3)
+        # end to end: engine steps through the public API, each one advancing
+        # every sequence by a token (the context grows; inputs go H2D from
+        # pinned memory, the sampled tokens come back D2H)
         h2d0, d2h0 = eng.h2d_bytes, eng.d2h_bytes
+        lens0 = [len(s_.prompt) + len(s_.output) for s_ in eng.scheduler.running]
         w = time.perf_counter()
-        for _ in range(args.steps):
+        for _ in range(args.e2e_steps):
             eng.step()
         sync_all()
         e2e_s = comm.max_scalar(time.perf_counter() - w)
+        lens1 = [len(s_.prompt) + len(s_.output) for s_ in eng.scheduler.running]
         clocks = sampler.stop()
-        return {"dev_s": dev_s, "e2e_s": e2e_s, "clocks": clocks,
-                "h2d": (eng.h2d_bytes - h2d0) // args.steps, "d2h": (eng.d2h_bytes - d2h0) // args.steps,
+        return {"dev_s": dev_s, "e2e_s": e2e_s, "clocks": clocks, "ctx": (min(lens0), max(lens1)),
+                "h2d": (eng.h2d_bytes - h2d0) // args.e2e_steps, "d2h": (eng.d2h_bytes - d2h0) // args.e2e_steps,
                 "launches": per_replay * args.steps}
 
     c1 = decode_phase(1)
@@ -251,8 +260,10 @@ def main() -> int:
         "decode_c1_tok_s": round(tok_c1, 2),
         "clocks": c1["clocks"],
         "e2e": {
-            "value": round(args.steps / c1["e2e_s"], 2),
+            "value": round(args.e2e_steps / c1["e2e_s"], 2),
             "unit": "tok/s",
+            "steps": args.e2e_steps,
+            "context": list(c1["ctx"]),
             "h2d_bytes_per_step": int(c1["h2d"]),
             "d2h_bytes_per_step": int(c1["d2h"]),
             "prefill_tok_s": round(ctx / prefill_wall, 1),
@@ -264,7 +275,7 @@ def main() -> int:
     if c4:
         line["decode_c4_tok_s"] = round(4 * args.steps / c4["dev_s"], 2)
         line["decode_c4_ms_per_step"] = round(1e3 * c4["dev_s"] / args.steps, 4)
-        line["e2e"]["decode_c4_tok_s"] = round(4 * args.steps / c4["e2e_s"], 2)
+        line["e2e"]["decode_c4_tok_s"] = round(4 * args.e2e_steps / c4["e2e_s"], 2)
         line["clocks_c4"] = c4["clocks"]
     if args.layers is not None or ctx != 128197:
         line["invalid"] = "debug run (layers=%s, ctx=%d)" % (args.layers, ctx)
