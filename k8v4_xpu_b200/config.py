@@ -50,6 +50,7 @@ ENV: dict[str, tuple[str, type]] = {
     "num_kv_blocks": ("K8V4_NUM_KV_BLOCKS", int),
     "speculative_tokens": ("K8V4_SPEC_TOKENS", int),
     "forced_accept_mean": ("K8V4_FORCED_ACCEPT_MEAN", float),
+    "mtp_prefill_slice": ("K8V4_MTP_PREFILL_SLICE", int),
     "cuda_graphs": ("K8V4_CUDA_GRAPHS", bool),
     "seed": ("K8V4_SEED", int),
     "host": ("K8V4_HOST", str),
@@ -129,6 +130,7 @@ class ServeConfig:
     num_kv_blocks: int | None = None
     speculative_tokens: int = 0
     forced_accept_mean: float | None = None
+    mtp_prefill_slice: int = 1024
     cuda_graphs: bool = True
     capture_sizes: tuple[int, ...] = ()
     seed: int = 0
@@ -169,7 +171,7 @@ class ServeConfig:
             block_size=self.block_size, gpu_memory_utilization=self.gpu_memory_utilization,
             num_kv_blocks=self.num_kv_blocks, speculative_tokens=self.speculative_tokens,
             cuda_graphs=self.cuda_graphs, capture_sizes=seqs, seed=self.seed, layers=self.layers,
-            forced_accept_mean=self.forced_accept_mean, device=device,
+            forced_accept_mean=self.forced_accept_mean, mtp_prefill_slice=self.mtp_prefill_slice, device=device,
             kv_cache_dtype_skip_layers=self.kv_cache_dtype_skip_layers, kv_skip_dtype=self.kv_skip_dtype)
 
     def validate(self) -> None:
@@ -195,6 +197,8 @@ class ServeConfig:
             raise ValueError("--port must lie in [0, 65535]")
         if self.seed < 0:
             raise ValueError("--seed must be non-negative")
+        if self.mtp_prefill_slice < 0:
+            raise ValueError("--mtp-prefill-slice must be >= 0")
         if self.forced_accept_mean is not None:
             if not self.speculative_tokens:
                 raise ValueError("--forced-accept-mean needs --speculative-config")
@@ -236,6 +240,8 @@ def build_parser() -> argparse.ArgumentParser:
     a("--num-kv-blocks", type=int)
     a("--speculative-config", help="mtp/6 or JSON")
     a("--forced-accept-mean", type=float, help="benchmark mode: seeded Bernoulli acceptance with this mean length")
+    a("--mtp-prefill-slice", type=int,
+      help="under MTP: prefill tokens run beside each speculative decode step (0: alternate whole steps)")
     a("--compilation-config", help="FULL_DECODE_ONLY, NONE, or JSON with cudagraph_capture_sizes")
     a("--enforce-eager", action="store_true", default=None)
     a("--seed", type=int)

@@ -61,6 +61,9 @@ class EngineConfig:
     seed: int = 0
     layers: int | None = None         # override (tests / smoke)
     forced_accept_mean: float | None = None  # MTP forced-acceptance benchmark mode
+    # under MTP: prefill tokens that run beside each speculative decode step
+    # while sequences decode (0: whole steps alternate between the two)
+    mtp_prefill_slice: int = 1024
     device: str = "cuda"
     # layers whose KV stays in a plain dtype (the MTP layer's index is the
     # target's layer count); the dtype name is resolved from the environment
@@ -122,7 +125,8 @@ class LLMEngine:
         spec = cfg.speculative_tokens > 0
         self.scheduler = Scheduler(self.blocks, cfg.max_num_seqs, cfg.max_num_batched_tokens, width,
                                    cfg.max_model_len, lookahead=width if spec else 0,
-                                   mix_prefill_with_decode=not spec)
+                                   mix_prefill_with_decode=not spec,
+                                   prefill_slice=cfg.mtp_prefill_slice if spec else 0)
         # a decoding sequence may write up to 2 * width slots past its length (verify + drafts)
         self.max_pages = (cfg.max_model_len + 2 * width + self.layout.page - 1) // self.layout.page + 1
         self.max_q = max(1, width)
@@ -283,7 +287,11 @@ class LLMEngine:
         if not sched.chunks:
             return []
         t0 = time.perf_counter()
-        if self.mtp is not None and sched.is_decode_only:
+        if self.mtp is not None and sched.split:
+            # the speculative graph over the decode rows, then the prefill slice
+            dec, pre = sched.parts()
+            finished = self.mtp.step(dec) + self._plain_step(pre)
+        elif self.mtp is not None and sched.is_decode_only:
             finished = self.mtp.step(sched)
         else:
             finished = self._plain_step(sched)

@@ -130,12 +130,22 @@ class SchedulerOutput:
     num_tokens: int
     is_decode_only: bool
     preempted: list[Sequence] = dataclasses.field(default_factory=list)
+    # decode rows and a prefill slice that run as two passes of one step (the
+    # speculative decode graph covers decode rows only); see ``parts``
+    split: bool = False
+
+    def parts(self) -> tuple["SchedulerOutput", "SchedulerOutput"]:
+        """The decode rows and the prefill chunks as separate outputs."""
+        dec = [c for c in self.chunks if not c.is_prefill]
+        pre = [c for c in self.chunks if c.is_prefill]
+        return (SchedulerOutput(dec, sum(c.num_tokens for c in dec), True, self.preempted),
+                SchedulerOutput(pre, sum(c.num_tokens for c in pre), False, []))
 
 
 class Scheduler:
     def __init__(self, blocks: BlockManager, max_num_seqs: int = 4, max_num_batched_tokens: int = 4224,
                  decode_width: int = 1, max_model_len: int = 262144, lookahead: int = 0,
-                 mix_prefill_with_decode: bool = True):
+                 mix_prefill_with_decode: bool = True, prefill_slice: int = 0):
         if max_num_batched_tokens < 1 or max_num_seqs < 1:
             raise ValueError("scheduler limits must be positive")
         self.blocks = blocks
@@ -145,9 +155,16 @@ class Scheduler:
         self.max_model_len = max_model_len
         # KV slots a decoding sequence may write past its verify window (MTP drafts)
         self.lookahead = lookahead
-        # False: a step is either all decode or all prefill, alternating when both
-        # are pending (the speculative step is one graph over decode rows only)
+        # False: decode rows and prefill chunks never share one forward (the
+        # speculative step is one graph over decode rows only). With a
+        # ``prefill_slice`` > 0 a step then carries the decode rows plus at
+        # most that many prefill tokens, run as two passes (``split``), so a
+        # long prompt delays each decode step by one slice only; with 0 steps
+        # alternate between all-decode and all-prefill.
         self.mix = mix_prefill_with_decode
+        if prefill_slice < 0:
+            raise ValueError("prefill_slice must be >= 0")
+        self.prefill_slice = int(prefill_slice)
         self._turn = 0
         self.waiting: collections.deque[Sequence] = collections.deque()
         self.running: list[Sequence] = []
@@ -191,13 +208,17 @@ class Scheduler:
         chunks: list[ScheduledChunk] = []
         preempted: list[Sequence] = []
         do_decode = do_prefill = True
+        sliced = False
         if not self.mix:
             decoding = any(not s.in_prefill for s in self.running)
             prefilling = any(s.in_prefill for s in self.running) or (
                 bool(self.waiting) and len(self.running) < self.max_num_seqs)
             if decoding and prefilling:
-                self._turn ^= 1
-                do_decode, do_prefill = self._turn == 1, self._turn == 0
+                if self.prefill_slice > 0:
+                    sliced = True
+                else:
+                    self._turn ^= 1
+                    do_decode, do_prefill = self._turn == 1, self._turn == 0
         # 1) decode tokens of generating sequences
         for seq in list(self.running) if do_decode else []:
             if seq.in_prefill:
@@ -215,6 +236,8 @@ class Scheduler:
             budget -= width
         if not do_prefill:
             return SchedulerOutput(chunks, sum(c.num_tokens for c in chunks), bool(chunks), preempted)
+        if sliced and any(not c.is_prefill for c in chunks):
+            budget = min(budget, self.prefill_slice)
         # 2) prefill chunks of admitted sequences, then admit new ones
         for seq in self.running:
             if budget <= 0:
@@ -240,7 +263,8 @@ class Scheduler:
             budget -= n
         total = sum(c.num_tokens for c in chunks)
         decode_only = bool(chunks) and all(not c.is_prefill for c in chunks)
-        return SchedulerOutput(chunks, total, decode_only, preempted)
+        split = (not self.mix) and not decode_only and any(not c.is_prefill for c in chunks)
+        return SchedulerOutput(chunks, total, decode_only, preempted, split)
 
     def _preempt(self, seq: Sequence) -> None:
         """Recompute-style preemption: free the blocks and requeue at the front.

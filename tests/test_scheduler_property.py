@@ -56,10 +56,12 @@ def test_the_random_runs_reached_preemption():
     assert sum(1 for n in preemptions if n > 0) >= 3, preemptions
 
 
+@pytest.mark.parametrize("prefill_slice", [0, 16])
 @pytest.mark.parametrize("seed", range(8))
-def test_mtp_shaped_scheduling_keeps_invariants(seed):
+def test_mtp_shaped_scheduling_keeps_invariants(seed, prefill_slice):
     """The scheduler as MTP6 drives it: decode rows of width 1 + drafts with a
-    KV lookahead, decode and prefill steps alternating; a fake verify accepts
+    KV lookahead, decode and prefill steps alternating (``prefill_slice`` 0)
+    or decode rows with a bounded prefill slice beside them; a fake verify accepts
     a random number of drafts and emits them plus one token (rollback by
     length, as the real commit does)."""
     from k8v4_xpu_b200.runtime.block_manager import BlockManager
@@ -68,7 +70,7 @@ def test_mtp_shaped_scheduling_keeps_invariants(seed):
     k, V = 6, 1000
     bm = BlockManager(rng.choice([12, 20, 48]), block_size=16)
     sch = Scheduler(bm, max_num_seqs=4, max_num_batched_tokens=rng.choice([32, 64]), decode_width=k + 1,
-                    max_model_len=200, lookahead=k, mix_prefill_with_decode=False)
+                    max_model_len=200, lookahead=k, mix_prefill_with_decode=False, prefill_slice=prefill_slice)
     seqs = []
     for step in range(3000):
         if step < 150 and rng.random() < 0.3:
@@ -79,6 +81,10 @@ def test_mtp_shaped_scheduling_keeps_invariants(seed):
                 break
             continue
         out = sch.schedule()
+        if out.split:  # decode rows plus prefill chunks: two passes of one step
+            dec, pre = out.parts()
+            assert dec.chunks and pre.chunks and dec.is_decode_only and not pre.is_decode_only
+            assert dec.num_tokens + pre.num_tokens == out.num_tokens
         for c in out.chunks:
             seq = c.seq
             if c.is_prefill:

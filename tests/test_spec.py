@@ -18,11 +18,11 @@ def test_forced_accept_prob_solves_mean_length():
         forced_accept_prob(8.0, 6)
 
 
-def _fake_engine(k=6, forced=3.0, seqs=2):
+def _fake_engine(k=6, forced=3.0, seqs=2, prefill_slice=0):
     cfg = types.SimpleNamespace(cuda_graphs=False, capture_sizes=(), max_num_seqs=seqs)
     bm = BlockManager(64, block_size=16)
     sch = Scheduler(bm, max_num_seqs=seqs, max_num_batched_tokens=256, decode_width=k + 1, lookahead=k + 1,
-                    mix_prefill_with_decode=False)
+                    mix_prefill_with_decode=False, prefill_slice=prefill_slice)
     eng = types.SimpleNamespace(cfg=cfg, blocks=bm, scheduler=sch, stats={"generated_tokens": 0})
 
     def should_stop(seq, tok):
@@ -87,6 +87,33 @@ def test_scheduler_alternates_decode_and_prefill_under_mtp():
         kinds.append(out.is_decode_only)
         assert all(c.is_prefill for c in out.chunks) or out.is_decode_only
     assert kinds == [True, False, True, False] or kinds == [False, True, False, True]
+
+
+def test_scheduler_runs_a_bounded_prefill_slice_beside_mtp_decode():
+    eng, _ = _fake_engine(prefill_slice=16)
+    sch = eng.scheduler
+    a = sch.add(list(range(20)), SamplingParams(max_tokens=50))
+    out = sch.schedule()
+    assert out.is_decode_only is False and not out.split  # nothing decodes yet: the whole budget prefills
+    a.computed = 20
+    a.output.append(1)
+    a.draft = [0] * 6
+    b = sch.add(list(range(40)), SamplingParams(max_tokens=5))
+    for want_start in (0, 16, 32):
+        out = sch.schedule()
+        assert out.split and not out.is_decode_only
+        dec, pre = out.parts()
+        assert [c.seq for c in dec.chunks] == [a] and dec.is_decode_only and dec.num_tokens == 7
+        assert [(c.seq, c.start) for c in pre.chunks] == [(b, want_start)]
+        assert pre.num_tokens == min(16, 40 - want_start) and not pre.is_decode_only
+        b.computed = want_start + pre.num_tokens
+    # b's prompt is done: every step is decode-only again
+    b.output.append(3)
+    b.draft = [0] * 6
+    out = sch.schedule()
+    assert out.is_decode_only and not out.split and len(out.chunks) == 2
+    with pytest.raises(ValueError):
+        Scheduler(eng.blocks, prefill_slice=-1)
 
 
 def test_spec_stats_mean():
