@@ -47,7 +47,10 @@ int k8v4_rmsnorm(const void* x, float* xf, void* residual, const void* w, void* 
                  unsigned long long* sync_state, unsigned long long sync_expected, cudaStream_t st);
 int k8v4_wq_gemm_allreduce(int mode, const void* w, const void* wscale, const void* x, const float* xscale,
                            float* ws_mc, unsigned long long* flag_mc, int M, int N, int K, int ldo, int split,
-                           cudaStream_t st);
+                           cudaStream_t st, void* limb_buf);
+int64_t k8v4_wq_gemm_limb_bytes(int M, int K);
+int k8v4_wq_gemm_limbs(const void* w, const void* wscale, const void* x, const void* residual, void* out, float* ws,
+                       void* limb_buf, int M, int N, int K, int ldo, int split, cudaStream_t st);
 int k8v4_wq_gemm_ctas(int mode, int M, int N, int K, int split);
 int k8v4_silu_mul(const void* gu, void* y, void* yq, float* yscale, int rows, int inter, cudaStream_t st);
 int k8v4_quant_rows(const void* x, void* q, float* scale, int rows, int n, cudaStream_t st);
@@ -245,6 +248,29 @@ void prefill_attn(const at::Tensor& q, const at::Tensor& cu_q, const at::Tensor&
 }
 
 // --------------------------------------------------------------------- GEMM
+// Decode-sized W4A16 calls (at most 32 rows) can run on 8-bit MMAs over two
+// int8 limbs of each token row (see wq_gemm.cu, mode W4L), at the cost of one
+// small preparation kernel. K8V4_DECODE_LIMBS: "auto" (default) takes that
+// path for wide outputs (N >= 16384, the gate/up projection up to TP2, where
+// it measured 17% faster; the narrower decode GEMMs measured 2 us slower with
+// the extra kernel), "1" for every decode-sized call, "0" never.
+static int limbs_policy() {  // 0 never, 1 always, 2 auto
+  static const int pol = [] {
+    const char* v = std::getenv("K8V4_DECODE_LIMBS");
+    if (!v || !*v || v[0] == 'a' || v[0] == 'A') return 2;
+    return (v[0] == '0' || v[0] == 'n' || v[0] == 'N' || v[0] == 'f' || v[0] == 'F') ? 0 : 1;
+  }();
+  return pol;
+}
+
+// The limb buffers of one W4A16 call (an empty tensor when the call does not take that path).
+static at::Tensor limb_buffer(const at::Tensor& x, int64_t M, int64_t N, int64_t K) {
+  const int pol = limbs_policy();
+  const bool use = pol == 1 || (pol == 2 && N >= 16384);
+  const int64_t bytes = use ? k8v4_wq_gemm_limb_bytes((int)M, (int)K) : 0;
+  return at::empty({bytes}, x.options().dtype(at::kByte));
+}
+
 // mode 0: W4A16 (x bf16), 1: W4A8 (x int8 + xscale), 2: W8A8 (w int8 [N,K] + per-row scale).
 void wq_gemm(int64_t mode, const at::Tensor& w, const at::Tensor& wscale, const at::Tensor& x,
              const c10::optional<at::Tensor>& xscale, const c10::optional<at::Tensor>& residual, at::Tensor& out,
@@ -293,9 +319,16 @@ void wq_gemm(int64_t mode, const at::Tensor& w, const at::Tensor& wscale, const 
   }
   c10::cuda::CUDAGuard g(x.device());
   const float* xs = (mode == 0) ? nullptr : xscale->data_ptr<float>();
-  check_rc(k8v4_wq_gemm((int)mode, w.data_ptr(), wscale.data_ptr(), x.data_ptr(), xs, res, out.data_ptr(), wsp,
-                        (int)M, (int)N, (int)K, (int)N, (int)split, cur_stream()),
-           "wq_gemm");
+  at::Tensor limbs = mode == 0 ? limb_buffer(x, M, N, K) : at::Tensor();
+  if (limbs.defined() && limbs.numel() > 0) {
+    check_rc(k8v4_wq_gemm_limbs(w.data_ptr(), wscale.data_ptr(), x.data_ptr(), res, out.data_ptr(), wsp,
+                                limbs.data_ptr(), (int)M, (int)N, (int)K, (int)N, (int)split, cur_stream()),
+             "wq_gemm (limbs)");
+  } else {
+    check_rc(k8v4_wq_gemm((int)mode, w.data_ptr(), wscale.data_ptr(), x.data_ptr(), xs, res, out.data_ptr(), wsp,
+                          (int)M, (int)N, (int)K, (int)N, (int)split, cur_stream()),
+             "wq_gemm");
+  }
   if (split > 1 && finish) {
     check_rc(k8v4_splitk_finish(wsp, res, out.data_ptr(), M * N, 1, cur_stream()), "splitk_finish");
   }
@@ -467,10 +500,12 @@ void wq_gemm_allreduce(int64_t mode, const at::Tensor& w, const at::Tensor& wsca
                 "W4A8 takes int8 activations + fp32 scales");
   }
   c10::cuda::CUDAGuard g(x.device());
+  at::Tensor limbs = mode == 0 ? limb_buffer(x, M, N, K) : at::Tensor();
   check_rc(k8v4_wq_gemm_allreduce((int)mode, w.data_ptr(), wscale.data_ptr(), x.data_ptr(),
                                   mode == 0 ? nullptr : xscale->data_ptr<float>(), reinterpret_cast<float*>(ws_mc),
                                   reinterpret_cast<unsigned long long*>(flag_mc), (int)M, (int)N, (int)K, (int)N,
-                                  (int)split, cur_stream()),
+                                  (int)split, cur_stream(),
+                                  limbs.defined() && limbs.numel() > 0 ? limbs.data_ptr() : nullptr),
            "wq_gemm_allreduce");
 }
 

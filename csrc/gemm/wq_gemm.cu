@@ -16,6 +16,19 @@
 //                k8v4_v030/w4a8_prefill.py:146-157)
 //   mode W8A8  : int8 per-row weights (lm_head) x int8 tokens; the weight
 //                tile goes straight from TMA into the MMA, one group = all K.
+//   mode W4L   : W4A16 at decode sizes (at most 32 tokens) through 8-bit
+//                integer MMAs. Each token row x is written as two int8 limbs
+//                x ~= s (128 hi + lo) with |128 hi + lo| <= 16319 (15 bits,
+//                finer than bf16 for the row's large entries); the limbs_kernel
+//                makes them, with the row scale s and the integer sum C of
+//                each 128-k group. Converters only unpack int4 codes to u8
+//                (q + 8, five instructions per 8 codes, no subtraction); one
+//                kind::i8 MMA of N = 2 BT takes the hi and the lo rows
+//                together (an MMA of N <= 64 costs the tensor pipe the same
+//                ~45 cycles as one of N = 16) with K = 32 per instruction, so
+//                a 128-k block is 4 MMAs instead of 8. The accumulators form
+//                128 D_hi + D_lo - 8 C = sum q X exactly in int32, scale it by
+//                the group scale, and apply s at the end.
 //
 // Roles: warp 0 issues TMA, warp 1 owns TMEM and issues MMAs (one elected
 // thread; at decode sizes two more warps issue too, each taking every third
@@ -45,7 +58,7 @@ namespace gemm {
 
 using namespace tc;
 
-enum Mode : int { W4A16 = 0, W4A8 = 1, W8A8 = 2 };
+enum Mode : int { W4A16 = 0, W4A8 = 1, W8A8 = 2, W4L = 3 };
 
 struct Params {
   const int32_t* qweight;      // W4: [K/8, N] int32 (GPTQ, low nibble first)
@@ -56,6 +69,7 @@ struct Params {
   float* ws;                   // [M, ldo] fp32 accumulation (split > 1)
   float* ws_mc;                // multicast alias of a symmetric [M, ldo] fp32 buffer (GEMM -> all-reduce)
   unsigned long long* flag_mc; // multicast alias of the counter each CTA signals when its sums are out
+  const int32_t* csum;         // W4L: [M, K/128] integer sum of each token's limb values per 128-k group
   int M, N, K, ldo;
   int k_per_split;             // multiple of 128
 };
@@ -65,12 +79,14 @@ struct Cfg {
   // Decode-sized tiles keep the converted weights in TMEM (the MMA reads A
   // from TMEM): no shared-memory round trip for A, and 128-k stages so each
   // wait / commit of the MMA thread covers eight MMAs.
-  static constexpr bool TA = (MODE == W4A16) && (BT <= 64);
+  static constexpr bool LIMB = (MODE == W4L);
+  static constexpr bool TA = ((MODE == W4A16) && (BT <= 64)) || LIMB;
   static constexpr int BK = (MODE == W4A16 && !TA) ? 64 : 128;  // k per stage
   static constexpr int KB_PER_GROUP = (BK == 64) ? 2 : 1;  // stages per K group (W8: all)
   static constexpr int A_BYTES = 128 * 128;                // 128 rows x 128 B
+  static constexpr int BROWS = LIMB ? 2 * BT : BT;         // B operand rows: tokens, or hi then lo limbs
   static constexpr int B_ATOMS = (MODE == W4A16) ? BK / 64 : 1;  // 128-byte k atoms per token row
-  static constexpr int B_BYTES = BT * 128 * B_ATOMS;
+  static constexpr int B_BYTES = BROWS * 128 * B_ATOMS;
   static constexpr int RAW_BYTES = (MODE == W8A8) ? 0 : (BK / 8) * 128 * 4;
   // Two MMA-issuing warps on the TMEM-A path (even / odd K groups, separate
   // accumulator buffers): at N <= 64 one tcgen05.mma costs its issuing thread
@@ -83,8 +99,8 @@ struct Cfg {
   static constexpr int NWARPS = 2 + NCONV + NACC + (NMMA - 1);
   static constexpr int NTHREADS = NWARPS * 32;
   static constexpr int NBUF = 4;                           // TMEM group partials in flight
-  static constexpr int D_COLS = NBUF * BT;
-  static constexpr int A_COLS = BK / 2;                    // TMEM columns of one A stage
+  static constexpr int D_COLS = NBUF * BROWS;
+  static constexpr int A_COLS = LIMB ? BK / 4 : BK / 2;    // TMEM columns of one A stage (u8: 4 k per column)
   static constexpr int TSTAGES = TA ? ((512 - D_COLS) / A_COLS > 12 ? 12 : (512 - D_COLS) / A_COLS) : 0;
   static constexpr int TMEM_NEED = D_COLS + TSTAGES * A_COLS;
   static constexpr int TMEM_COLS = TMEM_NEED <= 32 ? 32 : TMEM_NEED <= 64 ? 64 : TMEM_NEED <= 128 ? 128
@@ -99,13 +115,16 @@ struct Cfg {
   static constexpr int ACC_SPLIT = NACC / 4;               // column slices per lane quadrant
   static constexpr int COLS = BT / ACC_SPLIT;              // columns per accumulator thread
   static constexpr int UMMA_K = (MODE == W4A16) ? 16 : 32;
+  static constexpr int CSUM_BYTES = LIMB ? MAXG * BT * 4 : 0;  // W4L: group sums of the CTA's tokens
   static constexpr int SMEM_BYTES =
-      1024 + ASMEM * A_BYTES + BR * B_BYTES + RSTAGES * RAW_BYTES + BAR_BYTES + MAXG * 128 * 2;
+      1024 + ASMEM * A_BYTES + BR * B_BYTES + RSTAGES * RAW_BYTES + BAR_BYTES + MAXG * 128 * 2 + CSUM_BYTES;
   static_assert(TMEM_NEED <= 512, "TMEM budget");
   static_assert(!TA || NCONV % 4 == 0, "TMEM converters work in teams of 4 warps (one per lane quadrant)");
   static_assert(NACC == 4 || NACC == 8, "accumulator warps cover the 4 lane quadrants");
   static_assert(COLS % 8 == 0, "columns per accumulator thread");
   static_assert(BT % 16 == 0 && BT >= 16 && BT <= 256, "MMA N");
+  static_assert(!LIMB || BT <= 32, "limb GEMMs serve at most 32 tokens (MMA N = 2 BT <= 64)");
+  static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 };
 
 // int4 x 8 (GPTQ low nibble first) -> 8 exact bf16 values (q-8) as 4 words.
@@ -187,6 +206,7 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
   uint64_t* done_more = scale_bar + 1;       // [NMMA-1] drains of the other MMA issuers
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done_more + C::NMMA);
   __half* sScale = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(bars) + C::BAR_BYTES);  // [MAXG][128]
+  int32_t* sCsum = reinterpret_cast<int32_t*>(sScale + C::MAXG * 128);  // W4L: [MAXG][BT]
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -277,7 +297,8 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
         mbar_arrive_expect_tx(&b_full[bs], C::B_BYTES);
 #pragma unroll
         for (int at = 0; at < C::B_ATOMS; ++at)
-          tma_load_2d(sB + bs * C::B_BYTES + at * (BT * 128), &tm_x, &b_full[bs], k0 + at * 64, t0);
+          tma_load_2d(sB + bs * C::B_BYTES + at * (BT * 128), &tm_x, &b_full[bs], k0 + at * 64,
+                      C::LIMB ? blockIdx.y * C::BROWS : t0);
         K8V4_TRACE_EVENT(0, kb);
         ++issued;
       }
@@ -300,7 +321,9 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
     // waits on the accumulators whichever issuer filled it last.
     if (lane == 0 && nkb > 0) {
       const int issuer = (warp == 1) ? 0 : warp - (2 + NCONV + NACC) + 1;
-      const uint32_t idesc = (MODE == W4A16) ? idesc_bf16(128, BT) : idesc_s8(128, BT);
+      const uint32_t idesc = (MODE == W4A16) ? idesc_bf16(128, BT)
+                             : C::LIMB     ? idesc_i8(128, C::BROWS, false, true)  // u8 codes x s8 limbs
+                                           : idesc_s8(128, BT);
       bool ok = true;
       for (int g = issuer; g < ngroups && ok; g += C::NMMA) {
         const int buf = g % C::NBUF;
@@ -313,7 +336,7 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
           g_gemm_trace[6 * 256 + g] = globaltimer_ns() - te0;
 #endif
         tc_fence_after();
-        const uint32_t dtm = tmem + buf * BT;
+        const uint32_t dtm = tmem + buf * C::BROWS;
         for (int j = 0; j < kb_per_group; ++j) {
           const int kb = g * kb_per_group + j;
           const int s = kb % C::AR, bs = kb % C::BR;
@@ -332,7 +355,13 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
 #endif
           tc_fence_after();
           const uint32_t b_base = smem_u32(sB + bs * C::B_BYTES);
-          if (C::TA) {
+          if (C::LIMB) {
+            const uint32_t a_tm = tmem + C::D_COLS + s * C::A_COLS;
+#pragma unroll
+            for (int kk = 0; kk < C::BK / C::UMMA_K; ++kk)  // 4 MMAs of K = 32 (8 TMEM columns of A each)
+              mma_i8_ts(dtm, a_tm + kk * 8, sdesc_sw128(b_base + kk * 32, 16, 1024), idesc, kk > 0 ? 1u : 0u);
+            mma_commit(&a_empty[s]);  // frees the TMEM A stage and the limb stage
+          } else if (C::TA) {
             const uint32_t a_tm = tmem + C::D_COLS + s * C::A_COLS;
 #pragma unroll
             for (int kk = 0; kk < C::BK / C::UMMA_K; ++kk)
@@ -381,20 +410,35 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
         if (quad == 0 && lane == 0) K8V4_TRACE_EVENT(5, kb);
         const uint32_t* raw = reinterpret_cast<const uint32_t*>(sR + rs * C::RAW_BYTES);
         const uint32_t dst = lane_base + ts * C::A_COLS;
-#pragma unroll
-        for (int half = 0; half < C::BK / 64; ++half) {
+        if (C::LIMB) {
+          // 16 words of 8 codes -> 32 columns of 4 u8 codes (q + 8) in k order
           uint32_t v[32];
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            uint32_t o[4];
-            int4x8_to_bf16(raw[(half * 8 + c) * 128 + f], o);
-            v[4 * c] = o[0];
-            v[4 * c + 1] = o[1];
-            v[4 * c + 2] = o[2];
-            v[4 * c + 3] = o[3];
+          for (int c = 0; c < 16; ++c) {
+            const uint32_t w = raw[c * 128 + f];
+            const uint32_t lo = w & 0x0F0F0F0Fu;          // codes k0 k2 k4 k6
+            const uint32_t hi = (w >> 4) & 0x0F0F0F0Fu;   // codes k1 k3 k5 k7
+            v[2 * c] = __byte_perm(lo, hi, 0x5140);       // k0 k1 k2 k3
+            v[2 * c + 1] = __byte_perm(lo, hi, 0x7362);   // k4 k5 k6 k7
           }
-          if (half == 0) tc_fence_after();  // the MMA that read this TMEM stage has completed
-          tmem_st32(dst + half * 32, v);
+          tc_fence_after();  // the MMA that read this TMEM stage has completed
+          tmem_st32(dst, v);
+        } else {
+#pragma unroll
+          for (int half = 0; half < C::BK / 64; ++half) {
+            uint32_t v[32];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              uint32_t o[4];
+              int4x8_to_bf16(raw[(half * 8 + c) * 128 + f], o);
+              v[4 * c] = o[0];
+              v[4 * c + 1] = o[1];
+              v[4 * c + 2] = o[2];
+              v[4 * c + 3] = o[3];
+            }
+            if (half == 0) tc_fence_after();  // the MMA that read this TMEM stage has completed
+            tmem_st32(dst + half * 32, v);
+          }
         }
         if (quad == 0 && lane == 0) K8V4_TRACE_EVENT(7, kb);
         tmem_st_wait();
@@ -460,6 +504,16 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
     // MMA's completion and the release of its TMEM buffer.
     const bool staged = (MODE != W8A8) && p.k_per_split / 128 <= C::MAXG && nkb > 0;
     bool scales_ok = true;
+    if (C::LIMB) {
+      // the group sums of this CTA's tokens (made by the previous kernel)
+      pdl_wait();
+      const int kg0 = kbeg / 128, kgs = p.K / 128;
+      for (int i = threadIdx.x - 32 * (2 + NCONV); i < ngroups * BT; i += 32 * NACC) {
+        const int g = i / BT, c = i % BT, t = t0 + c;
+        sCsum[g * BT + c] = (t < p.M && g < C::MAXG) ? p.csum[(size_t)t * kgs + kg0 + g] : 0;
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(32 * NACC) : "memory");  // the accumulator warps only
+    }
     if (staged) scales_ok = mbar_wait_all(scale_bar, 0, abort_flag, 113);
     bool ok = nkb > 0 && scales_ok;
     for (int g = 0; g < ngroups && ok; ++g) {
@@ -470,18 +524,35 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
       if (MODE != W8A8)
         gs = staged ? __half2float(sScale[g * 128 + row])
                     : (n < p.N ? __half2float(p.wscale[(size_t)((kbeg / 128) + g) * p.N + n]) : 0.f);
-      const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + buf * BT + c0;
+      const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + buf * C::BROWS + c0;
+      if (C::LIMB) {
 #pragma unroll
-      for (int cc = 0; cc < C::COLS; cc += 16) {
-        uint32_t r[16];
-        tmem_ld8(taddr + cc, *reinterpret_cast<uint32_t(*)[8]>(&r[0]));
-        if (cc + 8 < C::COLS) tmem_ld8(taddr + cc + 8, *reinterpret_cast<uint32_t(*)[8]>(&r[8]));
-        tmem_ld_wait();
+        for (int cc = 0; cc < C::COLS; cc += 8) {
+          uint32_t h[8], l[8];
+          tmem_ld8(taddr + cc, h);
+          tmem_ld8(taddr + BT + cc, l);
+          tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          if (cc + i < C::COLS) {
-            const float v = (MODE == W4A16) ? __uint_as_float(r[i]) : ((MODE == W4A8) ? i2f_small(r[i]) : (float)(int)r[i]);
-            acc[cc + i] = fmaf(v, gs, acc[cc + i]);
+          for (int i = 0; i < 8; ++i) {
+            // 128 D_hi + D_lo - 8 C = sum over the group of q * X, exactly
+            const int v = (int)h[i] * 128 + (int)l[i] - 8 * sCsum[g * BT + c0 + cc + i];
+            acc[cc + i] = fmaf((float)v, gs, acc[cc + i]);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int cc = 0; cc < C::COLS; cc += 16) {
+          uint32_t r[16];
+          tmem_ld8(taddr + cc, *reinterpret_cast<uint32_t(*)[8]>(&r[0]));
+          if (cc + 8 < C::COLS) tmem_ld8(taddr + cc + 8, *reinterpret_cast<uint32_t(*)[8]>(&r[8]));
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            if (cc + i < C::COLS) {
+              const float v = (MODE == W4A16) ? __uint_as_float(r[i])
+                                              : ((MODE == W4A8) ? i2f_small(r[i]) : (float)(int)r[i]);
+              acc[cc + i] = fmaf(v, gs, acc[cc + i]);
+            }
           }
         }
       }
@@ -529,6 +600,68 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
   }
 }
 
+// ------------------------------------------------------------ limb preparation
+// One CTA per token row of x [M, K] (bf16): s = amax / 16319, X = rint(x / s)
+// (|X| <= 16319), hi = floor((X + 64) / 128) in [-127, 127], lo = X - 128 hi
+// in [-64, 63]. Rows go to the limb operand of tile t / bt: hi at row
+// t % bt, lo at row bt + t % bt. Also the per-row scale and the integer sum
+// of X over every 128-k group (the correction of the unsigned weight codes).
+constexpr float kLimbMax = 16319.f;
+
+__global__ void __launch_bounds__(256) limbs_kernel(const __nv_bfloat16* __restrict__ x, int K, int bt,
+                                                    int8_t* __restrict__ limbs, float* __restrict__ scale,
+                                                    int32_t* __restrict__ gsum) {
+  pdl_trigger();
+  pdl_wait();  // x comes from the previous kernel
+  __shared__ float red[8];
+  const int t = blockIdx.x;
+  const __nv_bfloat16* row = x + (size_t)t * K;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float am = 0.f;
+  for (int k = threadIdx.x * 8; k < K; k += 256 * 8) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(row + k);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 v = __bfloat1622float2(h[j]);
+      am = fmaxf(am, fmaxf(fabsf(v.x), fabsf(v.y)));
+    }
+  }
+  am = warp_max(am);
+  if (lane == 0) red[warp] = am;
+  __syncthreads();
+  am = lane < 8 ? red[lane] : 0.f;
+  am = warp_max(am);
+  const float s = am > 0.f ? am / kLimbMax : 1.f;
+  const float inv = 1.f / s;
+  int8_t* hi_row = limbs + ((size_t)(t / bt) * 2 * bt + (t % bt)) * K;
+  int8_t* lo_row = hi_row + (size_t)bt * K;
+  const int groups = K / 128;
+  for (int g = warp; g < groups; g += 8) {
+    const int k = g * 128 + lane * 4;
+    const uint2 raw = *reinterpret_cast<const uint2*>(row + k);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+    uint32_t hw = 0, lw = 0;
+    int sum = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float v = __bfloat162float(j & 1 ? h[j >> 1].y : h[j >> 1].x);
+      const int X = (int)fminf(fmaxf(rintf(v * inv), -kLimbMax), kLimbMax);
+      const int hv = (X + 64) >> 7;  // arithmetic shift: floor
+      const int lv = X - 128 * hv;
+      hw |= ((uint32_t)(uint8_t)(int8_t)hv) << (8 * j);
+      lw |= ((uint32_t)(uint8_t)(int8_t)lv) << (8 * j);
+      sum += X;
+    }
+    *reinterpret_cast<uint32_t*>(hi_row + k) = hw;
+    *reinterpret_cast<uint32_t*>(lo_row + k) = lw;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) gsum[(size_t)t * groups + g] = sum;
+  }
+  if (threadIdx.x == 0) scale[t] = s;
+}
+
 // -------------------------------------------------------------------- host
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -562,6 +695,12 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int
   return r == CUDA_SUCCESS ? 0 : -2;
 }
 
+struct LimbBufs {
+  int8_t* limbs;   // [tiles x 2 bt, K]
+  float* scale;    // [M]
+  int32_t* gsum;   // [M, K / 128]
+};
+
 template <int MODE, int BT, int NCONV, int NACC, int STAGES, int RSTAGES, int BSTAGES>
 static int launch_cfg(const void* w, const void* x, const Params& p, int split, cudaStream_t st) {
   const void* wscale_ptr = p.wscale;
@@ -576,6 +715,9 @@ static int launch_cfg(const void* w, const void* x, const Params& p, int split, 
   if (rc) return 100 + rc;
   if (MODE == W4A16)
     rc = make_tmap_2d(&tx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.K, p.M, (uint64_t)p.K * 2, 64, BT, true);
+  else if (MODE == W4L)  // the limb operand: [tiles x (hi rows, lo rows), K] int8
+    rc = make_tmap_2d(&tx, x, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.K, (uint64_t)cdiv(p.M, BT) * 2 * BT, p.K, 128,
+                      2 * BT, true);
   else
     rc = make_tmap_2d(&tx, x, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.K, p.M, p.K, 128, BT, true);
   if (rc) return 200 + rc;
@@ -634,9 +776,14 @@ static int k_per_split_for(int K, int split) {
   return cdiv(kgroups, split) * 128;
 }
 
+// Token rows up to which a W4A16 call runs as W4L (when the caller gave limb buffers).
+constexpr int kLimbMaxRows = 32;
+
+static int limb_bt(int M) { return M <= 16 ? 16 : 32; }
+
 static int gemm_impl(int mode, const void* w, const void* wscale, const void* x, const float* xscale,
                      const void* residual, void* out, float* ws, float* ws_mc, unsigned long long* flag_mc, int M,
-                     int N, int K, int ldo, int split, cudaStream_t st) {
+                     int N, int K, int ldo, int split, cudaStream_t st, const LimbBufs* lb = nullptr) {
   if (N % 128 || K % 128 || M <= 0) return 1;
   Params p;
   p.qweight = reinterpret_cast<const int32_t*>(w);
@@ -647,6 +794,7 @@ static int gemm_impl(int mode, const void* w, const void* wscale, const void* x,
   p.ws = ws;
   p.ws_mc = ws_mc;
   p.flag_mc = flag_mc;
+  p.csum = nullptr;
   p.M = M;
   p.N = N;
   p.K = K;
@@ -655,6 +803,16 @@ static int gemm_impl(int mode, const void* w, const void* wscale, const void* x,
   split = cdiv(K, p.k_per_split);
   if (split > 1 && !ws && !ws_mc) return 2;
   const int bt = pick_bt(mode, M);
+  if (mode == W4A16 && lb && lb->limbs && M <= kLimbMaxRows && K / 128 <= 144) {
+    const int lbt = limb_bt(M);
+    if (launch_k(limbs_kernel, dim3(M), dim3(256), 0, st, reinterpret_cast<const __nv_bfloat16*>(x), K, lbt,
+                 lb->limbs, lb->scale, lb->gsum) != cudaSuccess)
+      return 5;
+    p.xscale = lb->scale;
+    p.csum = lb->gsum;
+    if (lbt == 16) return launch_cfg<W4L, 16, K8V4_GEMM_NCONV, 4, 4, 12, 16>(w, lb->limbs, p, split, st);
+    return launch_cfg<W4L, 32, K8V4_GEMM_NCONV, 4, 4, 12, 16>(w, lb->limbs, p, split, st);
+  }
   if (mode == W4A16) {
     if (bt == 16) return launch_cfg<W4A16, 16, K8V4_GEMM_NCONV, 4, 4, 16, 16>(w, x, p, split, st);
     if (bt == 32) return launch_cfg<W4A16, 32, K8V4_GEMM_NCONV, 4, 4, 12, 16>(w, x, p, split, st);
@@ -678,15 +836,51 @@ extern "C" int k8v4_wq_gemm(int mode, const void* w, const void* wscale, const v
   return gemm_impl(mode, w, wscale, x, xscale, residual, out, ws, nullptr, nullptr, M, N, K, ldo, split, st);
 }
 
+// Bytes of the limb buffers a W4A16 call of M rows and K columns needs (0
+// when the call does not take the limb path): limb operand, row scales, group
+// sums, each part 256-byte aligned.
+extern "C" int64_t k8v4_wq_gemm_limb_bytes(int M, int K) {
+  if (M <= 0 || M > kLimbMaxRows || K % 128 || K / 128 > 144) return 0;
+  const int bt = limb_bt(M);
+  auto up = [](int64_t b) { return (b + 255) / 256 * 256; };
+  return up((int64_t)cdiv(M, bt) * 2 * bt * K) + up((int64_t)M * 4) + up((int64_t)M * (K / 128) * 4);
+}
+
+static LimbBufs carve_limbs(void* buf, int M, int K) {
+  LimbBufs lb{nullptr, nullptr, nullptr};
+  if (!buf) return lb;
+  const int bt = limb_bt(M);
+  auto up = [](int64_t b) { return (b + 255) / 256 * 256; };
+  uint8_t* b = static_cast<uint8_t*>(buf);
+  lb.limbs = reinterpret_cast<int8_t*>(b);
+  b += up((int64_t)cdiv(M, bt) * 2 * bt * K);
+  lb.scale = reinterpret_cast<float*>(b);
+  b += up((int64_t)M * 4);
+  lb.gsum = reinterpret_cast<int32_t*>(b);
+  return lb;
+}
+
+// W4A16 with the limb buffers of k8v4_wq_gemm_limb_bytes(M, K) bytes: calls of
+// at most 32 rows run as W4L (limbs_kernel, then the int8 GEMM); others as
+// k8v4_wq_gemm.
+extern "C" int k8v4_wq_gemm_limbs(const void* w, const void* wscale, const void* x, const void* residual, void* out,
+                                  float* ws, void* limb_buf, int M, int N, int K, int ldo, int split,
+                                  cudaStream_t st) {
+  const LimbBufs lb = carve_limbs(limb_buf, M, K);
+  return gemm_impl(W4A16, w, wscale, x, nullptr, residual, out, ws, nullptr, nullptr, M, N, K, ldo, split, st, &lb);
+}
+
 // GEMM -> all-reduce: fp32 sums into every rank's copy of a symmetric buffer
 // through its multicast address `ws_mc`, then one signal per CTA on the
 // multicast counter `flag_mc`. The consumer expects world x
 // k8v4_wq_gemm_ctas(...) signals for one call.
 extern "C" int k8v4_wq_gemm_allreduce(int mode, const void* w, const void* wscale, const void* x, const float* xscale,
                                       float* ws_mc, unsigned long long* flag_mc, int M, int N, int K, int ldo,
-                                      int split, cudaStream_t st) {
+                                      int split, cudaStream_t st, void* limb_buf) {
   if (!ws_mc || !flag_mc) return 4;
-  return gemm_impl(mode, w, wscale, x, xscale, nullptr, nullptr, nullptr, ws_mc, flag_mc, M, N, K, ldo, split, st);
+  const LimbBufs lb = carve_limbs(mode == W4A16 ? limb_buf : nullptr, M, K);
+  return gemm_impl(mode, w, wscale, x, xscale, nullptr, nullptr, nullptr, ws_mc, flag_mc, M, N, K, ldo, split, st,
+                   &lb);
 }
 
 // CTAs one call launches (the number of signals it sends per rank).

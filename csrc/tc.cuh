@@ -202,6 +202,17 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// D[tmem] (+)= A[tmem] x B[smem desc]^T, 8-bit integer inputs, int32
+// accumulate. A sits in TMEM K-major: lane = row, each 32-bit column packs
+// four consecutive k.
+__device__ __forceinline__ void mma_i8_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 // Arrive on `bar` once every tcgen05 op issued so far by this thread is done.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -294,6 +305,15 @@ K8V4_HOST_DEVICE constexpr uint32_t idesc_s8(int M, int N, bool a_mn_major = fal
          | (1u << 10)                               // B: signed int8
          | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// kind::i8 with each operand's signedness chosen: unsigned 8-bit A (codes
+// 0..15 of int4 weights) against signed 8-bit B, for example.
+K8V4_HOST_DEVICE constexpr uint32_t idesc_i8(int M, int N, bool a_signed, bool b_signed) {
+  return (2u << 4)                                  // D format: s32
+         | ((a_signed ? 1u : 0u) << 7)              // A: s8 or u8
+         | ((b_signed ? 1u : 0u) << 10)             // B: s8 or u8
+         | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 // Byte offset of 16-byte chunk `chunk` (0..7) of row `row` inside a 128B-swizzled

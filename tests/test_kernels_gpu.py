@@ -133,8 +133,8 @@ def test_w4a16_gemm(M, split):
 @pytest.mark.parametrize("M", [1, 5, 16, 32])
 @pytest.mark.parametrize("split", [1, 4])
 def test_w4a16_decode_precision(M, split):
-    """Decode tile sizes (int8 MMAs on two activation limbs): within bf16
-    output rounding of the fp32 reference, with activation outliers."""
+    """Decode tile sizes (bf16 MMAs, A in TMEM): within bf16 output rounding
+    of the fp32 reference, with activation outliers."""
     N, K = 256, 5120
     qw, sc = _int4_weights(N, K, 30)
     x = torch.randn(M, K, generator=_gen(31))
@@ -148,6 +148,33 @@ def test_w4a16_decode_precision(M, split):
     assert st == 0, "device status 0x%x (code | site<<8)" % st
     err = (out.float().cpu() - ref).abs().max().item()
     assert err <= 4e-3 * ref.abs().max().item() + 1e-4, err
+
+
+@pytest.mark.parametrize("M", [1, 4, 7, 16, 17, 32])
+@pytest.mark.parametrize("split", [1, 3])
+def test_w4a16_limb_path(M, split):
+    """Wide decode GEMMs (N >= 16384) run as 8-bit MMAs over two int8 limbs of
+    each token row (x ~= s (128 hi + lo), 15 bits) against u8 weight codes
+    corrected by the limbs' group sums: within bf16 output rounding of the
+    fp32 reference, with an outlier 60x the typical value in every row, a tiny
+    value, an all-zero row, and tiles of 16 and 32 rows (17 rows: padding)."""
+    N, K = 16384, 2048
+    qw, sc = _int4_weights(N, K, 40)
+    x = torch.randn(M, K, generator=_gen(41))
+    x[:, 9] = 60.0
+    x[0, 200] = -1e-3
+    if M > 2:
+        x[M - 1] = 0.0
+    x = x.bfloat16()
+    ref = gptq.w4a16_ref(x, qw, sc)
+    out = ops.wq_gemm(ops.W4A16, qw.to(DEV), sc.to(DEV), x.to(DEV), split=split)
+    torch.cuda.synchronize()
+    st = ops.status()
+    assert st == 0, "device status 0x%x (code | site<<8)" % st
+    err = (out.float().cpu() - ref).abs().max().item()
+    assert err <= 4e-3 * ref.abs().max().item() + 1e-4, err
+    if M > 2:
+        assert torch.equal(out[M - 1].cpu(), torch.zeros(N, dtype=torch.bfloat16))
 
 
 @pytest.mark.parametrize("M", [1, 28, 130, 300])
