@@ -49,6 +49,14 @@ int k8v4_wq_gemm_allreduce(int mode, const void* w, const void* wscale, const vo
                            float* ws_mc, unsigned long long* flag_mc, int M, int N, int K, int ldo, int split,
                            cudaStream_t st, void* limb_buf);
 int64_t k8v4_wq_gemm_limb_bytes(int M, int K);
+int k8v4_wq_gemm_sp(int mode, const void* w, const void* wscale, const void* x, const float* xscale, void* out, int M,
+                    int N, int K, int ldo, int world, int rank, const int* tile0, const unsigned long long* ag_flag,
+                    const unsigned long long* ag_target, void* const* rs_dst, unsigned long long* const* rs_sig,
+                    cudaStream_t st);
+int k8v4_rmsnorm_sp(const void* slots, int world, int64_t slot_stride, const void* x_local, void* residual,
+                    int init_residual, const void* w, int rows, int n, float eps, const unsigned long long* rs_flag,
+                    unsigned long long rs_target, void* y, void* yq, float* ys, int64_t row0, int mc,
+                    unsigned long long* ag_sig_mc, cudaStream_t st);
 int k8v4_wq_gemm_limbs(const void* w, const void* wscale, const void* x, const void* residual, void* out, float* ws,
                        void* limb_buf, int M, int N, int K, int ldo, int split, cudaStream_t st);
 int k8v4_wq_gemm_ctas(int mode, int M, int N, int K, int split);
@@ -509,6 +517,94 @@ void wq_gemm_allreduce(int64_t mode, const at::Tensor& w, const at::Tensor& wsca
            "wq_gemm_allreduce");
 }
 
+// Sequence-parallel prefill GEMM (see k8v4_wq_gemm_sp). Addresses that may
+// belong to peers (rs_dst, rs_sig) or to this rank's symmetric buffers
+// (ag_flag) come as integers; x is this rank's view of the input rows.
+void wq_gemm_sp(int64_t mode, const at::Tensor& w, const at::Tensor& wscale, const at::Tensor& x,
+                const c10::optional<at::Tensor>& xscale, const c10::optional<at::Tensor>& out, int64_t world,
+                int64_t rank, at::IntArrayRef tile0, int64_t ag_flag, at::IntArrayRef ag_target,
+                at::IntArrayRef rs_dst, at::IntArrayRef rs_sig) {
+  check_contig(w, "weight");
+  check_contig(wscale, "weight scale");
+  check_contig(x, "x");
+  TORCH_CHECK(mode == 0 || mode == 1, "sequence-parallel GEMMs are W4A16 or W4A8");
+  TORCH_CHECK(x.dim() == 2 && w.scalar_type() == at::kInt && w.size(0) * 8 == x.size(1), "W4 qweight [K/8, N]");
+  TORCH_CHECK(world >= 2 && world <= 8 && (int64_t)tile0.size() == world + 1, "tile0 has world + 1 entries");
+  const int64_t M = x.size(0), K = x.size(1), N = w.size(1);
+  if (mode == 0) {
+    TORCH_CHECK(x.scalar_type() == at::kBFloat16, "W4A16 takes bf16 activations");
+  } else {
+    TORCH_CHECK(x.scalar_type() == at::kChar && xscale.has_value() && xscale->numel() >= M &&
+                    xscale->scalar_type() == at::kFloat,
+                "W4A8 takes int8 activations + fp32 scales");
+  }
+  const bool rs = !rs_dst.empty();
+  TORCH_CHECK(!rs || ((int64_t)rs_dst.size() == world && (int64_t)rs_sig.size() == world), "rs_dst / rs_sig per rank");
+  TORCH_CHECK(ag_flag == 0 || (int64_t)ag_target.size() == world, "ag_target per rank");
+  TORCH_CHECK(rs || ag_flag != 0, "neither a gather wait nor a scatter");
+  void* outp = nullptr;
+  if (!rs) {
+    TORCH_CHECK(out.has_value() && out->scalar_type() == at::kBFloat16 && out->size(0) == M && out->size(1) == N &&
+                    out->is_contiguous(),
+                "out bf16 [M, N]");
+    outp = out->data_ptr();
+  }
+  int t0[9];
+  for (int i = 0; i <= world; ++i) t0[i] = (int)tile0[i];
+  unsigned long long tg[8] = {0};
+  void* dst[8] = {nullptr};
+  unsigned long long* sig[8] = {nullptr};
+  for (int i = 0; i < world; ++i) {
+    if (ag_flag) tg[i] = (unsigned long long)ag_target[i];
+    if (rs) {
+      TORCH_CHECK(rs_dst[i] % 16 == 0 && rs_sig[i] % 8 == 0 && rs_dst[i] && rs_sig[i], "peer addresses");
+      dst[i] = reinterpret_cast<void*>(rs_dst[i]);
+      sig[i] = reinterpret_cast<unsigned long long*>(rs_sig[i]);
+    }
+  }
+  c10::cuda::CUDAGuard g(x.device());
+  check_rc(k8v4_wq_gemm_sp((int)mode, w.data_ptr(), wscale.data_ptr(), x.data_ptr(),
+                           mode == 0 ? nullptr : xscale->data_ptr<float>(), outp, (int)M, (int)N, (int)K, (int)N,
+                           (int)world, (int)rank, t0, reinterpret_cast<const unsigned long long*>(ag_flag),
+                           ag_flag ? tg : nullptr, rs ? dst : nullptr, rs ? sig : nullptr, cur_stream()),
+           "wq_gemm_sp");
+}
+
+// Sequence-parallel norm of this rank's rows (see k8v4_rmsnorm_sp). y / yq /
+// ys are addresses: multicast addresses of the all-gather buffers (mc) or
+// local buffers.
+void rmsnorm_sp(const c10::optional<at::Tensor>& slots, int64_t world, int64_t slot_stride,
+                const c10::optional<at::Tensor>& x_local, at::Tensor& residual, bool init_residual, const at::Tensor& w,
+                int64_t rows, double eps, int64_t rs_flag, int64_t rs_target, int64_t y, int64_t yq, int64_t ys,
+                int64_t row0, bool mc, int64_t ag_sig) {
+  check_contig(residual, "residual");
+  check_contig(w, "w");
+  TORCH_CHECK(residual.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "bf16 residual / w");
+  const int64_t n = w.numel();
+  TORCH_CHECK(residual.numel() >= rows * n, "residual holds the rows");
+  const void* sp = nullptr;
+  if (slots.has_value()) {
+    check_contig(*slots, "slots");
+    TORCH_CHECK(slots->scalar_type() == at::kBFloat16 && slots->numel() >= world * slot_stride &&
+                    slot_stride >= rows * n,
+                "slots bf16 [world][rows >= %d][n]");
+    sp = slots->data_ptr();
+  }
+  const void* xl = nullptr;
+  if (x_local.has_value()) {
+    check_contig(*x_local, "x_local");
+    TORCH_CHECK(x_local->scalar_type() == at::kBFloat16 && x_local->numel() >= rows * n, "x_local bf16 [rows, n]");
+    xl = x_local->data_ptr();
+  }
+  c10::cuda::CUDAGuard g(residual.device());
+  check_rc(k8v4_rmsnorm_sp(sp, (int)world, slot_stride, xl, residual.data_ptr(), init_residual ? 1 : 0, w.data_ptr(),
+                           (int)rows, (int)n, (float)eps, reinterpret_cast<const unsigned long long*>(rs_flag),
+                           (unsigned long long)rs_target, reinterpret_cast<void*>(y), reinterpret_cast<void*>(yq),
+                           reinterpret_cast<float*>(ys), row0, mc ? 1 : 0,
+                           reinterpret_cast<unsigned long long*>(ag_sig), cur_stream()),
+           "rmsnorm_sp");
+}
+
 int64_t wq_gemm_ctas(int64_t mode, int64_t M, int64_t N, int64_t K, int64_t split) {
   return k8v4_wq_gemm_ctas((int)mode, (int)M, (int)N, (int)K, (int)split);
 }
@@ -663,6 +759,13 @@ TORCH_LIBRARY(k8v4, m) {
       "wq_gemm_allreduce(int mode, Tensor w, Tensor wscale, Tensor x, Tensor? xscale, Tensor(a!) ws, int ws_mc, "
       "int flag_mc, int split) -> ()");
   m.def("wq_gemm_ctas(int mode, int M, int N, int K, int split) -> int");
+  m.def(
+      "wq_gemm_sp(int mode, Tensor w, Tensor wscale, Tensor x, Tensor? xscale, Tensor(a!)? out, int world, int rank, "
+      "int[] tile0, int ag_flag, int[] ag_target, int[] rs_dst, int[] rs_sig) -> ()");
+  m.def(
+      "rmsnorm_sp(Tensor? slots, int world, int slot_stride, Tensor? x_local, Tensor(a!) residual, bool init_residual, "
+      "Tensor w, int rows, float eps, int rs_flag, int rs_target, int y, int yq, int ys, int row0, bool mc, "
+      "int ag_sig) -> ()");
   m.def("silu_mul(Tensor gate_up, Tensor(a!)? y, Tensor(b!)? yq, Tensor(c!)? yscale) -> ()");
   m.def("quant_rows(Tensor x, Tensor(a!) q, Tensor(b!) scale) -> ()");
   m.def("int8_dequant(Tensor q, Tensor scale, Tensor(a!) out) -> ()");
@@ -688,6 +791,8 @@ TORCH_LIBRARY(k8v4, m) {
 }
 
 TORCH_LIBRARY_IMPL(k8v4, CUDA, m) {
+  m.impl("wq_gemm_sp", &wq_gemm_sp);
+  m.impl("rmsnorm_sp", &rmsnorm_sp);
   m.impl("kv_store", &kv_store);
   m.impl("rope_store", &rope_store);
   m.impl("decode_attn", &decode_attn);

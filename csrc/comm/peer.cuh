@@ -29,6 +29,13 @@ __device__ __forceinline__ void mc_st_f32(float* mc_addr, float v) {
   asm volatile("multimem.st.relaxed.sys.global.f32 [%0], %1;" ::"l"(mc_addr), "f"(v) : "memory");
 }
 
+// +v on a 64-bit counter (this GPU's or a peer's), ordered after this
+// thread's earlier writes (and, through a preceding bar.sync and fence_sys,
+// its CTA's).
+__device__ __forceinline__ void red_release_add_u64(unsigned long long* addr, unsigned long long v) {
+  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(addr), "l"(v) : "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_alias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
 
 __device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }

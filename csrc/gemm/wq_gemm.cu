@@ -42,6 +42,21 @@
 // (the splitk_finish kernel, the fused RMSNorm, or the RoPE / cache-store
 // kernel for the qkv projection), zeroing `ws` for the next GEMM.
 //
+// Sequence-parallel prefill (tensor parallel, 128-row token tiles owned by
+// ranks in contiguous runs, sp_tile0[o] .. sp_tile0[o + 1] for rank o):
+//   all-gather -> GEMM (qkv, gate/up): the token rows are this rank's copy of
+//     a symmetric buffer that every rank's norm fills through its multicast
+//     address. The CTAs of tile j start at this rank's own tiles, and the
+//     producer waits (bounded) until ag_flag[owner(j)] reaches
+//     ag_target[owner(j)] before the first TMA load of the tile, so tiles of
+//     ranks that are still normalizing come last.
+//   GEMM -> reduce-scatter (o_proj, down): each CTA stores its bf16 partial
+//     rows straight into the owner's slot for this rank (rs_dst[owner], peer
+//     memory over NVLink, row stride ldo) and then adds 1 to the owner's
+//     counter rs_sig[owner] with release semantics; the owner's norm sums the
+//     slots once every rank's CTAs have signalled. The transfer of early
+//     tiles overlaps the math of later ones.
+//
 // GEMM -> all-reduce (tensor parallel row-parallel projections): with
 // `ws_mc` set, the partial sums go to the multicast address of a symmetric
 // fp32 buffer instead (multimem.red: the NVSwitch adds them into every
@@ -70,6 +85,13 @@ struct Params {
   float* ws_mc;                // multicast alias of a symmetric [M, ldo] fp32 buffer (GEMM -> all-reduce)
   unsigned long long* flag_mc; // multicast alias of the counter each CTA signals when its sums are out
   const int32_t* csum;         // W4L: [M, K/128] integer sum of each token's limb values per 128-k group
+  // sequence-parallel prefill (sp_world > 1; token tiles of 128 rows)
+  int sp_world, sp_rank;
+  int sp_tile0[9];                   // rank o owns token tiles [sp_tile0[o], sp_tile0[o + 1])
+  const unsigned long long* ag_flag; // all-gather -> GEMM: this rank's copy of the per-owner row counters
+  unsigned long long ag_target[8];   //   rows of owner o are all here once ag_flag[o] >= ag_target[o]
+  __nv_bfloat16* rs_dst[8];          // GEMM -> reduce-scatter: owner o's slot for this rank (peer memory)
+  unsigned long long* rs_sig[8];     //   owner o's completion counter (peer memory)
   int M, N, K, ldo;
   int k_per_split;             // multiple of 128
 };
@@ -212,7 +234,12 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * 128;
-  const int t0 = blockIdx.y * BT;
+  // token tile: under sequence parallelism the CTAs start at this rank's own tiles
+  const int tile = p.sp_world > 1 ? (int)((blockIdx.y + p.sp_tile0[p.sp_rank]) % gridDim.y) : (int)blockIdx.y;
+  int owner = 0;
+  if (p.sp_world > 1)
+    while (owner + 1 < p.sp_world && tile >= p.sp_tile0[owner + 1]) ++owner;
+  const int t0 = tile * BT;
   const int kbeg = blockIdx.z * p.k_per_split;
   const int kend = min(p.K, kbeg + p.k_per_split);
   const int nkb = (kend - kbeg) / C::BK;
@@ -276,7 +303,13 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
         ++raw_issued;
       }
       pdl_wait();
-      for (int kb = 0; kb < nkb; ++kb) {
+      if (p.ag_flag) {
+        // all-gather -> GEMM: the tile's rows arrived from their owner
+        if (!peer::wait_geq_u64(p.ag_flag + owner, p.ag_target[owner], 114)) *abort_flag = 1;
+        peer::fence_proxy_alias();                                 // written through the multicast alias
+        asm volatile("fence.proxy.async.global;" ::: "memory");    // read by TMA (the async proxy)
+      }
+      for (int kb = 0; kb < nkb && !*abort_flag; ++kb) {
         const int k0 = kbeg + kb * C::BK;
         if (MODE != W8A8) {
           if (kb >= pre) {
@@ -572,6 +605,9 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
           const size_t o = (size_t)t * p.ldo + n;
           if (p.ws_mc) {
             peer::mc_red_add_f32(p.ws_mc + o, v);
+          } else if (p.rs_dst[0]) {
+            // reduce-scatter: this rank's partial row goes to the owner's slot
+            p.rs_dst[owner][(size_t)(t - p.sp_tile0[owner] * BT) * p.ldo + n] = __float2bfloat16_rn(v);
           } else if (gridDim.z > 1) {
             atomicAdd(p.ws + o, v);
           } else {
@@ -588,6 +624,12 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+  if (p.rs_dst[0] && threadIdx.x == 0) {
+    // the CTA's partial rows (ordered before this point by the barrier) are
+    // in the owner's slot: signal it
+    peer::fence_sys();
+    peer::red_release_add_u64(p.rs_sig[owner], 1ull);
   }
   if (p.flag_mc && threadIdx.x == 0) {
     // the CTA's multicast adds (ordered before this point by the barrier) are
@@ -695,6 +737,16 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int
   return r == CUDA_SUCCESS ? 0 : -2;
 }
 
+// Sequence-parallel arguments of one GEMM call (see the kernel's notes).
+struct SpArgs {
+  int world, rank;
+  int tile0[9];
+  const unsigned long long* ag_flag;  // null: no all-gather wait
+  unsigned long long ag_target[8];
+  __nv_bfloat16* rs_dst[8];           // rs_dst[0] null: no reduce-scatter
+  unsigned long long* rs_sig[8];
+};
+
 struct LimbBufs {
   int8_t* limbs;   // [tiles x 2 bt, K]
   float* scale;    // [M]
@@ -783,7 +835,8 @@ static int limb_bt(int M) { return M <= 16 ? 16 : 32; }
 
 static int gemm_impl(int mode, const void* w, const void* wscale, const void* x, const float* xscale,
                      const void* residual, void* out, float* ws, float* ws_mc, unsigned long long* flag_mc, int M,
-                     int N, int K, int ldo, int split, cudaStream_t st, const LimbBufs* lb = nullptr) {
+                     int N, int K, int ldo, int split, cudaStream_t st, const LimbBufs* lb = nullptr,
+                     const SpArgs* sp = nullptr) {
   if (N % 128 || K % 128 || M <= 0) return 1;
   Params p;
   p.qweight = reinterpret_cast<const int32_t*>(w);
@@ -795,6 +848,31 @@ static int gemm_impl(int mode, const void* w, const void* wscale, const void* x,
   p.ws_mc = ws_mc;
   p.flag_mc = flag_mc;
   p.csum = nullptr;
+  p.sp_world = 0;
+  p.sp_rank = 0;
+  p.ag_flag = nullptr;
+  for (int i = 0; i < 9; ++i) p.sp_tile0[i] = 0;
+  for (int i = 0; i < 8; ++i) {
+    p.ag_target[i] = 0;
+    p.rs_dst[i] = nullptr;
+    p.rs_sig[i] = nullptr;
+  }
+  if (sp) {
+    // sequence parallelism works on whole 128-row token tiles
+    if (sp->world < 2 || sp->world > 8 || sp->rank < 0 || sp->rank >= sp->world || pick_bt(mode, M) != 128 ||
+        split != 1 || ws_mc || (!sp->ag_flag && !sp->rs_dst[0]))
+      return 6;
+    p.sp_world = sp->world;
+    p.sp_rank = sp->rank;
+    for (int i = 0; i <= sp->world; ++i) p.sp_tile0[i] = sp->tile0[i];
+    if (p.sp_tile0[0] != 0 || p.sp_tile0[sp->world] != cdiv(M, 128)) return 6;
+    p.ag_flag = sp->ag_flag;
+    for (int i = 0; i < sp->world; ++i) {
+      p.ag_target[i] = sp->ag_target[i];
+      p.rs_dst[i] = sp->rs_dst[i];
+      p.rs_sig[i] = sp->rs_sig[i];
+    }
+  }
   p.M = M;
   p.N = N;
   p.K = K;
@@ -881,6 +959,32 @@ extern "C" int k8v4_wq_gemm_allreduce(int mode, const void* w, const void* wscal
   const LimbBufs lb = carve_limbs(mode == W4A16 ? limb_buf : nullptr, M, K);
   return gemm_impl(mode, w, wscale, x, xscale, nullptr, nullptr, nullptr, ws_mc, flag_mc, M, N, K, ldo, split, st,
                    &lb);
+}
+
+// Sequence-parallel prefill GEMM (tensor parallel, token tiles of 128 rows
+// owned by ranks in runs tile0[o] .. tile0[o + 1]). With ag_flag set, x is
+// this rank's copy of the all-gathered rows and each CTA first waits until
+// ag_flag[owner] >= ag_target[owner]. With rs_dst set, the output goes as bf16
+// partial rows into rs_dst[owner] (row stride ldo) and each CTA then adds 1 to
+// rs_sig[owner]; `out` is not written. Returns 6 for an unsupported call.
+extern "C" int k8v4_wq_gemm_sp(int mode, const void* w, const void* wscale, const void* x, const float* xscale,
+                               void* out, int M, int N, int K, int ldo, int world, int rank, const int* tile0,
+                               const unsigned long long* ag_flag, const unsigned long long* ag_target,
+                               void* const* rs_dst, unsigned long long* const* rs_sig, cudaStream_t st) {
+  SpArgs sp;
+  sp.world = world;
+  sp.rank = rank;
+  if (world < 2 || world > 8) return 6;
+  for (int i = 0; i <= world; ++i) sp.tile0[i] = tile0[i];
+  sp.ag_flag = ag_flag;
+  for (int i = 0; i < 8; ++i) {
+    sp.ag_target[i] = (ag_target && i < world) ? ag_target[i] : 0;
+    sp.rs_dst[i] = (rs_dst && i < world) ? reinterpret_cast<__nv_bfloat16*>(rs_dst[i]) : nullptr;
+    sp.rs_sig[i] = (rs_sig && i < world) ? rs_sig[i] : nullptr;
+  }
+  if (rs_dst && (!sp.rs_dst[0] || !sp.rs_sig[0])) return 6;
+  return gemm_impl(mode, w, wscale, x, xscale, nullptr, out, nullptr, nullptr, nullptr, M, N, K, ldo, 1, st, nullptr,
+                   &sp);
 }
 
 // CTAs one call launches (the number of signals it sends per rank).

@@ -319,6 +319,151 @@ using namespace k8v4::misc;
 
 K8V4_STATUS_API(misc)
 
+
+// ------------------------------------------------------------ sequence parallel
+// Norm of this rank's rows between a GEMM -> reduce-scatter and an
+// all-gather -> GEMM (tensor-parallel prefill, see wq_gemm.cu). One CTA per
+// local row r:
+//   v = sum over the `world` slots of row r (bf16 partial rows that every
+//       rank's reduce-scatter GEMM stored here; waited for until rs_flag >=
+//       rs_target), or row r of x_local (bf16) when slots is null;
+//   residual[r] <- bf16(v + residual[r]) (or bf16(v) with init_residual);
+//   y = bf16(bf16(residual[r] * rsqrt(mean(residual[r]^2) + eps)) * w)
+// then y (bf16) or its int8 quantization (per-row amax / 127) goes out:
+// through the multicast address of the all-gather buffer at global row
+// row0 + r (every rank's copy, `mc` set), followed by +1 on the multicast row
+// counter ag_sig_mc; or to a local buffer at row r.
+__device__ __forceinline__ void mc_st_v4(void* mc, uint4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1,%2,%3,%4};" ::"l"(mc), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void mc_st_b64(void* mc, uint2 v) {
+  const unsigned long long b = ((unsigned long long)v.y << 32) | v.x;
+  asm volatile("multimem.st.relaxed.sys.global.b64 [%0], %1;" ::"l"(mc), "l"(b) : "memory");
+}
+
+template <int VPT>
+__global__ void __launch_bounds__(kThreads) rmsnorm_sp_kernel(
+    const __nv_bfloat16* slots, int world, int64_t slot_stride, const __nv_bfloat16* x_local,
+    __nv_bfloat16* residual, int init_residual, const __nv_bfloat16* __restrict__ w, int n, float eps,
+    const unsigned long long* rs_flag, unsigned long long rs_target, __nv_bfloat16* y, int8_t* yq, float* ys,
+    int64_t row0, int mc, unsigned long long* ag_sig_mc) {
+  pdl_trigger();
+  uint4 gw[VPT];
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = (threadIdx.x + i * kThreads) * 8;
+    gw[i] = c < n ? *reinterpret_cast<const uint4*>(w + c) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  pdl_wait();
+  __shared__ float red[32];
+  const int64_t r = blockIdx.x;
+  if (slots && rs_flag) {
+    if (threadIdx.x == 0) peer::wait_geq_u64(rs_flag, rs_target, 202);
+    __syncthreads();
+  }
+  float v[VPT][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = (threadIdx.x + i * kThreads) * 8;
+    if (c < n) {
+      if (slots) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
+        for (int src = 0; src < world; ++src) {
+          float f[8];
+          load8(slots + src * slot_stride + r * n + c, f);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[i][j] += f[j];
+        }
+      } else {
+        load8(x_local + r * n + c, v[i]);
+      }
+      if (!init_residual) {
+        float rs[8];
+        load8(residual + r * n + c, rs);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] += rs[j];
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[i][j] = __bfloat162float(__float2bfloat16_rn(v[i][j]));
+      store8(residual + r * n + c, v[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+    }
+  }
+  ss = block_sum(ss, red);
+  const float inv = rsqrtf(ss / (float)n + eps);
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = (threadIdx.x + i * kThreads) * 8;
+    if (c < n) {
+      const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gw[i]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 g = __bfloat1622float2(g2[j]);
+        v[i][2 * j] = __bfloat162float(__float2bfloat16_rn(__bfloat162float(__float2bfloat16_rn(v[i][2 * j] * inv)) * g.x));
+        v[i][2 * j + 1] =
+            __bfloat162float(__float2bfloat16_rn(__bfloat162float(__float2bfloat16_rn(v[i][2 * j + 1] * inv)) * g.y));
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[i][j]));
+    }
+  }
+  const int64_t orow = mc ? row0 + r : r;
+  if (yq) {
+    amax = block_max(amax, red);
+    const float sc = fmaxf(amax / 127.f, 1e-5f);
+    const float qi = 1.f / sc;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int c = (threadIdx.x + i * kThreads) * 8;
+      if (c < n) {
+        uint32_t wq[2] = {0, 0};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int q = (int)fminf(fmaxf(rintf(v[i][j] * qi), -127.f), 127.f);
+          wq[j >> 2] |= ((uint32_t)(uint8_t)(int8_t)q) << (8 * (j & 3));
+        }
+        int8_t* dst = yq + orow * n + c;
+        if (mc) mc_st_b64(dst, make_uint2(wq[0], wq[1]));
+        else *reinterpret_cast<uint2*>(dst) = make_uint2(wq[0], wq[1]);
+      }
+    }
+    if (threadIdx.x == 0) {
+      if (mc) peer::mc_st_f32(ys + orow, sc);
+      else ys[orow] = sc;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int c = (threadIdx.x + i * kThreads) * 8;
+      if (c < n) {
+        if (mc) {
+          uint4 raw;
+          __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(v[i][2 * j], v[i][2 * j + 1]);
+          mc_st_v4(y + orow * n + c, raw);
+        } else {
+          store8(y + orow * n + c, v[i]);
+        }
+      }
+    }
+  }
+  if (mc && ag_sig_mc) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      peer::fence_proxy_alias();
+      peer::fence_sys();
+      peer::mc_signal_add_u64(ag_sig_mc, 1ull);
+    }
+  }
+}
+
 #define K8V4_VPT_DISPATCH(n, KERNEL, ...)                                         \
   do {                                                                            \
     const int vpt_ = cdiv(cdiv((n), 8), kThreads);                                \
@@ -339,6 +484,25 @@ extern "C" int k8v4_rmsnorm(const void* x, float* xf, void* residual, const void
   K8V4_VPT_DISPATCH(n, rmsnorm_kernel, reinterpret_cast<const __nv_bfloat16*>(x), xf,
                     reinterpret_cast<__nv_bfloat16*>(residual), reinterpret_cast<const __nv_bfloat16*>(w),
                     reinterpret_cast<__nv_bfloat16*>(y), reinterpret_cast<int8_t*>(yq), yscale, n, ldy, eps, sync);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+// Sequence-parallel norm of `rows` local rows (see rmsnorm_sp_kernel).
+extern "C" int k8v4_rmsnorm_sp(const void* slots, int world, int64_t slot_stride, const void* x_local,
+                               void* residual, int init_residual, const void* w, int rows, int n, float eps,
+                               const unsigned long long* rs_flag, unsigned long long rs_target, void* y, void* yq,
+                               float* ys, int64_t row0, int mc, unsigned long long* ag_sig_mc, cudaStream_t st) {
+  if (rows <= 0) return 0;
+  if (n % 8) return 1;
+  if (!slots && !x_local) return 4;
+  if (!y && !yq) return 4;
+  if (yq && !ys) return 4;
+  if (mc && (!ag_sig_mc || (y && reinterpret_cast<uintptr_t>(y) % 16) || (yq && reinterpret_cast<uintptr_t>(yq) % 8)))
+    return 4;
+  K8V4_VPT_DISPATCH(n, rmsnorm_sp_kernel, reinterpret_cast<const __nv_bfloat16*>(slots), world, slot_stride,
+                    reinterpret_cast<const __nv_bfloat16*>(x_local), reinterpret_cast<__nv_bfloat16*>(residual),
+                    init_residual, reinterpret_cast<const __nv_bfloat16*>(w), n, eps, rs_flag, rs_target,
+                    reinterpret_cast<__nv_bfloat16*>(y), reinterpret_cast<int8_t*>(yq), ys, row0, mc, ag_sig_mc);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 

@@ -188,6 +188,43 @@ def wq_gemm_allreduce(mode: int, w, wscale, x, ws, ws_mc: int, flag_mc: int, xsc
     return ws
 
 
+def wq_gemm_sp(mode: int, w, wscale, x, world: int, rank: int, tile0, xscale=None, out=None, ag_flag: int = 0,
+               ag_target=(), rs_dst=(), rs_sig=()):
+    """Sequence-parallel prefill GEMM over 128-row token tiles owned by ranks
+    (``tile0[o]`` .. ``tile0[o + 1]`` for rank ``o``). With ``ag_flag`` (the
+    address of this rank's per-owner row counters) ``x`` is this rank's copy of
+    the all-gathered rows and each CTA waits for its tile's owner; the output
+    goes to ``out``. With ``rs_dst`` / ``rs_sig`` (peer addresses per owner)
+    the output goes as bf16 partial rows into the owners' slots instead."""
+    require()
+    if ag_flag == 0 and not rs_dst:
+        raise ValueError("wq_gemm_sp needs a gather wait or a scatter")
+    n = w.shape[1]
+    if not rs_dst and out is None:
+        out = torch.empty((x.shape[0], n), dtype=torch.bfloat16, device=x.device)
+    torch.ops.k8v4.wq_gemm_sp(mode, w, wscale, x, xscale, out, int(world), int(rank), [int(t) for t in tile0],
+                              int(ag_flag), [int(t) for t in ag_target], [int(a) for a in rs_dst],
+                              [int(a) for a in rs_sig])
+    _count()
+    return out
+
+
+def rmsnorm_sp(residual, w, rows: int, eps: float, slots=None, world: int = 1, slot_stride: int = 0, x_local=None,
+               init_residual: bool = False, rs_flag: int = 0, rs_target: int = 0, y: int = 0, yq: int = 0,
+               ys: int = 0, row0: int = 0, mc: bool = False, ag_sig: int = 0) -> None:
+    """Sequence-parallel norm of ``rows`` local rows: slots summed (after the
+    reduce-scatter signals) or ``x_local``, plus the residual, normalized, and
+    pushed to every rank through multicast addresses (``mc``) or written to
+    local addresses ``y`` / ``yq`` + ``ys``."""
+    require()
+    if rows <= 0:
+        return
+    torch.ops.k8v4.rmsnorm_sp(slots, int(world), int(slot_stride), x_local, residual, bool(init_residual), w,
+                              int(rows), float(eps), int(rs_flag), int(rs_target), int(y), int(yq), int(ys),
+                              int(row0), bool(mc), int(ag_sig))
+    _count()
+
+
 def wq_gemm_ctas(mode: int, M: int, N: int, K: int, split: int = 1) -> int:
     require()
     return int(torch.ops.k8v4.wq_gemm_ctas(mode, M, N, K, split))
