@@ -284,7 +284,8 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
       prefetch_tmap(&tm_w);
       prefetch_tmap(&tm_x);
       if (MODE != W8A8) prefetch_tmap(&tm_s);
-      if (MODE != W8A8 && p.k_per_split / 128 <= C::MAXG) {
+      const bool scale_copy = MODE != W8A8 && p.k_per_split / 128 <= C::MAXG;
+      if (scale_copy) {
         // the CTA's scale block in one copy: the box always moves k_per_split/128
         // rows (rows past K arrive zero-filled and are never read)
         mbar_arrive_expect_tx(scale_bar, (p.k_per_split / 128) * 256);
@@ -337,6 +338,7 @@ __global__ void __launch_bounds__(Cfg<MODE, BT, NCONV, NACC, STAGES, RSTAGES, BS
       }
       if (*abort_flag) {
         // Wait (bounded) for this CTA's own copies still in flight.
+        if (scale_copy) mbar_wait_drain(scale_bar, 0);
         for (int kb = issued - 1; kb >= 0 && kb >= issued - C::BR; --kb)
           mbar_wait_drain(&b_full[kb % C::BR], (kb / C::BR) & 1);
         if (MODE == W8A8)

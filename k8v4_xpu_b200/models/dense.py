@@ -121,6 +121,7 @@ class DenseModel:
         # layer index (the MTP layer: len(layers)) -> plain fp8 / bf16 cache layout
         self.skip_kv: dict[int, skip_layers.SkipLayout] = {}
         self.fused_ar = None  # parallel.fused_ar.FusedAllReduce when TP runs the fused path
+        self.sp = None        # parallel.seq_parallel.SeqParallel: fused reduce-scatter / all-gather prefill
         self.cp = None        # parallel.cp.CPGroup under context parallelism
 
     # ------------------------------------------------------------- weights
@@ -344,6 +345,10 @@ class DenseModel:
                 all_rows: bool = False) -> torch.Tensor:
         """Run every layer; returns the final-normed hidden rows ``inp.logit_rows``
         (every row with ``all_rows``, as the MTP drafter needs)."""
+        T = inp.input_ids.shape[0]
+        if (self.sp is not None and not inp.is_decode and not all_rows and self.cp is None and not self.skip_kv
+                and self.sp.fits(T, self.cfg.hidden) and self._sp_linears()):
+            return self._forward_sp(inp, kv_caches)
         with stage("embed"):
             x = self.embed(inp.input_ids)
         residual = None
@@ -354,6 +359,59 @@ class DenseModel:
                                             li)
         with stage("final_norm"):
             return self._final_norm(x, residual, self.final_norm, None if all_rows else inp.logit_rows, sync)
+
+    def _sp_linears(self) -> bool:
+        return all(isinstance(lin, Int4Linear) for L in self.layers for lin in (L.qkv, L.o, L.gate_up, L.down))
+
+    def _forward_sp(self, inp: StepInputs, kv_caches: list[torch.Tensor]) -> torch.Tensor:
+        """Tensor-parallel prefill with the residual stream sharded by token rows
+        between the fused GEMM -> reduce-scatter and all-gather -> GEMM kernels
+        (``parallel.seq_parallel``). Same math as ``_layer``; returns the
+        final-normed rows ``inp.logit_rows`` on every rank."""
+        cfg, sh, sp = self.cfg, self.shape, self.sp
+        T = inp.input_ids.shape[0]
+        D = cfg.head_dim
+        hq, hkv = sh.hq_local, sh.hkv_local
+        sp.begin(T)
+        with stage("embed"):
+            x = self.embed(inp.input_ids)  # vocab-parallel lookup, summed over the group
+        for li, L in enumerate(self.layers):
+            tag = "layers.%d" % li
+            with stage(tag + ".input_norm"):
+                if li == 0:
+                    sp.norm_push(L.input_norm, cfg.rms_eps, gather=0, x_local=x[sp.row0:sp.row0 + sp.nrows])
+                else:
+                    sp.norm_push(L.input_norm, cfg.rms_eps, gather=0, slot=1)
+            with stage(tag + ".gemm_qkv"):
+                qkv = sp.gemm_ag(L.qkv, 0)
+            q = torch.empty((T, hq, D), dtype=torch.bfloat16, device=self.device)
+            with stage(tag + ".rope_store"):
+                ops.rope_store(qkv, self.rope, inp.positions, q, inp.slots, kv_caches[li], hq, hkv)
+            with stage(tag + ".attn"), attention_span("prefill"):
+                a = ops.prefill_attn(q, inp.cu_q, inp.seq_lens, inp.block_table, kv_caches[li], hkv, sh.gqa_local,
+                                     inp.max_q_len)
+            with stage(tag + ".o_proj"):
+                sp.gemm_rs(L.o, 0, x=a.view(T, hq * D))
+            w4a8 = uses_w4a8(L.gate_up.name, T, self.w4a8) and L.gate_up.supports_w4a8 and L.down.supports_w4a8
+            note_gemm_branch(L.gate_up.name, T, "w4a8" if w4a8 else "w4a16")
+            gather = 1 if w4a8 else 2
+            with stage(tag + ".post_norm"):
+                sp.norm_push(L.post_norm, cfg.rms_eps, gather=gather, slot=0)
+            with stage(tag + ".gate_up"):
+                gu = sp.gemm_ag(L.gate_up, gather)
+            with stage(tag + ".act"):
+                if w4a8:
+                    aq, as_ = ops.silu_mul(gu, quant=True)
+                else:
+                    act = ops.silu_mul(gu)
+            with stage(tag + ".down"):
+                if w4a8:
+                    sp.gemm_rs(L.down, 1, xq=aq, xs=as_)
+                else:
+                    sp.gemm_rs(L.down, 1, x=act)
+        with stage("final_norm"):
+            local = sp.final_norm(self.final_norm, cfg.rms_eps, slot=1)
+            return sp.gather_rows(local, inp.logit_rows, self.comm)
 
     # ---------------------------------------------------------------- MTP
     def init_mtp(self, seed: int = 1) -> "DenseModel":

@@ -158,6 +158,7 @@ class LLMEngine:
         when the box supports it; NCCL otherwise and for larger steps."""
         from ..parallel.fused_ar import FusedAllReduce, fused_ar_mode
         self.tp_comm_mode = "nccl"
+        self.tp_prefill_mode = "nccl"
         if fused_ar_mode() != "fused":
             return
         rows = max(self.cfg.max_num_seqs * (1 + self.cfg.speculative_tokens), 1)
@@ -169,6 +170,19 @@ class LLMEngine:
         except Exception as e:  # no multicast on this box: NCCL all-reduce
             import logging
             logging.getLogger("k8v4").warning("fused all-reduce unavailable (%s); using NCCL", e)
+        # prefill chunks: sequence parallelism with the reduce-scatter and the
+        # all-gather fused into the GEMMs
+        from ..parallel.seq_parallel import SeqParallel, sp_mode
+        self.tp_prefill_mode = "nccl"
+        if sp_mode() != "sp":
+            return
+        try:
+            self.model.sp = SeqParallel(getattr(comm, "group", None), self.device, self.cfg.max_num_batched_tokens,
+                                        self.mcfg.hidden)
+            self.tp_prefill_mode = "sp"
+        except Exception as e:  # no multicast on this box: NCCL all-reduce
+            import logging
+            logging.getLogger("k8v4").warning("sequence-parallel prefill unavailable (%s); using NCCL", e)
 
     # ---------------------------------------------------------------- cache
     def _alloc_cache(self) -> None:

@@ -196,3 +196,20 @@ def test_cp_page_maps_against_a_brute_force_shard_model():
             # local key k of this rank is global token owned[k]: pages in order, 16 per page
             for k, p in enumerate(owned[g.rank]):
                 assert pages[k // 16] * 16 + k % 16 == g.slot(blocks, p)
+
+
+def test_sequence_parallel_tiles_cover_the_chunk_once():
+    from k8v4_xpu_b200.parallel.seq_parallel import TILE, owned_rows, tile_owners
+    for world in (2, 4, 8):
+        for rows in (1, 127, 128, 129, 777, 4224, 4225, 8192):
+            t0 = tile_owners(rows, world)
+            tiles = -(-rows // TILE)
+            assert t0[0] == 0 and t0[-1] == tiles and all(a <= b for a, b in zip(t0, t0[1:]))
+            sizes = [b - a for a, b in zip(t0, t0[1:])]
+            assert max(sizes) - min(sizes) <= 1  # as even as whole tiles allow
+            spans = [owned_rows(rows, t0, o) for o in range(world)]
+            assert sum(n for _, n in spans) == rows
+            at = 0
+            for r0, n in spans:  # contiguous, in rank order
+                assert r0 == at or n == 0
+                at += n

@@ -84,6 +84,16 @@ def _worker(rank, world, port, q):
         hid = m.forward(inp, caches)
         ids = m.greedy(hid)
         res = {"hidden": hid.float().cpu(), "ids": ids.cpu(), "logits": m.logits(hid).float().cpu()}
+        # prefill with the residual sharded by token rows between the fused
+        # GEMM -> reduce-scatter and all-gather -> GEMM kernels (twice: the
+        # running signal counts must keep matching)
+        from k8v4_xpu_b200.parallel.seq_parallel import SeqParallel
+        m.sp = SeqParallel(None, dev, 512, TP_MODEL.hidden)
+        for _ in range(2):
+            caches = [torch.zeros(64, m.layout.page_bytes, dtype=torch.uint8, device=dev) for _ in m.layers]
+            res["hidden_sp"] = m.forward(inp, caches).float().cpu()
+        res["sp_calls"] = m.sp.calls
+        m.sp = None
         # decode-sized batch (<= 64 rows): the GEMM -> all-reduce runs fused (NVLS multicast adds)
         from k8v4_xpu_b200.parallel.fused_ar import FusedAllReduce
         small = _prefill_inputs(SMALL_PROMPTS, dev)
@@ -103,6 +113,7 @@ def _worker(rank, world, port, q):
         res["gen"] = eng.generate(PROMPTS, SamplingParams(max_tokens=8, ignore_eos=True))
         res["graph"] = bool(eng.graphs and eng.graphs.captured)
         res["comm_mode"] = eng.tp_comm_mode
+        res["prefill_mode"] = eng.tp_prefill_mode
         res["status"] = ops.status()
         eng.graphs.release()
         comm.barrier()
@@ -142,7 +153,14 @@ def test_tp_matches_tp1(world):
         assert torch.equal(out[0]["small_fused"], out[r]["small_fused"]), r
         assert out[0]["gen"] == out[r]["gen"], r
     assert out[0]["fused_calls"] == 3 * 2 * TP_MODEL.num_layers
-    assert out[0]["comm_mode"] == "fused"
+    assert out[0]["comm_mode"] == "fused" and out[0]["prefill_mode"] == "sp"
+    # sequence-parallel prefill: 4 fused GEMMs per layer, ranks agree exactly,
+    # and it matches the NCCL all-reduce path up to bf16 partial sums
+    assert out[0]["sp_calls"] == 2 * 4 * TP_MODEL.num_layers
+    for r in range(1, world):
+        assert torch.equal(out[0]["hidden_sp"], out[r]["hidden_sp"]), r
+    err = (out[0]["hidden_sp"] - out[0]["hidden"]).abs().max().item()
+    assert err <= 0.02 * out[0]["hidden"].abs().max().item(), err
     ref_small = out[0]["small_nccl"]
     err = (out[0]["small_fused"] - ref_small).abs().max().item()
     assert err <= 0.02 * ref_small.abs().max().item(), err
