@@ -61,10 +61,17 @@ int k8v4_wq_gemm_limbs(const void* w, const void* wscale, const void* x, const v
                        void* limb_buf, int M, int N, int K, int ldo, int split, cudaStream_t st);
 int k8v4_wq_gemm_ctas(int mode, int M, int N, int K, int split);
 int k8v4_silu_mul(const void* gu, void* y, void* yq, float* yscale, int rows, int inter, cudaStream_t st);
+int k8v4_silu_mul_f32(float* gu, void* y, int rows, int inter, cudaStream_t st);
 int k8v4_quant_rows(const void* x, void* q, float* scale, int rows, int n, cudaStream_t st);
 int k8v4_embed_int8(const int64_t* ids, const void* codes, const void* scales, void* out, int T, int n,
                     int64_t start, int64_t rows, cudaStream_t st);
 int k8v4_splitk_finish(float* ws, const void* residual, void* out, int64_t total, int zero_ws, cudaStream_t st);
+int k8v4_gemv_w4_max_rows();
+int k8v4_gemv_w4_allreduce(const void* w, const void* wscale, const void* x, float* ws_mc, unsigned long long* flag_mc,
+                           int M, int N, int K, int ldx, int ldo, cudaStream_t st);
+int k8v4_gemv_w4_ctas(int M, int N, int K);
+int k8v4_gemv_w4(const void* w, const void* wscale, const void* x, float* ws, int M, int N, int K, int ldx, int ldo,
+                 cudaStream_t st);
 int k8v4_int8_dequant(const void* q, const void* scale, void* out, int N, int K, cudaStream_t st);
 int k8v4_argmax(const void* logits, int rows, int vocab, int64_t ld, int64_t offset, float* best_val,
                 int64_t* best_idx, cudaStream_t st);
@@ -279,6 +286,19 @@ static at::Tensor limb_buffer(const at::Tensor& x, int64_t M, int64_t N, int64_t
   return at::empty({bytes}, x.options().dtype(at::kByte));
 }
 
+// W4A16 calls of at most k8v4_gemv_w4_max_rows() rows that come with an fp32
+// workspace run as the decode GEMV (gemv_w4.cu: weights streamed once through
+// registers, dp4a over two int8 limbs of each activation), whose sums land in
+// the workspace like a split-K GEMM's. K8V4_DECODE_GEMV=0 keeps them on the
+// tcgen05 path.
+static bool gemv_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("K8V4_DECODE_GEMV");
+    return !(v && (v[0] == '0' || v[0] == 'n' || v[0] == 'N' || v[0] == 'f' || v[0] == 'F'));
+  }();
+  return on;
+}
+
 // mode 0: W4A16 (x bf16), 1: W4A8 (x int8 + xscale), 2: W8A8 (w int8 [N,K] + per-row scale).
 void wq_gemm(int64_t mode, const at::Tensor& w, const at::Tensor& wscale, const at::Tensor& x,
              const c10::optional<at::Tensor>& xscale, const c10::optional<at::Tensor>& residual, at::Tensor& out,
@@ -326,6 +346,16 @@ void wq_gemm(int64_t mode, const at::Tensor& w, const at::Tensor& wscale, const 
     wsp = ws->data_ptr<float>();
   }
   c10::cuda::CUDAGuard g(x.device());
+  if (mode == 0 && M <= k8v4_gemv_w4_max_rows() && gemv_enabled() && ws.has_value() && ws->is_cuda() &&
+      ws->scalar_type() == at::kFloat && ws->is_contiguous() && ws->numel() >= M * N) {
+    float* wsg = ws->data_ptr<float>();
+    check_rc(k8v4_gemv_w4(w.data_ptr(), wscale.data_ptr(), x.data_ptr(), wsg, (int)M, (int)N, (int)K, (int)K,
+                          (int)N, cur_stream()),
+             "gemv_w4");
+    if (finish)  // else the sums stay in ws for a consumer that finishes them
+      check_rc(k8v4_splitk_finish(wsg, res, out.data_ptr(), M * N, 1, cur_stream()), "splitk_finish");
+    return;
+  }
   const float* xs = (mode == 0) ? nullptr : xscale->data_ptr<float>();
   at::Tensor limbs = mode == 0 ? limb_buffer(x, M, N, K) : at::Tensor();
   if (limbs.defined() && limbs.numel() > 0) {
@@ -425,6 +455,18 @@ void silu_mul(const at::Tensor& gu, const c10::optional<at::Tensor>& y, const c1
   check_rc(k8v4_silu_mul(gu.data_ptr(), yp, qp, sp, (int)rows, (int)inter, cur_stream()), "silu_mul");
 }
 
+// y = silu(gate) * up from the gate/up projection's fp32 sums, which are zeroed.
+void silu_mul_f32(at::Tensor& sums, at::Tensor& y) {
+  check_contig(sums, "sums");
+  check_contig(y, "y");
+  TORCH_CHECK(sums.scalar_type() == at::kFloat && sums.dim() == 2 && sums.size(1) % 2 == 0, "sums fp32 [T, 2I]");
+  const int64_t rows = sums.size(0), inter = sums.size(1) / 2;
+  TORCH_CHECK(y.numel() == rows * inter && y.scalar_type() == at::kBFloat16, "y bf16 [T, I]");
+  c10::cuda::CUDAGuard g(sums.device());
+  check_rc(k8v4_silu_mul_f32(sums.data_ptr<float>(), y.data_ptr(), (int)rows, (int)inter, cur_stream()),
+           "silu_mul_f32");
+}
+
 void quant_rows(const at::Tensor& x, at::Tensor& q, at::Tensor& scale) {
   check_contig(x, "x");
   check_contig(q, "q");
@@ -508,6 +550,13 @@ void wq_gemm_allreduce(int64_t mode, const at::Tensor& w, const at::Tensor& wsca
                 "W4A8 takes int8 activations + fp32 scales");
   }
   c10::cuda::CUDAGuard g(x.device());
+  if (mode == 0 && M <= k8v4_gemv_w4_max_rows() && gemv_enabled()) {
+    check_rc(k8v4_gemv_w4_allreduce(w.data_ptr(), wscale.data_ptr(), x.data_ptr(), reinterpret_cast<float*>(ws_mc),
+                                    reinterpret_cast<unsigned long long*>(flag_mc), (int)M, (int)N, (int)K, (int)K,
+                                    (int)N, cur_stream()),
+             "gemv_w4_allreduce");
+    return;
+  }
   at::Tensor limbs = mode == 0 ? limb_buffer(x, M, N, K) : at::Tensor();
   check_rc(k8v4_wq_gemm_allreduce((int)mode, w.data_ptr(), wscale.data_ptr(), x.data_ptr(),
                                   mode == 0 ? nullptr : xscale->data_ptr<float>(), reinterpret_cast<float*>(ws_mc),
@@ -605,7 +654,9 @@ void rmsnorm_sp(const c10::optional<at::Tensor>& slots, int64_t world, int64_t s
            "rmsnorm_sp");
 }
 
+// CTAs (= signals per rank) of one wq_gemm_allreduce call.
 int64_t wq_gemm_ctas(int64_t mode, int64_t M, int64_t N, int64_t K, int64_t split) {
+  if (mode == 0 && M <= k8v4_gemv_w4_max_rows() && gemv_enabled()) return k8v4_gemv_w4_ctas((int)M, (int)N, (int)K);
   return k8v4_wq_gemm_ctas((int)mode, (int)M, (int)N, (int)K, (int)split);
 }
 
@@ -767,6 +818,7 @@ TORCH_LIBRARY(k8v4, m) {
       "Tensor w, int rows, float eps, int rs_flag, int rs_target, int y, int yq, int ys, int row0, bool mc, "
       "int ag_sig) -> ()");
   m.def("silu_mul(Tensor gate_up, Tensor(a!)? y, Tensor(b!)? yq, Tensor(c!)? yscale) -> ()");
+  m.def("silu_mul_f32(Tensor(a!) sums, Tensor(b!) y) -> ()");
   m.def("quant_rows(Tensor x, Tensor(a!) q, Tensor(b!) scale) -> ()");
   m.def("int8_dequant(Tensor q, Tensor scale, Tensor(a!) out) -> ()");
   m.def("embed_int8(Tensor ids, Tensor codes, Tensor scales, Tensor(a!) out, int start) -> ()");
@@ -801,6 +853,7 @@ TORCH_LIBRARY_IMPL(k8v4, CUDA, m) {
   m.impl("wq_gemm_allreduce", &wq_gemm_allreduce);
   m.impl("rmsnorm", &rmsnorm);
   m.impl("silu_mul", &silu_mul);
+  m.impl("silu_mul_f32", &silu_mul_f32);
   m.impl("quant_rows", &quant_rows);
   m.impl("int8_dequant", &int8_dequant);
   m.impl("embed_int8", &embed_int8);

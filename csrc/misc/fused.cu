@@ -227,6 +227,39 @@ __global__ void __launch_bounds__(256) silu_mul_wide_kernel(const __nv_bfloat16*
   store8(y + row * inter + c, o);
 }
 
+// The same from the gate/up projection's fp32 sums (a decode GEMV or split-K
+// accumulator, [T, 2I]): each sum is rounded to bf16 first, as the GEMM's own
+// bf16 output would be, and the accumulator is zeroed behind the read for
+// the next GEMM.
+__global__ void __launch_bounds__(256) silu_mul_f32_wide_kernel(float* __restrict__ gu, __nv_bfloat16* __restrict__ y,
+                                                                int inter, int64_t total) {
+  pdl_trigger();
+  pdl_wait();  // the sums come from the previous kernel
+  const int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (v >= total) return;
+  const int per_row = inter / 8;
+  const int64_t row = v / per_row;
+  const int c = (int)(v % per_row) * 8;
+  float4* gp = reinterpret_cast<float4*>(gu + row * 2 * inter + c);
+  float4* up = reinterpret_cast<float4*>(gu + row * 2 * inter + inter + c);
+  const float4 g0 = gp[0], g1 = gp[1], u0 = up[0], u1 = up[1];
+  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+  gp[0] = z;
+  gp[1] = z;
+  up[0] = z;
+  up[1] = z;
+  const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+  const float u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+  float o[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float gb = __bfloat162float(__float2bfloat16_rn(g[j]));
+    const float ub = __bfloat162float(__float2bfloat16_rn(u[j]));
+    o[j] = gb / (1.f + __expf(-gb)) * ub;
+  }
+  store8(y + row * inter + c, o);
+}
+
 // Row-wise int8 quantization of bf16 rows.
 template <int VPT>
 __global__ void __launch_bounds__(kThreads) quant_rows_kernel(const __nv_bfloat16* __restrict__ x, int8_t* q, float* scale,
@@ -518,6 +551,16 @@ extern "C" int k8v4_silu_mul(const void* gu, void* y, void* yq, float* yscale, i
   }
   K8V4_VPT_DISPATCH(inter, silu_mul_kernel, reinterpret_cast<const __nv_bfloat16*>(gu),
                     reinterpret_cast<__nv_bfloat16*>(y), reinterpret_cast<int8_t*>(yq), yscale, inter);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+// y = silu(gate) * up from fp32 sums [rows, 2 inter] that are zeroed after reading.
+extern "C" int k8v4_silu_mul_f32(float* gu, void* y, int rows, int inter, cudaStream_t st) {
+  if (rows <= 0) return 0;
+  if (inter % 8) return 1;
+  const int64_t total = (int64_t)rows * (inter / 8);
+  launch_k(silu_mul_f32_wide_kernel, dim3((unsigned)((total + 255) / 256)), dim3(256), 0, st, gu,
+           reinterpret_cast<__nv_bfloat16*>(y), inter, total);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 

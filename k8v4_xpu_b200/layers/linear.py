@@ -94,7 +94,7 @@ class Int4Linear:
         rows = x.shape[0]
         if split is None:
             split = self.split(rows, ws)
-        if defer and split > 1:
+        if defer and (split > 1 or ops.takes_gemv(ops.W4A16, rows, ws)):
             ops.wq_gemm(ops.W4A16, self.qweight, self.scales, x, out=out, ws=ws, split=split, finish=False)
             return ws[: rows * self.out_features].view(rows, self.out_features)
         return ops.wq_gemm(ops.W4A16, self.qweight, self.scales, x, out=out, ws=ws, split=split)

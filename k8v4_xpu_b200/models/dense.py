@@ -317,7 +317,8 @@ class DenseModel:
             with stage(tag + ".post_norm"):
                 h = ops.rmsnorm(x, L.post_norm, cfg.rms_eps, residual=residual, sync=sync_o)
             with stage(tag + ".gate_up"):
-                gu = L.gate_up(h, ws=splitk_ws)
+                # decode GEMV: the fp32 sums stay in the workspace for silu_mul
+                gu = L.gate_up(h, ws=splitk_ws, defer=True)
             with stage(tag + ".act"):
                 act = ops.silu_mul(gu)
             with stage(tag + ".down"):

@@ -171,8 +171,23 @@ def wq_gemm(mode: int, w: torch.Tensor, wscale: torch.Tensor, x: torch.Tensor, x
     if x.shape[0] == 0:
         return out
     torch.ops.k8v4.wq_gemm(mode, w, wscale, x, xscale, residual, out, ws, split, finish)
-    _count(2 if split > 1 and finish else 1)
+    if takes_gemv(mode, x.shape[0], ws):
+        _count(2 if finish else 1)  # the GEMV, then the finish unless a consumer does it
+    else:
+        _count(2 if split > 1 and finish else 1)
     return out
+
+
+GEMV_MAX_ROWS = 4
+
+
+def takes_gemv(mode: int, rows: int, ws) -> bool:
+    """Whether a GEMM call runs as the decode GEMV (``csrc/gemm/gemv_w4.cu``):
+    W4A16 at most 4 token rows with an fp32 workspace, unless
+    ``K8V4_DECODE_GEMV=0``. Mirrors the dispatch in ``csrc/bindings.cpp``."""
+    if mode != W4A16 or not 1 <= rows <= GEMV_MAX_ROWS or ws is None:
+        return False
+    return os.environ.get("K8V4_DECODE_GEMV", "1")[:1] not in ("0", "n", "N", "f", "F")
 
 
 # ------------------------------------------------------------------- fused
@@ -263,8 +278,19 @@ def int8_dequant(q, scale, out):
 
 
 def silu_mul(gu, out=None, quant=False):
+    """silu(gate) * up of ``gu = [gate | up]`` (bf16, or int8 + per-row scale
+    with ``quant``). ``gu`` may be the fp32 sums a decode GEMV left in the
+    split-K workspace (bf16 output only): they are consumed and zeroed."""
     require()
     rows, inter = gu.shape[0], gu.shape[1] // 2
+    if gu.dtype == torch.float32:
+        if quant:
+            raise ValueError("silu_mul of fp32 sums writes bf16 only")
+        if out is None:
+            out = torch.empty((rows, inter), dtype=torch.bfloat16, device=gu.device)
+        torch.ops.k8v4.silu_mul_f32(gu, out)
+        _count()
+        return out
     if quant:
         q = torch.empty((rows, inter), dtype=torch.int8, device=gu.device)
         s = torch.empty(rows, dtype=torch.float32, device=gu.device)

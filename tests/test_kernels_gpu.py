@@ -177,6 +177,44 @@ def test_w4a16_limb_path(M, split):
         assert torch.equal(out[M - 1].cpu(), torch.zeros(N, dtype=torch.bfloat16))
 
 
+@pytest.mark.parametrize("M", [1, 2, 3, 4])
+@pytest.mark.parametrize("shape", [(34816, 5120), (5120, 17408), (384, 1152)])
+def test_w4a16_decode_gemv(M, shape):
+    """Decode GEMV (dp4a over two int8 limbs per 64 activations, persistent
+    warp runs): within bf16 output rounding of the fp32 reference, with an
+    outlier 60x the typical value, a tiny value, an all-zero row; the sums
+    land in the fp32 workspace (deferred) or are finished to bf16, and the
+    finish leaves the workspace zero for the next call."""
+    N, K = shape
+    qw, sc = _int4_weights(N, K, 50 + M)
+    x = torch.randn(M, K, generator=_gen(51))
+    x[:, 9] = 60.0
+    x[0, 200] = -1e-3
+    if M > 2:
+        x[M - 1] = 0.0
+    x = x.bfloat16()
+    ref = gptq.w4a16_ref(x, qw, sc)
+    ws = torch.zeros(M * N, dtype=torch.float32, device=DEV)
+    qd, sd, xd = qw.to(DEV), sc.to(DEV), x.to(DEV)
+    out = ops.wq_gemm(ops.W4A16, qd, sd, xd, ws=ws, split=1)
+    torch.cuda.synchronize()
+    assert ops.status() == 0
+    err = (out.float().cpu() - ref).abs().max().item()
+    assert err <= 4e-3 * ref.abs().max().item() + 1e-4, err
+    assert torch.count_nonzero(ws).item() == 0
+    if M > 2:
+        assert torch.equal(out[M - 1].cpu(), torch.zeros(N, dtype=torch.bfloat16))
+    # deferred: the fp32 sums stay in the workspace for a fused consumer
+    ops.wq_gemm(ops.W4A16, qd, sd, xd, ws=ws, split=3, finish=False)
+    torch.cuda.synchronize()
+    sums = ws.view(M, N).cpu()
+    assert (sums - ref).abs().max().item() <= 2e-3 * ref.abs().max().item() + 1e-4
+    # the tcgen05 path on the same call agrees within output rounding
+    tc = ops.wq_gemm(ops.W4A16, qd, sd, xd)
+    torch.cuda.synchronize()
+    assert (tc.float() - out.float()).abs().max().item() <= 8e-3 * ref.abs().max().item() + 1e-4
+
+
 @pytest.mark.parametrize("M", [1, 28, 130, 300])
 def test_w4a8_gemm(M):
     N, K = 256, 1280

@@ -63,6 +63,7 @@ PROMPTS = [list(range(3, 3 + 150)), list(range(100, 100 + 45))]
 TP_MODEL = ModelConfig(name="tp-test", num_layers=2, hidden=1024, num_heads=24, num_kv_heads=4, head_dim=128,
                        intermediate=2048, vocab=8192, max_position=8192)
 SMALL_PROMPTS = [list(range(3, 3 + 40)), list(range(100, 100 + 17))]
+TINY_PROMPTS = [[5, 6], [9], [11]]
 
 
 def _worker(rank, world, port, q):
@@ -103,6 +104,15 @@ def _worker(rank, world, port, q):
         for _ in range(3):  # repeated uses: the running signal counts must keep matching
             caches = [torch.zeros(64, m.layout.page_bytes, dtype=torch.uint8, device=dev) for _ in m.layers]
             res["small_fused"] = m.forward(small, caches).float().cpu()
+        # at most 4 rows the row-parallel GEMMs run as the decode GEMV with its
+        # multicast all-reduce epilogue
+        tiny = _prefill_inputs(TINY_PROMPTS, dev)
+        caches = [torch.zeros(64, m.layout.page_bytes, dtype=torch.uint8, device=dev) for _ in m.layers]
+        res["tiny_fused"] = m.forward(tiny, caches).float().cpu()
+        m.fused_ar, far = None, m.fused_ar
+        caches = [torch.zeros(64, m.layout.page_bytes, dtype=torch.uint8, device=dev) for _ in m.layers]
+        res["tiny_nccl"] = m.forward(tiny, caches).float().cpu()
+        m.fused_ar = far
         torch.cuda.synchronize(dev)
         res["fused_calls"] = m.fused_ar.calls
         res["kv_heads"] = m.shape.kv_heads_of(rank, TP_MODEL.num_kv_heads)
@@ -152,7 +162,12 @@ def test_tp_matches_tp1(world):
         assert torch.equal(out[0]["hidden"], out[r]["hidden"]), r
         assert torch.equal(out[0]["small_fused"], out[r]["small_fused"]), r
         assert out[0]["gen"] == out[r]["gen"], r
-    assert out[0]["fused_calls"] == 3 * 2 * TP_MODEL.num_layers
+    assert out[0]["fused_calls"] == 4 * 2 * TP_MODEL.num_layers
+    for r in range(1, world):
+        assert torch.equal(out[0]["tiny_fused"], out[r]["tiny_fused"]), r
+    ref_tiny = out[0]["tiny_nccl"]
+    err = (out[0]["tiny_fused"] - ref_tiny).abs().max().item()
+    assert err <= 0.02 * ref_tiny.abs().max().item(), err
     assert out[0]["comm_mode"] == "fused" and out[0]["prefill_mode"] == "sp"
     # sequence-parallel prefill: 4 fused GEMMs per layer, ranks agree exactly,
     # and it matches the NCCL all-reduce path up to bf16 partial sums
