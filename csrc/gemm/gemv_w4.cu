@@ -1,4 +1,5 @@
-// Decode GEMV for GPTQ int4 weights at 1 to 4 token rows (W4A16 numerics):
+// Decode GEMV for GPTQ int4 weights at 1 to 4 token rows (W4A16 numerics;
+// the dispatch sends single-row calls here, see k8v4_gemv_w4_max_rows):
 //   ws[t, n] += sum_k x[t, k] * scale[k / 128, n] * (q[k, n] - 8)
 //
 // At a handful of token rows a decode projection is a stream of int4 weights
@@ -7,7 +8,10 @@
 // format first, and at 1 token row its converter / MMA / accumulator pipeline
 // moves ~8 KB of weights per CTA every ~0.4 us, about 0.3 of HBM. This kernel
 // streams the weights once through registers instead and does the products on
-// the integer pipe:
+// the integer pipe. (Two other forms measured slower at one row: packed fp16
+// FMAs on the unpacked codes, 34.9 us for the gate/up shape, being
+// instruction bound; the same fed by a 32-stage TMA ring with 12 compute
+// warps, 43.0 us.)
 //
 //   * work unit = 128 output features x 64 k (8 packed rows of the GPTQ
 //     [K/8, N] int32 layout); a lane owns 4 features and loads one 16-byte
@@ -251,8 +255,13 @@ static int dispatch(const void* w, const void* wscale, const void* x, float* ws,
 }  // namespace gemv
 }  // namespace k8v4
 
-// Rows up to which the decode GEMV serves a W4A16 call.
-extern "C" int k8v4_gemv_w4_max_rows() { return 4; }
+// Rows up to which the decode GEMV serves a W4A16 call. Measured (graph-timed,
+// L2 flushed, 27B shapes): at one row the GEMV beats the tcgen05 path
+// (gate/up 28.7 vs 43.0 us, down 20.5 vs 32.6 us); at four rows the integer
+// dot-product pipe (~16-21 dp4a per clock per SM here) makes it slower
+// (gate/up 71.6 vs 45.1 us), so wider calls stay on the tensor cores. The
+// kernel itself takes up to 4 rows.
+extern "C" int k8v4_gemv_w4_max_rows() { return 1; }
 
 // ws[t, n] (row stride ldo, fp32, zero on entry) += x[t, :] (bf16, row stride
 // ldx) times the GPTQ int4 weights [K/8, N] with fp16 group scales [K/128, N].

@@ -56,8 +56,10 @@ struct DecodeParams {
 
 #ifdef K8V4_TRACE
 // Timeline of CTA (0,0,0) (trace builds only): rows = 0 producer issued,
-// 1 converters done, 2 QK issued, 3 softmax done (p_full), 4 PV issued.
-__device__ uint64_t g_attn_trace[5 * 256];
+// 1 converters done, 2 QK issued, 3 softmax done (p_full), 4 PV issued;
+// keys-on-lanes kernel only: 5 softmax read S, 6 softmax past the maxima
+// barrier, 7 softmax past the P^T buffer wait.
+__device__ uint64_t g_attn_trace[8 * 256];
 #define K8V4_ATRACE(row, idx)                                                             \
   do {                                                                                    \
     if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (idx) < 256)             \
@@ -585,6 +587,494 @@ __global__ void __launch_bounds__(DCfg<NPAD>::NTHREADS, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Keys on TMEM lanes, query rows as the MMA N dimension (rows <= 16).
+//
+// With a handful of query rows per KV head (one decode token x GQA 6 at
+// c = 1), an MMA with the rows as M wastes most of its 128 lanes: QK and PV
+// of one 128-key tile then cost the tensor pipe ~800 cycles. Here the keys
+// (QK) and the head dims (PV) are M and the rows are N = 16:
+//
+//   S^T[key, row] = K_tile (A, smem, K-major) x Q8^T (B, smem)  kind::i8, N = 16
+//   softmax       : thread = key (4 warps = 128 TMEM lanes) holding its 16
+//                   row scores; per-row tile maxima through redux.sync on an
+//                   order-preserving integer image of the floats, then shared
+//                   memory across the 4 warps; lazy rescale (tau = 8, log2)
+//   P^T           : each thread writes its key's fp16 probabilities into the
+//                   K-major B operand [16 rows x 128 keys] in shared memory
+//   O^T[dim, row] += V^T (A, the converted fp16 tile, MN-major) x P^T (B)
+//                   kind::f16, N = 16; O^T stays in TMEM (16 columns)
+//
+// so a tile costs the tensor pipe ~100 cycles. The row sums stay per thread
+// until the epilogue. The producer, the V converters and the (m, l, O)
+// partial layout are the rows-on-lanes kernel's (decode_attn_kernel), so
+// decode_combine merges either kernel's splits.
+template <int NPAD>
+struct TCfg {
+  static constexpr int STAGES = 4;
+  static constexpr int NVT = 3;
+  static constexpr int NCONV = K8V4_DECODE_NCONV;
+  static constexpr int NWARPS = 8 + (NCONV - 2);
+  static constexpr int NTHREADS = 32 * NWARPS;
+  static constexpr int Q_BYTES = NPAD * 128;         // Q8 rows, K-major SW128 (NPAD % 8 == 0)
+  static constexpr int P_ATOM = NPAD * 128;          // 64 keys of every row (fp16), K-major SW128
+  static constexpr int P_BYTES = 2 * P_ATOM;         // one P^T buffer: 128 keys
+  static constexpr uint32_t COL_S = 0, COL_O = 2 * NPAD;
+  static constexpr int TMEM_COLS = (3 * NPAD <= 32) ? 32 : (3 * NPAD <= 64 ? 64 : 128);
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_VT = OFF_K + STAGES * K_TILE_BYTES;
+  static constexpr int OFF_Q = OFF_VT + NVT * VT_BYTES;
+  static constexpr int OFF_P = OFF_Q + ((Q_BYTES + 1023) / 1024) * 1024;
+  static constexpr int OFF_VS = OFF_P + 2 * P_BYTES;
+  static constexpr int OFF_KS = OFF_VS + STAGES * VS_TILE_BYTES;
+  static constexpr int OFF_MISC = OFF_KS + NVT * TILE * 4;
+  // misc: barriers (512 B), q_scale / row_end [NPAD], tile maxima [2][4][NPAD], row sums [4][NPAD]
+  static constexpr int SMEM_BYTES = 1024 + OFF_MISC + 512 + 2 * NPAD * 4 + 2 * 4 * NPAD * 4 + 4 * NPAD * 4;
+  static_assert(NPAD % 16 == 0 && NPAD <= 32, "rows as MMA N");
+  static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
+};
+
+// Order-preserving map float -> int32 (and back): redux.sync works on integers.
+__device__ __forceinline__ int f2ord(float f) {
+  const int i = __float_as_int(f);
+  return i >= 0 ? i : (i ^ 0x7FFFFFFF);
+}
+__device__ __forceinline__ float ord2f(int i) { return __int_as_float(i >= 0 ? i : (i ^ 0x7FFFFFFF)); }
+__device__ __forceinline__ int redux_max(int v) {
+  int r;
+  asm volatile("redux.sync.max.s32 %0, %1, 0xffffffff;" : "=r"(r) : "r"(v));
+  return r;
+}
+
+template <int NPAD>
+__global__ void __launch_bounds__(TCfg<NPAD>::NTHREADS, 1)
+    decode_attn_t_kernel(const __grid_constant__ KVTileMaps tm, const DecodeParams p) {
+  pdl_trigger();
+  pdl_wait();  // Q, the KV pages and the block table may come from the previous kernels
+  using C = TCfg<NPAD>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* sm = align_smem_1024(smem_raw);
+  uint8_t* sK = sm + C::OFF_K;
+  uint8_t* sVT = sm + C::OFF_VT;
+  uint8_t* sQ = sm + C::OFF_Q;
+  uint8_t* sP = sm + C::OFF_P;
+  uint8_t* sVS = sm + C::OFF_VS;
+  float* sKS = reinterpret_cast<float*>(sm + C::OFF_KS);
+  uint8_t* misc = sm + C::OFF_MISC;
+  uint64_t* kv_full = reinterpret_cast<uint64_t*>(misc);
+  uint64_t* kv_empty = kv_full + C::STAGES;  // QK commit + converter warps
+  uint64_t* s_full = kv_empty + C::STAGES;   // [2] QK done
+  uint64_t* s_empty = s_full + 2;            // [2] softmax read S
+  uint64_t* p_full = s_empty + 2;            // [2] softmax wrote P^T (and rescaled O)
+  uint64_t* pv_done = p_full + 2;            // [2] PV that read P^T[b] done (O current)
+  uint64_t* v_full = pv_done + 2;            // [NVT] V tile converted
+  uint64_t* vt_empty = v_full + C::NVT;      // [NVT] PV that read the V tile done
+  uint64_t* ks_full = vt_empty + C::NVT;     // [NVT] k scales copied out
+  uint64_t* done_bar = ks_full + C::NVT;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  float* q_scale = reinterpret_cast<float*>(misc + 512);  // [NPAD] q scale * softmax scale (log2)
+  int* row_end = reinterpret_cast<int*>(q_scale + NPAD);  // [NPAD] visible keys per row
+  float* mx_w = reinterpret_cast<float*>(row_end + NPAD); // [2][4][NPAD] per-warp tile maxima
+  float* l_w = mx_w + 2 * 4 * NPAD;                        // [4][NPAD] per-warp row sums
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int split = blockIdx.x, h = blockIdx.y + p.head_offset, seq = blockIdx.z;
+  const int hl = blockIdx.y;
+  const int qb = p.cu_q[seq], q_len = p.cu_q[seq + 1] - qb;
+  const int R = q_len * p.gqa;  // real rows (<= NPAD)
+  const int seq_len = p.seq_lens[seq];
+  const int n_pages = (seq_len + PAGE - 1) / PAGE;
+  const int n_tiles_all = (n_pages + TILE_PAGES - 1) / TILE_PAGES;
+  const int tile_beg = (int)(((int64_t)n_tiles_all * split) / p.nsplit);
+  const int tile_end = (int)(((int64_t)n_tiles_all * (split + 1)) / p.nsplit);
+  const int nt = tile_end - tile_beg;
+  const int32_t* bt = p.block_table + (int64_t)seq * p.bt_stride;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1 + C::NCONV);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&s_empty[b], 4);
+      mbar_init(&p_full[b], 4);
+      mbar_init(&pv_done[b], 1);
+    }
+    for (int v = 0; v < C::NVT; ++v) {
+      mbar_init(&v_full[v], C::NCONV);
+      mbar_init(&vt_empty[v], 1);
+      mbar_init(&ks_full[v], 4);
+    }
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  // ---- prologue: zero the Q8 tile, then quantize the real rows (K-major SW128)
+  for (int i = threadIdx.x; i < C::Q_BYTES / 16; i += C::NTHREADS)
+    reinterpret_cast<uint4*>(sQ)[i] = make_uint4(0, 0, 0, 0);
+  if (threadIdx.x < NPAD) {
+    q_scale[threadIdx.x] = 0.f;
+    row_end[threadIdx.x] = 0;
+  }
+  __syncthreads();
+  for (int r = warp; r < R; r += C::NWARPS) {
+    const int t = r / p.gqa, g = r % p.gqa;
+    const __nv_bfloat16* src = p.q + ((int64_t)(qb + t) * p.hq_total + (int64_t)h * p.gqa + g) * D + lane * 4;
+    const uint2 raw = *reinterpret_cast<const uint2*>(src);
+    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+    const float2 a = __bfloat1622float2(h2[0]), b2 = __bfloat1622float2(h2[1]);
+    const float x[4] = {a.x, a.y, b2.x, b2.y};
+    float amax = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
+    amax = warp_max(amax);
+    const float sc = amax / 127.f;
+    const float inv = sc > 0.f ? 1.f / sc : 0.f;
+    uint32_t w = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int qi = (int)fminf(fmaxf(rintf(x[j] * inv), -127.f), 127.f);
+      w |= ((uint32_t)(uint8_t)(int8_t)qi) << (8 * j);
+    }
+    *reinterpret_cast<uint32_t*>(sQ + sw128_offset(r, lane >> 2) + (lane & 3) * 4) = w;
+    if (lane == 0) {
+      q_scale[r] = sc * p.sm_scale_log2;
+      row_end[r] = p.q_ends ? p.q_ends[qb + t] : (seq_len - q_len + t + 1);
+    }
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    // (as in decode_attn_kernel) lane i holds page i of a tile, read one tile
+    // ahead; consecutive pages move in two TMA boxes, others page by page
+    if (lane == 0) {
+      prefetch_tmap(&tm.page);
+      prefetch_tmap(&tm.k8);
+      prefetch_tmap(&tm.vs8);
+    }
+    auto page_of = [&](int jt) -> int64_t {
+      const int pg = (tile_beg + jt) * TILE_PAGES + lane;
+      return (jt < nt && lane < TILE_PAGES && pg < n_pages) ? (int64_t)bt[pg] : 0;
+    };
+    int64_t next_page = page_of(0);
+    int issued = 0;
+    for (int j = 0; j < nt; ++j) {
+      const int s = j % C::STAGES;
+      const int64_t page = next_page;
+      next_page = page_of(j + 1);
+      if (j >= C::STAGES && !mbar_wait_all(&kv_empty[s], ((j / C::STAGES) - 1) & 1, abort_flag, 221)) break;
+      const int pg0 = (tile_beg + j) * TILE_PAGES;
+      const int npg = min(TILE_PAGES, n_pages - pg0);
+      const int64_t page0 = __shfl_sync(0xffffffffu, page, 0);
+      if (__all_sync(0xffffffffu, lane >= npg || page == page0 + lane)) {
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&kv_full[s], TILE_PAGES * (K_BYTES + VS_BYTES));
+          tma_load_4d(sK + s * K_TILE_BYTES, &tm.k8, &kv_full[s], 0, 0, h, (int)page0);
+          tma_load_3d(sVS + s * VS_TILE_BYTES, &tm.vs8, &kv_full[s], 0, h, (int)page0);
+        }
+      } else {
+        if (lane == 0) mbar_arrive_expect_tx(&kv_full[s], npg * (K_BYTES + VS_BYTES));
+        __syncwarp();
+        if (lane < npg) {
+          const int64_t run = page * p.hkv + h;
+          tma_load_3d(sK + s * K_TILE_BYTES + lane * K_BYTES, &tm.page, &kv_full[s], 0, 0, (int)run);
+          bulk_load(sVS + s * VS_TILE_BYTES + lane * VS_BYTES, p.cache + run * HEAD_BYTES + VS_OFF, VS_BYTES,
+                    &kv_full[s]);
+        }
+      }
+      if (lane == 0) K8V4_ATRACE(0, j);
+      ++issued;
+    }
+    if (lane == 0 && *abort_flag)
+      for (int j = issued - 1; j >= 0 && j >= issued - C::STAGES; --j)
+        mbar_wait_drain(&kv_full[j % C::STAGES], (j / C::STAGES) & 1);
+  } else if (warp == 1) {
+    // ----------------------------------------------------------------- MMA
+    if (lane == 0 && nt > 0) {
+      const uint32_t id_qk = idesc_s8(128, NPAD);                 // M = keys, N = rows
+      const uint32_t id_pv = idesc_f16(128, NPAD, true, false);   // M = dims (MN-major V), N = rows
+      const uint32_t q_base = smem_u32(sQ);
+      const uint32_t p_base = smem_u32(sP);
+      int jq = 0, jp = 0, idle = 0;
+      uint64_t t_idle = globaltimer_ns();
+      while (jp < nt) {
+        bool progressed = false;
+        if (jq < nt) {
+          const int s = jq % C::STAGES, b = jq & 1;
+          if (mbar_test_wait(&kv_full[s], (jq / C::STAGES) & 1) &&
+              (jq < 2 || mbar_test_wait(&s_empty[b], ((jq >> 1) - 1) & 1))) {
+            tc_fence_after();
+            const uint32_t k_base = smem_u32(sK + s * K_TILE_BYTES);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              mma_i8(tmem + C::COL_S + b * NPAD, sdesc_sw128(k_base + kk * 32, 16, 1024),
+                     sdesc_sw128(q_base + kk * 32, 16, 1024), id_qk, kk > 0 ? 1u : 0u);
+            mma_commit(&s_full[b]);
+            mma_commit(&kv_empty[s]);
+            K8V4_ATRACE(2, jq);
+            ++jq;
+            progressed = true;
+          }
+        }
+        if (jp < jq) {
+          const int b = jp & 1, vb = jp % C::NVT;
+          if (mbar_test_wait(&p_full[b], (jp >> 1) & 1) && mbar_test_wait(&v_full[vb], (jp / C::NVT) & 1)) {
+            tc_fence_after();
+            const uint32_t vt_base = smem_u32(sVT + vb * VT_BYTES);
+            const uint32_t pb = p_base + b * C::P_BYTES;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+              mma_f16(tmem + C::COL_O, sdesc_sw128(vt_base + kk * 2048, VT_LBO, 1024),
+                      sdesc_sw128(pb + (kk >> 2) * C::P_ATOM + (kk & 3) * 32, 16, 1024), id_pv,
+                      (jp > 0 || kk > 0) ? 1u : 0u);
+            mma_commit(&pv_done[b]);
+            mma_commit(&vt_empty[vb]);
+            K8V4_ATRACE(4, jp);
+            ++jp;
+            progressed = true;
+          }
+        }
+        if (progressed) {
+          idle = 0;
+        } else {
+          __nanosleep(20);
+          if (++idle == 1) t_idle = globaltimer_ns();
+          if ((idle & 63) == 0) {
+            if (*abort_flag) break;
+            if (globaltimer_ns() - t_idle > K8V4_WAIT_LIMIT_NS) {
+              *abort_flag = 1;
+              record_error(kErrMbarTimeout, 223);
+              break;
+            }
+          }
+        }
+      }
+      mma_commit(done_bar);
+      mbar_wait_drain(done_bar, 0);
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ------------------------------------------------- softmax (lane = key)
+    const int quad = warp - 4;
+    const int key = quad * 32 + lane;  // TMEM lane: key of the tile (S^T), head dim (O^T)
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const uint32_t tS = tmem + C::COL_S + lane_off, tO = tmem + C::COL_O + lane_off;
+    float qs[NPAD], m[NPAD], l[NPAD];
+    int rend[NPAD];
+#pragma unroll
+    for (int r = 0; r < NPAD; ++r) {
+      qs[r] = q_scale[r];
+      rend[r] = row_end[r];  // 0 past the real rows: no key visible
+      m[r] = -INFINITY;
+      l[r] = 0.f;
+    }
+    // this thread's key inside a P^T buffer (K-major SW128, 64-key atoms)
+    const int patom = (key >> 6) * C::P_ATOM, pchunk = (key & 63) >> 3, pbyte = (key & 7) * 2;
+    bool ok = true;
+    // Every softmax warp runs every iteration (the tile maxima meet at a
+    // named barrier); a failed wait only turns the work off.
+    for (int j = 0; j < nt; ++j) {
+      const int b = j & 1, vb = j % C::NVT;
+      if (ok && !mbar_wait_all(&s_full[b], (j >> 1) & 1, abort_flag, 224)) ok = false;
+      uint32_t sv[NPAD];
+      if (ok) {
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < NPAD; c += 16) tmem_ld16(tS + b * NPAD + c, *reinterpret_cast<uint32_t(*)[16]>(&sv[c]));
+        tmem_ld_wait();
+        tc_fence_before();
+      }
+      __syncwarp();
+      if (ok && lane == 0) mbar_arrive(&s_empty[b]);
+      if (quad == 0 && lane == 0) K8V4_ATRACE(5, j);
+      if (ok && !mbar_wait_all(&ks_full[vb], (j / C::NVT) & 1, abort_flag, 225)) ok = false;
+      const int keyg = (tile_beg + j) * TILE + key;
+      const float ks = ok ? sKS[vb * TILE + key] : 0.f;
+      float s[NPAD];
+#pragma unroll
+      for (int r = 0; r < NPAD; ++r)
+        if (r < R) s[r] = (ok && keyg < rend[r]) ? i2f_small(sv[r]) * (qs[r] * ks) : -INFINITY;
+      float* mxb = mx_w + b * 4 * NPAD;
+#pragma unroll
+      for (int r = 0; r < NPAD; ++r)
+        if (r < R) {
+          const int wm = redux_max(f2ord(s[r]));
+          if (lane == r) mxb[quad * NPAD + r] = ord2f(wm);
+        }
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // the four warps' maxima of tile j
+      if (quad == 0 && lane == 0) K8V4_ATRACE(6, j);
+      float alpha[NPAD];
+      bool moved = false;
+#pragma unroll
+      for (int r = 0; r < NPAD; ++r) {
+        alpha[r] = 1.f;
+        if (r < R) {
+          const float tmax = fmaxf(fmaxf(mxb[r], mxb[NPAD + r]), fmaxf(mxb[2 * NPAD + r], mxb[3 * NPAD + r]));
+          if (tmax > m[r] + RESCALE_TAU || (m[r] == -INFINITY && tmax > -INFINITY)) {
+            alpha[r] = (m[r] == -INFINITY) ? 0.f : ex2_approx(m[r] - tmax);
+            m[r] = tmax;
+            moved = true;
+          }
+          l[r] *= alpha[r];
+        }
+      }
+      // O^T holds PV(0..j-1) after PV(j-1): rescale its row columns when a max moved
+      // (`moved` is the same in every thread: all read the same maxima)
+      if (ok && j >= 1 && moved) {
+        if (!mbar_wait_all(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, 226)) {
+          ok = false;
+        } else {
+          tc_fence_after();
+          uint32_t ov[NPAD];
+#pragma unroll
+          for (int c = 0; c < NPAD; c += 16) tmem_ld16(tO + c, *reinterpret_cast<uint32_t(*)[16]>(&ov[c]));
+          tmem_ld_wait();
+#pragma unroll
+          for (int r = 0; r < NPAD; ++r) ov[r] = __float_as_uint(__uint_as_float(ov[r]) * alpha[r]);
+#pragma unroll
+          for (int c = 0; c < NPAD; c += 16) tmem_st16(tO + c, *reinterpret_cast<uint32_t(*)[16]>(&ov[c]));
+          tmem_st_wait();
+        }
+      }
+      // P^T[b] is free once the PV of tile j-2 finished
+      if (ok && j >= 2 && !mbar_wait_all(&pv_done[b], ((j >> 1) - 1) & 1, abort_flag, 227)) ok = false;
+      if (quad == 0 && lane == 0) K8V4_ATRACE(7, j);
+      if (ok) {
+        // rows past R are never read back (their O^T columns are ignored)
+        uint8_t* pt = sP + b * C::P_BYTES + patom;
+#pragma unroll
+        for (int r = 0; r < NPAD; ++r)
+          if (r < R) {
+            // rows with no visible key keep m = -inf: exponentiate against 0 (p = 0)
+            const float pr = ex2_approx(s[r] - (m[r] == -INFINITY ? 0.f : m[r]));
+            l[r] += pr;
+            *reinterpret_cast<__half*>(pt + sw128_offset(r, pchunk) + pbyte) = __float2half_rn(pr);
+          }
+        fence_async_smem();  // the tensor core reads P^T through the async proxy
+        tc_fence_before();
+      }
+      __syncwarp();
+      if (ok && lane == 0) {
+        mbar_arrive(&p_full[b]);
+        if (quad == 0) K8V4_ATRACE(3, j);
+      }
+    }
+    // ------------------------------------------------------------ epilogue
+    if (ok && nt > 0 && !mbar_wait_all(&pv_done[(nt - 1) & 1], ((nt - 1) >> 1) & 1, abort_flag, 228)) ok = false;
+#pragma unroll
+    for (int r = 0; r < NPAD; ++r)
+      if (r < R) {
+        const float ls = warp_sum(l[r]);
+        if (lane == 0) l_w[quad * NPAD + r] = ls;
+      }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    tc_fence_after();
+    uint32_t ov[NPAD];
+    const bool have = ok && nt > 0;
+    if (have) {
+#pragma unroll
+      for (int c = 0; c < NPAD; c += 16) tmem_ld16(tO + c, *reinterpret_cast<uint32_t(*)[16]>(&ov[c]));
+      tmem_ld_wait();
+    } else {
+#pragma unroll
+      for (int r = 0; r < NPAD; ++r) ov[r] = 0u;
+    }
+    // thread d of the 128 softmax threads writes dim d of every real row
+    const int d = key;
+    const int64_t wsi = (((int64_t)seq * gridDim.y + hl) * p.nsplit + split);
+#pragma unroll
+    for (int rr = 0; rr < NPAD; ++rr) {
+      if (rr >= R) break;
+      const float o = __uint_as_float(ov[rr]);
+      const float lt = have ? (l_w[rr] + l_w[NPAD + rr]) + (l_w[2 * NPAD + rr] + l_w[3 * NPAD + rr]) : 0.f;
+      const float mr = have ? m[rr] : -INFINITY;
+      if (p.push) {
+        peer::mc_st_f32(p.ws_o + (wsi * NPAD + rr) * D + d, o);
+        if (d == 0) {
+          peer::mc_st_f32(p.ws_ml + (wsi * 2) * NPAD + rr, mr);
+          peer::mc_st_f32(p.ws_ml + (wsi * 2 + 1) * NPAD + rr, lt);
+        }
+      } else if (p.nsplit == 1) {
+        const int t = rr / p.gqa, g = rr % p.gqa;
+        p.out[((int64_t)(qb + t) * p.hq_total + (int64_t)h * p.gqa + g) * D + d] =
+            __float2bfloat16_rn(lt > 0.f ? o / lt : 0.f);
+      } else {
+        p.ws_o[(wsi * NPAD + rr) * D + d] = o;
+        if (d == 0) {
+          p.ws_ml[(wsi * 2) * NPAD + rr] = mr;
+          p.ws_ml[(wsi * 2 + 1) * NPAD + rr] = lt;
+        }
+      }
+    }
+  } else {
+    // ---------------------------------------------------------- converters
+    // (as in decode_attn_kernel) one item = 32 dims (one scale group) of one key
+    const int cw = (warp < 4) ? warp - 2 : warp - 6;  // warps 2, 3, 8, 9, ... -> 0 .. NCONV-1
+    const int ct = cw * 32 + lane;
+    constexpr int CT = C::NCONV * 32;
+    for (int j = 0; j < nt; ++j) {
+      const int s = j % C::STAGES;
+      if (!mbar_wait_all(&kv_full[s], (j / C::STAGES) & 1, abort_flag, 229)) break;
+      const int vb = j % C::NVT;
+      if (j >= C::NVT && !mbar_wait_all(&vt_empty[vb], ((j / C::NVT) - 1) & 1, abort_flag, 230)) break;
+      const int key0 = (tile_beg + j) * TILE;
+      const int nvalid = min(TILE, seq_len - key0);
+      const uint8_t* vs = sVS + s * VS_TILE_BYTES;
+      uint8_t* vt = sVT + vb * VT_BYTES;
+      if (cw < 4) {
+        sKS[vb * TILE + ct] = (ct < nvalid) ? __half2float(*reinterpret_cast<const __half*>(
+                                                  vs + (ct >> 4) * VS_BYTES + KS_OFF + (ct & 15) * 2))
+                                            : 0.f;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ks_full[vb]);
+      }
+#pragma unroll
+      for (int item = ct; item < TILE * 4; item += CT) {
+        const int key = item >> 2, grp = item & 3;
+        if (key < nvalid) {
+          const uint8_t* run = vs + (key >> 4) * VS_BYTES;
+          const int kk = key & 15;
+          const uint4 w = *reinterpret_cast<const uint4*>(run + kk * 64 + grp * 16);
+          const __half sc = *reinterpret_cast<const __half*>(run + VSC_OFF + (kk * 4 + grp) * 2);
+          v_chunk_to_f16(w.x, sc, vt, key, grp * 4);
+          v_chunk_to_f16(w.y, sc, vt, key, grp * 4 + 1);
+          v_chunk_to_f16(w.z, sc, vt, key, grp * 4 + 2);
+          v_chunk_to_f16(w.w, sc, vt, key, grp * 4 + 3);
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) v_chunk_zero(vt, key, grp * 4 + q);
+        }
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&v_full[vb]);
+        mbar_arrive(&kv_empty[s]);
+        if (ct < 32) K8V4_ATRACE(1, j);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+  if (p.push && threadIdx.x == 0) {
+    peer::fence_proxy_alias();
+    peer::mc_signal_add_u64(p.flag_mc, 1ull);
+  }
+}
+
 // Merge split partials: grid (rows, heads, seqs), 128 threads (dims). The
 // per-split weights are computed once by the block; the O loads of all splits
 // are independent, so their latencies overlap. Context parallelism adds a
@@ -769,7 +1259,7 @@ K8V4_STATUS_API(decode)
 
 #ifdef K8V4_TRACE
 extern "C" int k8v4_attn_trace(uint64_t* host) {
-  return cudaMemcpyFromSymbol(host, g_attn_trace, sizeof(uint64_t) * 5 * 256);
+  return cudaMemcpyFromSymbol(host, g_attn_trace, sizeof(uint64_t) * 8 * 256);
 }
 #endif
 
@@ -779,6 +1269,23 @@ static int launch_decode(const KVTileMaps& tm, const DecodeParams& p, int heads,
   if (ensure_smem_limit<decode_attn_kernel<NPAD>>(C::SMEM_BYTES) != cudaSuccess) return 10;
   dim3 grid(p.nsplit, heads, nseq);
   return launch_k(decode_attn_kernel<NPAD>, grid, dim3(C::NTHREADS), C::SMEM_BYTES, st, tm, p) == cudaSuccess ? 0 : 10;
+}
+
+template <int NPAD>
+static int launch_decode_t(const KVTileMaps& tm, const DecodeParams& p, int heads, int nseq, cudaStream_t st) {
+  using C = TCfg<NPAD>;
+  if (ensure_smem_limit<decode_attn_t_kernel<NPAD>>(C::SMEM_BYTES) != cudaSuccess) return 10;
+  dim3 grid(p.nsplit, heads, nseq);
+  return launch_k(decode_attn_t_kernel<NPAD>, grid, dim3(C::NTHREADS), C::SMEM_BYTES, st, tm, p) == cudaSuccess ? 0
+                                                                                                            : 10;
+}
+
+// Launches of at most 16 query rows per KV head run keys-on-lanes
+// (decode_attn_t_kernel) with K8V4_DECODE_ATTN_T=1; rows on lanes otherwise.
+// (Read at every launch, so a process can switch between the two.)
+static bool keys_on_lanes() {
+  const char* v = getenv("K8V4_DECODE_ATTN_T");
+  return v && (v[0] == '1' || v[0] == 'y' || v[0] == 'Y' || v[0] == 't' || v[0] == 'T');
 }
 
 namespace {
@@ -812,7 +1319,8 @@ int decode_core(const void* q, const int32_t* cu_q, const int32_t* seq_lens, con
   p.push = flag_mc != nullptr;
   p.flag_mc = flag_mc;
   int npad, rc;
-  if (rows <= 16) { npad = 16; rc = launch_decode<16>(tm, p, heads, nseq, st); }
+  if (rows <= 16 && keys_on_lanes()) { npad = 16; rc = launch_decode_t<16>(tm, p, heads, nseq, st); }
+  else if (rows <= 16) { npad = 16; rc = launch_decode<16>(tm, p, heads, nseq, st); }
   else if (rows <= 32) { npad = 32; rc = launch_decode<32>(tm, p, heads, nseq, st); }
   else if (rows <= 48) { npad = 48; rc = launch_decode<48>(tm, p, heads, nseq, st); }
   else { npad = 64; rc = launch_decode<64>(tm, p, heads, nseq, st); }

@@ -178,12 +178,12 @@ def wq_gemm(mode: int, w: torch.Tensor, wscale: torch.Tensor, x: torch.Tensor, x
     return out
 
 
-GEMV_MAX_ROWS = 4
+GEMV_MAX_ROWS = 1
 
 
 def takes_gemv(mode: int, rows: int, ws) -> bool:
     """Whether a GEMM call runs as the decode GEMV (``csrc/gemm/gemv_w4.cu``):
-    W4A16 at most 4 token rows with an fp32 workspace, unless
+    W4A16 at one token row with an fp32 workspace, unless
     ``K8V4_DECODE_GEMV=0``. Mirrors the dispatch in ``csrc/bindings.cpp``."""
     if mode != W4A16 or not 1 <= rows <= GEMV_MAX_ROWS or ws is None:
         return False

@@ -1,4 +1,5 @@
 """Numerics of the sm_100a kernels against plain PyTorch fp32 references."""
+import ctypes
 import math
 
 import pytest
@@ -196,6 +197,16 @@ def test_w4a16_decode_gemv(M, shape):
     ref = gptq.w4a16_ref(x, qw, sc)
     ws = torch.zeros(M * N, dtype=torch.float32, device=DEV)
     qd, sd, xd = qw.to(DEV), sc.to(DEV), x.to(DEV)
+    # the GEMV through its exported C symbol (the op dispatch sends it one row)
+    lib = ctypes.CDLL(ops.extension_path())
+    rc = lib.k8v4_gemv_w4(ctypes.c_void_p(qd.data_ptr()), ctypes.c_void_p(sd.data_ptr()),
+                          ctypes.c_void_p(xd.data_ptr()), ctypes.c_void_p(ws.data_ptr()), M, N, K, K, N,
+                          ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0
+    torch.cuda.synchronize()
+    direct = ws.view(M, N).cpu().clone()
+    assert (direct - ref).abs().max().item() <= 2e-3 * ref.abs().max().item() + 1e-4
+    ws.zero_()
     out = ops.wq_gemm(ops.W4A16, qd, sd, xd, ws=ws, split=1)
     torch.cuda.synchronize()
     assert ops.status() == 0
@@ -329,6 +340,38 @@ def test_prefill_attn(ctx, q_len, gqa, hkv, contiguous):
     cu = torch.tensor([0, q_len, 2 * q_len], dtype=torch.int32, device=DEV)
     out = ops.prefill_attn(q, cu, torch.tensor(lens, dtype=torch.int32, device=DEV), bt.to(DEV), cache.to(DEV),
                            hkv, gqa, q_len)
+    torch.cuda.synchronize()
+    st = ops.status()
+    assert st == 0, "device status 0x%x (code | site<<8)" % st
+    err = (out.float().cpu() - ref).abs().max().item()
+    assert err < 2e-2, err
+
+
+@pytest.mark.parametrize("q_len,gqa,hkv", [(1, 6, 4), (2, 6, 2), (1, 3, 1), (3, 6, 4)])
+@pytest.mark.parametrize("nsplit", [1, 5])
+@pytest.mark.parametrize("keys_on_lanes", ["0", "1"])
+def test_decode_attn_sharp_rescale(q_len, gqa, hkv, nsplit, keys_on_lanes, monkeypatch):
+    """Decode rows (up to 16 per KV head: keys on TMEM lanes; more: rows on
+    lanes) against the fp32 oracle with logits that grow along a long context,
+    so the lazy running max moves several times per split and the O
+    accumulator is rescaled; exact int8 x 2^-5 queries keep the reference
+    tight. Both decode kernels run (K8V4_DECODE_ATTN_T selects keys on TMEM
+    lanes for up to 16 rows)."""
+    monkeypatch.setenv("K8V4_DECODE_ATTN_T", keys_on_lanes)
+    lens = [5000, 2100, 130]
+    q_lens = [q_len] * len(lens)
+    layout, cache, bt, seqs = _paged_setup(lens, hkv, gqa, 16, q_lens, k_ramp=2.0, contiguous=True)
+    g = _gen(17)
+    sharp = []
+    for q, pages in seqs:
+        qi = torch.randint(-127, 128, q.shape, generator=g).float()
+        qi[..., 0] = 127.0
+        sharp.append(((qi / 32.0).bfloat16(), pages))
+    ref = _reference(layout, cache, sharp, lens, q_lens)
+    q = torch.cat([s_[0] for s_ in sharp], 0).to(DEV)
+    cu = torch.tensor([0] + list(torch.cumsum(torch.tensor(q_lens), 0)), dtype=torch.int32, device=DEV)
+    out = ops.decode_attn(q, cu, torch.tensor(lens, dtype=torch.int32, device=DEV), bt.to(DEV), cache.to(DEV),
+                          hkv, gqa, q_len, nsplit=nsplit)
     torch.cuda.synchronize()
     st = ops.status()
     assert st == 0, "device status 0x%x (code | site<<8)" % st

@@ -130,7 +130,9 @@ def test_concurrent_requests_under_kv_pressure_keep_every_token():
     mid-generation; every response still carries exactly max_tokens tokens
     that follow the fake model's rule (next = last + 1)."""
     import concurrent.futures as cf
-    eng = FakeEngine(max_num_seqs=4, budget=48, num_blocks=10, max_model_len=160)
+    # a short pause per step keeps the requests overlapping even when the
+    # host is loaded (the pressure, and so the preemption, needs them at once)
+    eng = FakeEngine(max_num_seqs=4, budget=48, num_blocks=10, max_model_len=160, step_delay=0.002)
     driver = EngineDriver(eng).start()
     app = build_app(driver, ByteTokenizer(1000), "tiny", 160)
     with TestClient(app) as c:
