@@ -5,7 +5,7 @@ Each case holds at most a few hundred MB on the device (inputs just above the
 126 MB L2 so DRAM counters mean something) and launches the kernel a handful
 of times, so an ``ncu --set full -k <kernel> -c 1..3`` capture ends by itself.
 
-    python bench/profile_case.py --case decode|decode7|gemm_m1|gemm_prefill|w4a8_prefill|prefill
+    python bench/profile_case.py --case decode|decode7|gemm_m1|gemm_prefill|w4a8_prefill|prefill|sp_rs|sp_ag
 """
 from __future__ import annotations
 
@@ -63,6 +63,32 @@ def main():
             xq = torch.randint(-127, 127, (M, K), dtype=torch.int8, device="cuda")
             xs = torch.rand(M, device="cuda") * 0.01
             fn = lambda: ops.wq_gemm(ops.W4A8, qw, sc, xq, xscale=xs)  # noqa: E731
+    elif c in ("sp_rs", "sp_ag"):
+        # the sequence-parallel prefill GEMMs of a TP2 rank (W4A8, 4,224-row
+        # chunk) on one GPU: the other rank's slot and counters are local
+        # buffers and the all-gather counters are preset, so the kernel runs
+        # its full epilogue / wait code with no second process
+        from k8v4_xpu_b200.parallel.seq_parallel import tile_owners
+        M, H, I = 4224, 5120, 17408
+        tile0 = tile_owners(M, 2)
+        if c == "sp_rs":
+            N, K = H, I // 2      # down_proj shard
+        else:
+            N, K = I, H           # gate/up shard
+        qw, sc = rand_int4(N, K)
+        xq = torch.randint(-127, 127, (M, K), dtype=torch.int8, device="cuda")
+        xs = torch.rand(M, device="cuda") * 0.01
+        cnt = torch.zeros(16, dtype=torch.int64, device="cuda")
+        if c == "sp_rs":
+            rows = max(tile0[o + 1] - tile0[o] for o in range(2)) * 128  # the largest owner's share
+            slots = [torch.empty(rows * N, dtype=torch.bfloat16, device="cuda") for _ in range(2)]
+            fn = lambda: ops.wq_gemm_sp(ops.W4A8, qw, sc, xq, 2, 0, tile0, xscale=xs,  # noqa: E731
+                                         rs_dst=[t.data_ptr() for t in slots],
+                                         rs_sig=[cnt.data_ptr(), cnt.data_ptr() + 8])
+        else:
+            cnt.fill_(1 << 40)  # every owner's rows "arrived"
+            fn = lambda: ops.wq_gemm_sp(ops.W4A8, qw, sc, xq, 2, 0, tile0, xscale=xs,  # noqa: E731
+                                         ag_flag=cnt.data_ptr(), ag_target=[1, 1])
     elif c in ("decode_step", "decode_step4"):
         # two layers of the 27B decoder, 128K context written straight into
         # the KV pool, one eager decode step per call (kernel launch lists)

@@ -771,7 +771,8 @@ __global__ void __launch_bounds__(TCfg<NPAD>::NTHREADS, 1)
       const int s = j % C::STAGES;
       const int64_t page = next_page;
       next_page = page_of(j + 1);
-      if (j >= C::STAGES && !mbar_wait_all(&kv_empty[s], ((j / C::STAGES) - 1) & 1, abort_flag, 221)) break;
+      if (j >= C::STAGES && !mbar_wait_all_backoff(&kv_empty[s], ((j / C::STAGES) - 1) & 1, abort_flag, 221, 64))
+        break;
       const int pg0 = (tile_beg + j) * TILE_PAGES;
       const int npg = min(TILE_PAGES, n_pages - pg0);
       const int64_t page0 = __shfl_sync(0xffffffffu, page, 0);
@@ -1022,9 +1023,9 @@ __global__ void __launch_bounds__(TCfg<NPAD>::NTHREADS, 1)
     constexpr int CT = C::NCONV * 32;
     for (int j = 0; j < nt; ++j) {
       const int s = j % C::STAGES;
-      if (!mbar_wait_all(&kv_full[s], (j / C::STAGES) & 1, abort_flag, 229)) break;
+      if (!mbar_wait_all_backoff(&kv_full[s], (j / C::STAGES) & 1, abort_flag, 229, 64)) break;
       const int vb = j % C::NVT;
-      if (j >= C::NVT && !mbar_wait_all(&vt_empty[vb], ((j / C::NVT) - 1) & 1, abort_flag, 230)) break;
+      if (j >= C::NVT && !mbar_wait_all_backoff(&vt_empty[vb], ((j / C::NVT) - 1) & 1, abort_flag, 230, 64)) break;
       const int key0 = (tile_beg + j) * TILE;
       const int nvalid = min(TILE, seq_len - key0);
       const uint8_t* vs = sVS + s * VS_TILE_BYTES;

@@ -94,6 +94,31 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Bounded wait for roles that may wait long while other warps of the CTA
+// have work: after the first failed probe each poll sleeps `ns`
+// nanoseconds, so the waiting warp leaves its sub-partition's issue slots to
+// the others.
+__device__ __forceinline__ bool mbar_wait_backoff(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int site,
+                                                  uint32_t ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    __nanosleep(ns);
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > K8V4_WAIT_LIMIT_NS) {
+      *abort_flag = 1;
+      record_error(kErrMbarTimeout, site);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ bool mbar_wait_all_backoff(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                      int site, uint32_t ns) {
+  const bool ok = mbar_wait_backoff(bar, parity, abort_flag, site, ns);
+  return __all_sync(0xffffffffu, ok) != 0;
+}
+
 // Warp-uniform bounded wait: every lane polls, then the warp votes, so a
 // timeout seen by one lane turns the whole warp off together (the callers use
 // .sync.aligned tcgen05 ops and __syncwarp afterwards).
