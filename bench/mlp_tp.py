@@ -28,7 +28,7 @@ copy rate per direction).
 
     python bench/mlp_tp.py                                   # TP1
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \\
-        bench/mlp_tp.py [--comm nccl|fused] [--m 1,7,28,4224,16384]
+        bench/mlp_tp.py [--comm nccl|fused|sp] [--rows 1,7,28,4224,16384]
 """
 from __future__ import annotations
 
@@ -78,7 +78,7 @@ class _Shard:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--m", default="1,7,28,4224,16384")
+    ap.add_argument("--rows", default="1,7,28,4224,16384", help="token rows (M) to run, comma separated")
     ap.add_argument("--comm", default="nccl", choices=("nccl", "fused", "sp"))
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
@@ -95,7 +95,7 @@ def main() -> int:
     far = sp = None
     if a.comm == "sp" and world > 1:
         from k8v4_xpu_b200.parallel.seq_parallel import SeqParallel
-        sp = SeqParallel(None, torch.device("cuda", local), max(int(x) for x in a.m.split(",")), H)
+        sp = SeqParallel(None, torch.device("cuda", local), max(int(x) for x in a.rows.split(",")), H)
     if a.comm == "fused" and world > 1:
         from k8v4_xpu_b200.parallel.fused_ar import FusedAllReduce
         far = FusedAllReduce(None, torch.device("cuda", local), 64, H)
@@ -103,7 +103,7 @@ def main() -> int:
     norm_w = torch.ones(H, dtype=torch.bfloat16, device="cuda")
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     results = []
-    for M in [int(x) for x in a.m.split(",")]:
+    for M in [int(x) for x in a.rows.split(",")]:
         xq = torch.randint(-127, 127, (M, H), dtype=torch.int8, device="cuda", generator=gen)
         xs = torch.rand(M, device="cuda", generator=gen) * 0.01
         gu = torch.empty(M, 2 * I // world, dtype=torch.bfloat16, device="cuda")

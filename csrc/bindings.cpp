@@ -67,8 +67,9 @@ int k8v4_embed_int8(const int64_t* ids, const void* codes, const void* scales, v
                     int64_t start, int64_t rows, cudaStream_t st);
 int k8v4_splitk_finish(float* ws, const void* residual, void* out, int64_t total, int zero_ws, cudaStream_t st);
 int k8v4_gemv_w4_max_rows();
-int k8v4_gemv_w4_allreduce(const void* w, const void* wscale, const void* x, float* ws_mc, unsigned long long* flag_mc,
-                           int M, int N, int K, int ldx, int ldo, cudaStream_t st);
+int k8v4_gemv_w4_allreduce(const void* w, const void* wscale, const void* x, float* local, float* ws_mc,
+                           unsigned long long* flag_mc, unsigned int* ticket, int M, int N, int K, int ldx, int ldo,
+                           cudaStream_t st);
 int k8v4_gemv_w4_ctas(int M, int N, int K);
 int k8v4_gemv_w4(const void* w, const void* wscale, const void* x, float* ws, int M, int N, int K, int ldx, int ldo,
                  cudaStream_t st);
@@ -532,7 +533,8 @@ void argmax(const at::Tensor& logits, int64_t offset, at::Tensor& best_val, at::
 // the completion counter (from the symmetric-memory rendezvous).
 void wq_gemm_allreduce(int64_t mode, const at::Tensor& w, const at::Tensor& wscale, const at::Tensor& x,
                        const c10::optional<at::Tensor>& xscale, at::Tensor& ws, int64_t ws_mc, int64_t flag_mc,
-                       int64_t split) {
+                       int64_t split, const c10::optional<at::Tensor>& gemv_local,
+                       const c10::optional<at::Tensor>& gemv_ticket) {
   check_contig(w, "weight");
   check_contig(wscale, "weight scale");
   check_contig(x, "x");
@@ -551,9 +553,16 @@ void wq_gemm_allreduce(int64_t mode, const at::Tensor& w, const at::Tensor& wsca
   }
   c10::cuda::CUDAGuard g(x.device());
   if (mode == 0 && M <= k8v4_gemv_w4_max_rows() && gemv_enabled()) {
-    check_rc(k8v4_gemv_w4_allreduce(w.data_ptr(), wscale.data_ptr(), x.data_ptr(), reinterpret_cast<float*>(ws_mc),
-                                    reinterpret_cast<unsigned long long*>(flag_mc), (int)M, (int)N, (int)K, (int)K,
-                                    (int)N, cur_stream()),
+    // the decode GEMV: partial sums meet in a local accumulator, then one
+    // CTA adds the rows into every rank's copy (one signal per rank)
+    TORCH_CHECK(gemv_local.has_value() && gemv_ticket.has_value(), "the GEMV all-reduce needs its local buffers");
+    check_contig(*gemv_local, "gemv_local");
+    TORCH_CHECK(gemv_local->scalar_type() == at::kFloat && gemv_local->numel() >= M * N, "gemv_local fp32 [M, N]");
+    TORCH_CHECK(gemv_ticket->scalar_type() == at::kInt && gemv_ticket->numel() >= 1, "gemv_ticket int32");
+    check_rc(k8v4_gemv_w4_allreduce(w.data_ptr(), wscale.data_ptr(), x.data_ptr(), gemv_local->data_ptr<float>(),
+                                    reinterpret_cast<float*>(ws_mc), reinterpret_cast<unsigned long long*>(flag_mc),
+                                    reinterpret_cast<unsigned int*>(gemv_ticket->data_ptr<int>()), (int)M, (int)N,
+                                    (int)K, (int)K, (int)N, cur_stream()),
              "gemv_w4_allreduce");
     return;
   }
@@ -656,7 +665,7 @@ void rmsnorm_sp(const c10::optional<at::Tensor>& slots, int64_t world, int64_t s
 
 // CTAs (= signals per rank) of one wq_gemm_allreduce call.
 int64_t wq_gemm_ctas(int64_t mode, int64_t M, int64_t N, int64_t K, int64_t split) {
-  if (mode == 0 && M <= k8v4_gemv_w4_max_rows() && gemv_enabled()) return k8v4_gemv_w4_ctas((int)M, (int)N, (int)K);
+  if (mode == 0 && M <= k8v4_gemv_w4_max_rows() && gemv_enabled()) return 1;  // the GEMV's last CTA signals
   return k8v4_wq_gemm_ctas((int)mode, (int)M, (int)N, (int)K, (int)split);
 }
 
@@ -808,7 +817,7 @@ TORCH_LIBRARY(k8v4, m) {
       "float eps, Tensor? sync_flag=None, Tensor(f!)? sync_state=None, int sync_expected=0) -> ()");
   m.def(
       "wq_gemm_allreduce(int mode, Tensor w, Tensor wscale, Tensor x, Tensor? xscale, Tensor(a!) ws, int ws_mc, "
-      "int flag_mc, int split) -> ()");
+      "int flag_mc, int split, Tensor(b!)? gemv_local=None, Tensor(c!)? gemv_ticket=None) -> ()");
   m.def("wq_gemm_ctas(int mode, int M, int N, int K, int split) -> int");
   m.def(
       "wq_gemm_sp(int mode, Tensor w, Tensor wscale, Tensor x, Tensor? xscale, Tensor(a!)? out, int world, int rank, "

@@ -18,6 +18,13 @@ __device__ __forceinline__ void mc_red_add_f32(float* mc_addr, float v) {
   asm volatile("multimem.red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(mc_addr), "f"(v) : "memory");
 }
 
+// Four consecutive floats added into every rank's copy (16-byte aligned).
+__device__ __forceinline__ void mc_red_add_v4_f32(float* mc_addr, float4 v) {
+  asm volatile("multimem.red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc_addr), "f"(v.x),
+               "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
+
 // Signal: +v on every rank's copy of a 64-bit counter, ordered after this
 // thread's earlier writes (and, through a preceding bar.sync, its CTA's).
 __device__ __forceinline__ void mc_signal_add_u64(unsigned long long* mc_addr, unsigned long long v) {

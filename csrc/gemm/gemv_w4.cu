@@ -32,12 +32,17 @@
 //     (red.global.add), the split-K accumulator protocol of wq_gemm.cu: ws is
 //     zero on entry and the consumer (the fused RMSNorm, the RoPE / cache
 //     store kernel or splitk_finish) reads and re-zeroes it.
-//   * GEMM -> all-reduce (tensor parallel o_proj / down_proj): with `flag_mc`
-//     set, ws is the multicast address of a symmetric fp32 buffer and the
-//     adds are multimem.red (the NVSwitch sums every rank's partials into
-//     every rank's copy); each CTA then adds 1 to the multicast counter
-//     `flag_mc` with release semantics, and the consuming RMSNorm waits for
-//     world x (this grid's CTAs) signals, as for wq_gemm.cu's epilogue.
+//   * GEMM -> all-reduce (tensor parallel o_proj / down_proj), in two
+//     phases: the warps' sums first meet in a local fp32 accumulator
+//     (`ws`, L2 atomics); the CTA that finishes last (a ticket counter) then
+//     reads the reduced rows once and sends them with 16-byte multimem.red
+//     to the multicast address of the symmetric buffer `ws_mc` (the NVSwitch
+//     sums every rank's rows into every rank's copy), re-zeroes the local
+//     accumulator and the ticket, and adds 1 to the multicast counter
+//     `flag_mc` with release semantics; the consuming RMSNorm waits for
+//     `world` signals. (Sending every warp's partial straight through the
+//     switch, ~60 per output element at the 27B shapes, measured 110 tok/s
+//     at TP2 against 172 with an NCCL all-reduce.)
 //
 // Weights are streamed with no-allocate L1 loads; the first unit's loads go
 // out before the grid waits for its predecessor (programmatic launch), the
@@ -81,7 +86,7 @@ template <int M>
 __global__ void __launch_bounds__(kWarps * 32, ctas_per_sm<M>())
     gemv_w4_kernel(const uint32_t* __restrict__ qw, const __half* __restrict__ wscale,
                    const __nv_bfloat16* __restrict__ x, float* ws, int N, int K, int ldx, int ldo, int units,
-                   unsigned long long* flag_mc) {
+                   float* ws_mc, unsigned long long* flag_mc, unsigned int* ticket) {
   pdl_trigger();
   // per warp and token row: for each packed row j of the unit the four limb
   // words {even k hi, odd k hi, even k lo, odd k lo}
@@ -101,8 +106,20 @@ __global__ void __launch_bounds__(kWarps * 32, ctas_per_sm<M>())
 #pragma unroll
     for (int j = 0; j < kRows; ++j) dst[j] = ld_stream(base + j * row_vec);
   };
+  // a unit's activations (two per lane and token row) and its 4 group
+  // scales travel one unit ahead too, so the limb preparation and the
+  // epilogue do not wait on an L2 round trip every unit
+  auto load_side = [&](int uu, uint32_t (&xr)[M], uint2& sr) {
+    const int tile = uu / kunits, k0 = (uu - tile * kunits) * 8 * kRows;
+#pragma unroll
+    for (int m = 0; m < M; ++m) xr[m] = *reinterpret_cast<const uint32_t*>(x + (size_t)m * ldx + k0 + 2 * lane);
+    sr = *reinterpret_cast<const uint2*>(wscale + (size_t)(k0 >> 7) * N + tile * 128 + lane * 4);
+  };
   if (u < uend) load_unit(u, cur);
   pdl_wait();  // x comes from the previous kernel, which also re-zeroed ws
+  uint32_t xcur[M];
+  uint2 scur = make_uint2(0u, 0u);
+  if (u < uend) load_side(u, xcur, scur);
 
   int tile = -1;
   float facc[M][4];
@@ -111,11 +128,7 @@ __global__ void __launch_bounds__(kWarps * 32, ctas_per_sm<M>())
     for (int m = 0; m < M; ++m)
 #pragma unroll
       for (int f = 0; f < 4; ++f) {
-        float* dst = ws + (size_t)m * ldo + tile * 128 + lane * 4 + f;
-        if (flag_mc)
-          peer::mc_red_add_f32(dst, facc[m][f]);
-        else
-          atomicAdd(dst, facc[m][f]);
+        atomicAdd(ws + (size_t)m * ldo + tile * 128 + lane * 4 + f, facc[m][f]);
       }
   };
   uint8_t* lbytes = reinterpret_cast<uint8_t*>(&lsm[warp][0][0][0]);
@@ -130,9 +143,14 @@ __global__ void __launch_bounds__(kWarps * 32, ctas_per_sm<M>())
         for (int f = 0; f < 4; ++f) facc[m][f] = 0.f;
     }
     uint4 nxt[kRows];
+    uint32_t xnxt[M];
+    uint2 snxt = make_uint2(0u, 0u);
     const bool more = u + 1 < uend;
-    if (more) load_unit(u + 1, nxt);
-    const int k0 = ku * 8 * kRows;
+    if (more) {
+      load_unit(u + 1, nxt);
+      load_side(u + 1, xnxt, snxt);
+    }
+    (void)ku;
     // ---- the warp's own limbs of the unit's 64 activations per token row.
     // Lane l holds k0 + 2l and k0 + 2l + 1: packed row j = l / 4, byte l % 4
     // of the even-k word (codes 0, 2, 4, 6 after the unpack) and of the odd one.
@@ -140,8 +158,7 @@ __global__ void __launch_bounds__(kWarps * 32, ctas_per_sm<M>())
     int csum[M];
 #pragma unroll
     for (int m = 0; m < M; ++m) {
-      const __nv_bfloat162 xv = *reinterpret_cast<const __nv_bfloat162*>(x + (size_t)m * ldx + k0 + 2 * lane);
-      const float2 xf = __bfloat1622float2(xv);
+      const float2 xf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xcur[m]));
       const float am = warp_max(fmaxf(fabsf(xf.x), fabsf(xf.y)));
       const float sc = am > 0.f ? am / kLimbMax : 1.f;
       const float inv = 1.f / sc;
@@ -182,8 +199,7 @@ __global__ void __launch_bounds__(kWarps * 32, ctas_per_sm<M>())
       }
     }
     // group scales of the unit's 4 features (fp16)
-    const uint2 sraw = *reinterpret_cast<const uint2*>(wscale + (size_t)(k0 >> 7) * N + tile * 128 + lane * 4);
-    const __half2* sh = reinterpret_cast<const __half2*>(&sraw);
+    const __half2* sh = reinterpret_cast<const __half2*>(&scur);
     const float2 g01 = __half22float2(sh[0]), g23 = __half22float2(sh[1]);
     const float gsc[4] = {g01.x, g01.y, g23.x, g23.y};
 #pragma unroll
@@ -197,15 +213,37 @@ __global__ void __launch_bounds__(kWarps * 32, ctas_per_sm<M>())
     if (more) {
 #pragma unroll
       for (int j = 0; j < kRows; ++j) cur[j] = nxt[j];
+#pragma unroll
+      for (int m = 0; m < M; ++m) xcur[m] = xnxt[m];
+      scur = snxt;
     }
     ++u;
   }
   if (tile >= 0) flush();
   if (flag_mc) {
-    // every warp's multicast adds precede the CTA's signal
-    peer::fence_proxy_alias();
+    // second phase: the last CTA to finish sends the reduced rows to every rank
+    __shared__ int last;
+    __threadfence();  // this thread's atomics are visible before the ticket
     __syncthreads();
-    if (threadIdx.x == 0) peer::mc_signal_add_u64(flag_mc, 1ull);
+    if (threadIdx.x == 0) last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (last) {
+      __threadfence();  // every other CTA's atomics (ordered by their tickets)
+      for (int r = 0; r < M; ++r) {
+        float4* src = reinterpret_cast<float4*>(ws + (size_t)r * ldo);
+        for (int i = threadIdx.x; i < N / 4; i += blockDim.x) {
+          const float4 v = __ldcg(src + i);
+          src[i] = make_float4(0.f, 0.f, 0.f, 0.f);  // clean for the next call
+          peer::mc_red_add_v4_f32(ws_mc + (size_t)r * ldo + 4 * i, v);
+        }
+      }
+      peer::fence_proxy_alias();
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        *ticket = 0u;
+        peer::mc_signal_add_u64(flag_mc, 1ull);
+      }
+    }
   }
 }
 
@@ -232,23 +270,27 @@ static int grid_ctas(int M, int N, int K) {
 
 template <int M>
 static int launch(const void* w, const void* wscale, const void* x, float* ws, int N, int K, int ldx, int ldo,
-                  unsigned long long* flag_mc, cudaStream_t st) {
+                  float* ws_mc, unsigned long long* flag_mc, unsigned int* ticket, cudaStream_t st) {
   const int units = (N / 128) * (K / (8 * kRows));
   return launch_k(gemv_w4_kernel<M>, dim3(grid_ctas(M, N, K)), dim3(kWarps * 32), 0, st,
                   reinterpret_cast<const uint32_t*>(w), reinterpret_cast<const __half*>(wscale),
-                  reinterpret_cast<const __nv_bfloat16*>(x), ws, N, K, ldx, ldo, units, flag_mc) == cudaSuccess
+                  reinterpret_cast<const __nv_bfloat16*>(x), ws, N, K, ldx, ldo, units, ws_mc, flag_mc,
+                  ticket) == cudaSuccess
              ? 0
              : 300;
 }
 
 static int dispatch(const void* w, const void* wscale, const void* x, float* ws, int M, int N, int K, int ldx,
-                    int ldo, unsigned long long* flag_mc, cudaStream_t st) {
+                    int ldo, float* ws_mc, unsigned long long* flag_mc, unsigned int* ticket, cudaStream_t st) {
   if (M < 1 || M > 4 || N % 128 || K % 128 || ldx % 2 || ldo < N || !w || !wscale || !x || !ws) return 1;
+  if (flag_mc && (!ws_mc || !ticket || ldo % 4 || (reinterpret_cast<uintptr_t>(ws) & 15) ||
+                  (reinterpret_cast<uintptr_t>(ws_mc) & 15)))
+    return 1;
   switch (M) {
-    case 1: return launch<1>(w, wscale, x, ws, N, K, ldx, ldo, flag_mc, st);
-    case 2: return launch<2>(w, wscale, x, ws, N, K, ldx, ldo, flag_mc, st);
-    case 3: return launch<3>(w, wscale, x, ws, N, K, ldx, ldo, flag_mc, st);
-    default: return launch<4>(w, wscale, x, ws, N, K, ldx, ldo, flag_mc, st);
+    case 1: return launch<1>(w, wscale, x, ws, N, K, ldx, ldo, ws_mc, flag_mc, ticket, st);
+    case 2: return launch<2>(w, wscale, x, ws, N, K, ldx, ldo, ws_mc, flag_mc, ticket, st);
+    case 3: return launch<3>(w, wscale, x, ws, N, K, ldx, ldo, ws_mc, flag_mc, ticket, st);
+    default: return launch<4>(w, wscale, x, ws, N, K, ldx, ldo, ws_mc, flag_mc, ticket, st);
   }
 }
 
@@ -268,18 +310,21 @@ extern "C" int k8v4_gemv_w4_max_rows() { return 1; }
 // Returns 0, 1 for an unsupported shape, 300 for a launch error.
 extern "C" int k8v4_gemv_w4(const void* w, const void* wscale, const void* x, float* ws, int M, int N, int K,
                             int ldx, int ldo, cudaStream_t st) {
-  return k8v4::gemv::dispatch(w, wscale, x, ws, M, N, K, ldx, ldo, nullptr, st);
+  return k8v4::gemv::dispatch(w, wscale, x, ws, M, N, K, ldx, ldo, nullptr, nullptr, nullptr, st);
 }
 
-// GEMM -> all-reduce: the sums go to every rank's copy of a symmetric fp32
-// buffer through its multicast address ws_mc, then each CTA adds 1 to the
-// multicast counter flag_mc; the consumer expects world x
-// k8v4_gemv_w4_ctas(M, N, K) signals for one call.
-extern "C" int k8v4_gemv_w4_allreduce(const void* w, const void* wscale, const void* x, float* ws_mc,
-                                      unsigned long long* flag_mc, int M, int N, int K, int ldx, int ldo,
-                                      cudaStream_t st) {
-  if (!ws_mc || !flag_mc) return 4;
-  return k8v4::gemv::dispatch(w, wscale, x, ws_mc, M, N, K, ldx, ldo, flag_mc, st);
+// GEMM -> all-reduce: the sums meet in `local` (this rank's fp32 [M, ldo]
+// accumulator, zero on entry and left zero), then the last CTA adds them into
+// every rank's copy of a symmetric fp32 buffer through its multicast address
+// ws_mc and adds 1 to the multicast counter flag_mc; `ticket` (one unsigned
+// int, zero on entry and left zero) picks that CTA. The consumer expects
+// `world` signals for one call. Calls that overlap on the GPU must not share
+// `local` or `ticket`.
+extern "C" int k8v4_gemv_w4_allreduce(const void* w, const void* wscale, const void* x, float* local, float* ws_mc,
+                                      unsigned long long* flag_mc, unsigned int* ticket, int M, int N, int K,
+                                      int ldx, int ldo, cudaStream_t st) {
+  if (!local || !ws_mc || !flag_mc || !ticket) return 4;
+  return k8v4::gemv::dispatch(w, wscale, x, local, M, N, K, ldx, ldo, ws_mc, flag_mc, ticket, st);
 }
 
 // CTAs one call launches (0 for an unsupported shape).

@@ -191,14 +191,19 @@ def takes_gemv(mode: int, rows: int, ws) -> bool:
 
 
 # ------------------------------------------------------------------- fused
-def wq_gemm_allreduce(mode: int, w, wscale, x, ws, ws_mc: int, flag_mc: int, xscale=None, split: int = 1):
+def wq_gemm_allreduce(mode: int, w, wscale, x, ws, ws_mc: int, flag_mc: int, xscale=None, split: int = 1,
+                      gemv_local=None, gemv_ticket=None):
     """GEMM -> all-reduce: fp32 sums land in every rank's copy of ``ws`` (a
-    symmetric buffer, multicast address ``ws_mc``); each CTA then signals the
-    multicast counter ``flag_mc``. Returns ``ws``."""
+    symmetric buffer, multicast address ``ws_mc``); the call then signals the
+    multicast counter ``flag_mc`` (``wq_gemm_ctas`` times per rank). A
+    one-row W4A16 call runs as the decode GEMV, whose partial sums first meet
+    in ``gemv_local`` (fp32, zero, left zero) and whose last CTA, picked by
+    ``gemv_ticket`` (int32, zero, left zero), sends the rows. Returns ``ws``."""
     require()
     if x.shape[0] == 0:
         return ws
-    torch.ops.k8v4.wq_gemm_allreduce(mode, w, wscale, x, xscale, ws, int(ws_mc), int(flag_mc), int(split))
+    torch.ops.k8v4.wq_gemm_allreduce(mode, w, wscale, x, xscale, ws, int(ws_mc), int(flag_mc), int(split),
+                                     gemv_local, gemv_ticket)
     _count()
     return ws
 

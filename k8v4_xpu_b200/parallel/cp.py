@@ -17,7 +17,7 @@ of this framework (a KV-gather design, not ring attention):
   owner of the token's page writes its KV; each rank's decode attention
   covers its own pages and the (m, l, O) split partials of all ranks are
   exchanged and merged, so every rank continues with the same attention
-  output. The exchange is an NCCL all-gather, or (``K8V4_CP_COMBINE=peer``)
+  output. The exchange is an NCCL all-gather (``K8V4_CP_COMBINE=nccl``), or (the default)
   multicast stores from the attention kernel itself (``parallel.cp_combine``).
 
 Every rank's KV pool lives in symmetric memory and is mapped into every

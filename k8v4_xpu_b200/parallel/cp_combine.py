@@ -20,7 +20,8 @@ every rank's signals of that call, which each rank sends only after its merge
 of the call that read buffer ``s``. So no rank still reads a slot that is
 being overwritten.
 
-``K8V4_CP_COMBINE`` = ``nccl`` (default) or ``peer`` selects the exchange.
+``K8V4_CP_COMBINE`` = ``peer`` (default; the NCCL all-gather when the box has
+no multicast) or ``nccl`` selects the exchange.
 The reference has no context parallelism, so this module has no counterpart
 there.
 """
@@ -37,7 +38,7 @@ NUM_SMS = 148
 
 
 def cp_combine_mode() -> str:
-    mode = os.environ.get("K8V4_CP_COMBINE", "nccl").strip().lower()
+    mode = os.environ.get("K8V4_CP_COMBINE", "peer").strip().lower()
     if mode not in ("nccl", "peer"):
         raise ValueError("K8V4_CP_COMBINE must be nccl or peer, got %r" % mode)
     return mode

@@ -75,6 +75,11 @@ class FusedAllReduce:
             raise RuntimeError("the multicast address is the local buffer (no multicast object)")
         # per slot: [signals consumed so far, consumer CTAs done] (local to this rank)
         self.state = torch.zeros((self.SLOTS, 2), dtype=torch.int64, device=self.device)
+        # one-row calls (the decode GEMV): per slot a local fp32 row where the
+        # partial sums meet before one CTA sends them, and that CTA's ticket
+        self.gemv_local = torch.zeros((self.SLOTS, ops.GEMV_MAX_ROWS * self.hidden), dtype=torch.float32,
+                                      device=self.device)
+        self.gemv_ticket = torch.zeros((self.SLOTS, 4), dtype=torch.int32, device=self.device)
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)  # every copy is zero before the first multicast add
         self.calls = 0
@@ -95,7 +100,8 @@ class FusedAllReduce:
         per = self.max_rows * self.hidden
         view = self.data[slot * per: slot * per + rows * n].view(rows, n)
         ops.wq_gemm_allreduce(mode, linear.qweight, linear.scales, a, view, self.data_mc + slot * per * 4,
-                              self.flag_mc + slot * 8, xscale=xs, split=split)
+                              self.flag_mc + slot * 8, xscale=xs, split=split, gemv_local=self.gemv_local[slot],
+                              gemv_ticket=self.gemv_ticket[slot])
         expected = self.world * ops.wq_gemm_ctas(mode, rows, n, k, split)
         self.calls += 1
         return view, (self.flags[slot:slot + 1], self.state[slot], expected)

@@ -14,7 +14,7 @@ same steps. What differs per rank (see ``parallel.cp``):
   writes each token's KV, and attention merges every rank's partials.
 
 Decode runs eagerly here. The per-layer partial exchange is an NCCL
-all-gather, or with ``K8V4_CP_COMBINE=peer`` multicast stores from the decode
+all-gather (``K8V4_CP_COMBINE=nccl``) or, by default, multicast stores from the decode
 attention kernel (``parallel.cp_combine``). Tensor parallelism inside each
 CP rank (CP x TP, ``parallel.groups``) shards the model over the TP group as
 in the plain engine; the CP exchange then runs between the ranks that hold

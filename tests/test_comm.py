@@ -75,9 +75,9 @@ def test_cp_peer_exchange_slots_and_bounds(monkeypatch):
     slot size bound and the two alternating buffers' layout."""
     from k8v4_xpu_b200.parallel import cp_combine as X
     monkeypatch.delenv("K8V4_CP_COMBINE", raising=False)
-    assert X.cp_combine_mode() == "nccl"
-    monkeypatch.setenv("K8V4_CP_COMBINE", "peer")
     assert X.cp_combine_mode() == "peer"
+    monkeypatch.setenv("K8V4_CP_COMBINE", "nccl")
+    assert X.cp_combine_mode() == "nccl"
     monkeypatch.setenv("K8V4_CP_COMBINE", "ring")
     with pytest.raises(ValueError):
         X.cp_combine_mode()

@@ -66,6 +66,40 @@ SMALL_PROMPTS = [list(range(3, 3 + 40)), list(range(100, 100 + 17))]
 TINY_PROMPTS = [[5]]  # one row: the decode GEMV and its multicast all-reduce epilogue
 
 
+def _log(rank, msg):
+    """Progress of a rank, flushed to a file (a stalled rank shows where it
+    stopped) in $K8V4_TEST_LOG_DIR, else the system temporary directory."""
+    import tempfile
+    d = os.environ.get("K8V4_TEST_LOG_DIR") or tempfile.gettempdir()
+    os.makedirs(d, exist_ok=True)
+    with open(os.path.join(d, "k8v4_tp_rank%d.log" % rank), "a") as f:
+        f.write(msg + "\n")
+
+
+def _collect(procs, q, timeout_s=420):
+    """Results of every rank; fails (instead of waiting out the timeout) as
+    soon as a rank process has died without reporting."""
+    import queue
+    import time
+    out = {}
+    t0 = time.monotonic()
+    while len(out) < len(procs):
+        try:
+            r, res = q.get(timeout=5)
+            out[r] = res
+            continue
+        except queue.Empty:
+            pass
+        dead = [i for i, p in enumerate(procs) if i not in out and p.exitcode is not None]
+        if dead:
+            raise AssertionError("rank(s) %s exited (codes %s) without a result" %
+                                 (dead, [procs[i].exitcode for i in dead]))
+        if time.monotonic() - t0 > timeout_s:
+            raise AssertionError("ranks %s gave no result in %d s" %
+                                 (sorted(set(range(len(procs))) - set(out)), timeout_s))
+    return out
+
+
 def _worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
@@ -79,12 +113,15 @@ def _worker(rank, world, port, q):
         init_from_env(timeout_s=120)
         comm = TPComm()
         dev = torch.device("cuda", rank)
+        torch.cuda.set_device(dev)
+        _log(rank, "tp%d start" % world)
         m = DenseModel(TP_MODEL, tp=world, rank=rank, device=dev, comm=comm).random_init(seed=3)
         inp = _prefill_inputs(PROMPTS, dev)
         caches = [torch.zeros(64, m.layout.page_bytes, dtype=torch.uint8, device=dev) for _ in m.layers]
         hid = m.forward(inp, caches)
         ids = m.greedy(hid)
         res = {"hidden": hid.float().cpu(), "ids": ids.cpu(), "logits": m.logits(hid).float().cpu()}
+        _log(rank, "prefill (nccl all-reduce) done")
         # prefill with the residual sharded by token rows between the fused
         # GEMM -> reduce-scatter and all-gather -> GEMM kernels (twice: the
         # running signal counts must keep matching)
@@ -94,18 +131,21 @@ def _worker(rank, world, port, q):
             caches = [torch.zeros(64, m.layout.page_bytes, dtype=torch.uint8, device=dev) for _ in m.layers]
             res["hidden_sp"] = m.forward(inp, caches).float().cpu()
         res["sp_calls"] = m.sp.calls
+        _log(rank, "sequence-parallel prefill done")
         m.sp = None
         # decode-sized batch (<= 64 rows): the GEMM -> all-reduce runs fused (NVLS multicast adds)
         from k8v4_xpu_b200.parallel.fused_ar import FusedAllReduce
         small = _prefill_inputs(SMALL_PROMPTS, dev)
         caches = [torch.zeros(64, m.layout.page_bytes, dtype=torch.uint8, device=dev) for _ in m.layers]
         res["small_nccl"] = m.forward(small, caches).float().cpu()
+        _log(rank, "small rows (nccl) done")
         m.fused_ar = FusedAllReduce(None, dev, 64, TP_MODEL.hidden)
         for _ in range(3):  # repeated uses: the running signal counts must keep matching
             caches = [torch.zeros(64, m.layout.page_bytes, dtype=torch.uint8, device=dev) for _ in m.layers]
             res["small_fused"] = m.forward(small, caches).float().cpu()
         # a single row: the row-parallel GEMMs run as the decode GEMV with its
         # multicast all-reduce epilogue
+        _log(rank, "small rows (fused all-reduce) done")
         tiny = _prefill_inputs(TINY_PROMPTS, dev)
         caches = [torch.zeros(64, m.layout.page_bytes, dtype=torch.uint8, device=dev) for _ in m.layers]
         res["tiny_fused"] = m.forward(tiny, caches).float().cpu()
@@ -114,13 +154,16 @@ def _worker(rank, world, port, q):
         res["tiny_nccl"] = m.forward(tiny, caches).float().cpu()
         m.fused_ar = far
         torch.cuda.synchronize(dev)
+        _log(rank, "one row (GEMV all-reduce and nccl) done")
         res["fused_calls"] = m.fused_ar.calls
         res["kv_heads"] = m.shape.kv_heads_of(rank, TP_MODEL.num_kv_heads)
         res["gqa_local"] = m.shape.gqa_local
         cfg = EngineConfig(model="tp-test", tensor_parallel_size=world, max_model_len=2048, max_num_seqs=2,
                            max_num_batched_tokens=96, num_kv_blocks=128, device=str(dev))
         eng = LLMEngine(cfg, TP_MODEL, comm=comm, rank=rank)
+        _log(rank, "engine built")
         res["gen"] = eng.generate(PROMPTS, SamplingParams(max_tokens=8, ignore_eos=True))
+        _log(rank, "generate done")
         res["graph"] = bool(eng.graphs and eng.graphs.captured)
         res["comm_mode"] = eng.tp_comm_mode
         res["prefill_mode"] = eng.tp_prefill_mode
@@ -129,6 +172,7 @@ def _worker(rank, world, port, q):
         comm.barrier()
         q.put((rank, res))
     except Exception:
+        _log(rank, traceback.format_exc())
         q.put((rank, {"error": traceback.format_exc()}))
     finally:
         if dist.is_initialized():
@@ -146,9 +190,13 @@ def test_tp_matches_tp1(world):
     procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    out = dict(q.get(timeout=900) for _ in procs)
-    for p in procs:
-        p.join(timeout=120)
+    try:
+        out = _collect(procs, q)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.exitcode is None:
+                p.kill()
     for r in range(world):
         assert "error" not in out[r], out[r].get("error")
         assert out[r]["status"] == 0 and out[r]["graph"]
