@@ -76,10 +76,12 @@ class FusedAllReduce:
         # per slot: [signals consumed so far, consumer CTAs done] (local to this rank)
         self.state = torch.zeros((self.SLOTS, 2), dtype=torch.int64, device=self.device)
         # one-row calls (the decode GEMV): per slot a local fp32 row where the
-        # partial sums meet before one CTA sends them, and that CTA's ticket
+        # partial sums meet before each 128-feature tile is sent, and the
+        # tiles' tickets
         self.gemv_local = torch.zeros((self.SLOTS, ops.GEMV_MAX_ROWS * self.hidden), dtype=torch.float32,
                                       device=self.device)
-        self.gemv_ticket = torch.zeros((self.SLOTS, 4), dtype=torch.int32, device=self.device)
+        self.gemv_ticket = torch.zeros((self.SLOTS, max(1, self.hidden // 128)), dtype=torch.int32,
+                                       device=self.device)
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)  # every copy is zero before the first multicast add
         self.calls = 0

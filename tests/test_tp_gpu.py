@@ -101,6 +101,13 @@ def _collect(procs, q, timeout_s=420):
 
 
 def _worker(rank, world, port, q):
+    import faulthandler
+    import tempfile
+    d = os.environ.get("K8V4_TEST_LOG_DIR") or tempfile.gettempdir()
+    os.makedirs(d, exist_ok=True)
+    # a crash of the rank (signal) leaves its Python stack in the rank's log
+    fault_log = open(os.path.join(d, "k8v4_tp_rank%d.log" % rank), "a")
+    faulthandler.enable(file=fault_log, all_threads=True)
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
     import torch.distributed as dist
