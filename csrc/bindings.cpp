@@ -558,8 +558,7 @@ void wq_gemm_allreduce(int64_t mode, const at::Tensor& w, const at::Tensor& wsca
     TORCH_CHECK(gemv_local.has_value() && gemv_ticket.has_value(), "the GEMV all-reduce needs its local buffers");
     check_contig(*gemv_local, "gemv_local");
     TORCH_CHECK(gemv_local->scalar_type() == at::kFloat && gemv_local->numel() >= M * N, "gemv_local fp32 [M, N]");
-    TORCH_CHECK(gemv_ticket->scalar_type() == at::kInt && gemv_ticket->numel() >= N / 128,
-                "gemv_ticket int32 [N / 128]");
+    TORCH_CHECK(gemv_ticket->scalar_type() == at::kInt && gemv_ticket->numel() >= 1, "gemv_ticket int32");
     check_rc(k8v4_gemv_w4_allreduce(w.data_ptr(), wscale.data_ptr(), x.data_ptr(), gemv_local->data_ptr<float>(),
                                     reinterpret_cast<float*>(ws_mc), reinterpret_cast<unsigned long long*>(flag_mc),
                                     reinterpret_cast<unsigned int*>(gemv_ticket->data_ptr<int>()), (int)M, (int)N,
@@ -666,7 +665,7 @@ void rmsnorm_sp(const c10::optional<at::Tensor>& slots, int64_t world, int64_t s
 
 // CTAs (= signals per rank) of one wq_gemm_allreduce call.
 int64_t wq_gemm_ctas(int64_t mode, int64_t M, int64_t N, int64_t K, int64_t split) {
-  if (mode == 0 && M <= k8v4_gemv_w4_max_rows() && gemv_enabled()) return N / 128;  // one signal per GEMV tile
+  if (mode == 0 && M <= k8v4_gemv_w4_max_rows() && gemv_enabled()) return 1;  // the GEMV's last CTA signals
   return k8v4_wq_gemm_ctas((int)mode, (int)M, (int)N, (int)K, (int)split);
 }
 

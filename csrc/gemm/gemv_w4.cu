@@ -32,19 +32,20 @@
 //     (red.global.add), the split-K accumulator protocol of wq_gemm.cu: ws is
 //     zero on entry and the consumer (the fused RMSNorm, the RoPE / cache
 //     store kernel or splitk_finish) reads and re-zeroes it.
-//   * GEMM -> all-reduce (tensor parallel o_proj / down_proj), per feature
-//     tile of 128 outputs: the warps' sums first meet in a local fp32
-//     accumulator (`ws`, L2 atomics) and add their unit counts to the tile's
-//     ticket; the warp whose units complete the tile reads its 128 reduced
-//     features once, sends them with one 16-byte multimem.red per lane to
-//     the multicast address of the symmetric buffer `ws_mc` (the NVSwitch
-//     sums every rank's tile into every rank's copy), re-zeroes the tile and
-//     the ticket, and adds 1 to the multicast counter `flag_mc` with release
-//     semantics; the consuming RMSNorm waits for world x N / 128 signals.
-//     The sends overlap the GEMV's other tiles. (Sending every warp's
-//     partial through the switch, ~60 per output element at the 27B shapes,
-//     measured 110 tok/s at TP2 against 172 with an NCCL all-reduce; one
-//     send of the whole row by the last CTA, 161.9.)
+//   * GEMM -> all-reduce (tensor parallel o_proj / down_proj), in two
+//     phases: the warps' sums first meet in a local fp32 accumulator
+//     (`ws`, L2 atomics); the CTA that finishes last (a ticket counter) then
+//     reads the reduced rows once and sends them with 16-byte multimem.red
+//     to the multicast address of the symmetric buffer `ws_mc` (the NVSwitch
+//     sums every rank's rows into every rank's copy), re-zeroes the local
+//     accumulator and the ticket, and adds 1 to the multicast counter
+//     `flag_mc` with release semantics; the consuming RMSNorm waits for
+//     `world` signals. Measured at TP2 (27B, 128K, c = 1): 161.9 tok/s,
+//     against 172.2 for this GEMV followed by an NCCL all-reduce, so the
+//     engine keeps one-row calls on NCCL unless K8V4_TP_GEMV_FUSED=1.
+//     (Sending every warp's partial straight through the switch, ~60 per
+//     output element, measured 110 tok/s; one send per 128-feature tile by
+//     the warp that completes it, 142 tok/s.)
 //
 // Weights are streamed with no-allocate L1 loads; the first unit's loads go
 // out before the grid waits for its predecessor (programmatic launch), the
@@ -125,37 +126,13 @@ __global__ void __launch_bounds__(kWarps * 32, ctas_per_sm<M>())
 
   int tile = -1;
   float facc[M][4];
-  int tile_units = 0;  // units of the current tile this warp did
   auto flush = [&]() {
 #pragma unroll
     for (int m = 0; m < M; ++m)
 #pragma unroll
-      for (int f = 0; f < 4; ++f) atomicAdd(ws + (size_t)m * ldo + tile * 128 + lane * 4 + f, facc[m][f]);
-    if (flag_mc) {
-      // GEMM -> all-reduce: the warp whose units complete the tile sends its
-      // 128 reduced features to every rank and signals
-      __threadfence();  // this lane's adds are visible before the ticket
-      __syncwarp();
-      unsigned int done = 0;
-      if (lane == 0) done = atomicAdd(ticket + tile, (unsigned int)tile_units) + tile_units;
-      done = __shfl_sync(0xffffffffu, done, 0);
-      if (done == (unsigned int)kunits) {
-        __threadfence();  // the other warps' adds to this tile (ordered by their tickets)
-#pragma unroll
-        for (int m = 0; m < M; ++m) {
-          float4* src = reinterpret_cast<float4*>(ws + (size_t)m * ldo + tile * 128) + lane;
-          const float4 v = __ldcg(src);
-          *src = make_float4(0.f, 0.f, 0.f, 0.f);  // clean for the next call
-          peer::mc_red_add_v4_f32(ws_mc + (size_t)m * ldo + tile * 128 + lane * 4, v);
-        }
-        peer::fence_proxy_alias();
-        __syncwarp();
-        if (lane == 0) {
-          ticket[tile] = 0u;
-          peer::mc_signal_add_u64(flag_mc, 1ull);
-        }
+      for (int f = 0; f < 4; ++f) {
+        atomicAdd(ws + (size_t)m * ldo + tile * 128 + lane * 4 + f, facc[m][f]);
       }
-    }
   };
   uint8_t* lbytes = reinterpret_cast<uint8_t*>(&lsm[warp][0][0][0]);
   while (u < uend) {
@@ -163,7 +140,6 @@ __global__ void __launch_bounds__(kWarps * 32, ctas_per_sm<M>())
     if (t != tile) {
       if (tile >= 0) flush();
       tile = t;
-      tile_units = 0;
 #pragma unroll
       for (int m = 0; m < M; ++m)
 #pragma unroll
@@ -244,10 +220,34 @@ __global__ void __launch_bounds__(kWarps * 32, ctas_per_sm<M>())
       for (int m = 0; m < M; ++m) xcur[m] = xnxt[m];
       scur = snxt;
     }
-    ++tile_units;
     ++u;
   }
   if (tile >= 0) flush();
+  if (flag_mc) {
+    // second phase: the last CTA to finish sends the reduced rows to every rank
+    __shared__ int last;
+    __threadfence();  // this thread's atomics are visible before the ticket
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (last) {
+      __threadfence();  // every other CTA's atomics (ordered by their tickets)
+      for (int r = 0; r < M; ++r) {
+        float4* src = reinterpret_cast<float4*>(ws + (size_t)r * ldo);
+        for (int i = threadIdx.x; i < N / 4; i += blockDim.x) {
+          const float4 v = __ldcg(src + i);
+          src[i] = make_float4(0.f, 0.f, 0.f, 0.f);  // clean for the next call
+          peer::mc_red_add_v4_f32(ws_mc + (size_t)r * ldo + 4 * i, v);
+        }
+      }
+      peer::fence_proxy_alias();
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        *ticket = 0u;
+        peer::mc_signal_add_u64(flag_mc, 1ull);
+      }
+    }
+  }
 }
 
 static int sm_count() {
@@ -317,12 +317,11 @@ extern "C" int k8v4_gemv_w4(const void* w, const void* wscale, const void* x, fl
 }
 
 // GEMM -> all-reduce: the sums meet in `local` (this rank's fp32 [M, ldo]
-// accumulator, zero on entry and left zero); as each 128-feature tile
-// completes, one warp adds it into every rank's copy of a symmetric fp32
-// buffer through its multicast address ws_mc and adds 1 to the multicast
-// counter flag_mc. `ticket` (N / 128 unsigned ints, zero on entry and left
-// zero) counts each tile's finished units. The consumer expects world x
-// N / 128 signals for one call. Calls that overlap on the GPU must not share
+// accumulator, zero on entry and left zero), then the last CTA adds them into
+// every rank's copy of a symmetric fp32 buffer through its multicast address
+// ws_mc and adds 1 to the multicast counter flag_mc; `ticket` (one unsigned
+// int, zero on entry and left zero) picks that CTA. The consumer expects
+// `world` signals for one call. Calls that overlap on the GPU must not share
 // `local` or `ticket`.
 extern "C" int k8v4_gemv_w4_allreduce(const void* w, const void* wscale, const void* x, float* local, float* ws_mc,
                                       unsigned long long* flag_mc, unsigned int* ticket, int M, int N, int K,

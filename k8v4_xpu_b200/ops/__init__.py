@@ -197,9 +197,8 @@ def wq_gemm_allreduce(mode: int, w, wscale, x, ws, ws_mc: int, flag_mc: int, xsc
     symmetric buffer, multicast address ``ws_mc``); the call then signals the
     multicast counter ``flag_mc`` (``wq_gemm_ctas`` times per rank). A
     one-row W4A16 call runs as the decode GEMV, whose partial sums first meet
-    in ``gemv_local`` (fp32, zero, left zero); ``gemv_ticket`` (int32 [N/128],
-    zero, left zero) counts each 128-feature tile's units, and the warp that
-    completes a tile sends it. Returns ``ws``."""
+    in ``gemv_local`` (fp32, zero, left zero) and whose last CTA, picked by
+    ``gemv_ticket`` (int32, zero, left zero), sends the rows. Returns ``ws``."""
     require()
     if x.shape[0] == 0:
         return ws

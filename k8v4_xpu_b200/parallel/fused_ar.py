@@ -45,6 +45,12 @@ def fused_ar_mode() -> str:
     return mode
 
 
+def gemv_fused() -> bool:
+    """``K8V4_TP_GEMV_FUSED=1``: one-row row-parallel GEMMs use the decode
+    GEMV's multicast all-reduce epilogue instead of GEMV + NCCL."""
+    return os.environ.get("K8V4_TP_GEMV_FUSED", "0").strip().lower() in ("1", "true", "yes")
+
+
 class FusedAllReduce:
     SLOTS = 2
 
@@ -76,18 +82,22 @@ class FusedAllReduce:
         # per slot: [signals consumed so far, consumer CTAs done] (local to this rank)
         self.state = torch.zeros((self.SLOTS, 2), dtype=torch.int64, device=self.device)
         # one-row calls (the decode GEMV): per slot a local fp32 row where the
-        # partial sums meet before each 128-feature tile is sent, and the
-        # tiles' tickets
+        # partial sums meet before one CTA sends them, and that CTA's ticket
         self.gemv_local = torch.zeros((self.SLOTS, ops.GEMV_MAX_ROWS * self.hidden), dtype=torch.float32,
                                       device=self.device)
-        self.gemv_ticket = torch.zeros((self.SLOTS, max(1, self.hidden // 128)), dtype=torch.int32,
-                                       device=self.device)
+        self.gemv_ticket = torch.zeros((self.SLOTS, 4), dtype=torch.int32, device=self.device)
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)  # every copy is zero before the first multicast add
         self.calls = 0
 
     def fits(self, rows: int, n: int) -> bool:
-        return rows <= self.max_rows and n == self.hidden
+        """Calls this path serves. One-row calls run as the decode GEMV; there
+        the GEMV followed by an NCCL all-reduce measured faster (TP2, 128K,
+        c = 1: 172.2 tok/s against 161.9 with the GEMV's own multicast
+        epilogue), so they take NCCL unless ``K8V4_TP_GEMV_FUSED=1``."""
+        if rows == 1 and ops.takes_gemv(ops.W4A16, 1, True) and not gemv_fused():
+            return False
+        return 0 < rows <= self.max_rows and n == self.hidden
 
     def gemm(self, linear, slot: int, x: torch.Tensor | None = None, xq: torch.Tensor | None = None,
              xs: torch.Tensor | None = None, split: int | None = None):

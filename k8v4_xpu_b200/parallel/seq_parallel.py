@@ -127,7 +127,10 @@ class SeqParallel:
 
     # ------------------------------------------------------------- layout
     def fits(self, rows: int, hidden: int) -> bool:
-        return 0 < rows <= self.max_rows and hidden == self.hidden
+        """Chunks where every rank owns at least one 128-row tile (smaller
+        steps take the NCCL all-reduce: their collectives are latency, not
+        bandwidth, and a rank without rows would only wait)."""
+        return TILE * self.world <= rows <= self.max_rows and hidden == self.hidden
 
     def begin(self, rows: int) -> None:
         """Set up a chunk of ``rows`` token rows."""

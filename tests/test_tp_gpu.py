@@ -63,6 +63,13 @@ PROMPTS = [list(range(3, 3 + 150)), list(range(100, 100 + 45))]
 TP_MODEL = ModelConfig(name="tp-test", num_layers=2, hidden=1024, num_heads=24, num_kv_heads=4, head_dim=128,
                        intermediate=2048, vocab=8192, max_position=8192)
 SMALL_PROMPTS = [list(range(3, 3 + 40)), list(range(100, 100 + 17))]
+def _sp_prompts(world):
+    """Two prompts whose chunk gives every rank at least one 128-row tile and
+    a ragged last tile."""
+    n = 128 * world + 37
+    return [list(range(3, 3 + n // 2)), list(range(100, 100 + n - n // 2))]
+
+
 TINY_PROMPTS = [[5]]  # one row: the decode GEMV and its multicast all-reduce epilogue
 
 
@@ -109,7 +116,8 @@ def _worker(rank, world, port, q):
     fault_log = open(os.path.join(d, "k8v4_tp_rank%d.log" % rank), "a")
     faulthandler.enable(file=fault_log, all_threads=True)
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
-                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0",
+                      K8V4_TP_GEMV_FUSED="1")  # the one-row multicast GEMV epilogue (opt-in) is covered too
     import torch.distributed as dist
     try:
         from k8v4_xpu_b200 import ops
@@ -131,12 +139,18 @@ def _worker(rank, world, port, q):
         _log(rank, "prefill (nccl all-reduce) done")
         # prefill with the residual sharded by token rows between the fused
         # GEMM -> reduce-scatter and all-gather -> GEMM kernels (twice: the
-        # running signal counts must keep matching)
+        # running signal counts must keep matching), on a chunk where every
+        # rank owns at least one 128-row tile (smaller ones take NCCL)
         from k8v4_xpu_b200.parallel.seq_parallel import SeqParallel
-        m.sp = SeqParallel(None, dev, 512, TP_MODEL.hidden)
+        sp_prompts = _sp_prompts(world)
+        sp_inp = _prefill_inputs(sp_prompts, dev)
+        sp_pages = sum((len(p_) + 15) // 16 for p_ in sp_prompts)
+        caches = [torch.zeros(sp_pages, m.layout.page_bytes, dtype=torch.uint8, device=dev) for _ in m.layers]
+        res["hidden_sp_ref"] = m.forward(sp_inp, caches).float().cpu()
+        m.sp = SeqParallel(None, dev, sum(len(p_) for p_ in sp_prompts), TP_MODEL.hidden)
         for _ in range(2):
-            caches = [torch.zeros(64, m.layout.page_bytes, dtype=torch.uint8, device=dev) for _ in m.layers]
-            res["hidden_sp"] = m.forward(inp, caches).float().cpu()
+            caches = [torch.zeros(sp_pages, m.layout.page_bytes, dtype=torch.uint8, device=dev) for _ in m.layers]
+            res["hidden_sp"] = m.forward(sp_inp, caches).float().cpu()
         res["sp_calls"] = m.sp.calls
         _log(rank, "sequence-parallel prefill done")
         m.sp = None
@@ -229,8 +243,8 @@ def test_tp_matches_tp1(world):
     assert out[0]["sp_calls"] == 2 * 4 * TP_MODEL.num_layers
     for r in range(1, world):
         assert torch.equal(out[0]["hidden_sp"], out[r]["hidden_sp"]), r
-    err = (out[0]["hidden_sp"] - out[0]["hidden"]).abs().max().item()
-    assert err <= 0.02 * out[0]["hidden"].abs().max().item(), err
+    err = (out[0]["hidden_sp"] - out[0]["hidden_sp_ref"]).abs().max().item()
+    assert err <= 0.02 * out[0]["hidden_sp_ref"].abs().max().item(), err
     ref_small = out[0]["small_nccl"]
     err = (out[0]["small_fused"] - ref_small).abs().max().item()
     assert err <= 0.02 * ref_small.abs().max().item(), err
