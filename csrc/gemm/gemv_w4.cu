@@ -109,20 +109,8 @@ __global__ void __launch_bounds__(kWarps * 32, ctas_per_sm<M>())
 #pragma unroll
     for (int j = 0; j < kRows; ++j) dst[j] = ld_stream(base + j * row_vec);
   };
-  // a unit's activations (two per lane and token row) and its 4 group
-  // scales travel one unit ahead too, so the limb preparation and the
-  // epilogue do not wait on an L2 round trip every unit
-  auto load_side = [&](int uu, uint32_t (&xr)[M], uint2& sr) {
-    const int tile = uu / kunits, k0 = (uu - tile * kunits) * 8 * kRows;
-#pragma unroll
-    for (int m = 0; m < M; ++m) xr[m] = *reinterpret_cast<const uint32_t*>(x + (size_t)m * ldx + k0 + 2 * lane);
-    sr = *reinterpret_cast<const uint2*>(wscale + (size_t)(k0 >> 7) * N + tile * 128 + lane * 4);
-  };
   if (u < uend) load_unit(u, cur);
   pdl_wait();  // x comes from the previous kernel, which also re-zeroed ws
-  uint32_t xcur[M];
-  uint2 scur = make_uint2(0u, 0u);
-  if (u < uend) load_side(u, xcur, scur);
 
   int tile = -1;
   float facc[M][4];
@@ -146,14 +134,9 @@ __global__ void __launch_bounds__(kWarps * 32, ctas_per_sm<M>())
         for (int f = 0; f < 4; ++f) facc[m][f] = 0.f;
     }
     uint4 nxt[kRows];
-    uint32_t xnxt[M];
-    uint2 snxt = make_uint2(0u, 0u);
     const bool more = u + 1 < uend;
-    if (more) {
-      load_unit(u + 1, nxt);
-      load_side(u + 1, xnxt, snxt);
-    }
-    (void)ku;
+    if (more) load_unit(u + 1, nxt);
+    const int k0 = ku * 8 * kRows;
     // ---- the warp's own limbs of the unit's 64 activations per token row.
     // Lane l holds k0 + 2l and k0 + 2l + 1: packed row j = l / 4, byte l % 4
     // of the even-k word (codes 0, 2, 4, 6 after the unpack) and of the odd one.
@@ -161,7 +144,8 @@ __global__ void __launch_bounds__(kWarps * 32, ctas_per_sm<M>())
     int csum[M];
 #pragma unroll
     for (int m = 0; m < M; ++m) {
-      const float2 xf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xcur[m]));
+      const __nv_bfloat162 xv = *reinterpret_cast<const __nv_bfloat162*>(x + (size_t)m * ldx + k0 + 2 * lane);
+      const float2 xf = __bfloat1622float2(xv);
       const float am = warp_max(fmaxf(fabsf(xf.x), fabsf(xf.y)));
       const float sc = am > 0.f ? am / kLimbMax : 1.f;
       const float inv = 1.f / sc;
@@ -202,7 +186,8 @@ __global__ void __launch_bounds__(kWarps * 32, ctas_per_sm<M>())
       }
     }
     // group scales of the unit's 4 features (fp16)
-    const __half2* sh = reinterpret_cast<const __half2*>(&scur);
+    const uint2 sraw = *reinterpret_cast<const uint2*>(wscale + (size_t)(k0 >> 7) * N + tile * 128 + lane * 4);
+    const __half2* sh = reinterpret_cast<const __half2*>(&sraw);
     const float2 g01 = __half22float2(sh[0]), g23 = __half22float2(sh[1]);
     const float gsc[4] = {g01.x, g01.y, g23.x, g23.y};
 #pragma unroll
@@ -216,9 +201,6 @@ __global__ void __launch_bounds__(kWarps * 32, ctas_per_sm<M>())
     if (more) {
 #pragma unroll
       for (int j = 0; j < kRows; ++j) cur[j] = nxt[j];
-#pragma unroll
-      for (int m = 0; m < M; ++m) xcur[m] = xnxt[m];
-      scur = snxt;
     }
     ++u;
   }

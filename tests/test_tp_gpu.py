@@ -234,9 +234,11 @@ def test_tp_matches_tp1(world):
     assert out[0]["fused_calls"] == 4 * 2 * TP_MODEL.num_layers
     for r in range(1, world):
         assert torch.equal(out[0]["tiny_fused"], out[r]["tiny_fused"]), r
+    # the fused path adds the ranks' fp32 partials; the NCCL path rounds each
+    # rank's partial row and the sum to bf16 (two layers, one row)
     ref_tiny = out[0]["tiny_nccl"]
     err = (out[0]["tiny_fused"] - ref_tiny).abs().max().item()
-    assert err <= 0.02 * ref_tiny.abs().max().item(), err
+    assert err <= 0.05 * ref_tiny.abs().max().item(), err
     assert out[0]["comm_mode"] == "fused" and out[0]["prefill_mode"] == "sp"
     # sequence-parallel prefill: 4 fused GEMMs per layer, ranks agree exactly,
     # and it matches the NCCL all-reduce path up to bf16 partial sums
