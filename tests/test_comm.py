@@ -213,3 +213,19 @@ def test_sequence_parallel_tiles_cover_the_chunk_once():
             for r0, n in spans:  # contiguous, in rank order
                 assert r0 == at or n == 0
                 at += n
+
+
+def test_sequence_parallel_serves_chunks_where_every_rank_owns_a_tile():
+    """Smaller chunks (a rank would own no row) take the NCCL all-reduce; the
+    engine's fallback depends on `fits` saying so."""
+    from k8v4_xpu_b200.parallel.seq_parallel import TILE, SeqParallel, owned_rows, tile_owners
+    for world in (2, 4, 8):
+        sp = object.__new__(SeqParallel)  # the host bookkeeping only (no buffers)
+        sp.world, sp.max_rows, sp.hidden = world, 4224, 5120
+        for rows in (1, 96, TILE * world - 1, TILE * world, 4224, 4225):
+            ok = sp.fits(rows, 5120)
+            assert ok == (TILE * world <= rows <= 4224), (world, rows)
+            if ok:
+                t0 = tile_owners(rows, world)
+                assert all(owned_rows(rows, t0, o)[1] > 0 for o in range(world))
+        assert not sp.fits(4224, 4096)
