@@ -245,8 +245,10 @@ def test_tp_matches_tp1(world):
     assert out[0]["sp_calls"] == 2 * 4 * TP_MODEL.num_layers
     for r in range(1, world):
         assert torch.equal(out[0]["hidden_sp"], out[r]["hidden_sp"]), r
+    # (each rank's partial rows reach the owner as bf16 and are summed there;
+    # the NCCL path rounds the GEMM output and the all-reduced sum instead)
     err = (out[0]["hidden_sp"] - out[0]["hidden_sp_ref"]).abs().max().item()
-    assert err <= 0.02 * out[0]["hidden_sp_ref"].abs().max().item(), err
+    assert err <= 0.03 * out[0]["hidden_sp_ref"].abs().max().item(), err
     ref_small = out[0]["small_nccl"]
     err = (out[0]["small_fused"] - ref_small).abs().max().item()
     assert err <= 0.02 * ref_small.abs().max().item(), err
