@@ -116,7 +116,7 @@ def _int4_weights(N, K, seed):
     return t["qweight"], t["scales"]
 
 
-@pytest.mark.parametrize("M", [1, 7, 28, 64, 200])
+@pytest.mark.parametrize("M", [1, 7, 28, 64, 96, 200])
 @pytest.mark.parametrize("split", [1, 3])
 def test_w4a16_gemm(M, split):
     N, K = 384, 1024
