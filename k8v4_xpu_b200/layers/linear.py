@@ -163,10 +163,16 @@ class Int8IslandLinear:
     """A dense linear kept resident as per-output-row symmetric int8 weights
     ``q`` [N, K] with bf16 scales [N] (the reference's INT8 island,
     ``k8v4_v030/int8_island.py:60-130``: ``s = max(amax / 127, 1e-12)``,
-    ``q = round(w / s)`` clamped to +-127). The product is W8A16: bf16
-    activations against the weights dequantized by ``k8v4.int8_dequant`` into
-    a shared scratch, then a library bf16 GEMM. Islands halve the weight
-    memory of the dense layers they replace; they are not a hot path.
+    ``q = round(w / s)`` clamped to +-127). The product is W8A16 on the
+    in-tree tcgen05 int8 GEMM: the bf16 activations are split into two int8
+    limbs per row (x ~= s1 q1 + s2 q2, the second quantizing the residual of
+    the first, ~14 bits against the row's amax) and the W8A8 GEMM runs once
+    per limb, both adding fp32 sums into one accumulator that the second
+    call finishes to bf16. The weight bytes are read twice, against five per
+    weight when dequantizing into a bf16 scratch for a library GEMM (kept for
+    shapes the GEMM does not tile: K not a multiple of 128). Islands halve
+    the weight memory of the dense layers they replace; they are not a hot
+    path.
     """
 
     supports_w4a8 = False
@@ -178,6 +184,16 @@ class Int8IslandLinear:
         self.q = q.contiguous()
         self.scale = scale.reshape(-1).to(torch.bfloat16).contiguous()
         self.out_features, self.in_features = q.shape
+        # the int8 GEMM's operands: rows padded to its 128-row tile, fp16
+        # scales (exact for bf16 scales inside the fp16 normal range)
+        self._gemm = None
+        n, k = self.q.shape
+        s32 = self.scale.float().abs()
+        if k % 128 == 0 and bool(((s32 == 0) | ((s32 >= 6.2e-5) & (s32 <= 6.5e4))).all()):
+            pad = (-n) % 128
+            qp = torch.cat([self.q, self.q.new_zeros(pad, k)]) if pad else self.q
+            sp = torch.cat([self.scale, self.scale.new_zeros(pad)]) if pad else self.scale
+            self._gemm = (qp.contiguous(), sp.to(torch.float16).contiguous())
 
     @staticmethod
     def quantize(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
@@ -196,12 +212,26 @@ class Int8IslandLinear:
                  ws=None, split=None, defer: bool = False) -> torch.Tensor:
         if x is None:
             raise ValueError("%s: INT8 islands take bf16 activations" % self.name)
-        w = ops.int8_dequant(self.q, self.scale, _island_scratch(self.q.numel(), self.q.device))
-        y = torch.matmul(x, w.t())
+        if self._gemm is not None and x.is_cuda and x.dim() == 2 and x.shape[0] > 0:
+            y = self._two_limb_gemm(x)
+        else:
+            w = ops.int8_dequant(self.q, self.scale, _island_scratch(self.q.numel(), self.q.device))
+            y = torch.matmul(x, w.t())
         if out is not None:
             out.copy_(y)
             return out
         return y
+
+    def _two_limb_gemm(self, x: torch.Tensor) -> torch.Tensor:
+        qp, sp = self._gemm
+        rows = x.shape[0]
+        q1, s1 = ops.quant_rows(x.contiguous())
+        resid = (x.float() - q1.float() * s1.view(-1, 1)).to(torch.bfloat16)
+        q2, s2 = ops.quant_rows(resid)
+        ws = torch.zeros(rows * qp.shape[0], dtype=torch.float32, device=x.device)
+        ops.wq_gemm(ops.W8A8, qp, sp, q1, xscale=s1, ws=ws, split=2, finish=False)
+        y = ops.wq_gemm(ops.W8A8, qp, sp, q2, xscale=s2, ws=ws, split=2)
+        return y if y.shape[1] == self.out_features else y[:, : self.out_features]
 
     def reference(self, x: torch.Tensor) -> torch.Tensor:
         return x.float() @ (self.q.float() * self.scale.float()[:, None]).t()

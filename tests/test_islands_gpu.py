@@ -13,10 +13,14 @@ from test_engine_gpu import _inputs
 pytestmark = pytest.mark.gpu
 
 
-def test_island_linear_matches_fp32_reference():
+@pytest.mark.parametrize("n", [384, 200])
+def test_island_linear_matches_fp32_reference(n):
+    """The in-tree int8 GEMM over two activation limbs (rows padded to the
+    GEMM's tile for n = 200) against the fp32 product."""
     g = torch.Generator().manual_seed(0)
-    w = torch.randn(384, 1024, generator=g) * 0.02
+    w = torch.randn(n, 1024, generator=g) * 0.02
     lin = Int8IslandLinear.from_dense("x", w, "cuda")
+    assert lin._gemm is not None
     for M in (1, 7, 300):
         x = torch.randn(M, 1024, generator=g).bfloat16()
         y = lin(x.cuda())
