@@ -232,17 +232,20 @@ __global__ void __launch_bounds__(kWarps * 32, ctas_per_sm<M>())
   }
 }
 
+// SM count of the current device, cached per device (host threads may race
+// to fill an entry; they store the same value, and the atomics keep that
+// well defined). The grid size, and so the all-reduce signal count, follows it.
 static int sm_count() {
-  static int cache[64] = {0};
+  static std::atomic<int> cache[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;
   if (dev < 0 || dev >= 64) return 148;
-  if (!cache[dev]) {
-    int n = 0;
+  int n = cache[dev].load(std::memory_order_relaxed);
+  if (n <= 0) {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    cache[dev] = n;
+    cache[dev].store(n, std::memory_order_relaxed);
   }
-  return cache[dev];
+  return n;
 }
 
 // CTAs of one launch (persistent: at most ctas_per_sm per SM).
