@@ -229,3 +229,25 @@ def test_sequence_parallel_serves_chunks_where_every_rank_owns_a_tile():
                 t0 = tile_owners(rows, world)
                 assert all(owned_rows(rows, t0, o)[1] > 0 for o in range(world))
         assert not sp.fits(4224, 4096)
+
+
+def test_tp_decode_all_reduce_routing(monkeypatch):
+    """Which decode calls the fused GEMM -> all-reduce serves: 2-64 rows;
+    one-row calls (the decode GEMV) go to NCCL unless K8V4_TP_GEMV_FUSED=1,
+    and to the tcgen05 epilogue when the GEMV is switched off."""
+    from k8v4_xpu_b200 import ops
+    from k8v4_xpu_b200.parallel.fused_ar import FusedAllReduce
+    far = object.__new__(FusedAllReduce)  # the routing only (no buffers)
+    far.max_rows, far.hidden = 64, 5120
+    monkeypatch.delenv("K8V4_TP_GEMV_FUSED", raising=False)
+    monkeypatch.delenv("K8V4_DECODE_GEMV", raising=False)
+    assert ops.takes_gemv(ops.W4A16, 1, object()) and not ops.takes_gemv(ops.W4A16, 2, object())
+    assert not ops.takes_gemv(ops.W4A8, 1, object()) and not ops.takes_gemv(ops.W4A16, 1, None)
+    assert not far.fits(1, 5120)
+    assert far.fits(2, 5120) and far.fits(64, 5120)
+    assert not far.fits(65, 5120) and not far.fits(4, 4096)
+    monkeypatch.setenv("K8V4_TP_GEMV_FUSED", "1")
+    assert far.fits(1, 5120)
+    monkeypatch.delenv("K8V4_TP_GEMV_FUSED")
+    monkeypatch.setenv("K8V4_DECODE_GEMV", "0")
+    assert not ops.takes_gemv(ops.W4A16, 1, object()) and far.fits(1, 5120)
