@@ -181,6 +181,95 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const __nv_bfloat16* 
   if (sync.flag) peer::sync_done(sync);
 }
 
+// ------------------------------------------------------------ cluster norm
+// The same norm for a few decode rows (no int8 output, no all-reduce wait):
+// one thread-block cluster of kNormCluster CTAs per row, each CTA owning
+// n / kNormCluster columns (one 8-wide vector per thread). The CTAs' partial
+// sums of squares meet through distributed shared memory (each CTA reads the
+// others' partials in CTA-rank order, so every CTA forms the same sum); a
+// single CTA per row spent ~5 us on 5,120 columns, most of it latency.
+constexpr int kNormCluster = 8;
+constexpr int kNormThreads = 128;
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_cluster_kernel(const __nv_bfloat16* __restrict__ x, float* xf,
+                                                                       __nv_bfloat16* residual,
+                                                                       const __nv_bfloat16* __restrict__ w,
+                                                                       __nv_bfloat16* y, int n, int64_t ldy,
+                                                                       float eps) {
+  pdl_trigger();
+  __shared__ float red[kNormThreads / 32];
+  __shared__ float part;
+  const int64_t row = blockIdx.y;
+  const int per = n / kNormCluster;                 // columns of this CTA (a multiple of 8)
+  const int c = blockIdx.x * per + threadIdx.x * 8;  // blockIdx.x is the CTA's rank in the cluster
+  const bool mine = threadIdx.x * 8 < per;
+  // the norm weights come from no earlier kernel: load them before waiting
+  const uint4 gw = mine ? *reinterpret_cast<const uint4*>(w + c) : make_uint4(0u, 0u, 0u, 0u);
+  pdl_wait();  // x / xf / residual may come from the previous kernel
+  float v[8];
+  float ss = 0.f;
+  if (mine) {
+    if (xf) {
+      float4* p4 = reinterpret_cast<float4*>(xf + row * n + c);
+      const float4 a = p4[0], b = p4[1];
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+      v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      p4[0] = make_float4(0.f, 0.f, 0.f, 0.f);  // the shared split-K accumulator stays clean
+      p4[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    } else {
+      load8(x + row * n + c, v);
+    }
+    if (residual) {
+      float rs[8];
+      load8(residual + row * n + c, rs);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = __bfloat162float(__float2bfloat16_rn(v[j] + rs[j]));
+      store8(residual + row * n + c, v);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss += v[j] * v[j];
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < kNormThreads / 32; ++i) t += red[i];
+    part = t;
+  }
+  cluster_sync_all();  // every CTA's partial is written
+  float total = 0.f;
+  {
+    const uint32_t local = static_cast<uint32_t>(__cvta_generic_to_shared(&part));
+#pragma unroll
+    for (int r = 0; r < kNormCluster; ++r) {
+      uint32_t remote;
+      float pv;
+      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(r));
+      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(pv) : "r"(remote) : "memory");
+      total += pv;
+    }
+  }
+  const float inv = rsqrtf(total / (float)n + eps);
+  if (mine) {
+    const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gw);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 g = __bfloat1622float2(g2[j]);
+      v[2 * j] = __bfloat162float(__float2bfloat16_rn(__bfloat162float(__float2bfloat16_rn(v[2 * j] * inv)) * g.x));
+      v[2 * j + 1] =
+          __bfloat162float(__float2bfloat16_rn(__bfloat162float(__float2bfloat16_rn(v[2 * j + 1] * inv)) * g.y));
+    }
+    store8(y + row * ldy + c, v);
+  }
+  cluster_sync_all();  // no CTA leaves while another still reads its partial
+}
+
 // gu: [T, 2I] = [gate | up]. out = silu(gate) * up (bf16 and/or int8 + scale).
 template <int VPT>
 __global__ void __launch_bounds__(kThreads) silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* y,
@@ -507,12 +596,44 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_sp_kernel(
     else return 2;                                                                \
   } while (0)
 
+// A few decode rows without int8 output or all-reduce wait run on a cluster
+// per row (rmsnorm_cluster_kernel) unless K8V4_NORM_CLUSTER=0.
+static bool norm_cluster_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("K8V4_NORM_CLUSTER");
+    return !(v && (v[0] == '0' || v[0] == 'n' || v[0] == 'N' || v[0] == 'f' || v[0] == 'F'));
+  }();
+  return on;
+}
+
 extern "C" int k8v4_rmsnorm(const void* x, float* xf, void* residual, const void* w, void* y, int64_t ldy, void* yq,
                             float* yscale, int rows, int n, float eps, const unsigned long long* sync_flag,
                             unsigned long long* sync_state, unsigned long long sync_expected, cudaStream_t st) {
   if (rows <= 0) return 0;
   if (n % 8 || ldy < n || ldy % 8) return 1;
   if (sync_flag && (!xf || !sync_state)) return 4;
+  if (rows <= 4 && !yq && y && !sync_flag && n % (8 * kNormCluster) == 0 && n / kNormCluster <= 8 * kNormThreads &&
+      norm_cluster_enabled()) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kNormCluster, rows);
+    cfg.blockDim = dim3(kNormThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kNormCluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, rmsnorm_cluster_kernel, reinterpret_cast<const __nv_bfloat16*>(x),
+                                             xf, reinterpret_cast<__nv_bfloat16*>(residual),
+                                             reinterpret_cast<const __nv_bfloat16*>(w),
+                                             reinterpret_cast<__nv_bfloat16*>(y), n, ldy, eps);
+    return e == cudaSuccess ? 0 : 3;
+  }
   peer::ReduceSync sync{sync_flag, sync_state, sync_expected};
   K8V4_VPT_DISPATCH(n, rmsnorm_kernel, reinterpret_cast<const __nv_bfloat16*>(x), xf,
                     reinterpret_cast<__nv_bfloat16*>(residual), reinterpret_cast<const __nv_bfloat16*>(w),

@@ -426,6 +426,31 @@ def test_rmsnorm_and_quant():
     assert (q.cpu().int() - q_ref.int()).abs().max().item() <= 1
 
 
+@pytest.mark.parametrize("T", [1, 3])
+@pytest.mark.parametrize("fp32_sums", [False, True])
+def test_rmsnorm_decode_rows(T, fp32_sums):
+    """A few decode rows run one thread-block cluster per row (partial sums
+    of squares through distributed shared memory): residual stream exact,
+    output within bf16 rounding of the fp32 reference, and fp32 split-K sums
+    consumed and zeroed."""
+    n = 5120
+    x = torch.randn(T, n, generator=_gen(40))
+    r = torch.randn(T, n, generator=_gen(41)).bfloat16()
+    w = (1 + 0.1 * torch.randn(n, generator=_gen(42))).bfloat16()
+    xin = x.to(DEV) if fp32_sums else x.bfloat16().to(DEV)
+    h = (xin.float().cpu() + r.float()).bfloat16()
+    hf = h.float()
+    y_ref = (w.float() * (hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + 1e-6)).bfloat16().float()).bfloat16()
+    rd = r.to(DEV)
+    y = ops.rmsnorm(xin, w.to(DEV), 1e-6, residual=rd)
+    torch.cuda.synchronize()
+    assert ops.status() == 0
+    assert torch.equal(rd.cpu(), h)
+    assert (y.float().cpu() - y_ref.float()).abs().max().item() <= 0.02
+    if fp32_sums:
+        assert torch.count_nonzero(xin).item() == 0
+
+
 def test_rmsnorm_into_strided_halves():
     """Two norms writing the halves of one concatenated row (the MTP input)."""
     T, n = 7, 512
