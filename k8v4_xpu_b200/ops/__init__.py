@@ -161,7 +161,10 @@ def wq_gemm(mode: int, w: torch.Tensor, wscale: torch.Tensor, x: torch.Tensor, x
             out=None, ws=None, split: int = 1, finish: bool = True) -> torch.Tensor:
     """Quantized-weight GEMM. With ``split > 1`` and ``finish=False`` the fp32
     partial sums stay in ``ws`` for a consumer that finishes them (the fused
-    RMSNorm); ``out`` is then not written."""
+    RMSNorm); ``out`` is then not written. A one-row W4A16 call given ``ws``
+    runs as the decode GEMV (``takes_gemv``), which adds into ``ws`` even at
+    ``split == 1``: a workspace passed here must be all zero, and it is left
+    zero unless ``finish=False``."""
     require()
     n = w.shape[0] if mode == W8A8 else w.shape[1]
     if out is None:
