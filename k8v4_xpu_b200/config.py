@@ -204,8 +204,6 @@ class ServeConfig:
                 raise ValueError("--forced-accept-mean needs --speculative-config")
             if not 1.0 <= self.forced_accept_mean <= self.speculative_tokens + 1:
                 raise ValueError("--forced-accept-mean must lie in [1, %d]" % (self.speculative_tokens + 1))
-        if self.context_parallel_size > 1 and self.speculative_tokens:
-            raise ValueError("--speculative-config (MTP) is not supported with --context-parallel-size")
         if self.kv_cache_dtype_skip_layers:
             if self.context_parallel_size > 1:
                 raise ValueError("--kv-cache-dtype-skip-layers is not supported with --context-parallel-size")

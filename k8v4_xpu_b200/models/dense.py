@@ -233,10 +233,10 @@ class DenseModel:
         if cp.peer is not None and cp.peer.fits(rank_floats):
             # partials exchanged by the attention kernel itself (multicast stores)
             return cp.peer.attention(q, inp.cu_q, inp.cp_local_lens, inp.cp_local_bt, cache, hkv, gqa,
-                                     inp.max_q_len, nsplit)
+                                     inp.max_q_len, nsplit, q_ends=inp.q_ends)
         ws = torch.empty(rank_floats, dtype=torch.float32, device=self.device)
         ops.decode_attn(q, inp.cu_q, inp.cp_local_lens, inp.cp_local_bt, cache, hkv, gqa, inp.max_q_len,
-                        nsplit=nsplit, ws=ws)
+                        nsplit=nsplit, ws=ws, q_ends=inp.q_ends)
         out = torch.empty_like(q)
         return ops.decode_combine_ranks(cp.all_gather(ws), rank_floats, inp.cu_q, cp.world, nsplit, hkv, gqa,
                                         inp.max_q_len, out)

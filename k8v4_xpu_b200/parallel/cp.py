@@ -108,3 +108,38 @@ class CPGroup:
         if self.owner(pos) != self.rank:
             return -1
         return blocks[pos // (PAGE * self.world)] * PAGE + pos % PAGE
+
+    def broadcast_(self, t: torch.Tensor) -> torch.Tensor:
+        """Overwrite ``t`` with CP rank 0's copy, so that decisions the host
+        takes from device results (accepted drafts, next tokens) are the same
+        on every rank even where fp32 atomics left the ranks' sums a rounding
+        apart."""
+        dist.broadcast(t, src=dist.get_global_rank(self.group, 0), group=self.group)
+        return t
+
+
+def local_keys(n, rank: int, world: int):
+    """Keys among a sequence's first ``n`` positions that CP rank ``rank``
+    holds (its pages are logical pages rank, rank + world, ... of PAGE keys).
+
+    Because a rank's pages are in position order, those keys are a prefix of
+    its local key list: the keys that a query row at position ``n - 1`` may
+    see. Works on ints and, elementwise, on integer tensors."""
+    full = n // PAGE
+    rem = n - full * PAGE
+    # logical pages i < full with i % world == rank (never negative: rank < world)
+    nfull = (full - rank + world - 1) // world
+    if isinstance(n, torch.Tensor):
+        return nfull * PAGE + torch.where(full % world == rank, rem, torch.zeros_like(rem))
+    return nfull * PAGE + (rem if full % world == rank else 0)
+
+
+def local_slots(blk: torch.Tensor, nblk: torch.Tensor, pos: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """Device form of :meth:`CPGroup.slot` for one position per sequence:
+    ``blk`` [B, W] the sequences' block ids (zero padded), ``nblk`` [B] how
+    many are real, ``pos`` [B] int64. -1 where another rank owns the page or
+    the position lies past the sequence's blocks."""
+    b = pos // (PAGE * world)
+    own = ((pos // PAGE) % world == rank) & (b < nblk)
+    page = blk.gather(1, b.clamp(max=blk.shape[1] - 1).view(-1, 1)).view(-1).to(torch.int64)
+    return torch.where(own, page * PAGE + pos % PAGE, torch.full_like(pos, -1))

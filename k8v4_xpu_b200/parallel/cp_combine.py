@@ -102,14 +102,15 @@ class PeerCombine:
         return rank_floats <= self.slot_floats
 
     def attention(self, q, cu_q, local_lens, local_bt, cache, hkv: int, gqa: int, max_q_len: int,
-                  nsplit: int) -> torch.Tensor:
+                  nsplit: int, q_ends=None) -> torch.Tensor:
         """This rank's decode attention over its own pages, exchanged and
-        merged with every rank's: returns the full attention output."""
+        merged with every rank's: returns the full attention output.
+        ``q_ends`` [T]: per-row visible local key counts (MTP verify rows)."""
         B = cu_q.numel() - 1
         rank_floats = ops.decode_ws_floats(B, hkv, nsplit, max_q_len, gqa)
         b, base, mine = slot_layout(self.calls, self.world, self.rank, rank_floats, self.slot_floats, self.SLOTS)
         ops.decode_attn_push(q, cu_q, local_lens, local_bt, cache, hkv, gqa, max_q_len, nsplit,
-                             self.data_mc + 4 * mine, self.flag_mc + 8 * b)
+                             self.data_mc + 4 * mine, self.flag_mc + 8 * b, q_ends=q_ends)
         out = torch.empty_like(q)
         expected = self.world * ops.decode_push_ctas(B, hkv, nsplit)
         ops.decode_combine_ranks(self.data[base: base + self.world * rank_floats], rank_floats, cu_q, self.world,

@@ -18,7 +18,9 @@ all-gather (``K8V4_CP_COMBINE=nccl``) or, by default, multicast stores from the 
 attention kernel (``parallel.cp_combine``). Tensor parallelism inside each
 CP rank (CP x TP, ``parallel.groups``) shards the model over the TP group as
 in the plain engine; the CP exchange then runs between the ranks that hold
-the same KV heads. MTP under CP is not supported yet.
+the same KV heads. MTP speculative decoding runs through
+``spec.mtp_cp.CPMTPSpeculator`` (the MTP layer's pages are sharded like the
+others).
 """
 from __future__ import annotations
 
@@ -40,8 +42,6 @@ class CPEngine(LLMEngine):
     and ``rank`` this process's TP rank (``parallel.groups``)."""
 
     def __init__(self, cfg, model_cfg, cp: CPGroup, rank: int = 0, comm=None):
-        if cfg.speculative_tokens:
-            raise NotImplementedError("context parallelism runs without MTP")
         if cfg.tensor_parallel_size > 1 and comm is None:
             raise ValueError("tensor parallelism inside a CP group needs the TP group's communicator")
         if cfg.context_parallel_size != cp.world:
@@ -53,6 +53,9 @@ class CPEngine(LLMEngine):
         super().__init__(cfg, model_cfg, comm=comm, rank=rank)
         self.model.cp = cp
         self.cp_rank = cp.rank
+        if cfg.speculative_tokens:
+            from ..spec.mtp_cp import CPMTPSpeculator
+            self.mtp = CPMTPSpeculator(self, cfg.speculative_tokens, cfg.forced_accept_mean, cfg.seed)
         self.cp_graphs = CPDecodeGraphs(self) if cp_graphs_enabled() else None
         # shutdown paths release `graphs` before the process group goes
         self.graphs = self.cp_graphs
@@ -60,7 +63,8 @@ class CPEngine(LLMEngine):
             sh = self.model.shape
             try:
                 cp.peer = PeerCombine(cp.group, self.device,
-                                      max_slot_floats(cfg.max_num_seqs, sh.hkv_local, 1, sh.gqa_local))
+                                      max_slot_floats(cfg.max_num_seqs, sh.hkv_local, 1 + cfg.speculative_tokens,
+                                                      sh.gqa_local))
             except Exception as e:  # no multicast on this box: NCCL all-gather
                 import logging
                 logging.getLogger("k8v4").warning("peer partial exchange unavailable (%s); using NCCL", e)
@@ -68,7 +72,7 @@ class CPEngine(LLMEngine):
     def _alloc_cache(self) -> None:
         cfg = self.cfg
         page_bytes = self.layout.page_bytes
-        n_layers = len(self.model.layers)
+        n_layers = len(self.model.layers) + (1 if self.model.mtp is not None else 0)
         if cfg.num_kv_blocks is not None:
             blocks = int(cfg.num_kv_blocks)
         else:
@@ -142,12 +146,24 @@ class CPEngine(LLMEngine):
         self.h2d_bytes += T * 8 * 3 + B * 4 * 3
         return inp, owned_logit
 
+    def _agree(self, ids: torch.Tensor) -> torch.Tensor:
+        """Decode rows are replicated on every CP rank, but the fp32 atomics
+        of a GEMM can sum in a different order on each, so a near-tie of two
+        logits can break differently; CP rank 0's ids win."""
+        return self.cp.broadcast_(ids)
+
     def _plain_step(self, sched):
         if self.cp_graphs is not None and sched.is_decode_only and self.cp_graphs.can_run(sched):
             return self._commit(sched, self.cp_graphs.run(sched))
         inp, owned = self._build_inputs(sched)
         n_logit = sum(1 for c in sched.chunks if c.needs_logits)
-        hidden = self.model.forward(inp, self.kv_caches, self.ws)
+        hid_all = None
+        if self.mtp is not None and not sched.is_decode_only:
+            # the MTP layer catches up on every row this rank owns
+            hid_all = self.model.forward(inp, self.kv_caches, self.ws, all_rows=True)
+            hidden = hid_all.index_select(0, inp.logit_rows)
+        else:
+            hidden = self.model.forward(inp, self.kv_caches, self.ws)
         if sched.is_decode_only:
             tokens = self._sample(hidden) if n_logit else np.zeros(0, np.int64)
         else:
@@ -160,6 +176,8 @@ class CPEngine(LLMEngine):
             all_tok = vec.cpu().numpy()
             self.d2h_bytes += all_tok.size * 8
             tokens = np.array([all_tok[i] for i, c in enumerate(sched.chunks) if c.needs_logits], np.int64)
+            if hid_all is not None:
+                self.mtp.after_prefill_cp(sched, inp, hid_all, all_tok)
         return self._commit(sched, tokens)
 
 
@@ -233,11 +251,11 @@ class CPDecodeGraphs:
         stream.wait_stream(torch.cuda.current_stream(eng.device))
         with torch.cuda.stream(stream):
             for _ in range(2):  # warm-up: kernel attributes, allocator, communicator
-                out = eng.model.greedy(eng.model.forward(inp, eng.kv_caches, eng.ws))
+                out = eng._agree(eng.model.greedy(eng.model.forward(inp, eng.kv_caches, eng.ws)))
         torch.cuda.current_stream(eng.device).wait_stream(stream)
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, pool=self.pool, stream=stream):
-            out = eng.model.greedy(eng.model.forward(inp, eng.kv_caches, eng.ws))
+            out = eng._agree(eng.model.greedy(eng.model.forward(inp, eng.kv_caches, eng.ws)))
         if self.pool is None:
             self.pool = g.pool()
         torch.cuda.synchronize(eng.device)

@@ -337,8 +337,13 @@ class LLMEngine:
             tokens = self._sample(hidden) if rows else np.zeros(0, np.int64)
         return self._commit(sched, tokens)
 
+    def _agree(self, ids: torch.Tensor) -> torch.Tensor:
+        """Hook for engines whose ranks sample replicated rows (context
+        parallelism): makes every rank hold the same ids."""
+        return ids
+
     def _sample(self, hidden: torch.Tensor) -> np.ndarray:
-        ids = self.model.greedy(hidden)
+        ids = self._agree(self.model.greedy(hidden))
         n = ids.numel()
         out = self._pin_out[:n]
         out.copy_(ids, non_blocking=True)

@@ -122,8 +122,9 @@ def test_build_engine_picks_the_context_parallel_engine(monkeypatch):
     cfg = config.resolve(["--model", "tiny", "--tensor-parallel-size", "2"], env={})
     cli.build_engine(cfg, comm="tp-comm", rank=1, device="cpu")
     assert made[-1][0] == "LLMEngine" and made[-1][3] == {"comm": "tp-comm", "rank": 1}
-    with pytest.raises(ValueError):
-        config.resolve(["--context-parallel-size", "2", "--speculative-config", "mtp/6"], env={})
+    # MTP under CP resolves (the CP engine drafts through spec.mtp_cp)
+    cfg = config.resolve(["--context-parallel-size", "2", "--speculative-config", "mtp/6"], env={})
+    assert cfg.context_parallel_size == 2 and cfg.speculative_tokens == 6
 
 
 def test_out_of_range_values_are_refused_up_front():

@@ -30,7 +30,7 @@ def _log(rank, msg):
         f.write(msg + "\n")
 
 
-def _worker(rank, world, port, q, combine="nccl", graphs=False):
+def _worker(rank, world, port, q, combine="nccl", graphs=False, spec=0):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), K8V4_CP_COMBINE=combine, K8V4_CP_GRAPHS="1" if graphs else "0")
     import torch.distributed as dist
@@ -45,7 +45,8 @@ def _worker(rank, world, port, q, combine="nccl", graphs=False):
         init_from_env(timeout_s=60)
         _log(rank, "init")
         cfg = EngineConfig(model="tiny", context_parallel_size=world, max_model_len=2048, max_num_seqs=2,
-                           max_num_batched_tokens=96, num_kv_blocks=96, device="cuda:%d" % rank)
+                           max_num_batched_tokens=96, num_kv_blocks=96, speculative_tokens=spec,
+                           device="cuda:%d" % rank)
         eng = CPEngine(cfg, TINY, CPGroup())
         _log(rank, "engine")
         seqs = [eng.add_request(p, SamplingParams(max_tokens=10, ignore_eos=True)) for p in PROMPTS]
@@ -58,7 +59,8 @@ def _worker(rank, world, port, q, combine="nccl", graphs=False):
         outs = [s.output for s in seqs]
         torch.cuda.synchronize()
         res = {"outs": outs, "status": ops.status(), "peer": eng.cp.peer is not None,
-               "graphs": sorted(eng.cp_graphs.graphs) if eng.cp_graphs is not None else None}
+               "graphs": sorted(eng.cp_graphs.graphs) if eng.cp_graphs is not None else None,
+               "verify_steps": eng.mtp.stats.num_drafts if eng.mtp is not None else 0}
         if eng.graphs is not None:
             eng.graphs.release()  # graphs holding NCCL calls go before the process group
         q.put((rank, res))
@@ -97,6 +99,36 @@ def test_cp2_generation_matches_tp1_greedy(combine, graphs):
             assert out[r]["graphs"] and set(out[r]["graphs"]) <= {1, 2}
         else:
             assert out[r]["graphs"] is None
+    assert out[0]["outs"] == out[1]["outs"]
+    m = DenseModel(TINY, device="cuda:0").random_init(seed=0)
+    for p, o in zip(PROMPTS, out[0]["outs"]):
+        assert len(o) == 10
+        assert _teacher_forced_margin(m, p, o) < 0.05
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("combine", ["nccl", "peer"])
+def test_cp2_mtp_generation_matches_tp1_greedy(combine):
+    """MTP6 under CP2 (spec.mtp_cp): verify rows with per-row local visible
+    ends, the MTP layer's pages sharded like the others, drafts from the
+    owner's catch-up row. The output is the target's greedy continuation
+    whatever the drafter proposes."""
+    from test_mtp_gpu import _teacher_forced_margin
+    from k8v4_xpu_b200.models.config import TINY
+    from k8v4_xpu_b200.models.dense import DenseModel
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, combine, False, 6)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = dict(q.get(timeout=240) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+    for r in range(2):
+        assert "error" not in out[r], out[r].get("error")
+        assert out[r]["status"] == 0
+        assert out[r]["verify_steps"] > 0
     assert out[0]["outs"] == out[1]["outs"]
     m = DenseModel(TINY, device="cuda:0").random_init(seed=0)
     for p, o in zip(PROMPTS, out[0]["outs"]):
