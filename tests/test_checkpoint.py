@@ -193,3 +193,32 @@ def test_checkpoint_files_are_written_atomically_config_last(tmp_path, monkeypat
     names = set(os.listdir(tmp_path / "b"))
     assert "config.json" in names and C.SIDE_FILE in names
     assert not any(n.endswith(".partial") for n in names)
+
+
+def test_27b_shards_meet_the_kernels_tiling_at_every_tp():
+    """The headline model's per-rank shapes at TP 1/2/4/8 fit the GEMMs'
+    128-wide feature and k tiles (the lm_head pads its vocab shard), the
+    decode kernels' head layout, and the sequence-parallel prefill: every
+    chunk of the 128,197-token benchmark prompt gives every rank a tile."""
+    from k8v4_xpu_b200.models.config import DENSE_27B, TPShape
+    from k8v4_xpu_b200.parallel.seq_parallel import TILE, SeqParallel, owned_rows, tile_owners
+    cfg = DENSE_27B
+    D, H = cfg.head_dim, cfg.hidden
+    ctx, chunk = 128197, 4224
+    chunks = [min(chunk, ctx - s) for s in range(0, ctx, chunk)]
+    for tp in (1, 2, 4, 8):
+        sh = TPShape.make(cfg, tp)
+        gemms = {"qkv": ((sh.hq_local + 2 * sh.hkv_local) * D, H), "o": (H, sh.hq_local * D),
+                 "gate_up": (2 * sh.inter_local, H), "down": (H, sh.inter_local)}
+        for name, (n, k) in gemms.items():
+            assert n % 128 == 0 and k % 128 == 0, (tp, name, n, k)
+        assert sh.hkv_local >= 1 and sh.gqa_local * 7 <= 64  # MTP verify rows per KV head in one decode tile
+        assert H % 64 == 0 and sh.vocab_local % 8 == 0       # cluster norm slices, argmax vector loads
+        if tp > 1:
+            sp = object.__new__(SeqParallel)
+            sp.world, sp.max_rows, sp.hidden = tp, chunk, H
+            for rows in chunks:
+                assert sp.fits(rows, H), (tp, rows)
+                t0 = tile_owners(rows, tp)
+                assert all(owned_rows(rows, t0, o)[1] > 0 for o in range(tp)), (tp, rows)
+            assert TILE * tp <= min(chunks)
