@@ -50,10 +50,11 @@ GATHERS = 3    # 0: bf16 rows for qkv, 1: int8 rows (+ scales) for a W4A8 gate/u
 
 
 def sp_mode() -> str:
-    """``K8V4_TP_PREFILL`` = ``sp`` (default: the fused reduce-scatter /
-    all-gather prefill where the box supports multicast) or ``nccl`` (each
-    row-parallel GEMM followed by an NCCL all-reduce)."""
-    mode = os.environ.get("K8V4_TP_PREFILL", "sp").strip().lower()
+    """``K8V4_TP_PREFILL`` = ``nccl`` (default: each row-parallel GEMM
+    followed by an NCCL all-reduce; measured 6 % faster at TP2) or ``sp``
+    (the fused reduce-scatter / all-gather prefill where the box supports
+    multicast)."""
+    mode = os.environ.get("K8V4_TP_PREFILL", "nccl").strip().lower()
     if mode not in ("sp", "nccl"):
         raise ValueError("K8V4_TP_PREFILL must be sp or nccl, got %r" % mode)
     return mode

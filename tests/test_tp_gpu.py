@@ -117,7 +117,9 @@ def _worker(rank, world, port, q):
     faulthandler.enable(file=fault_log, all_threads=True)
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0",
-                      K8V4_TP_GEMV_FUSED="1")  # the one-row multicast GEMV epilogue (opt-in) is covered too
+                      # the opt-in paths are covered too: the one-row multicast GEMV
+                      # epilogue and the sequence-parallel prefill
+                      K8V4_TP_GEMV_FUSED="1", K8V4_TP_PREFILL="sp")
     import torch.distributed as dist
     try:
         from k8v4_xpu_b200 import ops
