@@ -19,7 +19,7 @@ from __future__ import annotations
 
 from collections.abc import Sequence
 
-from ..kv.layout import B200_FORMAT, PageLayout, b200_layout
+from ..kv.layout import B200_FORMAT, PageLayout
 
 DECODE_MAX_ROWS = 64  # query rows (tokens x GQA) one decode CTA holds
 

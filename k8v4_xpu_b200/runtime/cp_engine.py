@@ -32,7 +32,7 @@ import torch
 from ..models.dense import StepInputs
 from ..parallel.cp import PAGE, CPGroup
 from ..parallel.cp_combine import PeerCombine, cp_combine_mode, max_slot_floats
-from .block_manager import BlockManager, CapacityError
+from .block_manager import CapacityError
 from .engine import LLMEngine, decode_splits
 
 

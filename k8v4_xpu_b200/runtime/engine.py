@@ -21,7 +21,6 @@ batched tokens, prefix caching, MTP6, FULL_DECODE_ONLY graphs).
 from __future__ import annotations
 
 import dataclasses
-import math
 import os
 import time
 
@@ -30,7 +29,6 @@ import torch
 
 from .. import ops
 from ..kv import skip_layers
-from ..kv.layout import ATTN_TILE_ROWS
 from ..models.config import ModelConfig
 from ..models.dense import DenseModel, StepInputs
 from .block_manager import BlockManager, CapacityError

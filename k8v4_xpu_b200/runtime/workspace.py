@@ -41,7 +41,3 @@ class Workspace:
         self.write_en = torch.zeros(max_seqs, dtype=torch.int64, device=self.device)
         self.forced_a = torch.zeros(max_seqs, dtype=torch.int64, device=self.device)
 
-    def splitk_view(self, rows: int, n: int) -> torch.Tensor:
-        if rows * n > self.splitk.numel():
-            raise RuntimeError("split-K workspace too small for %dx%d" % (rows, n))
-        return self.splitk[: rows * n].view(rows, n)

@@ -4,7 +4,7 @@ import torch
 
 from k8v4_xpu_b200 import ops
 from k8v4_xpu_b200.attention.backend import K8V4AttentionImpl, K8V4MetadataBuilder
-from k8v4_xpu_b200.attention.reference import eager_prefill, gather_dequant_head
+from k8v4_xpu_b200.attention.reference import eager_prefill
 from k8v4_xpu_b200.kv.layout import b200_layout
 from k8v4_xpu_b200.kv.pack import gather_sequence, store_tokens
 

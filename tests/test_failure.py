@@ -4,7 +4,6 @@ import socket
 import time
 import traceback
 
-import pytest
 import torch
 import torch.multiprocessing as mp
 

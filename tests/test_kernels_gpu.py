@@ -1,6 +1,5 @@
 """Numerics of the sm_100a kernels against plain PyTorch fp32 references."""
 import ctypes
-import math
 
 import pytest
 import torch
