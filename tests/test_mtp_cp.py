@@ -195,3 +195,47 @@ def test_local_keys_and_slots_match_the_page_map():
                         assert s == -1  # past the sequence's blocks
                     else:
                         assert s == g.slot(blocks, p)
+
+
+def test_verify_rows_merge_to_full_causal_attention():
+    """Per-rank partial attention of MTP verify rows, each row seeing the
+    first ``local_keys(p + 1)`` keys of the rank's local list, merged over
+    the ranks by (m, l, O), equals causal attention over every key (fp32)."""
+    from k8v4_xpu_b200.parallel.cp import PAGE, local_keys
+    g = torch.Generator().manual_seed(0)
+    L, D, w = 16 * 11 + 5, 32, 7
+    k = torch.randn(L, D, generator=g)
+    v = torch.randn(L, D, generator=g)
+    q = torch.randn(w, D, generator=g)
+    rows = list(range(L - w, L))  # verify rows at the last w positions
+    for world in (2, 3, 4, 8):
+        m_all, l_all, o_all = [], [], []
+        for r in range(world):
+            local = [p for p in range(L) if (p // PAGE) % world == r]  # this rank's keys, page order
+            ms, ls, os_ = [], [], []
+            for i, p in enumerate(rows):
+                n = local_keys(p + 1, r, world)
+                vis = local[:n]
+                assert vis == [x for x in local if x <= p]  # a prefix of the local list
+                if not vis:
+                    ms.append(torch.tensor(float("-inf")))
+                    ls.append(torch.tensor(0.0))
+                    os_.append(torch.zeros(D))
+                    continue
+                s = k[vis] @ q[i] / D ** 0.5
+                m = s.max()
+                e = torch.exp(s - m)
+                ms.append(m)
+                ls.append(e.sum())
+                os_.append(e @ v[vis])
+            m_all.append(torch.stack(ms))
+            l_all.append(torch.stack(ls))
+            o_all.append(torch.stack(os_))
+        m = torch.stack(m_all)            # [ranks, w]
+        M = m.max(0).values
+        wgt = torch.exp(m - M)            # exp(-inf) = 0 for a rank with no visible key
+        out = (wgt.unsqueeze(-1) * torch.stack(o_all)).sum(0) / (wgt * torch.stack(l_all)).sum(0).unsqueeze(-1)
+        for i, p in enumerate(rows):
+            s = k[:p + 1] @ q[i] / D ** 0.5
+            ref = torch.softmax(s, 0) @ v[:p + 1]
+            assert torch.allclose(out[i], ref, atol=1e-5), (world, p)
