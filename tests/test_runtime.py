@@ -323,3 +323,45 @@ def test_block_manager_keeps_no_state_for_finished_sequences():
     bm.allocate(7, [1, 2, 3])
     assert bm.version[7] not in seen
     bm.check_invariants()
+
+
+def test_engine_fork_and_private_clone_copy_the_kv_pages():
+    """``fork_sequence`` shares the parent's full blocks and copies its tail
+    block's pages in every layer; ``clone_sequence_private`` copies every
+    written page into blocks of its own. The engine's host logic runs on CPU
+    tensors standing in for the KV pools."""
+    import types
+    from k8v4_xpu_b200.runtime.engine import LLMEngine
+    page, block, page_bytes = 16, 32, 8
+    eng = object.__new__(LLMEngine)  # host logic only (no model, no GPU)
+    eng.device = torch.device("cpu")
+    eng.blocks = BlockManager(12, block_size=block, page=page, enable_prefix_caching=False)
+    eng.scheduler = Scheduler(eng.blocks, 4, 256, 1, 4096)
+    eng.layout = types.SimpleNamespace(page=page)
+    ratio = block // page
+    eng.kv_caches = [torch.zeros((12 * ratio, page_bytes), dtype=torch.uint8) for _ in range(2)]
+    seq = eng.add_request(list(range(70)), SamplingParams(max_tokens=8))
+    eng.scheduler.schedule()
+    seq.computed = 70
+    for li, layer in enumerate(eng.kv_caches):  # every page of the pools carries its id and layer
+        layer.copy_((torch.arange(layer.shape[0]).view(-1, 1) * 3 + li).to(torch.uint8).expand_as(layer))
+    parent = list(eng.blocks.tables[seq.seq_id])
+    assert len(parent) == 3  # 70 tokens in 32-token blocks: two full, one partial
+
+    child = eng.fork_sequence(seq)
+    ct = eng.blocks.tables[child.seq_id]
+    assert ct[:2] == parent[:2] and ct[2] != parent[2]
+    assert child.computed == 70 and child in eng.scheduler.running
+    for layer in eng.kv_caches:
+        src, dst = parent[2], ct[2]
+        assert torch.equal(layer[dst * ratio:(dst + 1) * ratio], layer[src * ratio:(src + 1) * ratio])
+
+    clone = eng.clone_sequence_private(seq)
+    cp_pages = eng.blocks.page_table(clone.seq_id)
+    pp = eng.blocks.page_table(seq.seq_id)
+    n = (70 + page - 1) // page
+    assert not set(cp_pages[:n]) & set(pp[:n])  # nothing shared
+    for layer in eng.kv_caches:
+        assert torch.equal(layer[cp_pages[:n]], layer[pp[:n]])
+    assert clone.computed == 70 and clone.prompt == seq.prompt
+    eng.blocks.check_invariants()
