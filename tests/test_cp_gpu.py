@@ -126,3 +126,37 @@ def test_cp_push_exchange_one_rank_matches_the_workspace_path():
     finally:
         if own_group:
             dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("C", [2, 4])
+def test_cp_verify_rows_with_local_visible_ends_merge_across_ranks(C):
+    """MTP verify under context parallelism: 7 query rows of one sequence at
+    its last 7 positions; on each rank row p sees the rank's first
+    ``local_keys(p + 1)`` local keys (the kernel's per-row ``q_ends``), and
+    the ranks' split partials merge into causal attention over every key."""
+    from k8v4_xpu_b200.parallel.cp import local_keys
+    n, w = 3001, 7
+    lay, caches, table, kd, vd = _sharded(n, C, seed=11)
+    g = torch.Generator().manual_seed(12)
+    q = torch.randn(w, lay.hkv * lay.gqa, 128, generator=g).bfloat16().cuda()
+    cu = torch.tensor([0, w], dtype=torch.int32, device="cuda")
+    npg = (n + 15) // 16
+    nsplit = 3
+    pos = list(range(n - w, n))
+    rank_floats = ops.decode_ws_floats(1, lay.hkv, nsplit, w, lay.gqa)
+    ws_all = torch.empty(C * rank_floats, dtype=torch.float32, device="cuda")
+    for r in range(C):
+        local = [i // C for i in range(npg) if i % C == r]
+        ends = torch.tensor([local_keys(p + 1, r, C) for p in pos], dtype=torch.int32, device="cuda")
+        out = torch.empty_like(q)
+        ops.decode_attn(q, cu, torch.tensor([local_keys(n, r, C)], dtype=torch.int32, device="cuda"),
+                        torch.tensor(local, dtype=torch.int32, device="cuda").view(1, -1), caches[r], lay.hkv,
+                        lay.gqa, w, nsplit=nsplit, out=out, ws=ws_all[r * rank_floats:(r + 1) * rank_floats],
+                        q_ends=ends)
+    merged = torch.empty_like(q)
+    ops.decode_combine_ranks(ws_all, rank_floats, cu, C, nsplit, lay.hkv, lay.gqa, w, merged)
+    torch.cuda.synchronize()
+    ref = O.attention_ref(q.float().cpu(), kd, vd, [p + 1 for p in pos], lay.gqa)
+    err = (merged.float().cpu() - ref).abs().max().item()
+    assert err < 2e-2, err
+    assert ops.status() == 0
