@@ -5,8 +5,11 @@ Endpoints: ``POST /v1/chat/completions`` and ``POST /v1/completions``
 ``continuous_usage_stats``), ``GET /v1/models``, ``GET /health`` and
 ``GET /metrics`` (Prometheus, ``vllm:*`` names). This is the surface the
 reference's clients use against stock vLLM (``bench/serve_coding.py:27-45``,
-``launch.sh:219-232``). Decoding is greedy (the benchmark path of the
-reference); ``temperature`` is accepted and ignored, ``n`` must be 1.
+``launch.sh:219-232``). A request without ``temperature`` (or with 0)
+decodes greedily, the benchmark path of the reference; ``temperature`` > 0
+samples, with ``top_p``, ``top_k`` (0 or -1: off) and ``seed``
+(``runtime.sampling``; not combined with MTP speculative decoding). ``n``
+must be 1.
 """
 from __future__ import annotations
 
@@ -40,6 +43,7 @@ class _Common(BaseModel):
     stop_token_ids: list[int] = Field(default_factory=list)
     temperature: float | None = None
     top_p: float | None = None
+    top_k: int | None = None
     seed: int | None = None
     n: int = 1
 
@@ -78,8 +82,16 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
             raise HTTPException(400, "prompt (%d) + max_tokens (%d) exceeds max_model_len %d"
                                 % (prompt_len, mt, max_model_len))
         stops = tuple(req.stop_token_ids) + ((eos,) if eos is not None else ())
+        temperature = float(req.temperature or 0.0)
+        top_p = 1.0 if req.top_p is None else float(req.top_p)
+        top_k = 0 if req.top_k is None or req.top_k == -1 else int(req.top_k)
+        if temperature < 0 or not 0.0 < top_p <= 1.0 or top_k < 0:
+            raise HTTPException(400, "temperature must be >= 0, top_p in (0, 1], top_k >= 0 or -1")
+        if temperature > 0 and getattr(getattr(driver, "engine", None), "mtp", None) is not None:
+            raise HTTPException(400, "sampling (temperature > 0) is not supported with MTP speculative "
+                                     "decoding; send temperature 0")
         return SamplingParams(max_tokens=mt, ignore_eos=req.ignore_eos, stop_token_ids=stops,
-                              temperature=float(req.temperature or 0.0))
+                              temperature=temperature, top_p=top_p, top_k=top_k, seed=req.seed)
 
     async def run(prompt: list[int], params: SamplingParams):
         loop = asyncio.get_running_loop()

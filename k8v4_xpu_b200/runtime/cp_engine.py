@@ -34,6 +34,7 @@ from ..parallel.cp import PAGE, CPGroup
 from ..parallel.cp_combine import PeerCombine, cp_combine_mode, max_slot_floats
 from .block_manager import CapacityError
 from .engine import LLMEngine, decode_splits
+from .sampling import samples
 
 
 class CPEngine(LLMEngine):
@@ -165,12 +166,13 @@ class CPEngine(LLMEngine):
         else:
             hidden = self.model.forward(inp, self.kv_caches, self.ws)
         if sched.is_decode_only:
-            tokens = self._sample(hidden) if n_logit else np.zeros(0, np.int64)
+            seqs = [c.seq for c in sched.chunks if c.needs_logits]
+            tokens = self._sample(hidden, seqs) if n_logit else np.zeros(0, np.int64)
         else:
             # the owner of each prompt's last token samples it; the others add zeros
             vec = torch.zeros(len(sched.chunks), dtype=torch.int64, device=self.device)
             if owned:
-                ids = self.model.greedy(hidden)
+                ids = self._choose(hidden, [sched.chunks[ci].seq for ci, _ in owned])
                 vec[torch.tensor([ci for ci, _ in owned], device=self.device)] = ids
             self.cp.sum_(vec)
             all_tok = vec.cpu().numpy()
@@ -226,7 +228,8 @@ class CPDecodeGraphs:
         # step keeps that alternation across replays only with an even count
         if self.eng.cp.peer is not None and len(self.eng.model.layers) % 2:
             return False
-        return len(sched.chunks) <= len(self.sizes) and all(c.num_tokens == 1 for c in sched.chunks)
+        return (len(sched.chunks) <= len(self.sizes) and all(c.num_tokens == 1 for c in sched.chunks)
+                and not any(samples(c.seq.params) for c in sched.chunks))
 
     def _inputs(self, B: int, nsplit: int) -> StepInputs:
         return StepInputs(

@@ -31,6 +31,7 @@ from .. import ops
 from ..kv import skip_layers
 from ..models.config import ModelConfig
 from ..models.dense import DenseModel, StepInputs
+from . import sampling
 from .block_manager import BlockManager, CapacityError
 from .scheduler import SamplingParams, Scheduler, Sequence
 from .workspace import Workspace
@@ -220,6 +221,12 @@ class LLMEngine:
 
     # ------------------------------------------------------------- requests
     def add_request(self, prompt: list[int], params: SamplingParams | None = None) -> Sequence:
+        if params is not None:
+            if params.temperature < 0 or not 0.0 < params.top_p <= 1.0 or params.top_k < 0:
+                raise ValueError("temperature must be >= 0, top_p in (0, 1], top_k >= 0")
+            if sampling.samples(params) and self.mtp is not None:
+                raise ValueError("sampling (temperature > 0) is not supported with MTP speculative decoding; "
+                                 "send temperature 0")
         return self.scheduler.add(prompt, params)
 
     def has_unfinished(self) -> bool:
@@ -332,16 +339,30 @@ class LLMEngine:
             inp, rows = self._build_inputs(sched)
             hidden = self.model.forward(inp, self.kv_caches, self.ws)
             # a step made only of non-final prefill chunks samples nothing
-            tokens = self._sample(hidden) if rows else np.zeros(0, np.int64)
+            seqs = [c.seq for c in sched.chunks if c.needs_logits]
+            tokens = self._sample(hidden, seqs) if rows else np.zeros(0, np.int64)
         return self._commit(sched, tokens)
+
+    def _choose(self, hidden: torch.Tensor, seqs: list[Sequence] | None = None) -> torch.Tensor:
+        """Next-token ids [rows] on the device: the argmax, or, when a row's
+        request samples, a draw from its full-vocabulary logits (the TP
+        shards gathered on every rank; ``runtime.sampling``)."""
+        if not seqs or not any(sampling.samples(s.params) for s in seqs):
+            return self.model.greedy(hidden)
+        lg = self.model.logits(hidden)
+        if self.tp > 1:
+            lg = self.model.comm.all_gather(lg, dim=1)
+        gens = [sampling.generator_for(s, self.cfg.seed, self.device) if sampling.samples(s.params) else None
+                for s in seqs]
+        return sampling.sample_rows(lg, [s.params for s in seqs], gens)
 
     def _agree(self, ids: torch.Tensor) -> torch.Tensor:
         """Hook for engines whose ranks sample replicated rows (context
         parallelism): makes every rank hold the same ids."""
         return ids
 
-    def _sample(self, hidden: torch.Tensor) -> np.ndarray:
-        ids = self._agree(self.model.greedy(hidden))
+    def _sample(self, hidden: torch.Tensor, seqs: list[Sequence] | None = None) -> np.ndarray:
+        ids = self._agree(self._choose(hidden, seqs))
         n = ids.numel()
         out = self._pin_out[:n]
         out.copy_(ids, non_blocking=True)

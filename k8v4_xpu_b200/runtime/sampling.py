@@ -1,0 +1,73 @@
+"""Random sampling of next tokens (temperature, top-k, top-p, seed).
+
+The reference serves through stock vLLM, whose requests may sample instead
+of taking the argmax. Greedy rows stay on the argmax kernel inside the
+captured decode graphs; a step with at least one sampling row runs eagerly
+and draws those rows here from the full-vocabulary logits (under tensor
+parallelism every rank gathers the vocabulary shards, then draws with the
+same per-sequence generator, so the ranks agree).
+
+Each sequence owns a ``torch.Generator`` on the device, seeded with the
+request's ``seed``; without one the seed is derived from the engine seed
+and the sequence id, which every rank of a TP or CP group shares.
+"""
+from __future__ import annotations
+
+import torch
+
+_MIX = 0x9E3779B97F4A7C15  # odd 64-bit constant (golden ratio) to spread seq ids
+
+
+def samples(params) -> bool:
+    """Whether a request samples (temperature above zero) instead of taking the argmax."""
+    return params is not None and (params.temperature or 0.0) > 0.0
+
+
+def seed_for(params, engine_seed: int, seq_id: int) -> int:
+    if params.seed is not None:
+        return int(params.seed) & ((1 << 63) - 1)
+    return ((int(engine_seed) + 1) * _MIX + int(seq_id) * 0x2545F4914F6CDD1D) & ((1 << 63) - 1)
+
+
+def generator_for(seq, engine_seed: int, device) -> torch.Generator:
+    """The sequence's generator, created and seeded on first use."""
+    g = getattr(seq, "generator", None)
+    if g is None:
+        g = torch.Generator(device=device)
+        g.manual_seed(seed_for(seq.params, engine_seed, seq.seq_id))
+        seq.generator = g
+    return g
+
+
+def filter_logits(x: torch.Tensor, top_k: int, top_p: float) -> torch.Tensor:
+    """One row of fp32 logits (already divided by the temperature) with the
+    tokens outside the top-k and outside the top-p nucleus set to -inf. The
+    most likely token always stays."""
+    V = x.shape[-1]
+    if 0 < top_k < V:
+        kth = torch.topk(x, top_k).values[-1]
+        x = torch.where(x < kth, torch.full_like(x, float("-inf")), x)
+    if 0.0 < top_p < 1.0:
+        vals, idx = torch.sort(x, descending=True)
+        p = torch.softmax(vals, -1)
+        before = torch.cumsum(p, -1) - p          # mass of the tokens ranked above each one
+        drop = before >= top_p
+        drop[0] = False
+        x = x.clone()
+        x[idx[drop]] = float("-inf")
+    return x
+
+
+def sample_rows(logits: torch.Tensor, params: list, gens: list) -> torch.Tensor:
+    """Token ids [R] (int64) for logits [R, V]: rows whose params sample are
+    drawn from softmax(filtered logits / temperature) with their generator;
+    the others take the argmax."""
+    lg = logits.float()
+    out = torch.argmax(lg, dim=-1)
+    for i, (p, g) in enumerate(zip(params, gens)):
+        if not samples(p):
+            continue
+        x = filter_logits(lg[i] / float(p.temperature), int(p.top_k or 0), float(p.top_p if p.top_p else 1.0))
+        probs = torch.softmax(x, -1)
+        out[i] = torch.multinomial(probs, 1, generator=g)[0]
+    return out

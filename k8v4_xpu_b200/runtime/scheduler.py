@@ -30,7 +30,10 @@ class SamplingParams:
     max_tokens: int = 16
     ignore_eos: bool = False
     stop_token_ids: tuple[int, ...] = ()
-    temperature: float = 0.0  # greedy decoding (the benchmark path)
+    temperature: float = 0.0  # 0: greedy decoding (the benchmark path); > 0: sampling
+    top_p: float = 1.0        # nucleus sampling (1: off)
+    top_k: int = 0            # top-k sampling (0: off)
+    seed: int | None = None   # per-request generator seed (None: derived from the engine seed)
 
 
 @dataclasses.dataclass
@@ -51,6 +54,7 @@ class Sequence:
     # tokens to prefill: the prompt, or after a recompute preemption every
     # token the sequence held (prompt + output so far)
     prefill_len: int | None = None
+    generator: object = None   # torch.Generator of a sampling request (runtime.sampling)
 
     @property
     def tokens(self) -> "TokenView":

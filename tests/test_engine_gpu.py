@@ -101,3 +101,30 @@ def test_prefix_cache_hit_same_tokens():
     assert seq.cached_tokens >= 192
     b = eng.generate([prompt], SamplingParams(max_tokens=5, ignore_eos=True))[0]
     assert a == b
+
+
+def test_engine_samples_seeded_rows_beside_greedy_rows():
+    """A sampling request (temperature 5, seed) next to a greedy one: the
+    sampling steps run eagerly, the seeded draws repeat in a fresh engine,
+    they leave the greedy chain, and the greedy request still follows its
+    argmax."""
+    from test_mtp_gpu import _teacher_forced_margin
+    pg, ps = list(range(1, 120)), list(range(7, 90))
+
+    def run():
+        cfg = EngineConfig(model="tiny", max_model_len=2048, max_num_seqs=2, max_num_batched_tokens=96,
+                           num_kv_blocks=256, device="cuda")
+        eng = LLMEngine(cfg, TINY)
+        g = eng.add_request(pg, SamplingParams(max_tokens=8, ignore_eos=True))
+        s = eng.add_request(ps, SamplingParams(max_tokens=8, ignore_eos=True, temperature=5.0, seed=1234))
+        while eng.has_unfinished():
+            eng.step()
+        assert ops.status() == 0
+        return g.output, s.output
+
+    g1, s1 = run()
+    g2, s2 = run()
+    assert s1 == s2 and len(s1) == 8 and all(0 <= t < TINY.vocab for t in s1)
+    m = DenseModel(TINY, device="cuda").random_init(seed=0)
+    assert _teacher_forced_margin(m, pg, g1) < 0.05
+    assert _teacher_forced_margin(m, ps, s1) > 0.0  # not the argmax chain

@@ -1,0 +1,181 @@
+"""Random sampling (temperature, top-k, top-p, seed) on the host side (CPU)."""
+import os
+import socket
+import traceback
+import types
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from k8v4_xpu_b200.runtime import sampling
+from k8v4_xpu_b200.runtime.scheduler import SamplingParams, Sequence
+
+
+def test_filters_keep_the_top_k_and_the_nucleus():
+    x = torch.tensor([3.0, 1.0, 2.0, 0.0, -1.0])
+    k2 = sampling.filter_logits(x, 2, 1.0)
+    assert torch.isinf(k2[[1, 3, 4]]).all() and torch.equal(k2[[0, 2]], x[[0, 2]])
+    p = torch.softmax(x, 0)                        # 0.636, 0.086, 0.234, 0.032, 0.012
+    n1 = sampling.filter_logits(x, 0, 0.5)         # the first token alone holds 0.636 >= 0.5
+    assert torch.isfinite(n1).tolist() == [True, False, False, False, False]
+    n2 = sampling.filter_logits(x, 0, 0.8)         # 0.636 < 0.8: the second-ranked token joins
+    assert torch.isfinite(n2).tolist() == [True, False, True, False, False]
+    assert float(p[0] + p[2]) >= 0.8
+    tiny = sampling.filter_logits(x, 0, 1e-6)      # the most likely token always stays
+    assert torch.isfinite(tiny).tolist() == [True, False, False, False, False]
+    assert torch.equal(sampling.filter_logits(x, 0, 1.0), x)
+
+
+def test_greedy_rows_take_the_argmax_and_sampled_rows_follow_the_softmax():
+    g = torch.Generator().manual_seed(0)
+    logits = torch.randn(3, 50, generator=g)
+    greedy = SamplingParams()
+    assert sampling.sample_rows(logits, [greedy] * 3, [None] * 3).tolist() == logits.argmax(1).tolist()
+    top1 = SamplingParams(temperature=0.7, top_k=1)
+    gen = torch.Generator().manual_seed(1)
+    assert sampling.sample_rows(logits, [top1] * 3, [gen] * 3).tolist() == logits.argmax(1).tolist()
+    # frequencies of 20,000 draws at temperature 0.5 against softmax(logits / 0.5)
+    row = torch.tensor([[1.0, 0.5, 0.0, -0.5, -3.0]])
+    p = SamplingParams(temperature=0.5)
+    gen = torch.Generator().manual_seed(2)
+    counts = torch.zeros(5)
+    for _ in range(20000):
+        counts[sampling.sample_rows(row, [p], [gen])[0]] += 1
+    want = torch.softmax(row[0] / 0.5, 0)
+    assert (counts / 20000 - want).abs().max() < 0.015
+
+
+def test_seeds_are_reproducible_and_differ_between_sequences():
+    p = SamplingParams(temperature=1.0)
+    assert sampling.seed_for(p, 0, 5) == sampling.seed_for(p, 0, 5)
+    assert sampling.seed_for(p, 0, 5) != sampling.seed_for(p, 0, 6)
+    assert sampling.seed_for(p, 0, 5) != sampling.seed_for(p, 1, 5)
+    assert sampling.seed_for(SamplingParams(temperature=1.0, seed=42), 0, 5) == 42
+    logits = torch.randn(1, 1000, generator=torch.Generator().manual_seed(3))
+    draws = []
+    for _ in range(2):
+        seq = Sequence(7, [1, 2], SamplingParams(temperature=1.0, seed=123))
+        gen = sampling.generator_for(seq, 0, "cpu")
+        assert sampling.generator_for(seq, 0, "cpu") is gen  # created once per sequence
+        draws.append([int(sampling.sample_rows(logits, [seq.params], [gen])[0]) for _ in range(20)])
+    assert draws[0] == draws[1] and len(set(draws[0])) > 1
+
+
+class _LogitModel:
+    """A stand-in whose logits are a fixed function of the hidden row; under
+    TP it returns this rank's vocabulary shard."""
+
+    def __init__(self, tp=1, rank=0, vocab=64, comm=None):
+        self.tp, self.rank, self.vocab, self.comm = tp, rank, vocab, comm
+        self.vocab_start = rank * vocab // tp
+
+    def _full(self, hidden):
+        w = torch.arange(self.vocab, dtype=torch.float32)
+        return torch.sin(hidden[:, :1] * 0.37 + w * 0.11) * 3.0
+
+    def logits(self, hidden):
+        v = self.vocab // self.tp
+        return self._full(hidden)[:, self.rank * v:(self.rank + 1) * v]
+
+    def greedy(self, hidden):
+        return self._full(hidden).argmax(1)
+
+
+def _engine(tp=1, rank=0, comm=None, mtp=None):
+    from k8v4_xpu_b200.runtime.engine import LLMEngine
+    eng = object.__new__(LLMEngine)  # the sampling logic without the GPU set-up
+    eng.cfg = types.SimpleNamespace(seed=0)
+    eng.tp = tp
+    eng.device = torch.device("cpu")
+    eng.model = _LogitModel(tp, rank, comm=comm)
+    eng.mtp = mtp
+    eng.scheduler = types.SimpleNamespace(add=lambda prompt, params: Sequence(0, prompt, params))
+    return eng
+
+
+def test_engine_chooses_argmax_or_seeded_draws_per_row():
+    eng = _engine()
+    hidden = torch.arange(4, dtype=torch.float32).view(4, 1).repeat(1, 8)
+    seqs = [Sequence(i, [1], SamplingParams(temperature=(0.0 if i % 2 == 0 else 1.3), seed=i)) for i in range(4)]
+    a = eng._choose(hidden, seqs)
+    greedy = eng.model.greedy(hidden)
+    assert a[0] == greedy[0] and a[2] == greedy[2]
+    seqs2 = [Sequence(i, [1], SamplingParams(temperature=(0.0 if i % 2 == 0 else 1.3), seed=i)) for i in range(4)]
+    assert torch.equal(eng._choose(hidden, seqs2), a)      # same seeds, same draws
+    assert torch.equal(eng._choose(hidden, None), greedy)  # no sampling request: the argmax kernel path
+
+
+def test_engine_refuses_bad_params_and_sampling_under_mtp():
+    eng = _engine()
+    for p in (SamplingParams(temperature=-1.0), SamplingParams(top_p=0.0), SamplingParams(top_k=-2)):
+        with pytest.raises(ValueError):
+            eng.add_request([1, 2], p)
+    eng.add_request([1, 2], SamplingParams(temperature=0.8, top_p=0.9, top_k=40))
+    eng.mtp = object()
+    with pytest.raises(ValueError, match="MTP"):
+        eng.add_request([1, 2], SamplingParams(temperature=0.8))
+    eng.add_request([1, 2], SamplingParams())  # greedy requests still serve
+
+
+def test_decode_graphs_leave_sampling_steps_to_the_eager_path():
+    from k8v4_xpu_b200.runtime.graphs import DecodeGraphs
+    dg = object.__new__(DecodeGraphs)
+    dg.width, dg.sizes = 1, [1, 2, 4]
+
+    def sched(*temps):
+        return types.SimpleNamespace(chunks=[types.SimpleNamespace(num_tokens=1, seq=Sequence(
+            i, [1], SamplingParams(temperature=t))) for i, t in enumerate(temps)])
+    assert dg.can_run(sched(0.0, 0.0))
+    assert not dg.can_run(sched(0.0, 0.9))
+
+
+def _free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _tp_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
+    import torch.distributed as dist
+    try:
+        from k8v4_xpu_b200.parallel.comm import TPComm, init_from_env
+        init_from_env(timeout_s=60, backend="gloo")
+        eng = _engine(tp=world, rank=rank, comm=TPComm())
+        hidden = torch.arange(6, dtype=torch.float32).view(6, 1).repeat(1, 8)
+        seqs = [Sequence(i, [1], SamplingParams(temperature=1.0 if i % 3 else 0.0, top_k=20 if i == 4 else 0))
+                for i in range(6)]
+        draws = [eng._choose(hidden, seqs).tolist() for _ in range(5)]
+        q.put((rank, {"draws": draws, "greedy": eng.model.greedy(hidden).tolist()}))
+        dist.barrier()
+    except Exception:
+        q.put((rank, {"error": traceback.format_exc()}))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def test_tp_ranks_draw_the_same_tokens_from_gathered_shards():
+    """Two gloo ranks, each holding half of the vocabulary: the shards are
+    gathered and every rank's generator, seeded alike, draws the same ids."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_tp_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(2):
+        assert "error" not in out[r], out[r].get("error")
+    assert out[0]["draws"] == out[1]["draws"]
+    d = out[0]["draws"]
+    for step in d:
+        assert [step[i] for i in (0, 3)] == [out[0]["greedy"][i] for i in (0, 3)]  # greedy rows
+    assert len({tuple(s) for s in d}) > 1  # the sampled rows vary from step to step
+    assert all(0 <= t < 64 for s in d for t in s)

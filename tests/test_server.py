@@ -221,3 +221,28 @@ def test_iteration_token_history_is_drained_by_the_exporter(client):
     count = [ln for ln in body.splitlines() if ln.startswith("vllm:iteration_tokens_total_count")]
     assert count and float(count[0].split()[-1]) >= 3
     assert len(eng.stats["iteration_tokens"]) <= 1  # drained after each step (one may be in flight)
+
+
+def test_sampling_fields_reach_the_engine_and_bad_ones_are_refused(client):
+    c, eng, driver = client
+    seen = []
+    orig = eng.add_request
+
+    def spy(prompt, params=None):
+        seen.append(params)
+        return orig(prompt, params)
+    eng.add_request = spy
+    r = c.post("/v1/completions", json={"prompt": [1, 2, 3], "max_tokens": 2, "ignore_eos": True,
+                                        "temperature": 0.7, "top_p": 0.9, "top_k": -1, "seed": 11})
+    assert r.status_code == 200
+    p = seen[-1]
+    assert (p.temperature, p.top_p, p.top_k, p.seed) == (0.7, 0.9, 0, 11)
+    r = c.post("/v1/completions", json={"prompt": [1, 2, 3], "max_tokens": 2, "ignore_eos": True})
+    assert r.status_code == 200 and seen[-1].temperature == 0.0  # no temperature: greedy
+    for bad in ({"temperature": -0.5}, {"top_p": 0.0}, {"top_p": 1.5}, {"top_k": -3}):
+        body = {"prompt": [1, 2], "max_tokens": 2, **bad}
+        assert c.post("/v1/completions", json=body).status_code == 400, bad
+    eng.mtp = object()  # an engine serving MTP refuses sampling up front
+    body = {"prompt": [1, 2], "max_tokens": 2, "temperature": 0.5}
+    assert c.post("/v1/completions", json=body).status_code == 400
+    eng.mtp = None
