@@ -8,8 +8,9 @@ reference's clients use against stock vLLM (``bench/serve_coding.py:27-45``,
 ``launch.sh:219-232``). A request without ``temperature`` (or with 0)
 decodes greedily, the benchmark path of the reference; ``temperature`` > 0
 samples, with ``top_p``, ``top_k`` (0 or -1: off) and ``seed``
-(``runtime.sampling``; not combined with MTP speculative decoding). ``n``
-must be 1.
+(``runtime.sampling``; not combined with MTP speculative decoding). Stop
+strings (``stop``) end a request before the first match, in streamed and
+whole responses, and drop its sequence from the engine. ``n`` must be 1.
 """
 from __future__ import annotations
 
@@ -25,7 +26,7 @@ from prometheus_client import CONTENT_TYPE_LATEST
 from pydantic import BaseModel, Field
 
 from ..runtime.scheduler import SamplingParams
-from .tokenizer import IncrementalDecoder
+from .tokenizer import IncrementalDecoder, StopMatcher
 
 
 class StreamOptions(BaseModel):
@@ -41,6 +42,7 @@ class _Common(BaseModel):
     stream_options: StreamOptions | None = None
     ignore_eos: bool = False
     stop_token_ids: list[int] = Field(default_factory=list)
+    stop: str | list[str] | None = None
     temperature: float | None = None
     top_p: float | None = None
     top_k: int | None = None
@@ -130,9 +132,20 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
         if not req.stream:
             toks: list[int] = []
             reason = None
+            matcher = StopMatcher(req.stop)
+            detok = IncrementalDecoder(tokenizer)
+            parts: list[str] = []
             while True:
                 new, fin, why = await out.get()
                 toks.extend(new)
+                if matcher.stops and not (fin and why and (why == "error" or why.startswith("rejected: "))):
+                    shown, stopped = matcher.feed(detok.push(new, final=fin), final=fin)
+                    parts.append(shown)
+                    if stopped:  # a stop string ends the request: the engine drops the sequence
+                        if not fin:
+                            driver.abort(h)
+                        reason = "stop"
+                        break
                 if fin:
                     reason = why
                     break
@@ -140,7 +153,7 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
                 raise HTTPException(500, "engine failed")
             if reason and reason.startswith("rejected: "):
                 raise HTTPException(400, reason[len("rejected: "):])
-            text = tokenizer.decode(toks)
+            text = "".join(parts) if matcher.stops else tokenizer.decode(toks)
             choice = ({"index": 0, "message": {"role": "assistant", "content": text}, "finish_reason": reason}
                       if chat else {"index": 0, "text": text, "finish_reason": reason, "logprobs": None})
             choice["token_ids"] = toks
@@ -150,6 +163,7 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
         async def events():
             n_out = 0
             detok = IncrementalDecoder(tokenizer)
+            matcher = StopMatcher(req.stop)
             chunk_obj = "chat.completion.chunk" if chat else "text_completion"
             if chat:
                 first = {"id": rid, "object": chunk_obj, "created": created, "model": served_model_name,
@@ -169,8 +183,13 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
                                                                       "type": "invalid_request_error"}})
                         break
                     n_out += len(new)
+                    text, stopped = matcher.feed(detok.push(new, final=fin), final=fin)
+                    if stopped and not fin:  # a stop string ends the request here
+                        driver.abort(h)
+                        fin, why = True, "stop"
+                    elif stopped:
+                        why = "stop"
                     if new or fin:
-                        text = detok.push(new, final=fin)
                         ch = ({"index": 0, "delta": {"content": text}, "finish_reason": why if fin else None}
                               if chat else {"index": 0, "text": text, "finish_reason": why if fin else None,
                                             "logprobs": None})

@@ -101,3 +101,36 @@ def load_tokenizer(path: str | None, vocab_size: int):
     if path and os.path.isdir(path):
         return HFTokenizer(path)
     return ByteTokenizer(vocab_size)
+
+
+class StopMatcher:
+    """Stop strings over streamed text (the OpenAI ``stop`` field).
+
+    Text is fed as it is decoded; ``feed`` returns what may be shown now and
+    whether a stop string was met. Up to ``len(longest stop) - 1`` trailing
+    characters are held back, because they may be the start of a stop string
+    that the next tokens complete; text from the first stop string on is
+    never shown. Without stop strings the text passes through unchanged."""
+
+    def __init__(self, stops=None):
+        if isinstance(stops, str):
+            stops = [stops]
+        self.stops = [s for s in (stops or []) if s]
+        self.hold = max((len(s) for s in self.stops), default=1) - 1
+        self.buf = ""
+        self.done = False
+
+    def feed(self, text: str, final: bool = False) -> tuple[str, bool]:
+        if self.done:
+            return "", True
+        self.buf += text
+        hits = [i for i in (self.buf.find(s) for s in self.stops) if i >= 0]
+        if hits:
+            out, self.buf, self.done = self.buf[:min(hits)], "", True
+            return out, True
+        if final or self.hold == 0:
+            out, self.buf = self.buf, ""
+            return out, False
+        cut = max(0, len(self.buf) - self.hold)
+        out, self.buf = self.buf[:cut], self.buf[cut:]
+        return out, False

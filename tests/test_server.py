@@ -1,5 +1,6 @@
 """OpenAI-compatible server against a CPU engine stand-in (CPU)."""
 import json
+import time
 
 import pytest
 from fastapi.testclient import TestClient
@@ -246,3 +247,46 @@ def test_sampling_fields_reach_the_engine_and_bad_ones_are_refused(client):
     body = {"prompt": [1, 2], "max_tokens": 2, "temperature": 0.5}
     assert c.post("/v1/completions", json=body).status_code == 400
     eng.mtp = None
+
+
+def test_stop_matcher_holds_back_possible_starts():
+    from k8v4_xpu_b200.api.tokenizer import StopMatcher
+    m = StopMatcher(["cde", "zz"])
+    assert m.feed("ab") == ("", False)        # "ab" might start a stop string: held (2 characters)
+    assert m.feed("c") == ("a", False)
+    assert m.feed("d") == ("b", False)
+    assert m.feed("ef") == ("", True)         # "cde" completes: nothing from it on is shown
+    m = StopMatcher(["cde"])
+    shown = "".join(m.feed(ch)[0] for ch in "xyzab")
+    assert shown == "xyz"
+    assert m.feed("cdef") == ("ab", True) and m.feed("more") == ("", True)
+    m = StopMatcher(["\n\n"])
+    assert m.feed("line\n") == ("line", False) and m.feed("next", final=True) == ("\nnext", False)
+    p = StopMatcher(None)
+    assert p.feed("abc") == ("abc", False) and p.feed("", final=True) == ("", False)
+
+
+def test_stop_strings_end_requests_streamed_and_not(client):
+    """The stand-in engine continues a prompt byte by byte (next id = last + 1):
+    after "a" it writes "bcdefg...". A stop string ends the request before it
+    (finish reason "stop") and the engine drops the sequence."""
+    c, eng, _ = client
+    a = ord("a") + 3  # byte-tokenizer id of "a"
+    body = {"prompt": [a], "max_tokens": 20, "ignore_eos": True, "stop": ["ef", "zz"]}
+    r = c.post("/v1/completions", json=body).json()
+    ch = r["choices"][0]
+    assert ch["text"] == "bcd" and ch["finish_reason"] == "stop"
+    chunks = []
+    with c.stream("POST", "/v1/completions", json={**body, "stream": True}) as s:
+        for line in s.iter_lines():
+            if line.startswith("data: ") and line != "data: [DONE]":
+                chunks.append(json.loads(line[6:]))
+    text = "".join(x["choices"][0]["text"] for x in chunks if x["choices"])
+    assert text == "bcd" and chunks[-1]["choices"][0]["finish_reason"] == "stop"
+    r = c.post("/v1/completions", json={"prompt": [a], "max_tokens": 4, "ignore_eos": True, "stop": "zz"}).json()
+    assert r["choices"][0]["text"] == "bcde" and r["choices"][0]["finish_reason"] == "length"
+    deadline = time.monotonic() + 5
+    while eng.has_unfinished() and time.monotonic() < deadline:
+        time.sleep(0.01)
+    assert not eng.has_unfinished()  # the stopped requests were dropped, not left decoding
+    eng.blocks.check_invariants()
