@@ -8,7 +8,8 @@ reference's clients use against stock vLLM (``bench/serve_coding.py:27-45``,
 ``launch.sh:219-232``). A request without ``temperature`` (or with 0)
 decodes greedily, the benchmark path of the reference; ``temperature`` > 0
 samples, with ``top_p``, ``top_k`` (0 or -1: off) and ``seed``
-(``runtime.sampling``; not combined with MTP speculative decoding). Stop
+(``runtime.sampling``; under MTP the drafts are verified by speculative
+sampling). Stop
 strings (``stop``) end a request before the first match, in streamed and
 whole responses, and drop its sequence from the engine. ``n`` must be 1.
 """
@@ -89,9 +90,6 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
         top_k = 0 if req.top_k is None or req.top_k == -1 else int(req.top_k)
         if temperature < 0 or not 0.0 < top_p <= 1.0 or top_k < 0:
             raise HTTPException(400, "temperature must be >= 0, top_p in (0, 1], top_k >= 0 or -1")
-        if temperature > 0 and getattr(getattr(driver, "engine", None), "mtp", None) is not None:
-            raise HTTPException(400, "sampling (temperature > 0) is not supported with MTP speculative "
-                                     "decoding; send temperature 0")
         return SamplingParams(max_tokens=mt, ignore_eos=req.ignore_eos, stop_token_ids=stops,
                               temperature=temperature, top_p=top_p, top_k=top_k, seed=req.seed)
 

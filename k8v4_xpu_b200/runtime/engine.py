@@ -224,9 +224,6 @@ class LLMEngine:
         if params is not None:
             if params.temperature < 0 or not 0.0 < params.top_p <= 1.0 or params.top_k < 0:
                 raise ValueError("temperature must be >= 0, top_p in (0, 1], top_k >= 0")
-            if sampling.samples(params) and self.mtp is not None:
-                raise ValueError("sampling (temperature > 0) is not supported with MTP speculative decoding; "
-                                 "send temperature 0")
         return self.scheduler.add(prompt, params)
 
     def has_unfinished(self) -> bool:
@@ -333,7 +330,8 @@ class LLMEngine:
             # speculative serving: the MTP layer catches up on every prefill row
             inp, rows = self._build_inputs(sched)
             hid_all = self.model.forward(inp, self.kv_caches, self.ws, all_rows=True)
-            tokens = self._sample(hid_all.index_select(0, inp.logit_rows)) if rows else np.zeros(0, np.int64)
+            seqs = [c.seq for c in sched.chunks if c.needs_logits]
+            tokens = self._sample(hid_all.index_select(0, inp.logit_rows), seqs) if rows else np.zeros(0, np.int64)
             self.mtp.after_prefill(sched, inp, hid_all, tokens)
         else:
             inp, rows = self._build_inputs(sched)

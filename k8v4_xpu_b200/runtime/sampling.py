@@ -71,3 +71,42 @@ def sample_rows(logits: torch.Tensor, params: list, gens: list) -> torch.Tensor:
         probs = torch.softmax(x, -1)
         out[i] = torch.multinomial(probs, 1, generator=g)[0]
     return out
+
+
+def probs_rows(logits: torch.Tensor, p) -> torch.Tensor:
+    """Sampling distribution [R, V] (fp32) of the rows of ``logits`` under one
+    request's temperature, top-k and top-p."""
+    lg = logits.float() / float(p.temperature)
+    rows = [torch.softmax(filter_logits(lg[j], int(p.top_k or 0), float(p.top_p if p.top_p else 1.0)), -1)
+            for j in range(lg.shape[0])]
+    return torch.stack(rows)
+
+
+def speculative_sample(logits: torch.Tensor, drafts: torch.Tensor, p, gen: torch.Generator) -> tuple[int, int]:
+    """Speculative sampling of one sequence's verify rows.
+
+    ``logits`` [k + 1, V]: row j scores the token after verify row j (row 0
+    is the last committed token, rows 1..k the drafts); ``drafts`` [k]. The
+    drafter proposes deterministically (its argmax: all its mass on one
+    token), so draft j is kept with probability p_j(draft j) under the
+    target's sampling distribution p_j, and the first rejected position draws
+    from p_j with the rejected token removed (renormalized); after k kept
+    drafts the bonus token draws from p_k. The emitted tokens then have the
+    target's sampling distribution at every position (the standard
+    speculative sampling argument with a one-point draft distribution).
+    Returns (accepted drafts a, the token drawn at position a)."""
+    k = drafts.shape[0]
+    probs = probs_rows(logits, p)
+    u = torch.rand(k, generator=gen, device=gen.device) if k else None
+    a = 0
+    while a < k and float(u[a]) < float(probs[a, drafts[a]]):
+        a += 1
+    if a < k:
+        res = probs[a].clone()
+        res[drafts[a]] = 0.0
+        if float(res.sum()) <= 0.0:  # the target puts all its mass on the rejected token (u hit the edge)
+            res = probs[a]
+        x = torch.multinomial(res / res.sum(), 1, generator=gen)[0]
+    else:
+        x = torch.multinomial(probs[k], 1, generator=gen)[0]
+    return a, int(x)

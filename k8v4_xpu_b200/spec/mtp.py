@@ -35,6 +35,7 @@ import torch
 
 from ..models.dense import StepInputs
 from ..runtime.block_manager import CapacityError
+from ..runtime.sampling import generator_for, samples, speculative_sample
 from ..runtime.graphs import decode_inputs, prepare_benign, stage_decode_inputs
 
 
@@ -176,8 +177,39 @@ class MTPSpeculator:
             drafts.append(d)
         return torch.stack(drafts, 1)
 
-    def _body(self, B: int, nsplit: int) -> torch.Tensor:
-        """The whole speculative decode step on the graph buffers.
+    def _accept(self, hid: torch.Tensor, ids: torch.Tensor, B: int, seqs=None, forced=None):
+        """Targets ``t`` [B, w] and accepted drafts ``a`` [B] of the verify rows.
+
+        Greedy sequences keep the longest draft prefix that equals the
+        target's argmax (``t`` holds the argmax). Sampling sequences (an eager
+        step) run speculative sampling against the target's sampling
+        distribution (``runtime.sampling.speculative_sample``), and ``t[i, a]``
+        holds the token drawn there, so the commit emits ``d[:a] + t[a]`` for
+        both kinds. ``forced`` [B]: the benchmark's accepted counts."""
+        m = self.eng.model
+        w = self.w
+        d = ids[:, 1:]
+        if forced is not None or not seqs or not any(samples(s.params) for s in seqs):
+            t = m.greedy(hid).view(B, w)
+            a = forced if forced is not None else (d == t[:, :-1]).to(torch.int64).cumprod(1).sum(1)
+            return t, a
+        lg = m.logits(hid)
+        if self.eng.tp > 1:
+            lg = m.comm.all_gather(lg, dim=1)
+        lg = lg.view(B, w, -1)
+        t = torch.argmax(lg.float(), dim=-1)
+        a = (d == t[:, :-1]).to(torch.int64).cumprod(1).sum(1)
+        for i, s in enumerate(seqs):
+            if samples(s.params):
+                g = generator_for(s, self.eng.cfg.seed, self.eng.device)
+                ai, x = speculative_sample(lg[i], d[i], s.params, g)
+                a[i] = ai
+                t[i, ai] = x
+        return t, a
+
+    def _body(self, B: int, nsplit: int, seqs=None) -> torch.Tensor:
+        """The whole speculative decode step on the graph buffers (``seqs``:
+        the real sequences of an eager step, for the ones that sample).
 
         Returns int64 ``[B*w (targets) | B (accepted) | B*k (next drafts)]``."""
         eng, m, ws = self.eng, self.eng.model, self.eng.ws
@@ -185,13 +217,9 @@ class MTPSpeculator:
         T = B * w
         inp = decode_inputs(ws, B, w, nsplit)
         hid = m.forward(inp, eng.kv_caches, ws, all_rows=True)     # [T, H]
-        t = m.greedy(hid).view(B, w)
         ids = inp.input_ids.view(B, w)
         d = ids[:, 1:]
-        if self.forced:
-            a = ws.forced_a[:B]
-        else:
-            a = (d == t[:, :-1]).to(torch.int64).cumprod(1).sum(1)
+        t, a = self._accept(hid, ids, B, seqs, ws.forced_a[:B] if self.forced else None)
         j = torch.arange(w, device=eng.device).view(1, w)
         nxt = torch.cat([d, t[:, -1:]], 1)
         catch_ids = torch.where(j < a.view(B, 1), nxt, t).reshape(T)
@@ -248,11 +276,11 @@ class MTPSpeculator:
         forced = self.forced_counts(B_real) if self.forced else None
         stage_decode_inputs(eng, sched, B, self.w, forced)
         self._topk = []
-        if self.use_graphs:
+        if self.use_graphs and not any(samples(c.seq.params) for c in chunks):
             g, out = self.graphs[B]
             g.replay()
-        else:
-            out = self._body(B, decode_splits(eng.max_pages, B, eng.layout.hkv))
+        else:  # eager: no graphs, or a request that samples
+            out = self._body(B, decode_splits(eng.max_pages, B, eng.layout.hkv), [c.seq for c in chunks])
         n = out.numel()
         host = eng._pin_out[:n]
         host.copy_(out, non_blocking=True)

@@ -125,7 +125,7 @@ class CPMTPSpeculator(MTPSpeculator):
         forced = None
         if self.forced:
             forced = torch.from_numpy(self.forced_counts(B)).to(eng.device)
-        out = self._verify(inp, blk, nblk, B, forced)
+        out = self._verify(inp, blk, nblk, B, forced, [c.seq for c in chunks])
         eng.cp.broadcast_(out)
         res = out.cpu().numpy()
         eng.d2h_bytes += res.size * 8
@@ -133,15 +133,15 @@ class CPMTPSpeculator(MTPSpeculator):
         return self.commit(sched, res[:B * w].reshape(B, w), res[B * w:B * w + B], res[B * w + B:].reshape(B, k))
 
     # ----------------------------------------------------------- device body
-    def _verify(self, inp: StepInputs, blk, nblk, B: int, forced) -> torch.Tensor:
+    def _verify(self, inp: StepInputs, blk, nblk, B: int, forced, seqs=None) -> torch.Tensor:
         """Returns int64 ``[B*w (targets) | B (accepted) | B*k (next drafts)]``."""
         eng, m, ws = self.eng, self.eng.model, self.eng.ws
         w = self.w
         T = B * w
         hid = m.forward(inp, eng.kv_caches, ws, all_rows=True)
-        t = m.greedy(hid).view(B, w)
-        d = inp.input_ids.view(B, w)[:, 1:]
-        a = forced if forced is not None else (d == t[:, :-1]).to(torch.int64).cumprod(1).sum(1)
+        ids = inp.input_ids.view(B, w)
+        d = ids[:, 1:]
+        t, a = self._accept(hid, ids, B, seqs, forced)
         j = torch.arange(w, device=eng.device).view(1, w)
         nxt = torch.cat([d, t[:, -1:]], 1)
         catch_ids = torch.where(j < a.view(B, 1), nxt, t).reshape(T)

@@ -79,3 +79,28 @@ def test_mtp_forced_acceptance_mean_length():
     assert st.num_drafts >= 200
     assert abs(st.mean_accepted_length - 3.0) < 0.35, st.mean_accepted_length
     eng.blocks.check_invariants()
+
+
+def test_mtp_serves_sampling_requests_by_speculative_sampling():
+    """A sampling request (temperature 5, seed) beside a greedy one under
+    MTP6: those steps run eagerly with speculative sampling; the seeded
+    output repeats in a fresh engine and leaves the argmax chain, and the
+    greedy request still follows its argmax."""
+    pg, ps = PROMPTS[2], PROMPTS[1]
+
+    def run():
+        eng = _engine(speculative_tokens=6)
+        g = eng.add_request(pg, SamplingParams(max_tokens=16, ignore_eos=True))
+        s = eng.add_request(ps, SamplingParams(max_tokens=16, ignore_eos=True, temperature=5.0, seed=99))
+        while eng.has_unfinished():
+            eng.step()
+        assert ops.status() == 0
+        eng.blocks.check_invariants()
+        return eng, g.output, s.output
+
+    eng, g1, s1 = run()
+    _, g2, s2 = run()
+    assert s1 == s2 and len(s1) == 16 and all(0 <= t < TINY.vocab for t in s1)
+    assert eng.mtp.stats.num_drafts > 0
+    assert _teacher_forced_margin(eng.model, pg, g1) < 0.05
+    assert _teacher_forced_margin(eng.model, ps, s1) > 0.0

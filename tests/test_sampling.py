@@ -106,16 +106,14 @@ def test_engine_chooses_argmax_or_seeded_draws_per_row():
     assert torch.equal(eng._choose(hidden, None), greedy)  # no sampling request: the argmax kernel path
 
 
-def test_engine_refuses_bad_params_and_sampling_under_mtp():
+def test_engine_refuses_bad_params():
     eng = _engine()
     for p in (SamplingParams(temperature=-1.0), SamplingParams(top_p=0.0), SamplingParams(top_k=-2)):
         with pytest.raises(ValueError):
             eng.add_request([1, 2], p)
     eng.add_request([1, 2], SamplingParams(temperature=0.8, top_p=0.9, top_k=40))
-    eng.mtp = object()
-    with pytest.raises(ValueError, match="MTP"):
-        eng.add_request([1, 2], SamplingParams(temperature=0.8))
-    eng.add_request([1, 2], SamplingParams())  # greedy requests still serve
+    eng.mtp = object()  # sampling requests are served under MTP too (speculative sampling)
+    eng.add_request([1, 2], SamplingParams(temperature=0.8))
 
 
 def test_decode_graphs_leave_sampling_steps_to_the_eager_path():
@@ -179,3 +177,58 @@ def test_tp_ranks_draw_the_same_tokens_from_gathered_shards():
         assert [step[i] for i in (0, 3)] == [out[0]["greedy"][i] for i in (0, 3)]  # greedy rows
     assert len({tuple(s) for s in d}) > 1  # the sampled rows vary from step to step
     assert all(0 <= t < 64 for s in d for t in s)
+
+
+def test_speculative_sampling_keeps_the_target_distribution():
+    """With a deterministic drafter, the emitted tokens follow the target's
+    sampling distribution: the first token has p_0, and the second, given
+    that the first was the draft, has p_1 (Monte Carlo, 40,000 steps)."""
+    V, k = 6, 3
+    lg = torch.randn(k + 1, V, generator=torch.Generator().manual_seed(0))
+    p = SamplingParams(temperature=0.8)
+    probs = sampling.probs_rows(lg, p)
+    d = torch.tensor([2, 4, 1])
+    g = torch.Generator().manual_seed(1)
+    N = 40000
+    first, second, n2, accepted = torch.zeros(V), torch.zeros(V), 0, 0
+    for _ in range(N):
+        a, x = sampling.speculative_sample(lg, d, p, g)
+        emitted = d[:a].tolist() + [x]
+        accepted += a
+        first[emitted[0]] += 1
+        if len(emitted) > 1 and emitted[0] == int(d[0]):
+            second[emitted[1]] += 1
+            n2 += 1
+    assert (first / N - probs[0]).abs().max() < 0.012
+    assert (second / n2 - probs[1]).abs().max() < 0.035
+    # the kept fraction of the first draft is p_0(d_0)
+    assert abs(n2 / N - float(probs[0, d[0]])) < 0.012 and accepted > 0
+    # a draft the target cannot produce (top-k excludes it) is never kept
+    pk = SamplingParams(temperature=1.0, top_k=1)
+    for _ in range(50):
+        a, x = sampling.speculative_sample(lg, torch.tensor([int(lg[0].argmin()), 0, 0]), pk, g)
+        assert a == 0 and x == int(lg[0].argmax())
+
+
+def test_mtp_accept_mixes_greedy_and_sampling_sequences():
+    """The verify step's acceptance: greedy sequences keep the draft prefix
+    equal to the argmax; sampling ones draw, and t[i, a] holds the drawn token."""
+    from k8v4_xpu_b200.spec.mtp import MTPSpeculator
+    spec = object.__new__(MTPSpeculator)
+    spec.w, spec.k = 4, 3
+    eng = _engine()
+    spec.eng = eng
+    B, w = 2, 4
+    hid = torch.arange(B * w, dtype=torch.float32).view(B * w, 1).repeat(1, 8)
+    greedy = eng.model.greedy(hid).view(B, w)
+    ids = torch.zeros(B, w, dtype=torch.int64)
+    ids[0, 1:] = torch.tensor([greedy[0, 0], greedy[0, 1], 7])       # two drafts match the argmax
+    ids[1, 1:] = greedy[1, :3]
+    seqs = [Sequence(0, [1], SamplingParams()), Sequence(1, [1], SamplingParams(temperature=1.0, seed=5))]
+    t, a = spec._accept(hid, ids, B, seqs)
+    assert int(a[0]) == 2 and torch.equal(t[0], greedy[0])
+    t2, a2 = spec._accept(hid, ids, B, [seqs[0], Sequence(1, [1], SamplingParams(temperature=1.0, seed=5))])
+    assert torch.equal(t, t2) and torch.equal(a, a2)  # same seed, same draws
+    assert 0 <= int(a[1]) <= 3 and torch.equal(t[1, :int(a[1])], ids[1, 1:1 + int(a[1])])
+    tg, ag = spec._accept(hid, ids, B, [Sequence(0, [1], SamplingParams())] * 2)  # no sampling: argmax kernel path
+    assert torch.equal(tg, greedy) and int(ag[1]) == 3
