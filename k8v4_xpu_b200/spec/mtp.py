@@ -196,7 +196,7 @@ class MTPSpeculator:
         lg = m.logits(hid)
         if self.eng.tp > 1:
             lg = m.comm.all_gather(lg, dim=1)
-        lg = lg.view(B, w, -1)
+        lg = lg.reshape(B, w, -1)  # the lm_head may return a view over padded vocab rows
         t = torch.argmax(lg.float(), dim=-1)
         a = (d == t[:, :-1]).to(torch.int64).cumprod(1).sum(1)
         for i, s in enumerate(seqs):
