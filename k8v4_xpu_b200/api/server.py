@@ -11,11 +11,14 @@ samples, with ``top_p``, ``top_k`` (0 or -1: off) and ``seed``
 (``runtime.sampling``; under MTP the drafts are verified by speculative
 sampling). Stop
 strings (``stop``) end a request before the first match, in streamed and
-whole responses, and drop its sequence from the engine. ``n`` must be 1.
+whole responses, and drop its sequence from the engine. ``n`` (1-16)
+choices run as n engine requests over the same prompt (seed + i for choice
+i of a seeded request).
 """
 from __future__ import annotations
 
 import asyncio
+import dataclasses
 import json
 import time
 import uuid
@@ -73,8 +76,6 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
     eos = getattr(tokenizer, "eos_token_id", None)
 
     def params_for(req: _Common, prompt_len: int) -> SamplingParams:
-        if req.n != 1:
-            raise HTTPException(400, "only n=1 is supported")
         mt = req.max_completion_tokens if req.max_completion_tokens is not None else req.max_tokens
         mt = 16 if mt is None else mt  # an explicit 0 is refused below, not defaulted
         if mt < 1:
@@ -121,75 +122,110 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
 
     async def generate(prompt: list[int], req: _Common, chat: bool, request: Request):
         params = params_for(req, len(prompt))
-        h, out = await run(prompt, params)
+        if not 1 <= req.n <= 16:
+            raise HTTPException(400, "n must lie in [1, 16]")
+        # n choices are n engine requests over the same prompt (the prefix
+        # cache shares its pages); seeded requests give choice i seed + i
+        runs = []
+        for i in range(req.n):
+            p = params if i == 0 else dataclasses.replace(
+                params, seed=None if params.seed is None else params.seed + i)
+            runs.append(await run(prompt, p))
         rid = ("chatcmpl-" if chat else "cmpl-") + uuid.uuid4().hex[:24]
         created = int(time.time())
         obj = "chat.completion" if chat else "text_completion"
         opts = req.stream_options or StreamOptions()
 
+        def abort_all():
+            for h, _ in runs:
+                driver.abort(h)
+
         if not req.stream:
-            toks: list[int] = []
-            reason = None
-            matcher = StopMatcher(req.stop)
-            detok = IncrementalDecoder(tokenizer)
-            parts: list[str] = []
-            while True:
-                new, fin, why = await out.get()
-                toks.extend(new)
-                if matcher.stops and not (fin and why and (why == "error" or why.startswith("rejected: "))):
-                    shown, stopped = matcher.feed(detok.push(new, final=fin), final=fin)
-                    parts.append(shown)
-                    if stopped:  # a stop string ends the request: the engine drops the sequence
-                        if not fin:
-                            driver.abort(h)
-                        reason = "stop"
+            async def collect(h, out):
+                toks: list[int] = []
+                reason = None
+                matcher = StopMatcher(req.stop)
+                detok = IncrementalDecoder(tokenizer)
+                parts: list[str] = []
+                while True:
+                    new, fin, why = await out.get()
+                    toks.extend(new)
+                    if matcher.stops and not (fin and why and (why == "error" or why.startswith("rejected: "))):
+                        shown, stopped = matcher.feed(detok.push(new, final=fin), final=fin)
+                        parts.append(shown)
+                        if stopped:  # a stop string ends the request: the engine drops the sequence
+                            if not fin:
+                                driver.abort(h)
+                            reason = "stop"
+                            break
+                    if fin:
+                        reason = why
                         break
-                if fin:
-                    reason = why
-                    break
-            if reason == "error":
-                raise HTTPException(500, "engine failed")
-            if reason and reason.startswith("rejected: "):
-                raise HTTPException(400, reason[len("rejected: "):])
-            text = "".join(parts) if matcher.stops else tokenizer.decode(toks)
-            choice = ({"index": 0, "message": {"role": "assistant", "content": text}, "finish_reason": reason}
-                      if chat else {"index": 0, "text": text, "finish_reason": reason, "logprobs": None})
-            choice["token_ids"] = toks
+                text = "".join(parts) if matcher.stops else tokenizer.decode(toks)
+                return toks, text, reason
+
+            results = await asyncio.gather(*(collect(h, out) for h, out in runs))
+            for _, _, reason in results:
+                if reason == "error":
+                    raise HTTPException(500, "engine failed")
+                if reason and reason.startswith("rejected: "):
+                    raise HTTPException(400, reason[len("rejected: "):])
+            choices = []
+            for i, (toks, text, reason) in enumerate(results):
+                choice = ({"index": i, "message": {"role": "assistant", "content": text}, "finish_reason": reason}
+                          if chat else {"index": i, "text": text, "finish_reason": reason, "logprobs": None})
+                choice["token_ids"] = toks
+                choices.append(choice)
             return {"id": rid, "object": obj, "created": created, "model": served_model_name,
-                    "choices": [choice], "usage": _usage(len(prompt), len(toks))}
+                    "choices": choices, "usage": _usage(len(prompt), sum(len(r[0]) for r in results))}
 
         async def events():
             n_out = 0
-            detok = IncrementalDecoder(tokenizer)
-            matcher = StopMatcher(req.stop)
             chunk_obj = "chat.completion.chunk" if chat else "text_completion"
-            if chat:
-                first = {"id": rid, "object": chunk_obj, "created": created, "model": served_model_name,
-                         "choices": [{"index": 0, "delta": {"role": "assistant", "content": ""},
-                                      "finish_reason": None}]}
-                if opts.continuous_usage_stats:
-                    first["usage"] = _usage(len(prompt), 0)
-                yield "data: %s\n\n" % json.dumps(first)
-            try:
+            merged: asyncio.Queue = asyncio.Queue()
+
+            async def pump(i, out):
                 while True:
-                    if await request.is_disconnected():
-                        driver.abort(h)
+                    item = await out.get()
+                    await merged.put((i, item))
+                    if item[1]:
                         return
-                    new, fin, why = await out.get()
+
+            pumps = [asyncio.ensure_future(pump(i, out)) for i, (_, out) in enumerate(runs)]
+            detoks = [IncrementalDecoder(tokenizer) for _ in runs]
+            matchers = [StopMatcher(req.stop) for _ in runs]
+            live = set(range(len(runs)))
+            if chat:
+                for i in range(len(runs)):
+                    first = {"id": rid, "object": chunk_obj, "created": created, "model": served_model_name,
+                             "choices": [{"index": i, "delta": {"role": "assistant", "content": ""},
+                                          "finish_reason": None}]}
+                    if opts.continuous_usage_stats:
+                        first["usage"] = _usage(len(prompt), 0)
+                    yield "data: %s\n\n" % json.dumps(first)
+            try:
+                while live:
+                    if await request.is_disconnected():
+                        abort_all()
+                        return
+                    i, (new, fin, why) = await merged.get()
+                    if i not in live:
+                        continue
                     if fin and why and why.startswith("rejected: "):
                         yield "data: %s\n\n" % json.dumps({"error": {"message": why[len("rejected: "):],
                                                                       "type": "invalid_request_error"}})
+                        abort_all()
                         break
                     n_out += len(new)
-                    text, stopped = matcher.feed(detok.push(new, final=fin), final=fin)
-                    if stopped and not fin:  # a stop string ends the request here
-                        driver.abort(h)
+                    text, stopped = matchers[i].feed(detoks[i].push(new, final=fin), final=fin)
+                    if stopped and not fin:  # a stop string ends this choice here
+                        driver.abort(runs[i][0])
                         fin, why = True, "stop"
                     elif stopped:
                         why = "stop"
                     if new or fin:
-                        ch = ({"index": 0, "delta": {"content": text}, "finish_reason": why if fin else None}
-                              if chat else {"index": 0, "text": text, "finish_reason": why if fin else None,
+                        ch = ({"index": i, "delta": {"content": text}, "finish_reason": why if fin else None}
+                              if chat else {"index": i, "text": text, "finish_reason": why if fin else None,
                                             "logprobs": None})
                         ch["token_ids"] = list(new)
                         body = {"id": rid, "object": chunk_obj, "created": created, "model": served_model_name,
@@ -198,15 +234,18 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
                             body["usage"] = _usage(len(prompt), n_out)
                         yield "data: %s\n\n" % json.dumps(body)
                     if fin:
-                        break
+                        live.discard(i)
                 if opts.include_usage:
                     yield "data: %s\n\n" % json.dumps({"id": rid, "object": chunk_obj, "created": created,
                                                        "model": served_model_name, "choices": [],
                                                        "usage": _usage(len(prompt), n_out)})
                 yield "data: [DONE]\n\n"
             except asyncio.CancelledError:
-                driver.abort(h)
+                abort_all()
                 raise
+            finally:
+                for t in pumps:
+                    t.cancel()
 
         return StreamingResponse(events(), media_type="text/event-stream")
 

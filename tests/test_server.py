@@ -84,7 +84,8 @@ def test_concurrent_requests_and_limits(client):
     for i, o in enumerate(outs, 1):
         assert o["choices"][0]["token_ids"][0] == 100 * i + 20
     assert c.post("/v1/completions", json={"prompt": [1] * 500, "max_tokens": 20}).status_code == 400
-    assert c.post("/v1/completions", json={"prompt": [1], "max_tokens": 2, "n": 2}).status_code == 400
+    assert c.post("/v1/completions", json={"prompt": [1], "max_tokens": 2, "n": 17}).status_code == 400
+    assert c.post("/v1/completions", json={"prompt": [1], "max_tokens": 2, "n": 0}).status_code == 400
     eng.blocks.check_invariants()
     assert driver.healthy
 
@@ -285,4 +286,29 @@ def test_stop_strings_end_requests_streamed_and_not(client):
     while eng.has_unfinished() and time.monotonic() < deadline:
         time.sleep(0.01)
     assert not eng.has_unfinished()  # the stopped requests were dropped, not left decoding
+    eng.blocks.check_invariants()
+
+
+def test_n_choices_streamed_and_not(client):
+    """n choices come back with their indices, usage counts every choice's
+    tokens once, and a stream interleaves the choices' chunks."""
+    c, eng, _ = client
+    body = {"prompt": [ord("a") + 3], "max_tokens": 3, "ignore_eos": True, "n": 3}
+    r = c.post("/v1/completions", json=body).json()
+    assert [ch["index"] for ch in r["choices"]] == [0, 1, 2]
+    assert all(ch["text"] == "bcd" and ch["finish_reason"] == "length" for ch in r["choices"])
+    assert r["usage"] == {"prompt_tokens": 1, "completion_tokens": 9, "total_tokens": 10}
+    texts = {0: "", 1: "", 2: ""}
+    fins = {}
+    with c.stream("POST", "/v1/chat/completions", json={"messages": [{"role": "user", "content": "x"}],
+                                                        "max_tokens": 3, "ignore_eos": True, "n": 3,
+                                                        "stream": True}) as s:
+        for line in s.iter_lines():
+            if line.startswith("data: ") and line != "data: [DONE]":
+                ch = json.loads(line[6:])["choices"][0]
+                texts[ch["index"]] += ch["delta"].get("content", "")
+                if ch["finish_reason"]:
+                    fins[ch["index"]] = ch["finish_reason"]
+    assert fins == {0: "length", 1: "length", 2: "length"}
+    assert len({t for t in texts.values()}) == 1 and texts[0]
     eng.blocks.check_invariants()
