@@ -102,6 +102,13 @@ def decode_splits(max_pages: int, nseq: int, heads: int) -> int:
     return int(max(1, min(want, tiles, 64)))
 
 
+def stream_sync(device) -> None:
+    """Wait for the device's current stream (host-side stand-in tensors on a
+    CPU device need no wait)."""
+    if torch.device(device).type == "cuda":
+        torch.cuda.current_stream(device).synchronize()
+
+
 class LLMEngine:
     def __init__(self, cfg: EngineConfig, model_cfg: ModelConfig, comm=None, rank: int = 0):
         self.cfg = cfg
@@ -282,11 +289,13 @@ class LLMEngine:
         i32[: B + 1] = cu
         i32[B + 1: 2 * B + 1] = lens
         i32[2 * B + 1:] = bt.reshape(-1)
-        g64 = self._pin_i64[: 3 * T + L].to(dev, non_blocking=True)
-        g32 = self._pin_i32[: 2 * B + 1 + B * W].to(dev, non_blocking=True)
+        # copy=True: the inputs never alias the staging buffer (they would on a CPU device)
+        g64 = self._pin_i64[: 3 * T + L].to(dev, non_blocking=True, copy=True)
+        g32 = self._pin_i32[: 2 * B + 1 + B * W].to(dev, non_blocking=True, copy=True)
         self.h2d_bytes += g64.numel() * 8 + g32.numel() * 4
-        self._h2d_done = torch.cuda.Event()
-        self._h2d_done.record(torch.cuda.current_stream(dev))
+        if dev.type == "cuda":
+            self._h2d_done = torch.cuda.Event()
+            self._h2d_done.record(torch.cuda.current_stream(dev))
         inp = StepInputs(
             input_ids=g64[:T], positions=g64[T:2 * T], slots=g64[2 * T:3 * T], logit_rows=g64[3 * T:],
             cu_q=g32[: B + 1], seq_lens=g32[B + 1: 2 * B + 1], block_table=g32[2 * B + 1:].view(B, W),
@@ -364,7 +373,7 @@ class LLMEngine:
         n = ids.numel()
         out = self._pin_out[:n]
         out.copy_(ids, non_blocking=True)
-        torch.cuda.current_stream(self.device).synchronize()
+        stream_sync(self.device)
         self.d2h_bytes += n * 8
         return out.numpy().copy()
 

@@ -36,6 +36,7 @@ import torch
 from ..models.dense import StepInputs
 from ..runtime.block_manager import CapacityError
 from ..runtime.sampling import generator_for, samples, speculative_sample
+from ..runtime.engine import stream_sync
 from ..runtime.graphs import decode_inputs, prepare_benign, stage_decode_inputs
 
 
@@ -284,7 +285,7 @@ class MTPSpeculator:
         n = out.numel()
         host = eng._pin_out[:n]
         host.copy_(out, non_blocking=True)
-        torch.cuda.current_stream(eng.device).synchronize()
+        stream_sync(eng.device)
         eng.d2h_bytes += n * 8
         res = host.numpy().copy()
         w, k = self.w, self.k
@@ -370,7 +371,7 @@ class MTPSpeculator:
         eng.h2d_bytes += T * 8
         mh = m.mtp_forward(hid_all, dev_ids, inp, eng.kv_caches[-1], eng.ws)
         if not finals:
-            torch.cuda.current_stream(eng.device).synchronize()
+            stream_sync(eng.device)
             return
         live = []
         for c, row in finals:

@@ -1,0 +1,116 @@
+"""The MTP speculative step end to end on the host (CPU).
+
+``LLMEngine`` and ``MTPSpeculator`` run their real host logic (scheduling,
+input staging into the workspace buffers, the verify / catch-up / draft body,
+acceptance, commit and rollback) on CPU tensors, against a stand-in model:
+the target scores the next token of ``x`` with logits 30, 29, 28 at
+``7x + 3``, ``7x + 4``, ``7x + 5`` (mod V) and 0 elsewhere, and the drafter
+proposes ``7x + 3`` except after multiples of 5. Greedy requests must emit
+the argmax chain whatever was accepted; sampling requests must emit one of
+the three scored tokens at every step, repeat under the same seed, and leave
+the argmax chain.
+"""
+import types
+
+import torch
+
+from k8v4_xpu_b200.runtime.block_manager import BlockManager
+from k8v4_xpu_b200.runtime.scheduler import SamplingParams, Scheduler
+
+V = 997
+
+
+class _Model:
+    def __init__(self):
+        self.vocab_start = 0
+        self.shape = types.SimpleNamespace(gqa_local=6)
+
+    def forward(self, inp, kv_caches, ws=None, all_rows=False):
+        h = inp.input_ids.to(torch.float32).view(-1, 1).repeat(1, 4)
+        return h if all_rows else h.index_select(0, inp.logit_rows)
+
+    def logits(self, h):
+        x = h[:, 0].to(torch.int64)
+        lg = torch.zeros(h.shape[0], V)
+        for off, val in ((3, 30.0), (4, 29.0), (5, 28.0)):
+            lg.scatter_(1, ((7 * x + off) % V).view(-1, 1), val)
+        return lg
+
+    def greedy(self, h):
+        return (h[:, 0].to(torch.int64) * 7 + 3) % V
+
+    def mtp_forward(self, hidden, ids, inp, cache, ws=None):
+        x = torch.where(ids % 5 == 0, ids + 1, ids)  # the drafter errs after multiples of 5
+        return x.to(torch.float32).view(-1, 1).repeat(1, 4)
+
+
+def _engine(k=6, seqs=2):
+    from k8v4_xpu_b200.runtime.engine import LLMEngine
+    from k8v4_xpu_b200.runtime.workspace import Workspace
+    from k8v4_xpu_b200.spec.mtp import MTPSpeculator
+    eng = object.__new__(LLMEngine)  # the engine's host logic without its GPU set-up
+    w = k + 1
+    eng.cfg = types.SimpleNamespace(cuda_graphs=False, capture_sizes=(), max_num_seqs=seqs, seed=0,
+                                    speculative_tokens=k)
+    eng.tp = 1
+    eng.device = torch.device("cpu")
+    eng.blocks = BlockManager(96, block_size=16, page=16, enable_prefix_caching=False)
+    eng.scheduler = Scheduler(eng.blocks, max_num_seqs=seqs, max_num_batched_tokens=64, decode_width=w,
+                              max_model_len=1024, lookahead=w, mix_prefill_with_decode=False, prefill_slice=32)
+    eng.stats = {"steps": 0, "prompt_tokens": 0, "generated_tokens": 0, "prefill_time": 0.0,
+                 "decode_time": 0.0, "iteration_tokens": []}
+    eng.h2d_bytes = eng.d2h_bytes = 0
+    eng.layout = types.SimpleNamespace(hkv=2, gqa=6, page=16)
+    eng.max_pages = (1024 + 2 * w + 15) // 16 + 1
+    max_tokens = max(64, seqs * w)
+    eng.ws = Workspace("cpu", max_tokens, seqs, eng.max_pages, 64, 2, 6, w, 64)
+    eng._pin_i64 = torch.zeros(4 * max_tokens, dtype=torch.int64)
+    eng._pin_i32 = torch.zeros(2 * (seqs + 1) + seqs * eng.max_pages + max_tokens, dtype=torch.int32)
+    eng._pin_out = torch.zeros(max_tokens, dtype=torch.int64)
+    eng._h2d_done = None
+    eng.kv_caches = [None, None, None]
+    eng.graphs = None
+    eng.model = _Model()
+    eng.mtp = None
+    eng.mtp = MTPSpeculator(eng, k, None, seed=0)
+    return eng
+
+
+def _chain(prompt, n):
+    out, t = [], prompt[-1]
+    for _ in range(n):
+        t = (7 * t + 3) % V
+        out.append(t)
+    return out
+
+
+def _run(n_tokens=30, seed=7):
+    eng = _engine()
+    pg, ps = list(range(5, 5 + 45)), list(range(600, 600 + 21))
+    g = eng.add_request(pg, SamplingParams(max_tokens=n_tokens, ignore_eos=True))
+    s = eng.add_request(ps, SamplingParams(max_tokens=n_tokens, ignore_eos=True, temperature=1.0, seed=seed))
+    steps = 0
+    while eng.has_unfinished():
+        eng.step()
+        steps += 1
+        assert steps < 200
+    eng.blocks.check_invariants()
+    return eng, pg, ps, g.output, s.output
+
+
+def test_mtp_step_on_the_host_greedy_and_sampling():
+    eng, pg, ps, g1, s1 = _run()
+    assert g1 == _chain(pg, 30)
+    prev = ps[-1]
+    for t in s1:  # every sampled token is one of the three the target scores
+        assert t in {(7 * prev + off) % V for off in (3, 4, 5)}
+        prev = t
+    # tokens after the first come from the speculative step: some leave the argmax
+    off_argmax = sum(1 for a, b in zip(s1, s1[1:]) if b != (7 * a + 3) % V)
+    assert off_argmax >= 3
+    st = eng.mtp.stats
+    assert st.num_drafts > 0 and 0 < st.num_accepted_tokens < st.num_draft_tokens
+    _, _, _, g2, s2 = _run()
+    assert (g2, s2) == (g1, s1)          # same seeds, same draws
+    _, _, _, _, s3 = _run(seed=8)
+    assert s3 != s1
