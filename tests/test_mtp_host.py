@@ -114,3 +114,29 @@ def test_mtp_step_on_the_host_greedy_and_sampling():
     assert (g2, s2) == (g1, s1)          # same seeds, same draws
     _, _, _, _, s3 = _run(seed=8)
     assert s3 != s1
+
+
+def test_plain_engine_step_on_the_host_greedy_and_sampling():
+    """The same stand-in without MTP: prefill chunks mixed with decode rows,
+    the argmax for greedy requests and seeded draws for sampling ones."""
+    def run(seed):
+        eng = _engine()
+        eng.mtp = None
+        eng.scheduler = Scheduler(eng.blocks, max_num_seqs=2, max_num_batched_tokens=24, decode_width=1,
+                                  max_model_len=1024)
+        pg, ps = list(range(5, 5 + 45)), list(range(600, 600 + 21))
+        g = eng.add_request(pg, SamplingParams(max_tokens=20, ignore_eos=True))
+        s = eng.add_request(ps, SamplingParams(max_tokens=20, ignore_eos=True, temperature=1.0, seed=seed))
+        while eng.has_unfinished():
+            eng.step()
+        eng.blocks.check_invariants()
+        return pg, ps, g.output, s.output
+
+    pg, ps, g1, s1 = run(3)
+    assert g1 == _chain(pg, 20)
+    prev = ps[-1]
+    for t in s1:
+        assert t in {(7 * prev + off) % V for off in (3, 4, 5)}
+        prev = t
+    assert sum(1 for a, b in zip([ps[-1]] + s1, s1) if b != (7 * a + 3) % V) >= 3
+    assert run(3)[3] == s1 and run(4)[3] != s1
