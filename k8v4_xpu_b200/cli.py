@@ -91,6 +91,24 @@ def build_engine(cfg: ServeConfig, comm=None, rank: int = 0, device: str = "cuda
     return eng
 
 
+def gpu_checks(cfg: ServeConfig, local: int, nvml=None):
+    """Start-up GPU checks of one rank (the reference launcher's fault-log
+    warning and card settings, ``launch.sh:201-213``): local rank 0 prints
+    NVML's warnings about every GPU (read only), and each rank applies the
+    opt-in power limit / clock range to its own GPU. Returns (nvml, what was
+    changed) when something was set, for ``gpu_setup.restore`` at exit."""
+    from .tools import gpu_setup
+    nvml = nvml or gpu_setup.load_nvml()
+    if nvml is None:
+        return None
+    if local == 0:
+        for w in gpu_setup.preflight(nvml):
+            print("WARN: " + w, file=sys.stderr, flush=True)
+    done = gpu_setup.apply_settings(nvml, [local], cfg.gpu_power_limit,
+                                    gpu_setup.parse_clock_range(cfg.gpu_clock_range))
+    return (nvml, done) if done else None
+
+
 def run_rank(cfg: ServeConfig) -> int:
     import torch
     import torch.distributed as dist
@@ -100,6 +118,7 @@ def run_rank(cfg: ServeConfig) -> int:
     from .parallel.comm import TPComm, init_from_env
     rank, world, local = init_from_env(timeout_s=600)
     device = "cuda:%d" % local
+    gpu_settings = gpu_checks(cfg, local)
     pg = groups.build(cfg.tensor_parallel_size, cfg.context_parallel_size)
     comm = TPComm(pg.tp_group) if pg.tp > 1 else None
     control = TPControl(dist.new_group(backend="gloo")) if world > 1 else None
@@ -132,6 +151,9 @@ def run_rank(cfg: ServeConfig) -> int:
         if eng.mtp is not None:
             eng.mtp.release()
         torch.cuda.synchronize()
+        if gpu_settings:
+            from .tools import gpu_setup
+            gpu_setup.restore(gpu_settings[0], gpu_settings[1])
         if world > 1 and dist.is_initialized():
             dist.destroy_process_group()
     return 0
@@ -196,6 +218,9 @@ def doctor() -> dict:
     rep["sm100"] = bool(devs) and all(d["sm"] == "10.0" for d in devs)
     if torch.distributed.is_available() and torch.distributed.is_nccl_available():
         rep["nccl"] = ".".join(str(x) for x in torch.cuda.nccl.version()) if rep["gpus"] else "available"
+    from .tools import gpu_setup
+    nvml = gpu_setup.load_nvml() if rep["gpus"] else None
+    rep["gpu_warnings"] = gpu_setup.preflight(nvml) if nvml is not None else []  # read-only NVML queries
     rep["ok"] = bool(rep["layout_ok"] and rep["library_loads"] and (rep["gpus"] == 0 or rep["sm100"]))
     return rep
 

@@ -60,6 +60,8 @@ ENV: dict[str, tuple[str, type]] = {
     "tokenizer": ("K8V4_TOKENIZER", str),
     "dry_run": ("K8V4_DRY_RUN", bool),
     "profile": ("K8V4_PROFILE_NAME", str),
+    "gpu_power_limit": ("K8V4_GPU_POWER_LIMIT", float),
+    "gpu_clock_range": ("K8V4_GPU_CLOCK_RANGE", str),
 }
 
 
@@ -145,6 +147,9 @@ class ServeConfig:
     fit_capacity: bool = True
     kv_cache_dtype_skip_layers: tuple[int, ...] = ()
     kv_skip_dtype: str | None = None
+    # opt-in GPU settings (off unless given; they outlast the process): tools/gpu_setup.py
+    gpu_power_limit: float | None = None
+    gpu_clock_range: str | None = None
 
     @property
     def world_size(self) -> int:
@@ -197,6 +202,11 @@ class ServeConfig:
             raise ValueError("--port must lie in [0, 65535]")
         if self.seed < 0:
             raise ValueError("--seed must be non-negative")
+        if self.gpu_power_limit is not None and self.gpu_power_limit <= 0:
+            raise ValueError("--gpu-power-limit must be positive (watts)")
+        if self.gpu_clock_range is not None:
+            from .tools.gpu_setup import parse_clock_range
+            parse_clock_range(self.gpu_clock_range)
         if self.mtp_prefill_slice < 0:
             raise ValueError("--mtp-prefill-slice must be >= 0")
         if self.forced_accept_mean is not None:
@@ -254,6 +264,8 @@ def build_parser() -> argparse.ArgumentParser:
     a("--kv-cache-dtype-skip-layers", help="comma-separated layers whose KV stays in --kv-skip-dtype "
       "(the MTP layer's index is the layer count)")
     a("--kv-skip-dtype", help="skip layers' KV dtype: auto (bf16), bfloat16, fp8, fp8_e4m3, fp8_e5m2")
+    a("--gpu-power-limit", type=float, help="opt-in: set each GPU's power limit (W) at start, restored at exit")
+    a("--gpu-clock-range", help="opt-in: lock each GPU's SM clocks to MIN,MAX MHz at start, unlocked at exit")
     return ap
 
 
