@@ -28,7 +28,7 @@ class RequestHandle:
     prompt: list[int]
     params: SamplingParams
     loop: object = None          # asyncio loop of the HTTP handler
-    out: object = None           # asyncio.Queue of (new_ids, finished, reason)
+    out: object = None           # asyncio.Queue of (new_ids, finished, reason, new_logprobs or None)
     seq: object = None
     emitted: int = 0
     arrival: float = dataclasses.field(default_factory=time.monotonic)
@@ -129,10 +129,10 @@ class EngineDriver:
             pass
         return cmds
 
-    def _emit(self, h: RequestHandle, new: list[int], finished: bool, reason: str | None) -> None:
+    def _emit(self, h: RequestHandle, new: list[int], finished: bool, reason: str | None, lps=None) -> None:
         if h.out is None:
             return
-        item = (new, finished, reason)
+        item = (new, finished, reason, lps)
         if h.loop is not None:
             h.loop.call_soon_threadsafe(h.out.put_nowait, item)
         else:
@@ -147,8 +147,9 @@ class EngineDriver:
             new = seq.output[h.emitted:]
             fin = seq.seq_id in done_ids or seq.done
             if new or fin:
+                lps = list(seq.logprobs[h.emitted:len(seq.output)]) if seq.params.logprobs is not None else None
                 h.emitted = len(seq.output)
-                self._emit(h, list(new), fin, seq.finish_reason if fin else None)
+                self._emit(h, list(new), fin, seq.finish_reason if fin else None, lps)
             if fin:
                 if self.metrics is not None:
                     self.metrics.observe_finished(seq)

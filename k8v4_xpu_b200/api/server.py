@@ -11,7 +11,9 @@ samples, with ``top_p``, ``top_k`` (0 or -1: off) and ``seed``
 (``runtime.sampling``; under MTP the drafts are verified by speculative
 sampling). Stop
 strings (``stop``) end a request before the first match, in streamed and
-whole responses, and drop its sequence from the engine. ``n`` (1-16)
+whole responses, and drop its sequence from the engine. ``logprobs``
+(completions: the top-N count; chat: ``logprobs`` + ``top_logprobs``) gives
+each token's log-probability under the model's logits. ``n`` (1-16)
 choices run as n engine requests over the same prompt (seed + i for choice
 i of a seeded request).
 """
@@ -47,6 +49,8 @@ class _Common(BaseModel):
     ignore_eos: bool = False
     stop_token_ids: list[int] = Field(default_factory=list)
     stop: str | list[str] | None = None
+    logprobs: int | bool | None = None   # completions: top-N count; chat: on / off
+    top_logprobs: int | None = None      # chat: top-N count
     temperature: float | None = None
     top_p: float | None = None
     top_k: int | None = None
@@ -124,6 +128,40 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
         params = params_for(req, len(prompt))
         if not 1 <= req.n <= 16:
             raise HTTPException(400, "n must lie in [1, 16]")
+        if chat:
+            n_lp = int(req.top_logprobs or 0) if req.logprobs else None
+        else:
+            n_lp = None if req.logprobs is None or req.logprobs is False else int(req.logprobs)
+        if n_lp is not None:
+            if not 0 <= n_lp <= 20:
+                raise HTTPException(400, "logprobs / top_logprobs must lie in [0, 20]")
+            params = dataclasses.replace(params, logprobs=n_lp)
+
+        def tok_str(t: int) -> str:
+            return tokenizer.decode([int(t)])
+
+        def lp_object(toks, lps, offset: int = 0):
+            """The OpenAI logprobs object of ``toks`` (None when not asked for)."""
+            if n_lp is None:
+                return None
+            lps = list(lps or []) + [None] * (len(toks) - len(lps or []))
+            if chat:
+                content = []
+                for t, e in zip(toks, lps):
+                    s = tok_str(t)
+                    top = [{"token": tok_str(i), "logprob": v, "bytes": list(tok_str(i).encode("utf-8"))}
+                           for i, v in (e[1] if e else [])]
+                    content.append({"token": s, "logprob": e[0] if e else None, "bytes": list(s.encode("utf-8")),
+                                    "top_logprobs": top})
+                return {"content": content}
+            tokens = [tok_str(t) for t in toks]
+            offsets = []
+            for s in tokens:
+                offsets.append(offset)
+                offset += len(s)
+            return {"tokens": tokens, "token_logprobs": [e[0] if e else None for e in lps],
+                    "top_logprobs": [({tok_str(i): v for i, v in e[1]} if e else None) for e in lps],
+                    "text_offset": offsets}
         # n choices are n engine requests over the same prompt (the prefix
         # cache shares its pages); seeded requests give choice i seed + i
         runs = []
@@ -143,13 +181,15 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
         if not req.stream:
             async def collect(h, out):
                 toks: list[int] = []
+                all_lps: list = []
                 reason = None
                 matcher = StopMatcher(req.stop)
                 detok = IncrementalDecoder(tokenizer)
                 parts: list[str] = []
                 while True:
-                    new, fin, why = await out.get()
+                    new, fin, why, lps = await out.get()
                     toks.extend(new)
+                    all_lps.extend(lps or [None] * len(new))
                     if matcher.stops and not (fin and why and (why == "error" or why.startswith("rejected: "))):
                         shown, stopped = matcher.feed(detok.push(new, final=fin), final=fin)
                         parts.append(shown)
@@ -162,18 +202,20 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
                         reason = why
                         break
                 text = "".join(parts) if matcher.stops else tokenizer.decode(toks)
-                return toks, text, reason
+                return toks, text, reason, all_lps
 
             results = await asyncio.gather(*(collect(h, out) for h, out in runs))
-            for _, _, reason in results:
+            for _, _, reason, _ in results:
                 if reason == "error":
                     raise HTTPException(500, "engine failed")
                 if reason and reason.startswith("rejected: "):
                     raise HTTPException(400, reason[len("rejected: "):])
             choices = []
-            for i, (toks, text, reason) in enumerate(results):
+            for i, (toks, text, reason, lps) in enumerate(results):
                 choice = ({"index": i, "message": {"role": "assistant", "content": text}, "finish_reason": reason}
                           if chat else {"index": i, "text": text, "finish_reason": reason, "logprobs": None})
+                if n_lp is not None:
+                    choice["logprobs"] = lp_object(toks, lps)
                 choice["token_ids"] = toks
                 choices.append(choice)
             return {"id": rid, "object": obj, "created": created, "model": served_model_name,
@@ -193,6 +235,7 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
 
             pumps = [asyncio.ensure_future(pump(i, out)) for i, (_, out) in enumerate(runs)]
             detoks = [IncrementalDecoder(tokenizer) for _ in runs]
+            offsets = [0] * len(runs)  # text offsets of the completions logprobs
             matchers = [StopMatcher(req.stop) for _ in runs]
             live = set(range(len(runs)))
             if chat:
@@ -208,7 +251,7 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
                     if await request.is_disconnected():
                         abort_all()
                         return
-                    i, (new, fin, why) = await merged.get()
+                    i, (new, fin, why, lps) = await merged.get()
                     if i not in live:
                         continue
                     if fin and why and why.startswith("rejected: "):
@@ -228,6 +271,9 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
                               if chat else {"index": i, "text": text, "finish_reason": why if fin else None,
                                             "logprobs": None})
                         ch["token_ids"] = list(new)
+                        if n_lp is not None:
+                            ch["logprobs"] = lp_object(list(new), lps, offsets[i])
+                            offsets[i] += sum(len(tok_str(t)) for t in new)
                         body = {"id": rid, "object": chunk_obj, "created": created, "model": served_model_name,
                                 "choices": [ch]}
                         if opts.continuous_usage_stats:

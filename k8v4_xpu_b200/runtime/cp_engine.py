@@ -34,7 +34,7 @@ from ..parallel.cp import PAGE, CPGroup
 from ..parallel.cp_combine import PeerCombine, cp_combine_mode, max_slot_floats
 from .block_manager import CapacityError
 from .engine import LLMEngine, decode_splits
-from .sampling import samples
+from .sampling import needs_logits
 
 
 class CPEngine(LLMEngine):
@@ -229,7 +229,7 @@ class CPDecodeGraphs:
         if self.eng.cp.peer is not None and len(self.eng.model.layers) % 2:
             return False
         return (len(sched.chunks) <= len(self.sizes) and all(c.num_tokens == 1 for c in sched.chunks)
-                and not any(samples(c.seq.params) for c in sched.chunks))
+                and not any(needs_logits(c.seq.params) for c in sched.chunks))
 
     def _inputs(self, B: int, nsplit: int) -> StepInputs:
         return StepInputs(

@@ -231,6 +231,8 @@ class LLMEngine:
         if params is not None:
             if params.temperature < 0 or not 0.0 < params.top_p <= 1.0 or params.top_k < 0:
                 raise ValueError("temperature must be >= 0, top_p in (0, 1], top_k >= 0")
+            if params.logprobs is not None and not 0 <= params.logprobs <= 20:
+                raise ValueError("logprobs must lie in [0, 20]")
         return self.scheduler.add(prompt, params)
 
     def has_unfinished(self) -> bool:
@@ -354,14 +356,21 @@ class LLMEngine:
         """Next-token ids [rows] on the device: the argmax, or, when a row's
         request samples, a draw from its full-vocabulary logits (the TP
         shards gathered on every rank; ``runtime.sampling``)."""
-        if not seqs or not any(sampling.samples(s.params) for s in seqs):
+        if not seqs or not any(sampling.needs_logits(s.params) for s in seqs):
             return self.model.greedy(hidden)
         lg = self.model.logits(hidden)
         if self.tp > 1:
             lg = self.model.comm.all_gather(lg, dim=1)
         gens = [sampling.generator_for(s, self.cfg.seed, self.device) if sampling.samples(s.params) else None
                 for s in seqs]
-        return sampling.sample_rows(lg, [s.params for s in seqs], gens)
+        ids = sampling.sample_rows(lg, [s.params for s in seqs], gens)
+        if any(sampling.wants_logprobs(s.params) for s in seqs):
+            host = ids.tolist()
+            stash = sampling.stash_of(self)
+            for i, s in enumerate(seqs):
+                if sampling.wants_logprobs(s.params):
+                    stash[s.seq_id] = [sampling.logprob_entry(lg[i], host[i], s.params.logprobs)]
+        return ids
 
     def _agree(self, ids: torch.Tensor) -> torch.Tensor:
         """Hook for engines whose ranks sample replicated rows (context
@@ -394,6 +403,7 @@ class LLMEngine:
             if seq.first_token_time is None:
                 seq.first_token_time = now
             seq.output.append(tok)
+            sampling.record(self, seq)
             self.stats["generated_tokens"] += 1
             if self._should_stop(seq, tok):
                 self.scheduler.finish(seq, "length" if len(seq.output) >= seq.params.max_tokens else "stop")

@@ -16,7 +16,7 @@ import torch
 
 from .. import ops
 from ..models.dense import StepInputs
-from .sampling import samples
+from .sampling import needs_logits
 
 
 def decode_inputs(ws, B: int, w: int, nsplit: int) -> StepInputs:
@@ -129,11 +129,12 @@ class DecodeGraphs:
 
     def can_run(self, sched) -> bool:
         """Uniform decode batches that fit a captured size and take the
-        argmax (a sampling request runs the step eagerly)."""
+        argmax (a step with a request that samples or asks for
+        log-probabilities runs eagerly)."""
         B = len(sched.chunks)
         widths = {c.num_tokens for c in sched.chunks}
         return (len(widths) == 1 and next(iter(widths)) in (1, self.width) and B <= max(self.sizes)
-                and not any(samples(c.seq.params) for c in sched.chunks))
+                and not any(needs_logits(c.seq.params) for c in sched.chunks))
 
     def capture(self, widths: tuple[int, ...] | None = None) -> None:
         eng = self.engine

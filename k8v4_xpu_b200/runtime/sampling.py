@@ -110,3 +110,42 @@ def speculative_sample(logits: torch.Tensor, drafts: torch.Tensor, p, gen: torch
     else:
         x = torch.multinomial(probs[k], 1, generator=gen)[0]
     return a, int(x)
+
+
+def wants_logprobs(params) -> bool:
+    """Whether a request asks for the log-probabilities of its tokens."""
+    return params is not None and getattr(params, "logprobs", None) is not None
+
+
+def needs_logits(params) -> bool:
+    """Requests whose steps need the full-vocabulary logits (so they run
+    eagerly): sampling ones and the ones asking for log-probabilities."""
+    return samples(params) or wants_logprobs(params)
+
+
+def logprob_entry(row_logits: torch.Tensor, token: int, top_n: int) -> tuple:
+    """(log-probability of ``token``, [(id, log-probability)] of the ``top_n``
+    most likely tokens) under the model's distribution (the raw logits, before
+    temperature and filtering, as vLLM reports them)."""
+    lsm = torch.log_softmax(row_logits.float(), -1)
+    top = []
+    if top_n:
+        v, i = torch.topk(lsm, int(top_n))
+        top = list(zip(i.tolist(), v.tolist()))
+    return float(lsm[int(token)]), top
+
+
+def stash_of(engine) -> dict:
+    """Per-sequence log-probability entries waiting for the commit of their tokens."""
+    return engine.__dict__.setdefault("_lp_next", {})
+
+
+def record(engine, seq) -> None:
+    """Append the next waiting entry (or None) to a sequence that asked for
+    log-probabilities, for the token just appended to its output."""
+    if wants_logprobs(seq.params):
+        stash = stash_of(engine)
+        lst = stash.get(seq.seq_id)
+        seq.logprobs.append(lst.pop(0) if lst else None)
+        if not lst:
+            stash.pop(seq.seq_id, None)

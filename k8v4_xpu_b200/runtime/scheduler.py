@@ -34,6 +34,7 @@ class SamplingParams:
     top_p: float = 1.0        # nucleus sampling (1: off)
     top_k: int = 0            # top-k sampling (0: off)
     seed: int | None = None   # per-request generator seed (None: derived from the engine seed)
+    logprobs: int | None = None  # None: off; N: each token's log-probability and the top N
 
 
 @dataclasses.dataclass
@@ -55,6 +56,7 @@ class Sequence:
     # token the sequence held (prompt + output so far)
     prefill_len: int | None = None
     generator: object = None   # torch.Generator of a sampling request (runtime.sampling)
+    logprobs: list = dataclasses.field(default_factory=list)  # per output token, when requested
 
     @property
     def tokens(self) -> "TokenView":

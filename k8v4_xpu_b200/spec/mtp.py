@@ -35,6 +35,7 @@ import torch
 
 from ..models.dense import StepInputs
 from ..runtime.block_manager import CapacityError
+from ..runtime import sampling
 from ..runtime.sampling import generator_for, samples, speculative_sample
 from ..runtime.engine import stream_sync
 from ..runtime.graphs import decode_inputs, prepare_benign, stage_decode_inputs
@@ -190,7 +191,7 @@ class MTPSpeculator:
         m = self.eng.model
         w = self.w
         d = ids[:, 1:]
-        if forced is not None or not seqs or not any(samples(s.params) for s in seqs):
+        if forced is not None or not seqs or not any(sampling.needs_logits(s.params) for s in seqs):
             t = m.greedy(hid).view(B, w)
             a = forced if forced is not None else (d == t[:, :-1]).to(torch.int64).cumprod(1).sum(1)
             return t, a
@@ -200,12 +201,18 @@ class MTPSpeculator:
         lg = lg.reshape(B, w, -1)  # the lm_head may return a view over padded vocab rows
         t = torch.argmax(lg.float(), dim=-1)
         a = (d == t[:, :-1]).to(torch.int64).cumprod(1).sum(1)
+        stash = sampling.stash_of(self.eng)
         for i, s in enumerate(seqs):
             if samples(s.params):
                 g = generator_for(s, self.eng.cfg.seed, self.eng.device)
                 ai, x = speculative_sample(lg[i], d[i], s.params, g)
                 a[i] = ai
                 t[i, ai] = x
+            if sampling.wants_logprobs(s.params):  # one entry per token the commit will emit
+                ai = int(a[i])
+                toks = d[i, :ai].tolist() + [int(t[i, ai])]
+                stash[s.seq_id] = [sampling.logprob_entry(lg[i, j], tok, s.params.logprobs)
+                                   for j, tok in enumerate(toks)]
         return t, a
 
     def _body(self, B: int, nsplit: int, seqs=None) -> torch.Tensor:
@@ -277,10 +284,10 @@ class MTPSpeculator:
         forced = self.forced_counts(B_real) if self.forced else None
         stage_decode_inputs(eng, sched, B, self.w, forced)
         self._topk = []
-        if self.use_graphs and not any(samples(c.seq.params) for c in chunks):
+        if self.use_graphs and not any(sampling.needs_logits(c.seq.params) for c in chunks):
             g, out = self.graphs[B]
             g.replay()
-        else:  # eager: no graphs, or a request that samples
+        else:  # eager: no graphs, or a request that samples or asks for log-probabilities
             out = self._body(B, decode_splits(eng.max_pages, B, eng.layout.hkv), [c.seq for c in chunks])
         n = out.numel()
         host = eng._pin_out[:n]
@@ -325,6 +332,7 @@ class MTPSpeculator:
             stopped = False
             for tok in emitted:
                 seq.output.append(tok)
+                sampling.record(eng, seq)
                 eng.stats["generated_tokens"] += 1
                 if eng._should_stop(seq, tok):
                     reason = "length" if len(seq.output) >= seq.params.max_tokens else "stop"
@@ -332,6 +340,7 @@ class MTPSpeculator:
                     finished.append(seq)
                     stopped = True
                     break
+            sampling.stash_of(eng).pop(seq.seq_id, None)  # entries past a stop are dropped
             if not stopped:
                 eng.blocks.publish(seq.seq_id, seq.tokens, seq.computed)
         return finished

@@ -46,6 +46,9 @@ class FakeEngine:
             if seq.first_token_time is None:
                 seq.first_token_time = now
             seq.output.append(tok)
+            n_lp = getattr(seq.params, "logprobs", None)
+            if n_lp is not None:  # a made-up distribution
+                seq.logprobs.append((-0.5, [(tok, -0.5), (tok + 1, -1.5), (tok + 2, -2.5)][:n_lp]))
             self.stats["generated_tokens"] += 1
             p = seq.params
             if len(seq.output) >= p.max_tokens or (not p.ignore_eos and tok in p.stop_token_ids):

@@ -140,3 +140,34 @@ def test_plain_engine_step_on_the_host_greedy_and_sampling():
         prev = t
     assert sum(1 for a, b in zip([ps[-1]] + s1, s1) if b != (7 * a + 3) % V) >= 3
     assert run(3)[3] == s1 and run(4)[3] != s1
+
+
+def _lp_ref(prev, tok):
+    x = torch.zeros(V)
+    for off, val in ((3, 30.0), (4, 29.0), (5, 28.0)):
+        x[(7 * prev + off) % V] = val
+    return float(torch.log_softmax(x, -1)[tok])
+
+
+def test_logprobs_of_every_emitted_token_with_and_without_mtp():
+    """A request asking for log-probabilities gets one entry per output
+    token: the token's log-probability under the model's logits and the top
+    N, from plain steps and from MTP verify rows alike."""
+    for mtp in (True, False):
+        eng = _engine()
+        if not mtp:
+            eng.mtp = None
+            eng.scheduler = Scheduler(eng.blocks, max_num_seqs=2, max_num_batched_tokens=24, decode_width=1,
+                                      max_model_len=1024)
+        ps = list(range(600, 600 + 21))
+        s = eng.add_request(ps, SamplingParams(max_tokens=17, ignore_eos=True, temperature=1.0, seed=1, logprobs=2))
+        g = eng.add_request(list(range(5, 50)), SamplingParams(max_tokens=17, ignore_eos=True))
+        while eng.has_unfinished():
+            eng.step()
+        assert len(s.logprobs) == len(s.output) == 17 and g.logprobs == []
+        prev = ps[-1]
+        for tok, (lp, top) in zip(s.output, s.logprobs):
+            assert abs(lp - _lp_ref(prev, tok)) < 1e-5
+            assert [t for t, _ in top] == [(7 * prev + 3) % V, (7 * prev + 4) % V]
+            prev = tok
+        assert not eng.__dict__.get("_lp_next")  # nothing left waiting

@@ -312,3 +312,34 @@ def test_n_choices_streamed_and_not(client):
     assert fins == {0: "length", 1: "length", 2: "length"}
     assert len({t for t in texts.values()}) == 1 and texts[0]
     eng.blocks.check_invariants()
+
+
+def test_logprobs_in_completions_and_chat(client):
+    """The stand-in engine reports log-probability -0.5 for each token it
+    emits and a made-up top list; the server formats them the OpenAI way."""
+    c, eng, _ = client
+    a = ord("a") + 3
+    r = c.post("/v1/completions", json={"prompt": [a], "max_tokens": 3, "ignore_eos": True, "logprobs": 2}).json()
+    lp = r["choices"][0]["logprobs"]
+    assert lp["tokens"] == ["b", "c", "d"] and lp["token_logprobs"] == [-0.5, -0.5, -0.5]
+    assert lp["top_logprobs"][0] == {"b": -0.5, "c": -1.5} and lp["text_offset"] == [0, 1, 2]
+    r = c.post("/v1/completions", json={"prompt": [a], "max_tokens": 2, "ignore_eos": True}).json()
+    assert r["choices"][0]["logprobs"] is None  # not asked for
+    r = c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "x"}], "max_tokens": 2,
+                                             "ignore_eos": True, "logprobs": True, "top_logprobs": 1}).json()
+    content = r["choices"][0]["logprobs"]["content"]
+    assert len(content) == 2 and all(e["logprob"] == -0.5 and len(e["top_logprobs"]) == 1 for e in content)
+    assert content[0]["bytes"] == list(content[0]["token"].encode("utf-8"))
+    got = []
+    with c.stream("POST", "/v1/completions", json={"prompt": [a], "max_tokens": 3, "ignore_eos": True,
+                                                   "logprobs": 0, "stream": True}) as s:
+        for line in s.iter_lines():
+            if line.startswith("data: ") and line != "data: [DONE]":
+                ch = json.loads(line[6:])["choices"]
+                if ch and ch[0].get("logprobs"):
+                    got.append(ch[0]["logprobs"])
+    assert [t for g in got for t in g["tokens"]] == ["b", "c", "d"]
+    assert [o for g in got for o in g["text_offset"]] == [0, 1, 2]
+    assert all(x == {} for g in got for x in g["top_logprobs"])  # logprobs 0: no top list
+    for bad in ({"logprobs": 21}, {"logprobs": -1}):
+        assert c.post("/v1/completions", json={"prompt": [a], "max_tokens": 2, **bad}).status_code == 400
