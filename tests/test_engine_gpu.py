@@ -128,3 +128,21 @@ def test_engine_samples_seeded_rows_beside_greedy_rows():
     m = DenseModel(TINY, device="cuda").random_init(seed=0)
     assert _teacher_forced_margin(m, pg, g1) < 0.05
     assert _teacher_forced_margin(m, ps, s1) > 0.0  # not the argmax chain
+
+
+def test_engine_reports_logprobs_of_greedy_tokens():
+    """A greedy request asking for log-probabilities runs its steps eagerly
+    and gets one entry per token: the chosen token holds the top
+    log-probability, and the top list is sorted."""
+    cfg = EngineConfig(model="tiny", max_model_len=2048, max_num_seqs=2, max_num_batched_tokens=96,
+                       num_kv_blocks=256, device="cuda")
+    eng = LLMEngine(cfg, TINY)
+    s = eng.add_request(list(range(3, 140)), SamplingParams(max_tokens=6, ignore_eos=True, logprobs=3))
+    while eng.has_unfinished():
+        eng.step()
+    assert ops.status() == 0
+    assert len(s.logprobs) == len(s.output) == 6
+    for tok, (lp, top) in zip(s.output, s.logprobs):
+        assert len(top) == 3 and lp <= 0.0
+        assert abs(lp - top[0][1]) < 1e-6
+        assert top[0][1] >= top[1][1] >= top[2][1]
