@@ -1,5 +1,4 @@
 """The CPU K8/V4 paged decode-attention oracle (CPU)."""
-import math
 
 import torch
 
