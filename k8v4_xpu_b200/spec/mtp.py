@@ -21,6 +21,11 @@ Here one decode step is ONE CUDA graph per batch size:
    MTP layer on one row per sequence, with positions and KV slots computed on
    the device from ``a`` and the block table.
 
+A step with a request that samples (temperature > 0) or asks for
+log-probabilities runs the same body eagerly: such sequences are verified by
+speculative sampling against the target's sampling distribution, and their
+entry ``t[a]`` holds the token drawn there (``_accept``).
+
 The host reads back ``(t, a, drafts)`` in one copy, emits ``d[1..a] + t[a]``
 and rolls the sequence's valid length back to ``start + a + 1``: KV written
 past it is dead and overwritten by later steps (rollback by length, as the
