@@ -13,7 +13,9 @@ sampling). Stop
 strings (``stop``) end a request before the first match, in streamed and
 whole responses, and drop its sequence from the engine. ``logprobs``
 (completions: the top-N count; chat: ``logprobs`` + ``top_logprobs``) gives
-each token's log-probability under the model's logits. ``n`` (1-16)
+each token's log-probability under the model's logits; with ``echo`` the
+prompt comes back first, with its tokens' log-probabilities when asked
+(computed during the prefill, which then takes no prefix-cache hit). ``n`` (1-16)
 choices run as n engine requests over the same prompt (seed + i for choice
 i of a seeded request).
 """
@@ -60,6 +62,7 @@ class _Common(BaseModel):
 
 class CompletionRequest(_Common):
     prompt: str | list[int] | list[str]
+    echo: bool = False  # the prompt comes back before the completion (with its logprobs when asked)
 
 
 class ChatMessage(BaseModel):
@@ -136,6 +139,17 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
             if not 0 <= n_lp <= 20:
                 raise HTTPException(400, "logprobs / top_logprobs must lie in [0, 20]")
             params = dataclasses.replace(params, logprobs=n_lp)
+        echo = bool(getattr(req, "echo", False))
+        if echo and n_lp is not None:
+            params = dataclasses.replace(params, prompt_logprobs=n_lp)
+        prompt_text = tokenizer.decode(prompt) if echo else ""
+
+        def echo_part(h):
+            """(tokens, entries) of the echoed prompt: the prompt's log-probabilities
+            the engine recorded during prefill (the first token has none)."""
+            seq = h.seq
+            lps = list(getattr(seq, "prompt_logprobs", None) or []) if seq is not None else []
+            return list(prompt), lps[:len(prompt)]
 
         def tok_str(t: int) -> str:
             return tokenizer.decode([int(t)])
@@ -212,10 +226,16 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
                     raise HTTPException(400, reason[len("rejected: "):])
             choices = []
             for i, (toks, text, reason, lps) in enumerate(results):
+                if echo:
+                    ptoks, plps = echo_part(runs[i][0])
+                    plps = plps + [None] * (len(ptoks) - len(plps))
+                    text, lp_toks, lps = prompt_text + text, ptoks + toks, plps + list(lps)
+                else:
+                    lp_toks = toks
                 choice = ({"index": i, "message": {"role": "assistant", "content": text}, "finish_reason": reason}
                           if chat else {"index": i, "text": text, "finish_reason": reason, "logprobs": None})
                 if n_lp is not None:
-                    choice["logprobs"] = lp_object(toks, lps)
+                    choice["logprobs"] = lp_object(lp_toks, lps)
                 choice["token_ids"] = toks
                 choices.append(choice)
             return {"id": rid, "object": obj, "created": created, "model": served_model_name,
@@ -236,6 +256,7 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
             pumps = [asyncio.ensure_future(pump(i, out)) for i, (_, out) in enumerate(runs)]
             detoks = [IncrementalDecoder(tokenizer) for _ in runs]
             offsets = [0] * len(runs)  # text offsets of the completions logprobs
+            echoed = [not echo] * len(runs)
             matchers = [StopMatcher(req.stop) for _ in runs]
             live = set(range(len(runs)))
             if chat:
@@ -259,6 +280,15 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
                                                                       "type": "invalid_request_error"}})
                         abort_all()
                         break
+                    if not echoed[i]:  # the prompt goes out first, once the prefill has scored it
+                        echoed[i] = True
+                        ptoks, plps = echo_part(runs[i][0])
+                        ch = {"index": i, "text": prompt_text, "finish_reason": None, "logprobs": None}
+                        if n_lp is not None:
+                            ch["logprobs"] = lp_object(ptoks, plps)
+                            offsets[i] += len(prompt_text)
+                        yield "data: %s\n\n" % json.dumps({"id": rid, "object": chunk_obj, "created": created,
+                                                            "model": served_model_name, "choices": [ch]})
                     n_out += len(new)
                     text, stopped = matchers[i].feed(detoks[i].push(new, final=fin), final=fin)
                     if stopped and not fin:  # a stop string ends this choice here

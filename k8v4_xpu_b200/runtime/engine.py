@@ -233,6 +233,11 @@ class LLMEngine:
                 raise ValueError("temperature must be >= 0, top_p in (0, 1], top_k >= 0")
             if params.logprobs is not None and not 0 <= params.logprobs <= 20:
                 raise ValueError("logprobs must lie in [0, 20]")
+            if params.prompt_logprobs is not None:
+                if not 0 <= params.prompt_logprobs <= 20:
+                    raise ValueError("prompt_logprobs must lie in [0, 20]")
+                if getattr(self, "cp", None) is not None:
+                    raise ValueError("prompt log-probabilities are not served under context parallelism")
         return self.scheduler.add(prompt, params)
 
     def has_unfinished(self) -> bool:
@@ -342,15 +347,48 @@ class LLMEngine:
             inp, rows = self._build_inputs(sched)
             hid_all = self.model.forward(inp, self.kv_caches, self.ws, all_rows=True)
             seqs = [c.seq for c in sched.chunks if c.needs_logits]
+            self._prompt_logprobs(sched, hid_all)
             tokens = self._sample(hid_all.index_select(0, inp.logit_rows), seqs) if rows else np.zeros(0, np.int64)
             self.mtp.after_prefill(sched, inp, hid_all, tokens)
         else:
             inp, rows = self._build_inputs(sched)
-            hidden = self.model.forward(inp, self.kv_caches, self.ws)
+            if any(c.is_prefill and sampling.wants_prompt_logprobs(c.seq.params) for c in sched.chunks):
+                hid_all = self.model.forward(inp, self.kv_caches, self.ws, all_rows=True)
+                self._prompt_logprobs(sched, hid_all)
+                hidden = hid_all.index_select(0, inp.logit_rows)
+            else:
+                hidden = self.model.forward(inp, self.kv_caches, self.ws)
             # a step made only of non-final prefill chunks samples nothing
             seqs = [c.seq for c in sched.chunks if c.needs_logits]
             tokens = self._sample(hidden, seqs) if rows else np.zeros(0, np.int64)
         return self._commit(sched, tokens)
+
+    def _prompt_logprobs(self, sched, hid_all: torch.Tensor, rows_per_call: int = 256) -> None:
+        """Log-probabilities of the prompt tokens in this step's prefill chunks,
+        for the requests that ask for them: row p of a chunk scores the prompt
+        token at p + 1 (``seq.prompt_logprobs[k]`` is prompt token k's entry;
+        the first token has none). Logits are made ``rows_per_call`` rows at a
+        time (under TP every rank gathers the vocabulary shards alike)."""
+        t = 0
+        for c in sched.chunks:
+            seq, n = c.seq, c.num_tokens
+            if c.is_prefill and sampling.wants_prompt_logprobs(seq.params):
+                if c.start == 0 and not seq.prompt_logprobs:
+                    seq.prompt_logprobs.append(None)
+                rows, targets = [], []
+                for j in range(n):
+                    p = c.start + j
+                    if p + 1 < len(seq.prompt) and p + 1 == len(seq.prompt_logprobs) + len(targets):
+                        rows.append(t + j)
+                        targets.append(seq.prompt[p + 1])
+                for k in range(0, len(rows), rows_per_call):
+                    idx = torch.tensor(rows[k:k + rows_per_call], dtype=torch.int64, device=self.device)
+                    lg = self.model.logits(hid_all.index_select(0, idx))
+                    if self.tp > 1:
+                        lg = self.model.comm.all_gather(lg, dim=1)
+                    seq.prompt_logprobs.extend(
+                        sampling.logprob_rows(lg, targets[k:k + rows_per_call], seq.params.prompt_logprobs))
+            t += n
 
     def _choose(self, hidden: torch.Tensor, seqs: list[Sequence] | None = None) -> torch.Tensor:
         """Next-token ids [rows] on the device: the argmax, or, when a row's

@@ -149,3 +149,21 @@ def record(engine, seq) -> None:
         seq.logprobs.append(lst.pop(0) if lst else None)
         if not lst:
             stash.pop(seq.seq_id, None)
+
+
+def wants_prompt_logprobs(params) -> bool:
+    """Whether a request asks for the log-probabilities of its prompt tokens."""
+    return params is not None and getattr(params, "prompt_logprobs", None) is not None
+
+
+def logprob_rows(logits: torch.Tensor, tokens: list[int], top_n: int) -> list[tuple]:
+    """:func:`logprob_entry` of many rows at once: row i scores ``tokens[i]``."""
+    lsm = torch.log_softmax(logits.float(), -1)
+    idx = torch.tensor(tokens, dtype=torch.int64, device=lsm.device).view(-1, 1)
+    lp = lsm.gather(1, idx).view(-1).tolist()
+    if top_n:
+        v, i = torch.topk(lsm, int(top_n), dim=-1)
+        tops = [list(zip(a, b)) for a, b in zip(i.tolist(), v.tolist())]
+    else:
+        tops = [[] for _ in tokens]
+    return list(zip(lp, tops))

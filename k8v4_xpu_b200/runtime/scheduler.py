@@ -35,6 +35,7 @@ class SamplingParams:
     top_k: int = 0            # top-k sampling (0: off)
     seed: int | None = None   # per-request generator seed (None: derived from the engine seed)
     logprobs: int | None = None  # None: off; N: each token's log-probability and the top N
+    prompt_logprobs: int | None = None  # the same for the prompt tokens (no prefix-cache hits then)
 
 
 @dataclasses.dataclass
@@ -57,6 +58,7 @@ class Sequence:
     prefill_len: int | None = None
     generator: object = None   # torch.Generator of a sampling request (runtime.sampling)
     logprobs: list = dataclasses.field(default_factory=list)  # per output token, when requested
+    prompt_logprobs: list = dataclasses.field(default_factory=list)  # per prompt token (None for the first)
 
     @property
     def tokens(self) -> "TokenView":
@@ -195,7 +197,9 @@ class Scheduler:
         are reserved now, so the later chunks of a chunked prefill never find
         the pool emptied by decoding sequences in between."""
         try:
-            cached = self.blocks.allocate(seq.seq_id, seq.tokens[:seq.prefill_target])
+            # a request for prompt log-probabilities computes every prompt row: no prefix hits
+            cached = self.blocks.allocate(seq.seq_id, seq.tokens[:seq.prefill_target],
+                                          prefix=getattr(seq.params, "prompt_logprobs", None) is None)
         except CapacityError:
             return False
         try:

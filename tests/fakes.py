@@ -42,6 +42,8 @@ class FakeEngine:
             self.blocks.publish(seq.seq_id, seq.tokens, seq.computed)
             if not c.needs_logits:
                 continue
+            if getattr(seq.params, "prompt_logprobs", None) is not None and not seq.prompt_logprobs:
+                seq.prompt_logprobs = [None] + [(-1.0, [])] * (len(seq.prompt) - 1)  # made up
             tok = (seq.tokens[-1] + 1) % self.vocab
             if seq.first_token_time is None:
                 seq.first_token_time = now

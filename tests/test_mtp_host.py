@@ -171,3 +171,37 @@ def test_logprobs_of_every_emitted_token_with_and_without_mtp():
             assert [t for t, _ in top] == [(7 * prev + 3) % V, (7 * prev + 4) % V]
             prev = tok
         assert not eng.__dict__.get("_lp_next")  # nothing left waiting
+
+
+def test_prompt_logprobs_over_chunked_prefill_without_prefix_hits():
+    """Prompt log-probabilities: entry k scores prompt token k given the
+    ones before it (none for the first), across prefill chunks, with and
+    without MTP; such a request takes no prefix-cache hit."""
+    for mtp in (True, False):
+        eng = _engine()
+        eng.blocks = BlockManager(96, block_size=16, page=16, enable_prefix_caching=True)
+        if mtp:
+            eng.scheduler = Scheduler(eng.blocks, max_num_seqs=2, max_num_batched_tokens=24, decode_width=7,
+                                      max_model_len=1024, lookahead=7, mix_prefill_with_decode=False,
+                                      prefill_slice=16)
+        else:
+            eng.mtp = None
+            eng.scheduler = Scheduler(eng.blocks, max_num_seqs=2, max_num_batched_tokens=24, decode_width=1,
+                                      max_model_len=1024)
+        prompt = [int(x) for x in torch.randint(0, V, (53,), generator=torch.Generator().manual_seed(5))]
+        first = eng.add_request(prompt, SamplingParams(max_tokens=3, ignore_eos=True))
+        while eng.has_unfinished():
+            eng.step()
+        s = eng.add_request(prompt, SamplingParams(max_tokens=3, ignore_eos=True, prompt_logprobs=2))
+        while eng.has_unfinished():
+            eng.step()
+        assert first.output and s.cached_tokens == 0
+        again = eng.add_request(prompt, SamplingParams(max_tokens=3, ignore_eos=True))
+        while eng.has_unfinished():
+            eng.step()
+        assert again.cached_tokens > 0  # the cache holds the prompt: only the logprob request skipped it
+        assert len(s.prompt_logprobs) == len(prompt) and s.prompt_logprobs[0] is None
+        for k in range(1, len(prompt)):
+            lp, top = s.prompt_logprobs[k]
+            assert abs(lp - _lp_ref(prompt[k - 1], prompt[k])) < 1e-4
+            assert [t for t, _ in top] == [(7 * prompt[k - 1] + 3) % V, (7 * prompt[k - 1] + 4) % V]

@@ -343,3 +343,25 @@ def test_logprobs_in_completions_and_chat(client):
     assert all(x == {} for g in got for x in g["top_logprobs"])  # logprobs 0: no top list
     for bad in ({"logprobs": 21}, {"logprobs": -1}):
         assert c.post("/v1/completions", json={"prompt": [a], "max_tokens": 2, **bad}).status_code == 400
+
+
+def test_echo_returns_the_prompt_and_its_logprobs(client):
+    c, eng, _ = client
+    a = ord("a") + 3
+    prompt = [a, a + 1]  # "ab"
+    r = c.post("/v1/completions", json={"prompt": prompt, "max_tokens": 2, "ignore_eos": True, "echo": True}).json()
+    assert r["choices"][0]["text"] == "abcd" and r["usage"]["completion_tokens"] == 2
+    r = c.post("/v1/completions", json={"prompt": prompt, "max_tokens": 1, "ignore_eos": True, "echo": True,
+                                        "logprobs": 1}).json()
+    lp = r["choices"][0]["logprobs"]
+    assert lp["tokens"] == ["a", "b", "c"] and lp["token_logprobs"] == [None, -1.0, -0.5]
+    assert lp["text_offset"] == [0, 1, 2]
+    chunks = []
+    with c.stream("POST", "/v1/completions", json={"prompt": prompt, "max_tokens": 2, "ignore_eos": True,
+                                                   "echo": True, "logprobs": 0, "stream": True}) as s:
+        for line in s.iter_lines():
+            if line.startswith("data: ") and line != "data: [DONE]":
+                chunks.append(json.loads(line[6:])["choices"][0])
+    assert "".join(ch["text"] for ch in chunks) == "abcd"
+    assert [t for ch in chunks if ch.get("logprobs") for t in ch["logprobs"]["token_logprobs"]] == \
+        [None, -1.0, -0.5, -0.5]
