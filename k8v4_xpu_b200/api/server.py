@@ -85,7 +85,9 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
     def params_for(req: _Common, prompt_len: int) -> SamplingParams:
         mt = req.max_completion_tokens if req.max_completion_tokens is not None else req.max_tokens
         mt = 16 if mt is None else mt  # an explicit 0 is refused below, not defaulted
-        if mt < 1:
+        if mt == 0 and getattr(req, "echo", False):
+            mt = 1  # echo only (prompt scoring): one token is generated and dropped
+        elif mt < 1:
             raise HTTPException(400, "max_tokens must be positive")
         if prompt_len < 1:
             raise HTTPException(400, "empty prompt")
@@ -140,6 +142,10 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
                 raise HTTPException(400, "logprobs / top_logprobs must lie in [0, 20]")
             params = dataclasses.replace(params, logprobs=n_lp)
         echo = bool(getattr(req, "echo", False))
+        echo_only = echo and (req.max_completion_tokens if req.max_completion_tokens is not None
+                              else req.max_tokens) == 0
+        if echo_only and req.stream:
+            raise HTTPException(400, "max_tokens 0 with echo (prompt scoring) is served without streaming")
         if echo and n_lp is not None:
             params = dataclasses.replace(params, prompt_logprobs=n_lp)
         prompt_text = tokenizer.decode(prompt) if echo else ""
@@ -225,6 +231,8 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
                 if reason and reason.startswith("rejected: "):
                     raise HTTPException(400, reason[len("rejected: "):])
             choices = []
+            if echo_only:  # prompt scoring: the one generated token is dropped
+                results = [([], "", "length", []) for _ in results]
             for i, (toks, text, reason, lps) in enumerate(results):
                 if echo:
                     ptoks, plps = echo_part(runs[i][0])

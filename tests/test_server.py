@@ -365,3 +365,18 @@ def test_echo_returns_the_prompt_and_its_logprobs(client):
     assert "".join(ch["text"] for ch in chunks) == "abcd"
     assert [t for ch in chunks if ch.get("logprobs") for t in ch["logprobs"]["token_logprobs"]] == \
         [None, -1.0, -0.5, -0.5]
+
+
+def test_prompt_scoring_with_echo_and_no_new_tokens(client):
+    """``echo`` with ``max_tokens`` 0 (how evaluation harnesses score a
+    prompt): the prompt and its log-probabilities, no completion tokens."""
+    c, eng, _ = client
+    a = ord("a") + 3
+    r = c.post("/v1/completions", json={"prompt": [a, a + 1, a + 2], "max_tokens": 0, "echo": True,
+                                        "logprobs": 1}).json()
+    ch = r["choices"][0]
+    assert ch["text"] == "abc" and ch["logprobs"]["token_logprobs"] == [None, -1.0, -1.0]
+    assert r["usage"]["completion_tokens"] == 0 and ch["token_ids"] == []
+    assert c.post("/v1/completions", json={"prompt": [a], "max_tokens": 0}).status_code == 400
+    assert c.post("/v1/completions", json={"prompt": [a], "max_tokens": 0, "echo": True,
+                                           "stream": True}).status_code == 400
