@@ -2,7 +2,8 @@
 
 Endpoints: ``POST /v1/chat/completions`` and ``POST /v1/completions``
 (streaming as server-sent events, ``stream_options.include_usage`` and
-``continuous_usage_stats``), ``GET /v1/models``, ``GET /health`` and
+``continuous_usage_stats``), ``GET /v1/models``, ``GET /health`` (``/ping``), ``GET /version``,
+``POST /tokenize``, ``POST /detokenize`` and
 ``GET /metrics`` (Prometheus, ``vllm:*`` names). This is the surface the
 reference's clients use against stock vLLM (``bench/serve_coding.py:27-45``,
 ``launch.sh:219-232``). A request without ``temperature`` (or with 0)
@@ -74,6 +75,17 @@ class ChatRequest(_Common):
     messages: list[ChatMessage]
 
 
+class TokenizeRequest(BaseModel):
+    model: str | None = None
+    prompt: str | None = None
+    messages: list[ChatMessage] | None = None
+
+
+class DetokenizeRequest(BaseModel):
+    model: str | None = None
+    tokens: list[int]
+
+
 def _usage(prompt: int, completion: int) -> dict:
     return {"prompt_tokens": prompt, "completion_tokens": completion, "total_tokens": prompt + completion}
 
@@ -118,6 +130,28 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
             return JSONResponse({"status": "error", "detail": (driver.error or "engine stopped")[-2000:]},
                                 status_code=503)
         return {"status": "ok"}
+
+    @app.get("/ping")
+    async def ping():
+        return await health()
+
+    @app.get("/version")
+    async def version():
+        from .. import __version__
+        return {"version": __version__}
+
+    @app.post("/tokenize")
+    async def tokenize(req: TokenizeRequest):
+        """Token ids of a prompt, or of chat messages through the chat template."""
+        if (req.prompt is None) == (req.messages is None):
+            raise HTTPException(400, "give either prompt or messages")
+        ids = (tokenizer.encode(req.prompt) if req.prompt is not None
+               else tokenizer.apply_chat_template([m.model_dump() for m in req.messages]))
+        return {"tokens": ids, "count": len(ids), "max_model_len": max_model_len}
+
+    @app.post("/detokenize")
+    async def detokenize(req: DetokenizeRequest):
+        return {"prompt": tokenizer.decode(req.tokens)}
 
     @app.get("/v1/models")
     async def models():

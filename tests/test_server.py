@@ -380,3 +380,15 @@ def test_prompt_scoring_with_echo_and_no_new_tokens(client):
     assert c.post("/v1/completions", json={"prompt": [a], "max_tokens": 0}).status_code == 400
     assert c.post("/v1/completions", json={"prompt": [a], "max_tokens": 0, "echo": True,
                                            "stream": True}).status_code == 400
+
+
+def test_tokenize_detokenize_ping_version(client):
+    c, _, _ = client
+    r = c.post("/tokenize", json={"prompt": "ab"}).json()
+    assert r["tokens"] == [ord("a") + 3, ord("b") + 3] and r["count"] == 2 and r["max_model_len"] == 512
+    r = c.post("/tokenize", json={"messages": [{"role": "user", "content": "hi"}]}).json()
+    assert r["count"] > 2
+    assert c.post("/tokenize", json={}).status_code == 400
+    assert c.post("/detokenize", json={"tokens": [ord("a") + 3, ord("b") + 3]}).json() == {"prompt": "ab"}
+    assert c.get("/ping").json() == {"status": "ok"}
+    assert c.get("/version").json()["version"]
