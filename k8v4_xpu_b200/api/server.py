@@ -8,7 +8,8 @@ Endpoints: ``POST /v1/chat/completions`` and ``POST /v1/completions``
 reference's clients use against stock vLLM (``bench/serve_coding.py:27-45``,
 ``launch.sh:219-232``). A request without ``temperature`` (or with 0)
 decodes greedily, the benchmark path of the reference; ``temperature`` > 0
-samples, with ``top_p``, ``top_k`` (0 or -1: off) and ``seed``
+samples, with ``top_p``, ``top_k`` (0 or -1: off) and ``seed``; the
+repetition, presence and frequency penalties apply to either
 (``runtime.sampling``; under MTP the drafts are verified by speculative
 sampling). Stop
 strings (``stop``) end a request before the first match, in streamed and
@@ -58,6 +59,9 @@ class _Common(BaseModel):
     top_p: float | None = None
     top_k: int | None = None
     seed: int | None = None
+    repetition_penalty: float | None = None
+    presence_penalty: float | None = None
+    frequency_penalty: float | None = None
     n: int = 1
 
 
@@ -112,8 +116,14 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
         top_k = 0 if req.top_k is None or req.top_k == -1 else int(req.top_k)
         if temperature < 0 or not 0.0 < top_p <= 1.0 or top_k < 0:
             raise HTTPException(400, "temperature must be >= 0, top_p in (0, 1], top_k >= 0 or -1")
+        rep = 1.0 if req.repetition_penalty is None else float(req.repetition_penalty)
+        pres = float(req.presence_penalty or 0.0)
+        freq = float(req.frequency_penalty or 0.0)
+        if rep <= 0 or not -2.0 <= pres <= 2.0 or not -2.0 <= freq <= 2.0:
+            raise HTTPException(400, "repetition_penalty must be > 0; presence / frequency penalties in [-2, 2]")
         return SamplingParams(max_tokens=mt, ignore_eos=req.ignore_eos, stop_token_ids=stops,
-                              temperature=temperature, top_p=top_p, top_k=top_k, seed=req.seed)
+                              temperature=temperature, top_p=top_p, top_k=top_k, seed=req.seed,
+                              repetition_penalty=rep, presence_penalty=pres, frequency_penalty=freq)
 
     async def run(prompt: list[int], params: SamplingParams):
         loop = asyncio.get_running_loop()

@@ -233,6 +233,9 @@ class LLMEngine:
                 raise ValueError("temperature must be >= 0, top_p in (0, 1], top_k >= 0")
             if params.logprobs is not None and not 0 <= params.logprobs <= 20:
                 raise ValueError("logprobs must lie in [0, 20]")
+            if params.repetition_penalty <= 0 or not -2.0 <= params.presence_penalty <= 2.0 \
+                    or not -2.0 <= params.frequency_penalty <= 2.0:
+                raise ValueError("repetition_penalty must be > 0; presence / frequency penalties in [-2, 2]")
             if params.prompt_logprobs is not None:
                 if not 0 <= params.prompt_logprobs <= 20:
                     raise ValueError("prompt_logprobs must lie in [0, 20]")
@@ -401,7 +404,13 @@ class LLMEngine:
             lg = self.model.comm.all_gather(lg, dim=1)
         gens = [sampling.generator_for(s, self.cfg.seed, self.device) if sampling.samples(s.params) else None
                 for s in seqs]
-        ids = sampling.sample_rows(lg, [s.params for s in seqs], gens)
+        pick = lg
+        if any(sampling.has_penalties(s.params) for s in seqs):
+            pick = lg.float().clone()
+            for i, s in enumerate(seqs):
+                if sampling.has_penalties(s.params):
+                    pick[i] = sampling.apply_penalties(lg[i], s.prompt, s.output, s.params)
+        ids = sampling.sample_rows(pick, [s.params for s in seqs], gens)
         if any(sampling.wants_logprobs(s.params) for s in seqs):
             host = ids.tolist()
             stash = sampling.stash_of(self)

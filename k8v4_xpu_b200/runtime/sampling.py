@@ -119,8 +119,9 @@ def wants_logprobs(params) -> bool:
 
 def needs_logits(params) -> bool:
     """Requests whose steps need the full-vocabulary logits (so they run
-    eagerly): sampling ones and the ones asking for log-probabilities."""
-    return samples(params) or wants_logprobs(params)
+    eagerly): sampling ones, the ones asking for log-probabilities and the
+    ones with penalties."""
+    return samples(params) or wants_logprobs(params) or has_penalties(params)
 
 
 def logprob_entry(row_logits: torch.Tensor, token: int, top_n: int) -> tuple:
@@ -167,3 +168,35 @@ def logprob_rows(logits: torch.Tensor, tokens: list[int], top_n: int) -> list[tu
     else:
         tops = [[] for _ in tokens]
     return list(zip(lp, tops))
+
+
+def has_penalties(params) -> bool:
+    """Whether a request asks for repetition / presence / frequency penalties."""
+    return params is not None and (float(getattr(params, "repetition_penalty", 1.0)) != 1.0
+                                   or float(getattr(params, "presence_penalty", 0.0)) != 0.0
+                                   or float(getattr(params, "frequency_penalty", 0.0)) != 0.0)
+
+
+def apply_penalties(row: torch.Tensor, prompt: list[int], output: list[int], p) -> torch.Tensor:
+    """Penalized fp32 logits of one row, as vLLM defines the penalties:
+    ``repetition_penalty`` r divides a positive logit (multiplies a negative
+    one) of every token seen in the prompt or the output; ``presence_penalty``
+    subtracts a constant from tokens the output holds, ``frequency_penalty``
+    that constant times how often the output holds them."""
+    x = row.float().clone()
+    V = x.shape[-1]
+    dev = x.device
+    out = torch.tensor(output, dtype=torch.int64, device=dev) if output else None
+    r = float(getattr(p, "repetition_penalty", 1.0))
+    if r != 1.0:
+        seen = torch.zeros(V, dtype=torch.bool, device=dev)
+        if prompt:
+            seen[torch.tensor(prompt, dtype=torch.int64, device=dev)] = True
+        if out is not None:
+            seen[out] = True
+        x = torch.where(seen, torch.where(x > 0, x / r, x * r), x)
+    if out is not None:
+        counts = torch.bincount(out, minlength=V).to(x.dtype)
+        x = x - float(getattr(p, "frequency_penalty", 0.0)) * counts \
+            - float(getattr(p, "presence_penalty", 0.0)) * (counts > 0).to(x.dtype)
+    return x

@@ -36,6 +36,9 @@ class SamplingParams:
     seed: int | None = None   # per-request generator seed (None: derived from the engine seed)
     logprobs: int | None = None  # None: off; N: each token's log-probability and the top N
     prompt_logprobs: int | None = None  # the same for the prompt tokens (no prefix-cache hits then)
+    repetition_penalty: float = 1.0   # vLLM's penalties (1 / 0: off)
+    presence_penalty: float = 0.0
+    frequency_penalty: float = 0.0
 
 
 @dataclasses.dataclass

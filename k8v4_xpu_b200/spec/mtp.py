@@ -204,13 +204,22 @@ class MTPSpeculator:
         if self.eng.tp > 1:
             lg = m.comm.all_gather(lg, dim=1)
         lg = lg.reshape(B, w, -1)  # the lm_head may return a view over padded vocab rows
-        t = torch.argmax(lg.float(), dim=-1)
+        pick = lg
+        if any(sampling.has_penalties(s.params) for s in seqs):
+            # row j follows the committed output and drafts 1..j
+            pick = lg.float().clone()
+            for i, s in enumerate(seqs):
+                if sampling.has_penalties(s.params):
+                    dj = d[i].tolist()
+                    for j in range(w):
+                        pick[i, j] = sampling.apply_penalties(lg[i, j], s.prompt, list(s.output) + dj[:j], s.params)
+        t = torch.argmax(pick.float(), dim=-1)
         a = (d == t[:, :-1]).to(torch.int64).cumprod(1).sum(1)
         stash = sampling.stash_of(self.eng)
         for i, s in enumerate(seqs):
             if samples(s.params):
                 g = generator_for(s, self.eng.cfg.seed, self.eng.device)
-                ai, x = speculative_sample(lg[i], d[i], s.params, g)
+                ai, x = speculative_sample(pick[i], d[i], s.params, g)
                 a[i] = ai
                 t[i, ai] = x
             if sampling.wants_logprobs(s.params):  # one entry per token the commit will emit

@@ -205,3 +205,29 @@ def test_prompt_logprobs_over_chunked_prefill_without_prefix_hits():
             lp, top = s.prompt_logprobs[k]
             assert abs(lp - _lp_ref(prompt[k - 1], prompt[k])) < 1e-4
             assert [t for t, _ in top] == [(7 * prompt[k - 1] + 3) % V, (7 * prompt[k - 1] + 4) % V]
+
+
+def test_repetition_penalty_steers_greedy_tokens_with_and_without_mtp():
+    """The stand-in target prefers 7x + 3, then 7x + 4. With the preferred
+    token already in the prompt and repetition_penalty 2 (its logit 30 -> 15),
+    the greedy choice moves to 7x + 4; plain steps and MTP verify agree."""
+    for mtp in (True, False):
+        eng = _engine()
+        if not mtp:
+            eng.mtp = None
+            eng.scheduler = Scheduler(eng.blocks, max_num_seqs=2, max_num_batched_tokens=24, decode_width=1,
+                                      max_model_len=1024)
+        last = 40
+        prompt = [(7 * last + 3) % V, 11, last]
+        s = eng.add_request(prompt, SamplingParams(max_tokens=6, ignore_eos=True, repetition_penalty=2.0))
+        g = eng.add_request(prompt, SamplingParams(max_tokens=6, ignore_eos=True))
+        while eng.has_unfinished():
+            eng.step()
+        assert g.output[0] == (7 * last + 3) % V
+        assert s.output[0] == (7 * last + 4) % V
+        seen, prev = set(prompt), last
+        for tok in s.output:  # every step: the best-scored token not yet seen
+            want = next((7 * prev + off) % V for off in (3, 4, 5) if (7 * prev + off) % V not in seen)
+            assert tok == want
+            seen.add(tok)
+            prev = tok

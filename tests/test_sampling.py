@@ -232,3 +232,15 @@ def test_mtp_accept_mixes_greedy_and_sampling_sequences():
     assert 0 <= int(a[1]) <= 3 and torch.equal(t[1, :int(a[1])], ids[1, 1:1 + int(a[1])])
     tg, ag = spec._accept(hid, ids, B, [Sequence(0, [1], SamplingParams())] * 2)  # no sampling: argmax kernel path
     assert torch.equal(tg, greedy) and int(ag[1]) == 3
+
+
+def test_penalties_follow_vllm_definitions():
+    row = torch.tensor([2.0, -2.0, 1.0, 0.5, -1.0])
+    p = SamplingParams(repetition_penalty=2.0)
+    got = sampling.apply_penalties(row, [0], [1], p)         # tokens 0 (prompt) and 1 (output) seen
+    assert torch.allclose(got, torch.tensor([1.0, -4.0, 1.0, 0.5, -1.0]))
+    p = SamplingParams(presence_penalty=0.5, frequency_penalty=0.25)
+    got = sampling.apply_penalties(row, [2], [3, 3, 4], p)   # the prompt takes no presence / frequency penalty
+    assert torch.allclose(got, torch.tensor([2.0, -2.0, 1.0, 0.5 - 0.5 - 0.5, -1.0 - 0.5 - 0.25]))
+    assert not sampling.has_penalties(SamplingParams()) and sampling.has_penalties(p)
+    assert sampling.needs_logits(p)
