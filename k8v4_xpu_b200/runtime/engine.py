@@ -394,9 +394,11 @@ class LLMEngine:
             t += n
 
     def _choose(self, hidden: torch.Tensor, seqs: list[Sequence] | None = None) -> torch.Tensor:
-        """Next-token ids [rows] on the device: the argmax, or, when a row's
-        request samples, a draw from its full-vocabulary logits (the TP
-        shards gathered on every rank; ``runtime.sampling``)."""
+        """Next-token ids [rows] on the device: the argmax kernel, or, when a
+        row's request samples, asks for log-probabilities or sets penalties,
+        the full-vocabulary logits (the TP shards gathered on every rank),
+        penalized, then the argmax or a seeded draw; log-probability entries
+        wait in the engine's stash for the commit (``runtime.sampling``)."""
         if not seqs or not any(sampling.needs_logits(s.params) for s in seqs):
             return self.model.greedy(hidden)
         lg = self.model.logits(hidden)
@@ -409,7 +411,7 @@ class LLMEngine:
             pick = lg.float().clone()
             for i, s in enumerate(seqs):
                 if sampling.has_penalties(s.params):
-                    pick[i] = sampling.apply_penalties(lg[i], s.prompt, s.output, s.params)
+                    pick[i] = sampling.apply_penalties(lg[i], s.prompt, s.output, s.params, holder=s)
         ids = sampling.sample_rows(pick, [s.params for s in seqs], gens)
         if any(sampling.wants_logprobs(s.params) for s in seqs):
             host = ids.tolist()

@@ -177,21 +177,35 @@ def has_penalties(params) -> bool:
                                    or float(getattr(params, "frequency_penalty", 0.0)) != 0.0)
 
 
-def apply_penalties(row: torch.Tensor, prompt: list[int], output: list[int], p) -> torch.Tensor:
+def _prompt_mask(prompt, V: int, dev, holder=None) -> torch.Tensor:
+    """Tokens of the prompt as a [V] bool mask, kept on ``holder`` (the
+    sequence) so that a long prompt is turned into a mask once."""
+    key = (V, str(dev))
+    cached = getattr(holder, "_prompt_mask", None) if holder is not None else None
+    if cached is not None and cached[0] == key:
+        return cached[1]
+    seen = torch.zeros(V, dtype=torch.bool, device=dev)
+    if len(prompt):
+        seen[torch.tensor(list(prompt), dtype=torch.int64, device=dev)] = True
+    if holder is not None:
+        holder._prompt_mask = (key, seen)
+    return seen
+
+
+def apply_penalties(row: torch.Tensor, prompt, output: list[int], p, holder=None) -> torch.Tensor:
     """Penalized fp32 logits of one row, as vLLM defines the penalties:
     ``repetition_penalty`` r divides a positive logit (multiplies a negative
     one) of every token seen in the prompt or the output; ``presence_penalty``
     subtracts a constant from tokens the output holds, ``frequency_penalty``
-    that constant times how often the output holds them."""
+    that constant times how often the output holds them. ``holder`` (the
+    sequence) keeps the prompt's token mask between steps."""
     x = row.float().clone()
     V = x.shape[-1]
     dev = x.device
     out = torch.tensor(output, dtype=torch.int64, device=dev) if output else None
     r = float(getattr(p, "repetition_penalty", 1.0))
     if r != 1.0:
-        seen = torch.zeros(V, dtype=torch.bool, device=dev)
-        if prompt:
-            seen[torch.tensor(prompt, dtype=torch.int64, device=dev)] = True
+        seen = _prompt_mask(prompt, V, dev, holder).clone()
         if out is not None:
             seen[out] = True
         x = torch.where(seen, torch.where(x > 0, x / r, x * r), x)

@@ -212,7 +212,8 @@ class MTPSpeculator:
                 if sampling.has_penalties(s.params):
                     dj = d[i].tolist()
                     for j in range(w):
-                        pick[i, j] = sampling.apply_penalties(lg[i, j], s.prompt, list(s.output) + dj[:j], s.params)
+                        pick[i, j] = sampling.apply_penalties(lg[i, j], s.prompt, list(s.output) + dj[:j],
+                                                              s.params, holder=s)
         t = torch.argmax(pick.float(), dim=-1)
         a = (d == t[:, :-1]).to(torch.int64).cumprod(1).sum(1)
         stash = sampling.stash_of(self.eng)
