@@ -8,8 +8,9 @@ Endpoints: ``POST /v1/chat/completions`` and ``POST /v1/completions``
 reference's clients use against stock vLLM (``bench/serve_coding.py:27-45``,
 ``launch.sh:219-232``). A request without ``temperature`` (or with 0)
 decodes greedily, the benchmark path of the reference; ``temperature`` > 0
-samples, with ``top_p``, ``top_k`` (0 or -1: off) and ``seed``; the
-repetition, presence and frequency penalties apply to either
+samples, with ``top_p``, ``top_k`` (0 or -1: off), ``min_p`` and ``seed``;
+the repetition, presence and frequency penalties, ``logit_bias`` and
+``min_tokens`` apply to either
 (``runtime.sampling``; under MTP the drafts are verified by speculative
 sampling). Stop
 strings (``stop``) end a request before the first match, in streamed and
@@ -59,6 +60,9 @@ class _Common(BaseModel):
     top_p: float | None = None
     top_k: int | None = None
     seed: int | None = None
+    min_p: float | None = None
+    logit_bias: dict[str, float] | None = None
+    min_tokens: int | None = None
     repetition_penalty: float | None = None
     presence_penalty: float | None = None
     frequency_penalty: float | None = None
@@ -121,9 +125,18 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
         freq = float(req.frequency_penalty or 0.0)
         if rep <= 0 or not -2.0 <= pres <= 2.0 or not -2.0 <= freq <= 2.0:
             raise HTTPException(400, "repetition_penalty must be > 0; presence / frequency penalties in [-2, 2]")
+        min_p = float(req.min_p or 0.0)
+        min_tokens = int(req.min_tokens or 0)
+        try:
+            bias = {int(t): float(v) for t, v in (req.logit_bias or {}).items()}
+        except ValueError:
+            raise HTTPException(400, "logit_bias maps token ids to numbers")
+        if not 0.0 <= min_p <= 1.0 or not 0 <= min_tokens <= mt or any(not -100 <= v <= 100 for v in bias.values()):
+            raise HTTPException(400, "min_p in [0, 1], min_tokens in [0, max_tokens], logit_bias values in [-100, 100]")
         return SamplingParams(max_tokens=mt, ignore_eos=req.ignore_eos, stop_token_ids=stops,
                               temperature=temperature, top_p=top_p, top_k=top_k, seed=req.seed,
-                              repetition_penalty=rep, presence_penalty=pres, frequency_penalty=freq)
+                              repetition_penalty=rep, presence_penalty=pres, frequency_penalty=freq,
+                              min_p=min_p, logit_bias=bias or None, min_tokens=min_tokens)
 
     async def run(prompt: list[int], params: SamplingParams):
         loop = asyncio.get_running_loop()

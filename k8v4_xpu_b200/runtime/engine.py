@@ -407,11 +407,11 @@ class LLMEngine:
         gens = [sampling.generator_for(s, self.cfg.seed, self.device) if sampling.samples(s.params) else None
                 for s in seqs]
         pick = lg
-        if any(sampling.has_penalties(s.params) for s in seqs):
+        if any(sampling.has_processors(s.params) for s in seqs):
             pick = lg.float().clone()
             for i, s in enumerate(seqs):
-                if sampling.has_penalties(s.params):
-                    pick[i] = sampling.apply_penalties(lg[i], s.prompt, s.output, s.params, holder=s)
+                if sampling.has_processors(s.params):
+                    pick[i] = sampling.process_row(lg[i], s.prompt, s.output, s.params, holder=s)
         ids = sampling.sample_rows(pick, [s.params for s in seqs], gens)
         if any(sampling.wants_logprobs(s.params) for s in seqs):
             host = ids.tolist()

@@ -39,11 +39,15 @@ def generator_for(seq, engine_seed: int, device) -> torch.Generator:
     return g
 
 
-def filter_logits(x: torch.Tensor, top_k: int, top_p: float) -> torch.Tensor:
+def filter_logits(x: torch.Tensor, top_k: int, top_p: float, min_p: float = 0.0) -> torch.Tensor:
     """One row of fp32 logits (already divided by the temperature) with the
-    tokens outside the top-k and outside the top-p nucleus set to -inf. The
-    most likely token always stays."""
+    tokens outside the top-k, outside the top-p nucleus, and below ``min_p``
+    times the most likely token's probability set to -inf. The most likely
+    token always stays."""
     V = x.shape[-1]
+    if 0.0 < min_p <= 1.0:
+        p = torch.softmax(x, -1)
+        x = torch.where(p < min_p * p.max(), torch.full_like(x, float("-inf")), x)
     if 0 < top_k < V:
         kth = torch.topk(x, top_k).values[-1]
         x = torch.where(x < kth, torch.full_like(x, float("-inf")), x)
@@ -67,8 +71,7 @@ def sample_rows(logits: torch.Tensor, params: list, gens: list) -> torch.Tensor:
     for i, (p, g) in enumerate(zip(params, gens)):
         if not samples(p):
             continue
-        x = filter_logits(lg[i] / float(p.temperature), int(p.top_k or 0), float(p.top_p if p.top_p else 1.0))
-        probs = torch.softmax(x, -1)
+        probs = torch.softmax(_filtered(lg[i], p), -1)
         out[i] = torch.multinomial(probs, 1, generator=g)[0]
     return out
 
@@ -76,10 +79,13 @@ def sample_rows(logits: torch.Tensor, params: list, gens: list) -> torch.Tensor:
 def probs_rows(logits: torch.Tensor, p) -> torch.Tensor:
     """Sampling distribution [R, V] (fp32) of the rows of ``logits`` under one
     request's temperature, top-k and top-p."""
-    lg = logits.float() / float(p.temperature)
-    rows = [torch.softmax(filter_logits(lg[j], int(p.top_k or 0), float(p.top_p if p.top_p else 1.0)), -1)
-            for j in range(lg.shape[0])]
-    return torch.stack(rows)
+    lg = logits.float()
+    return torch.stack([torch.softmax(_filtered(lg[j], p), -1) for j in range(lg.shape[0])])
+
+
+def _filtered(row: torch.Tensor, p) -> torch.Tensor:
+    return filter_logits(row / float(p.temperature), int(p.top_k or 0), float(p.top_p if p.top_p else 1.0),
+                         float(getattr(p, "min_p", 0.0) or 0.0))
 
 
 def speculative_sample(logits: torch.Tensor, drafts: torch.Tensor, p, gen: torch.Generator) -> tuple[int, int]:
@@ -121,7 +127,7 @@ def needs_logits(params) -> bool:
     """Requests whose steps need the full-vocabulary logits (so they run
     eagerly): sampling ones, the ones asking for log-probabilities and the
     ones with penalties."""
-    return samples(params) or wants_logprobs(params) or has_penalties(params)
+    return samples(params) or wants_logprobs(params) or has_processors(params)
 
 
 def logprob_entry(row_logits: torch.Tensor, token: int, top_n: int) -> tuple:
@@ -170,11 +176,15 @@ def logprob_rows(logits: torch.Tensor, tokens: list[int], top_n: int) -> list[tu
     return list(zip(lp, tops))
 
 
-def has_penalties(params) -> bool:
-    """Whether a request asks for repetition / presence / frequency penalties."""
+def has_processors(params) -> bool:
+    """Whether a request changes its logits before the choice: repetition /
+    presence / frequency penalties, a logit bias, or a minimum length that
+    holds back its stop tokens."""
     return params is not None and (float(getattr(params, "repetition_penalty", 1.0)) != 1.0
                                    or float(getattr(params, "presence_penalty", 0.0)) != 0.0
-                                   or float(getattr(params, "frequency_penalty", 0.0)) != 0.0)
+                                   or float(getattr(params, "frequency_penalty", 0.0)) != 0.0
+                                   or bool(getattr(params, "logit_bias", None))
+                                   or int(getattr(params, "min_tokens", 0) or 0) > 0)
 
 
 def _prompt_mask(prompt, V: int, dev, holder=None) -> torch.Tensor:
@@ -192,13 +202,15 @@ def _prompt_mask(prompt, V: int, dev, holder=None) -> torch.Tensor:
     return seen
 
 
-def apply_penalties(row: torch.Tensor, prompt, output: list[int], p, holder=None) -> torch.Tensor:
-    """Penalized fp32 logits of one row, as vLLM defines the penalties:
+def process_row(row: torch.Tensor, prompt, output: list[int], p, holder=None) -> torch.Tensor:
+    """Processed fp32 logits of one row, as vLLM defines the processors:
     ``repetition_penalty`` r divides a positive logit (multiplies a negative
     one) of every token seen in the prompt or the output; ``presence_penalty``
     subtracts a constant from tokens the output holds, ``frequency_penalty``
-    that constant times how often the output holds them. ``holder`` (the
-    sequence) keeps the prompt's token mask between steps."""
+    that constant times how often the output holds them; ``logit_bias`` adds
+    its value to its token; while the output is shorter than ``min_tokens``
+    the stop tokens are held back (-inf). ``holder`` (the sequence) keeps the
+    prompt's token mask between steps."""
     x = row.float().clone()
     V = x.shape[-1]
     dev = x.device
@@ -210,7 +222,15 @@ def apply_penalties(row: torch.Tensor, prompt, output: list[int], p, holder=None
             seen[out] = True
         x = torch.where(seen, torch.where(x > 0, x / r, x * r), x)
     if out is not None:
-        counts = torch.bincount(out, minlength=V).to(x.dtype)
+        counts = torch.bincount(out, minlength=V)[:V].to(x.dtype)
         x = x - float(getattr(p, "frequency_penalty", 0.0)) * counts \
             - float(getattr(p, "presence_penalty", 0.0)) * (counts > 0).to(x.dtype)
+    bias = [(int(t), float(v)) for t, v in (getattr(p, "logit_bias", None) or {}).items() if 0 <= int(t) < V]
+    if bias:
+        ids = torch.tensor([t for t, _ in bias], dtype=torch.int64, device=dev)
+        x[ids] += torch.tensor([v for _, v in bias], dtype=x.dtype, device=dev)
+    if len(output) < int(getattr(p, "min_tokens", 0) or 0) and p.stop_token_ids:
+        stops = [int(t) for t in p.stop_token_ids if 0 <= int(t) < V]
+        if stops:
+            x[torch.tensor(stops, dtype=torch.int64, device=dev)] = float("-inf")
     return x

@@ -39,6 +39,9 @@ class SamplingParams:
     repetition_penalty: float = 1.0   # vLLM's penalties (1 / 0: off)
     presence_penalty: float = 0.0
     frequency_penalty: float = 0.0
+    min_p: float = 0.0          # drop tokens below min_p x the top probability (0: off)
+    logit_bias: dict | None = None  # token id -> bias added to its logit
+    min_tokens: int = 0         # stop tokens are held back until the output is this long
 
 
 @dataclasses.dataclass

@@ -205,14 +205,14 @@ class MTPSpeculator:
             lg = m.comm.all_gather(lg, dim=1)
         lg = lg.reshape(B, w, -1)  # the lm_head may return a view over padded vocab rows
         pick = lg
-        if any(sampling.has_penalties(s.params) for s in seqs):
+        if any(sampling.has_processors(s.params) for s in seqs):
             # row j follows the committed output and drafts 1..j
             pick = lg.float().clone()
             for i, s in enumerate(seqs):
-                if sampling.has_penalties(s.params):
+                if sampling.has_processors(s.params):
                     dj = d[i].tolist()
                     for j in range(w):
-                        pick[i, j] = sampling.apply_penalties(lg[i, j], s.prompt, list(s.output) + dj[:j],
+                        pick[i, j] = sampling.process_row(lg[i, j], s.prompt, list(s.output) + dj[:j],
                                                               s.params, holder=s)
         t = torch.argmax(pick.float(), dim=-1)
         a = (d == t[:, :-1]).to(torch.int64).cumprod(1).sum(1)

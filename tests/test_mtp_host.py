@@ -231,3 +231,22 @@ def test_repetition_penalty_steers_greedy_tokens_with_and_without_mtp():
             assert tok == want
             seen.add(tok)
             prev = tok
+
+
+def test_logit_bias_and_min_tokens_with_and_without_mtp():
+    for mtp in (True, False):
+        eng = _engine()
+        if not mtp:
+            eng.mtp = None
+            eng.scheduler = Scheduler(eng.blocks, max_num_seqs=2, max_num_batched_tokens=24, decode_width=1,
+                                      max_model_len=1024)
+        last = 40
+        forced = eng.add_request([3, last], SamplingParams(max_tokens=5, ignore_eos=True, logit_bias={"77": 100.0}))
+        stop = (7 * last + 3) % V  # the target's first choice after the prompt is a stop token here
+        held = eng.add_request([3, last], SamplingParams(max_tokens=8, stop_token_ids=(stop,), min_tokens=3))
+        free = eng.add_request([3, last], SamplingParams(max_tokens=8, stop_token_ids=(stop,)))
+        while eng.has_unfinished():
+            eng.step()
+        assert forced.output == [77] * 5
+        assert free.output == [stop]                      # stops at once
+        assert held.output[0] == (7 * last + 4) % V and len(held.output) >= 3

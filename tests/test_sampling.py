@@ -237,10 +237,23 @@ def test_mtp_accept_mixes_greedy_and_sampling_sequences():
 def test_penalties_follow_vllm_definitions():
     row = torch.tensor([2.0, -2.0, 1.0, 0.5, -1.0])
     p = SamplingParams(repetition_penalty=2.0)
-    got = sampling.apply_penalties(row, [0], [1], p)         # tokens 0 (prompt) and 1 (output) seen
+    got = sampling.process_row(row, [0], [1], p)         # tokens 0 (prompt) and 1 (output) seen
     assert torch.allclose(got, torch.tensor([1.0, -4.0, 1.0, 0.5, -1.0]))
     p = SamplingParams(presence_penalty=0.5, frequency_penalty=0.25)
-    got = sampling.apply_penalties(row, [2], [3, 3, 4], p)   # the prompt takes no presence / frequency penalty
+    got = sampling.process_row(row, [2], [3, 3, 4], p)   # the prompt takes no presence / frequency penalty
     assert torch.allclose(got, torch.tensor([2.0, -2.0, 1.0, 0.5 - 0.5 - 0.5, -1.0 - 0.5 - 0.25]))
-    assert not sampling.has_penalties(SamplingParams()) and sampling.has_penalties(p)
+    assert not sampling.has_processors(SamplingParams()) and sampling.has_processors(p)
     assert sampling.needs_logits(p)
+
+
+def test_min_p_logit_bias_and_min_tokens():
+    x = torch.tensor([0.0, -0.1, -3.0, -5.0])                 # probabilities ~ .50, .45, .02, .003
+    kept = torch.isfinite(sampling.filter_logits(x, 0, 1.0, min_p=0.1)).tolist()
+    assert kept == [True, True, False, False]
+    row = torch.zeros(6)
+    p = SamplingParams(logit_bias={"3": 5.0, "99": 1.0})       # out-of-vocabulary ids are ignored
+    assert sampling.process_row(row, [], [], p).tolist() == [0, 0, 0, 5.0, 0, 0]
+    p = SamplingParams(min_tokens=2, stop_token_ids=(1, 4))
+    assert torch.isinf(sampling.process_row(row, [], [5], p)[[1, 4]]).all()   # one token so far: held back
+    assert torch.isfinite(sampling.process_row(row, [], [5, 2], p)).all()     # long enough: free
+    assert sampling.has_processors(p) and not sampling.has_processors(SamplingParams(min_p=0.5))
