@@ -54,6 +54,7 @@ class _Common(BaseModel):
     ignore_eos: bool = False
     stop_token_ids: list[int] = Field(default_factory=list)
     stop: str | list[str] | None = None
+    include_stop_str_in_output: bool = False
     logprobs: int | bool | None = None   # completions: top-N count; chat: on / off
     top_logprobs: int | None = None      # chat: top-N count
     temperature: float | None = None
@@ -260,7 +261,7 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
                 toks: list[int] = []
                 all_lps: list = []
                 reason = None
-                matcher = StopMatcher(req.stop)
+                matcher = StopMatcher(req.stop, req.include_stop_str_in_output)
                 detok = IncrementalDecoder(tokenizer)
                 parts: list[str] = []
                 while True:
@@ -322,7 +323,7 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
             detoks = [IncrementalDecoder(tokenizer) for _ in runs]
             offsets = [0] * len(runs)  # text offsets of the completions logprobs
             echoed = [not echo] * len(runs)
-            matchers = [StopMatcher(req.stop) for _ in runs]
+            matchers = [StopMatcher(req.stop, req.include_stop_str_in_output) for _ in runs]
             live = set(range(len(runs)))
             if chat:
                 for i in range(len(runs)):

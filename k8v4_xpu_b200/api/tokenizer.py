@@ -112,10 +112,11 @@ class StopMatcher:
     that the next tokens complete; text from the first stop string on is
     never shown. Without stop strings the text passes through unchanged."""
 
-    def __init__(self, stops=None):
+    def __init__(self, stops=None, include: bool = False):
         if isinstance(stops, str):
             stops = [stops]
         self.stops = [s for s in (stops or []) if s]
+        self.include = include  # vLLM's include_stop_str_in_output: the matched string is shown too
         self.hold = max((len(s) for s in self.stops), default=1) - 1
         self.buf = ""
         self.done = False
@@ -124,9 +125,10 @@ class StopMatcher:
         if self.done:
             return "", True
         self.buf += text
-        hits = [i for i in (self.buf.find(s) for s in self.stops) if i >= 0]
+        hits = [(i, len(s)) for i, s in ((self.buf.find(s), s) for s in self.stops) if i >= 0]
         if hits:
-            out, self.buf, self.done = self.buf[:min(hits)], "", True
+            at, n = min(hits)
+            out, self.buf, self.done = self.buf[:at + (n if self.include else 0)], "", True
             return out, True
         if final or self.hold == 0:
             out, self.buf = self.buf, ""

@@ -392,3 +392,14 @@ def test_tokenize_detokenize_ping_version(client):
     assert c.post("/detokenize", json={"tokens": [ord("a") + 3, ord("b") + 3]}).json() == {"prompt": "ab"}
     assert c.get("/ping").json() == {"status": "ok"}
     assert c.get("/version").json()["version"]
+
+
+def test_stop_string_can_be_kept_in_the_output(client):
+    from k8v4_xpu_b200.api.tokenizer import StopMatcher
+    m = StopMatcher(["cd", "c"], include=True)
+    assert m.feed("abcde") == ("abc", True)  # the earliest match ("c" at 2) ends the text, kept
+    c, _, _ = client
+    body = {"prompt": [ord("a") + 3], "max_tokens": 20, "ignore_eos": True, "stop": ["ef"],
+            "include_stop_str_in_output": True}
+    r = c.post("/v1/completions", json=body).json()
+    assert r["choices"][0]["text"] == "bcdef" and r["choices"][0]["finish_reason"] == "stop"
