@@ -20,7 +20,9 @@ each token's log-probability under the model's logits; with ``echo`` the
 prompt comes back first, with its tokens' log-probabilities when asked
 (computed during the prefill, which then takes no prefix-cache hit). ``n`` (1-16)
 choices run as n engine requests over the same prompt (seed + i for choice
-i of a seeded request).
+i of a seeded request). Beam search, ``best_of``, structured output
+(``response_format``, guided decoding) and tool calls are not built: such
+requests get a 400 instead of being served as if the field were absent.
 """
 from __future__ import annotations
 
@@ -68,6 +70,14 @@ class _Common(BaseModel):
     presence_penalty: float | None = None
     frequency_penalty: float | None = None
     n: int = 1
+    # accepted only in their neutral form: refused with a 400 rather than ignored
+    best_of: int | None = None
+    use_beam_search: bool = False
+    response_format: dict | None = None
+    tools: list | None = None
+    guided_json: Any = None
+    guided_regex: str | None = None
+    guided_choice: list | None = None
 
 
 class CompletionRequest(_Common):
@@ -103,7 +113,18 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
     app = FastAPI(title="k8v4_xpu_b200")
     eos = getattr(tokenizer, "eos_token_id", None)
 
+    def refuse_unsupported(req: _Common) -> None:
+        if req.best_of is not None and req.best_of != req.n:
+            raise HTTPException(400, "best_of is not supported (use n)")
+        if req.use_beam_search:
+            raise HTTPException(400, "beam search is not supported")
+        if req.response_format and req.response_format.get("type", "text") != "text":
+            raise HTTPException(400, "structured output (response_format) is not supported")
+        if req.tools or req.guided_json is not None or req.guided_regex or req.guided_choice:
+            raise HTTPException(400, "tool calls and guided decoding are not supported")
+
     def params_for(req: _Common, prompt_len: int) -> SamplingParams:
+        refuse_unsupported(req)
         mt = req.max_completion_tokens if req.max_completion_tokens is not None else req.max_tokens
         mt = 16 if mt is None else mt  # an explicit 0 is refused below, not defaulted
         if mt == 0 and getattr(req, "echo", False):

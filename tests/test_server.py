@@ -403,3 +403,13 @@ def test_stop_string_can_be_kept_in_the_output(client):
             "include_stop_str_in_output": True}
     r = c.post("/v1/completions", json=body).json()
     assert r["choices"][0]["text"] == "bcdef" and r["choices"][0]["finish_reason"] == "stop"
+
+
+def test_unsupported_features_are_refused_not_ignored(client):
+    c, _, _ = client
+    base = {"prompt": [5, 6], "max_tokens": 2}
+    for extra in ({"best_of": 3}, {"use_beam_search": True}, {"response_format": {"type": "json_object"}},
+                  {"tools": [{"type": "function", "function": {"name": "f"}}]}, {"guided_choice": ["a", "b"]}):
+        assert c.post("/v1/completions", json={**base, **extra}).status_code == 400, extra
+    ok = {**base, "best_of": 1, "response_format": {"type": "text"}, "tools": [], "user": "x"}
+    assert c.post("/v1/completions", json=ok).status_code == 200
