@@ -6,7 +6,7 @@ L2 flush (a 256 MB write) between iterations so weights and KV come from
 HBM. Fractions are against MEASURED_PEAKS.json (STREAM copy GB/s and cuBLAS
 bf16 TFLOP/s) when present, else the pool's fallback (6,650 GB/s, 1,590 TF).
 
-    python bench/microbench.py [--only gemm|mlp|attn|misc] [--ctx 128197]
+    python bench/microbench.py [--only gemm|mlp|attn|attnlib|misc] [--ctx 128197]
 """
 from __future__ import annotations
 
@@ -194,6 +194,55 @@ def bench_attn(ctx):
     report("prefill_attn q=%d ctx=%d" % (ql, ctx), t, flops=flops)
 
 
+def bench_attn_libraries(ctx):
+    """The reference's flash-vs-oneDNN comparison (``bench/prefill_flash_paged.py``)
+    on B200: this framework's paged K8/V4 prefill attention against library
+    attention (flash_attn's varlen kernel and torch SDPA) given the same K/V
+    dequantized to dense bf16, one 4,224-token chunk at the end of ``ctx``
+    keys. The libraries read 2 x 128 x 2 bytes per key and head instead of
+    202; each row reports its max difference from ours."""
+    hkv, gqa, ql = 4, 6, 4224
+    layout, cache, bt = fill_cache(ctx, 1, hkv, gqa)
+    q = torch.randn(ql, hkv * gqa, 128, device="cuda").bfloat16()
+    cu = torch.tensor([0, ql], dtype=torch.int32, device="cuda")
+    lens = torch.tensor([ctx], dtype=torch.int32, device="cuda")
+    ours = ops.prefill_attn(q, cu, lens, bt, cache, hkv, gqa, ql)
+    t = timeit(lambda: ops.prefill_attn(q, cu, lens, bt, cache, hkv, gqa, ql), iters=5, warmup=2)
+    keys = ctx - ql + ql / 2
+    flops = 4 * hkv * gqa * 128 * ql * keys
+    report("prefill_attn (K8/V4 pages) q=%d ctx=%d" % (ql, ctx), t, flops=flops)
+    kd = torch.empty(ctx, hkv, 128, dtype=torch.bfloat16, device="cuda")
+    vd = torch.empty_like(kd)
+    for h in range(hkv):
+        k, v = ops.gather_dequant(cache, bt[0], hkv, h, ctx, dtype=torch.bfloat16)
+        kd[:, h], vd[:, h] = k, v
+    del cache
+    try:
+        from flash_attn import flash_attn_varlen_func
+        cuq = torch.tensor([0, ql], dtype=torch.int32, device="cuda")
+        cuk = torch.tensor([0, ctx], dtype=torch.int32, device="cuda")
+        fa = lambda: flash_attn_varlen_func(q, kd, vd, cuq, cuk, ql, ctx, causal=True)  # noqa: E731
+        out = fa()
+        t = timeit(fa, iters=5, warmup=2)
+        report("flash_attn varlen (dense bf16 K/V) q=%d ctx=%d" % (ql, ctx), t, flops=flops,
+               max_diff_vs_ours=round((out.float() - ours.float()).abs().max().item(), 4))
+    except Exception as e:  # not installed, or no kernel for this GPU
+        print(json.dumps({"kernel": "flash_attn varlen", "unavailable": str(e)[:200]}), flush=True)
+    try:
+        import torch.nn.functional as F
+        qh = q.transpose(0, 1).unsqueeze(0)
+        kh, vh = kd.transpose(0, 1).unsqueeze(0), vd.transpose(0, 1).unsqueeze(0)
+        # bottom-right causal: query i sees keys [0, ctx - ql + i]
+        mask = torch.ones(ql, ctx, dtype=torch.bool, device="cuda").tril(ctx - ql)
+        sd = lambda: F.scaled_dot_product_attention(qh, kh, vh, attn_mask=mask, enable_gqa=True)  # noqa: E731
+        out = sd().squeeze(0).transpose(0, 1)
+        t = timeit(sd, iters=3, warmup=1)
+        report("torch SDPA (dense bf16 K/V, mask) q=%d ctx=%d" % (ql, ctx), t, flops=flops,
+               max_diff_vs_ours=round((out.float() - ours.float()).abs().max().item(), 4))
+    except Exception as e:
+        print(json.dumps({"kernel": "torch SDPA", "unavailable": str(e)[:200]}), flush=True)
+
+
 def bench_misc():
     H, I = 5120, 17408
     for T in (1, 4224):
@@ -222,6 +271,8 @@ def main():
         bench_attn(a.ctx)
     if a.only in (None, "misc"):
         bench_misc()
+    if a.only == "attnlib":  # only on request: the libraries need dense K/V (and SDPA a dense mask)
+        bench_attn_libraries(a.ctx)
     assert ops.status() == 0
 
 
