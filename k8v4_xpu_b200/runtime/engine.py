@@ -176,8 +176,9 @@ class LLMEngine:
         except Exception as e:  # no multicast on this box: NCCL all-reduce
             import logging
             logging.getLogger("k8v4").warning("fused all-reduce unavailable (%s); using NCCL", e)
-        # prefill chunks: sequence parallelism with the reduce-scatter and the
-        # all-gather fused into the GEMMs
+        # prefill chunks, with K8V4_TP_PREFILL=sp (the default is GEMM + NCCL):
+        # sequence parallelism with the reduce-scatter and the all-gather fused
+        # into the GEMMs
         from ..parallel.seq_parallel import SeqParallel, sp_mode
         self.tp_prefill_mode = "nccl"
         if sp_mode() != "sp":
