@@ -20,7 +20,8 @@ each token's log-probability under the model's logits; with ``echo`` the
 prompt comes back first, with its tokens' log-probabilities when asked
 (computed during the prefill, which then takes no prefix-cache hit). ``n`` (1-16)
 choices run as n engine requests over the same prompt (seed + i for choice
-i of a seeded request). Beam search, ``best_of``, structured output
+i of a seeded request); ``best_of`` runs that many and returns the n with
+the highest cumulative log-probability. Beam search, structured output
 (``response_format``, guided decoding) and tool calls are not built: such
 requests get a 400 instead of being served as if the field were absent.
 """
@@ -114,8 +115,10 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
     eos = getattr(tokenizer, "eos_token_id", None)
 
     def refuse_unsupported(req: _Common) -> None:
-        if req.best_of is not None and req.best_of != req.n:
-            raise HTTPException(400, "best_of is not supported (use n)")
+        if req.best_of is not None and not req.n <= req.best_of <= 16:
+            raise HTTPException(400, "best_of must lie in [n, 16]")
+        if req.best_of is not None and req.best_of > req.n and req.stream:
+            raise HTTPException(400, "best_of above n is served without streaming")
         if req.use_beam_search:
             raise HTTPException(400, "beam search is not supported")
         if req.response_format and req.response_format.get("type", "text") != "text":
@@ -263,8 +266,14 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
                     "text_offset": offsets}
         # n choices are n engine requests over the same prompt (the prefix
         # cache shares its pages); seeded requests give choice i seed + i
+        # best_of candidates (n when unset) run as engine requests; the n with
+        # the highest cumulative log-probability come back
+        n_run = max(req.n, req.best_of or req.n)
+        rank_by_lp = n_run > req.n
+        if rank_by_lp and params.logprobs is None:
+            params = dataclasses.replace(params, logprobs=0)  # the chosen tokens' entries rank the candidates
         runs = []
-        for i in range(req.n):
+        for i in range(n_run):
             p = params if i == 0 else dataclasses.replace(
                 params, seed=None if params.seed is None else params.seed + i)
             runs.append(await run(prompt, p))
@@ -309,9 +318,15 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
                     raise HTTPException(500, "engine failed")
                 if reason and reason.startswith("rejected: "):
                     raise HTTPException(400, reason[len("rejected: "):])
-            choices = []
             if echo_only:  # prompt scoring: the one generated token is dropped
                 results = [([], "", "length", []) for _ in results]
+            usage = _usage(len(prompt), sum(len(r[0]) for r in results))
+            if rank_by_lp:
+                order = sorted(range(len(results)),
+                               key=lambda j: -sum(e[0] for e in results[j][3] if e is not None))
+                results = [results[j] for j in order[:req.n]]
+                runs = [runs[j] for j in order[:req.n]]
+            choices = []
             for i, (toks, text, reason, lps) in enumerate(results):
                 if echo:
                     ptoks, plps = echo_part(runs[i][0])
@@ -326,7 +341,7 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
                 choice["token_ids"] = toks
                 choices.append(choice)
             return {"id": rid, "object": obj, "created": created, "model": served_model_name,
-                    "choices": choices, "usage": _usage(len(prompt), sum(len(r[0]) for r in results))}
+                    "choices": choices, "usage": usage}
 
         async def events():
             n_out = 0

@@ -408,8 +408,38 @@ def test_stop_string_can_be_kept_in_the_output(client):
 def test_unsupported_features_are_refused_not_ignored(client):
     c, _, _ = client
     base = {"prompt": [5, 6], "max_tokens": 2}
-    for extra in ({"best_of": 3}, {"use_beam_search": True}, {"response_format": {"type": "json_object"}},
+    for extra in ({"best_of": 17}, {"use_beam_search": True}, {"response_format": {"type": "json_object"}},
                   {"tools": [{"type": "function", "function": {"name": "f"}}]}, {"guided_choice": ["a", "b"]}):
         assert c.post("/v1/completions", json={**base, **extra}).status_code == 400, extra
     ok = {**base, "best_of": 1, "response_format": {"type": "text"}, "tools": [], "user": "x"}
     assert c.post("/v1/completions", json=ok).status_code == 200
+
+
+def test_best_of_returns_the_most_likely_candidates(client, monkeypatch):
+    """best_of candidates are ranked by their tokens' summed log-probability;
+    the stand-in engine scores each candidate by its request order."""
+    c, eng, _ = client
+    orig = eng.add_request
+    count = {"n": 0}
+
+    def add(prompt, params=None):
+        seq = orig(prompt, params)
+        count["n"] += 1
+        seq.rank_score = -float(count["n"])   # later candidates are less likely
+        return seq
+    eng.add_request = add
+    orig_step = eng.step
+
+    def step():
+        fin = orig_step()
+        for s in list(eng.scheduler.running) + fin:
+            if s.logprobs and getattr(s, "rank_score", None) is not None:
+                s.logprobs[-1] = (s.rank_score, [])
+        return fin
+    eng.step = step
+    r = c.post("/v1/completions", json={"prompt": [5], "max_tokens": 2, "ignore_eos": True, "best_of": 3,
+                                        "n": 1}).json()
+    assert len(r["choices"]) == 1 and r["choices"][0]["logprobs"] is None
+    assert r["usage"]["completion_tokens"] == 6  # every candidate's tokens count
+    assert c.post("/v1/completions", json={"prompt": [5], "max_tokens": 2, "best_of": 3,
+                                           "stream": True}).status_code == 400
