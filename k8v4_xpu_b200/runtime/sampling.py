@@ -126,8 +126,15 @@ def wants_logprobs(params) -> bool:
 def needs_logits(params) -> bool:
     """Requests whose steps need the full-vocabulary logits (so they run
     eagerly): sampling ones, the ones asking for log-probabilities and the
-    ones with penalties."""
-    return samples(params) or wants_logprobs(params) or has_processors(params)
+    ones with logits processors. Asked every decode step for every sequence,
+    so the answer is kept on the (unchanging) params object."""
+    if params is None:
+        return False
+    memo = params.__dict__.get("_needs_logits")
+    if memo is None:
+        memo = samples(params) or wants_logprobs(params) or has_processors(params)
+        params.__dict__["_needs_logits"] = memo
+    return memo
 
 
 def logprob_entry(row_logits: torch.Tensor, token: int, top_n: int) -> tuple:
