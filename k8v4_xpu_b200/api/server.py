@@ -21,8 +21,10 @@ prompt comes back first, with its tokens' log-probabilities when asked
 (computed during the prefill, which then takes no prefix-cache hit). ``n`` (1-16)
 choices run as n engine requests over the same prompt (seed + i for choice
 i of a seeded request); ``best_of`` runs that many and returns the n with
-the highest cumulative log-probability. Beam search, structured output
-(``response_format``, guided decoding) and tool calls are not built: such
+the highest cumulative log-probability. ``guided_choice`` confines the
+output to one of the given strings (as the tokenizer encodes them). Beam
+search, structured output (``response_format``, JSON / regex guided
+decoding) and tool calls are not built: such
 requests get a 400 instead of being served as if the field were absent.
 """
 from __future__ import annotations
@@ -123,8 +125,11 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
             raise HTTPException(400, "beam search is not supported")
         if req.response_format and req.response_format.get("type", "text") != "text":
             raise HTTPException(400, "structured output (response_format) is not supported")
-        if req.tools or req.guided_json is not None or req.guided_regex or req.guided_choice:
-            raise HTTPException(400, "tool calls and guided decoding are not supported")
+        if req.tools or req.guided_json is not None or req.guided_regex:
+            raise HTTPException(400, "tool calls and JSON / regex guided decoding are not supported")
+        if req.guided_choice is not None and (not req.guided_choice
+                                              or not all(isinstance(c, str) and c for c in req.guided_choice)):
+            raise HTTPException(400, "guided_choice takes a list of non-empty strings")
 
     def params_for(req: _Common, prompt_len: int) -> SamplingParams:
         refuse_unsupported(req)
@@ -161,7 +166,9 @@ def build_app(driver, tokenizer, served_model_name: str, max_model_len: int, met
         return SamplingParams(max_tokens=mt, ignore_eos=req.ignore_eos, stop_token_ids=stops,
                               temperature=temperature, top_p=top_p, top_k=top_k, seed=req.seed,
                               repetition_penalty=rep, presence_penalty=pres, frequency_penalty=freq,
-                              min_p=min_p, logit_bias=bias or None, min_tokens=min_tokens)
+                              min_p=min_p, logit_bias=bias or None, min_tokens=min_tokens,
+                              allowed_sequences=(tuple(tuple(tokenizer.encode(c)) for c in req.guided_choice)
+                                                 if req.guided_choice else None))
 
     async def run(prompt: list[int], params: SamplingParams):
         loop = asyncio.get_running_loop()

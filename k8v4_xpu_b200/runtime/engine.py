@@ -463,6 +463,8 @@ class LLMEngine:
     def _should_stop(self, seq: Sequence, tok: int) -> bool:
         if len(seq.output) >= seq.params.max_tokens:
             return True
+        if seq.params.allowed_sequences and sampling.choice_finished(seq.params, seq.output):
+            return True
         return (not seq.params.ignore_eos) and tok in seq.params.stop_token_ids
 
     # ------------------------------------------------------------ helpers

@@ -191,7 +191,8 @@ def has_processors(params) -> bool:
                                    or float(getattr(params, "presence_penalty", 0.0)) != 0.0
                                    or float(getattr(params, "frequency_penalty", 0.0)) != 0.0
                                    or bool(getattr(params, "logit_bias", None))
-                                   or int(getattr(params, "min_tokens", 0) or 0) > 0)
+                                   or int(getattr(params, "min_tokens", 0) or 0) > 0
+                                   or bool(getattr(params, "allowed_sequences", None)))
 
 
 def _prompt_mask(prompt, V: int, dev, holder=None) -> torch.Tensor:
@@ -240,4 +241,43 @@ def process_row(row: torch.Tensor, prompt, output: list[int], p, holder=None) ->
         stops = [int(t) for t in p.stop_token_ids if 0 <= int(t) < V]
         if stops:
             x[torch.tensor(stops, dtype=torch.int64, device=dev)] = float("-inf")
+    allowed = choice_continuations(p, output)
+    if allowed is not None:
+        ids = [t for t in allowed if 0 <= t < V]
+        if ids:
+            keep = torch.full_like(x, float("-inf"))
+            idx = torch.tensor(ids, dtype=torch.int64, device=dev)
+            keep[idx] = x[idx]
+            x = keep
     return x
+
+
+def choice_continuations(p, output) -> set | None:
+    """Guided choice: the tokens that keep ``output`` a prefix of one of the
+    allowed sequences (plus the stop tokens when it already equals one), or
+    None when the request is not guided."""
+    seqs = getattr(p, "allowed_sequences", None)
+    if not seqs:
+        return None
+    n = len(output)
+    out = list(output)
+    nxt, complete = set(), False
+    for s in seqs:
+        if list(s[:n]) == out:
+            if len(s) > n:
+                nxt.add(int(s[n]))
+            else:
+                complete = True
+    if complete:
+        nxt |= {int(t) for t in (p.stop_token_ids or ())}
+    return nxt
+
+
+def choice_finished(p, output) -> bool:
+    """Guided choice: the output equals an allowed sequence that no other one extends."""
+    seqs = getattr(p, "allowed_sequences", None)
+    if not seqs:
+        return False
+    out = list(output)
+    return any(list(s) == out for s in seqs) and not any(len(s) > len(out) and list(s[:len(out)]) == out
+                                                         for s in seqs)

@@ -42,6 +42,7 @@ class SamplingParams:
     min_p: float = 0.0          # drop tokens below min_p x the top probability (0: off)
     logit_bias: dict | None = None  # token id -> bias added to its logit
     min_tokens: int = 0         # stop tokens are held back until the output is this long
+    allowed_sequences: tuple | None = None  # guided choice: the output must be one of these token lists
 
 
 @dataclasses.dataclass

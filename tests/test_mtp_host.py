@@ -250,3 +250,22 @@ def test_logit_bias_and_min_tokens_with_and_without_mtp():
         assert forced.output == [77] * 5
         assert free.output == [stop]                      # stops at once
         assert held.output[0] == (7 * last + 4) % V and len(held.output) >= 3
+
+
+def test_guided_choice_with_and_without_mtp():
+    """The output is one of the allowed token sequences, whatever the target
+    prefers, and the request stops when a choice is complete."""
+    choices = ((11, 12, 13), (11, 14), (20,))
+    for mtp in (True, False):
+        eng = _engine()
+        if not mtp:
+            eng.mtp = None
+            eng.scheduler = Scheduler(eng.blocks, max_num_seqs=2, max_num_batched_tokens=24, decode_width=1,
+                                      max_model_len=1024)
+        s = eng.add_request([3, 40], SamplingParams(max_tokens=10, ignore_eos=True, allowed_sequences=choices))
+        t = eng.add_request([3, 41], SamplingParams(max_tokens=10, ignore_eos=True, temperature=1.0, seed=2,
+                                                    allowed_sequences=choices))
+        while eng.has_unfinished():
+            eng.step()
+        assert tuple(s.output) in choices and tuple(t.output) in choices
+        assert s.finish_reason == "stop"

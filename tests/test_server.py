@@ -409,7 +409,8 @@ def test_unsupported_features_are_refused_not_ignored(client):
     c, _, _ = client
     base = {"prompt": [5, 6], "max_tokens": 2}
     for extra in ({"best_of": 17}, {"use_beam_search": True}, {"response_format": {"type": "json_object"}},
-                  {"tools": [{"type": "function", "function": {"name": "f"}}]}, {"guided_choice": ["a", "b"]}):
+                  {"tools": [{"type": "function", "function": {"name": "f"}}]}, {"guided_regex": "a+"},
+                  {"guided_choice": []}):
         assert c.post("/v1/completions", json={**base, **extra}).status_code == 400, extra
     ok = {**base, "best_of": 1, "response_format": {"type": "text"}, "tools": [], "user": "x"}
     assert c.post("/v1/completions", json=ok).status_code == 200
@@ -443,3 +444,17 @@ def test_best_of_returns_the_most_likely_candidates(client, monkeypatch):
     assert r["usage"]["completion_tokens"] == 6  # every candidate's tokens count
     assert c.post("/v1/completions", json={"prompt": [5], "max_tokens": 2, "best_of": 3,
                                            "stream": True}).status_code == 400
+
+
+def test_guided_choice_reaches_the_engine_as_token_sequences(client):
+    c, eng, _ = client
+    seen = []
+    orig = eng.add_request
+
+    def spy(prompt, params=None):
+        seen.append(params)
+        return orig(prompt, params)
+    eng.add_request = spy
+    r = c.post("/v1/completions", json={"prompt": [5], "max_tokens": 3, "guided_choice": ["yes", "no"]})
+    assert r.status_code == 200
+    assert seen[-1].allowed_sequences == (tuple(b + 3 for b in b"yes"), tuple(b + 3 for b in b"no"))
